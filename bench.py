@@ -1,0 +1,289 @@
+"""Benchmark of the B200 GEMM engine: one JSON line on rank 0.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kl|reference] [--workload NAME]
+
+A step is one GEMM over the workload's operands. The default workload is the 8192^3 bf16 GEMM
+(N(0,1)*0.02 inputs, seed 2), sharded along N over the ranks: rank r owns B rows
+[r*N/g, (r+1)*N/g) and produces C[:, shard] (no collective on the data path); `value` is the
+whole-job TFLOP/s, the total flops over the max-over-ranks device time. The operands (268 MB)
+exceed the 126 MB L2, so no flush runs between steps.
+
+  value      device time of K kl_gemm launches on resident inputs (CUDA events on the stream).
+  e2e        the same through the public API with host buffers: pinned H2D of A and B, kl_gemm,
+             D2H of C, all inside the timed region, every step.
+  roofline   the GEMM kernel's achieved TFLOP/s against the measured dense bf16 (or fp8) peak.
+  cpu_baseline  the CPU GEMM (fp32 accumulate, all host threads) on a bounded row slab.
+`--impl reference` times only the reference arm: the CPU GEMM restatement (the reference ships no
+GEMM of its own), rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+DEFAULT_WORKLOAD = "c3_8192_bf16"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in getattr(self, "lines", []):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(w, budget_s: float = 6.0):
+    """fp32-accumulate CPU GEMM on a row slab of A, doubled until it takes >= budget_s / 3."""
+    from maia_b200 import workloads as wl
+    from oracle import gemm as og
+
+    threads = og.threads_default()
+    rows = 16
+    while True:
+        a, b, sa, sb = wl.make_inputs(w, rows_a=rows)
+        t0 = time.perf_counter()
+        og.gemm_f32(a, b, sa * sb, threads=threads)
+        dt = time.perf_counter() - t0
+        if dt >= budget_s / 3 or rows >= w.m:
+            break
+        rows = min(w.m, rows * 2 if dt > 0.05 else rows * 8)
+    tflops = 2.0 * rows * w.n * w.k / dt / 1e12
+    return {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"rows [0,{rows}) of A x all of B ({rows}x{w.n}x{w.k}, {w.dtype}, fp32 accumulate), {dt:.2f} s"}
+
+
+def run_reference(args, w):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    base = None
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(w, budget_s=3.0)
+        if i >= args.warmup:
+            vals.append(r["value"])
+            base = r
+    v = statistics.median(vals)
+    base["value"] = v
+    line = {"metric": "GEMM TFLOP/s (CPU reference GEMM restatement)", "value": v, "unit": "TFLOP/s",
+            "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 2.0 * w.m * w.n * w.k / (v * 1e12) * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
+            "config": {"workload": w.name, "m": w.m, "n": w.n, "k": w.k},
+            "cpu_baseline": base, "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["kl", "reference"], default="kl")
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
+    ap.add_argument("--algo", type=int, default=0, help="kl_algo (0 = library default)")
+    ap.add_argument("--group-m", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    from maia_b200 import workloads as wl
+
+    w = wl.ALL[args.workload]
+    if args.impl == "reference":
+        return run_reference(args, w)
+
+    import numpy as np
+    import torch
+
+    import maia_b200 as kl
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    # Inputs: full A, this rank's N-shard of B (host-generated, seeded, then pinned).
+    a_bits, b_bits, sa, sb = wl.make_inputs(w)
+    n_lo, n_hi = w.n * rank // world, w.n * (rank + 1) // world
+    b_bits = np.ascontiguousarray(b_bits[n_lo:n_hi])
+    nshard = n_hi - n_lo
+    np_view = np.int16 if w.dtype == "bf16" else np.uint8
+    tdt = torch.bfloat16 if w.dtype == "bf16" else torch.float8_e4m3fn
+    odt = torch.bfloat16 if w.out == "bf16" else torch.float32
+    a_host = torch.from_numpy(a_bits.view(np_view)).view(tdt).pin_memory()
+    b_host = torch.from_numpy(b_bits.view(np_view)).view(tdt).pin_memory()
+    del a_bits, b_bits
+    a = a_host.to(dev)
+    b = b_host.to(dev)
+    c = torch.empty((w.m, nshard), dtype=odt, device=dev)
+    c_host = torch.empty((w.m, nshard), dtype=odt).pin_memory()
+    scale_a = scale_b = None
+    if w.dtype == "e4m3":
+        scale_a = torch.tensor([sa], dtype=torch.float32, device=dev)
+        scale_b = torch.tensor([sb], dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    kw = dict(scale_a=scale_a, scale_b=scale_b, algo=args.algo, group_m=args.group_m)
+
+    def step():
+        kl.gemm(a, b, c, **kw)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing
+    for _ in range(max(args.warmup, 3)):
+        step()
+    kl.read_status()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        barrier()
+    dev_ms = ev0.elapsed_time(ev1) / args.steps
+    if kl.read_status() != 0:
+        raise RuntimeError("a device-side wait timed out during the benchmark")
+    dev_ms = max_over_ranks(dev_ms)
+    flops_total = 2.0 * w.m * w.n * w.k
+    value = flops_total / (dev_ms * 1e-3) / 1e12
+
+    # ---- end to end through the public API with host buffers
+    h2d = a_host.numel() * a_host.element_size() + b_host.numel() * b_host.element_size()
+    d2h = c.numel() * c.element_size()
+
+    def e2e_step():
+        a.copy_(a_host, non_blocking=True)
+        b.copy_(b_host, non_blocking=True)
+        kl.gemm(a, b, c, **kw)
+        c_host.copy_(c, non_blocking=True)
+
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+
+    peaks, peak_src = load_peaks()
+    per_rank_flops = 2.0 * w.m * nshard * w.k
+    achieved = per_rank_flops / (dev_ms * 1e-3) / 1e12
+    peak = peaks["bf16_tflops"] if w.dtype == "bf16" else 2.0 * peaks["bf16_tflops"]
+    traffic = None
+    tf = ROOT / "profiles" / f"traffic_{w.name}.json"
+    if tf.exists() and world == 1:
+        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+
+    if rank == 0:
+        line = {
+            "metric": "GEMM TFLOP/s per B200 and % of tcgen05 dense peak",
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": w.dtype, "data": "synthetic",
+            "config": {"workload": w.name, "m": w.m, "n": w.n, "k": w.k, "out": w.out,
+                       "parallelism": f"N-sharded x{world}", "output": "C[:, shard] per rank (no gather)",
+                       "l2": "operands exceed L2 (no flush)", "algo": args.algo},
+            "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak,
+                         "peak_source": f"{peak_src} {'bf16_tflops' if w.dtype == 'bf16' else '2 x bf16_tflops (fp8 dense = 2x bf16)'}",
+                         "traffic": traffic},
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(w)
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,155 @@
+#pragma once
+
+// Host-side launchers for the kl GEMM kernels (C++ API; the C ABI in kl_gemm.h wraps these).
+// No counterpart in the reference: kernel_lib stops at the descriptor encoders.
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <stdexcept>
+
+#include <kl/gemm/gemm_kernel.cuh>
+#include <kl/kl.hpp>
+
+namespace kl::gemm {
+
+struct Problem {
+  int64_t m = 0, n = 0, k = 0;
+  const void* a = nullptr;
+  int64_t lda = 0;
+  const void* b = nullptr;
+  int64_t ldb = 0;
+  void* c = nullptr;
+  int64_t ldc = 0;
+  float alpha = 1.0f;
+  const float* scale_a = nullptr;
+  const float* scale_b = nullptr;
+  int group_m = 0;   // 0 = default for the config
+  int max_ctas = 0;  // 0 = every SM
+};
+
+struct LaunchInfo {
+  int grid = 0;
+  int tiles = 0;
+  int cluster = 1;
+};
+
+namespace detail {
+
+inline int sm_count(int device) {
+  static int cache[64] = {};
+  if (device < 0 || device >= 64) return 0;
+  if (cache[device] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+    cache[device] = n;
+  }
+  return cache[device];
+}
+
+template <class Cfg>
+inline cudaError_t prepare_kernel(int device, int* max_workers) {
+  // Per device: opt in to the shared-memory size and ask how many CTA groups fit at once.
+  static int workers[64] = {};
+  if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+  if (workers[device] == 0) {
+    auto kernel = gemm_tn_kernel<Cfg>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::kSmemBytes));
+    if (e != cudaSuccess) return e;
+    int n = 0;
+    if constexpr (Cfg::kCtaGroup == 1) {
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, Cfg::kThreads, Cfg::kSmemBytes);
+      if (e != cudaSuccess) return e;
+      n *= sm_count(device);
+    } else {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+      if (e != cudaSuccess) return e;
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = Cfg::kCtaGroup;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(Cfg::kCtaGroup * sm_count(device), 1, 1);
+      cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+      cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+      if (e != cudaSuccess) return e;
+    }
+    if (n <= 0) return cudaErrorInvalidConfiguration;
+    workers[device] = n;
+  }
+  *max_workers = workers[device];
+  return cudaSuccess;
+}
+
+}  // namespace detail
+
+// Queue C = alpha * A . B^T with the persistent tcgen05 kernel `Cfg` on `stream`. Throws
+// std::invalid_argument (bad layout, from the tensor-map builder) and returns CUDA errors.
+template <class Cfg>
+cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout_ns, cudaStream_t stream,
+                      LaunchInfo* info = nullptr) {
+  using InT = typename Cfg::in_type;
+  using OutT = typename Cfg::out_type;
+  if (pr.m <= 0 || pr.n <= 0 || pr.k <= 0) throw std::invalid_argument("kl::gemm: m, n and k must be positive");
+  if (pr.m > INT32_MAX || pr.n > INT32_MAX || pr.k > INT32_MAX)
+    throw std::invalid_argument("kl::gemm: extents must fit in 32 bits");
+
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  int max_workers = 0;
+  e = detail::prepare_kernel<Cfg>(device, &max_workers);
+  if (e != cudaSuccess) return e;
+
+  TnParams p{};
+  p.map_a = make_tma_load<typename Cfg::ATile>(row_major_strided(static_cast<InT const*>(pr.a), pr.m, pr.k, pr.lda)).map;
+  p.map_b = make_tma_load<typename Cfg::BTile>(row_major_strided(static_cast<InT const*>(pr.b), pr.n, pr.k, pr.ldb)).map;
+  p.map_c = make_tma_store<typename Cfg::CBox>(row_major_strided(static_cast<OutT*>(pr.c), pr.m, pr.n, pr.ldc)).map;
+
+  TnArgs& a = p.args;
+  a.m = int(pr.m);
+  a.n = int(pr.n);
+  a.k = int(pr.k);
+  a.tiles_m = int((pr.m + Cfg::kTileM - 1) / Cfg::kTileM);
+  a.tiles_n = int((pr.n + Cfg::kTileN - 1) / Cfg::kTileN);
+  a.k_blocks = int((pr.k + Cfg::kBlockK - 1) / Cfg::kBlockK);
+  a.group_m = pr.group_m > 0 ? pr.group_m : (Cfg::kCtaGroup == 2 ? 8 : 16);
+  a.group_m = std::min(a.group_m, a.tiles_m);
+  a.alpha = pr.alpha;
+  a.scale_a = pr.scale_a;
+  a.scale_b = pr.scale_b;
+  a.status = status;
+  a.timeout_ns = timeout_ns;
+
+  const int tiles = a.tiles_m * a.tiles_n;
+  int workers = std::min(tiles, max_workers);
+  if (pr.max_ctas > 0) workers = std::min(workers, std::max(1, pr.max_ctas / Cfg::kCtaGroup));
+
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(unsigned(workers * Cfg::kCtaGroup), 1, 1);
+  cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  if constexpr (Cfg::kCtaGroup > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = Cfg::kCtaGroup;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  if (info) {
+    info->grid = workers * Cfg::kCtaGroup;
+    info->tiles = tiles;
+    info->cluster = Cfg::kCtaGroup;
+  }
+  return cudaLaunchKernelEx(&cfg, gemm_tn_kernel<Cfg>, p);
+}
+
+}  // namespace kl::gemm

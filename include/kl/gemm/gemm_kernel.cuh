@@ -1,0 +1,389 @@
+#pragma once
+
+// Persistent, warp-specialised dense GEMM for sm_100a:  C[M,N] = alpha * A[M,K] . B[N,K]^T
+// (both operands K-major, C row-major). No counterpart in the reference: kernel_lib ships the
+// descriptor encoders (tma_desc.hpp, umma_desc.hpp) this kernel is built from, but no kernel.
+//
+// Roles (192 threads, one CTA per SM):
+//   warp 0      TMA producer: fills a Stages-deep ring of (A, B) K-blocks in shared memory.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma into a TMEM accumulator and commits
+//               each consumed stage back to the producer; warp 1 also owns the TMEM allocation.
+//   warps 2..5  epilogue: tcgen05.ld -> scale -> convert -> swizzled shared staging -> TMA store.
+// Two TMEM accumulators (2 x BlockN fp32 columns) let the epilogue of tile i overlap the main
+// loop of tile i + 1. Tiles are walked persistently in groups of `group_m` tile-rows so that the
+// CTAs running at the same time share A and B tiles in L2.
+//
+// CtaGroup = 2 runs a CTA pair (cluster of 2) on a 256-row tile with cta_group::2 MMAs: each CTA
+// loads its own 128 rows of A and its own half of B (no multicast), the even CTA issues the MMAs,
+// and every byte, stage release and accumulator hand-off is signalled through mbarriers in both
+// CTAs.
+//
+// Every wait is bounded (args.timeout_ns). On a timeout the role records a bit in *args.status,
+// stops, and the CTA still drains its MMAs and frees TMEM before it exits.
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <cstdint>
+
+#include <kl/arch/cluster.hpp>
+#include <kl/arch/mbarrier.hpp>
+#include <kl/arch/tcgen05.hpp>
+#include <kl/arch/tma.hpp>
+#include <kl/kl.hpp>
+
+namespace kl::gemm {
+
+// Status bits a kernel ORs into *status when a bounded wait runs out.
+enum : int {
+  kStatusProducerTimeout = 1,
+  kStatusMmaTimeout = 2,
+  kStatusEpilogueTimeout = 4,
+  kStatusDrainTimeout = 8,
+};
+
+template <typename InT, typename OutT, int CtaGroup, int BlockN, int Stages>
+struct TnConfig {
+  using in_type = InT;
+  using out_type = OutT;
+  static constexpr int kCtaGroup = CtaGroup;
+  static constexpr int kThreads = 192;
+  static constexpr int kCtaM = 128;                    // rows of A (= TMEM lanes) per CTA
+  static constexpr int kTileM = kCtaM * CtaGroup;      // rows of C per tile
+  static constexpr int kTileN = BlockN;                // columns of C per tile (UMMA N)
+  static constexpr int kCtaN = BlockN / CtaGroup;      // rows of B each CTA loads
+  static constexpr int kBlockK = 128 / int(sizeof(InT));  // one 128-byte swizzle span of K
+  static constexpr int kUmmaK = 32 / int(sizeof(InT));    // K of one tcgen05.mma
+  static constexpr int kStages = Stages;
+  static constexpr int kNumAcc = 2;
+  static constexpr int kAccCols = BlockN;              // fp32 accumulator columns per buffer
+  static constexpr int kTmemCols = (kAccCols * kNumAcc <= 32) ? 32 : (kAccCols * kNumAcc <= 64) ? 64
+                                 : (kAccCols * kNumAcc <= 128) ? 128 : (kAccCols * kNumAcc <= 256) ? 256 : 512;
+  static constexpr int kChunkCols = 128 / int(sizeof(OutT));  // epilogue store box width (128 B)
+  static constexpr int kChunks = BlockN / kChunkCols;
+
+  using ATile = SmemTile<InT, kCtaM, kBlockK>;
+  using BTile = SmemTile<InT, kCtaN, kBlockK>;
+  using CBox = SmemTile<OutT, 32, kChunkCols>;
+
+  static constexpr uint32_t kABytes = ATile::bytes;
+  static constexpr uint32_t kBBytes = BTile::bytes;
+  static constexpr uint32_t kCBytes = CBox::bytes;     // 4 KB per staging buffer
+  static constexpr uint32_t kOffA = 0;
+  static constexpr uint32_t kOffB = kOffA + kStages * kABytes;
+  static constexpr uint32_t kOffC = kOffB + kStages * kBBytes;
+  static constexpr uint32_t kOffBar = kOffC + 8 * kCBytes;  // 4 epilogue warps x 2 buffers
+  static constexpr uint32_t kNumBars = 2 * kStages + 2 * kNumAcc + 1;
+  static constexpr uint32_t kOffSlot = kOffBar + 8 * kNumBars;
+  static constexpr uint32_t kSmemBytes = kOffSlot + 16 + 1024;  // + slack to align the base to 1 KB
+
+  static constexpr bool kIsF8 = sizeof(InT) == 1;
+  static constexpr uint32_t kIdesc = mma_instr_desc<InT, InT, float, kTileM, BlockN>();
+
+  static_assert(kTmemCols <= 512 && kAccCols * kNumAcc <= 512, "accumulators exceed TMEM");
+  static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
+  static_assert(BlockN % (16 * CtaGroup) == 0 && BlockN <= 256, "UMMA N");
+  static_assert(kCtaN % 8 == 0 && kCtaN <= 256, "B tile rows");
+  static_assert(BlockN % kChunkCols == 0, "epilogue chunking");
+  static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "stages must keep 1 KB alignment");
+};
+
+struct TnArgs {
+  int m, n, k;
+  int tiles_m, tiles_n, k_blocks;
+  int group_m;                  // raster group height, in tiles
+  float alpha;                  // C = alpha * (A . B^T) [* *scale_a * *scale_b]
+  const float* scale_a;         // optional device scalars (nullptr = 1)
+  const float* scale_b;
+  int* status;                  // device word; timeout bits are ORed in
+  unsigned long long timeout_ns;
+};
+
+struct TnParams {
+  CUtensorMap map_a;  // A [M, K], box {kBlockK, 128}
+  CUtensorMap map_b;  // B [N, K], box {kBlockK, kCtaN}
+  CUtensorMap map_c;  // C [M, N], box {kChunkCols, 32}
+  TnArgs args;
+};
+
+// Grouped raster: tiles [g*group_m, (g+1)*group_m) x [0, tiles_n) are visited column by column.
+KL_HOST_DEVICE void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int& tm, int& tn) {
+  const int per_group = group_m * tiles_n;
+  const int g = t / per_group;
+  const int first_m = g * group_m;
+  const int rows = (tiles_m - first_m) < group_m ? (tiles_m - first_m) : group_m;
+  const int r = t - g * per_group;
+  tm = first_m + r % rows;
+  tn = r / rows;
+}
+
+#if defined(__CUDACC__)
+
+KL_DEVICE void record_status(int* status, int bit) { atomicOr(status, bit); }
+
+KL_DEVICE void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+KL_DEVICE uint32_t ld_shared_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+KL_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_constant__ TnParams p) {
+#if defined(KL_ARCH_SM100)
+  using InT = typename Cfg::in_type;
+  using OutT = typename Cfg::out_type;
+  constexpr int CG = Cfg::kCtaGroup;
+  constexpr int S = Cfg::kStages;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_addr(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t a_smem = base + Cfg::kOffA;
+  const uint32_t b_smem = base + Cfg::kOffB;
+  const uint32_t c_smem = base + Cfg::kOffC;
+  const uint32_t bar0 = base + Cfg::kOffBar;
+  const uint32_t tmem_slot = base + Cfg::kOffSlot;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (S + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * S + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * S + Cfg::kNumAcc + a); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * S + 2 * Cfg::kNumAcc);
+
+  const TnArgs& args = p.args;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t cta_rank = (CG == 2) ? cluster_ctarank() : 0u;  // rank inside the pair
+  const int worker = blockIdx.x / CG;
+  const int num_workers = gridDim.x / CG;
+  const int num_tiles = args.tiles_m * args.tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbarrier_init(full_bar(s), 1);
+      mbarrier_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < Cfg::kNumAcc; ++a) {
+      mbarrier_init(tfull_bar(a), 1);
+      mbarrier_init(tempty_bar(a), 4 * CG);  // one arrival per epilogue warp of the pair
+    }
+    mbarrier_init(drain_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&p.map_a);
+    tma_prefetch_map(&p.map_b);
+    tma_prefetch_map(&p.map_c);
+  }
+  if (warp == 1) {
+    tmem_alloc<CG>(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish<CG>();
+  }
+  tcgen05_fence_before();
+  if constexpr (CG == 2) {
+    cluster_sync();  // the peer's barriers must exist before any cross-CTA arrive or TMA
+  } else {
+    __syncthreads();
+  }
+  tcgen05_fence_after();
+  const uint32_t tmem_base = ld_shared_u32(tmem_slot);
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (elect_one()) {
+      const uint32_t leader_full0 = (CG == 2) ? mapa_shared(full_bar(0), 0) : full_bar(0);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int t = worker; ok && t < num_tiles; t += num_workers) {
+        int tm, tn;
+        tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
+        const int a_row = tm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM;
+        const int b_row = tn * Cfg::kTileN + int(cta_rank) * Cfg::kCtaN;
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if (!mbarrier_wait(empty_bar(stage), phase ^ 1u, args.timeout_ns)) {
+            record_status(args.status, kStatusProducerTimeout);
+            ok = false;
+            break;
+          }
+          const int kx = kb * Cfg::kBlockK;
+          if constexpr (CG == 1) {
+            mbarrier_arrive_expect_tx(full_bar(stage), Cfg::kABytes + Cfg::kBBytes);
+            tma_load_2d(a_smem + stage * Cfg::kABytes, &p.map_a, full_bar(stage), kx, a_row);
+            tma_load_2d(b_smem + stage * Cfg::kBBytes, &p.map_b, full_bar(stage), kx, b_row);
+          } else {
+            // The leader's barrier counts the bytes of both CTAs; only the leader arrives.
+            if (cta_rank == 0) mbarrier_arrive_expect_tx(full_bar(stage), 2u * (Cfg::kABytes + Cfg::kBBytes));
+            const uint32_t fb = leader_full0 + 8u * stage;
+            tma_load_2d_pair(a_smem + stage * Cfg::kABytes, &p.map_a, fb, kx, a_row);
+            tma_load_2d_pair(b_smem + stage * Cfg::kBBytes, &p.map_b, fb, kx, b_row);
+          }
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let copies already in flight land before the CTA can exit (bounded, short).
+        for (int s = 0; s < S; ++s) (void)mbarrier_wait(empty_bar(s), phase ^ 1u, 1000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if ((CG == 1 || cta_rank == 0) && elect_one()) {
+      const uint64_t a_desc0 = umma_desc_at<typename Cfg::ATile>(a_smem).desc_;
+      const uint64_t b_desc0 = umma_desc_at<typename Cfg::BTile>(b_smem).desc_;
+      const uint32_t peer = cta_rank ^ 1u;
+      uint32_t stage = 0, phase = 0;
+      uint32_t iter = 0;
+      bool ok = true;
+      for (int t = worker; ok && t < num_tiles; t += num_workers, ++iter) {
+        const uint32_t acc = iter & 1u;
+        const uint32_t acc_phase = (iter >> 1) & 1u;
+        if (!mbarrier_wait(tempty_bar(acc), acc_phase ^ 1u, args.timeout_ns)) {
+          record_status(args.status, kStatusMmaTimeout);
+          ok = false;
+          break;
+        }
+        tcgen05_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * Cfg::kAccCols;
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if (!mbarrier_wait(full_bar(stage), phase, args.timeout_ns)) {
+            record_status(args.status, kStatusMmaTimeout);
+            ok = false;
+            break;
+          }
+          tcgen05_fence_after();
+          const uint64_t a_desc = a_desc0 + ((stage * Cfg::kABytes) >> 4);
+          const uint64_t b_desc = b_desc0 + ((stage * Cfg::kBBytes) >> 4);
+#pragma unroll
+          for (int k = 0; k < Cfg::kBlockK / Cfg::kUmmaK; ++k) {
+            const uint64_t koff = block_offset_16B<typename Cfg::ATile>(k);
+            const uint32_t accumulate = (kb | k) != 0;
+            if constexpr (Cfg::kIsF8)
+              umma_f8_ss<CG>(d_tmem, a_desc + koff, b_desc + koff, Cfg::kIdesc, accumulate);
+            else
+              umma_f16_ss<CG>(d_tmem, a_desc + koff, b_desc + koff, Cfg::kIdesc, accumulate);
+          }
+          // Stage consumed once these MMAs complete: release it in both CTAs of the pair.
+          umma_commit<CG>(empty_bar(stage));
+          if constexpr (CG == 2) umma_commit<CG>(mapa_shared(empty_bar(stage), peer));
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit<CG>(tfull_bar(acc));
+        if constexpr (CG == 2) umma_commit<CG>(mapa_shared(tfull_bar(acc), peer));
+      }
+      // Every MMA this thread issued must finish before TMEM is freed.
+      umma_commit<CG>(drain_bar);
+      if (!mbarrier_wait(drain_bar, 0, args.timeout_ns)) record_status(args.status, kStatusDrainTimeout);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int ew = warp - 2;       // epilogue warp index -> staging buffers
+    const uint32_t lane_base = uint32_t(quarter * 32) << 16;
+    float alpha = args.alpha;
+    if (args.scale_a != nullptr) alpha *= *args.scale_a;
+    if (args.scale_b != nullptr) alpha *= *args.scale_b;
+    const uint32_t tempty_leader0 = (CG == 2) ? mapa_shared(tempty_bar(0), 0) : tempty_bar(0);
+    uint32_t iter = 0, nbuf = 0;
+    for (int t = worker; t < num_tiles; t += num_workers, ++iter) {
+      int tm, tn;
+      tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
+      const uint32_t acc = iter & 1u;
+      const uint32_t acc_phase = (iter >> 1) & 1u;
+      if (!mbarrier_wait(tfull_bar(acc), acc_phase, args.timeout_ns)) {
+        if (lane == 0) record_status(args.status, kStatusEpilogueTimeout);
+        break;
+      }
+      tcgen05_fence_after();
+      const int row0 = tm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM + quarter * 32;
+      const int col0 = tn * Cfg::kTileN;
+#pragma unroll 1
+      for (int c = 0; c < Cfg::kChunks; ++c) {
+        uint32_t v[Cfg::kChunkCols];
+        const uint32_t taddr = tmem_base + lane_base + acc * Cfg::kAccCols + uint32_t(c * Cfg::kChunkCols);
+        if constexpr (Cfg::kChunkCols == 64) {
+          tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+          tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        } else {
+          tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        }
+        tmem_wait_ld();
+        if (c == Cfg::kChunks - 1) {
+          // This warp is done with the accumulator: hand it back to the MMA issuer.
+          tcgen05_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (CG == 2)
+              mbarrier_arrive_cluster(tempty_leader0 + 8u * acc);
+            else
+              mbarrier_arrive(tempty_bar(acc));
+          }
+        }
+        const int col = col0 + c * Cfg::kChunkCols;
+        const bool store = row0 < args.m && col < args.n;
+        const uint32_t buf = c_smem + uint32_t(ew * 2 + (nbuf & 1u)) * Cfg::kCBytes;
+        // The buffer's previous store (two chunks ago) must have finished reading it.
+        if (lane == 0) tma_store_wait_read<1>();
+        __syncwarp();
+        const uint32_t row_addr = buf + uint32_t(lane) * 128u;
+        const uint32_t sw = uint32_t(lane & 7);
+        if constexpr (sizeof(OutT) == 2) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float* f = reinterpret_cast<const float*>(&v[8 * j]);
+            st_shared_v4(row_addr + ((uint32_t(j) ^ sw) << 4), pack_bf16x2(f[0] * alpha, f[1] * alpha),
+                         pack_bf16x2(f[2] * alpha, f[3] * alpha), pack_bf16x2(f[4] * alpha, f[5] * alpha),
+                         pack_bf16x2(f[6] * alpha, f[7] * alpha));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float* f = reinterpret_cast<const float*>(&v[4 * j]);
+            st_shared_v4(row_addr + ((uint32_t(j) ^ sw) << 4), __float_as_uint(f[0] * alpha),
+                         __float_as_uint(f[1] * alpha), __float_as_uint(f[2] * alpha), __float_as_uint(f[3] * alpha));
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (store) tma_store_2d(&p.map_c, buf, col, row0);
+          tma_store_commit();  // one group per chunk, empty or not, so wait_read<1> tracks buffers
+        }
+        ++nbuf;
+      }
+    }
+    if (lane == 0) tma_store_wait<0>();
+  }
+
+  // ------------------------------------------------------------------ teardown
+  __syncwarp();
+  tcgen05_fence_before();
+  if constexpr (CG == 2) {
+    cluster_sync();  // neither CTA frees TMEM or exits while the pair still signals it
+  } else {
+    __syncthreads();
+  }
+  if (warp == 1) {
+    tcgen05_fence_after();
+    tmem_dealloc<CG>(tmem_base, Cfg::kTmemCols);
+  }
+#endif  // KL_ARCH_SM100
+}
+
+#endif  // __CUDACC__
+
+}  // namespace kl::gemm

@@ -1,0 +1,152 @@
+/*
+ * kl_gemm.h — C ABI of the B200 dense-GEMM engine (libkl_b200.so).
+ *
+ * Plain pointers, sizes and status codes only, so any FFI (ctypes, cgo, JNI, N-API) can bind it.
+ * The reference (govindansriram/maia, kernel_lib) is a header-only C++20 library with no C ABI;
+ * each entry point below names the reference interface it exposes (file:line inside the
+ * reference project) or says that it has none.
+ *
+ * Memory: every pointer named "device" is CUDA device memory owned by the caller; the library
+ * keeps no pointer after a call returns. `stream` is a cudaStream_t (NULL = legacy default
+ * stream). GEMM launches are stream-ordered and asynchronous: they return once the kernel is
+ * queued. No entry point throws; failures return a kl_status and kl_last_error() describes the
+ * latest failure on the calling thread.
+ */
+#ifndef KL_GEMM_H_
+#define KL_GEMM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KL_API __attribute__((visibility("default")))
+#else
+#define KL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum kl_status {
+  KL_OK = 0,
+  KL_ERR_INVALID_ARGUMENT = 1, /* bad shape, stride, alignment or combination */
+  KL_ERR_NOT_SUPPORTED = 2,    /* valid request this build or device cannot run */
+  KL_ERR_CUDA = 3,             /* a CUDA runtime/driver call failed */
+  KL_ERR_TIMEOUT = 4,          /* a bounded device-side wait ran out (kl_read_status) */
+  KL_ERR_NCCL = 5              /* reserved for collective failures */
+} kl_status;
+
+typedef enum kl_dtype {
+  KL_BF16 = 0,
+  KL_F16 = 1,
+  KL_E4M3 = 2,
+  KL_E5M2 = 3,
+  KL_F32 = 4,
+  KL_I8 = 5,
+  KL_U8 = 6,
+  KL_I32 = 7
+} kl_dtype;
+
+typedef enum kl_algo {
+  KL_ALGO_AUTO = 0,
+  KL_ALGO_1CTA = 1,   /* 128 x 256 tile per CTA, cta_group::1 */
+  KL_ALGO_2CTA = 2,   /* 256 x 256 tile per CTA pair, cta_group::2 */
+  KL_ALGO_SKINNY = 3  /* memory-bound small-M path: weights stream once, K split over all SMs */
+} kl_algo;
+
+/* C[M,N] = alpha * (A[M,K] . B[N,K]^T) [* *scale_a * *scale_b].
+ * A and B are K-major (row-major with K contiguous), C is row-major. Leading dimensions are in
+ * elements; every base address must be 16-byte aligned and every row pitch a multiple of 16 bytes
+ * (TMA rules). */
+typedef struct kl_gemm_desc {
+  int64_t m, n, k;
+  const void* a; /* device, [m, lda] */
+  int64_t lda;
+  const void* b; /* device, [n, ldb] */
+  int64_t ldb;
+  void* c;       /* device, [m, ldc] */
+  int64_t ldc;
+  int32_t ab_type;        /* kl_dtype of A and B: KL_BF16 or KL_E4M3 */
+  int32_t c_type;         /* kl_dtype of C: KL_BF16 or KL_F32 */
+  float alpha;            /* host scalar */
+  const float* scale_a;   /* optional device scalar (NULL = 1): per-tensor dequant scale of A */
+  const float* scale_b;   /* optional device scalar (NULL = 1) */
+  int32_t algo;           /* kl_algo */
+  int32_t group_m;        /* tile-raster group height in tiles; 0 = library default */
+  int32_t max_ctas;       /* cap on resident CTAs; 0 = one per SM */
+  int32_t split_k;        /* KL_ALGO_SKINNY only: 0 = library default */
+} kl_gemm_desc;
+
+/* Library version: major * 10000 + minor * 100 + patch. */
+KL_API int32_t kl_version(void);
+
+/* Message of the latest failure on this thread ("" if none). */
+KL_API const char* kl_last_error(void);
+
+/* No reference counterpart: kernel_lib has descriptor builders only (layout/tma_desc.hpp,
+ * layout/umma_desc.hpp) and no GEMM. Queues one GEMM on `stream`. */
+KL_API kl_status kl_gemm(const kl_gemm_desc* desc, void* stream);
+
+/* No reference counterpart. Bytes of device workspace kl_gemm needs for `desc` (0 for every
+ * algorithm except KL_ALGO_SKINNY, which keeps fp32 partial sums). */
+KL_API kl_status kl_gemm_workspace_size(const kl_gemm_desc* desc, size_t* bytes);
+
+/* No reference counterpart. Like kl_gemm, with caller-provided device workspace (at least
+ * kl_gemm_workspace_size bytes, zero-filled before its first use; the kernel leaves it zeroed). */
+KL_API kl_status kl_gemm_ws(const kl_gemm_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Upper bound on any device-side wait, in nanoseconds (default 2e9). A wait that runs out sets a
+ * bit in the device status word instead of hanging the GPU. */
+KL_API void kl_set_wait_timeout_ns(uint64_t ns);
+
+/* Synchronises the current device, then returns KL_ERR_TIMEOUT if any kernel on it recorded a
+ * timed-out wait since the last clear (bits in *bits, may be NULL), else KL_OK. clear != 0 resets. */
+KL_API kl_status kl_read_status(int32_t* bits, int32_t clear);
+
+/* Launches a one-thread kernel that waits on an mbarrier nobody arrives on, with `timeout_ns` as
+ * its bound: the failure path of every kl wait, exercised without harming the GPU. The kernel
+ * records a timeout bit; read it back with kl_read_status. */
+KL_API kl_status kl_probe_wait_timeout(uint64_t timeout_ns, void* stream);
+
+/* ---- descriptor encoders (host, no GPU needed except kl_make_tma_desc) ---------------------- */
+
+/* Element offset of (row, col) in a rows x cols shared-memory tile of `elem_bytes`-byte elements,
+ * swizzled (`swizzled`) and before the swizzle (`plain`). swizzle_span: 16 (none), 32, 64, 128.
+ * kernel_lib/include/kl/layout/smem_tile.hpp:33-42 (smem_atom / smem_layout). */
+KL_API kl_status kl_smem_tile_offset(int32_t elem_bytes, int32_t rows, int32_t cols, int32_t swizzle_span, int32_t row,
+                              int32_t col, int64_t* swizzled, int64_t* plain);
+
+typedef struct kl_tma_box {
+  int32_t inner, outer, col_boxes, row_boxes, count, bytes;
+} kl_tma_box;
+
+/* TMA box geometry of a tile, and box i's (row, col, smem byte offset).
+ * kernel_lib/include/kl/layout/tma_desc.hpp:47-74 (TmaBox). */
+KL_API kl_status kl_tma_box_geometry(int32_t elem_bytes, int32_t rows, int32_t cols, int32_t swizzle_span, kl_tma_box* out);
+KL_API kl_status kl_tma_box_position(int32_t elem_bytes, int32_t rows, int32_t cols, int32_t swizzle_span, int32_t box,
+                              int32_t* row, int32_t* col, uint32_t* smem_offset);
+
+/* 64-bit UMMA shared-memory descriptor of K-slice `k_block`, rows from `row`, of a K-major tile at
+ * shared address `tile_addr`. kernel_lib/include/kl/layout/umma_desc.hpp:19-47
+ * (num_k_blocks, block_offset_16B, umma_desc). */
+KL_API kl_status kl_umma_smem_desc(int32_t elem_bytes, int32_t rows, int32_t cols, int32_t swizzle_span, uint32_t tile_addr,
+                            int32_t k_block, int32_t row, uint64_t* out);
+
+/* 32-bit tcgen05.mma instruction descriptor, both operands K-major. M = 64/128 (one CTA) or 256
+ * (CTA pair). kernel_lib/include/kl/layout/umma_desc.hpp:49-58 (mma_instr_desc, M <= 128 there). */
+KL_API kl_status kl_mma_instr_desc(int32_t a_type, int32_t b_type, int32_t acc_type, int32_t m, int32_t n, uint32_t* out);
+
+/* 128-byte TMA tensor map for a rank-`rank` row-major global tensor (shape/stride outermost
+ * first, in elements) moved in tiles of tile_rows x tile_cols with the given swizzle. Needs a CUDA
+ * driver (the encoding is the driver's). kernel_lib/include/kl/layout/tma_desc.hpp:100-164
+ * (make_tma_desc / make_tma_load / make_tma_store). Same validation and messages. */
+KL_API kl_status kl_make_tma_desc(int32_t dtype, int32_t tile_rows, int32_t tile_cols, int32_t swizzle_span, int32_t is_store,
+                           const void* gmem, int32_t rank, const int64_t* shape, const int64_t* stride,
+                           void* map_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KL_GEMM_H_ */

@@ -1,0 +1,227 @@
+"""Python binding of libkl_b200.so, the B200 dense-GEMM engine (C ABI in include/kl_gemm.h).
+
+Device memory, streams and the process group come from PyTorch; every GEMM runs in the library's
+own sm_100a kernels. There is no fallback: if the library is missing or a call fails, the error is
+raised.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libkl_b200.so"
+
+# kl_status
+KL_OK = 0
+KL_ERR_INVALID_ARGUMENT = 1
+KL_ERR_NOT_SUPPORTED = 2
+KL_ERR_CUDA = 3
+KL_ERR_TIMEOUT = 4
+KL_ERR_NCCL = 5
+
+# kl_dtype
+KL_BF16, KL_F16, KL_E4M3, KL_E5M2, KL_F32, KL_I8, KL_U8, KL_I32 = range(8)
+
+# kl_algo
+ALGO_AUTO, ALGO_1CTA, ALGO_2CTA, ALGO_SKINNY = range(4)
+
+EXPORTED = (
+    "kl_version", "kl_last_error", "kl_gemm", "kl_gemm_workspace_size", "kl_gemm_ws",
+    "kl_set_wait_timeout_ns", "kl_read_status", "kl_probe_wait_timeout", "kl_smem_tile_offset",
+    "kl_tma_box_geometry", "kl_tma_box_position", "kl_umma_smem_desc", "kl_mma_instr_desc",
+    "kl_make_tma_desc",
+)
+
+
+class KlError(RuntimeError):
+    """A kl_status other than KL_OK, with the library's message."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"kl status {status}: {message}")
+        self.status = status
+        self.message = message
+
+
+class GemmDesc(ctypes.Structure):
+    _fields_ = [
+        ("m", ctypes.c_int64), ("n", ctypes.c_int64), ("k", ctypes.c_int64),
+        ("a", ctypes.c_void_p), ("lda", ctypes.c_int64),
+        ("b", ctypes.c_void_p), ("ldb", ctypes.c_int64),
+        ("c", ctypes.c_void_p), ("ldc", ctypes.c_int64),
+        ("ab_type", ctypes.c_int32), ("c_type", ctypes.c_int32),
+        ("alpha", ctypes.c_float),
+        ("scale_a", ctypes.c_void_p), ("scale_b", ctypes.c_void_p),
+        ("algo", ctypes.c_int32), ("group_m", ctypes.c_int32),
+        ("max_ctas", ctypes.c_int32), ("split_k", ctypes.c_int32),
+    ]
+
+
+class TmaBox(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("inner", "outer", "col_boxes", "row_boxes", "count", "bytes")]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m maia_b200.build`")
+        L = ctypes.CDLL(str(LIB_PATH))
+        i32, i64, u32, u64, vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_void_p
+        P = ctypes.POINTER
+        sig = {
+            "kl_version": (i32, []),
+            "kl_last_error": (ctypes.c_char_p, []),
+            "kl_gemm": (i32, [P(GemmDesc), vp]),
+            "kl_gemm_workspace_size": (i32, [P(GemmDesc), P(ctypes.c_size_t)]),
+            "kl_gemm_ws": (i32, [P(GemmDesc), vp, ctypes.c_size_t, vp]),
+            "kl_set_wait_timeout_ns": (None, [u64]),
+            "kl_read_status": (i32, [P(i32), i32]),
+            "kl_probe_wait_timeout": (i32, [u64, vp]),
+            "kl_smem_tile_offset": (i32, [i32, i32, i32, i32, i32, i32, P(i64), P(i64)]),
+            "kl_tma_box_geometry": (i32, [i32, i32, i32, i32, P(TmaBox)]),
+            "kl_tma_box_position": (i32, [i32, i32, i32, i32, i32, P(i32), P(i32), P(u32)]),
+            "kl_umma_smem_desc": (i32, [i32, i32, i32, i32, u32, i32, i32, P(u64)]),
+            "kl_mma_instr_desc": (i32, [i32, i32, i32, i32, i32, P(u32)]),
+            "kl_make_tma_desc": (i32, [i32, i32, i32, i32, i32, vp, i32, P(i64), P(i64), vp]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().kl_last_error().decode()
+
+
+def check(status: int) -> None:
+    if status != KL_OK:
+        raise KlError(status, last_error())
+
+
+# ------------------------------------------------------------------------------------- encoders
+
+def smem_tile_offset(elem_bytes, rows, cols, span, row, col):
+    sw, pl = ctypes.c_int64(), ctypes.c_int64()
+    check(lib().kl_smem_tile_offset(elem_bytes, rows, cols, span, row, col, ctypes.byref(sw), ctypes.byref(pl)))
+    return sw.value, pl.value
+
+
+def tma_box_geometry(elem_bytes, rows, cols, span):
+    b = TmaBox()
+    check(lib().kl_tma_box_geometry(elem_bytes, rows, cols, span, ctypes.byref(b)))
+    return {f: getattr(b, f) for f, _ in TmaBox._fields_}
+
+
+def tma_box_position(elem_bytes, rows, cols, span, i):
+    r, c, o = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_uint32()
+    check(lib().kl_tma_box_position(elem_bytes, rows, cols, span, i, ctypes.byref(r), ctypes.byref(c), ctypes.byref(o)))
+    return r.value, c.value, o.value
+
+
+def umma_smem_desc(elem_bytes, rows, cols, span, tile_addr, k_block=0, row=0) -> int:
+    out = ctypes.c_uint64()
+    check(lib().kl_umma_smem_desc(elem_bytes, rows, cols, span, tile_addr, k_block, row, ctypes.byref(out)))
+    return out.value
+
+
+def mma_instr_desc(a_type, b_type, acc_type, m, n) -> int:
+    out = ctypes.c_uint32()
+    check(lib().kl_mma_instr_desc(a_type, b_type, acc_type, m, n, ctypes.byref(out)))
+    return out.value
+
+
+def make_tma_desc(dtype, tile_rows, tile_cols, span, ptr, shape, stride, is_store=False) -> bytes:
+    """128-byte tensor map (needs a CUDA driver)."""
+    rank = len(shape)
+    sh = (ctypes.c_int64 * rank)(*shape)
+    st = (ctypes.c_int64 * rank)(*stride)
+    buf = ctypes.create_string_buffer(128)
+    check(lib().kl_make_tma_desc(dtype, tile_rows, tile_cols, span, int(is_store), ctypes.c_void_p(ptr), rank, sh, st, buf))
+    return buf.raw
+
+
+# ------------------------------------------------------------------------------------- GEMM
+
+_TORCH_DTYPES = None
+
+
+def _dtype_code(t) -> int:
+    import torch
+
+    global _TORCH_DTYPES
+    if _TORCH_DTYPES is None:
+        _TORCH_DTYPES = {torch.bfloat16: KL_BF16, torch.float16: KL_F16, torch.float8_e4m3fn: KL_E4M3,
+                         torch.float8_e5m2: KL_E5M2, torch.float32: KL_F32, torch.int8: KL_I8,
+                         torch.uint8: KL_U8, torch.int32: KL_I32}
+    return _TORCH_DTYPES[t]
+
+
+def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, group_m=0, max_ctas=0,
+              split_k=0) -> GemmDesc:
+    """Descriptor for C = alpha * A . B^T on torch CUDA tensors (A [M,K], B [N,K], C [M,N])."""
+    for name, t in (("a", a), ("b", b), ("c", c)):
+        if t.dim() != 2 or t.stride(1) != 1:
+            raise ValueError(f"{name} must be a 2-D tensor with a contiguous last dimension")
+    m, k = a.shape
+    n = b.shape[0]
+    if b.shape[1] != k or tuple(c.shape) != (m, n):
+        raise ValueError(f"shape mismatch: a {tuple(a.shape)}, b {tuple(b.shape)}, c {tuple(c.shape)}")
+    return GemmDesc(m=m, n=n, k=k, a=a.data_ptr(), lda=a.stride(0), b=b.data_ptr(), ldb=b.stride(0),
+                    c=c.data_ptr(), ldc=c.stride(0), ab_type=_dtype_code(a.dtype), c_type=_dtype_code(c.dtype),
+                    alpha=float(alpha), scale_a=None if scale_a is None else scale_a.data_ptr(),
+                    scale_b=None if scale_b is None else scale_b.data_ptr(), algo=algo, group_m=group_m,
+                    max_ctas=max_ctas, split_k=split_k)
+
+
+def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
+         group_m=0, max_ctas=0, split_k=0, workspace=None, stream=None):
+    """out = alpha * a @ b.T [* scale_a * scale_b] on the current CUDA stream, via kl_gemm."""
+    import torch
+
+    if out is None:
+        out = torch.empty((a.shape[0], b.shape[0]), dtype=out_dtype or torch.bfloat16, device=a.device)
+    d = gemm_desc(a, b, out, alpha, scale_a, scale_b, algo, group_m, max_ctas, split_k)
+    s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
+    if workspace is None:
+        check(lib().kl_gemm(ctypes.byref(d), ctypes.c_void_p(s)))
+    else:
+        check(lib().kl_gemm_ws(ctypes.byref(d), ctypes.c_void_p(workspace.data_ptr()), workspace.numel() *
+                               workspace.element_size(), ctypes.c_void_p(s)))
+    return out
+
+
+def workspace_size(a, b, c, **kw) -> int:
+    d = gemm_desc(a, b, c, **kw)
+    n = ctypes.c_size_t()
+    check(lib().kl_gemm_workspace_size(ctypes.byref(d), ctypes.byref(n)))
+    return n.value
+
+
+def read_status(clear=True) -> int:
+    """Synchronise and return the device status bits (raises KlError on a recorded timeout)."""
+    bits = ctypes.c_int32()
+    st = lib().kl_read_status(ctypes.byref(bits), int(clear))
+    if st not in (KL_OK, KL_ERR_TIMEOUT):
+        check(st)
+    return bits.value
+
+
+def set_wait_timeout_ns(ns: int) -> None:
+    lib().kl_set_wait_timeout_ns(int(ns))
+
+
+def probe_wait_timeout(timeout_ns: int, stream=None) -> None:
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+    check(lib().kl_probe_wait_timeout(int(timeout_ns), ctypes.c_void_p(s)))

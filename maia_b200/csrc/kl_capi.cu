@@ -1,0 +1,318 @@
+// C ABI of libkl_b200.so (declared in include/kl_gemm.h): GEMM dispatch, device status word,
+// and the runtime forms of the kl descriptor encoders.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <exception>
+#include <stdexcept>
+#include <string>
+
+#include <kl/gemm/gemm.hpp>
+#include <kl/kl.hpp>
+#include <kl_gemm.h>
+
+#include "kl_internal.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+unsigned long long g_timeout_ns = 2000000000ull;
+
+}  // namespace
+
+// Timeout bits of every kl kernel on this device land here.
+__device__ int kl_device_status_word;
+
+namespace kl::capi {
+
+kl_status fail(kl_status s, std::string const& msg) {
+  g_last_error = msg;
+  return s;
+}
+
+kl_status cuda_fail(cudaError_t e, char const* where) {
+  return fail(KL_ERR_CUDA, std::string(where) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+
+unsigned long long wait_timeout_ns() { return g_timeout_ns; }
+
+kl_status device_status_ptr(int** out) {
+  static int* cache[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(KL_ERR_NOT_SUPPORTED, "device index above 63");
+  if (cache[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, kl_device_status_word);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status)");
+    cache[dev] = static_cast<int*>(p);
+  }
+  *out = cache[dev];
+  return KL_OK;
+}
+
+}  // namespace kl::capi
+
+using kl::capi::cuda_fail;
+using kl::capi::fail;
+
+namespace {
+
+using namespace kl::gemm;
+
+// The instantiated kernels: (inputs, output, CTA group, tile N, stages).
+using Bf16Bf16_1 = TnConfig<kl::bf16, kl::bf16, 1, 256, 4>;
+using Bf16F32_1 = TnConfig<kl::bf16, float, 1, 256, 4>;
+using E4m3Bf16_1 = TnConfig<kl::e4m3, kl::bf16, 1, 256, 4>;
+using Bf16Bf16_2 = TnConfig<kl::bf16, kl::bf16, 2, 256, 6>;
+using Bf16F32_2 = TnConfig<kl::bf16, float, 2, 256, 6>;
+using E4m3Bf16_2 = TnConfig<kl::e4m3, kl::bf16, 2, 256, 6>;
+
+template <class Cfg>
+kl_status run(Problem const& pr, cudaStream_t stream) {
+  int* status = nullptr;
+  kl_status s = kl::capi::device_status_ptr(&status);
+  if (s != KL_OK) return s;
+  cudaError_t e = launch_tn<Cfg>(pr, status, kl::capi::wait_timeout_ns(), stream);
+  if (e != cudaSuccess) return cuda_fail(e, "kl_gemm launch");
+  return KL_OK;
+}
+
+int elem_bytes_of(int32_t t) {
+  switch (t) {
+    case KL_BF16:
+    case KL_F16:
+      return 2;
+    case KL_E4M3:
+    case KL_E5M2:
+    case KL_I8:
+    case KL_U8:
+      return 1;
+    case KL_F32:
+    case KL_I32:
+      return 4;
+    default:
+      return 0;
+  }
+}
+
+kl_status check_tile(int32_t elem_bytes, int32_t rows, int32_t cols, int32_t span) {
+  if (elem_bytes != 1 && elem_bytes != 2 && elem_bytes != 4) return fail(KL_ERR_INVALID_ARGUMENT, "elem_bytes must be 1, 2 or 4");
+  if (span != 16 && span != 32 && span != 64 && span != 128)
+    return fail(KL_ERR_INVALID_ARGUMENT, "swizzle_span must be 16, 32, 64 or 128");
+  const int atom = span / elem_bytes;
+  if (rows <= 0 || rows % 8 != 0) return fail(KL_ERR_INVALID_ARGUMENT, "rows must be a positive multiple of 8");
+  if (cols <= 0 || cols % atom != 0) return fail(KL_ERR_INVALID_ARGUMENT, "cols must be a multiple of the swizzle atom width");
+  return KL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t kl_version(void) { return 100; }
+
+const char* kl_last_error(void) { return g_last_error.c_str(); }
+
+void kl_set_wait_timeout_ns(uint64_t ns) { g_timeout_ns = ns; }
+
+kl_status kl_gemm_workspace_size(const kl_gemm_desc* d, size_t* bytes) {
+  if (d == nullptr || bytes == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null argument");
+  *bytes = 0;
+  if (d->algo == KL_ALGO_SKINNY) return kl::capi::skinny_workspace_size(*d, bytes);
+  return KL_OK;
+}
+
+kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_bytes, void* stream_ptr) {
+  if (d == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null descriptor");
+  g_last_error.clear();
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (d->m < 0 || d->n < 0 || d->k < 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: negative extent");
+  if (d->m == 0 || d->n == 0) return KL_OK;
+  if (d->c == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: null C");
+  const int c_bytes = elem_bytes_of(d->c_type);
+  if (d->k == 0) {
+    // An empty sum: C = 0.
+    if (d->ldc < d->n) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: ldc < n");
+    cudaError_t e = cudaMemset2DAsync(d->c, size_t(d->ldc) * c_bytes, 0, size_t(d->n) * c_bytes, size_t(d->m), stream);
+    return e == cudaSuccess ? KL_OK : cuda_fail(e, "cudaMemset2DAsync");
+  }
+  if (d->a == nullptr || d->b == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: null A or B");
+
+  Problem pr;
+  pr.m = d->m;
+  pr.n = d->n;
+  pr.k = d->k;
+  pr.a = d->a;
+  pr.lda = d->lda;
+  pr.b = d->b;
+  pr.ldb = d->ldb;
+  pr.c = d->c;
+  pr.ldc = d->ldc;
+  pr.alpha = d->alpha;
+  pr.scale_a = d->scale_a;
+  pr.scale_b = d->scale_b;
+  pr.group_m = d->group_m;
+  pr.max_ctas = d->max_ctas;
+
+  int algo = d->algo;
+  if (algo == KL_ALGO_AUTO) algo = kl::capi::choose_algo(*d);
+  try {
+    if (algo == KL_ALGO_SKINNY) return kl::capi::run_skinny(*d, workspace, workspace_bytes, stream);
+    if (algo != KL_ALGO_1CTA && algo != KL_ALGO_2CTA) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: unknown algo");
+    const bool pair = algo == KL_ALGO_2CTA;
+    if (d->ab_type == KL_BF16 && d->c_type == KL_BF16)
+      return pair ? run<Bf16Bf16_2>(pr, stream) : run<Bf16Bf16_1>(pr, stream);
+    if (d->ab_type == KL_BF16 && d->c_type == KL_F32)
+      return pair ? run<Bf16F32_2>(pr, stream) : run<Bf16F32_1>(pr, stream);
+    if (d->ab_type == KL_E4M3 && d->c_type == KL_BF16)
+      return pair ? run<E4m3Bf16_2>(pr, stream) : run<E4m3Bf16_1>(pr, stream);
+    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: supported (A/B, C) types are (bf16, bf16), (bf16, f32), (e4m3, bf16)");
+  } catch (std::invalid_argument const& ex) {
+    return fail(KL_ERR_INVALID_ARGUMENT, ex.what());
+  } catch (std::exception const& ex) {
+    return fail(KL_ERR_CUDA, ex.what());
+  }
+}
+
+kl_status kl_gemm(const kl_gemm_desc* d, void* stream) { return kl_gemm_ws(d, nullptr, 0, stream); }
+
+kl_status kl_read_status(int32_t* bits, int32_t clear) {
+  int* status = nullptr;
+  kl_status s = kl::capi::device_status_ptr(&status);
+  if (s != KL_OK) return s;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  int v = 0;
+  e = cudaMemcpy(&v, status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status)");
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpy(status, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status clear)");
+  }
+  if (bits) *bits = v;
+  if (v != 0) return fail(KL_ERR_TIMEOUT, "a device-side wait timed out (status bits " + std::to_string(v) + ")");
+  return KL_OK;
+}
+
+kl_status kl_probe_wait_timeout(uint64_t timeout_ns, void* stream) {
+  int* status = nullptr;
+  kl_status s = kl::capi::device_status_ptr(&status);
+  if (s != KL_OK) return s;
+  return kl::capi::launch_wait_probe(status, timeout_ns, static_cast<cudaStream_t>(stream));
+}
+
+kl_status kl_smem_tile_offset(int32_t elem_bytes, int32_t rows, int32_t cols, int32_t span, int32_t row, int32_t col,
+                              int64_t* swizzled, int64_t* plain) {
+  kl_status s = check_tile(elem_bytes, rows, cols, span);
+  if (s != KL_OK) return s;
+  if (row < 0 || row >= rows || col < 0 || col >= cols) return fail(KL_ERR_INVALID_ARGUMENT, "(row, col) outside the tile");
+  int sw_bits = span == 128 ? 3 : span == 64 ? 2 : span == 32 ? 1 : 0;
+  const int atom = span / elem_bytes;
+  if (plain) *plain = kl::detail::tile_offset(rows, atom, row, col);
+  if (swizzled) *swizzled = kl::detail::swizzled_tile_offset(elem_bytes, rows, atom, sw_bits, row, col);
+  return KL_OK;
+}
+
+kl_status kl_tma_box_geometry(int32_t elem_bytes, int32_t rows, int32_t cols, int32_t span, kl_tma_box* out) {
+  kl_status s = check_tile(elem_bytes, rows, cols, span);
+  if (s != KL_OK) return s;
+  if (out == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null output");
+  const auto g = kl::tma_box_geometry(elem_bytes, rows, cols, span);
+  if (rows % g.outer != 0) return fail(KL_ERR_INVALID_ARGUMENT, "tiles taller than 256 rows must be a multiple of 256 rows");
+  *out = kl_tma_box{g.inner, g.outer, g.col_boxes, g.row_boxes, g.count, g.bytes};
+  return KL_OK;
+}
+
+kl_status kl_tma_box_position(int32_t elem_bytes, int32_t rows, int32_t cols, int32_t span, int32_t box, int32_t* row,
+                              int32_t* col, uint32_t* smem_offset) {
+  kl_tma_box geo;
+  kl_status s = kl_tma_box_geometry(elem_bytes, rows, cols, span, &geo);
+  if (s != KL_OK) return s;
+  if (box < 0 || box >= geo.count) return fail(KL_ERR_INVALID_ARGUMENT, "box index out of range");
+  const auto g = kl::tma_box_geometry(elem_bytes, rows, cols, span);
+  if (row) *row = g.row(box);
+  if (col) *col = g.col(box);
+  if (smem_offset) *smem_offset = g.smem_offset(box);
+  return KL_OK;
+}
+
+kl_status kl_umma_smem_desc(int32_t elem_bytes, int32_t rows, int32_t cols, int32_t span, uint32_t tile_addr,
+                            int32_t k_block, int32_t row, uint64_t* out) {
+  kl_status s = check_tile(elem_bytes, rows, cols, span);
+  if (s != KL_OK) return s;
+  if (out == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null output");
+  const int mma_k = 32 / elem_bytes;
+  if (cols % mma_k != 0) return fail(KL_ERR_INVALID_ARGUMENT, "tile K extent must be a multiple of the MMA K");
+  if (k_block < 0 || k_block >= cols / mma_k) return fail(KL_ERR_INVALID_ARGUMENT, "k_block out of range");
+  if (row < 0 || row % 8 != 0 || row >= rows) return fail(KL_ERR_INVALID_ARGUMENT, "row must be a multiple of 8 inside the tile");
+  *out = kl::detail::umma_desc_rt(tile_addr, elem_bytes, rows, span, k_block, row);
+  return KL_OK;
+}
+
+kl_status kl_mma_instr_desc(int32_t a_type, int32_t b_type, int32_t acc_type, int32_t m, int32_t n, uint32_t* out) {
+  if (out == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null output");
+  auto operand = [](int32_t t, int* kind) -> int {
+    switch (t) {
+      case KL_F16: *kind = 0; return 0;
+      case KL_BF16: *kind = 0; return 1;
+      case KL_F32: *kind = 1; return 2;  // tf32
+      case KL_E4M3: *kind = 2; return 0;
+      case KL_E5M2: *kind = 2; return 1;
+      case KL_U8: *kind = 3; return 0;
+      case KL_I8: *kind = 3; return 1;
+      default: return -1;
+    }
+  };
+  int ka = -1, kb = -1;
+  const int fa = operand(a_type, &ka), fb = operand(b_type, &kb);
+  if (fa < 0 || fb < 0) return fail(KL_ERR_INVALID_ARGUMENT, "no UMMA operand format for this type");
+  if (ka != kb) return fail(KL_ERR_INVALID_ARGUMENT, "A and B must belong to the same MMA kind");
+  int fc = acc_type == KL_F16 ? 0 : acc_type == KL_F32 ? 1 : acc_type == KL_I32 ? 2 : -1;
+  if (fc < 0) return fail(KL_ERR_INVALID_ARGUMENT, "no UMMA accumulator format for this type");
+  if (m != 64 && m != 128 && m != 256) return fail(KL_ERR_INVALID_ARGUMENT, "M must be 64, 128 or 256");
+  const int step = m == 64 ? 8 : 16;
+  if (n < step || n > 256 || n % step != 0) return fail(KL_ERR_INVALID_ARGUMENT, "N must be a multiple of 8 (M=64) or 16, at most 256");
+  *out = kl::detail::instr_desc_rt(uint32_t(fa), uint32_t(fb), uint32_t(fc), m, n);
+  return KL_OK;
+}
+
+kl_status kl_make_tma_desc(int32_t dtype, int32_t tile_rows, int32_t tile_cols, int32_t span, int32_t is_store,
+                           const void* gmem, int32_t rank, const int64_t* shape, const int64_t* stride, void* map_out) {
+  (void)is_store;  // loads and stores encode identically
+  const int eb = elem_bytes_of(dtype);
+  if (eb == 0) return fail(KL_ERR_INVALID_ARGUMENT, "unknown dtype");
+  kl_status s = check_tile(eb, tile_rows, tile_cols, span);
+  if (s != KL_OK) return s;
+  if (map_out == nullptr || shape == nullptr || stride == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null argument");
+  const auto g = kl::tma_box_geometry(eb, tile_rows, tile_cols, span);
+  if (tile_rows % g.outer != 0) return fail(KL_ERR_INVALID_ARGUMENT, "tiles taller than 256 rows must be a multiple of 256 rows");
+  CUtensorMapDataType t;
+  switch (dtype) {
+    case KL_BF16: t = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; break;
+    case KL_F16: t = CU_TENSOR_MAP_DATA_TYPE_FLOAT16; break;
+    case KL_F32: t = CU_TENSOR_MAP_DATA_TYPE_FLOAT32; break;
+    case KL_I32: t = CU_TENSOR_MAP_DATA_TYPE_INT32; break;
+    default: t = CU_TENSOR_MAP_DATA_TYPE_UINT8; break;
+  }
+  CUtensorMapSwizzle sw = span == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                        : span == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
+                        : span == 32  ? CU_TENSOR_MAP_SWIZZLE_32B
+                                      : CU_TENSOR_MAP_SWIZZLE_NONE;
+  try {
+    CUtensorMap map;
+    kl::detail::encode_tma_map(&map, t, eb, sw, uint32_t(g.inner), uint32_t(g.outer), gmem, rank, shape, stride,
+                               kl::TmaOptions{});
+    std::memcpy(map_out, &map, sizeof(CUtensorMap));
+  } catch (std::invalid_argument const& ex) {
+    return fail(KL_ERR_INVALID_ARGUMENT, ex.what());
+  }
+  return KL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,32 @@
+#pragma once
+
+// Shared between the translation units of libkl_b200.so; not part of the public ABI.
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <string>
+
+#include <kl_gemm.h>
+
+namespace kl::capi {
+
+// Record `msg` as this thread's last error and return `s`.
+kl_status fail(kl_status s, std::string const& msg);
+kl_status cuda_fail(cudaError_t e, char const* where);
+
+// Bound for every device-side wait, and the device status word those waits report into.
+unsigned long long wait_timeout_ns();
+kl_status device_status_ptr(int** out);
+
+// KL_ALGO_AUTO resolution.
+int choose_algo(kl_gemm_desc const& d);
+
+// Memory-bound small-M path (kl_skinny.cu).
+kl_status skinny_workspace_size(kl_gemm_desc const& d, size_t* bytes);
+kl_status run_skinny(kl_gemm_desc const& d, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+// Failure-path probe (kl_probe.cu).
+kl_status launch_wait_probe(int* status, unsigned long long timeout_ns, cudaStream_t stream);
+
+}  // namespace kl::capi

@@ -1,0 +1,124 @@
+"""The benchmark workloads of this GEMM engine, with seeded synthetic inputs.
+
+Each tensor comes from its own numpy PCG64 stream seeded ``seed * 1000 + tensor_id`` (A = 0,
+B = 1), drawn in row-major order as float32, then rounded to the input type:
+  * bf16: round-to-nearest-even of the float32 value;
+  * e4m3: per-tensor scale = amax / 448, q = RNE(x / scale) (|x / scale| <= 448, so no overflow).
+Inputs are returned as raw bits (uint16 / uint8 numpy arrays) so that the GPU and the CPU oracle
+see byte-identical operands.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+
+@dataclass(frozen=True)
+class Workload:
+    name: str
+    m: int
+    n: int
+    k: int
+    dtype: str          # "bf16" or "e4m3"
+    out: str            # "bf16" or "f32"
+    dist: str           # "uniform" (on [-1, 1]) or "normal"
+    a_scale: float      # multiplier of A's standard normal (normal) draws
+    b_scale: float
+    seed: int
+
+    @property
+    def flops(self) -> float:
+        return 2.0 * self.m * self.n * self.k
+
+    @property
+    def in_bytes(self) -> int:
+        return 2 if self.dtype == "bf16" else 1
+
+    @property
+    def out_bytes(self) -> int:
+        return 2 if self.out == "bf16" else 4
+
+    @property
+    def bytes(self) -> int:
+        """Algorithmic bytes: every matrix moved once."""
+        return (self.m * self.k + self.n * self.k) * self.in_bytes + self.m * self.n * self.out_bytes
+
+
+# C1..C5: the reference's GEMM contract at its benchmark shapes.
+C1 = Workload("c1_256_bf16_f32", 256, 256, 256, "bf16", "f32", "uniform", 1.0, 1.0, 0)
+C2 = Workload("c2_4096_bf16", 4096, 4096, 4096, "bf16", "bf16", "normal", 0.05, 0.05, 1)
+C3 = Workload("c3_8192_bf16", 8192, 8192, 8192, "bf16", "bf16", "normal", 0.02, 0.02, 2)
+C4 = Workload("c4_16384x16384x8192_e4m3", 16384, 16384, 8192, "e4m3", "bf16", "normal", 1.0, 1.0, 3)
+C5 = {m: Workload(f"c5_skinny_m{m}", m, 28672, 8192, "bf16", "bf16", "normal", 1.0, 0.02, 4) for m in (16, 64, 128)}
+
+ALL = {w.name: w for w in (C1, C2, C3, C4, *C5.values())}
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round float32 to bf16 (nearest, ties to even); returns the 16-bit patterns."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    rounding = ((u >> 16) & np.uint32(1)) + np.uint32(0x7FFF)
+    return ((u + rounding) >> 16).astype(np.uint16)
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+_E4M3_TABLE = None
+
+
+def e4m3_values() -> np.ndarray:
+    """The 256 e4m3 ("fn") values by bit pattern (NaN at 0x7F and 0xFF)."""
+    global _E4M3_TABLE
+    if _E4M3_TABLE is None:
+        v = np.arange(256)
+        sign = np.where(v & 0x80, -1.0, 1.0)
+        exp = (v >> 3) & 0xF
+        man = v & 7
+        mag = np.where(exp == 0, man / 8.0 * 2.0 ** -6, (1 + man / 8.0) * 2.0 ** (exp - 7.0))
+        vals = sign * mag
+        vals[(exp == 15) & (man == 7)] = np.nan
+        _E4M3_TABLE = vals
+    return _E4M3_TABLE
+
+
+def f32_to_e4m3_bits(x: np.ndarray) -> np.ndarray:
+    """Round to the nearest e4m3 value (ties to even mantissa), saturating at +-448."""
+    vals = e4m3_values()
+    pos = np.arange(0, 0x7F)  # non-negative finite patterns 0x00..0x7E, increasing in value
+    grid = vals[pos]
+    a = np.minimum(np.abs(np.asarray(x, dtype=np.float64)), 448.0)
+    idx = np.searchsorted(grid, a)  # grid[idx-1] < a <= grid[idx]
+    idx = np.clip(idx, 1, len(grid) - 1)
+    lo, hi = grid[idx - 1], grid[idx]
+    pick_hi = (a - lo > hi - a) | ((a - lo == hi - a) & (idx % 2 == 0))
+    q = np.where(pick_hi, idx, idx - 1).astype(np.uint8)
+    q = np.where(a == 0, 0, q).astype(np.uint8)
+    return np.where(np.signbit(x) & (q != 0), q | 0x80, q).astype(np.uint8)
+
+
+def draw(w: Workload, tensor_id: int, rows: int, cols: int, scale: float) -> np.ndarray:
+    rng = np.random.Generator(np.random.PCG64(w.seed * 1000 + tensor_id))
+    if w.dist == "uniform":
+        x = rng.random((rows, cols), dtype=np.float32) * np.float32(2.0) - np.float32(1.0)
+    else:
+        x = rng.standard_normal((rows, cols), dtype=np.float32)
+        if scale != 1.0:
+            x *= np.float32(scale)
+    return x
+
+
+def make_inputs(w: Workload, rows_a: int | None = None):
+    """(A bits, B bits, scale_a, scale_b). rows_a limits A to its first rows (a bounded CPU sample)."""
+    ra = w.m if rows_a is None else min(rows_a, w.m)
+    xa = draw(w, 0, w.m, w.k, w.a_scale)[:ra] if rows_a is not None else draw(w, 0, w.m, w.k, w.a_scale)
+    xb = draw(w, 1, w.n, w.k, w.b_scale)
+    if w.dtype == "bf16":
+        return f32_to_bf16_bits(xa), f32_to_bf16_bits(xb), 1.0, 1.0
+    # fp8: per-tensor scales from the full tensors' amax.
+    sa = float(np.abs(draw(w, 0, w.m, w.k, w.a_scale)).max()) / 448.0 if rows_a is not None else float(np.abs(xa).max()) / 448.0
+    sb = float(np.abs(xb).max()) / 448.0
+    return f32_to_e4m3_bits(xa / np.float32(sa)), f32_to_e4m3_bits(xb / np.float32(sb)), sa, sb

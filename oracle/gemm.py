@@ -1,0 +1,100 @@
+"""ctypes binding of libkl_oracle.so (gemm_oracle.c). TEST INFRASTRUCTURE ONLY.
+
+Inputs are raw element bits as numpy arrays: uint16 for bf16, uint8 for e4m3, row-major with the
+given leading dimension.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libkl_oracle.so"
+BF16, E4M3 = 0, 2
+_lib = None
+
+
+def build() -> Path:
+    src = HERE / "gemm_oracle.c"
+    if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+        subprocess.run(["make", "-C", str(HERE), "libkl_oracle.so"], check=True, capture_output=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(str(LIB_PATH))
+        vp, i64, i32, dbl = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_double
+        L.kl_oracle_gemm_f64.argtypes = [i32, vp, i64, vp, i64, i64, i64, i64, dbl, vp, i64, i32]
+        L.kl_oracle_gemm_f64.restype = i32
+        L.kl_oracle_gemm_f32.argtypes = [i32, vp, i64, vp, i64, i64, i64, i64, dbl, vp, i64, i32]
+        L.kl_oracle_gemm_f32.restype = i32
+        L.kl_oracle_decode.argtypes = [i32, vp, i64, vp]
+        L.kl_oracle_decode.restype = None
+        _lib = L
+    return _lib
+
+
+def _kind(a: np.ndarray) -> int:
+    if a.dtype == np.uint16:
+        return BF16
+    if a.dtype == np.uint8:
+        return E4M3
+    raise TypeError("inputs are raw bits: uint16 (bf16) or uint8 (e4m3)")
+
+
+def threads_default() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+def decode(bits: np.ndarray) -> np.ndarray:
+    bits = np.ascontiguousarray(bits)
+    out = np.empty(bits.shape, dtype=np.float64)
+    lib().kl_oracle_decode(_kind(bits), bits.ctypes.data, bits.size, out.ctypes.data)
+    return out
+
+
+def gemm_f64(a: np.ndarray, b: np.ndarray, scale: float = 1.0, threads: int | None = None) -> np.ndarray:
+    """scale * A . B^T with fp64 accumulation; A [M,K], B [N,K] raw bits."""
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    assert a.dtype == b.dtype and a.shape[1] == b.shape[1]
+    m, k = a.shape
+    n = b.shape[0]
+    c = np.empty((m, n), dtype=np.float64)
+    rc = lib().kl_oracle_gemm_f64(_kind(a), a.ctypes.data, k, b.ctypes.data, k, m, n, k, float(scale),
+                                  c.ctypes.data, n, threads or threads_default())
+    assert rc == 0
+    return c
+
+
+def gemm_f32(a: np.ndarray, b: np.ndarray, scale: float = 1.0, threads: int | None = None) -> np.ndarray:
+    """scale * A . B^T with fp32 accumulation (the timed CPU baseline)."""
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    m, k = a.shape
+    n = b.shape[0]
+    c = np.empty((m, n), dtype=np.float32)
+    rc = lib().kl_oracle_gemm_f32(_kind(a), a.ctypes.data, k, b.ctypes.data, k, m, n, k, float(scale),
+                                  c.ctypes.data, n, threads or threads_default())
+    assert rc == 0
+    return c
+
+
+def rel_error(c: np.ndarray, ref: np.ndarray) -> tuple[float, float]:
+    """(element-wise max of |c - r| / max(|r|, 1e-3 * rms(r)), normwise max|c - r| / max|r|)."""
+    c = np.asarray(c, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    diff = np.abs(c - ref)
+    rms = float(np.sqrt(np.mean(ref * ref))) if ref.size else 0.0
+    floor = max(1e-3 * rms, 1e-30)
+    elem = float(np.max(diff / np.maximum(np.abs(ref), floor))) if ref.size else 0.0
+    norm = float(diff.max() / max(np.abs(ref).max(), 1e-30)) if ref.size else 0.0
+    return elem, norm

@@ -1,0 +1,194 @@
+/*
+ * CPU oracle for the GEMM path — TEST INFRASTRUCTURE ONLY. Only tests/, __graft_entry__.smoke()
+ * and bench.py's CPU-baseline leg may load this library; the product never calls it.
+ *
+ * What it restates. The reference (govindansriram/maia, kernel_lib) ships the descriptor encoders
+ * for a Blackwell GEMM but no GEMM and no CPU GEMM of its own; its GEMM contract is the one
+ * the descriptors encode: C = A . B^T with A [M,K] and B [N,K] both K-major
+ * (kernel_lib/include/kl/layout/umma_desc.hpp:49-58, a_major = b_major = K;
+ * kernel_lib/include/kl/layout/smem_tile.hpp:44-47, "MMA operands are (M or N, K), so they are
+ * K-major"), bf16 or fp8 inputs, fp32 accumulation. GEMM parity is therefore unpinned against the
+ * reference: there is no reference GEMM output to pin to. The tests pin this file instead against
+ * numpy float64 matmul on the same decoded inputs.
+ *
+ *   kl_oracle_gemm_f64   fp64 accumulation over the decoded inputs, times `scale`: the checker.
+ *   kl_oracle_gemm_f32   fp32 accumulation, cache-blocked, all host threads: the timed CPU
+ *                        baseline (the "CPU reference GEMM" of the benchmark's smallest config).
+ *   kl_oracle_decode     element decoders (bf16, e4m3), exposed so tests can check them.
+ *
+ * Element decoding follows the formats' definitions: bf16 is the top half of an IEEE binary32;
+ * e4m3 (OCP FP8, "fn" variant) has 1 sign, 4 exponent (bias 7), 3 mantissa bits, no infinities,
+ * and S.1111.111 is NaN.
+ */
+#include <math.h>
+#include <pthread.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define KL_ORACLE_BF16 0
+#define KL_ORACLE_E4M3 2
+
+static double decode_bf16(uint16_t h) {
+  uint32_t bits = (uint32_t)h << 16;
+  float f;
+  memcpy(&f, &bits, sizeof f);
+  return (double)f;
+}
+
+static double decode_e4m3(uint8_t v) {
+  const int sign = (v >> 7) & 1;
+  const int exp = (v >> 3) & 0xF;
+  const int man = v & 0x7;
+  double x;
+  if (exp == 0xF && man == 0x7) return NAN;
+  if (exp == 0)
+    x = ldexp((double)man / 8.0, -6); /* subnormal: 0.mmm * 2^(1-7) */
+  else
+    x = ldexp(1.0 + (double)man / 8.0, exp - 7);
+  return sign ? -x : x;
+}
+
+/* Decode `n` elements of type `t` (KL_ORACLE_BF16 / KL_ORACLE_E4M3) to double. */
+void kl_oracle_decode(int t, const void* src, int64_t n, double* dst) {
+  if (t == KL_ORACLE_BF16) {
+    const uint16_t* s = (const uint16_t*)src;
+    for (int64_t i = 0; i < n; ++i) dst[i] = decode_bf16(s[i]);
+  } else {
+    const uint8_t* s = (const uint8_t*)src;
+    for (int64_t i = 0; i < n; ++i) dst[i] = decode_e4m3(s[i]);
+  }
+}
+
+typedef struct {
+  int t;
+  const void* a;
+  int64_t lda;
+  const void* b;
+  int64_t ldb;
+  int64_t m, n, k;
+  double scale;
+  void* c;
+  int64_t ldc;
+  int64_t row_begin, row_end;
+  const double* bdec; /* decoded B, n x k (f64 path) */
+  const float* bdecf; /* decoded B, n x k (f32 path) */
+} job_t;
+
+static void* f64_rows(void* arg) {
+  job_t* j = (job_t*)arg;
+  double* arow = (double*)malloc(sizeof(double) * (size_t)j->k);
+  double* c = (double*)j->c;
+  const int esz = j->t == KL_ORACLE_BF16 ? 2 : 1;
+  for (int64_t i = j->row_begin; i < j->row_end; ++i) {
+    kl_oracle_decode(j->t, (const char*)j->a + (size_t)(i * j->lda) * esz, j->k, arow);
+    for (int64_t col = 0; col < j->n; ++col) {
+      const double* brow = j->bdec + (size_t)col * (size_t)j->k;
+      double s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+      int64_t kk = 0;
+      for (; kk + 4 <= j->k; kk += 4) {
+        s0 += arow[kk] * brow[kk];
+        s1 += arow[kk + 1] * brow[kk + 1];
+        s2 += arow[kk + 2] * brow[kk + 2];
+        s3 += arow[kk + 3] * brow[kk + 3];
+      }
+      for (; kk < j->k; ++kk) s0 += arow[kk] * brow[kk];
+      c[(size_t)(i * j->ldc + col)] = ((s0 + s1) + (s2 + s3)) * j->scale;
+    }
+  }
+  free(arow);
+  return NULL;
+}
+
+static int clamp_threads(int threads, int64_t rows) {
+  if (threads < 1) threads = 1;
+  if (threads > 512) threads = 512;
+  if (rows < threads) threads = (int)(rows > 0 ? rows : 1);
+  return threads;
+}
+
+/* c[i*ldc + j] = scale * sum_k A[i,k] * B[j,k] in double, for rows [0, m). Returns 0 on success. */
+int kl_oracle_gemm_f64(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                       int64_t k, double scale, double* c, int64_t ldc, int threads) {
+  const int esz = t == KL_ORACLE_BF16 ? 2 : 1;
+  double* bdec = (double*)malloc(sizeof(double) * (size_t)n * (size_t)(k > 0 ? k : 1));
+  if (!bdec) return 1;
+  for (int64_t r = 0; r < n; ++r) kl_oracle_decode(t, (const char*)b + (size_t)(r * ldb) * esz, k, bdec + r * k);
+  threads = clamp_threads(threads, m);
+  pthread_t tid[512];
+  job_t jobs[512];
+  for (int w = 0; w < threads; ++w) {
+    job_t j = {t, a, lda, b, ldb, m, n, k, scale, c, ldc, m * w / threads, m * (w + 1) / threads, bdec, NULL};
+    jobs[w] = j;
+    pthread_create(&tid[w], NULL, f64_rows, &jobs[w]);
+  }
+  for (int w = 0; w < threads; ++w) pthread_join(tid[w], NULL);
+  free(bdec);
+  return 0;
+}
+
+/* fp32-accumulate baseline. Blocks of 4 rows of A against 4 rows of B, K in chunks that stay in
+ * L1/L2, 8 independent fp32 partial sums per dot so the compiler can vectorise. */
+#define KB 512
+static void* f32_rows(void* arg) {
+  job_t* j = (job_t*)arg;
+  const int esz = j->t == KL_ORACLE_BF16 ? 2 : 1;
+  const int64_t k = j->k;
+  float* c = (float*)j->c;
+  float* ablk = (float*)malloc(sizeof(float) * 4 * (size_t)k);
+  double* tmp = (double*)malloc(sizeof(double) * (size_t)k);
+  for (int64_t i0 = j->row_begin; i0 < j->row_end; i0 += 4) {
+    const int64_t ni = (j->row_end - i0) < 4 ? (j->row_end - i0) : 4;
+    for (int64_t r = 0; r < ni; ++r) {
+      kl_oracle_decode(j->t, (const char*)j->a + (size_t)((i0 + r) * j->lda) * esz, k, tmp);
+      for (int64_t kk = 0; kk < k; ++kk) ablk[r * k + kk] = (float)tmp[kk];
+    }
+    for (int64_t r = ni; r < 4; ++r) memset(ablk + r * k, 0, sizeof(float) * (size_t)k);
+    for (int64_t col = 0; col < j->n; ++col) {
+      const float* brow = j->bdecf + (size_t)col * (size_t)k;
+      float acc[4][8];
+      memset(acc, 0, sizeof acc);
+      int64_t kk = 0;
+      for (; kk + 8 <= k; kk += 8)
+        for (int r = 0; r < 4; ++r)
+          for (int v = 0; v < 8; ++v) acc[r][v] += ablk[r * k + kk + v] * brow[kk + v];
+      for (int r = 0; r < ni; ++r) {
+        float s = 0.f;
+        for (int v = 0; v < 8; ++v) s += acc[r][v];
+        for (int64_t q = kk; q < k; ++q) s += ablk[r * k + q] * brow[q];
+        c[(size_t)((i0 + r) * j->ldc + col)] = s * (float)j->scale;
+      }
+    }
+  }
+  free(ablk);
+  free(tmp);
+  return NULL;
+}
+
+int kl_oracle_gemm_f32(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                       int64_t k, double scale, float* c, int64_t ldc, int threads) {
+  const int esz = t == KL_ORACLE_BF16 ? 2 : 1;
+  float* bdec = (float*)malloc(sizeof(float) * (size_t)n * (size_t)(k > 0 ? k : 1));
+  double* tmp = (double*)malloc(sizeof(double) * (size_t)(k > 0 ? k : 1));
+  if (!bdec || !tmp) return 1;
+  for (int64_t r = 0; r < n; ++r) {
+    kl_oracle_decode(t, (const char*)b + (size_t)(r * ldb) * esz, k, tmp);
+    for (int64_t kk = 0; kk < k; ++kk) bdec[r * k + kk] = (float)tmp[kk];
+  }
+  free(tmp);
+  threads = clamp_threads(threads, m);
+  pthread_t tid[512];
+  job_t jobs[512];
+  for (int w = 0; w < threads; ++w) {
+    /* Split rows in multiples of 4 so blocks never straddle workers. */
+    int64_t b0 = ((m + 3) / 4) * w / threads * 4, b1 = ((m + 3) / 4) * (w + 1) / threads * 4;
+    if (b1 > m) b1 = m;
+    if (b0 > m) b0 = m;
+    job_t j = {t, a, lda, b, ldb, m, n, k, scale, c, ldc, b0, b1, NULL, bdec};
+    jobs[w] = j;
+    pthread_create(&tid[w], NULL, f32_rows, &jobs[w]);
+  }
+  for (int w = 0; w < threads; ++w) pthread_join(tid[w], NULL);
+  free(bdec);
+  return 0;
+}

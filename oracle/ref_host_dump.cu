@@ -1,0 +1,162 @@
+// Reference descriptor tables, computed by the reference's OWN headers (kernel_lib/include/kl)
+// compiled against CUTLASS/CuTe 4.5.0. TEST INFRASTRUCTURE ONLY: built by oracle/Makefile into
+// oracle/_ref/ref_host_dump from the sources under the reference checkout; its JSON output is
+// committed as tests/golden/ref_host_tables.json by tests/golden/gen_golden.py.
+//
+// Host-only parts: smem layouts (kernel_lib/include/kl/layout/smem_tile.hpp:33-76), TmaBox
+// (kernel_lib/include/kl/layout/tma_desc.hpp:47-74), block_offset_16B and the UMMA smem descriptor
+// body of kl::umma_desc evaluated at shared address 0 (kernel_lib/include/kl/layout/umma_desc.hpp:
+// 24-47; CuTe's host path of cast_smem_ptr_to_uint yields 0), and mma_instr_desc
+// (kernel_lib/include/kl/layout/umma_desc.hpp:51-58). Instruction descriptors the reference rejects
+// (M = 256) come from CuTe's make_instr_desc directly and are tagged "cute".
+#include <cstdint>
+#include <cstdio>
+#include <string>
+#include <vector>
+
+#include <kl/kl.hpp>
+
+namespace {
+
+FILE* out = nullptr;
+bool first_entry = true;
+
+void begin_entry() {
+  std::fprintf(out, first_entry ? "\n" : ",\n");
+  first_entry = false;
+}
+
+template <typename T>
+const char* tname();
+template <> const char* tname<kl::bf16>() { return "bf16"; }
+template <> const char* tname<kl::f16>() { return "f16"; }
+template <> const char* tname<float>() { return "f32"; }
+template <> const char* tname<int8_t>() { return "i8"; }
+template <> const char* tname<kl::e4m3>() { return "e4m3"; }
+
+template <typename Tile>
+void dump_tile() {
+  using T = typename Tile::value_type;
+  using Box = kl::TmaBox<Tile>;
+  begin_entry();
+  std::fprintf(out, "{\"kind\": \"tile\", \"type\": \"%s\", \"rows\": %d, \"cols\": %d, \"swizzle\": %d, ", tname<T>(),
+               Tile::rows, Tile::cols, Tile::swizzle::bytes);
+  std::fprintf(out, "\"bytes\": %d, \"alignment\": %d, \"atom_elems\": %d, ", Tile::bytes, Tile::alignment,
+               Tile::atom_elems);
+  // Layout offsets, as layout_type{}(r, c) and as element distance through tile.tensor() on a
+  // 1 KB-aligned host tile (where the swizzle of the pointer's address bits applies).
+  alignas(1024) static unsigned char storage[1 << 20];
+  Tile& tile = *reinterpret_cast<Tile*>(storage);
+  auto L = typename Tile::layout_type{};
+  auto inner = L.layout_b();
+  std::fprintf(out, "\"layout\": [");
+  for (int r = 0; r < Tile::rows; ++r)
+    for (int c = 0; c < Tile::cols; ++c) std::fprintf(out, "%s%lld", (r | c) ? "," : "", (long long)L(r, c));
+  std::fprintf(out, "], \"layout_b\": [");
+  for (int r = 0; r < Tile::rows; ++r)
+    for (int c = 0; c < Tile::cols; ++c) std::fprintf(out, "%s%lld", (r | c) ? "," : "", (long long)inner(r, c));
+  std::fprintf(out, "], \"tensor\": [");
+  auto t = tile.tensor();
+  for (int r = 0; r < Tile::rows; ++r)
+    for (int c = 0; c < Tile::cols; ++c)
+      std::fprintf(out, "%s%lld", (r | c) ? "," : "", (long long)(&t(r, c) - tile.data()));
+  std::fprintf(out, "], ");
+  std::fprintf(out, "\"box\": {\"inner\": %d, \"outer\": %d, \"col_boxes\": %d, \"row_boxes\": %d, \"count\": %d, \"bytes\": %d, \"pos\": [",
+               Box::inner, Box::outer, Box::col_boxes, Box::row_boxes, Box::count, Box::bytes);
+  for (int i = 0; i < Box::count; ++i)
+    std::fprintf(out, "%s[%d, %d, %u]", i ? "," : "", Box::row(i), Box::col(i), Box::smem_offset(i));
+  std::fprintf(out, "]}");
+  if constexpr (Tile::cols % kl::mma_k<T> == 0) {
+    constexpr int nk = kl::num_k_blocks<Tile>;
+    std::fprintf(out, ", \"num_k_blocks\": %d, \"block_offset_16B\": [", nk);
+    bool f = true;
+    for (int row = 0; row < Tile::rows; row += 8)
+      for (int k = 0; k < nk; ++k) {
+        std::fprintf(out, "%s[%d, %d, %u]", f ? "" : ",", row, k, kl::block_offset_16B<Tile>(k, row));
+        f = false;
+      }
+    std::fprintf(out, "], \"umma_desc_base0\": [");
+    // kl::umma_desc's body (umma_desc.hpp:40-45) on the host: CuTe's descriptor of the first
+    // (Rows x mma_k) slice, then the 32-bit add of block_offset_16B.
+    f = true;
+    for (int row = 0; row < Tile::rows; row += 8)
+      for (int k = 0; k < nk; ++k) {
+        auto first = cute::local_tile(tile.tensor(), cute::Shape<cute::Int<Tile::rows>, cute::Int<kl::mma_k<T>>>{},
+                                      cute::make_coord(0, 0));
+        kl::SmemDesc desc = cute::UMMA::make_umma_desc<cute::UMMA::Major::K>(first);
+        desc.lo += kl::block_offset_16B<Tile>(k, row);
+        std::fprintf(out, "%s[%d, %d, \"0x%016llx\"]", f ? "" : ",", row, k, (unsigned long long)desc.desc_);
+        f = false;
+      }
+    std::fprintf(out, "]");
+  }
+  std::fprintf(out, "}");
+}
+
+template <typename A, typename B, typename Acc, int M, int N>
+void dump_idesc_ref() {
+  begin_entry();
+  std::fprintf(out, "{\"kind\": \"idesc\", \"a\": \"%s\", \"b\": \"%s\", \"acc\": \"%s\", \"m\": %d, \"n\": %d, \"source\": \"kl\", \"value\": \"0x%08x\"}",
+               tname<A>(), tname<B>(), tname<Acc>(), M, N, (unsigned)kl::mma_instr_desc<A, B, Acc, M, N>());
+}
+
+template <typename A, typename B, typename Acc, int M, int N>
+void dump_idesc_cute() {
+  begin_entry();
+  auto d = cute::UMMA::make_instr_desc<A, B, Acc, M, N, cute::UMMA::Major::K, cute::UMMA::Major::K>();
+  std::fprintf(out, "{\"kind\": \"idesc\", \"a\": \"%s\", \"b\": \"%s\", \"acc\": \"%s\", \"m\": %d, \"n\": %d, \"source\": \"cute\", \"value\": \"0x%08x\"}",
+               tname<A>(), tname<B>(), tname<Acc>(), M, N, (unsigned)d.desc_);
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  if (argc < 2) {
+    std::fprintf(stderr, "usage: %s out.json\n", argv[0]);
+    return 2;
+  }
+  out = std::fopen(argv[1], "w");
+  if (!out) return 1;
+  std::fprintf(out, "[");
+  using kl::SmemTile;
+  dump_tile<SmemTile<kl::bf16, 128, 64>>();
+  dump_tile<SmemTile<kl::bf16, 256, 64>>();
+  dump_tile<SmemTile<kl::bf16, 128, 128>>();
+  dump_tile<SmemTile<kl::bf16, 512, 64>>();
+  dump_tile<SmemTile<kl::bf16, 512, 128>>();
+  dump_tile<SmemTile<kl::bf16, 128, 64, kl::Swizzle64B>>();
+  dump_tile<SmemTile<kl::bf16, 256, 64, kl::Swizzle64B>>();
+  dump_tile<SmemTile<kl::bf16, 128, 32, kl::Swizzle64B>>();
+  dump_tile<SmemTile<kl::bf16, 128, 32, kl::Swizzle32B>>();
+  dump_tile<SmemTile<kl::bf16, 128, 16, kl::Swizzle32B>>();
+  dump_tile<SmemTile<kl::bf16, 128, 8, kl::SwizzleNone>>();
+  dump_tile<SmemTile<kl::bf16, 128, 16, kl::SwizzleNone>>();
+  dump_tile<SmemTile<kl::bf16, 32, 64>>();
+  dump_tile<SmemTile<kl::f16, 128, 64>>();
+  dump_tile<SmemTile<int8_t, 128, 128>>();
+  dump_tile<SmemTile<int8_t, 256, 128>>();
+  dump_tile<SmemTile<kl::e4m3, 128, 128>>();
+  dump_tile<SmemTile<kl::e4m3, 256, 128>>();
+  dump_tile<SmemTile<float, 128, 32>>();
+  dump_tile<SmemTile<float, 32, 32>>();
+  dump_tile<SmemTile<float, 64, 32, kl::Swizzle64B>>();
+
+  dump_idesc_ref<kl::bf16, kl::bf16, float, 128, 256>();
+  dump_idesc_ref<kl::bf16, kl::bf16, float, 128, 128>();
+  dump_idesc_ref<kl::bf16, kl::bf16, float, 128, 16>();
+  dump_idesc_ref<kl::bf16, kl::bf16, float, 128, 64>();
+  dump_idesc_ref<kl::bf16, kl::bf16, float, 64, 8>();
+  dump_idesc_ref<kl::bf16, kl::bf16, float, 64, 256>();
+  dump_idesc_ref<kl::f16, kl::f16, float, 128, 256>();
+  dump_idesc_ref<kl::f16, kl::f16, kl::f16, 128, 128>();
+  dump_idesc_ref<kl::e4m3, kl::e4m3, float, 128, 256>();
+  dump_idesc_ref<kl::e4m3, kl::e4m3, float, 128, 128>();
+  dump_idesc_ref<kl::e4m3, kl::e4m3, float, 64, 64>();
+  dump_idesc_cute<kl::bf16, kl::bf16, float, 256, 256>();
+  dump_idesc_cute<kl::bf16, kl::bf16, float, 256, 128>();
+  dump_idesc_cute<kl::e4m3, kl::e4m3, float, 256, 256>();
+  dump_idesc_cute<kl::f16, kl::f16, float, 256, 64>();
+  std::fprintf(out, "\n]\n");
+  std::fclose(out);
+  return 0;
+}

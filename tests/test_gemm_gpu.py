@@ -1,0 +1,120 @@
+"""GEMM parity on the GPU: libkl_b200.so through its C ABI against the fp64 CPU oracle.
+
+Tolerances (max element-wise relative error against fp64 accumulation of the same rounded
+inputs, floor 1e-3 * rms): 1e-2 for bf16 inputs, 5e-2 for e4m3 inputs.
+"""
+
+import numpy as np
+import pytest
+
+import maia_b200 as kl
+from maia_b200 import workloads as wl
+
+from gpu_util import check, random_inputs, run_kl
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 1e-2
+FP8_TOL = 5e-2
+
+
+@pytest.mark.parametrize("algo", [kl.ALGO_1CTA, kl.ALGO_2CTA], ids=["1cta", "2cta"])
+def test_c1_256_bf16_f32(cuda, algo):
+    a, b, _, _ = wl.make_inputs(wl.C1)
+    c = run_kl(a, b, "bf16", "f32", cuda, algo)
+    _, norm = check(c, a, b, 1.0, BF16_TOL)
+    assert norm < 1e-5  # fp32 output: only accumulation-order differences remain
+
+
+@pytest.mark.parametrize("algo", [kl.ALGO_1CTA, kl.ALGO_2CTA], ids=["1cta", "2cta"])
+def test_c2_4096_bf16(cuda, algo):
+    a, b, _, _ = wl.make_inputs(wl.C2)
+    c = run_kl(a, b, "bf16", "bf16", cuda, algo)
+    check(c, a, b, 1.0, BF16_TOL)
+
+
+RAGGED = [(1, 8, 8), (8, 16, 64), (130, 264, 200), (200, 136, 72), (257, 520, 136), (384, 512, 1024), (1000, 1000, 1000)]
+
+
+@pytest.mark.parametrize("algo", [kl.ALGO_1CTA, kl.ALGO_2CTA], ids=["1cta", "2cta"])
+@pytest.mark.parametrize("shape", RAGGED)
+def test_ragged_bf16(cuda, algo, shape):
+    m, n, k = shape
+    a, b, _, _ = random_inputs(m, n, k, "bf16", seed=m * 7 + n * 3 + k)
+    check(run_kl(a, b, "bf16", "bf16", cuda, algo), a, b, 1.0, BF16_TOL)
+    check(run_kl(a, b, "bf16", "f32", cuda, algo), a, b, 1.0, BF16_TOL)
+
+
+@pytest.mark.parametrize("algo", [kl.ALGO_1CTA, kl.ALGO_2CTA], ids=["1cta", "2cta"])
+@pytest.mark.parametrize("shape", [(256, 256, 256), (512, 768, 1024), (300, 200, 160)])
+def test_e4m3_scaled(cuda, algo, shape):
+    m, n, k = shape
+    a, b, sa, sb = random_inputs(m, n, k, "e4m3", seed=11 + m)
+    c = run_kl(a, b, "e4m3", "bf16", cuda, algo, scale_a=sa, scale_b=sb)
+    check(c, a, b, sa * sb, FP8_TOL)
+
+
+@pytest.mark.parametrize("algo", [kl.ALGO_1CTA, kl.ALGO_2CTA], ids=["1cta", "2cta"])
+def test_persistent_few_ctas(cuda, algo):
+    """More tiles than CTAs: every CTA loops over several tiles and both TMEM accumulators."""
+    a, b, _, _ = random_inputs(1024, 2048, 512, "bf16", seed=5)
+    c = run_kl(a, b, "bf16", "bf16", cuda, algo, max_ctas=6, group_m=3)
+    check(c, a, b, 1.0, BF16_TOL)
+
+
+def test_strided_operands(cuda):
+    """Leading dimensions larger than the extents (padded rows) on A, B and C."""
+    import torch
+
+    m, n, k = 384, 256, 320
+    a_bits, b_bits, _, _ = random_inputs(m, n, k, "bf16", seed=9)
+    from gpu_util import to_device
+
+    a_full = torch.zeros((m, k + 64), dtype=torch.bfloat16, device=cuda)
+    b_full = torch.zeros((n, k + 32), dtype=torch.bfloat16, device=cuda)
+    a_full[:, :k] = to_device(a_bits, "bf16", cuda)
+    b_full[:, :k] = to_device(b_bits, "bf16", cuda)
+    c_full = torch.full((m, n + 24), 7.0, dtype=torch.bfloat16, device=cuda)
+    kl.gemm(a_full[:, :k], b_full[:, :k], c_full[:, :n], algo=kl.ALGO_1CTA)
+    torch.cuda.synchronize()
+    assert (c_full[:, n:] == 7.0).all(), "wrote outside C's columns"
+    check(c_full[:, :n].float().cpu().numpy(), a_bits, b_bits, 1.0, BF16_TOL)
+
+
+def test_k_zero_gives_zeros(cuda):
+    import torch
+
+    a = torch.zeros((64, 0), dtype=torch.bfloat16, device=cuda)
+    b = torch.zeros((32, 0), dtype=torch.bfloat16, device=cuda)
+    c = torch.full((64, 32), 3.0, dtype=torch.bfloat16, device=cuda)
+    d = kl.GemmDesc(m=64, n=32, k=0, a=0, lda=8, b=0, ldb=8, c=c.data_ptr(), ldc=32, ab_type=kl.KL_BF16,
+                    c_type=kl.KL_BF16, alpha=1.0)
+    import ctypes
+
+    kl.check(kl.lib().kl_gemm(ctypes.byref(d), None))
+    torch.cuda.synchronize()
+    assert (c == 0).all()
+
+
+def test_bad_alignment_is_an_error(cuda):
+    import torch
+
+    a = torch.zeros((64, 72), dtype=torch.bfloat16, device=cuda)
+    b = torch.zeros((64, 64), dtype=torch.bfloat16, device=cuda)
+    c = torch.zeros((64, 64), dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(kl.KlError) as e:
+        kl.gemm(a[:, 1:65], b, c)  # A starts 2 bytes past a 16-byte boundary
+    assert e.value.status == kl.KL_ERR_INVALID_ARGUMENT
+    assert "16-byte aligned" in e.value.message
+
+
+def test_wait_timeout_reports_instead_of_hanging(cuda):
+    """A wait nobody satisfies gives up after its bound and the context stays usable."""
+    import torch
+
+    kl.read_status(clear=True)
+    kl.probe_wait_timeout(2_000_000)  # 2 ms
+    bits = kl.read_status(clear=True)
+    assert bits & 16
+    a, b, _, _ = random_inputs(128, 256, 64, "bf16", seed=1)
+    check(run_kl(a, b, "bf16", "bf16", cuda, kl.ALGO_1CTA), a, b, 1.0, BF16_TOL)
