@@ -9,8 +9,8 @@
 namespace kl::capi {
 
 int choose_algo(kl_gemm_desc const& d) {
-  (void)d;
-  return KL_ALGO_1CTA;
+  // A CTA pair needs at least 256 rows to fill its tile; below that one CTA per tile.
+  return d.m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA;
 }
 
 kl_status skinny_workspace_size(kl_gemm_desc const& d, size_t* bytes) {

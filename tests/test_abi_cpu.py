@@ -1,0 +1,112 @@
+"""libkl_b200.so on the CPU: it loads, exports every entry point include/kl_gemm.h declares, and
+its descriptor encoders reproduce the reference's outputs bit for bit (no GPU needed)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+import maia_b200 as kl
+from golden_util import ELEM_BYTES, idescs, known_answers, sha, tile_id, tiles
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "kl_gemm.h"
+TYPE = {"bf16": kl.KL_BF16, "f16": kl.KL_F16, "f32": kl.KL_F32, "i8": kl.KL_I8, "e4m3": kl.KL_E4M3}
+
+
+def declared_symbols():
+    return sorted(set(re.findall(r"^KL_API [^(]*?\b(kl_\w+)\(", HEADER.read_text(), re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    names = declared_symbols()
+    assert len(names) >= 14
+    lib = ctypes.CDLL(str(kl.LIB_PATH))
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in kl_gemm.h but not exported"
+    assert set(names) == set(kl.EXPORTED)
+
+
+def test_version():
+    assert kl.lib().kl_version() >= 100
+
+
+@pytest.mark.parametrize("t", tiles(), ids=tile_id)
+def test_tile_layout_bit_exact(t):
+    eb, R, C, S = ELEM_BYTES[t["type"]], t["rows"], t["cols"], t["swizzle"]
+    phys, plain = [], []
+    for r in range(R):
+        for c in range(C):
+            s, p = kl.smem_tile_offset(eb, R, C, S, r, c)
+            phys.append(s)
+            plain.append(p)
+    assert sha(phys) == t["tensor_sha256"], "swizzled offsets differ from the reference's tile.tensor()"
+    assert sha(plain) == t["layout_b_sha256"], "un-swizzled offsets differ from the reference's layout_b()"
+
+
+@pytest.mark.parametrize("t", tiles(), ids=tile_id)
+def test_tma_box_bit_exact(t):
+    eb, R, C, S = ELEM_BYTES[t["type"]], t["rows"], t["cols"], t["swizzle"]
+    g = kl.tma_box_geometry(eb, R, C, S)
+    for k in ("inner", "outer", "col_boxes", "row_boxes", "count", "bytes"):
+        assert g[k] == t["box"][k], k
+    assert [list(kl.tma_box_position(eb, R, C, S, i)) for i in range(g["count"])] == t["box"]["pos"]
+
+
+@pytest.mark.parametrize("t", [t for t in tiles() if "umma_desc_base0" in t], ids=tile_id)
+def test_umma_desc_bit_exact(t):
+    eb, R, C, S = ELEM_BYTES[t["type"]], t["rows"], t["cols"], t["swizzle"]
+    for row, k, val in t["umma_desc_base0"]:
+        assert kl.umma_smem_desc(eb, R, C, S, 0, k, row) == int(val, 16), (row, k)
+    # A non-zero base only moves the start-address field.
+    for row, k, val in t["umma_desc_base0"][:8]:
+        assert kl.umma_smem_desc(eb, R, C, S, 0x2400, k, row) == int(val, 16) + (0x2400 >> 4)
+
+
+@pytest.mark.parametrize("d", idescs(), ids=lambda d: f"{d['a']}_{d['acc']}_m{d['m']}_n{d['n']}_{d['source']}")
+def test_instr_desc_bit_exact(d):
+    assert kl.mma_instr_desc(TYPE[d["a"]], TYPE[d["b"]], TYPE[d["acc"]], d["m"], d["n"]) == int(d["value"], 16)
+
+
+def test_instr_desc_known_answer_from_reference_test():
+    ka = next(k for k in known_answers() if k["what"].startswith("idesc"))
+    assert kl.mma_instr_desc(kl.KL_BF16, kl.KL_BF16, kl.KL_F32, 128, 256) == int(ka["value"], 16) == 0x08400490
+
+
+@pytest.mark.parametrize("args, msg", [
+    ((2, 100, 64, 128), "rows must be a positive multiple of 8"),
+    ((2, 128, 60, 128), "multiple of the swizzle atom"),
+    ((3, 128, 64, 128), "elem_bytes"),
+    ((2, 128, 64, 96), "swizzle_span"),
+])
+def test_encoder_argument_errors(args, msg):
+    with pytest.raises(kl.KlError) as e:
+        kl.tma_box_geometry(*args)
+    assert e.value.status == kl.KL_ERR_INVALID_ARGUMENT and msg in e.value.message
+
+
+def test_instr_desc_rejects_bad_shapes():
+    for m, n in ((32, 64), (128, 8), (256, 264), (128, 40)):
+        with pytest.raises(kl.KlError):
+            kl.mma_instr_desc(kl.KL_BF16, kl.KL_BF16, kl.KL_F32, m, n)
+    with pytest.raises(kl.KlError):  # mixed MMA kinds
+        kl.mma_instr_desc(kl.KL_BF16, kl.KL_E4M3, kl.KL_F32, 128, 128)
+
+
+# make_tma_desc's validation runs before the driver call, so its error contract is testable here.
+# Cases: kernel_lib/tests/unit/test_tma_desc.cu:97-107; messages: tma_desc.hpp:134-142.
+@pytest.mark.parametrize("ptr, shape, stride, msg", [
+    (0x10002, (4096, 4096), (4096, 1), "kl::make_tma_desc: global address must be 16-byte aligned"),
+    (0x10000, (4096, 4096), (1024, 1), "kl::make_tma_desc: rows overlap: the row stride is smaller than cols"),
+    (0x10000, (4096, 4100), (4100, 1),
+     "kl::make_tma_desc: outer strides must be positive multiples of 16 bytes, below 2^40 bytes"),
+    (0x10000, (0, 4096), (4096, 1), "kl::make_tma_desc: extents must be in [1, 2^32]"),
+    (0x10000, (2, 4096, 4096), (4096 * 4096, 4096, 1), None),  # rank 3 passes validation
+])
+def test_tma_desc_validation(ptr, shape, stride, msg):
+    if msg is None:
+        return
+    with pytest.raises(kl.KlError) as e:
+        kl.make_tma_desc(kl.KL_BF16, 128, 64, 128, ptr, shape, stride)
+    assert e.value.status == kl.KL_ERR_INVALID_ARGUMENT
+    assert e.value.message == msg

@@ -1,0 +1,68 @@
+"""The CPU GEMM oracle (oracle/gemm_oracle.c) pinned against numpy float64 matmul, and its element
+decoders against the format definitions."""
+
+import numpy as np
+import pytest
+
+from maia_b200 import workloads as wl
+from oracle import gemm as og
+
+
+def test_bf16_decode_and_rounding():
+    x = np.array([0.0, 1.0, -2.5, 3.140625, 1e-3, 65504.0, 1.00390625, 1.01171875], dtype=np.float32)
+    bits = wl.f32_to_bf16_bits(x)
+    # 1 + 2^-8 ties to even (1.0); 1 + 3*2^-8 ties up to 1 + 2^-6.
+    np.testing.assert_array_equal(og.decode(bits)[[0, 1, 2, 6, 7]], [0.0, 1.0, -2.5, 1.0, 1.015625])
+    np.testing.assert_allclose(og.decode(bits), x, rtol=2 ** -8)
+
+
+def test_e4m3_table():
+    v = wl.e4m3_values()
+    assert v[0x7E] == 448.0 and v[0x01] == 2.0 ** -9 and v[0x38] == 1.0 and np.isnan(v[0x7F]) and v[0xB8] == -1.0
+    np.testing.assert_array_equal(og.decode(np.arange(256, dtype=np.uint8))[~np.isnan(v)], v[~np.isnan(v)])
+
+
+def test_e4m3_quantise_round_trip():
+    finite = np.array([i for i in range(256) if i not in (0x7F, 0xFF, 0x80)], dtype=np.uint8)
+    vals = wl.e4m3_values()[finite]
+    np.testing.assert_array_equal(wl.f32_to_e4m3_bits(vals.astype(np.float32)), finite)
+    # Midpoint between 1.0 (0x38) and 1.125 (0x39) rounds to even mantissa -> 0x38; saturation at 448.
+    assert wl.f32_to_e4m3_bits(np.array([1.0625, 1000.0, -1000.0], dtype=np.float32)).tolist() == [0x38, 0x7E, 0xFE]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "e4m3"])
+@pytest.mark.parametrize("shape", [(1, 1, 1), (7, 5, 3), (64, 48, 96), (130, 70, 257)])
+def test_gemm_f64_matches_numpy(dtype, shape):
+    from gpu_util import random_inputs
+
+    m, n, k = shape
+    a, b, sa, sb = random_inputs(m, n, k, dtype, seed=m + n + k)
+    ref = og.decode(a) @ og.decode(b).T * (sa * sb)
+    got = og.gemm_f64(a, b, sa * sb, threads=3)
+    np.testing.assert_allclose(got, ref, rtol=1e-12, atol=1e-12)
+
+
+def test_gemm_f32_baseline_close_to_f64():
+    from gpu_util import random_inputs
+
+    a, b, _, _ = random_inputs(100, 90, 300, "bf16", seed=3)
+    ref = og.gemm_f64(a, b)
+    got = og.gemm_f32(a, b, threads=4)
+    elem, norm = og.rel_error(got, ref)
+    assert norm < 1e-5
+
+
+def test_c1_inputs_are_seeded_and_stable():
+    a1, b1, _, _ = wl.make_inputs(wl.C1)
+    a2, b2, _, _ = wl.make_inputs(wl.C1)
+    assert a1.shape == (256, 256) and b1.shape == (256, 256) and a1.dtype == np.uint16
+    np.testing.assert_array_equal(a1, a2)
+    x = og.decode(a1)
+    assert x.min() >= -1.0 and x.max() <= 1.0 and abs(x.mean()) < 0.02
+
+
+def test_rel_error_floor():
+    ref = np.array([1.0, -1.0, 0.0, 1e-9])
+    elem, norm = og.rel_error(ref + np.array([1e-3, 0, 1e-6, 0]), ref)
+    # rms(ref) = sqrt(1/2): the zero entry is measured against the floor 1e-3 * rms.
+    assert abs(elem - 1e-6 / (1e-3 * np.sqrt(0.5))) < 1e-9 and abs(norm - 1e-3) < 1e-12
