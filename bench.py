@@ -78,7 +78,7 @@ class ClockSampler:
                     self.samples.append((float(mhz), int(reasons)))
                 except Exception:
                     pass
-                self._stop.wait(0.002)
+                self._stop.wait(0.0005)
 
         self._thread = threading.Thread(target=run, daemon=True)
         self._thread.start()
@@ -143,8 +143,8 @@ def run_reference(args, w):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["kl", "reference"], default="kl")
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
     ap.add_argument("--algo", type=int, default=0, help="kl_algo (0 = library default)")
@@ -177,8 +177,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
     # Inputs: full A, this rank's N-shard of B (host-generated, seeded, then pinned).
+    from maia_b200 import sharding
+
     a_bits, b_bits, sa, sb = wl.make_inputs(w)
-    n_lo, n_hi = w.n * rank // world, w.n * (rank + 1) // world
+    n_lo, n_hi = sharding.shard_range(w.n, world, rank)
     b_bits = np.ascontiguousarray(b_bits[n_lo:n_hi])
     nshard = n_hi - n_lo
     np_view = np.int16 if w.dtype == "bf16" else np.uint8
@@ -208,11 +210,7 @@ def main():
         torch.cuda.synchronize(dev)
 
     def max_over_ranks(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return sharding.max_over_ranks(x, dist, dev)
 
     # ---- device-resident timing
     for _ in range(max(args.warmup, 3)):
@@ -254,14 +252,47 @@ def main():
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
 
+    # ---- N > 1: the same GEMM followed by the NCCL all-gather of C (where the full C is needed)
+    gather = None
+    if dist is not None:
+        def gather_step():
+            kl.gemm(a, b, c, **kw)
+            sharding.gather_columns(c, w.n, dist)
+
+        for _ in range(max(args.warmup, 3)):
+            gather_step()
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(args.steps):
+            gather_step()
+        g1.record(stream)
+        barrier()
+        g_ms = max_over_ranks(g0.elapsed_time(g1) / args.steps)
+        gather = {"value": flops_total / (g_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": g_ms,
+                  "what": "kl_gemm + NCCL all-gather of C and re-layout to [M, N] on every rank"}
+
     peaks, peak_src = load_peaks()
     per_rank_flops = 2.0 * w.m * nshard * w.k
-    achieved = per_rank_flops / (dev_ms * 1e-3) / 1e12
-    peak = peaks["bf16_tflops"] if w.dtype == "bf16" else 2.0 * peaks["bf16_tflops"]
+    memory_bound = w.m <= 256
+    if memory_bound:
+        # Decode shapes: every operand byte moved once, against the measured copy bandwidth.
+        alg_bytes = (w.m * w.k + nshard * w.k) * w.in_bytes + w.m * nshard * w.out_bytes
+        roofline = {"bound": "hbm", "achieved": alg_bytes / (dev_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
+                    "unit": "GB/s", "peak_source": f"{peak_src} hbm_gbs", "algorithmic_bytes_per_launch": alg_bytes}
+    else:
+        peak = peaks["bf16_tflops"] if w.dtype == "bf16" else 2.0 * peaks["bf16_tflops"]
+        roofline = {"bound": "tensor", "achieved": per_rank_flops / (dev_ms * 1e-3) / 1e12, "peak": peak,
+                    "unit": "TFLOP/s",
+                    "peak_source": f"{peak_src} " + ("bf16_tflops (burst)" if w.dtype == "bf16" else
+                                                     "2 x bf16_tflops (burst; fp8 dense rate is twice bf16)"),
+                    "algorithmic_flops_per_launch": per_rank_flops}
+    roofline["frac"] = roofline["achieved"] / roofline["peak"]
     traffic = None
     tf = ROOT / "profiles" / f"traffic_{w.name}.json"
     if tf.exists() and world == 1:
         traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+    roofline["traffic"] = traffic
 
     if rank == 0:
         line = {
@@ -274,11 +305,9 @@ def main():
                        "l2": "operands exceed L2 (no flush)", "algo": args.algo},
             "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak,
-                         "peak_source": f"{peak_src} {'bf16_tflops' if w.dtype == 'bf16' else '2 x bf16_tflops (fp8 dense = 2x bf16)'}",
-                         "traffic": traffic},
+            "roofline": roofline,
             "gpu_launches": args.steps,
+            "gemm_plus_allgather": gather,
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:

@@ -92,8 +92,15 @@ KL_API kl_status kl_gemm(const kl_gemm_desc* desc, void* stream);
  * algorithm except KL_ALGO_SKINNY, which keeps fp32 partial sums). */
 KL_API kl_status kl_gemm_workspace_size(const kl_gemm_desc* desc, size_t* bytes);
 
-/* No reference counterpart. Like kl_gemm, with caller-provided device workspace (at least
- * kl_gemm_workspace_size bytes, zero-filled before its first use; the kernel leaves it zeroed). */
+/* No reference counterpart. Like kl_gemm, with caller-provided device workspace: at least
+ * kl_gemm_workspace_size bytes, 16-byte aligned, zero-filled before its first use. Its head holds
+ * 16 bytes of arrival counters per 128 rows of B, which the skinny kernel leaves at zero after
+ * every call; the partial sums after them are overwritten each call. So the buffer can be reused
+ * as is for any call whose B has at most as many rows as the previous call's; before a call with
+ * more rows of B, zero it again (or just its first 16 * ceil(N / 128) bytes). Calls that share one
+ * workspace must not overlap on the GPU. After kl_read_status reports KL_ERR_TIMEOUT, zero it
+ * again. (kl_gemm without a workspace uses one library-owned buffer per device, with the same
+ * no-overlap rule, and does all of this itself.) */
 KL_API kl_status kl_gemm_ws(const kl_gemm_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Upper bound on any device-side wait, in nanoseconds (default 2e9). A wait that runs out sets a

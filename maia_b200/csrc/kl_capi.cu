@@ -196,6 +196,10 @@ kl_status kl_read_status(int32_t* bits, int32_t clear) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status clear)");
   }
   if (bits) *bits = v;
+  if (v != 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) kl::capi::mark_workspace_dirty(dev);
+  }
   if (v != 0) return fail(KL_ERR_TIMEOUT, "a device-side wait timed out (status bits " + std::to_string(v) + ")");
   return KL_OK;
 }

@@ -25,6 +25,8 @@ int choose_algo(kl_gemm_desc const& d);
 // Memory-bound small-M path (kl_skinny.cu).
 kl_status skinny_workspace_size(kl_gemm_desc const& d, size_t* bytes);
 kl_status run_skinny(kl_gemm_desc const& d, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+// After a timed-out kernel the library workspace's tickets may be mid-count: re-zero before reuse.
+void mark_workspace_dirty(int device);
 
 // Failure-path probe (kl_probe.cu).
 kl_status launch_wait_probe(int* status, unsigned long long timeout_ns, cudaStream_t stream);

@@ -1,30 +1,210 @@
-// Memory-bound small-M GEMM (decode shapes). Filled in below the dispatch helpers.
+// KL_ALGO_SKINNY: dispatch, workspace sizing and launch of the memory-bound small-M kernel
+// (include/kl/gemm/skinny_kernel.cuh).
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cstdint>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
 #include <kl/gemm/gemm.hpp>
+#include <kl/gemm/skinny_kernel.cuh>
 
 #include "kl_internal.cuh"
 
 namespace kl::capi {
 
+namespace {
+
+using namespace kl::gemm;
+
+constexpr size_t kAlign = 256;
+size_t round_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+int token_tile(int64_t m) { return m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256; }
+
+// Stages that fit next to the tile sizes (weights 16 KB, activations tok x 128 B per stage).
+template <typename InT, typename OutT, int Tok>
+using Skinny = SkinnyConfig<InT, OutT, Tok, (Tok == 16 ? 11 : Tok == 32 ? 10 : Tok == 64 ? 8 : Tok == 128 ? 6 : 4)>;
+
+struct Plan {
+  int tok = 0;
+  int n_tiles = 0, k_blocks = 0, grid = 0;
+  long long total = 0;
+  size_t ticket_bytes = 0, slot_bytes = 0;
+};
+
+kl_status make_plan(kl_gemm_desc const& d, Plan* p) {
+  if (d.m > 256) return fail(KL_ERR_INVALID_ARGUMENT, "KL_ALGO_SKINNY handles at most 256 rows of A");
+  if (d.m <= 0 || d.n <= 0 || d.k <= 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: m, n and k must be positive");
+  if (d.n > INT32_MAX || d.k > INT32_MAX) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: extents must fit in 32 bits");
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  const int elem = d.ab_type == KL_E4M3 ? 1 : 2;
+  const int block_k = 128 / elem;
+  p->tok = token_tile(d.m);
+  p->n_tiles = int((d.n + 127) / 128);
+  p->k_blocks = int((d.k + block_k - 1) / block_k);
+  p->total = (long long)p->n_tiles * p->k_blocks;
+  int cap = d.max_ctas > 0 ? std::min(d.max_ctas, sms) : sms;
+  p->grid = int(std::min<long long>(cap, p->total));
+  p->ticket_bytes = round_up(size_t(p->n_tiles) * 4 * sizeof(int));
+  p->slot_bytes = size_t(p->n_tiles + p->grid - 1) * size_t(p->tok) * 128 * sizeof(float);
+  return KL_OK;
+}
+
+template <class Cfg>
+kl_status launch(kl_gemm_desc const& d, Plan const& pl, void* ws, cudaStream_t stream) {
+  using InT = typename Cfg::in_type;
+  int* status = nullptr;
+  kl_status s = device_status_ptr(&status);
+  if (s != KL_OK) return s;
+  static int configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_skinny_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(Cfg::kSmemBytes));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(skinny)");
+    configured[dev] = 1;
+  }
+  SkinnyParams p{};
+  p.map_w = make_tma_load<typename Cfg::WTile>(row_major_strided(static_cast<InT const*>(d.b), d.n, d.k, d.ldb)).map;
+  p.map_x = make_tma_load<typename Cfg::XTile>(row_major_strided(static_cast<InT const*>(d.a), d.m, d.k, d.lda)).map;
+  if (d.ldc < d.n) throw std::invalid_argument("kl_gemm: ldc < n");
+  if (reinterpret_cast<uintptr_t>(d.c) % (d.c_type == KL_F32 ? 4 : 2) != 0)
+    throw std::invalid_argument("kl_gemm: C is not aligned to its element size");
+  SkinnyArgs& a = p.args;
+  a.m = int(d.m);
+  a.n = int(d.n);
+  a.k = int(d.k);
+  a.n_tiles = pl.n_tiles;
+  a.k_blocks = pl.k_blocks;
+  a.total_units = pl.total;
+  a.grid = pl.grid;
+  a.alpha = d.alpha;
+  a.scale_a = d.scale_a;
+  a.scale_b = d.scale_b;
+  a.c = d.c;
+  a.ldc = d.ldc;
+  a.tickets = static_cast<int*>(ws);
+  a.slots = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.ticket_bytes);
+  a.status = status;
+  a.timeout_ns = wait_timeout_ns();
+  gemm_skinny_kernel<Cfg><<<pl.grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? KL_OK : cuda_fail(e, "skinny launch");
+}
+
+template <typename InT, typename OutT>
+kl_status dispatch_tok(kl_gemm_desc const& d, Plan const& pl, void* ws, cudaStream_t stream) {
+  switch (pl.tok) {
+    case 16: return launch<Skinny<InT, OutT, 16>>(d, pl, ws, stream);
+    case 32: return launch<Skinny<InT, OutT, 32>>(d, pl, ws, stream);
+    case 64: return launch<Skinny<InT, OutT, 64>>(d, pl, ws, stream);
+    case 128: return launch<Skinny<InT, OutT, 128>>(d, pl, ws, stream);
+    default: return launch<Skinny<InT, OutT, 256>>(d, pl, ws, stream);
+  }
+}
+
+// Library-owned workspace for kl_gemm (no caller workspace): one per device, grown on demand.
+// Layout per call: tickets in [0, ticket_bytes), slots after them. A call leaves its own ticket
+// range at zero but writes slots right after it, so a later call with more weight tiles (a longer
+// ticket range) would find slot data where it expects zero tickets: `clean` tracks the prefix
+// known to hold only zero tickets, and the gap is cleared on the stream before such a call.
+// Calls that overlap on one device share the buffer.
+struct DeviceWorkspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  size_t clean = 0;
+  bool dirty = false;
+};
+std::mutex g_ws_mutex;
+DeviceWorkspace g_ws[64];
+
+kl_status library_workspace(size_t need, size_t tickets, cudaStream_t stream, void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(KL_ERR_NOT_SUPPORTED, "device index above 63");
+  std::lock_guard<std::mutex> lock(g_ws_mutex);
+  DeviceWorkspace& w = g_ws[dev];
+  if (w.bytes < need) {
+    if (w.ptr) {
+      e = cudaDeviceSynchronize();  // the old buffer may still be in use
+      if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+      cudaFree(w.ptr);
+      w.ptr = nullptr;
+      w.bytes = 0;
+    }
+    e = cudaMalloc(&w.ptr, need);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(skinny workspace)");
+    e = cudaMemset(w.ptr, 0, need);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(skinny workspace)");
+    w.bytes = need;
+    w.clean = need;
+  } else if (w.dirty) {
+    e = cudaMemset(w.ptr, 0, w.bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(skinny workspace)");
+    w.clean = w.bytes;
+  }
+  w.dirty = false;
+  if (tickets > w.clean) {
+    e = cudaMemsetAsync(static_cast<char*>(w.ptr) + w.clean, 0, tickets - w.clean, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(skinny tickets)");
+  }
+  w.clean = tickets;  // this call writes slots from here on
+  *out = w.ptr;
+  return KL_OK;
+}
+
+}  // namespace
+
+void mark_workspace_dirty(int device) {
+  if (device < 0 || device >= 64) return;
+  std::lock_guard<std::mutex> lock(g_ws_mutex);
+  g_ws[device].dirty = true;
+}
+
 int choose_algo(kl_gemm_desc const& d) {
-  // A CTA pair needs at least 256 rows to fill its tile; below that one CTA per tile.
+  // A CTA pair needs at least 256 rows to fill its tile; up to 128 rows the weights dominate
+  // traffic and the stream-K skinny kernel keeps every SM streaming.
+  if (d.m <= 128 && (d.ab_type == KL_BF16 || d.ab_type == KL_E4M3)) return KL_ALGO_SKINNY;
   return d.m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA;
 }
 
 kl_status skinny_workspace_size(kl_gemm_desc const& d, size_t* bytes) {
-  (void)d;
-  *bytes = 0;
-  return fail(KL_ERR_NOT_SUPPORTED, "KL_ALGO_SKINNY is not built yet");
+  Plan pl;
+  kl_status s = make_plan(d, &pl);
+  if (s != KL_OK) return s;
+  *bytes = pl.ticket_bytes + pl.slot_bytes;
+  return KL_OK;
 }
 
 kl_status run_skinny(kl_gemm_desc const& d, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  (void)d;
-  (void)workspace;
-  (void)workspace_bytes;
-  (void)stream;
-  return fail(KL_ERR_NOT_SUPPORTED, "KL_ALGO_SKINNY is not built yet");
+  Plan pl;
+  kl_status s = make_plan(d, &pl);
+  if (s != KL_OK) return s;
+  const size_t need = pl.ticket_bytes + pl.slot_bytes;
+  void* ws = workspace;
+  if (ws == nullptr) {
+    s = library_workspace(need, pl.ticket_bytes, stream, &ws);
+    if (s != KL_OK) return s;
+  } else if (workspace_bytes < need) {
+    return fail(KL_ERR_INVALID_ARGUMENT,
+                "kl_gemm_ws: workspace of " + std::to_string(workspace_bytes) + " bytes, need " + std::to_string(need));
+  } else if (reinterpret_cast<uintptr_t>(ws) % 16 != 0) {
+    return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_ws: workspace must be 16-byte aligned");
+  }
+  if (d.ab_type == KL_BF16 && d.c_type == KL_BF16) return dispatch_tok<kl::bf16, kl::bf16>(d, pl, ws, stream);
+  if (d.ab_type == KL_BF16 && d.c_type == KL_F32) return dispatch_tok<kl::bf16, float>(d, pl, ws, stream);
+  if (d.ab_type == KL_E4M3 && d.c_type == KL_BF16) return dispatch_tok<kl::e4m3, kl::bf16>(d, pl, ws, stream);
+  return fail(KL_ERR_NOT_SUPPORTED, "KL_ALGO_SKINNY supports (A/B, C) = (bf16, bf16), (bf16, f32), (e4m3, bf16)");
 }
 
 }  // namespace kl::capi

@@ -86,17 +86,32 @@ def e4m3_values() -> np.ndarray:
 
 
 def f32_to_e4m3_bits(x: np.ndarray) -> np.ndarray:
-    """Round to the nearest e4m3 value (ties to even mantissa), saturating at +-448."""
+    """Round float32 to the nearest e4m3 value (ties to even mantissa), saturating at +-448.
+
+    Normal range: keep 3 mantissa bits of the float32 pattern with round-to-nearest-even (a carry
+    moves into the exponent) and rebias the exponent from 127 to 7. Below 2^-6 the e4m3 grid is
+    uniform (step 2^-9), so the pattern is the rounded multiple of 2^-9."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32)
+    sign = ((u >> 24) & np.uint32(0x80)).astype(np.uint8)
+    mag = u & np.uint32(0x7FFFFFFF)
+    rounded = (mag + np.uint32(0x7FFFF) + ((mag >> 20) & np.uint32(1))) >> 20
+    normal = rounded.astype(np.int64) - (120 << 3)
+    sub = np.rint(np.abs(x).astype(np.float64) * 512.0).astype(np.int64)  # rint: ties to even
+    q = np.where(mag < np.uint32(0x3C800000), sub, normal)               # 0x3C800000 = 2^-6
+    q = np.clip(q, 0, 0x7E).astype(np.uint8)
+    return np.where(q != 0, q | sign, q).astype(np.uint8)
+
+
+def f32_to_e4m3_bits_nearest(x: np.ndarray) -> np.ndarray:
+    """Slow definition of the same rounding: search the sorted grid of e4m3 values."""
     vals = e4m3_values()
-    pos = np.arange(0, 0x7F)  # non-negative finite patterns 0x00..0x7E, increasing in value
-    grid = vals[pos]
+    grid = vals[np.arange(0, 0x7F)]
     a = np.minimum(np.abs(np.asarray(x, dtype=np.float64)), 448.0)
-    idx = np.searchsorted(grid, a)  # grid[idx-1] < a <= grid[idx]
-    idx = np.clip(idx, 1, len(grid) - 1)
+    idx = np.clip(np.searchsorted(grid, a), 1, len(grid) - 1)
     lo, hi = grid[idx - 1], grid[idx]
     pick_hi = (a - lo > hi - a) | ((a - lo == hi - a) & (idx % 2 == 0))
     q = np.where(pick_hi, idx, idx - 1).astype(np.uint8)
-    q = np.where(a == 0, 0, q).astype(np.uint8)
     return np.where(np.signbit(x) & (q != 0), q | 0x80, q).astype(np.uint8)
 
 

@@ -45,5 +45,6 @@ def check(c, a_bits, b_bits, scale, tol, threads=None):
     ref = og.gemm_f64(a_bits, b_bits, scale, threads=threads)
     assert not np.isnan(c).any(), "output has unwritten (NaN) entries"
     elem, norm = og.rel_error(c, ref)
+    assert norm <= tol, f"max relative error (normwise) {norm:.3e} > {tol}"
     assert elem <= tol, f"max element-wise relative error {elem:.3e} > {tol} (normwise {norm:.3e})"
     return elem, norm

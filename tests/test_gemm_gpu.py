@@ -1,7 +1,8 @@
 """GEMM parity on the GPU: libkl_b200.so through its C ABI against the fp64 CPU oracle.
 
-Tolerances (max element-wise relative error against fp64 accumulation of the same rounded
-inputs, floor 1e-3 * rms): 1e-2 for bf16 inputs, 5e-2 for e4m3 inputs.
+Tolerances, against fp64 accumulation of the same rounded inputs: 1e-2 for bf16 inputs, 5e-2 for
+e4m3 inputs, applied to both the normwise max relative error max|c - r| / max|r| and the
+element-wise |c - r| / max(|r|, 1e-2 * rms(r)).
 """
 
 import numpy as np

@@ -22,6 +22,15 @@ def test_e4m3_table():
     np.testing.assert_array_equal(og.decode(np.arange(256, dtype=np.uint8))[~np.isnan(v)], v[~np.isnan(v)])
 
 
+def test_e4m3_fast_rounding_matches_nearest_search():
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.standard_normal(200000).astype(np.float32) * s for s in (1e-3, 0.05, 1.0, 30.0, 200.0)])
+    grid = wl.e4m3_values()[:0x7F].astype(np.float32)
+    mids = ((grid[1:] + grid[:-1]) / 2).astype(np.float32)  # exact ties
+    x = np.concatenate([x, grid, -grid, mids, -mids, np.array([447.9, 448.0, 460.0, 5e-4, 1e-9], np.float32)])
+    np.testing.assert_array_equal(wl.f32_to_e4m3_bits(x), wl.f32_to_e4m3_bits_nearest(x))
+
+
 def test_e4m3_quantise_round_trip():
     finite = np.array([i for i in range(256) if i not in (0x7F, 0xFF, 0x80)], dtype=np.uint8)
     vals = wl.e4m3_values()[finite]
@@ -64,5 +73,8 @@ def test_c1_inputs_are_seeded_and_stable():
 def test_rel_error_floor():
     ref = np.array([1.0, -1.0, 0.0, 1e-9])
     elem, norm = og.rel_error(ref + np.array([1e-3, 0, 1e-6, 0]), ref)
-    # rms(ref) = sqrt(1/2): the zero entry is measured against the floor 1e-3 * rms.
-    assert abs(elem - 1e-6 / (1e-3 * np.sqrt(0.5))) < 1e-9 and abs(norm - 1e-3) < 1e-12
+    # rms(ref) = sqrt(1/2): the zero entry is measured against the floor 1e-2 * rms.
+    elem, norm = og.rel_error(ref + np.array([1e-3, 0, 1e-5, 0]), ref)
+    assert abs(elem - 1e-5 / (1e-2 * np.sqrt(0.5))) < 1e-9 and abs(norm - 1e-3) < 1e-12
+    elem, _ = og.rel_error(ref + np.array([1e-3, 0, 1e-6, 0]), ref, floor_frac=1e-3)
+    assert abs(elem - 1e-6 / (1e-3 * np.sqrt(0.5))) < 1e-9
