@@ -103,6 +103,21 @@ KL_API kl_status kl_gemm_workspace_size(const kl_gemm_desc* desc, size_t* bytes)
  * no-overlap rule, and does all of this itself.) */
 KL_API kl_status kl_gemm_ws(const kl_gemm_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference. The skinny (KL_ALGO_SKINNY) GEMM for callers that may not
+ * allocate device memory while they run and cannot lend the library a workspace (for example an
+ * inference-runtime plugin that is handed only its input and output tensors, or a serving loop
+ * that forbids allocation after warm-up). Its scratch is a fixed 16 MiB array inside the library,
+ * reserved on every GPU that loads it for the life of the process; this call allocates nothing.
+ * Limits: at most 256 rows of A, at most 524288 rows of B, and (ceil(N/128) + SMs - 1) x
+ * token_tile x 512 bytes of partial sums within 16 MiB - 64 KiB (token_tile = M rounded up to 16,
+ * 32, 64, 128 or 256; at N = 28672 on a 148-SM B200 that is M <= 64); larger problems are
+ * rejected with KL_ERR_INVALID_ARGUMENT and a message. The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before any stream capture.
+ * Every call shares the one array, which keeps the last call's contents: each call clears the
+ * arrival counters it uses on `stream` before its kernel, and calls that overlap on the GPU race
+ * on the array, so serialise them. desc->algo must be KL_ALGO_AUTO or KL_ALGO_SKINNY. */
+KL_API kl_status kl_gemm_skinny_noalloc(const kl_gemm_desc* desc, void* stream);
+
 /* Upper bound on any device-side wait, in nanoseconds (default 2e9). A wait that runs out sets a
  * bit in the device status word instead of hanging the GPU. */
 KL_API void kl_set_wait_timeout_ns(uint64_t ns);

@@ -32,7 +32,7 @@ EXPORTED = (
     "kl_version", "kl_last_error", "kl_gemm", "kl_gemm_workspace_size", "kl_gemm_ws",
     "kl_set_wait_timeout_ns", "kl_read_status", "kl_probe_wait_timeout", "kl_smem_tile_offset",
     "kl_tma_box_geometry", "kl_tma_box_position", "kl_umma_smem_desc", "kl_mma_instr_desc",
-    "kl_make_tma_desc",
+    "kl_make_tma_desc", "kl_gemm_skinny_noalloc",
 )
 
 
@@ -90,6 +90,7 @@ def lib() -> ctypes.CDLL:
             "kl_umma_smem_desc": (i32, [i32, i32, i32, i32, u32, i32, i32, P(u64)]),
             "kl_mma_instr_desc": (i32, [i32, i32, i32, i32, i32, P(u32)]),
             "kl_make_tma_desc": (i32, [i32, i32, i32, i32, i32, vp, i32, P(i64), P(i64), vp]),
+            "kl_gemm_skinny_noalloc": (i32, [P(GemmDesc), vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
