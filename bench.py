@@ -9,8 +9,8 @@ whole-job TFLOP/s, the total flops over the max-over-ranks device time. The oper
 exceed the 126 MB L2, so no flush runs between steps.
 
   value      device time of K kl_gemm launches on resident inputs (CUDA events on the stream).
-  e2e        the same through the public API with host buffers: pinned H2D of A and B, kl_gemm,
-             D2H of C, all inside the timed region, every step.
+  e2e        the same through the public host-buffer API (kl_gemm_host): every step copies A and B
+             in from pinned host memory and C back out, overlapped with the GEMM in column blocks.
   roofline   the GEMM kernel's achieved TFLOP/s against the measured dense bf16 (or fp8) peak.
   cpu_baseline  the CPU GEMM (fp32 accumulate, all host threads) on a bounded row slab.
 `--impl reference` times only the reference arm: the CPU GEMM restatement (the reference ships no
@@ -149,6 +149,8 @@ def main():
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
     ap.add_argument("--algo", type=int, default=0, help="kl_algo (0 = library default)")
     ap.add_argument("--group-m", type=int, default=0)
+    ap.add_argument("--prefetch", type=int, default=0, help="L2 prefetch distance (0 = library default, -1 = off)")
+    ap.add_argument("--variant", type=int, default=0, help="kl_gemm_desc.variant (0 = library default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
 
@@ -198,7 +200,8 @@ def main():
         scale_a = torch.tensor([sa], dtype=torch.float32, device=dev)
         scale_b = torch.tensor([sb], dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
-    kw = dict(scale_a=scale_a, scale_b=scale_b, algo=args.algo, group_m=args.group_m)
+    kw = dict(scale_a=scale_a, scale_b=scale_b, algo=args.algo, group_m=args.group_m, prefetch=args.prefetch,
+              variant=args.variant)
 
     def step():
         kl.gemm(a, b, c, **kw)
@@ -236,10 +239,8 @@ def main():
     d2h = c.numel() * c.element_size()
 
     def e2e_step():
-        a.copy_(a_host, non_blocking=True)
-        b.copy_(b_host, non_blocking=True)
-        kl.gemm(a, b, c, **kw)
-        c_host.copy_(c, non_blocking=True)
+        # The host-buffer entry point: copies in, GEMM and copy out, pipelined over column blocks.
+        kl.gemm_host(a_host, b_host, c_host, a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo)
 
     for _ in range(max(args.warmup, 3)):
         e2e_step()
@@ -302,7 +303,8 @@ def main():
             "dtype": w.dtype, "data": "synthetic",
             "config": {"workload": w.name, "m": w.m, "n": w.n, "k": w.k, "out": w.out,
                        "parallelism": f"N-sharded x{world}", "output": "C[:, shard] per rank (no gather)",
-                       "l2": "operands exceed L2 (no flush)", "algo": args.algo},
+                       "l2": "operands exceed L2 (no flush)", "algo": args.algo, "group_m": args.group_m,
+                       "prefetch": args.prefetch, "variant": args.variant},
             "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "roofline": roofline,

@@ -46,6 +46,14 @@ KL_DEVICE void tma_load_2d_pair(uint32_t dst, const void* map, uint32_t bar_clus
       : "memory");
 }
 
+// Ask the TMA unit to bring a 2-D tile into L2 (no shared memory, no barrier): lets a producer
+// run further ahead of its shared-memory ring than the ring itself allows.
+KL_DEVICE void tma_prefetch_l2_2d(const void* map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 KL_DEVICE uint64_t l2_policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

@@ -27,7 +27,11 @@ struct Problem {
   const float* scale_b = nullptr;
   int group_m = 0;   // 0 = default for the config
   int max_ctas = 0;  // 0 = every SM
+  int prefetch = 0;  // L2 prefetch distance in K-blocks: 0 = default, < 0 = off
 };
+
+// Library defaults for the knobs a Problem leaves at 0.
+inline constexpr int kDefaultPrefetchTn = 0;
 
 struct LaunchInfo {
   int grid = 0;
@@ -125,6 +129,7 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   a.scale_b = pr.scale_b;
   a.status = status;
   a.timeout_ns = timeout_ns;
+  a.prefetch = pr.prefetch > 0 ? pr.prefetch : pr.prefetch < 0 ? 0 : kDefaultPrefetchTn;
 
   const int tiles = a.tiles_m * a.tiles_n;
   int workers = std::min(tiles, max_workers);

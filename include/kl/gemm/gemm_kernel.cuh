@@ -97,6 +97,7 @@ struct TnArgs {
   const float* scale_b;
   int* status;                  // device word; timeout bits are ORed in
   unsigned long long timeout_ns;
+  int prefetch;                 // L2 prefetch distance, in K-blocks of the producer's sequence (0 = off)
 };
 
 struct TnParams {
@@ -200,6 +201,22 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
     // ---------------------------------------------------------------- TMA producer
     if (elect_one()) {
       const uint32_t leader_full0 = (CG == 2) ? mapa_shared(full_bar(0), 0) : full_bar(0);
+      // L2 prefetch runs `pf` K-blocks ahead of the loads along this CTA's own sequence of
+      // (tile, K-block) units, crossing into its next tile where needed.
+      const int pf = args.prefetch;
+      auto prefetch_unit = [&](int t, int kb) {
+        while (kb >= args.k_blocks && t < num_tiles) {
+          kb -= args.k_blocks;
+          t += num_workers;
+        }
+        if (t >= num_tiles) return;
+        int ptm, ptn;
+        tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, ptm, ptn);
+        tma_prefetch_l2_2d(&p.map_a, kb * Cfg::kBlockK, ptm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM);
+        tma_prefetch_l2_2d(&p.map_b, kb * Cfg::kBlockK, ptn * Cfg::kTileN + int(cta_rank) * Cfg::kCtaN);
+      };
+      if (pf > 0)
+        for (int j = 0; j < pf; ++j) prefetch_unit(worker, j);
       uint32_t stage = 0, phase = 0;
       bool ok = true;
       for (int t = worker; ok && t < num_tiles; t += num_workers) {
@@ -208,6 +225,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         const int a_row = tm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM;
         const int b_row = tn * Cfg::kTileN + int(cta_rank) * Cfg::kCtaN;
         for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if (pf > 0) prefetch_unit(t, kb + pf);
           if (!mbarrier_wait(empty_bar(stage), phase ^ 1u, args.timeout_ns)) {
             record_status(args.status, kStatusProducerTimeout);
             ok = false;

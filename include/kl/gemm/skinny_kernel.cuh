@@ -32,22 +32,25 @@
 
 namespace kl::gemm {
 
-template <typename InT, typename OutT, int TokPad, int Stages>
+template <typename InT, typename OutT, int TokPad, int Stages, int WSub = 1>
 struct SkinnyConfig {
   using in_type = InT;
   using out_type = OutT;
   static constexpr int kThreads = 192;
-  static constexpr int kTileW = 128;                       // weight rows per tile (UMMA M)
+  static constexpr int kSub = WSub;                        // 128-row weight boxes per tile
+  static constexpr int kTileW = 128 * WSub;                // weight rows per tile
   static constexpr int kTok = TokPad;                      // UMMA N
   static constexpr int kBlockK = 128 / int(sizeof(InT));   // one 128-byte swizzle span
   static constexpr int kUmmaK = 32 / int(sizeof(InT));
   static constexpr int kStages = Stages;
   static constexpr int kNumAcc = 2;
-  static constexpr int kTmemCols = (TokPad * 2 <= 32) ? 32 : (TokPad * 2 <= 64) ? 64 : (TokPad * 2 <= 128) ? 128
-                                 : (TokPad * 2 <= 256) ? 256 : 512;
-  using WTile = SmemTile<InT, kTileW, kBlockK>;
+  static constexpr int kAccCols = TokPad * WSub;           // one accumulator: WSub blocks of TokPad columns
+  static constexpr int kTmemCols = (kAccCols * 2 <= 32) ? 32 : (kAccCols * 2 <= 64) ? 64 : (kAccCols * 2 <= 128) ? 128
+                                 : (kAccCols * 2 <= 256) ? 256 : 512;
+  using WTile = SmemTile<InT, 128, kBlockK>;               // one UMMA M = 128 box
   using XTile = SmemTile<InT, kTok, kBlockK>;
-  static constexpr uint32_t kWBytes = WTile::bytes;
+  static constexpr uint32_t kWBoxBytes = WTile::bytes;
+  static constexpr uint32_t kWBytes = WTile::bytes * WSub;
   static constexpr uint32_t kXBytes = XTile::bytes;
   static constexpr uint32_t kOffW = 0;
   static constexpr uint32_t kOffX = kStages * kWBytes;
@@ -56,8 +59,10 @@ struct SkinnyConfig {
   static constexpr uint32_t kOffSlot = kOffBar + 8 * kNumBars;
   static constexpr uint32_t kSmemBytes = kOffSlot + 16 + 1024;
   static constexpr bool kIsF8 = sizeof(InT) == 1;
-  static constexpr uint32_t kIdesc = mma_instr_desc<InT, InT, float, kTileW, kTok>();
+  static constexpr uint32_t kIdesc = mma_instr_desc<InT, InT, float, 128, kTok>();
 
+  static_assert(WSub == 1 || WSub == 2, "one or two 128-row weight boxes per tile");
+  static_assert(kAccCols * 2 <= 512, "two accumulators must fit in TMEM");
   static_assert(TokPad == 16 || (TokPad % 32 == 0 && TokPad <= 256), "token tile: 16 or a multiple of 32 up to 256");
   static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
   static_assert(kWBytes % 1024 == 0 && kXBytes % 1024 == 0, "stages keep 1 KB alignment");
@@ -65,7 +70,7 @@ struct SkinnyConfig {
 
 struct SkinnyArgs {
   int m, n, k;            // C[m, n], m = tokens
-  int n_tiles, k_blocks;  // weight tiles (of 128 rows) and K-blocks per tile
+  int n_tiles, k_blocks;  // weight tiles (of kTileW rows) and K-blocks per tile
   long long total_units;  // n_tiles * k_blocks
   int grid;               // CTAs (each owns one contiguous unit range)
   float alpha;
@@ -74,16 +79,20 @@ struct SkinnyArgs {
   void* c;                // C, row-major [m, ldc]
   long long ldc;
   int* tickets;           // [n_tiles][4] arrival counters, zero between calls
-  float* slots;           // [n_tiles + grid - 1][TokPad][128] fp32 partials
+  float* slots;           // [n_tiles + grid - 1][TokPad][tile rows] fp32 partials
   int* status;
   unsigned long long timeout_ns;
+  int prefetch;           // L2 prefetch distance for weight tiles, in units (0 = off)
 };
 
 struct SkinnyParams {
-  CUtensorMap map_w;  // B [N, K], box {kBlockK, 128}
+  CUtensorMap map_w;  // B [N, K], box {kBlockK, 128} (kSub boxes per tile)
   CUtensorMap map_x;  // A [M, K], box {kBlockK, TokPad}
   SkinnyArgs args;
 };
+
+// Library default L2 prefetch distance of the skinny kernel, in K-blocks (0 = off).
+inline constexpr int kDefaultPrefetchSkinny = 0;
 
 // The CTA whose unit range contains unit f, for ranges [floor(i*T/G), floor((i+1)*T/G)).
 KL_HOST_DEVICE int cta_of_unit(long long f, long long total, int grid) {
@@ -176,9 +185,18 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_skinny_kernel(const __g
       const uint64_t keep_policy = l2_policy_evict_last();
       uint32_t stage = 0, phase = 0;
       bool ok = true;
+      const int pf = args.prefetch;
+      auto prefetch_unit = [&](long long v) {
+        if (v >= u_end) return;
+        const int pt = int(v / KB);
+        for (int sub = 0; sub < Cfg::kSub; ++sub)
+          tma_prefetch_l2_2d(&p.map_w, int(v - (long long)pt * KB) * Cfg::kBlockK, pt * Cfg::kTileW + sub * 128);
+      };
+      for (int j = 0; j < pf; ++j) prefetch_unit(u_begin + j);
       for (long long u = u_begin; u < u_end; ++u) {
         const int tile = int(u / KB);
         const int kb = int(u - (long long)tile * KB);
+        if (pf > 0) prefetch_unit(u + pf);
         if (!mbarrier_wait(empty_bar(stage), phase ^ 1u, args.timeout_ns)) {
           record_status(args.status, kStatusProducerTimeout);
           ok = false;
@@ -186,8 +204,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_skinny_kernel(const __g
         }
         mbarrier_arrive_expect_tx(full_bar(stage), Cfg::kWBytes + Cfg::kXBytes);
         const int kx = kb * Cfg::kBlockK;
-        tma_load_2d_hint(w_smem + stage * Cfg::kWBytes, &p.map_w, full_bar(stage), kx, tile * Cfg::kTileW,
-                         stream_policy);
+#pragma unroll
+        for (int sub = 0; sub < Cfg::kSub; ++sub)
+          tma_load_2d_hint(w_smem + stage * Cfg::kWBytes + sub * Cfg::kWBoxBytes, &p.map_w, full_bar(stage), kx,
+                           tile * Cfg::kTileW + sub * 128, stream_policy);
         tma_load_2d_hint(x_smem + stage * Cfg::kXBytes, &p.map_x, full_bar(stage), kx, 0, keep_policy);
         if (++stage == S) {
           stage = 0;
@@ -215,7 +235,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_skinny_kernel(const __g
           break;
         }
         tcgen05_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * TOK;
+        const uint32_t d_tmem = tmem_base + acc * Cfg::kAccCols;
         for (long long v = u; v < seg_end; ++v) {
           if (!mbarrier_wait(full_bar(stage), phase, args.timeout_ns)) {
             record_status(args.status, kStatusMmaTimeout);
@@ -229,10 +249,14 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_skinny_kernel(const __g
           for (int k = 0; k < Cfg::kBlockK / Cfg::kUmmaK; ++k) {
             const uint64_t koff = block_offset_16B<typename Cfg::WTile>(k);
             const uint32_t accumulate = (v != u || k != 0) ? 1u : 0u;
-            if constexpr (Cfg::kIsF8)
-              umma_f8_ss<1>(d_tmem, w_desc + koff, x_desc + koff, Cfg::kIdesc, accumulate);
-            else
-              umma_f16_ss<1>(d_tmem, w_desc + koff, x_desc + koff, Cfg::kIdesc, accumulate);
+#pragma unroll
+            for (int sub = 0; sub < Cfg::kSub; ++sub) {
+              const uint64_t wd = w_desc + ((sub * Cfg::kWBoxBytes) >> 4) + koff;
+              if constexpr (Cfg::kIsF8)
+                umma_f8_ss<1>(d_tmem + sub * TOK, wd, x_desc + koff, Cfg::kIdesc, accumulate);
+              else
+                umma_f16_ss<1>(d_tmem + sub * TOK, wd, x_desc + koff, Cfg::kIdesc, accumulate);
+            }
           }
           umma_commit<1>(empty_bar(stage));
           if (++stage == S) {
@@ -255,7 +279,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_skinny_kernel(const __g
     float alpha = args.alpha;
     if (args.scale_a != nullptr) alpha *= *args.scale_a;
     if (args.scale_b != nullptr) alpha *= *args.scale_b;
-    const int row = quarter * 32 + lane;  // weight row inside the tile = C column offset
+    const int lrow = quarter * 32 + lane;  // row inside a 128-row weight box
     uint32_t iter = 0;
     long long u = u_begin;
     while (u < u_end) {
@@ -272,29 +296,33 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_skinny_kernel(const __g
       const int first = cta_of_unit(tile_begin, args.total_units, args.grid);
       const int last = cta_of_unit(tile_begin + KB - 1, args.total_units, args.grid);
       const int contributors = last - first + 1;
-      const int col = tile * Cfg::kTileW + row;  // C column this thread owns
-      const bool col_ok = col < args.n;
-
       const int me = cta - first;
       const long long slot0 = (long long)tile + first;  // slots of this tile: slot0 .. slot0 + contributors - 1
       float* mine = args.slots + (slot0 + me) * (long long)(TOK * Cfg::kTileW);
       // Drain the accumulator 32 tokens at a time: straight to C when this CTA owns the whole
-      // tile, else into this contributor's slot (layout [token][128 rows]: 128-byte warp stores).
+      // tile, else into this contributor's slot (layout [token][tile rows]: 128-byte warp stores).
 #pragma unroll 1
-      for (int j0 = 0; j0 < TOK; j0 += 32) {
-        uint32_t r[32];
-        if constexpr (TOK % 32 == 0) {
-          tmem_ld_32x32b_x32(tmem_base + lane_base + acc * TOK + uint32_t(j0), r);
-        } else {
-          tmem_ld_32x32b_x16(tmem_base + lane_base + acc * TOK + uint32_t(j0), *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
-        }
-        tmem_wait_ld();
-        constexpr int kW = (TOK % 32 == 0) ? 32 : 16;
-        if (contributors == 1) {
-          if (col_ok) store_c_column<OutT, kW>(args, r, j0, col, alpha);
-        } else {
+      for (int sub = 0; sub < Cfg::kSub; ++sub) {
+        const int row = sub * 128 + lrow;          // weight row inside the tile
+        const int col = tile * Cfg::kTileW + row;  // = the C column this thread owns
+        const bool col_ok = col < args.n;
+#pragma unroll 1
+        for (int j0 = 0; j0 < TOK; j0 += 32) {
+          uint32_t r[32];
+          const uint32_t taddr = tmem_base + lane_base + acc * Cfg::kAccCols + uint32_t(sub * TOK + j0);
+          if constexpr (TOK % 32 == 0) {
+            tmem_ld_32x32b_x32(taddr, r);
+          } else {
+            tmem_ld_32x32b_x16(taddr, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+          }
+          tmem_wait_ld();
+          constexpr int kW = (TOK % 32 == 0) ? 32 : 16;
+          if (contributors == 1) {
+            if (col_ok) store_c_column<OutT, kW>(args, r, j0, col, alpha);
+          } else {
 #pragma unroll
-          for (int q = 0; q < kW; ++q) mine[(j0 + q) * Cfg::kTileW + row] = __uint_as_float(r[q]);
+            for (int q = 0; q < kW; ++q) mine[(j0 + q) * Cfg::kTileW + row] = __uint_as_float(r[q]);
+          }
         }
       }
       tcgen05_fence_before();
@@ -312,20 +340,25 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_skinny_kernel(const __g
           // slots in contributor order, so the result does not depend on who finished last.
           __threadfence();
 #pragma unroll 1
-          for (int j0 = 0; j0 < TOK; j0 += 32) {
-            float sum[32];
+          for (int sub = 0; sub < Cfg::kSub; ++sub) {
+            const int row = sub * 128 + lrow;
+            const int col = tile * Cfg::kTileW + row;
+#pragma unroll 1
+            for (int j0 = 0; j0 < TOK; j0 += 32) {
+              float sum[32];
 #pragma unroll
-            for (int q = 0; q < 32; ++q) sum[q] = 0.0f;
-            for (int s2 = 0; s2 < contributors; ++s2) {
-              const float* part = args.slots + (slot0 + s2) * (long long)(TOK * Cfg::kTileW);
+              for (int q = 0; q < 32; ++q) sum[q] = 0.0f;
+              for (int s2 = 0; s2 < contributors; ++s2) {
+                const float* part = args.slots + (slot0 + s2) * (long long)(TOK * Cfg::kTileW);
 #pragma unroll
-              for (int q = 0; q < 32; ++q)
-                if (j0 + q < TOK) sum[q] += __ldcg(part + (j0 + q) * Cfg::kTileW + row);
+                for (int q = 0; q < 32; ++q)
+                  if (j0 + q < TOK) sum[q] += __ldcg(part + (j0 + q) * Cfg::kTileW + row);
+              }
+              uint32_t r[32];
+#pragma unroll
+              for (int q = 0; q < 32; ++q) r[q] = __float_as_uint(sum[q]);
+              if (col < args.n) store_c_column<OutT, 32>(args, r, j0, col, alpha);
             }
-            uint32_t r[32];
-#pragma unroll
-            for (int q = 0; q < 32; ++q) r[q] = __float_as_uint(sum[q]);
-            if (col_ok) store_c_column<OutT, 32>(args, r, j0, col, alpha);
           }
           if (lane == 0) args.tickets[tile * 4 + quarter] = 0;  // re-arm for the next call
         }

@@ -75,7 +75,9 @@ typedef struct kl_gemm_desc {
   int32_t algo;           /* kl_algo */
   int32_t group_m;        /* tile-raster group height in tiles; 0 = library default */
   int32_t max_ctas;       /* cap on resident CTAs; 0 = one per SM */
-  int32_t split_k;        /* KL_ALGO_SKINNY only: 0 = library default */
+  int32_t variant;        /* algorithm variant, 0 = library default. KL_ALGO_SKINNY: weight rows
+                             per tile / 128 (1 or 2) */
+  int32_t prefetch;       /* L2 prefetch distance in K-blocks: 0 = library default, < 0 = off */
 } kl_gemm_desc;
 
 /* Library version: major * 10000 + minor * 100 + patch. */
@@ -102,6 +104,16 @@ KL_API kl_status kl_gemm_workspace_size(const kl_gemm_desc* desc, size_t* bytes)
  * again. (kl_gemm without a workspace uses one library-owned buffer per device, with the same
  * no-overlap rule, and does all of this itself.) */
 KL_API kl_status kl_gemm_ws(const kl_gemm_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+
+/* No reference counterpart. The same GEMM with A, B and C in HOST memory (page-locked for full
+ * speed): desc->a, desc->b, desc->c are host pointers with desc's leading dimensions, and dev_a,
+ * dev_b, dev_c are device buffers of at least m*lda, n*ldb, m*ldc elements that the call uses as
+ * staging. The library copies A in, then streams B in `chunks` column blocks of C (0 = choose; a
+ * block is a multiple of 256 columns) so that the copy in of block j+1, the GEMM of block j and
+ * the copy back of block j-1 overlap. Ordered after the work already on `stream`; `stream` waits
+ * for C to be on the host. The call only queues work: synchronise `stream` before reading C. */
+KL_API kl_status kl_gemm_host(const kl_gemm_desc* desc, void* dev_a, void* dev_b, void* dev_c, int32_t chunks,
+                              void* stream);
 
 /* No counterpart in the reference. The skinny (KL_ALGO_SKINNY) GEMM for callers that may not
  * allocate device memory while they run and cannot lend the library a workspace (for example an

@@ -32,7 +32,7 @@ EXPORTED = (
     "kl_version", "kl_last_error", "kl_gemm", "kl_gemm_workspace_size", "kl_gemm_ws",
     "kl_set_wait_timeout_ns", "kl_read_status", "kl_probe_wait_timeout", "kl_smem_tile_offset",
     "kl_tma_box_geometry", "kl_tma_box_position", "kl_umma_smem_desc", "kl_mma_instr_desc",
-    "kl_make_tma_desc", "kl_gemm_skinny_noalloc",
+    "kl_make_tma_desc", "kl_gemm_skinny_noalloc", "kl_gemm_host",
 )
 
 
@@ -55,7 +55,8 @@ class GemmDesc(ctypes.Structure):
         ("alpha", ctypes.c_float),
         ("scale_a", ctypes.c_void_p), ("scale_b", ctypes.c_void_p),
         ("algo", ctypes.c_int32), ("group_m", ctypes.c_int32),
-        ("max_ctas", ctypes.c_int32), ("split_k", ctypes.c_int32),
+        ("max_ctas", ctypes.c_int32), ("variant", ctypes.c_int32),
+        ("prefetch", ctypes.c_int32),
     ]
 
 
@@ -91,6 +92,7 @@ def lib() -> ctypes.CDLL:
             "kl_mma_instr_desc": (i32, [i32, i32, i32, i32, i32, P(u32)]),
             "kl_make_tma_desc": (i32, [i32, i32, i32, i32, i32, vp, i32, P(i64), P(i64), vp]),
             "kl_gemm_skinny_noalloc": (i32, [P(GemmDesc), vp]),
+            "kl_gemm_host": (i32, [P(GemmDesc), vp, vp, vp, i32, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -168,7 +170,7 @@ def _dtype_code(t) -> int:
 
 
 def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, group_m=0, max_ctas=0,
-              split_k=0) -> GemmDesc:
+              variant=0, prefetch=0) -> GemmDesc:
     """Descriptor for C = alpha * A . B^T on torch CUDA tensors (A [M,K], B [N,K], C [M,N])."""
     for name, t in (("a", a), ("b", b), ("c", c)):
         if t.dim() != 2 or t.stride(1) != 1:
@@ -181,17 +183,17 @@ def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, gr
                     c=c.data_ptr(), ldc=c.stride(0), ab_type=_dtype_code(a.dtype), c_type=_dtype_code(c.dtype),
                     alpha=float(alpha), scale_a=None if scale_a is None else scale_a.data_ptr(),
                     scale_b=None if scale_b is None else scale_b.data_ptr(), algo=algo, group_m=group_m,
-                    max_ctas=max_ctas, split_k=split_k)
+                    max_ctas=max_ctas, variant=variant, prefetch=prefetch)
 
 
 def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
-         group_m=0, max_ctas=0, split_k=0, workspace=None, stream=None):
+         group_m=0, max_ctas=0, variant=0, prefetch=0, workspace=None, stream=None):
     """out = alpha * a @ b.T [* scale_a * scale_b] on the current CUDA stream, via kl_gemm."""
     import torch
 
     if out is None:
         out = torch.empty((a.shape[0], b.shape[0]), dtype=out_dtype or torch.bfloat16, device=a.device)
-    d = gemm_desc(a, b, out, alpha, scale_a, scale_b, algo, group_m, max_ctas, split_k)
+    d = gemm_desc(a, b, out, alpha, scale_a, scale_b, algo, group_m, max_ctas, variant, prefetch)
     s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
     if workspace is None:
         check(lib().kl_gemm(ctypes.byref(d), ctypes.c_void_p(s)))
@@ -199,6 +201,20 @@ def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=Non
         check(lib().kl_gemm_ws(ctypes.byref(d), ctypes.c_void_p(workspace.data_ptr()), workspace.numel() *
                                workspace.element_size(), ctypes.c_void_p(s)))
     return out
+
+
+def gemm_host(a_host, b_host, c_host, a_dev, b_dev, c_dev, *, alpha=1.0, scale_a=None, scale_b=None,
+              algo=ALGO_AUTO, chunks=0, stream=None):
+    """c_host = alpha * a_host @ b_host.T with host (ideally pinned) tensors, through kl_gemm_host:
+    the copies in and out overlap the GEMM. a_dev/b_dev/c_dev are device staging tensors of the
+    same shapes. Returns c_host once the stream has been synchronised."""
+    import torch
+
+    d = gemm_desc(a_host, b_host, c_host, alpha, scale_a, scale_b, algo)
+    s = stream if stream is not None else torch.cuda.current_stream(a_dev.device).cuda_stream
+    check(lib().kl_gemm_host(ctypes.byref(d), ctypes.c_void_p(a_dev.data_ptr()), ctypes.c_void_p(b_dev.data_ptr()),
+                             ctypes.c_void_p(c_dev.data_ptr()), int(chunks), ctypes.c_void_p(s)))
+    return c_host
 
 
 def workspace_size(a, b, c, **kw) -> int:

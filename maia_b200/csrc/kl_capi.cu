@@ -158,6 +158,7 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
   pr.scale_b = d->scale_b;
   pr.group_m = d->group_m;
   pr.max_ctas = d->max_ctas;
+  pr.prefetch = d->prefetch;
 
   int algo = d->algo;
   if (algo == KL_ALGO_AUTO) algo = kl::capi::choose_algo(*d);

@@ -1,0 +1,124 @@
+// kl_gemm_host: a GEMM whose operands and result live in host memory. The library moves A to the
+// device, then streams B in column blocks of C, so that the host-to-device copies of block j+1,
+// the GEMM of block j and the device-to-host copy of block j-1 run at the same time on three
+// streams (two copy engines and the SMs). Chained with events; ordered after and before the
+// caller's stream.
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include <kl_gemm.h>
+
+#include "kl_internal.cuh"
+
+namespace {
+
+struct HostPipe {
+  cudaStream_t in = nullptr, mm = nullptr, out = nullptr;
+  cudaEvent_t start = nullptr, done = nullptr;
+  std::vector<cudaEvent_t> loaded, computed;
+};
+
+std::mutex g_pipe_mutex;
+HostPipe g_pipes[64];
+
+// Called with g_pipe_mutex held.
+kl_status get_pipe(int dev, int chunks, HostPipe** out) {
+  HostPipe& p = g_pipes[dev];
+  cudaError_t e = cudaSuccess;
+  if (p.in == nullptr) {
+    if ((e = cudaStreamCreateWithFlags(&p.in, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaStreamCreateWithFlags(&p.mm, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaStreamCreateWithFlags(&p.out, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&p.start, cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&p.done, cudaEventDisableTiming)) != cudaSuccess)
+      return kl::capi::cuda_fail(e, "kl_gemm_host: stream/event creation");
+  }
+  while (int(p.loaded.size()) < chunks) {
+    cudaEvent_t a = nullptr, b = nullptr;
+    if ((e = cudaEventCreateWithFlags(&a, cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&b, cudaEventDisableTiming)) != cudaSuccess)
+      return kl::capi::cuda_fail(e, "kl_gemm_host: event creation");
+    p.loaded.push_back(a);
+    p.computed.push_back(b);
+  }
+  *out = &p;
+  return KL_OK;
+}
+
+int elem_bytes(int32_t t) {
+  return (t == KL_BF16 || t == KL_F16) ? 2 : (t == KL_E4M3 || t == KL_E5M2 || t == KL_I8 || t == KL_U8) ? 1 : 4;
+}
+
+}  // namespace
+
+extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_b, void* dev_c, int32_t chunks,
+                                  void* stream_ptr) {
+  using kl::capi::cuda_fail;
+  using kl::capi::fail;
+  if (h == nullptr || dev_a == nullptr || dev_b == nullptr || dev_c == nullptr)
+    return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_host: null argument");
+  if (h->m <= 0 || h->n <= 0 || h->k <= 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_host: m, n and k must be positive");
+  if (h->lda < h->k || h->ldb < h->k || h->ldc < h->n) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_host: leading dimension too small");
+  cudaStream_t caller = static_cast<cudaStream_t>(stream_ptr);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(KL_ERR_NOT_SUPPORTED, "device index above 63");
+
+  // Column blocks of C (rows of B): multiples of 256 so every block starts on a tile boundary and
+  // a 16-byte-aligned column of C.
+  if (chunks <= 0) chunks = int(std::min<int64_t>(8, std::max<int64_t>(1, h->n / 1024)));
+  int64_t block = (h->n + chunks - 1) / chunks;
+  block = (block + 255) / 256 * 256;
+  chunks = int((h->n + block - 1) / block);
+
+  // One pipeline per device: calls from several host threads take turns enqueueing.
+  std::lock_guard<std::mutex> lock(g_pipe_mutex);
+  HostPipe* p = nullptr;
+  kl_status s = get_pipe(dev, chunks, &p);
+  if (s != KL_OK) return s;
+
+  const int eab = elem_bytes(h->ab_type), ec = elem_bytes(h->c_type);
+  const char* ha = static_cast<const char*>(h->a);
+  const char* hb = static_cast<const char*>(h->b);
+  char* hc = static_cast<char*>(h->c);
+  char* da = static_cast<char*>(dev_a);
+  char* db = static_cast<char*>(dev_b);
+  char* dc = static_cast<char*>(dev_c);
+
+  // Start after everything already queued on the caller's stream.
+  if ((e = cudaEventRecord(p->start, caller)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  if ((e = cudaStreamWaitEvent(p->in, p->start, 0)) != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
+  if ((e = cudaMemcpyAsync(da, ha, size_t(h->m) * h->lda * eab, cudaMemcpyHostToDevice, p->in)) != cudaSuccess)
+    return cuda_fail(e, "kl_gemm_host: copy of A");
+  for (int j = 0; j < chunks; ++j) {
+    const int64_t n0 = int64_t(j) * block, nj = std::min<int64_t>(block, h->n - n0);
+    e = cudaMemcpyAsync(db + size_t(n0) * h->ldb * eab, hb + size_t(n0) * h->ldb * eab, size_t(nj) * h->ldb * eab,
+                        cudaMemcpyHostToDevice, p->in);
+    if (e != cudaSuccess) return cuda_fail(e, "kl_gemm_host: copy of B");
+    if ((e = cudaEventRecord(p->loaded[j], p->in)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+    if ((e = cudaStreamWaitEvent(p->mm, p->loaded[j], 0)) != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
+    kl_gemm_desc d = *h;
+    d.n = nj;
+    d.a = da;
+    d.b = db + size_t(n0) * h->ldb * eab;
+    d.c = dc + size_t(n0) * ec;
+    s = kl_gemm(&d, p->mm);
+    if (s != KL_OK) return s;
+    if ((e = cudaEventRecord(p->computed[j], p->mm)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+    if ((e = cudaStreamWaitEvent(p->out, p->computed[j], 0)) != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
+    e = cudaMemcpy2DAsync(hc + size_t(n0) * ec, size_t(h->ldc) * ec, dc + size_t(n0) * ec, size_t(h->ldc) * ec,
+                          size_t(nj) * ec, size_t(h->m), cudaMemcpyDeviceToHost, p->out);
+    if (e != cudaSuccess) return cuda_fail(e, "kl_gemm_host: copy of C");
+  }
+  // The caller's stream continues once C is back on the host.
+  if ((e = cudaEventRecord(p->done, p->out)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  if ((e = cudaStreamWaitEvent(caller, p->done, 0)) != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
+  return KL_OK;
+}

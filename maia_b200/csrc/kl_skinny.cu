@@ -21,16 +21,23 @@ namespace {
 using namespace kl::gemm;
 
 constexpr size_t kAlign = 256;
+constexpr int kDefaultSkinnySub = 1;
 size_t round_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 int token_tile(int64_t m) { return m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256; }
 
-// Stages that fit next to the tile sizes (weights 16 KB, activations tok x 128 B per stage).
-template <typename InT, typename OutT, int Tok>
-using Skinny = SkinnyConfig<InT, OutT, Tok, (Tok == 16 ? 11 : Tok == 32 ? 10 : Tok == 64 ? 8 : Tok == 128 ? 6 : 4)>;
+// Stages that fit next to the tile sizes (weights 16 KB per 128-row box, activations tok x 128 B
+// per stage) in ~200 KB of shared memory.
+constexpr int skinny_stages(int tok, int sub) {
+  return sub == 1 ? (tok == 16 ? 11 : tok == 32 ? 10 : tok == 64 ? 8 : tok == 128 ? 6 : 4)
+                  : (tok <= 32 ? 6 : tok == 64 ? 5 : 4);
+}
+template <typename InT, typename OutT, int Tok, int Sub>
+using Skinny = SkinnyConfig<InT, OutT, Tok, skinny_stages(Tok, Sub), Sub>;
 
 struct Plan {
   int tok = 0;
+  int sub = 1;  // 128-row weight boxes per tile
   int n_tiles = 0, k_blocks = 0, grid = 0;
   long long total = 0;
   size_t ticket_bytes = 0, slot_bytes = 0;
@@ -48,13 +55,16 @@ kl_status make_plan(kl_gemm_desc const& d, Plan* p) {
   const int elem = d.ab_type == KL_E4M3 ? 1 : 2;
   const int block_k = 128 / elem;
   p->tok = token_tile(d.m);
-  p->n_tiles = int((d.n + 127) / 128);
+  p->sub = d.variant == 2 ? 2 : d.variant == 1 ? 1 : kDefaultSkinnySub;
+  if (p->sub == 2 && p->tok > 128) p->sub = 1;  // two 256-token accumulators would not fit in TMEM
+  if (d.variant < 0 || d.variant > 2) return fail(KL_ERR_INVALID_ARGUMENT, "KL_ALGO_SKINNY variant must be 0, 1 or 2");
+  p->n_tiles = int((d.n + 128 * p->sub - 1) / (128 * p->sub));
   p->k_blocks = int((d.k + block_k - 1) / block_k);
   p->total = (long long)p->n_tiles * p->k_blocks;
   int cap = d.max_ctas > 0 ? std::min(d.max_ctas, sms) : sms;
   p->grid = int(std::min<long long>(cap, p->total));
   p->ticket_bytes = round_up(size_t(p->n_tiles) * 4 * sizeof(int));
-  p->slot_bytes = size_t(p->n_tiles + p->grid - 1) * size_t(p->tok) * 128 * sizeof(float);
+  p->slot_bytes = size_t(p->n_tiles + p->grid - 1) * size_t(p->tok) * 128 * p->sub * sizeof(float);
   return KL_OK;
 }
 
@@ -96,6 +106,7 @@ kl_status launch(kl_gemm_desc const& d, Plan const& pl, void* ws, cudaStream_t s
   a.slots = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.ticket_bytes);
   a.status = status;
   a.timeout_ns = wait_timeout_ns();
+  a.prefetch = d.prefetch > 0 ? d.prefetch : d.prefetch < 0 ? 0 : kDefaultPrefetchSkinny;
   gemm_skinny_kernel<Cfg><<<pl.grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? KL_OK : cuda_fail(e, "skinny launch");
@@ -103,12 +114,20 @@ kl_status launch(kl_gemm_desc const& d, Plan const& pl, void* ws, cudaStream_t s
 
 template <typename InT, typename OutT>
 kl_status dispatch_tok(kl_gemm_desc const& d, Plan const& pl, void* ws, cudaStream_t stream) {
+  if (pl.sub == 2) {
+    switch (pl.tok) {
+      case 16: return launch<Skinny<InT, OutT, 16, 2>>(d, pl, ws, stream);
+      case 32: return launch<Skinny<InT, OutT, 32, 2>>(d, pl, ws, stream);
+      case 64: return launch<Skinny<InT, OutT, 64, 2>>(d, pl, ws, stream);
+      default: return launch<Skinny<InT, OutT, 128, 2>>(d, pl, ws, stream);
+    }
+  }
   switch (pl.tok) {
-    case 16: return launch<Skinny<InT, OutT, 16>>(d, pl, ws, stream);
-    case 32: return launch<Skinny<InT, OutT, 32>>(d, pl, ws, stream);
-    case 64: return launch<Skinny<InT, OutT, 64>>(d, pl, ws, stream);
-    case 128: return launch<Skinny<InT, OutT, 128>>(d, pl, ws, stream);
-    default: return launch<Skinny<InT, OutT, 256>>(d, pl, ws, stream);
+    case 16: return launch<Skinny<InT, OutT, 16, 1>>(d, pl, ws, stream);
+    case 32: return launch<Skinny<InT, OutT, 32, 1>>(d, pl, ws, stream);
+    case 64: return launch<Skinny<InT, OutT, 64, 1>>(d, pl, ws, stream);
+    case 128: return launch<Skinny<InT, OutT, 128, 1>>(d, pl, ws, stream);
+    default: return launch<Skinny<InT, OutT, 256, 1>>(d, pl, ws, stream);
   }
 }
 

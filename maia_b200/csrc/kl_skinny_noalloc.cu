@@ -100,6 +100,7 @@ kl_status launch(kl_gemm_desc const& d, int n_tiles, int k_blocks, int grid, uns
   a.slots = reinterpret_cast<float*>(scratch + kTicketBytes);
   a.status = status;
   a.timeout_ns = kl::capi::wait_timeout_ns();
+  a.prefetch = d.prefetch > 0 ? d.prefetch : d.prefetch < 0 ? 0 : kDefaultPrefetchSkinny;
   gemm_skinny_kernel<Cfg><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? KL_OK : kl::capi::cuda_fail(e, "no-alloc skinny launch");

@@ -1,0 +1,41 @@
+"""PyTorch operators over the C ABI: torch.ops.kl.gemm and torch.ops.kl.gemm_fp8.
+
+Registered with torch.library so they compose with the rest of a PyTorch program (fake tensors
+for shape inference, the dispatcher, torch.compile graphs that call them as opaque ops). The work
+is the library's own kernels, launched on the tensors' current CUDA stream.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import ALGO_AUTO, gemm as _kl_gemm
+
+
+@torch.library.custom_op("kl::gemm", mutates_args=())
+def gemm(a: torch.Tensor, b: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16, alpha: float = 1.0) -> torch.Tensor:
+    """alpha * a @ b.T for bf16 a [M, K] and b [N, K] (K contiguous), out bf16 or fp32."""
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise TypeError("kl::gemm takes bf16 operands (use kl::gemm_fp8 for e4m3)")
+    out = torch.empty((a.shape[0], b.shape[0]), dtype=out_dtype, device=a.device)
+    return _kl_gemm(a, b, out, alpha=alpha, algo=ALGO_AUTO)
+
+
+@gemm.register_fake
+def _(a, b, out_dtype=torch.bfloat16, alpha=1.0):
+    return a.new_empty((a.shape[0], b.shape[0]), dtype=out_dtype)
+
+
+@torch.library.custom_op("kl::gemm_fp8", mutates_args=())
+def gemm_fp8(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor) -> torch.Tensor:
+    """(a @ b.T) * scale_a * scale_b for e4m3 a [M, K], b [N, K] and fp32 scalar scales; bf16 out."""
+    if a.dtype != torch.float8_e4m3fn or b.dtype != torch.float8_e4m3fn:
+        raise TypeError("kl::gemm_fp8 takes float8_e4m3fn operands")
+    out = torch.empty((a.shape[0], b.shape[0]), dtype=torch.bfloat16, device=a.device)
+    return _kl_gemm(a, b, out, scale_a=scale_a.float().contiguous(), scale_b=scale_b.float().contiguous(),
+                    algo=ALGO_AUTO)
+
+
+@gemm_fp8.register_fake
+def _(a, b, scale_a, scale_b):
+    return a.new_empty((a.shape[0], b.shape[0]), dtype=torch.bfloat16)

@@ -63,6 +63,14 @@ def test_persistent_few_ctas(cuda, algo):
     check(c, a, b, 1.0, BF16_TOL)
 
 
+@pytest.mark.parametrize("algo", [kl.ALGO_1CTA, kl.ALGO_2CTA], ids=["1cta", "2cta"])
+@pytest.mark.parametrize("prefetch", [3, 16])
+def test_l2_prefetch_keeps_results(cuda, algo, prefetch):
+    """L2 prefetch ahead of the loads (across tile boundaries too) changes no result."""
+    a, b, _, _ = random_inputs(640, 768, 1216, "bf16", seed=prefetch)
+    check(run_kl(a, b, "bf16", "bf16", cuda, algo, max_ctas=10, prefetch=prefetch), a, b, 1.0, BF16_TOL)
+
+
 def test_strided_operands(cuda):
     """Leading dimensions larger than the extents (padded rows) on A, B and C."""
     import torch
@@ -119,3 +127,29 @@ def test_wait_timeout_reports_instead_of_hanging(cuda):
     assert bits & 16
     a, b, _, _ = random_inputs(128, 256, 64, "bf16", seed=1)
     check(run_kl(a, b, "bf16", "bf16", cuda, kl.ALGO_1CTA), a, b, 1.0, BF16_TOL)
+
+
+def _sample_indices(n, tile, rng, extra=24):
+    """Rows (or columns) at every kind of boundary the kernels have, plus random ones."""
+    picks = {0, 1, 31, 32, 127, 128, 255, 256, 511, 512, n // 2 - 1, n // 2, n - 257, n - 256, n - 129, n - 128,
+             n - 1}
+    picks.update(int(x) for x in rng.integers(0, n, extra))
+    return np.array(sorted(p for p in picks if 0 <= p < n))
+
+
+@pytest.mark.parametrize("name, algo", [("c3_8192_bf16", kl.ALGO_2CTA), ("c3_8192_bf16", kl.ALGO_1CTA),
+                                        ("c4_16384x16384x8192_e4m3", kl.ALGO_2CTA)],
+                         ids=["c3-2cta", "c3-1cta", "c4-fp8-2cta"])
+def test_full_size_sampled_rows_and_columns(cuda, name, algo):
+    """The benchmark-size GEMMs, checked on whole rows and whole columns of C that cross every tile,
+    CTA-pair and raster-group boundary, plus random ones (the fp64 oracle on all 5e11+ entries
+    would take hours on the host)."""
+    w = wl.ALL[name]
+    a, b, sa, sb = wl.make_inputs(w)
+    c = run_kl(a, b, w.dtype, w.out, cuda, algo, scale_a=sa, scale_b=sb)
+    rng = np.random.default_rng(7)
+    rows = _sample_indices(w.m, 256, rng)
+    cols = _sample_indices(w.n, 256, rng)
+    tol = BF16_TOL if w.dtype == "bf16" else FP8_TOL
+    check(c[rows, :], a[rows], b, sa * sb, tol)
+    check(c[:, cols], a, b[cols], sa * sb, tol)

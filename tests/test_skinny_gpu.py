@@ -20,28 +20,34 @@ BF16_TOL = 1e-2
 FP8_TOL = 5e-2
 
 
+@pytest.mark.parametrize("variant", [1, 2], ids=["w128", "w256"])
 @pytest.mark.parametrize("m", [16, 64, 128])
-def test_c5_decode_shapes(cuda, m):
+def test_c5_decode_shapes(cuda, m, variant):
     w = wl.C5[m]
     a, b, _, _ = wl.make_inputs(w)
-    c = run_kl(a, b, "bf16", "bf16", cuda, kl.ALGO_SKINNY)
+    c = run_kl(a, b, "bf16", "bf16", cuda, kl.ALGO_SKINNY, variant=variant)
     check(c, a, b, 1.0, BF16_TOL)
 
 
+@pytest.mark.parametrize("variant", [1, 2], ids=["w128", "w256"])
 @pytest.mark.parametrize("shape", [(1, 8, 64), (5, 136, 200), (17, 1000, 512), (33, 640, 1096), (100, 384, 2048),
                                    (200, 256, 640), (256, 520, 320), (128, 128, 64)])
-def test_ragged(cuda, shape):
+def test_ragged(cuda, shape, variant):
     m, n, k = shape
     a, b, _, _ = random_inputs(m, n, k, "bf16", seed=m + 3 * n + 7 * k)
-    check(run_kl(a, b, "bf16", "bf16", cuda, kl.ALGO_SKINNY), a, b, 1.0, BF16_TOL)
-    check(run_kl(a, b, "bf16", "f32", cuda, kl.ALGO_SKINNY), a, b, 1.0, BF16_TOL)
+    check(run_kl(a, b, "bf16", "bf16", cuda, kl.ALGO_SKINNY, variant=variant), a, b, 1.0, BF16_TOL)
+    check(run_kl(a, b, "bf16", "f32", cuda, kl.ALGO_SKINNY, variant=variant), a, b, 1.0, BF16_TOL)
 
 
+@pytest.mark.parametrize("variant", [1, 2], ids=["w128", "w256"])
 @pytest.mark.parametrize("ctas", [1, 3, 7, 50])
-def test_tiles_split_across_ctas(cuda, ctas):
-    """Few CTAs over many units: tiles shared by 2+ CTAs go through the slot reduction."""
+@pytest.mark.parametrize("prefetch", [-1, 24])
+def test_tiles_split_across_ctas(cuda, ctas, prefetch, variant):
+    """Few CTAs over many units: tiles shared by 2+ CTAs go through the slot reduction (with and
+    without L2 prefetch of the weight tiles ahead of the loads)."""
     a, b, _, _ = random_inputs(48, 5 * 128 + 40, 64 * 37, "bf16", seed=ctas)
-    check(run_kl(a, b, "bf16", "bf16", cuda, kl.ALGO_SKINNY, max_ctas=ctas), a, b, 1.0, BF16_TOL)
+    check(run_kl(a, b, "bf16", "bf16", cuda, kl.ALGO_SKINNY, max_ctas=ctas, prefetch=prefetch, variant=variant),
+          a, b, 1.0, BF16_TOL)
 
 
 def test_deterministic_and_rearmed(cuda):
@@ -88,11 +94,12 @@ def test_caller_workspace(cuda):
     assert e.value.status == kl.KL_ERR_INVALID_ARGUMENT
 
 
+@pytest.mark.parametrize("variant", [1, 2], ids=["w128", "w256"])
 @pytest.mark.parametrize("shape", [(16, 1024, 2048), (100, 640, 1024)])
-def test_e4m3(cuda, shape):
+def test_e4m3(cuda, shape, variant):
     m, n, k = shape
     a, b, sa, sb = random_inputs(m, n, k, "e4m3", seed=k)
-    c = run_kl(a, b, "e4m3", "bf16", cuda, kl.ALGO_SKINNY, scale_a=sa, scale_b=sb)
+    c = run_kl(a, b, "e4m3", "bf16", cuda, kl.ALGO_SKINNY, scale_a=sa, scale_b=sb, variant=variant)
     check(c, a, b, sa * sb, FP8_TOL)
 
 
