@@ -61,7 +61,7 @@ kl_status make_plan(kl_gemm_desc const& d, Plan* p) {
   p->n_tiles = int((d.n + 128 * p->sub - 1) / (128 * p->sub));
   p->k_blocks = int((d.k + block_k - 1) / block_k);
   p->total = (long long)p->n_tiles * p->k_blocks;
-  int cap = d.max_ctas > 0 ? std::min(d.max_ctas, sms) : sms;
+  int cap = d.max_ctas > 0 ? std::min(d.max_ctas, sms) : skinny_default_ctas(sms);
   p->grid = int(std::min<long long>(cap, p->total));
   p->ticket_bytes = round_up(size_t(p->n_tiles) * 4 * sizeof(int));
   p->slot_bytes = size_t(p->n_tiles + p->grid - 1) * size_t(p->tok) * 128 * p->sub * sizeof(float);

@@ -149,7 +149,7 @@ extern "C" kl_status kl_gemm_skinny_noalloc(const kl_gemm_desc* d, void* stream_
   const int n_tiles = int((d->n + 127) / 128);
   const int k_blocks = int((d->k + 128 / elem - 1) / (128 / elem));
   const long long total = (long long)n_tiles * k_blocks;
-  const int cap = d->max_ctas > 0 ? std::min(d->max_ctas, sms) : sms;
+  const int cap = d->max_ctas > 0 ? std::min(d->max_ctas, sms) : skinny_default_ctas(sms);
   const int grid = int(std::min<long long>(cap, total));
   const size_t slots = size_t(n_tiles + grid - 1) * size_t(tok) * 128 * sizeof(float);
   if (n_tiles > kMaxWeightTiles)
