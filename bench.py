@@ -228,6 +228,11 @@ def main():
         ev1.record(stream)
         barrier()
     dev_ms = ev0.elapsed_time(ev1) / args.steps
+    in_kernel = None
+    if w.m > 256 and args.algo in (0, kl.ALGO_1CTA, kl.ALGO_2CTA):
+        # One more launch, right after the timed ones, with every CTA stamping clock64 and
+        # %globaltimer: the SM clock the kernel really ran at (NVML may report the boost target).
+        in_kernel = kl.clock_probe(a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo, group_m=args.group_m)
     if kl.read_status() != 0:
         raise RuntimeError("a device-side wait timed out during the benchmark")
     dev_ms = max_over_ranks(dev_ms)
@@ -310,7 +315,7 @@ def main():
             "roofline": roofline,
             "gpu_launches": args.steps,
             "gemm_plus_allgather": gather,
-            "clocks": clocks.summary(),
+            "clocks": dict(clocks.summary(), in_kernel=in_kernel),
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w)

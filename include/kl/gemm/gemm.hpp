@@ -28,6 +28,7 @@ struct Problem {
   int group_m = 0;   // 0 = default for the config
   int max_ctas = 0;  // 0 = every SM
   int prefetch = 0;  // L2 prefetch distance in K-blocks: 0 = default, < 0 = off
+  unsigned long long* clock_probe = nullptr;  // device [4 * grid]: per CTA clock64/globaltimer at start and end
 };
 
 // Library defaults for the knobs a Problem leaves at 0.
@@ -130,6 +131,9 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   a.status = status;
   a.timeout_ns = timeout_ns;
   a.prefetch = pr.prefetch > 0 ? pr.prefetch : pr.prefetch < 0 ? 0 : kDefaultPrefetchTn;
+  a.c = pr.c;
+  a.ldc = pr.ldc;
+  a.clock_probe = pr.clock_probe;
 
   const int tiles = a.tiles_m * a.tiles_n;
   int workers = std::min(tiles, max_workers);

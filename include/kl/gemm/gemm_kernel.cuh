@@ -42,11 +42,14 @@ enum : int {
   kStatusDrainTimeout = 8,
 };
 
-template <typename InT, typename OutT, int CtaGroup, int BlockN, int Stages>
+template <typename InT, typename OutT, int CtaGroup, int BlockN, int Stages, bool DirectStore = false>
 struct TnConfig {
   using in_type = InT;
   using out_type = OutT;
   static constexpr int kCtaGroup = CtaGroup;
+  // true: the epilogue writes C straight from registers (16-byte vector stores per row) and the
+  // shared memory that would stage TMA stores goes to the operand ring instead.
+  static constexpr bool kDirectStore = DirectStore;
   static constexpr int kThreads = 192;
   static constexpr int kCtaM = 128;                    // rows of A (= TMEM lanes) per CTA
   static constexpr int kTileM = kCtaM * CtaGroup;      // rows of C per tile
@@ -72,7 +75,7 @@ struct TnConfig {
   static constexpr uint32_t kOffA = 0;
   static constexpr uint32_t kOffB = kOffA + kStages * kABytes;
   static constexpr uint32_t kOffC = kOffB + kStages * kBBytes;
-  static constexpr uint32_t kOffBar = kOffC + 8 * kCBytes;  // 4 epilogue warps x 2 buffers
+  static constexpr uint32_t kOffBar = kOffC + (DirectStore ? 0u : 8u * kCBytes);  // 4 epilogue warps x 2 buffers
   static constexpr uint32_t kNumBars = 2 * kStages + 2 * kNumAcc + 1;
   static constexpr uint32_t kOffSlot = kOffBar + 8 * kNumBars;
   static constexpr uint32_t kSmemBytes = kOffSlot + 16 + 1024;  // + slack to align the base to 1 KB
@@ -98,6 +101,9 @@ struct TnArgs {
   int* status;                  // device word; timeout bits are ORed in
   unsigned long long timeout_ns;
   int prefetch;                 // L2 prefetch distance, in K-blocks of the producer's sequence (0 = off)
+  void* c;                      // C and its row pitch in elements, for the direct-store epilogue
+  long long ldc;
+  unsigned long long* clock_probe;  // optional: per CTA {clock64, globaltimer} at start and end
 };
 
 struct TnParams {
@@ -132,6 +138,10 @@ KL_DEVICE uint32_t ld_shared_u32(uint32_t addr) {
   return v;
 }
 
+KL_DEVICE void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
 KL_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -160,6 +170,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
   const uint32_t drain_bar = bar0 + 8u * (2 * S + 2 * Cfg::kNumAcc);
 
   const TnArgs& args = p.args;
+  if (args.clock_probe != nullptr && threadIdx.x == 0) {
+    args.clock_probe[4 * blockIdx.x + 0] = clock64();
+    args.clock_probe[4 * blockIdx.x + 1] = globaltimer_ns();
+  }
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t cta_rank = (CG == 2) ? cluster_ctarank() : 0u;  // rank inside the pair
@@ -352,6 +366,41 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
           }
         }
         const int col = col0 + c * Cfg::kChunkCols;
+        if constexpr (Cfg::kDirectStore) {
+          // Each thread owns one row of the chunk (128 bytes of C): eight 16-byte stores, or
+          // element by element on the ragged right edge.
+          const int row = row0 + lane;
+          if (row < args.m && col < args.n) {
+            OutT* dst = static_cast<OutT*>(args.c) + (long long)row * args.ldc + col;
+            if (col + Cfg::kChunkCols <= args.n) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                if constexpr (sizeof(OutT) == 2) {
+                  const float* f = reinterpret_cast<const float*>(&v[8 * j]);
+                  st_global_v4(dst + 8 * j, pack_bf16x2(f[0] * alpha, f[1] * alpha),
+                               pack_bf16x2(f[2] * alpha, f[3] * alpha), pack_bf16x2(f[4] * alpha, f[5] * alpha),
+                               pack_bf16x2(f[6] * alpha, f[7] * alpha));
+                } else {
+                  const float* f = reinterpret_cast<const float*>(&v[4 * j]);
+                  st_global_v4(dst + 4 * j, __float_as_uint(f[0] * alpha), __float_as_uint(f[1] * alpha),
+                               __float_as_uint(f[2] * alpha), __float_as_uint(f[3] * alpha));
+                }
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < Cfg::kChunkCols; ++e) {  // unrolled: v stays in registers
+                if (col + e < args.n) {
+                  const float x = __uint_as_float(v[e]) * alpha;
+                  if constexpr (sizeof(OutT) == 2)
+                    dst[e] = __float2bfloat16_rn(x);
+                  else
+                    dst[e] = x;
+                }
+              }
+            }
+          }
+          continue;
+        } else {
         const bool store = row0 < args.m && col < args.n;
         const uint32_t buf = c_smem + uint32_t(ew * 2 + (nbuf & 1u)) * Cfg::kCBytes;
         // The buffer's previous store (two chunks ago) must have finished reading it.
@@ -382,9 +431,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
           tma_store_commit();  // one group per chunk, empty or not, so wait_read<1> tracks buffers
         }
         ++nbuf;
+        }
       }
     }
-    if (lane == 0) tma_store_wait<0>();
+    if constexpr (!Cfg::kDirectStore) {
+      if (lane == 0) tma_store_wait<0>();
+    }
   }
 
   // ------------------------------------------------------------------ teardown
@@ -398,6 +450,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
   if (warp == 1) {
     tcgen05_fence_after();
     tmem_dealloc<CG>(tmem_base, Cfg::kTmemCols);
+  }
+  if (args.clock_probe != nullptr && threadIdx.x == 0) {
+    args.clock_probe[4 * blockIdx.x + 2] = clock64();
+    args.clock_probe[4 * blockIdx.x + 3] = globaltimer_ns();
   }
 #endif  // KL_ARCH_SM100
 }

@@ -130,6 +130,13 @@ KL_API kl_status kl_gemm_host(const kl_gemm_desc* desc, void* dev_a, void* dev_b
  * on the array, so serialise them. desc->algo must be KL_ALGO_AUTO or KL_ALGO_SKINNY. */
 KL_API kl_status kl_gemm_skinny_noalloc(const kl_gemm_desc* desc, void* stream);
 
+/* No reference counterpart; a diagnostic. Runs one tile-kernel GEMM (KL_ALGO_1CTA / 2CTA) with
+ * every CTA recording {clock64, %globaltimer} at its start and end, waits for it, and copies the
+ * 4 words per CTA to `out` (host, out_words >= 4 * CTAs); *ctas receives the CTA count. The ratio
+ * of cycles to nanoseconds is the SM clock the kernel actually ran at. */
+KL_API kl_status kl_gemm_clock_probe(const kl_gemm_desc* desc, uint64_t* out, int32_t out_words, int32_t* ctas,
+                                     void* stream);
+
 /* Upper bound on any device-side wait, in nanoseconds (default 2e9). A wait that runs out sets a
  * bit in the device status word instead of hanging the GPU. */
 KL_API void kl_set_wait_timeout_ns(uint64_t ns);

@@ -32,7 +32,7 @@ EXPORTED = (
     "kl_version", "kl_last_error", "kl_gemm", "kl_gemm_workspace_size", "kl_gemm_ws",
     "kl_set_wait_timeout_ns", "kl_read_status", "kl_probe_wait_timeout", "kl_smem_tile_offset",
     "kl_tma_box_geometry", "kl_tma_box_position", "kl_umma_smem_desc", "kl_mma_instr_desc",
-    "kl_make_tma_desc", "kl_gemm_skinny_noalloc", "kl_gemm_host",
+    "kl_make_tma_desc", "kl_gemm_skinny_noalloc", "kl_gemm_host", "kl_gemm_clock_probe",
 )
 
 
@@ -93,6 +93,7 @@ def lib() -> ctypes.CDLL:
             "kl_make_tma_desc": (i32, [i32, i32, i32, i32, i32, vp, i32, P(i64), P(i64), vp]),
             "kl_gemm_skinny_noalloc": (i32, [P(GemmDesc), vp]),
             "kl_gemm_host": (i32, [P(GemmDesc), vp, vp, vp, i32, vp]),
+            "kl_gemm_clock_probe": (i32, [P(GemmDesc), P(u64), i32, P(i32), vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -215,6 +216,27 @@ def gemm_host(a_host, b_host, c_host, a_dev, b_dev, c_dev, *, alpha=1.0, scale_a
     check(lib().kl_gemm_host(ctypes.byref(d), ctypes.c_void_p(a_dev.data_ptr()), ctypes.c_void_p(b_dev.data_ptr()),
                              ctypes.c_void_p(c_dev.data_ptr()), int(chunks), ctypes.c_void_p(s)))
     return c_host
+
+
+def clock_probe(a, b, c, **kw) -> dict:
+    """Run one tile-kernel GEMM with per-CTA clock64/%globaltimer stamps; return the SM clock it ran at."""
+    import torch
+
+    d = gemm_desc(a, b, c, **kw)
+    buf = (ctypes.c_uint64 * (4 * 4096))()
+    ctas = ctypes.c_int32()
+    s = torch.cuda.current_stream(a.device).cuda_stream
+    check(lib().kl_gemm_clock_probe(ctypes.byref(d), buf, 4 * 4096, ctypes.byref(ctas), ctypes.c_void_p(s)))
+    mhz, us = [], []
+    for i in range(ctas.value):
+        cyc, ns = buf[4 * i + 2] - buf[4 * i], buf[4 * i + 3] - buf[4 * i + 1]
+        if ns > 0:
+            mhz.append(cyc / ns * 1e3)
+            us.append(ns / 1e3)
+    mhz.sort()
+    return {"ctas": ctas.value, "sm_mhz_median": mhz[len(mhz) // 2] if mhz else None,
+            "sm_mhz_min": mhz[0] if mhz else None, "sm_mhz_max": mhz[-1] if mhz else None,
+            "cta_us_max": max(us) if us else None}
 
 
 def workspace_size(a, b, c, **kw) -> int:

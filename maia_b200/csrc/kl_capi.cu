@@ -73,14 +73,17 @@ using Bf16F32_2 = TnConfig<kl::bf16, float, 2, 256, 6>;
 using E4m3Bf16_2 = TnConfig<kl::e4m3, kl::bf16, 2, 256, 6>;
 
 template <class Cfg>
-kl_status run(Problem const& pr, cudaStream_t stream) {
+kl_status run(Problem const& pr, cudaStream_t stream, LaunchInfo* info = nullptr) {
   int* status = nullptr;
   kl_status s = kl::capi::device_status_ptr(&status);
   if (s != KL_OK) return s;
-  cudaError_t e = launch_tn<Cfg>(pr, status, kl::capi::wait_timeout_ns(), stream);
+  cudaError_t e = launch_tn<Cfg>(pr, status, kl::capi::wait_timeout_ns(), stream, info);
   if (e != cudaSuccess) return cuda_fail(e, "kl_gemm launch");
   return KL_OK;
 }
+
+// Probe buffer for kl_gemm_clock_probe: one per device, 4 words per CTA, allocated on first use.
+unsigned long long* g_probe[64] = {};
 
 int elem_bytes_of(int32_t t) {
   switch (t) {
@@ -181,6 +184,52 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
 }
 
 kl_status kl_gemm(const kl_gemm_desc* d, void* stream) { return kl_gemm_ws(d, nullptr, 0, stream); }
+
+kl_status kl_gemm_clock_probe(const kl_gemm_desc* d, uint64_t* out, int32_t out_words, int32_t* ctas, void* stream_ptr) {
+  if (d == nullptr || out == nullptr || ctas == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null argument");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  int algo = d->algo == KL_ALGO_AUTO ? kl::capi::choose_algo(*d) : d->algo;
+  if (algo != KL_ALGO_1CTA && algo != KL_ALGO_2CTA)
+    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_clock_probe: tile kernels only (1CTA / 2CTA)");
+  if (d->m <= 0 || d->n <= 0 || d->k <= 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_clock_probe: empty problem");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(KL_ERR_NOT_SUPPORTED, "device index above 63");
+  if (g_probe[dev] == nullptr) {
+    e = cudaMalloc(&g_probe[dev], 4096 * 4 * sizeof(unsigned long long));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(clock probe)");
+  }
+  Problem pr;
+  pr.m = d->m; pr.n = d->n; pr.k = d->k;
+  pr.a = d->a; pr.lda = d->lda; pr.b = d->b; pr.ldb = d->ldb; pr.c = d->c; pr.ldc = d->ldc;
+  pr.alpha = d->alpha; pr.scale_a = d->scale_a; pr.scale_b = d->scale_b;
+  pr.group_m = d->group_m; pr.max_ctas = d->max_ctas; pr.prefetch = d->prefetch;
+  pr.clock_probe = g_probe[dev];
+  LaunchInfo info;
+  kl_status s = KL_OK;
+  try {
+    const bool pair = algo == KL_ALGO_2CTA;
+    if (d->ab_type == KL_BF16 && d->c_type == KL_BF16)
+      s = pair ? run<Bf16Bf16_2>(pr, stream, &info) : run<Bf16Bf16_1>(pr, stream, &info);
+    else if (d->ab_type == KL_BF16 && d->c_type == KL_F32)
+      s = pair ? run<Bf16F32_2>(pr, stream, &info) : run<Bf16F32_1>(pr, stream, &info);
+    else if (d->ab_type == KL_E4M3 && d->c_type == KL_BF16)
+      s = pair ? run<E4m3Bf16_2>(pr, stream, &info) : run<E4m3Bf16_1>(pr, stream, &info);
+    else
+      return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_clock_probe: unsupported types");
+  } catch (std::invalid_argument const& ex) {
+    return fail(KL_ERR_INVALID_ARGUMENT, ex.what());
+  }
+  if (s != KL_OK) return s;
+  if (info.grid > 4096 || 4 * info.grid > out_words) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_clock_probe: output too small");
+  e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  e = cudaMemcpy(out, g_probe[dev], size_t(4) * info.grid * sizeof(uint64_t), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(clock probe)");
+  *ctas = info.grid;
+  return KL_OK;
+}
 
 kl_status kl_read_status(int32_t* bits, int32_t clear) {
   int* status = nullptr;

@@ -153,3 +153,18 @@ def test_full_size_sampled_rows_and_columns(cuda, name, algo):
     tol = BF16_TOL if w.dtype == "bf16" else FP8_TOL
     check(c[rows, :], a[rows], b, sa * sb, tol)
     check(c[:, cols], a, b[cols], sa * sb, tol)
+
+
+def test_clock_probe_reports_the_kernel_clock(cuda):
+    """kl_gemm_clock_probe: every CTA stamps clock64/%globaltimer; the ratio is a plausible SM clock."""
+    import torch
+
+    a_bits, b_bits, _, _ = random_inputs(2048, 2048, 2048, "bf16", seed=2)
+    from gpu_util import to_device
+
+    a, b = to_device(a_bits, "bf16", cuda), to_device(b_bits, "bf16", cuda)
+    c = torch.empty((2048, 2048), dtype=torch.bfloat16, device=cuda)
+    r = kl.clock_probe(a, b, c, algo=kl.ALGO_2CTA)
+    assert r["ctas"] == 2 * (r["ctas"] // 2) > 0
+    assert 300 < r["sm_mhz_min"] <= r["sm_mhz_max"] < 2500
+    check(c.float().cpu().numpy(), a_bits, b_bits, 1.0, BF16_TOL)
