@@ -182,7 +182,7 @@ def main():
     from maia_b200 import sharding
 
     a_bits, b_bits, sa, sb = wl.make_inputs(w)
-    n_lo, n_hi = sharding.shard_range(w.n, world, rank)
+    n_lo, n_hi = sharding.shard_range(w.n, world, rank, align=256)
     b_bits = np.ascontiguousarray(b_bits[n_lo:n_hi])
     nshard = n_hi - n_lo
     np_view = np.int16 if w.dtype == "bf16" else np.uint8
@@ -263,7 +263,7 @@ def main():
     if dist is not None:
         def gather_step():
             kl.gemm(a, b, c, **kw)
-            sharding.gather_columns(c, w.n, dist)
+            sharding.gather_columns(c, w.n, dist, align=256)
 
         for _ in range(max(args.warmup, 3)):
             gather_step()
@@ -277,6 +277,30 @@ def main():
         g_ms = max_over_ranks(g0.elapsed_time(g1) / args.steps)
         gather = {"value": flops_total / (g_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": g_ms,
                   "what": "kl_gemm + NCCL all-gather of C and re-layout to [M, N] on every rank"}
+
+        # The same result with the gather fused into the GEMM: every tile is also TMA-stored into
+        # the other ranks' copies of C over NVLink (kl_gemm_gather).
+        shared = sharding.SharedC(w.m, w.n, odt, dev, dist)
+        c_view = shared.full[:, n_lo:n_hi]
+        peers = shared.peer_ptrs(n_lo)
+
+        def fused_step():
+            kl.gemm_gather(a, b, c_view, peers, scale_a=scale_a, scale_b=scale_b, algo=args.algo)
+
+        for _ in range(max(args.warmup, 3)):
+            fused_step()
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            fused_step()
+        f1.record(stream)
+        barrier()
+        f_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps)
+        gather["fused"] = {"value": flops_total / (f_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": f_ms,
+                           "what": "kl_gemm_gather: tiles stored to every rank's C by the GEMM epilogue (P2P over NVLink)"}
+        barrier()
+        shared.close()
 
     peaks, peak_src = load_peaks()
     per_rank_flops = 2.0 * w.m * nshard * w.k

@@ -29,6 +29,10 @@ struct Problem {
   int max_ctas = 0;  // 0 = every SM
   int prefetch = 0;  // L2 prefetch distance in K-blocks: 0 = default, < 0 = off
   unsigned long long* clock_probe = nullptr;  // device [4 * grid]: per CTA clock64/globaltimer at start and end
+  // Peer copies of C (same shape and pitch, in other GPUs' memory, already mapped into this
+  // process): the epilogue TMA-stores every tile there too. Not with the direct-store epilogue.
+  void* const* peer_c = nullptr;
+  int n_peers = 0;
 };
 
 // Library defaults for the knobs a Problem leaves at 0.
@@ -115,6 +119,13 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   p.map_a = make_tma_load<typename Cfg::ATile>(row_major_strided(static_cast<InT const*>(pr.a), pr.m, pr.k, pr.lda)).map;
   p.map_b = make_tma_load<typename Cfg::BTile>(row_major_strided(static_cast<InT const*>(pr.b), pr.n, pr.k, pr.ldb)).map;
   p.map_c = make_tma_store<typename Cfg::CBox>(row_major_strided(static_cast<OutT*>(pr.c), pr.m, pr.n, pr.ldc)).map;
+  if (pr.n_peers < 0 || pr.n_peers > kMaxPeers) throw std::invalid_argument("kl::gemm: at most 7 peer copies of C");
+  if (pr.n_peers > 0 && Cfg::kDirectStore)
+    throw std::invalid_argument("kl::gemm: peer stores need the TMA-store epilogue");
+  for (int q = 0; q < pr.n_peers; ++q)
+    p.map_peer[q] =
+        make_tma_store<typename Cfg::CBox>(row_major_strided(static_cast<OutT*>(pr.peer_c[q]), pr.m, pr.n, pr.ldc)).map;
+  p.n_peers = pr.n_peers;
 
   TnArgs& a = p.args;
   a.m = int(pr.m);

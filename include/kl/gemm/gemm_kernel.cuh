@@ -106,10 +106,18 @@ struct TnArgs {
   unsigned long long* clock_probe;  // optional: per CTA {clock64, globaltimer} at start and end
 };
 
+// Most peers an epilogue can push C tiles to (one NVLink/NVSwitch domain of 8 GPUs).
+inline constexpr int kMaxPeers = 7;
+
 struct TnParams {
   CUtensorMap map_a;  // A [M, K], box {kBlockK, 128}
   CUtensorMap map_b;  // B [N, K], box {kBlockK, kCtaN}
   CUtensorMap map_c;  // C [M, N], box {kChunkCols, 32}
+  // The same C block in other GPUs' memory (peer-mapped pointers): every finished tile is also
+  // TMA-stored there, so a column-sharded GEMM leaves the whole C on every GPU with no separate
+  // all-gather. Stores only; nothing in this kernel reads peer memory.
+  CUtensorMap map_peer[kMaxPeers];
+  int n_peers;
   TnArgs args;
 };
 
@@ -427,7 +435,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (store) tma_store_2d(&p.map_c, buf, col, row0);
+          if (store) {
+            tma_store_2d(&p.map_c, buf, col, row0);
+            for (int q = 0; q < p.n_peers; ++q) tma_store_2d(&p.map_peer[q], buf, col, row0);
+          }
           tma_store_commit();  // one group per chunk, empty or not, so wait_read<1> tracks buffers
         }
         ++nbuf;

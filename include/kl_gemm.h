@@ -130,6 +130,22 @@ KL_API kl_status kl_gemm_host(const kl_gemm_desc* desc, void* dev_a, void* dev_b
  * on the array, so serialise them. desc->algo must be KL_ALGO_AUTO or KL_ALGO_SKINNY. */
 KL_API kl_status kl_gemm_skinny_noalloc(const kl_gemm_desc* desc, void* stream);
 
+/* No reference counterpart. The tile-kernel GEMM (KL_ALGO_1CTA / 2CTA) whose epilogue also writes
+ * every finished tile of C into `n_peers` (<= 7) other copies of C: device pointers of the same
+ * shape and pitch in other GPUs' memory, mapped into this process (kl_ipc_open_handle). With
+ * desc->b one rank's column shard of B and desc->c that shard's columns of the full C on every
+ * GPU, the GEMM leaves the whole C on every GPU without a separate all-gather: the NVLink
+ * transfers overlap the next tiles' math. The kernel only stores to peer memory. Before reading C,
+ * every rank's kernel must have finished (e.g. a stream-ordered collective after this call). */
+KL_API kl_status kl_gemm_gather(const kl_gemm_desc* desc, void* const* peer_c, int32_t n_peers, void* stream);
+
+/* CUDA IPC for peer copies of C: a 64-byte handle of the device allocation that contains dev_ptr
+ * plus dev_ptr's byte offset inside it; kl_ipc_open_handle maps the allocation in another process
+ * (peer access enabled lazily) and returns its base: add the offset. */
+KL_API kl_status kl_ipc_get_handle(const void* dev_ptr, void* handle, int64_t* offset);
+KL_API kl_status kl_ipc_open_handle(const void* handle, void** dev_ptr);
+KL_API kl_status kl_ipc_close(void* dev_ptr);
+
 /* No reference counterpart; a diagnostic. Runs one tile-kernel GEMM (KL_ALGO_1CTA / 2CTA) with
  * every CTA recording {clock64, %globaltimer} at its start and end, waits for it, and copies the
  * 4 words per CTA to `out` (host, out_words >= 4 * CTAs); *ctas receives the CTA count. The ratio

@@ -32,7 +32,8 @@ EXPORTED = (
     "kl_version", "kl_last_error", "kl_gemm", "kl_gemm_workspace_size", "kl_gemm_ws",
     "kl_set_wait_timeout_ns", "kl_read_status", "kl_probe_wait_timeout", "kl_smem_tile_offset",
     "kl_tma_box_geometry", "kl_tma_box_position", "kl_umma_smem_desc", "kl_mma_instr_desc",
-    "kl_make_tma_desc", "kl_gemm_skinny_noalloc", "kl_gemm_host", "kl_gemm_clock_probe",
+    "kl_make_tma_desc", "kl_gemm_skinny_noalloc", "kl_gemm_host", "kl_gemm_clock_probe", "kl_gemm_gather",
+    "kl_ipc_get_handle", "kl_ipc_open_handle", "kl_ipc_close",
 )
 
 
@@ -94,6 +95,10 @@ def lib() -> ctypes.CDLL:
             "kl_gemm_skinny_noalloc": (i32, [P(GemmDesc), vp]),
             "kl_gemm_host": (i32, [P(GemmDesc), vp, vp, vp, i32, vp]),
             "kl_gemm_clock_probe": (i32, [P(GemmDesc), P(u64), i32, P(i32), vp]),
+            "kl_gemm_gather": (i32, [P(GemmDesc), P(vp), i32, vp]),
+            "kl_ipc_get_handle": (i32, [vp, vp, P(i64)]),
+            "kl_ipc_open_handle": (i32, [vp, P(vp)]),
+            "kl_ipc_close": (i32, [vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -216,6 +221,39 @@ def gemm_host(a_host, b_host, c_host, a_dev, b_dev, c_dev, *, alpha=1.0, scale_a
     check(lib().kl_gemm_host(ctypes.byref(d), ctypes.c_void_p(a_dev.data_ptr()), ctypes.c_void_p(b_dev.data_ptr()),
                              ctypes.c_void_p(c_dev.data_ptr()), int(chunks), ctypes.c_void_p(s)))
     return c_host
+
+
+def gemm_gather(a, b, c_shard, peer_ptrs, *, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
+                group_m=0, stream=None):
+    """c_shard = alpha * a @ b.T, and the same tiles written to each peer pointer (a view of the same
+    columns in another GPU's copy of C, with c_shard's pitch), through kl_gemm_gather."""
+    import torch
+
+    d = gemm_desc(a, b, c_shard, alpha, scale_a, scale_b, algo, group_m)
+    arr = (ctypes.c_void_p * max(1, len(peer_ptrs)))(*[ctypes.c_void_p(p) for p in peer_ptrs])
+    s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
+    check(lib().kl_gemm_gather(ctypes.byref(d), arr, len(peer_ptrs), ctypes.c_void_p(s)))
+    return c_shard
+
+
+def ipc_handle(ptr: int) -> tuple[bytes, int]:
+    """(64-byte IPC handle of the allocation containing ptr, ptr's byte offset in it)."""
+    buf = ctypes.create_string_buffer(64)
+    off = ctypes.c_int64()
+    check(lib().kl_ipc_get_handle(ctypes.c_void_p(ptr), buf, ctypes.byref(off)))
+    return buf.raw, off.value
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map another process's allocation; returns its base address in this process."""
+    out = ctypes.c_void_p()
+    raw = ctypes.create_string_buffer(handle, 64)
+    check(lib().kl_ipc_open_handle(raw, ctypes.byref(out)))
+    return out.value
+
+
+def ipc_close(ptr: int) -> None:
+    check(lib().kl_ipc_close(ctypes.c_void_p(ptr)))
 
 
 def clock_probe(a, b, c, **kw) -> dict:

@@ -185,6 +185,80 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
 
 kl_status kl_gemm(const kl_gemm_desc* d, void* stream) { return kl_gemm_ws(d, nullptr, 0, stream); }
 
+kl_status kl_gemm_gather(const kl_gemm_desc* d, void* const* peer_c, int32_t n_peers, void* stream_ptr) {
+  if (d == nullptr || (n_peers > 0 && peer_c == nullptr)) return fail(KL_ERR_INVALID_ARGUMENT, "null argument");
+  if (n_peers < 0 || n_peers > kMaxPeers) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: 0 to 7 peers");
+  g_last_error.clear();
+  if (d->m <= 0 || d->n <= 0 || d->k <= 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: empty problem");
+  if (d->a == nullptr || d->b == nullptr || d->c == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: null A, B or C");
+  for (int q = 0; q < n_peers; ++q)
+    if (peer_c[q] == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: null peer C");
+  int algo = d->algo;
+  if (algo == KL_ALGO_AUTO || algo == KL_ALGO_SKINNY) algo = d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA;
+  if (algo != KL_ALGO_1CTA && algo != KL_ALGO_2CTA) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: unknown algo");
+  Problem pr;
+  pr.m = d->m; pr.n = d->n; pr.k = d->k;
+  pr.a = d->a; pr.lda = d->lda; pr.b = d->b; pr.ldb = d->ldb; pr.c = d->c; pr.ldc = d->ldc;
+  pr.alpha = d->alpha; pr.scale_a = d->scale_a; pr.scale_b = d->scale_b;
+  pr.group_m = d->group_m; pr.max_ctas = d->max_ctas; pr.prefetch = d->prefetch;
+  pr.peer_c = peer_c;
+  pr.n_peers = n_peers;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  try {
+    const bool pair = algo == KL_ALGO_2CTA;
+    if (d->ab_type == KL_BF16 && d->c_type == KL_BF16)
+      return pair ? run<Bf16Bf16_2>(pr, stream) : run<Bf16Bf16_1>(pr, stream);
+    if (d->ab_type == KL_BF16 && d->c_type == KL_F32)
+      return pair ? run<Bf16F32_2>(pr, stream) : run<Bf16F32_1>(pr, stream);
+    if (d->ab_type == KL_E4M3 && d->c_type == KL_BF16)
+      return pair ? run<E4m3Bf16_2>(pr, stream) : run<E4m3Bf16_1>(pr, stream);
+    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_gather: unsupported types");
+  } catch (std::invalid_argument const& ex) {
+    return fail(KL_ERR_INVALID_ARGUMENT, ex.what());
+  }
+}
+
+kl_status kl_ipc_get_handle(const void* dev_ptr, void* handle, int64_t* offset) {
+  if (dev_ptr == nullptr || handle == nullptr || offset == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null argument");
+  // The handle names the whole allocation that contains dev_ptr (a caching allocator hands out
+  // pieces of larger allocations), so the importer also needs dev_ptr's offset inside it.
+  using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static AddressRangeFn range = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return AddressRangeFn{nullptr};
+    return reinterpret_cast<AddressRangeFn>(p);
+  }();
+  if (range == nullptr) return fail(KL_ERR_NOT_SUPPORTED, "cuMemGetAddressRange is unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+    return fail(KL_ERR_INVALID_ARGUMENT, "kl_ipc_get_handle: not a device allocation");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handles are 64 bytes");
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = int64_t(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
+  return KL_OK;
+}
+
+kl_status kl_ipc_open_handle(const void* handle, void** dev_ptr) {
+  if (dev_ptr == nullptr || handle == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  return KL_OK;
+}
+
+kl_status kl_ipc_close(void* dev_ptr) {
+  cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  return e == cudaSuccess ? KL_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
 kl_status kl_gemm_clock_probe(const kl_gemm_desc* d, uint64_t* out, int32_t out_words, int32_t* ctas, void* stream_ptr) {
   if (d == nullptr || out == nullptr || ctas == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null argument");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);

@@ -20,6 +20,11 @@ def test_shard_ranges_cover_n():
             assert max(h - l for l, h in spans) - min(h - l for l, h in spans) <= 1
     with pytest.raises(ValueError):
         sharding.shard_range(10, 2, 2)
+    for n, world in ((8192, 8), (1000, 2), (28672, 3), (300, 4)):
+        spans = [sharding.shard_range(n, world, r, align=256) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == n
+        assert all(a[1] == b[0] and a[0] <= a[1] for a, b in zip(spans, spans[1:]))
+        assert all(lo % 256 == 0 for lo, _ in spans)
 
 
 def _free_port():

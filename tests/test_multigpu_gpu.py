@@ -1,0 +1,73 @@
+"""N-sharded GEMM on 2+ GPUs of one node (skipped with fewer): every rank computes its column
+shard with kl_gemm_gather, whose epilogue also stores the tiles into the other ranks' copies of C
+over NVLink; after one collective every rank holds the whole C, equal bit for bit to a single-GPU
+kl_gemm of the full problem."""
+
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parent.parent
+
+WORKER = r'''
+import os, sys, datetime
+import numpy as np
+import torch
+import torch.distributed as dist
+sys.path.insert(0, os.environ["KL_ROOT"]); sys.path.insert(0, os.path.join(os.environ["KL_ROOT"], "tests"))
+import maia_b200 as kl
+from maia_b200 import sharding
+from gpu_util import random_inputs, to_device
+
+rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+dev = torch.device("cuda", rank)
+dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+try:
+    for (m, n, k) in [(512, 1024, 768), (384, 1000, 520), (1024, 4096, 1024)]:
+        a_bits, b_bits, _, _ = random_inputs(m, n, k, "bf16", seed=n + k)
+        a, b = to_device(a_bits, "bf16", dev), to_device(b_bits, "bf16", dev)
+        ref = kl.gemm(a, b)                                   # whole problem on this GPU
+        lo, hi = sharding.shard_range(n, world, rank, align=256)
+        shared = sharding.SharedC(m, n, torch.bfloat16, dev, dist)
+        shared.full.fill_(float("nan"))
+        dist.barrier()
+        kl.gemm_gather(a, b[lo:hi], shared.full[:, lo:hi], shared.peer_ptrs(lo))
+        dist.barrier()                                        # every rank's kernel has finished
+        torch.cuda.synchronize()
+        assert kl.read_status() == 0
+        assert torch.equal(shared.full.view(torch.int16), ref.view(torch.int16)), f"rank {rank} shape {(m, n, k)}"
+        dist.barrier()
+        shared.close()
+finally:
+    dist.destroy_process_group()
+print("OK", rank)
+'''
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_sharded_gemm_with_fused_gather(cuda, tmp_path):
+    import torch
+
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs 2+ GPUs")
+    script = tmp_path / "worker.py"
+    script.write_text(WORKER)
+    env = dict(os.environ, KL_ROOT=str(ROOT), NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(script)]
+    r = subprocess.run(["timeout", "-k", "30", "300", *cmd], env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.stdout.count("OK") == world
