@@ -189,7 +189,9 @@ kl_status kl_gemm_gather(const kl_gemm_desc* d, void* const* peer_c, int32_t n_p
   if (d == nullptr || (n_peers > 0 && peer_c == nullptr)) return fail(KL_ERR_INVALID_ARGUMENT, "null argument");
   if (n_peers < 0 || n_peers > kMaxPeers) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: 0 to 7 peers");
   g_last_error.clear();
-  if (d->m <= 0 || d->n <= 0 || d->k <= 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: empty problem");
+  if (d->m < 0 || d->n < 0 || d->k < 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: negative extent");
+  if (d->m == 0 || d->n == 0) return KL_OK;  // an empty shard: nothing to compute or send
+  if (d->k == 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: k must be positive");
   if (d->a == nullptr || d->b == nullptr || d->c == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: null A, B or C");
   for (int q = 0; q < n_peers; ++q)
     if (peer_c[q] == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: null peer C");
