@@ -8,6 +8,7 @@
 #include <algorithm>
 #include <cstdint>
 #include <stdexcept>
+#include <type_traits>
 
 #include <kl/gemm/gemm_kernel.cuh>
 #include <kl/kl.hpp>
@@ -33,6 +34,9 @@ struct Problem {
   // process): the epilogue TMA-stores every tile there too. Not with the direct-store epilogue.
   void* const* peer_c = nullptr;
   int n_peers = 0;
+  // Batched GEMM: `batch` independent problems, A/B/C matrix b at a/b/c + b * stride_*.
+  int64_t batch = 1;
+  int64_t stride_a = 0, stride_b = 0, stride_c = 0;  // elements
 };
 
 // Library defaults for the knobs a Problem leaves at 0.
@@ -115,16 +119,37 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   e = detail::prepare_kernel<Cfg>(device, &max_workers);
   if (e != cudaSuccess) return e;
 
+  if (pr.batch < 1 || pr.batch > 65535) throw std::invalid_argument("kl::gemm: batch must be in [1, 65535]");
   TnParams p{};
-  p.map_a = make_tma_load<typename Cfg::ATile>(row_major_strided(static_cast<InT const*>(pr.a), pr.m, pr.k, pr.lda)).map;
-  p.map_b = make_tma_load<typename Cfg::BTile>(row_major_strided(static_cast<InT const*>(pr.b), pr.n, pr.k, pr.ldb)).map;
-  p.map_c = make_tma_store<typename Cfg::CBox>(row_major_strided(static_cast<OutT*>(pr.c), pr.m, pr.n, pr.ldc)).map;
+  // A batched problem is a rank-3 tensor (batch, rows, cols) per operand; one problem is rank 2.
+  auto matrix = [&](auto* ptr, int64_t rows, int64_t cols, int64_t ld, int64_t bstride) {
+    GmemTensor<std::remove_pointer_t<decltype(ptr)>, 3> g;
+    g.ptr = ptr;
+    g.shape[0] = pr.batch;
+    g.shape[1] = rows;
+    g.shape[2] = cols;
+    g.stride[0] = bstride;
+    g.stride[1] = ld;
+    g.stride[2] = 1;
+    return g;
+  };
+  if (pr.batch > 1) {
+    p.map_a = make_tma_load<typename Cfg::ATile>(matrix(static_cast<InT const*>(pr.a), pr.m, pr.k, pr.lda, pr.stride_a)).map;
+    p.map_b = make_tma_load<typename Cfg::BTile>(matrix(static_cast<InT const*>(pr.b), pr.n, pr.k, pr.ldb, pr.stride_b)).map;
+    p.map_c = make_tma_store<typename Cfg::CBox>(matrix(static_cast<OutT*>(pr.c), pr.m, pr.n, pr.ldc, pr.stride_c)).map;
+  } else {
+    p.map_a = make_tma_load<typename Cfg::ATile>(row_major_strided(static_cast<InT const*>(pr.a), pr.m, pr.k, pr.lda)).map;
+    p.map_b = make_tma_load<typename Cfg::BTile>(row_major_strided(static_cast<InT const*>(pr.b), pr.n, pr.k, pr.ldb)).map;
+    p.map_c = make_tma_store<typename Cfg::CBox>(row_major_strided(static_cast<OutT*>(pr.c), pr.m, pr.n, pr.ldc)).map;
+  }
   if (pr.n_peers < 0 || pr.n_peers > kMaxPeers) throw std::invalid_argument("kl::gemm: at most 7 peer copies of C");
   if (pr.n_peers > 0 && Cfg::kDirectStore)
     throw std::invalid_argument("kl::gemm: peer stores need the TMA-store epilogue");
-  for (int q = 0; q < pr.n_peers; ++q)
-    p.map_peer[q] =
-        make_tma_store<typename Cfg::CBox>(row_major_strided(static_cast<OutT*>(pr.peer_c[q]), pr.m, pr.n, pr.ldc)).map;
+  for (int q = 0; q < pr.n_peers; ++q) {
+    auto* pc = static_cast<OutT*>(pr.peer_c[q]);
+    p.map_peer[q] = pr.batch > 1 ? make_tma_store<typename Cfg::CBox>(matrix(pc, pr.m, pr.n, pr.ldc, pr.stride_c)).map
+                                 : make_tma_store<typename Cfg::CBox>(row_major_strided(pc, pr.m, pr.n, pr.ldc)).map;
+  }
   p.n_peers = pr.n_peers;
 
   TnArgs& a = p.args;
@@ -145,8 +170,12 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   a.c = pr.c;
   a.ldc = pr.ldc;
   a.clock_probe = pr.clock_probe;
+  a.batch = int(pr.batch);
+  a.batch_stride_c = pr.stride_c;
 
-  const int tiles = a.tiles_m * a.tiles_n;
+  const long long all_tiles = (long long)a.tiles_m * a.tiles_n * a.batch;
+  if (all_tiles > INT32_MAX) throw std::invalid_argument("kl::gemm: too many tiles");
+  const int tiles = int(all_tiles);
   int workers = std::min(tiles, max_workers);
   if (pr.max_ctas > 0) workers = std::min(workers, std::max(1, pr.max_ctas / Cfg::kCtaGroup));
 

@@ -104,6 +104,8 @@ struct TnArgs {
   void* c;                      // C and its row pitch in elements, for the direct-store epilogue
   long long ldc;
   unsigned long long* clock_probe;  // optional: per CTA {clock64, globaltimer} at start and end
+  int batch;                    // independent GEMMs (rank-3 tensor maps when > 1)
+  long long batch_stride_c;     // elements between the C matrices (direct-store epilogue)
 };
 
 // Most peers an epilogue can push C tiles to (one NVLink/NVSwitch domain of 8 GPUs).
@@ -130,6 +132,13 @@ KL_HOST_DEVICE void tile_coords(int t, int tiles_m, int tiles_n, int group_m, in
   const int r = t - g * per_group;
   tm = first_m + r % rows;
   tn = r / rows;
+}
+
+// Batched tiles: all tiles of matrix 0, then matrix 1, ...; each matrix in grouped raster order.
+KL_HOST_DEVICE void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int& bz, int& tm, int& tn) {
+  const int per_matrix = tiles_m * tiles_n;
+  bz = t / per_matrix;
+  tile_coords(t - bz * per_matrix, tiles_m, tiles_n, group_m, tm, tn);
 }
 
 #if defined(__CUDACC__)
@@ -187,7 +196,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
   const uint32_t cta_rank = (CG == 2) ? cluster_ctarank() : 0u;  // rank inside the pair
   const int worker = blockIdx.x / CG;
   const int num_workers = gridDim.x / CG;
-  const int num_tiles = args.tiles_m * args.tiles_n;
+  const int num_tiles = args.tiles_m * args.tiles_n * args.batch;
+  const bool batched = args.batch > 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -232,8 +242,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
           t += num_workers;
         }
         if (t >= num_tiles) return;
-        int ptm, ptn;
-        tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, ptm, ptn);
+        int pbz, ptm, ptn;
+        tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, pbz, ptm, ptn);
+        if (batched) return;  // the 2-D prefetch form does not address batched maps
         tma_prefetch_l2_2d(&p.map_a, kb * Cfg::kBlockK, ptm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM);
         tma_prefetch_l2_2d(&p.map_b, kb * Cfg::kBlockK, ptn * Cfg::kTileN + int(cta_rank) * Cfg::kCtaN);
       };
@@ -242,8 +253,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
       uint32_t stage = 0, phase = 0;
       bool ok = true;
       for (int t = worker; ok && t < num_tiles; t += num_workers) {
-        int tm, tn;
-        tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
+        int bz, tm, tn;
+        tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, bz, tm, tn);
         const int a_row = tm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM;
         const int b_row = tn * Cfg::kTileN + int(cta_rank) * Cfg::kCtaN;
         for (int kb = 0; kb < args.k_blocks; ++kb) {
@@ -256,14 +267,24 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
           const int kx = kb * Cfg::kBlockK;
           if constexpr (CG == 1) {
             mbarrier_arrive_expect_tx(full_bar(stage), Cfg::kABytes + Cfg::kBBytes);
-            tma_load_2d(a_smem + stage * Cfg::kABytes, &p.map_a, full_bar(stage), kx, a_row);
-            tma_load_2d(b_smem + stage * Cfg::kBBytes, &p.map_b, full_bar(stage), kx, b_row);
+            if (batched) {
+              tma_load_3d(a_smem + stage * Cfg::kABytes, &p.map_a, full_bar(stage), kx, a_row, bz);
+              tma_load_3d(b_smem + stage * Cfg::kBBytes, &p.map_b, full_bar(stage), kx, b_row, bz);
+            } else {
+              tma_load_2d(a_smem + stage * Cfg::kABytes, &p.map_a, full_bar(stage), kx, a_row);
+              tma_load_2d(b_smem + stage * Cfg::kBBytes, &p.map_b, full_bar(stage), kx, b_row);
+            }
           } else {
             // The leader's barrier counts the bytes of both CTAs; only the leader arrives.
             if (cta_rank == 0) mbarrier_arrive_expect_tx(full_bar(stage), 2u * (Cfg::kABytes + Cfg::kBBytes));
             const uint32_t fb = leader_full0 + 8u * stage;
-            tma_load_2d_pair(a_smem + stage * Cfg::kABytes, &p.map_a, fb, kx, a_row);
-            tma_load_2d_pair(b_smem + stage * Cfg::kBBytes, &p.map_b, fb, kx, b_row);
+            if (batched) {
+              tma_load_3d_pair(a_smem + stage * Cfg::kABytes, &p.map_a, fb, kx, a_row, bz);
+              tma_load_3d_pair(b_smem + stage * Cfg::kBBytes, &p.map_b, fb, kx, b_row, bz);
+            } else {
+              tma_load_2d_pair(a_smem + stage * Cfg::kABytes, &p.map_a, fb, kx, a_row);
+              tma_load_2d_pair(b_smem + stage * Cfg::kBBytes, &p.map_b, fb, kx, b_row);
+            }
           }
           if (++stage == S) {
             stage = 0;
@@ -340,8 +361,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
     const uint32_t tempty_leader0 = (CG == 2) ? mapa_shared(tempty_bar(0), 0) : tempty_bar(0);
     uint32_t iter = 0, nbuf = 0;
     for (int t = worker; t < num_tiles; t += num_workers, ++iter) {
-      int tm, tn;
-      tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
+      int bz, tm, tn;
+      tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, bz, tm, tn);
       const uint32_t acc = iter & 1u;
       const uint32_t acc_phase = (iter >> 1) & 1u;
       if (!mbarrier_wait(tfull_bar(acc), acc_phase, args.timeout_ns)) {
@@ -379,7 +400,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
           // element by element on the ragged right edge.
           const int row = row0 + lane;
           if (row < args.m && col < args.n) {
-            OutT* dst = static_cast<OutT*>(args.c) + (long long)row * args.ldc + col;
+            OutT* dst = static_cast<OutT*>(args.c) + (long long)bz * args.batch_stride_c + (long long)row * args.ldc + col;
             if (col + Cfg::kChunkCols <= args.n) {
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
@@ -436,8 +457,13 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         __syncwarp();
         if (lane == 0) {
           if (store) {
-            tma_store_2d(&p.map_c, buf, col, row0);
-            for (int q = 0; q < p.n_peers; ++q) tma_store_2d(&p.map_peer[q], buf, col, row0);
+            if (batched) {
+              tma_store_3d(&p.map_c, buf, col, row0, bz);
+              for (int q = 0; q < p.n_peers; ++q) tma_store_3d(&p.map_peer[q], buf, col, row0, bz);
+            } else {
+              tma_store_2d(&p.map_c, buf, col, row0);
+              for (int q = 0; q < p.n_peers; ++q) tma_store_2d(&p.map_peer[q], buf, col, row0);
+            }
           }
           tma_store_commit();  // one group per chunk, empty or not, so wait_read<1> tracks buffers
         }

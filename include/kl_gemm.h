@@ -78,6 +78,11 @@ typedef struct kl_gemm_desc {
   int32_t variant;        /* algorithm variant, 0 = library default. KL_ALGO_SKINNY: weight rows
                              per tile / 128 (1 or 2) */
   int32_t prefetch;       /* L2 prefetch distance in K-blocks: 0 = library default, < 0 = off */
+  /* Batched GEMM: `batch` independent problems (0 or 1 = one), matrix i of A/B/C at
+   * a/b/c + i * stride_a/b/c elements (strides positive, multiples of 16 bytes). Tile kernels
+   * only (KL_ALGO_AUTO picks one). */
+  int64_t batch;
+  int64_t stride_a, stride_b, stride_c;
 } kl_gemm_desc;
 
 /* Library version: major * 10000 + minor * 100 + patch. */

@@ -58,6 +58,8 @@ class GemmDesc(ctypes.Structure):
         ("algo", ctypes.c_int32), ("group_m", ctypes.c_int32),
         ("max_ctas", ctypes.c_int32), ("variant", ctypes.c_int32),
         ("prefetch", ctypes.c_int32),
+        ("batch", ctypes.c_int64),
+        ("stride_a", ctypes.c_int64), ("stride_b", ctypes.c_int64), ("stride_c", ctypes.c_int64),
     ]
 
 
@@ -177,19 +179,25 @@ def _dtype_code(t) -> int:
 
 def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, group_m=0, max_ctas=0,
               variant=0, prefetch=0) -> GemmDesc:
-    """Descriptor for C = alpha * A . B^T on torch CUDA tensors (A [M,K], B [N,K], C [M,N])."""
+    """Descriptor for C = alpha * A . B^T on torch CUDA tensors: A [M,K], B [N,K], C [M,N], or the
+    batched forms A [L,M,K], B [L,N,K], C [L,M,N] (L independent GEMMs)."""
     for name, t in (("a", a), ("b", b), ("c", c)):
-        if t.dim() != 2 or t.stride(1) != 1:
-            raise ValueError(f"{name} must be a 2-D tensor with a contiguous last dimension")
-    m, k = a.shape
-    n = b.shape[0]
-    if b.shape[1] != k or tuple(c.shape) != (m, n):
+        if t.dim() not in (2, 3) or t.stride(-1) != 1:
+            raise ValueError(f"{name} must be a 2-D or 3-D tensor with a contiguous last dimension")
+    if not a.dim() == b.dim() == c.dim():
+        raise ValueError("a, b and c must all be 2-D or all 3-D")
+    m, k = a.shape[-2:]
+    n = b.shape[-2]
+    batch = a.shape[0] if a.dim() == 3 else 0
+    if b.shape[-1] != k or tuple(c.shape[-2:]) != (m, n) or (a.dim() == 3 and not (b.shape[0] == c.shape[0] == batch)):
         raise ValueError(f"shape mismatch: a {tuple(a.shape)}, b {tuple(b.shape)}, c {tuple(c.shape)}")
-    return GemmDesc(m=m, n=n, k=k, a=a.data_ptr(), lda=a.stride(0), b=b.data_ptr(), ldb=b.stride(0),
-                    c=c.data_ptr(), ldc=c.stride(0), ab_type=_dtype_code(a.dtype), c_type=_dtype_code(c.dtype),
+    bs = (a.stride(0), b.stride(0), c.stride(0)) if a.dim() == 3 else (0, 0, 0)
+    return GemmDesc(m=m, n=n, k=k, a=a.data_ptr(), lda=a.stride(-2), b=b.data_ptr(), ldb=b.stride(-2),
+                    c=c.data_ptr(), ldc=c.stride(-2), ab_type=_dtype_code(a.dtype), c_type=_dtype_code(c.dtype),
                     alpha=float(alpha), scale_a=None if scale_a is None else scale_a.data_ptr(),
                     scale_b=None if scale_b is None else scale_b.data_ptr(), algo=algo, group_m=group_m,
-                    max_ctas=max_ctas, variant=variant, prefetch=prefetch)
+                    max_ctas=max_ctas, variant=variant, prefetch=prefetch, batch=batch, stride_a=bs[0],
+                    stride_b=bs[1], stride_c=bs[2])
 
 
 def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
@@ -198,7 +206,8 @@ def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=Non
     import torch
 
     if out is None:
-        out = torch.empty((a.shape[0], b.shape[0]), dtype=out_dtype or torch.bfloat16, device=a.device)
+        shape = (a.shape[0], a.shape[1], b.shape[1]) if a.dim() == 3 else (a.shape[0], b.shape[0])
+        out = torch.empty(shape, dtype=out_dtype or torch.bfloat16, device=a.device)
     d = gemm_desc(a, b, out, alpha, scale_a, scale_b, algo, group_m, max_ctas, variant, prefetch)
     s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
     if workspace is None:

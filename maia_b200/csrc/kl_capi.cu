@@ -138,11 +138,16 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
   if (d->m == 0 || d->n == 0) return KL_OK;
   if (d->c == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: null C");
   const int c_bytes = elem_bytes_of(d->c_type);
+  const int64_t batch = d->batch > 1 ? d->batch : 1;
   if (d->k == 0) {
     // An empty sum: C = 0.
     if (d->ldc < d->n) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: ldc < n");
-    cudaError_t e = cudaMemset2DAsync(d->c, size_t(d->ldc) * c_bytes, 0, size_t(d->n) * c_bytes, size_t(d->m), stream);
-    return e == cudaSuccess ? KL_OK : cuda_fail(e, "cudaMemset2DAsync");
+    for (int64_t i = 0; i < batch; ++i) {
+      cudaError_t e = cudaMemset2DAsync(static_cast<char*>(d->c) + size_t(i) * d->stride_c * c_bytes,
+                                        size_t(d->ldc) * c_bytes, 0, size_t(d->n) * c_bytes, size_t(d->m), stream);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemset2DAsync");
+    }
+    return KL_OK;
   }
   if (d->a == nullptr || d->b == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: null A or B");
 
@@ -162,9 +167,14 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
   pr.group_m = d->group_m;
   pr.max_ctas = d->max_ctas;
   pr.prefetch = d->prefetch;
+  pr.batch = batch;
+  pr.stride_a = d->stride_a;
+  pr.stride_b = d->stride_b;
+  pr.stride_c = d->stride_c;
 
   int algo = d->algo;
-  if (algo == KL_ALGO_AUTO) algo = kl::capi::choose_algo(*d);
+  if (algo == KL_ALGO_AUTO) algo = batch > 1 ? (d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA) : kl::capi::choose_algo(*d);
+  if (algo == KL_ALGO_SKINNY && batch > 1) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: KL_ALGO_SKINNY is not batched");
   try {
     if (algo == KL_ALGO_SKINNY) return kl::capi::run_skinny(*d, workspace, workspace_bytes, stream);
     if (algo != KL_ALGO_1CTA && algo != KL_ALGO_2CTA) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: unknown algo");
@@ -205,6 +215,10 @@ kl_status kl_gemm_gather(const kl_gemm_desc* d, void* const* peer_c, int32_t n_p
   pr.group_m = d->group_m; pr.max_ctas = d->max_ctas; pr.prefetch = d->prefetch;
   pr.peer_c = peer_c;
   pr.n_peers = n_peers;
+  pr.batch = d->batch > 1 ? d->batch : 1;
+  pr.stride_a = d->stride_a;
+  pr.stride_b = d->stride_b;
+  pr.stride_c = d->stride_c;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   try {
     const bool pair = algo == KL_ALGO_2CTA;

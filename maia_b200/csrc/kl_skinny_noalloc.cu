@@ -129,6 +129,7 @@ extern "C" kl_status kl_gemm_skinny_noalloc(const kl_gemm_desc* d, void* stream_
   if (d->m <= 0 || d->n <= 0 || d->k <= 0)
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_skinny_noalloc: m, n and k must be positive");
   if (d->m > 256) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_skinny_noalloc: at most 256 rows of A");
+  if (d->batch > 1) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_skinny_noalloc: one problem per call");
   if (d->n > INT32_MAX || d->k > INT32_MAX)
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_skinny_noalloc: extents must fit in 32 bits");
   if (d->a == nullptr || d->b == nullptr || d->c == nullptr)
