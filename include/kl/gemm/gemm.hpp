@@ -133,13 +133,16 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
     g.stride[2] = 1;
     return g;
   };
+  // A K-major operand is stored [rows, K]; an MN-major one [K, rows].
+  const int64_t a_rows = Cfg::kAMn ? pr.k : pr.m, a_cols = Cfg::kAMn ? pr.m : pr.k;
+  const int64_t b_rows = Cfg::kBMn ? pr.k : pr.n, b_cols = Cfg::kBMn ? pr.n : pr.k;
   if (pr.batch > 1) {
-    p.map_a = make_tma_load<typename Cfg::ATile>(matrix(static_cast<InT const*>(pr.a), pr.m, pr.k, pr.lda, pr.stride_a)).map;
-    p.map_b = make_tma_load<typename Cfg::BTile>(matrix(static_cast<InT const*>(pr.b), pr.n, pr.k, pr.ldb, pr.stride_b)).map;
+    p.map_a = make_tma_load<typename Cfg::ATile>(matrix(static_cast<InT const*>(pr.a), a_rows, a_cols, pr.lda, pr.stride_a)).map;
+    p.map_b = make_tma_load<typename Cfg::BTile>(matrix(static_cast<InT const*>(pr.b), b_rows, b_cols, pr.ldb, pr.stride_b)).map;
     p.map_c = make_tma_store<typename Cfg::CBox>(matrix(static_cast<OutT*>(pr.c), pr.m, pr.n, pr.ldc, pr.stride_c)).map;
   } else {
-    p.map_a = make_tma_load<typename Cfg::ATile>(row_major_strided(static_cast<InT const*>(pr.a), pr.m, pr.k, pr.lda)).map;
-    p.map_b = make_tma_load<typename Cfg::BTile>(row_major_strided(static_cast<InT const*>(pr.b), pr.n, pr.k, pr.ldb)).map;
+    p.map_a = make_tma_load<typename Cfg::ATile>(row_major_strided(static_cast<InT const*>(pr.a), a_rows, a_cols, pr.lda)).map;
+    p.map_b = make_tma_load<typename Cfg::BTile>(row_major_strided(static_cast<InT const*>(pr.b), b_rows, b_cols, pr.ldb)).map;
     p.map_c = make_tma_store<typename Cfg::CBox>(row_major_strided(static_cast<OutT*>(pr.c), pr.m, pr.n, pr.ldc)).map;
   }
   if (pr.n_peers < 0 || pr.n_peers > kMaxPeers) throw std::invalid_argument("kl::gemm: at most 7 peer copies of C");

@@ -25,6 +25,7 @@
 #include <cuda_bf16.h>
 
 #include <cstdint>
+#include <type_traits>
 
 #include <kl/arch/cluster.hpp>
 #include <kl/arch/mbarrier.hpp>
@@ -42,7 +43,8 @@ enum : int {
   kStatusDrainTimeout = 8,
 };
 
-template <typename InT, typename OutT, int CtaGroup, int BlockN, int Stages, bool DirectStore = false>
+template <typename InT, typename OutT, int CtaGroup, int BlockN, int Stages, bool DirectStore = false,
+          bool AMn = false, bool BMn = false>
 struct TnConfig {
   using in_type = InT;
   using out_type = OutT;
@@ -65,8 +67,13 @@ struct TnConfig {
   static constexpr int kChunkCols = 128 / int(sizeof(OutT));  // epilogue store box width (128 B)
   static constexpr int kChunks = BlockN / kChunkCols;
 
-  using ATile = SmemTile<InT, kCtaM, kBlockK>;
-  using BTile = SmemTile<InT, kCtaN, kBlockK>;
+  // Operand majors. K-major (the default): the operand is stored [rows, K] and its smem tile is
+  // rows x K. MN-major: stored [K, rows] (A^T / B^T in memory), smem tile K x rows, MN contiguous,
+  // read by the MMA through MN-major descriptors (instruction-descriptor major bit 1).
+  static constexpr bool kAMn = AMn;
+  static constexpr bool kBMn = BMn;
+  using ATile = std::conditional_t<AMn, SmemTile<InT, kBlockK, kCtaM>, SmemTile<InT, kCtaM, kBlockK>>;
+  using BTile = std::conditional_t<BMn, SmemTile<InT, kBlockK, kCtaN>, SmemTile<InT, kCtaN, kBlockK>>;
   using CBox = SmemTile<OutT, 32, kChunkCols>;
 
   static constexpr uint32_t kABytes = ATile::bytes;
@@ -81,7 +88,8 @@ struct TnConfig {
   static constexpr uint32_t kSmemBytes = kOffSlot + 16 + 1024;  // + slack to align the base to 1 KB
 
   static constexpr bool kIsF8 = sizeof(InT) == 1;
-  static constexpr uint32_t kIdesc = mma_instr_desc<InT, InT, float, kTileM, BlockN>();
+  static constexpr uint32_t kIdesc = mma_instr_desc<InT, InT, float, kTileM, BlockN, AMn ? UmmaMajor::MN : UmmaMajor::K,
+                                                    BMn ? UmmaMajor::MN : UmmaMajor::K>();
 
   static_assert(kTmemCols <= 512 && kAccCols * kNumAcc <= 512, "accumulators exceed TMEM");
   static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
@@ -164,6 +172,47 @@ KL_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Issue the TMA boxes of one operand tile. K-major tiles are (rows, K) boxes at (x = k, y = row);
+// MN-major tiles are (K, rows) with the MN coordinate innermost: x = row, y = k.
+template <class Tile, bool Mn, int CG>
+KL_DEVICE void load_operand(uint32_t dst, const void* map, uint32_t bar, int k0, int row0, int bz, bool batched) {
+  using Box = TmaBox<Tile>;
+#pragma unroll
+  for (int i = 0; i < Box::count; ++i) {
+    const int x = Mn ? row0 + Box::col(i) : k0 + Box::col(i);
+    const int y = Mn ? k0 + Box::row(i) : row0 + Box::row(i);
+    const uint32_t d = dst + Box::smem_offset(i);
+    if constexpr (CG == 1) {
+      if (batched)
+        tma_load_3d(d, map, bar, x, y, bz);
+      else
+        tma_load_2d(d, map, bar, x, y);
+    } else {
+      if (batched)
+        tma_load_3d_pair(d, map, bar, x, y, bz);
+      else
+        tma_load_2d_pair(d, map, bar, x, y);
+    }
+  }
+}
+
+// Descriptor of K-slice 0 of an operand tile at `addr`, and the 16-byte-unit step to K-slice k.
+template <class Tile, bool Mn>
+KL_HOST_DEVICE constexpr uint64_t operand_desc0(uint32_t addr) {
+  if constexpr (Mn)
+    return umma_desc_mn_at<Tile>(addr, 0, 0, Tile::cols).desc_;
+  else
+    return umma_desc_at<Tile>(addr).desc_;
+}
+template <class Tile, bool Mn>
+KL_HOST_DEVICE constexpr uint32_t operand_kstep_16B(int k) {
+  using T = typename Tile::value_type;
+  if constexpr (Mn)
+    return static_cast<uint32_t>(detail::tile_offset(Tile::rows, Tile::atom_elems, k * mma_k<T>, 0) * bits_of<T> / 128);
+  else
+    return block_offset_16B<Tile>(k);
+}
+
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_constant__ TnParams p) {
 #if defined(KL_ARCH_SM100)
@@ -244,7 +293,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         if (t >= num_tiles) return;
         int pbz, ptm, ptn;
         tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, pbz, ptm, ptn);
-        if (batched) return;  // the 2-D prefetch form does not address batched maps
+        if (batched || Cfg::kAMn || Cfg::kBMn) return;  // 2-D, K-major maps only
         tma_prefetch_l2_2d(&p.map_a, kb * Cfg::kBlockK, ptm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM);
         tma_prefetch_l2_2d(&p.map_b, kb * Cfg::kBlockK, ptn * Cfg::kTileN + int(cta_rank) * Cfg::kCtaN);
       };
@@ -267,24 +316,18 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
           const int kx = kb * Cfg::kBlockK;
           if constexpr (CG == 1) {
             mbarrier_arrive_expect_tx(full_bar(stage), Cfg::kABytes + Cfg::kBBytes);
-            if (batched) {
-              tma_load_3d(a_smem + stage * Cfg::kABytes, &p.map_a, full_bar(stage), kx, a_row, bz);
-              tma_load_3d(b_smem + stage * Cfg::kBBytes, &p.map_b, full_bar(stage), kx, b_row, bz);
-            } else {
-              tma_load_2d(a_smem + stage * Cfg::kABytes, &p.map_a, full_bar(stage), kx, a_row);
-              tma_load_2d(b_smem + stage * Cfg::kBBytes, &p.map_b, full_bar(stage), kx, b_row);
-            }
+            load_operand<typename Cfg::ATile, Cfg::kAMn, 1>(a_smem + stage * Cfg::kABytes, &p.map_a, full_bar(stage),
+                                                            kx, a_row, bz, batched);
+            load_operand<typename Cfg::BTile, Cfg::kBMn, 1>(b_smem + stage * Cfg::kBBytes, &p.map_b, full_bar(stage),
+                                                            kx, b_row, bz, batched);
           } else {
             // The leader's barrier counts the bytes of both CTAs; only the leader arrives.
             if (cta_rank == 0) mbarrier_arrive_expect_tx(full_bar(stage), 2u * (Cfg::kABytes + Cfg::kBBytes));
             const uint32_t fb = leader_full0 + 8u * stage;
-            if (batched) {
-              tma_load_3d_pair(a_smem + stage * Cfg::kABytes, &p.map_a, fb, kx, a_row, bz);
-              tma_load_3d_pair(b_smem + stage * Cfg::kBBytes, &p.map_b, fb, kx, b_row, bz);
-            } else {
-              tma_load_2d_pair(a_smem + stage * Cfg::kABytes, &p.map_a, fb, kx, a_row);
-              tma_load_2d_pair(b_smem + stage * Cfg::kBBytes, &p.map_b, fb, kx, b_row);
-            }
+            load_operand<typename Cfg::ATile, Cfg::kAMn, 2>(a_smem + stage * Cfg::kABytes, &p.map_a, fb, kx, a_row, bz,
+                                                            batched);
+            load_operand<typename Cfg::BTile, Cfg::kBMn, 2>(b_smem + stage * Cfg::kBBytes, &p.map_b, fb, kx, b_row, bz,
+                                                            batched);
           }
           if (++stage == S) {
             stage = 0;
@@ -300,8 +343,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if ((CG == 1 || cta_rank == 0) && elect_one()) {
-      const uint64_t a_desc0 = umma_desc_at<typename Cfg::ATile>(a_smem).desc_;
-      const uint64_t b_desc0 = umma_desc_at<typename Cfg::BTile>(b_smem).desc_;
+      const uint64_t a_desc0 = operand_desc0<typename Cfg::ATile, Cfg::kAMn>(a_smem);
+      const uint64_t b_desc0 = operand_desc0<typename Cfg::BTile, Cfg::kBMn>(b_smem);
       const uint32_t peer = cta_rank ^ 1u;
       uint32_t stage = 0, phase = 0;
       uint32_t iter = 0;
@@ -327,12 +370,13 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
           const uint64_t b_desc = b_desc0 + ((stage * Cfg::kBBytes) >> 4);
 #pragma unroll
           for (int k = 0; k < Cfg::kBlockK / Cfg::kUmmaK; ++k) {
-            const uint64_t koff = block_offset_16B<typename Cfg::ATile>(k);
+            const uint64_t ka = operand_kstep_16B<typename Cfg::ATile, Cfg::kAMn>(k);
+            const uint64_t kb16 = operand_kstep_16B<typename Cfg::BTile, Cfg::kBMn>(k);
             const uint32_t accumulate = (kb | k) != 0;
             if constexpr (Cfg::kIsF8)
-              umma_f8_ss<CG>(d_tmem, a_desc + koff, b_desc + koff, Cfg::kIdesc, accumulate);
+              umma_f8_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16, Cfg::kIdesc, accumulate);
             else
-              umma_f16_ss<CG>(d_tmem, a_desc + koff, b_desc + koff, Cfg::kIdesc, accumulate);
+              umma_f16_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16, Cfg::kIdesc, accumulate);
           }
           // Stage consumed once these MMAs complete: release it in both CTAs of the pair.
           umma_commit<CG>(empty_bar(stage));

@@ -88,11 +88,14 @@ struct TmaBox {
   static_assert(inner * bits_of<T> / 8 <= Tile::swizzle::bytes,
                 "a swizzled TMA box row can't be wider than the swizzle span");
 
-  // Position of box i's first element inside the tile, in elements.
-  KL_HOST_DEVICE static constexpr int row(int i) { return geometry.row(i); }
-  KL_HOST_DEVICE static constexpr int col(int i) { return geometry.col(i); }
+  // Position of box i's first element inside the tile, in elements. (Same formulas as
+  // TmaBoxGeometry, written on the scalar members so device code can call them.)
+  KL_HOST_DEVICE static constexpr int row(int i) { return i % row_boxes * outer; }
+  KL_HOST_DEVICE static constexpr int col(int i) { return i / row_boxes * inner; }
   // Byte offset of box i inside the tile.
-  KL_HOST_DEVICE static constexpr uint32_t smem_offset(int i) { return geometry.smem_offset(i); }
+  KL_HOST_DEVICE static constexpr uint32_t smem_offset(int i) {
+    return static_cast<uint32_t>(detail::tile_offset(Tile::rows, inner, row(i), col(i)) * (bits_of<T> / 8));
+  }
 };
 
 struct TmaLoadTag {};

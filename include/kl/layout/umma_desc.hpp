@@ -111,7 +111,40 @@ KL_HOST_DEVICE constexpr uint64_t umma_desc_rt(uint32_t tile_addr, int elem_byte
   return (d & 0xFFFFFFFF00000000ull) | lo;
 }
 
+// MN-major operands. The tile is stored K rows x MN columns (MN contiguous, SmemTile<T, K, MN, Sw>),
+// atoms stacked down the K rows first, so a strip of one swizzle span of MN is contiguous over
+// all K rows. Canonical MN-major swizzled form, in 16-byte units:
+//   ((Sw/16, n), (8, k)) : ((1, LBO), (Sw/16, SBO))
+// LBO = bytes between MN strips (K rows x Sw bytes; 0 when the operand is a single strip, as CuTe
+// encodes an unused stride), SBO = bytes between 8-row K groups (8 x Sw bytes). The K-slice of one
+// MMA (32 bytes of K = mma_k rows) starts mma_k rows further.
+KL_HOST_DEVICE constexpr uint64_t umma_desc_mn_rt(uint32_t tile_addr, int elem_bytes, int k_rows, int swizzle_span,
+                                                  int k_block, int mn_col, int mn_extent) {
+  const UmmaLayout layout = umma_layout_rt(swizzle_span);
+  const uint32_t lbo = mn_extent > swizzle_span / elem_bytes ? uint32_t(k_rows) * uint32_t(swizzle_span) : 0u;
+  const uint32_t sbo = 8u * uint32_t(swizzle_span);
+  const int atom_elems = swizzle_span / elem_bytes;
+  const int mma_k_rows = 32 / elem_bytes;
+  const uint32_t off = static_cast<uint32_t>(tile_offset(k_rows, atom_elems, k_block * mma_k_rows, mn_col) * elem_bytes);
+  return encode_smem_desc(tile_addr + off, lbo, sbo, layout);
+}
+
 }  // namespace detail
+
+// Descriptor of the k-th MMA K-slice of an MN-major tile (SmemTile<T, K rows, MN cols, Sw>, Sw a
+// 32/64/128-byte swizzle) at shared address `tile_addr`, for the MN columns [mn_col, mn_col +
+// mn_extent) one MMA reads (mn_col a multiple of the atom width; mn_extent 0 = all columns).
+// No counterpart in the reference, whose descriptors are K-major only.
+template <SmemTileType Tile>
+KL_HOST_DEVICE constexpr SmemDesc umma_desc_mn_at(uint32_t tile_addr, int k_block = 0, int mn_col = 0,
+                                                  int mn_extent = 0) {
+  using T = typename Tile::value_type;
+  static_assert(Tile::swizzle::bytes >= 32, "MN-major descriptors here cover the swizzled layouts");
+  SmemDesc d;
+  d.desc_ = detail::umma_desc_mn_rt(tile_addr, bits_of<T> / 8, Tile::rows, Tile::swizzle::bytes, k_block, mn_col,
+                                    mn_extent > 0 ? mn_extent : Tile::cols);
+  return d;
+}
 
 // Offset of the k-th MMA K-slice, starting at `row`, from the start of the tile, in 16-byte units,
 // measured on the un-swizzled layout (the hardware applies the swizzle itself).

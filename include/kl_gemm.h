@@ -83,6 +83,10 @@ typedef struct kl_gemm_desc {
    * only (KL_ALGO_AUTO picks one). */
   int64_t batch;
   int64_t stride_a, stride_b, stride_c;
+  /* Operand storage: 0 = K-major (A [M, K], B [N, K], K contiguous), 1 = MN-major (A stored
+   * [K, M] with M contiguous, B stored [K, N]); lda / ldb are then the pitch of the stored
+   * matrix. MN-major operands: bf16 inputs with bf16 C on the tile kernels. */
+  int32_t a_major, b_major;
 } kl_gemm_desc;
 
 /* Library version: major * 10000 + minor * 100 + patch. */
@@ -198,6 +202,18 @@ KL_API kl_status kl_umma_smem_desc(int32_t elem_bytes, int32_t rows, int32_t col
 /* 32-bit tcgen05.mma instruction descriptor, both operands K-major. M = 64/128 (one CTA) or 256
  * (CTA pair). kernel_lib/include/kl/layout/umma_desc.hpp:49-58 (mma_instr_desc, M <= 128 there). */
 KL_API kl_status kl_mma_instr_desc(int32_t a_type, int32_t b_type, int32_t acc_type, int32_t m, int32_t n, uint32_t* out);
+
+/* MN-major form of kl_umma_smem_desc: a tile stored k_rows x mn_cols (MN contiguous, swizzle
+ * 32/64/128 bytes), K-slice `k_block`, MN columns [mn_col, mn_col + mn_extent) (0 = to the end).
+ * No counterpart in the reference (K-major only); pinned to CuTe's make_umma_desc<Major::MN>. */
+KL_API kl_status kl_umma_smem_desc_mn(int32_t elem_bytes, int32_t k_rows, int32_t mn_cols, int32_t swizzle_span,
+                                      uint32_t tile_addr, int32_t k_block, int32_t mn_col, int32_t mn_extent,
+                                      uint64_t* out);
+
+/* kl_mma_instr_desc with the operand majors: 0 = K-major, 1 = MN-major. No counterpart in the
+ * reference (K-major only). */
+KL_API kl_status kl_mma_instr_desc_major(int32_t a_type, int32_t b_type, int32_t acc_type, int32_t m, int32_t n,
+                                         int32_t a_major, int32_t b_major, uint32_t* out);
 
 /* 128-byte TMA tensor map for a rank-`rank` row-major global tensor (shape/stride outermost
  * first, in elements) moved in tiles of tile_rows x tile_cols with the given swizzle. Needs a CUDA

@@ -33,7 +33,7 @@ EXPORTED = (
     "kl_set_wait_timeout_ns", "kl_read_status", "kl_probe_wait_timeout", "kl_smem_tile_offset",
     "kl_tma_box_geometry", "kl_tma_box_position", "kl_umma_smem_desc", "kl_mma_instr_desc",
     "kl_make_tma_desc", "kl_gemm_skinny_noalloc", "kl_gemm_host", "kl_gemm_clock_probe", "kl_gemm_gather",
-    "kl_ipc_get_handle", "kl_ipc_open_handle", "kl_ipc_close",
+    "kl_ipc_get_handle", "kl_ipc_open_handle", "kl_ipc_close", "kl_umma_smem_desc_mn", "kl_mma_instr_desc_major",
 )
 
 
@@ -60,6 +60,7 @@ class GemmDesc(ctypes.Structure):
         ("prefetch", ctypes.c_int32),
         ("batch", ctypes.c_int64),
         ("stride_a", ctypes.c_int64), ("stride_b", ctypes.c_int64), ("stride_c", ctypes.c_int64),
+        ("a_major", ctypes.c_int32), ("b_major", ctypes.c_int32),
     ]
 
 
@@ -101,6 +102,8 @@ def lib() -> ctypes.CDLL:
             "kl_ipc_get_handle": (i32, [vp, vp, P(i64)]),
             "kl_ipc_open_handle": (i32, [vp, P(vp)]),
             "kl_ipc_close": (i32, [vp]),
+            "kl_umma_smem_desc_mn": (i32, [i32, i32, i32, i32, u32, i32, i32, i32, P(u64)]),
+            "kl_mma_instr_desc_major": (i32, [i32, i32, i32, i32, i32, i32, i32, P(u32)]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -145,6 +148,19 @@ def umma_smem_desc(elem_bytes, rows, cols, span, tile_addr, k_block=0, row=0) ->
     return out.value
 
 
+def umma_smem_desc_mn(elem_bytes, k_rows, mn_cols, span, tile_addr, k_block=0, mn_col=0, mn_extent=0) -> int:
+    out = ctypes.c_uint64()
+    check(lib().kl_umma_smem_desc_mn(elem_bytes, k_rows, mn_cols, span, tile_addr, k_block, mn_col, mn_extent,
+                                     ctypes.byref(out)))
+    return out.value
+
+
+def mma_instr_desc_major(a_type, b_type, acc_type, m, n, a_major, b_major) -> int:
+    out = ctypes.c_uint32()
+    check(lib().kl_mma_instr_desc_major(a_type, b_type, acc_type, m, n, a_major, b_major, ctypes.byref(out)))
+    return out.value
+
+
 def mma_instr_desc(a_type, b_type, acc_type, m, n) -> int:
     out = ctypes.c_uint32()
     check(lib().kl_mma_instr_desc(a_type, b_type, acc_type, m, n, ctypes.byref(out)))
@@ -178,18 +194,19 @@ def _dtype_code(t) -> int:
 
 
 def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, group_m=0, max_ctas=0,
-              variant=0, prefetch=0) -> GemmDesc:
+              variant=0, prefetch=0, a_major=0, b_major=0) -> GemmDesc:
     """Descriptor for C = alpha * A . B^T on torch CUDA tensors: A [M,K], B [N,K], C [M,N], or the
-    batched forms A [L,M,K], B [L,N,K], C [L,M,N] (L independent GEMMs)."""
+    batched forms A [L,M,K], B [L,N,K], C [L,M,N] (L independent GEMMs). a_major / b_major = 1
+    pass the operand MN-major: `a` as the stored [K, M] (A transposed in memory), `b` as [K, N]."""
     for name, t in (("a", a), ("b", b), ("c", c)):
         if t.dim() not in (2, 3) or t.stride(-1) != 1:
             raise ValueError(f"{name} must be a 2-D or 3-D tensor with a contiguous last dimension")
     if not a.dim() == b.dim() == c.dim():
         raise ValueError("a, b and c must all be 2-D or all 3-D")
-    m, k = a.shape[-2:]
-    n = b.shape[-2]
+    m, k = (a.shape[-1], a.shape[-2]) if a_major else (a.shape[-2], a.shape[-1])
+    n, kb = (b.shape[-1], b.shape[-2]) if b_major else (b.shape[-2], b.shape[-1])
     batch = a.shape[0] if a.dim() == 3 else 0
-    if b.shape[-1] != k or tuple(c.shape[-2:]) != (m, n) or (a.dim() == 3 and not (b.shape[0] == c.shape[0] == batch)):
+    if kb != k or tuple(c.shape[-2:]) != (m, n) or (a.dim() == 3 and not (b.shape[0] == c.shape[0] == batch)):
         raise ValueError(f"shape mismatch: a {tuple(a.shape)}, b {tuple(b.shape)}, c {tuple(c.shape)}")
     bs = (a.stride(0), b.stride(0), c.stride(0)) if a.dim() == 3 else (0, 0, 0)
     return GemmDesc(m=m, n=n, k=k, a=a.data_ptr(), lda=a.stride(-2), b=b.data_ptr(), ldb=b.stride(-2),
@@ -197,18 +214,20 @@ def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, gr
                     alpha=float(alpha), scale_a=None if scale_a is None else scale_a.data_ptr(),
                     scale_b=None if scale_b is None else scale_b.data_ptr(), algo=algo, group_m=group_m,
                     max_ctas=max_ctas, variant=variant, prefetch=prefetch, batch=batch, stride_a=bs[0],
-                    stride_b=bs[1], stride_c=bs[2])
+                    stride_b=bs[1], stride_c=bs[2], a_major=a_major, b_major=b_major)
 
 
 def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
-         group_m=0, max_ctas=0, variant=0, prefetch=0, workspace=None, stream=None):
+         group_m=0, max_ctas=0, variant=0, prefetch=0, a_major=0, b_major=0, workspace=None, stream=None):
     """out = alpha * a @ b.T [* scale_a * scale_b] on the current CUDA stream, via kl_gemm."""
     import torch
 
     if out is None:
-        shape = (a.shape[0], a.shape[1], b.shape[1]) if a.dim() == 3 else (a.shape[0], b.shape[0])
+        m = a.shape[-1] if a_major else a.shape[-2]
+        n = b.shape[-1] if b_major else b.shape[-2]
+        shape = (a.shape[0], m, n) if a.dim() == 3 else (m, n)
         out = torch.empty(shape, dtype=out_dtype or torch.bfloat16, device=a.device)
-    d = gemm_desc(a, b, out, alpha, scale_a, scale_b, algo, group_m, max_ctas, variant, prefetch)
+    d = gemm_desc(a, b, out, alpha, scale_a, scale_b, algo, group_m, max_ctas, variant, prefetch, a_major, b_major)
     s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
     if workspace is None:
         check(lib().kl_gemm(ctypes.byref(d), ctypes.c_void_p(s)))

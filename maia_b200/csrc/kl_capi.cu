@@ -82,6 +82,18 @@ kl_status run(Problem const& pr, cudaStream_t stream, LaunchInfo* info = nullptr
   return KL_OK;
 }
 
+// MN-major operands (A and/or B stored transposed), bf16 -> bf16.
+template <bool AMn, bool BMn>
+using Bf16Mn_1 = TnConfig<kl::bf16, kl::bf16, 1, 256, 4, false, AMn, BMn>;
+template <bool AMn, bool BMn>
+using Bf16Mn_2 = TnConfig<kl::bf16, kl::bf16, 2, 256, 6, false, AMn, BMn>;
+
+kl_status run_mn(Problem const& pr, bool pair, bool a_mn, bool b_mn, cudaStream_t stream) {
+  if (a_mn && b_mn) return pair ? run<Bf16Mn_2<true, true>>(pr, stream) : run<Bf16Mn_1<true, true>>(pr, stream);
+  if (a_mn) return pair ? run<Bf16Mn_2<true, false>>(pr, stream) : run<Bf16Mn_1<true, false>>(pr, stream);
+  return pair ? run<Bf16Mn_2<false, true>>(pr, stream) : run<Bf16Mn_1<false, true>>(pr, stream);
+}
+
 // Probe buffer for kl_gemm_clock_probe: one per device, 4 words per CTA, allocated on first use.
 unsigned long long* g_probe[64] = {};
 
@@ -172,13 +184,24 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
   pr.stride_b = d->stride_b;
   pr.stride_c = d->stride_c;
 
+  const bool a_mn = d->a_major == 1, b_mn = d->b_major == 1;
+  if ((d->a_major != 0 && !a_mn) || (d->b_major != 0 && !b_mn))
+    return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: a_major / b_major must be 0 (K) or 1 (MN)");
   int algo = d->algo;
-  if (algo == KL_ALGO_AUTO) algo = batch > 1 ? (d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA) : kl::capi::choose_algo(*d);
+  if (algo == KL_ALGO_AUTO)
+    algo = (batch > 1 || a_mn || b_mn) ? (d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA) : kl::capi::choose_algo(*d);
   if (algo == KL_ALGO_SKINNY && batch > 1) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: KL_ALGO_SKINNY is not batched");
+  if (algo == KL_ALGO_SKINNY && (a_mn || b_mn))
+    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: KL_ALGO_SKINNY takes K-major operands");
   try {
     if (algo == KL_ALGO_SKINNY) return kl::capi::run_skinny(*d, workspace, workspace_bytes, stream);
     if (algo != KL_ALGO_1CTA && algo != KL_ALGO_2CTA) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: unknown algo");
     const bool pair = algo == KL_ALGO_2CTA;
+    if (a_mn || b_mn) {
+      if (d->ab_type != KL_BF16 || d->c_type != KL_BF16)
+        return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: MN-major operands are built for bf16 inputs and bf16 C");
+      return run_mn(pr, pair, a_mn, b_mn, stream);
+    }
     if (d->ab_type == KL_BF16 && d->c_type == KL_BF16)
       return pair ? run<Bf16Bf16_2>(pr, stream) : run<Bf16Bf16_1>(pr, stream);
     if (d->ab_type == KL_BF16 && d->c_type == KL_F32)
@@ -396,6 +419,33 @@ kl_status kl_umma_smem_desc(int32_t elem_bytes, int32_t rows, int32_t cols, int3
   if (k_block < 0 || k_block >= cols / mma_k) return fail(KL_ERR_INVALID_ARGUMENT, "k_block out of range");
   if (row < 0 || row % 8 != 0 || row >= rows) return fail(KL_ERR_INVALID_ARGUMENT, "row must be a multiple of 8 inside the tile");
   *out = kl::detail::umma_desc_rt(tile_addr, elem_bytes, rows, span, k_block, row);
+  return KL_OK;
+}
+
+kl_status kl_umma_smem_desc_mn(int32_t elem_bytes, int32_t k_rows, int32_t mn_cols, int32_t span, uint32_t tile_addr,
+                               int32_t k_block, int32_t mn_col, int32_t mn_extent, uint64_t* out) {
+  kl_status s = check_tile(elem_bytes, k_rows, mn_cols, span);
+  if (s != KL_OK) return s;
+  if (out == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null output");
+  if (span < 32) return fail(KL_ERR_NOT_SUPPORTED, "MN-major descriptors cover the 32/64/128-byte swizzles");
+  const int mma_k_rows = 32 / elem_bytes;
+  if (k_rows % mma_k_rows != 0) return fail(KL_ERR_INVALID_ARGUMENT, "tile K extent must be a multiple of the MMA K");
+  if (k_block < 0 || k_block >= k_rows / mma_k_rows) return fail(KL_ERR_INVALID_ARGUMENT, "k_block out of range");
+  const int atom = span / elem_bytes;
+  if (mn_col < 0 || mn_col % atom != 0 || mn_col >= mn_cols)
+    return fail(KL_ERR_INVALID_ARGUMENT, "mn_col must be a multiple of the atom width inside the tile");
+  if (mn_extent <= 0) mn_extent = mn_cols - mn_col;
+  *out = kl::detail::umma_desc_mn_rt(tile_addr, elem_bytes, k_rows, span, k_block, mn_col, mn_extent);
+  return KL_OK;
+}
+
+kl_status kl_mma_instr_desc_major(int32_t a_type, int32_t b_type, int32_t acc_type, int32_t m, int32_t n,
+                                  int32_t a_major, int32_t b_major, uint32_t* out) {
+  if ((a_major != 0 && a_major != 1) || (b_major != 0 && b_major != 1))
+    return fail(KL_ERR_INVALID_ARGUMENT, "major must be 0 (K) or 1 (MN)");
+  kl_status s = kl_mma_instr_desc(a_type, b_type, acc_type, m, n, out);
+  if (s != KL_OK) return s;
+  *out |= (uint32_t(a_major) << 15) | (uint32_t(b_major) << 16);
   return KL_OK;
 }
 

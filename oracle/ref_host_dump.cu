@@ -93,6 +93,38 @@ void dump_tile() {
   std::fprintf(out, "}");
 }
 
+// MN-major operand tiles (no counterpart in the reference, which is K-major only): CuTe's own
+// canonical MN-major atom tiled K-groups first (Step<_2,_1>), the arrangement a TMA box of
+// one swizzle span of MN by all K rows produces. Records CuTe's physical offsets and
+// make_umma_desc<Major::MN> for every K-slice at shared address 0.
+template <typename T, int MN, int K, typename Atom, int SwBytes>
+void dump_mn_tile(const char* sw_name) {
+  begin_entry();
+  auto L = cute::tile_to_shape(Atom{}, cute::Shape<cute::Int<MN>, cute::Int<K>>{}, cute::Step<cute::_2, cute::_1>{});
+  alignas(1024) static unsigned char storage[1 << 20];
+  T* base = reinterpret_cast<T*>(storage);
+  auto t = cute::make_tensor(cute::make_smem_ptr(base), L);
+  std::fprintf(out, "{\"kind\": \"mn_tile\", \"type\": \"%s\", \"mn\": %d, \"k\": %d, \"swizzle\": %d, \"tensor\": [", tname<T>(),
+               MN, K, SwBytes);
+  bool f = true;
+  for (int k = 0; k < K; ++k)
+    for (int mn = 0; mn < MN; ++mn) {
+      std::fprintf(out, "%s%lld", f ? "" : ",", (long long)(&t(mn, k) - base));
+      f = false;
+    }
+  std::fprintf(out, "], \"umma_desc_mn_base0\": [");
+  constexpr int mk = kl::mma_k<T>;
+  for (int kb = 0; kb < K / mk; ++kb) {
+    auto slice = cute::local_tile(t, cute::Shape<cute::Int<MN>, cute::Int<mk>>{}, cute::make_coord(0, kb));
+    kl::SmemDesc d = cute::UMMA::make_umma_desc<cute::UMMA::Major::MN>(slice);
+    // make_umma_desc reads the slice's address through the host path (0): add the slice offset.
+    d.desc_ += uint64_t((&slice(0, 0) - base) * sizeof(T) >> 4);
+    std::fprintf(out, "%s\"0x%016llx\"", kb ? "," : "", (unsigned long long)d.desc_);
+  }
+  std::fprintf(out, "]}");
+  (void)sw_name;
+}
+
 template <typename A, typename B, typename Acc, int M, int N>
 void dump_idesc_ref() {
   begin_entry();
@@ -141,6 +173,13 @@ int main(int argc, char** argv) {
   dump_tile<SmemTile<float, 32, 32>>();
   dump_tile<SmemTile<float, 64, 32, kl::Swizzle64B>>();
 
+  namespace GM = cute::SM90::GMMA;
+  dump_mn_tile<kl::bf16, 128, 64, GM::Layout_MN_SW128_Atom<kl::bf16>, 128>("sw128");
+  dump_mn_tile<kl::bf16, 256, 64, GM::Layout_MN_SW128_Atom<kl::bf16>, 128>("sw128");
+  dump_mn_tile<kl::bf16, 128, 32, GM::Layout_MN_SW64_Atom<kl::bf16>, 64>("sw64");
+  dump_mn_tile<kl::bf16, 64, 32, GM::Layout_MN_SW32_Atom<kl::bf16>, 32>("sw32");
+  dump_mn_tile<kl::e4m3, 128, 128, GM::Layout_MN_SW128_Atom<kl::e4m3>, 128>("sw128");
+
   dump_idesc_ref<kl::bf16, kl::bf16, float, 128, 256>();
   dump_idesc_ref<kl::bf16, kl::bf16, float, 128, 128>();
   dump_idesc_ref<kl::bf16, kl::bf16, float, 128, 16>();
@@ -156,6 +195,16 @@ int main(int argc, char** argv) {
   dump_idesc_cute<kl::bf16, kl::bf16, float, 256, 128>();
   dump_idesc_cute<kl::e4m3, kl::e4m3, float, 256, 256>();
   dump_idesc_cute<kl::f16, kl::f16, float, 256, 64>();
+  {  // MN-major operand bits (a_major / b_major = 1), CuTe's encoder.
+    auto mn = [](auto d, const char* what) {
+      begin_entry();
+      std::fprintf(out, "{\"kind\": \"idesc_major\", \"what\": \"%s\", \"value\": \"0x%08x\"}", what, (unsigned)d.desc_);
+    };
+    using cute::UMMA::Major;
+    mn(cute::UMMA::make_instr_desc<kl::bf16, kl::bf16, float, 128, 256, Major::MN, Major::K>(), "bf16 M128 N256 A=MN B=K");
+    mn(cute::UMMA::make_instr_desc<kl::bf16, kl::bf16, float, 128, 256, Major::K, Major::MN>(), "bf16 M128 N256 A=K B=MN");
+    mn(cute::UMMA::make_instr_desc<kl::bf16, kl::bf16, float, 256, 256, Major::MN, Major::MN>(), "bf16 M256 N256 A=MN B=MN");
+  }
   std::fprintf(out, "\n]\n");
   std::fclose(out);
   return 0;

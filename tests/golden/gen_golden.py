@@ -9,8 +9,9 @@ CUTLASS/CuTe headers:
    (kernel_lib/include/kl) compiled against CuTe 4.5.0, evaluated on the host: smem layouts
    (physical offsets through tile.tensor(), and the un-swizzled layout_b), TmaBox geometry,
    block_offset_16B, the UMMA smem descriptor body at shared address 0, and instruction
-   descriptors. Large offset arrays are stored as SHA-256 of their little-endian int64 bytes plus a
-   64-entry prefix.
+   descriptors; plus CuTe's own MN-major operand tiles and make_umma_desc<Major::MN> (the reference
+   is K-major only). Large offset arrays are stored as SHA-256 of their little-endian int64 bytes
+   plus a 64-entry prefix.
 2. ref_test_known_answers.json: the known answers written into the reference's unit tests,
    extracted from the test sources as text (file:line recorded with each).
 """
@@ -52,6 +53,11 @@ def host_tables() -> list:
             t["tensor_prefix"] = e["tensor"][:64]
             t["layout_b_sha256"] = sha(e["layout_b"])
             t["layout_b_prefix"] = e["layout_b"][:64]
+            tables.append(t)
+        elif e["kind"] == "mn_tile":
+            t = {k: v for k, v in e.items() if k != "tensor"}
+            t["tensor_sha256"] = sha(e["tensor"])
+            t["tensor_prefix"] = e["tensor"][:64]
             tables.append(t)
         else:
             tables.append(e)

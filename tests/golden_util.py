@@ -35,3 +35,11 @@ def tile_id(t):
 
 def sha(values) -> str:
     return hashlib.sha256(np.asarray(values, dtype="<i8").tobytes()).hexdigest()
+
+
+def mn_tiles():
+    return [t for t in host_tables() if t["kind"] == "mn_tile"]
+
+
+def idesc_majors():
+    return [t for t in host_tables() if t["kind"] == "idesc_major"]

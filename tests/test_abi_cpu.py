@@ -8,7 +8,7 @@ from pathlib import Path
 import pytest
 
 import maia_b200 as kl
-from golden_util import ELEM_BYTES, idescs, known_answers, sha, tile_id, tiles
+from golden_util import ELEM_BYTES, idesc_majors, idescs, known_answers, mn_tiles, sha, tile_id, tiles
 
 HEADER = Path(__file__).resolve().parent.parent / "include" / "kl_gemm.h"
 TYPE = {"bf16": kl.KL_BF16, "f16": kl.KL_F16, "f32": kl.KL_F32, "i8": kl.KL_I8, "e4m3": kl.KL_E4M3}
@@ -110,3 +110,24 @@ def test_tma_desc_validation(ptr, shape, stride, msg):
         kl.make_tma_desc(kl.KL_BF16, 128, 64, 128, ptr, shape, stride)
     assert e.value.status == kl.KL_ERR_INVALID_ARGUMENT
     assert e.value.message == msg
+
+
+@pytest.mark.parametrize("t", mn_tiles(), ids=lambda t: f"{t['type']}_mn{t['mn']}_k{t['k']}_sw{t['swizzle']}")
+def test_mn_major_tile_and_descriptors_match_cute(t):
+    """MN-major operands: SmemTile<T, K, MN, Sw> (MN contiguous, atoms down K first) is the layout of
+    CuTe's MN-major atom tiled K first; the descriptors equal CuTe's make_umma_desc<Major::MN>."""
+    eb, mn, k, sw = ELEM_BYTES[t["type"]], t["mn"], t["k"], t["swizzle"]
+    phys = [kl.smem_tile_offset(eb, k, mn, sw, kk, m)[0] for kk in range(k) for m in range(mn)]
+    assert phys[:64] == t["tensor_prefix"] and sha(phys) == t["tensor_sha256"]
+    for kb, val in enumerate(t["umma_desc_mn_base0"]):
+        assert kl.umma_smem_desc_mn(eb, k, mn, sw, 0, kb) == int(val, 16), kb
+
+
+def test_instr_desc_majors_match_cute():
+    want = {"bf16 M128 N256 A=MN B=K": (128, 256, 1, 0), "bf16 M128 N256 A=K B=MN": (128, 256, 0, 1),
+            "bf16 M256 N256 A=MN B=MN": (256, 256, 1, 1)}
+    got = idesc_majors()
+    assert len(got) == 3
+    for d in got:
+        m, n, am, bm = want[d["what"]]
+        assert kl.mma_instr_desc_major(kl.KL_BF16, kl.KL_BF16, kl.KL_F32, m, n, am, bm) == int(d["value"], 16)
