@@ -97,6 +97,23 @@ KL_DEVICE void tma_store_2d(const void* map, uint32_t src, int32_t x, int32_t y)
                : "memory");
 }
 
+// Reducing stores: global[box] += shared[box], element-wise in the tensor map's data type (the
+// kernels here use them on fp32 tensors only), performed by the TMA unit. Same bulk-group
+// completion as the plain stores.
+KL_DEVICE void tma_reduce_add_2d(const void* map, uint32_t src, int32_t x, int32_t y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+
+KL_DEVICE void tma_reduce_add_3d(const void* map, uint32_t src, int32_t x, int32_t y, int32_t z) {
+  asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
 KL_DEVICE void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Wait until at most N committed store groups still read shared memory.

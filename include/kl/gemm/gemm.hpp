@@ -37,6 +37,9 @@ struct Problem {
   // Batched GEMM: `batch` independent problems, A/B/C matrix b at a/b/c + b * stride_*.
   int64_t batch = 1;
   int64_t stride_a = 0, stride_b = 0, stride_c = 0;  // elements
+  // 0: C = result. 1: C += result, by TMA reducing stores (fp32 add in the TMA unit, so fp32 C
+  // only; every peer copy of C gets the same add; not with the direct-store epilogue).
+  int c_reduce = 0;
 };
 
 // Library defaults for the knobs a Problem leaves at 0.
@@ -148,6 +151,11 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   if (pr.n_peers < 0 || pr.n_peers > kMaxPeers) throw std::invalid_argument("kl::gemm: at most 7 peer copies of C");
   if (pr.n_peers > 0 && Cfg::kDirectStore)
     throw std::invalid_argument("kl::gemm: peer stores need the TMA-store epilogue");
+  if (pr.c_reduce != 0 && pr.c_reduce != 1) throw std::invalid_argument("kl::gemm: c_reduce must be 0 (store) or 1 (add)");
+  if (pr.c_reduce && Cfg::kDirectStore)
+    throw std::invalid_argument("kl::gemm: reducing stores need the TMA-store epilogue");
+  if (pr.c_reduce && !std::is_same_v<OutT, float>)
+    throw std::invalid_argument("kl::gemm: reducing stores (C += result) need an fp32 C");
   for (int q = 0; q < pr.n_peers; ++q) {
     auto* pc = static_cast<OutT*>(pr.peer_c[q]);
     p.map_peer[q] = pr.batch > 1 ? make_tma_store<typename Cfg::CBox>(matrix(pc, pr.m, pr.n, pr.ldc, pr.stride_c)).map
@@ -175,6 +183,7 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   a.clock_probe = pr.clock_probe;
   a.batch = int(pr.batch);
   a.batch_stride_c = pr.stride_c;
+  a.c_reduce = pr.c_reduce;
 
   const long long all_tiles = (long long)a.tiles_m * a.tiles_n * a.batch;
   if (all_tiles > INT32_MAX) throw std::invalid_argument("kl::gemm: too many tiles");

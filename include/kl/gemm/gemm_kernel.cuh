@@ -23,6 +23,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <cstdint>
 #include <type_traits>
@@ -44,7 +45,7 @@ enum : int {
 };
 
 template <typename InT, typename OutT, int CtaGroup, int BlockN, int Stages, bool DirectStore = false,
-          bool AMn = false, bool BMn = false>
+          bool AMn = false, bool BMn = false, class Sw = Swizzle128B>
 struct TnConfig {
   using in_type = InT;
   using out_type = OutT;
@@ -57,7 +58,7 @@ struct TnConfig {
   static constexpr int kTileM = kCtaM * CtaGroup;      // rows of C per tile
   static constexpr int kTileN = BlockN;                // columns of C per tile (UMMA N)
   static constexpr int kCtaN = BlockN / CtaGroup;      // rows of B each CTA loads
-  static constexpr int kBlockK = 128 / int(sizeof(InT));  // one 128-byte swizzle span of K
+  static constexpr int kBlockK = 128 / int(sizeof(InT));  // 128 bytes of K per stage
   static constexpr int kUmmaK = 32 / int(sizeof(InT));    // K of one tcgen05.mma
   static constexpr int kStages = Stages;
   static constexpr int kNumAcc = 2;
@@ -72,8 +73,12 @@ struct TnConfig {
   // read by the MMA through MN-major descriptors (instruction-descriptor major bit 1).
   static constexpr bool kAMn = AMn;
   static constexpr bool kBMn = BMn;
-  using ATile = std::conditional_t<AMn, SmemTile<InT, kBlockK, kCtaM>, SmemTile<InT, kCtaM, kBlockK>>;
-  using BTile = std::conditional_t<BMn, SmemTile<InT, kBlockK, kCtaN>, SmemTile<InT, kCtaN, kBlockK>>;
+  // Operand swizzle of K-major tiles. 128 B (the default) makes a stage's K one swizzle atom wide;
+  // with 64 B or 32 B the same 128 bytes of K are two or four atom columns, each its own TMA box,
+  // and the K-slices of the MMAs step across them (block_offset_16B).
+  using swizzle = Sw;
+  using ATile = std::conditional_t<AMn, SmemTile<InT, kBlockK, kCtaM>, SmemTile<InT, kCtaM, kBlockK, Sw>>;
+  using BTile = std::conditional_t<BMn, SmemTile<InT, kBlockK, kCtaN>, SmemTile<InT, kCtaN, kBlockK, Sw>>;
   using CBox = SmemTile<OutT, 32, kChunkCols>;
 
   static constexpr uint32_t kABytes = ATile::bytes;
@@ -97,6 +102,8 @@ struct TnConfig {
   static_assert(kCtaN % 8 == 0 && kCtaN <= 256, "B tile rows");
   static_assert(BlockN % kChunkCols == 0, "epilogue chunking");
   static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "stages must keep 1 KB alignment");
+  static_assert(std::is_same_v<Sw, Swizzle128B> || (!AMn && !BMn), "MN-major operands use 128-byte swizzle");
+  static_assert(!std::is_same_v<Sw, SwizzleNone>, "operand tiles are swizzled");
 };
 
 struct TnArgs {
@@ -114,6 +121,7 @@ struct TnArgs {
   unsigned long long* clock_probe;  // optional: per CTA {clock64, globaltimer} at start and end
   int batch;                    // independent GEMMs (rank-3 tensor maps when > 1)
   long long batch_stride_c;     // elements between the C matrices (direct-store epilogue)
+  int c_reduce;                 // 0: C = result; 1: C += result (TMA reducing stores, fp32 add)
 };
 
 // Most peers an epilogue can push C tiles to (one NVLink/NVSwitch domain of 8 GPUs).
@@ -170,6 +178,27 @@ KL_DEVICE void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_
 KL_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Two fp32 results rounded (to nearest even) to a 16-bit output type and packed low-first.
+template <typename OutT>
+KL_DEVICE uint32_t pack_out2(float lo, float hi) {
+  if constexpr (std::is_same_v<OutT, __half>) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    return pack_bf16x2(lo, hi);
+  }
+}
+
+template <typename OutT>
+KL_DEVICE OutT to_out(float x) {
+  if constexpr (std::is_same_v<OutT, __half>)
+    return __float2half_rn(x);
+  else if constexpr (std::is_same_v<OutT, __nv_bfloat16>)
+    return __float2bfloat16_rn(x);
+  else
+    return x;
 }
 
 // Issue the TMA boxes of one operand tile. K-major tiles are (rows, K) boxes at (x = k, y = row);
@@ -450,9 +479,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
               for (int j = 0; j < 8; ++j) {
                 if constexpr (sizeof(OutT) == 2) {
                   const float* f = reinterpret_cast<const float*>(&v[8 * j]);
-                  st_global_v4(dst + 8 * j, pack_bf16x2(f[0] * alpha, f[1] * alpha),
-                               pack_bf16x2(f[2] * alpha, f[3] * alpha), pack_bf16x2(f[4] * alpha, f[5] * alpha),
-                               pack_bf16x2(f[6] * alpha, f[7] * alpha));
+                  st_global_v4(dst + 8 * j, pack_out2<OutT>(f[0] * alpha, f[1] * alpha),
+                               pack_out2<OutT>(f[2] * alpha, f[3] * alpha), pack_out2<OutT>(f[4] * alpha, f[5] * alpha),
+                               pack_out2<OutT>(f[6] * alpha, f[7] * alpha));
                 } else {
                   const float* f = reinterpret_cast<const float*>(&v[4 * j]);
                   st_global_v4(dst + 4 * j, __float_as_uint(f[0] * alpha), __float_as_uint(f[1] * alpha),
@@ -463,11 +492,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
 #pragma unroll
               for (int e = 0; e < Cfg::kChunkCols; ++e) {  // unrolled: v stays in registers
                 if (col + e < args.n) {
-                  const float x = __uint_as_float(v[e]) * alpha;
-                  if constexpr (sizeof(OutT) == 2)
-                    dst[e] = __float2bfloat16_rn(x);
-                  else
-                    dst[e] = x;
+                  dst[e] = to_out<OutT>(__uint_as_float(v[e]) * alpha);
                 }
               }
             }
@@ -485,9 +510,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const float* f = reinterpret_cast<const float*>(&v[8 * j]);
-            st_shared_v4(row_addr + ((uint32_t(j) ^ sw) << 4), pack_bf16x2(f[0] * alpha, f[1] * alpha),
-                         pack_bf16x2(f[2] * alpha, f[3] * alpha), pack_bf16x2(f[4] * alpha, f[5] * alpha),
-                         pack_bf16x2(f[6] * alpha, f[7] * alpha));
+            st_shared_v4(row_addr + ((uint32_t(j) ^ sw) << 4), pack_out2<OutT>(f[0] * alpha, f[1] * alpha),
+                         pack_out2<OutT>(f[2] * alpha, f[3] * alpha), pack_out2<OutT>(f[4] * alpha, f[5] * alpha),
+                         pack_out2<OutT>(f[6] * alpha, f[7] * alpha));
           }
         } else {
 #pragma unroll
@@ -501,7 +526,16 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         __syncwarp();
         if (lane == 0) {
           if (store) {
-            if (batched) {
+            if (args.c_reduce) {
+              // C += tile: the TMA unit reads C, adds the staged values and writes the sum back.
+              if (batched) {
+                tma_reduce_add_3d(&p.map_c, buf, col, row0, bz);
+                for (int q = 0; q < p.n_peers; ++q) tma_reduce_add_3d(&p.map_peer[q], buf, col, row0, bz);
+              } else {
+                tma_reduce_add_2d(&p.map_c, buf, col, row0);
+                for (int q = 0; q < p.n_peers; ++q) tma_reduce_add_2d(&p.map_peer[q], buf, col, row0);
+              }
+            } else if (batched) {
               tma_store_3d(&p.map_c, buf, col, row0, bz);
               for (int q = 0; q < p.n_peers; ++q) tma_store_3d(&p.map_peer[q], buf, col, row0, bz);
             } else {

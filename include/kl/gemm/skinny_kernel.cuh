@@ -83,6 +83,7 @@ struct SkinnyArgs {
   int* status;
   unsigned long long timeout_ns;
   int prefetch;           // L2 prefetch distance for weight tiles, in units (0 = off)
+  int c_reduce;           // 0: C = result; 1: C += result (fp32 C)
 };
 
 struct SkinnyParams {
@@ -114,7 +115,8 @@ KL_DEVICE void st_global_b16(void* p, uint16_t v) {
 }
 
 // C[j0 + q][col] = alpha * r[q] for the tokens q < W that exist (one C column per thread: a warp
-// writes 32 consecutive columns of each token row).
+// writes 32 consecutive columns of each token row). With args.c_reduce (fp32 C only) the result
+// is added to C; exactly one thread writes each element, so the read-modify-write needs no atomics.
 template <typename OutT, int W>
 KL_DEVICE void store_c_column(SkinnyArgs const& args, const uint32_t (&r)[32], int j0, int col, float alpha) {
 #pragma unroll
@@ -126,7 +128,8 @@ KL_DEVICE void store_c_column(SkinnyArgs const& args, const uint32_t (&r)[32], i
         __nv_bfloat16 h = __float2bfloat16_rn(v);
         st_global_b16(static_cast<uint16_t*>(args.c) + (long long)j * args.ldc + col, *reinterpret_cast<uint16_t*>(&h));
       } else {
-        static_cast<float*>(args.c)[(long long)j * args.ldc + col] = v;
+        float* dst = static_cast<float*>(args.c) + (long long)j * args.ldc + col;
+        *dst = args.c_reduce ? *dst + v : v;
       }
     }
   }

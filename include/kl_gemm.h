@@ -67,8 +67,10 @@ typedef struct kl_gemm_desc {
   int64_t ldb;
   void* c;       /* device, [m, ldc] */
   int64_t ldc;
-  int32_t ab_type;        /* kl_dtype of A and B: KL_BF16 or KL_E4M3 */
-  int32_t c_type;         /* kl_dtype of C: KL_BF16 or KL_F32 */
+  int32_t ab_type;        /* kl_dtype of A and B: KL_BF16, KL_F16, KL_E4M3 or KL_E5M2 */
+  int32_t c_type;         /* kl_dtype of C. (ab_type, c_type): (bf16, bf16), (bf16, f32), (f16, f16),
+                             (f16, f32), (e4m3, bf16), (e4m3, f32), (e5m2, bf16), (e5m2, f32).
+                             KL_ALGO_SKINNY: (bf16, bf16), (bf16, f32), (e4m3, bf16) */
   float alpha;            /* host scalar */
   const float* scale_a;   /* optional device scalar (NULL = 1): per-tensor dequant scale of A */
   const float* scale_b;   /* optional device scalar (NULL = 1) */
@@ -87,6 +89,16 @@ typedef struct kl_gemm_desc {
    * [K, M] with M contiguous, B stored [K, N]); lda / ldb are then the pitch of the stored
    * matrix. MN-major operands: bf16 inputs with bf16 C on the tile kernels. */
   int32_t a_major, b_major;
+  /* 0: C = result. 1 (add): C += result, in fp32 (c_type must be KL_F32): split-K partial sums,
+   * accumulation into a residual. The tile kernels add with TMA reducing stores
+   * (cp.reduce.async.bulk.tensor .add, performed by the TMA unit), the skinny kernel with a
+   * read-modify-write by the one thread that owns each element. Calls that add into one C from
+   * the same stream are ordered; concurrent calls race on the skinny path. */
+  int32_t c_reduce;
+  /* Operand swizzle span in bytes: 0 (= 128), 128, 64 or 32. 64 and 32 select tile kernels whose
+   * stages hold the same 128 bytes of K as two or four swizzle atoms (one TMA box each); bf16
+   * inputs with bf16 or f32 C, K-major operands. */
+  int32_t swizzle;
 } kl_gemm_desc;
 
 /* Library version: major * 10000 + minor * 100 + patch. */

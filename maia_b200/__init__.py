@@ -61,6 +61,7 @@ class GemmDesc(ctypes.Structure):
         ("batch", ctypes.c_int64),
         ("stride_a", ctypes.c_int64), ("stride_b", ctypes.c_int64), ("stride_c", ctypes.c_int64),
         ("a_major", ctypes.c_int32), ("b_major", ctypes.c_int32),
+        ("c_reduce", ctypes.c_int32), ("swizzle", ctypes.c_int32),
     ]
 
 
@@ -194,10 +195,12 @@ def _dtype_code(t) -> int:
 
 
 def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, group_m=0, max_ctas=0,
-              variant=0, prefetch=0, a_major=0, b_major=0) -> GemmDesc:
+              variant=0, prefetch=0, a_major=0, b_major=0, c_reduce=0, swizzle=0) -> GemmDesc:
     """Descriptor for C = alpha * A . B^T on torch CUDA tensors: A [M,K], B [N,K], C [M,N], or the
     batched forms A [L,M,K], B [L,N,K], C [L,M,N] (L independent GEMMs). a_major / b_major = 1
-    pass the operand MN-major: `a` as the stored [K, M] (A transposed in memory), `b` as [K, N]."""
+    pass the operand MN-major: `a` as the stored [K, M] (A transposed in memory), `b` as [K, N].
+    c_reduce = 1 adds the result into C instead of overwriting it; swizzle picks the operand
+    swizzle span in bytes (0 = 128, 64, 32)."""
     for name, t in (("a", a), ("b", b), ("c", c)):
         if t.dim() not in (2, 3) or t.stride(-1) != 1:
             raise ValueError(f"{name} must be a 2-D or 3-D tensor with a contiguous last dimension")
@@ -214,20 +217,26 @@ def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, gr
                     alpha=float(alpha), scale_a=None if scale_a is None else scale_a.data_ptr(),
                     scale_b=None if scale_b is None else scale_b.data_ptr(), algo=algo, group_m=group_m,
                     max_ctas=max_ctas, variant=variant, prefetch=prefetch, batch=batch, stride_a=bs[0],
-                    stride_b=bs[1], stride_c=bs[2], a_major=a_major, b_major=b_major)
+                    stride_b=bs[1], stride_c=bs[2], a_major=a_major, b_major=b_major, c_reduce=int(c_reduce),
+                    swizzle=swizzle)
 
 
 def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
-         group_m=0, max_ctas=0, variant=0, prefetch=0, a_major=0, b_major=0, workspace=None, stream=None):
-    """out = alpha * a @ b.T [* scale_a * scale_b] on the current CUDA stream, via kl_gemm."""
+         group_m=0, max_ctas=0, variant=0, prefetch=0, a_major=0, b_major=0, accumulate=False, swizzle=0,
+         workspace=None, stream=None):
+    """out = alpha * a @ b.T [* scale_a * scale_b] on the current CUDA stream, via kl_gemm.
+    accumulate=True: out += alpha * a @ b.T (out must be given)."""
     import torch
 
+    if accumulate and out is None:
+        raise ValueError("accumulate=True adds into `out`, which must be given")
     if out is None:
         m = a.shape[-1] if a_major else a.shape[-2]
         n = b.shape[-1] if b_major else b.shape[-2]
         shape = (a.shape[0], m, n) if a.dim() == 3 else (m, n)
         out = torch.empty(shape, dtype=out_dtype or torch.bfloat16, device=a.device)
-    d = gemm_desc(a, b, out, alpha, scale_a, scale_b, algo, group_m, max_ctas, variant, prefetch, a_major, b_major)
+    d = gemm_desc(a, b, out, alpha, scale_a, scale_b, algo, group_m, max_ctas, variant, prefetch, a_major, b_major,
+                  int(bool(accumulate)), swizzle)
     s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
     if workspace is None:
         check(lib().kl_gemm(ctypes.byref(d), ctypes.c_void_p(s)))

@@ -10,6 +10,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -50,14 +51,20 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         return LIB
     objdir = PKG / "_build"
     objdir.mkdir(exist_ok=True)
-    objs = []
+    cmds = []
     for src in SOURCES:
         obj = objdir / (src.stem + ".o")
-        cmd = [nvcc(), *NVCC_FLAGS, "-I", str(ROOT / "include"), "-c", str(src), "-o", str(obj)]
+        cmds.append([nvcc(), *NVCC_FLAGS, "-I", str(ROOT / "include"), "-c", str(src), "-o", str(obj)])
+    objs = [c[-1] for c in cmds]
+
+    def compile_one(cmd):
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
-        objs.append(str(obj))
+
+    # The translation units are independent: compile them side by side.
+    with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as pool:
+        list(pool.map(compile_one, cmds))
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", str(tmp), *objs,
            "-cudart", "static", "-Xlinker", "--no-undefined", "-ldl", "-lpthread", "-lrt"]

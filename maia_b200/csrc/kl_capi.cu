@@ -15,6 +15,7 @@
 #include <kl_gemm.h>
 
 #include "kl_internal.cuh"
+#include "kl_tile.cuh"
 
 namespace {
 
@@ -74,12 +75,7 @@ using E4m3Bf16_2 = TnConfig<kl::e4m3, kl::bf16, 2, 256, 6>;
 
 template <class Cfg>
 kl_status run(Problem const& pr, cudaStream_t stream, LaunchInfo* info = nullptr) {
-  int* status = nullptr;
-  kl_status s = kl::capi::device_status_ptr(&status);
-  if (s != KL_OK) return s;
-  cudaError_t e = launch_tn<Cfg>(pr, status, kl::capi::wait_timeout_ns(), stream, info);
-  if (e != cudaSuccess) return cuda_fail(e, "kl_gemm launch");
-  return KL_OK;
+  return kl::capi::run_cfg<Cfg>(pr, stream, info);
 }
 
 // MN-major operands (A and/or B stored transposed), bf16 -> bf16.
@@ -88,10 +84,70 @@ using Bf16Mn_1 = TnConfig<kl::bf16, kl::bf16, 1, 256, 4, false, AMn, BMn>;
 template <bool AMn, bool BMn>
 using Bf16Mn_2 = TnConfig<kl::bf16, kl::bf16, 2, 256, 6, false, AMn, BMn>;
 
-kl_status run_mn(Problem const& pr, bool pair, bool a_mn, bool b_mn, cudaStream_t stream) {
-  if (a_mn && b_mn) return pair ? run<Bf16Mn_2<true, true>>(pr, stream) : run<Bf16Mn_1<true, true>>(pr, stream);
-  if (a_mn) return pair ? run<Bf16Mn_2<true, false>>(pr, stream) : run<Bf16Mn_1<true, false>>(pr, stream);
-  return pair ? run<Bf16Mn_2<false, true>>(pr, stream) : run<Bf16Mn_1<false, true>>(pr, stream);
+kl_status run_mn(Problem const& pr, bool pair, bool a_mn, bool b_mn, cudaStream_t stream, LaunchInfo* info) {
+  if (a_mn && b_mn) return pair ? run<Bf16Mn_2<true, true>>(pr, stream, info) : run<Bf16Mn_1<true, true>>(pr, stream, info);
+  if (a_mn) return pair ? run<Bf16Mn_2<true, false>>(pr, stream, info) : run<Bf16Mn_1<true, false>>(pr, stream, info);
+  return pair ? run<Bf16Mn_2<false, true>>(pr, stream, info) : run<Bf16Mn_1<false, true>>(pr, stream, info);
+}
+
+// The tile kernel for a request: by operand majors, operand swizzle and (A/B, C) types. Throws
+// std::invalid_argument from the tensor-map builders, like launch_tn.
+kl_status run_tile(kl_gemm_desc const& d, Problem const& pr, bool pair, cudaStream_t stream, LaunchInfo* info,
+                   char const* who) {
+  const bool a_mn = d.a_major == 1, b_mn = d.b_major == 1;
+  const int32_t sw = d.swizzle == 0 ? 128 : d.swizzle;
+  if (sw != 128 && sw != 64 && sw != 32)
+    return fail(KL_ERR_INVALID_ARGUMENT, std::string(who) + ": swizzle must be 0 (default), 128, 64 or 32 bytes");
+  if (a_mn || b_mn) {
+    if (d.ab_type != KL_BF16 || d.c_type != KL_BF16 || sw != 128)
+      return fail(KL_ERR_NOT_SUPPORTED,
+                  std::string(who) + ": MN-major operands are built for bf16 inputs, bf16 C and the 128-byte swizzle");
+    return run_mn(pr, pair, a_mn, b_mn, stream, info);
+  }
+  bool handled = false;
+  kl_status s = KL_OK;
+  if (sw != 128) {
+    s = kl::capi::run_tile_swizzle(sw, d.ab_type, d.c_type, pr, pair, stream, info, &handled);
+    if (handled) return s;
+    return fail(KL_ERR_NOT_SUPPORTED, std::string(who) + ": 64- and 32-byte operand swizzle take bf16 inputs and bf16 or f32 C");
+  }
+  if (d.ab_type == KL_BF16 && d.c_type == KL_BF16)
+    return pair ? run<Bf16Bf16_2>(pr, stream, info) : run<Bf16Bf16_1>(pr, stream, info);
+  if (d.ab_type == KL_BF16 && d.c_type == KL_F32)
+    return pair ? run<Bf16F32_2>(pr, stream, info) : run<Bf16F32_1>(pr, stream, info);
+  if (d.ab_type == KL_E4M3 && d.c_type == KL_BF16)
+    return pair ? run<E4m3Bf16_2>(pr, stream, info) : run<E4m3Bf16_1>(pr, stream, info);
+  s = kl::capi::run_tile_types(d.ab_type, d.c_type, pr, pair, stream, info, &handled);
+  if (handled) return s;
+  return fail(KL_ERR_NOT_SUPPORTED,
+              std::string(who) + ": supported (A/B, C) types are (bf16, bf16), (bf16, f32), (f16, f16), (f16, f32), "
+                                 "(e4m3, bf16), (e4m3, f32), (e5m2, bf16), (e5m2, f32)");
+}
+
+// Problem fields shared by every entry point.
+Problem problem_of(kl_gemm_desc const& d) {
+  Problem pr;
+  pr.m = d.m;
+  pr.n = d.n;
+  pr.k = d.k;
+  pr.a = d.a;
+  pr.lda = d.lda;
+  pr.b = d.b;
+  pr.ldb = d.ldb;
+  pr.c = d.c;
+  pr.ldc = d.ldc;
+  pr.alpha = d.alpha;
+  pr.scale_a = d.scale_a;
+  pr.scale_b = d.scale_b;
+  pr.group_m = d.group_m;
+  pr.max_ctas = d.max_ctas;
+  pr.prefetch = d.prefetch;
+  pr.batch = d.batch > 1 ? d.batch : 1;
+  pr.stride_a = d.stride_a;
+  pr.stride_b = d.stride_b;
+  pr.stride_c = d.stride_c;
+  pr.c_reduce = d.c_reduce;
+  return pr;
 }
 
 // Probe buffer for kl_gemm_clock_probe: one per device, 4 words per CTA, allocated on first use.
@@ -147,13 +203,16 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
   g_last_error.clear();
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   if (d->m < 0 || d->n < 0 || d->k < 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: negative extent");
+  if (d->c_reduce != 0 && d->c_reduce != 1) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: c_reduce must be 0 (store) or 1 (add)");
+  if (d->c_reduce && d->c_type != KL_F32) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: c_reduce (C += result) needs an fp32 C");
   if (d->m == 0 || d->n == 0) return KL_OK;
   if (d->c == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: null C");
   const int c_bytes = elem_bytes_of(d->c_type);
   const int64_t batch = d->batch > 1 ? d->batch : 1;
   if (d->k == 0) {
-    // An empty sum: C = 0.
+    // An empty sum: C = 0, or C unchanged when adding into it.
     if (d->ldc < d->n) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: ldc < n");
+    if (d->c_reduce) return KL_OK;
     for (int64_t i = 0; i < batch; ++i) {
       cudaError_t e = cudaMemset2DAsync(static_cast<char*>(d->c) + size_t(i) * d->stride_c * c_bytes,
                                         size_t(d->ldc) * c_bytes, 0, size_t(d->n) * c_bytes, size_t(d->m), stream);
@@ -163,52 +222,24 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
   }
   if (d->a == nullptr || d->b == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: null A or B");
 
-  Problem pr;
-  pr.m = d->m;
-  pr.n = d->n;
-  pr.k = d->k;
-  pr.a = d->a;
-  pr.lda = d->lda;
-  pr.b = d->b;
-  pr.ldb = d->ldb;
-  pr.c = d->c;
-  pr.ldc = d->ldc;
-  pr.alpha = d->alpha;
-  pr.scale_a = d->scale_a;
-  pr.scale_b = d->scale_b;
-  pr.group_m = d->group_m;
-  pr.max_ctas = d->max_ctas;
-  pr.prefetch = d->prefetch;
-  pr.batch = batch;
-  pr.stride_a = d->stride_a;
-  pr.stride_b = d->stride_b;
-  pr.stride_c = d->stride_c;
-
+  const Problem pr = problem_of(*d);
   const bool a_mn = d->a_major == 1, b_mn = d->b_major == 1;
   if ((d->a_major != 0 && !a_mn) || (d->b_major != 0 && !b_mn))
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: a_major / b_major must be 0 (K) or 1 (MN)");
+  const bool default_swizzle = d->swizzle == 0 || d->swizzle == 128;
   int algo = d->algo;
   if (algo == KL_ALGO_AUTO)
-    algo = (batch > 1 || a_mn || b_mn) ? (d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA) : kl::capi::choose_algo(*d);
+    algo = (batch > 1 || a_mn || b_mn || !default_swizzle) ? (d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA)
+                                                           : kl::capi::choose_algo(*d);
   if (algo == KL_ALGO_SKINNY && batch > 1) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: KL_ALGO_SKINNY is not batched");
   if (algo == KL_ALGO_SKINNY && (a_mn || b_mn))
     return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: KL_ALGO_SKINNY takes K-major operands");
+  if (algo == KL_ALGO_SKINNY && !default_swizzle)
+    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: KL_ALGO_SKINNY uses the 128-byte swizzle");
   try {
     if (algo == KL_ALGO_SKINNY) return kl::capi::run_skinny(*d, workspace, workspace_bytes, stream);
     if (algo != KL_ALGO_1CTA && algo != KL_ALGO_2CTA) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: unknown algo");
-    const bool pair = algo == KL_ALGO_2CTA;
-    if (a_mn || b_mn) {
-      if (d->ab_type != KL_BF16 || d->c_type != KL_BF16)
-        return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: MN-major operands are built for bf16 inputs and bf16 C");
-      return run_mn(pr, pair, a_mn, b_mn, stream);
-    }
-    if (d->ab_type == KL_BF16 && d->c_type == KL_BF16)
-      return pair ? run<Bf16Bf16_2>(pr, stream) : run<Bf16Bf16_1>(pr, stream);
-    if (d->ab_type == KL_BF16 && d->c_type == KL_F32)
-      return pair ? run<Bf16F32_2>(pr, stream) : run<Bf16F32_1>(pr, stream);
-    if (d->ab_type == KL_E4M3 && d->c_type == KL_BF16)
-      return pair ? run<E4m3Bf16_2>(pr, stream) : run<E4m3Bf16_1>(pr, stream);
-    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: supported (A/B, C) types are (bf16, bf16), (bf16, f32), (e4m3, bf16)");
+    return run_tile(*d, pr, algo == KL_ALGO_2CTA, stream, nullptr, "kl_gemm");
   } catch (std::invalid_argument const& ex) {
     return fail(KL_ERR_INVALID_ARGUMENT, ex.what());
   } catch (std::exception const& ex) {
@@ -231,29 +262,20 @@ kl_status kl_gemm_gather(const kl_gemm_desc* d, void* const* peer_c, int32_t n_p
   int algo = d->algo;
   if (algo == KL_ALGO_AUTO || algo == KL_ALGO_SKINNY) algo = d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA;
   if (algo != KL_ALGO_1CTA && algo != KL_ALGO_2CTA) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: unknown algo");
-  Problem pr;
-  pr.m = d->m; pr.n = d->n; pr.k = d->k;
-  pr.a = d->a; pr.lda = d->lda; pr.b = d->b; pr.ldb = d->ldb; pr.c = d->c; pr.ldc = d->ldc;
-  pr.alpha = d->alpha; pr.scale_a = d->scale_a; pr.scale_b = d->scale_b;
-  pr.group_m = d->group_m; pr.max_ctas = d->max_ctas; pr.prefetch = d->prefetch;
+  if (d->c_reduce != 0 && d->c_reduce != 1)
+    return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: c_reduce must be 0 (store) or 1 (add)");
+  if (d->c_reduce && d->c_type != KL_F32)
+    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_gather: c_reduce (C += result) needs an fp32 C");
+  Problem pr = problem_of(*d);
   pr.peer_c = peer_c;
   pr.n_peers = n_peers;
-  pr.batch = d->batch > 1 ? d->batch : 1;
-  pr.stride_a = d->stride_a;
-  pr.stride_b = d->stride_b;
-  pr.stride_c = d->stride_c;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   try {
-    const bool pair = algo == KL_ALGO_2CTA;
-    if (d->ab_type == KL_BF16 && d->c_type == KL_BF16)
-      return pair ? run<Bf16Bf16_2>(pr, stream) : run<Bf16Bf16_1>(pr, stream);
-    if (d->ab_type == KL_BF16 && d->c_type == KL_F32)
-      return pair ? run<Bf16F32_2>(pr, stream) : run<Bf16F32_1>(pr, stream);
-    if (d->ab_type == KL_E4M3 && d->c_type == KL_BF16)
-      return pair ? run<E4m3Bf16_2>(pr, stream) : run<E4m3Bf16_1>(pr, stream);
-    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_gather: unsupported types");
+    return run_tile(*d, pr, algo == KL_ALGO_2CTA, stream, nullptr, "kl_gemm_gather");
   } catch (std::invalid_argument const& ex) {
     return fail(KL_ERR_INVALID_ARGUMENT, ex.what());
+  } catch (std::exception const& ex) {
+    return fail(KL_ERR_CUDA, ex.what());
   }
 }
 
@@ -313,26 +335,16 @@ kl_status kl_gemm_clock_probe(const kl_gemm_desc* d, uint64_t* out, int32_t out_
     e = cudaMalloc(&g_probe[dev], 4096 * 4 * sizeof(unsigned long long));
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(clock probe)");
   }
-  Problem pr;
-  pr.m = d->m; pr.n = d->n; pr.k = d->k;
-  pr.a = d->a; pr.lda = d->lda; pr.b = d->b; pr.ldb = d->ldb; pr.c = d->c; pr.ldc = d->ldc;
-  pr.alpha = d->alpha; pr.scale_a = d->scale_a; pr.scale_b = d->scale_b;
-  pr.group_m = d->group_m; pr.max_ctas = d->max_ctas; pr.prefetch = d->prefetch;
+  Problem pr = problem_of(*d);
   pr.clock_probe = g_probe[dev];
   LaunchInfo info;
   kl_status s = KL_OK;
   try {
-    const bool pair = algo == KL_ALGO_2CTA;
-    if (d->ab_type == KL_BF16 && d->c_type == KL_BF16)
-      s = pair ? run<Bf16Bf16_2>(pr, stream, &info) : run<Bf16Bf16_1>(pr, stream, &info);
-    else if (d->ab_type == KL_BF16 && d->c_type == KL_F32)
-      s = pair ? run<Bf16F32_2>(pr, stream, &info) : run<Bf16F32_1>(pr, stream, &info);
-    else if (d->ab_type == KL_E4M3 && d->c_type == KL_BF16)
-      s = pair ? run<E4m3Bf16_2>(pr, stream, &info) : run<E4m3Bf16_1>(pr, stream, &info);
-    else
-      return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_clock_probe: unsupported types");
+    s = run_tile(*d, pr, algo == KL_ALGO_2CTA, stream, &info, "kl_gemm_clock_probe");
   } catch (std::invalid_argument const& ex) {
     return fail(KL_ERR_INVALID_ARGUMENT, ex.what());
+  } catch (std::exception const& ex) {
+    return fail(KL_ERR_CUDA, ex.what());
   }
   if (s != KL_OK) return s;
   if (info.grid > 4096 || 4 * info.grid > out_words) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_clock_probe: output too small");

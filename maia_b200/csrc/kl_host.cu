@@ -66,6 +66,9 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
   if (h->m <= 0 || h->n <= 0 || h->k <= 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_host: m, n and k must be positive");
   if (h->lda < h->k || h->ldb < h->k || h->ldc < h->n) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_host: leading dimension too small");
   if (h->batch > 1) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_host: one problem per call (batch must be 0 or 1)");
+  if (h->c_reduce != 0) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_host: C is output only (c_reduce must be 0)");
+  if (h->a_major != 0 || h->b_major != 0)
+    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_host: K-major operands only (B is streamed by rows)");
   cudaStream_t caller = static_cast<cudaStream_t>(stream_ptr);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

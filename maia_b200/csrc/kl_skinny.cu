@@ -107,6 +107,7 @@ kl_status launch(kl_gemm_desc const& d, Plan const& pl, void* ws, cudaStream_t s
   a.status = status;
   a.timeout_ns = wait_timeout_ns();
   a.prefetch = d.prefetch > 0 ? d.prefetch : d.prefetch < 0 ? 0 : kDefaultPrefetchSkinny;
+  a.c_reduce = d.c_reduce;
   gemm_skinny_kernel<Cfg><<<pl.grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? KL_OK : cuda_fail(e, "skinny launch");
@@ -193,7 +194,9 @@ void mark_workspace_dirty(int device) {
 int choose_algo(kl_gemm_desc const& d) {
   // A CTA pair needs at least 256 rows to fill its tile; up to 128 rows the weights dominate
   // traffic and the stream-K skinny kernel keeps every SM streaming.
-  if (d.m <= 128 && (d.ab_type == KL_BF16 || d.ab_type == KL_E4M3)) return KL_ALGO_SKINNY;
+  const bool skinny_types = (d.ab_type == KL_BF16 && (d.c_type == KL_BF16 || d.c_type == KL_F32)) ||
+                            (d.ab_type == KL_E4M3 && d.c_type == KL_BF16);
+  if (d.m <= 128 && skinny_types) return KL_ALGO_SKINNY;
   return d.m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA;
 }
 

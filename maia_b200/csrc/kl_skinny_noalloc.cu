@@ -101,6 +101,7 @@ kl_status launch(kl_gemm_desc const& d, int n_tiles, int k_blocks, int grid, uns
   a.status = status;
   a.timeout_ns = kl::capi::wait_timeout_ns();
   a.prefetch = d.prefetch > 0 ? d.prefetch : d.prefetch < 0 ? 0 : kDefaultPrefetchSkinny;
+  a.c_reduce = d.c_reduce;
   gemm_skinny_kernel<Cfg><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? KL_OK : kl::capi::cuda_fail(e, "no-alloc skinny launch");
@@ -130,6 +131,12 @@ extern "C" kl_status kl_gemm_skinny_noalloc(const kl_gemm_desc* d, void* stream_
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_skinny_noalloc: m, n and k must be positive");
   if (d->m > 256) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_skinny_noalloc: at most 256 rows of A");
   if (d->batch > 1) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_skinny_noalloc: one problem per call");
+  if (d->a_major != 0 || d->b_major != 0 || (d->swizzle != 0 && d->swizzle != 128))
+    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_skinny_noalloc: K-major operands with the 128-byte swizzle only");
+  if (d->c_reduce != 0 && d->c_reduce != 1)
+    return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_skinny_noalloc: c_reduce must be 0 (store) or 1 (add)");
+  if (d->c_reduce && d->c_type != KL_F32)
+    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_skinny_noalloc: c_reduce (C += result) needs an fp32 C");
   if (d->n > INT32_MAX || d->k > INT32_MAX)
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_skinny_noalloc: extents must fit in 32 bits");
   if (d->a == nullptr || d->b == nullptr || d->c == nullptr)

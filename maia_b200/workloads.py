@@ -115,6 +115,57 @@ def f32_to_e4m3_bits_nearest(x: np.ndarray) -> np.ndarray:
     return np.where(np.signbit(x) & (q != 0), q | 0x80, q).astype(np.uint8)
 
 
+_E5M2_TABLE = None
+
+
+def e5m2_values() -> np.ndarray:
+    """The 256 e5m2 values by bit pattern (infinities at 0x7C / 0xFC, NaN above them)."""
+    global _E5M2_TABLE
+    if _E5M2_TABLE is None:
+        v = np.arange(256)
+        sign = np.where(v & 0x80, -1.0, 1.0)
+        exp = (v >> 2) & 0x1F
+        man = v & 3
+        mag = np.where(exp == 0, man / 4.0 * 2.0 ** -14, (1 + man / 4.0) * 2.0 ** (exp - 15.0))
+        vals = sign * mag
+        vals[exp == 31] = np.where(man[exp == 31] == 0, np.inf, np.nan) * sign[exp == 31]
+        _E5M2_TABLE = vals
+    return _E5M2_TABLE
+
+
+def f32_to_e5m2_bits(x: np.ndarray) -> np.ndarray:
+    """Round float32 to the nearest e5m2 value (ties to even mantissa), saturating at +-57344.
+
+    As for e4m3: keep 2 mantissa bits of the float32 pattern with round-to-nearest-even and rebias
+    the exponent from 127 to 15; below 2^-14 the grid is uniform with step 2^-16."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32)
+    sign = ((u >> 24) & np.uint32(0x80)).astype(np.uint8)
+    mag = u & np.uint32(0x7FFFFFFF)
+    rounded = (mag + np.uint32(0xFFFFF) + ((mag >> 21) & np.uint32(1))) >> 21
+    normal = rounded.astype(np.int64) - (112 << 2)
+    sub = np.rint(np.minimum(np.abs(x).astype(np.float64), 1.0) * 65536.0).astype(np.int64)
+    q = np.where(mag < np.uint32(0x38800000), sub, normal)                # 0x38800000 = 2^-14
+    q = np.clip(q, 0, 0x7B).astype(np.uint8)
+    return np.where(q != 0, q | sign, q).astype(np.uint8)
+
+
+def f32_to_e5m2_bits_nearest(x: np.ndarray) -> np.ndarray:
+    """Slow definition of the same rounding: search the sorted grid of finite e5m2 values."""
+    grid = e5m2_values()[np.arange(0, 0x7C)]
+    a = np.minimum(np.abs(np.asarray(x, dtype=np.float64)), 57344.0)
+    idx = np.clip(np.searchsorted(grid, a), 1, len(grid) - 1)
+    lo, hi = grid[idx - 1], grid[idx]
+    pick_hi = (a - lo > hi - a) | ((a - lo == hi - a) & (idx % 2 == 0))
+    q = np.where(pick_hi, idx, idx - 1).astype(np.uint8)
+    return np.where(np.signbit(x) & (q != 0), q | 0x80, q).astype(np.uint8)
+
+
+def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
+    """Round float32 to IEEE binary16 (nearest, ties to even); returns the 16-bit patterns."""
+    return np.ascontiguousarray(x, dtype=np.float32).astype(np.float16).view(np.uint16)
+
+
 def draw(w: Workload, tensor_id: int, rows: int, cols: int, scale: float) -> np.ndarray:
     rng = np.random.Generator(np.random.PCG64(w.seed * 1000 + tensor_id))
     if w.dist == "uniform":

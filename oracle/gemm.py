@@ -1,7 +1,8 @@
 """ctypes binding of libkl_oracle.so (gemm_oracle.c). TEST INFRASTRUCTURE ONLY.
 
-Inputs are raw element bits as numpy arrays: uint16 for bf16, uint8 for e4m3, row-major with the
-given leading dimension.
+Inputs are raw element bits as numpy arrays, row-major: uint16 for bf16, uint8 for e4m3 (the
+defaults), np.float16 for f16; pass `kind` for the other formats (F16 on uint16 bits, E5M2 on
+uint8 bits). Type codes follow the library's kl_dtype.
 """
 
 from __future__ import annotations
@@ -15,7 +16,8 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libkl_oracle.so"
-BF16, E4M3 = 0, 2
+BF16, F16, E4M3, E5M2 = 0, 1, 2, 3
+KINDS = {"bf16": BF16, "f16": F16, "e4m3": E4M3, "e5m2": E5M2}
 _lib = None
 
 
@@ -42,26 +44,33 @@ def lib():
     return _lib
 
 
-def _kind(a: np.ndarray) -> int:
+def _kind(a: np.ndarray, kind=None) -> int:
+    if kind is not None:
+        k = KINDS[kind] if isinstance(kind, str) else int(kind)
+        if (k in (BF16, F16)) != (a.dtype.itemsize == 2) or a.dtype.itemsize not in (1, 2):
+            raise TypeError(f"element kind {kind} does not match {a.dtype} bits")
+        return k
     if a.dtype == np.uint16:
         return BF16
+    if a.dtype == np.float16:
+        return F16
     if a.dtype == np.uint8:
         return E4M3
-    raise TypeError("inputs are raw bits: uint16 (bf16) or uint8 (e4m3)")
+    raise TypeError("inputs are raw bits: uint16 (bf16), uint8 (e4m3), float16, or pass kind=")
 
 
 def threads_default() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
 
 
-def decode(bits: np.ndarray) -> np.ndarray:
+def decode(bits: np.ndarray, kind=None) -> np.ndarray:
     bits = np.ascontiguousarray(bits)
     out = np.empty(bits.shape, dtype=np.float64)
-    lib().kl_oracle_decode(_kind(bits), bits.ctypes.data, bits.size, out.ctypes.data)
+    lib().kl_oracle_decode(_kind(bits, kind), bits.ctypes.data, bits.size, out.ctypes.data)
     return out
 
 
-def gemm_f64(a: np.ndarray, b: np.ndarray, scale: float = 1.0, threads: int | None = None) -> np.ndarray:
+def gemm_f64(a: np.ndarray, b: np.ndarray, scale: float = 1.0, threads: int | None = None, kind=None) -> np.ndarray:
     """scale * A . B^T with fp64 accumulation; A [M,K], B [N,K] raw bits."""
     a = np.ascontiguousarray(a)
     b = np.ascontiguousarray(b)
@@ -69,20 +78,20 @@ def gemm_f64(a: np.ndarray, b: np.ndarray, scale: float = 1.0, threads: int | No
     m, k = a.shape
     n = b.shape[0]
     c = np.empty((m, n), dtype=np.float64)
-    rc = lib().kl_oracle_gemm_f64(_kind(a), a.ctypes.data, k, b.ctypes.data, k, m, n, k, float(scale),
+    rc = lib().kl_oracle_gemm_f64(_kind(a, kind), a.ctypes.data, k, b.ctypes.data, k, m, n, k, float(scale),
                                   c.ctypes.data, n, threads or threads_default())
     assert rc == 0
     return c
 
 
-def gemm_f32(a: np.ndarray, b: np.ndarray, scale: float = 1.0, threads: int | None = None) -> np.ndarray:
+def gemm_f32(a: np.ndarray, b: np.ndarray, scale: float = 1.0, threads: int | None = None, kind=None) -> np.ndarray:
     """scale * A . B^T with fp32 accumulation (the timed CPU baseline)."""
     a = np.ascontiguousarray(a)
     b = np.ascontiguousarray(b)
     m, k = a.shape
     n = b.shape[0]
     c = np.empty((m, n), dtype=np.float32)
-    rc = lib().kl_oracle_gemm_f32(_kind(a), a.ctypes.data, k, b.ctypes.data, k, m, n, k, float(scale),
+    rc = lib().kl_oracle_gemm_f32(_kind(a, kind), a.ctypes.data, k, b.ctypes.data, k, m, n, k, float(scale),
                                   c.ctypes.data, n, threads or threads_default())
     assert rc == 0
     return c

@@ -14,11 +14,14 @@
  *   kl_oracle_gemm_f64   fp64 accumulation over the decoded inputs, times `scale`: the checker.
  *   kl_oracle_gemm_f32   fp32 accumulation, cache-blocked, all host threads: the timed CPU
  *                        baseline (the "CPU reference GEMM" of the benchmark's smallest config).
- *   kl_oracle_decode     element decoders (bf16, e4m3), exposed so tests can check them.
+ *   kl_oracle_decode     element decoders (bf16, f16, e4m3, e5m2), exposed so tests can check
+ *                        them.
  *
  * Element decoding follows the formats' definitions: bf16 is the top half of an IEEE binary32;
- * e4m3 (OCP FP8, "fn" variant) has 1 sign, 4 exponent (bias 7), 3 mantissa bits, no infinities,
- * and S.1111.111 is NaN.
+ * f16 is IEEE binary16 (1 sign, 5 exponent bits with bias 15, 10 mantissa bits); e4m3 (OCP FP8,
+ * "fn" variant) has 1 sign, 4 exponent (bias 7), 3 mantissa bits, no infinities, and S.1111.111 is
+ * NaN; e5m2 (OCP FP8) has 1 sign, 5 exponent (bias 15), 2 mantissa bits, with IEEE infinities and
+ * NaNs at exponent 31. Type codes follow the library's kl_dtype: bf16 0, f16 1, e4m3 2, e5m2 3.
  */
 #include <math.h>
 #include <pthread.h>
@@ -27,7 +30,11 @@
 #include <string.h>
 
 #define KL_ORACLE_BF16 0
+#define KL_ORACLE_F16 1
 #define KL_ORACLE_E4M3 2
+#define KL_ORACLE_E5M2 3
+
+static int elem_size(int t) { return (t == KL_ORACLE_BF16 || t == KL_ORACLE_F16) ? 2 : 1; }
 
 static double decode_bf16(uint16_t h) {
   uint32_t bits = (uint32_t)h << 16;
@@ -49,11 +56,34 @@ static double decode_e4m3(uint8_t v) {
   return sign ? -x : x;
 }
 
-/* Decode `n` elements of type `t` (KL_ORACLE_BF16 / KL_ORACLE_E4M3) to double. */
+/* IEEE-style binary format with `eb` exponent bits (bias 2^(eb-1) - 1) and `mb` mantissa bits:
+ * f16 (5, 10) and e5m2 (5, 2). The all-ones exponent holds infinities and NaNs. */
+static double decode_ieee(uint32_t v, int eb, int mb) {
+  const int sign = (v >> (eb + mb)) & 1;
+  const int exp = (v >> mb) & ((1 << eb) - 1);
+  const uint32_t man = v & ((1u << mb) - 1);
+  const int bias = (1 << (eb - 1)) - 1;
+  double x;
+  if (exp == (1 << eb) - 1)
+    x = man ? NAN : INFINITY;
+  else if (exp == 0)
+    x = ldexp((double)man, 1 - bias - mb); /* subnormal: 0.m * 2^(1-bias) */
+  else
+    x = ldexp((double)((1u << mb) | man), exp - bias - mb);
+  return sign ? -x : x;
+}
+
+/* Decode `n` elements of type `t` (KL_ORACLE_*) to double. */
 void kl_oracle_decode(int t, const void* src, int64_t n, double* dst) {
   if (t == KL_ORACLE_BF16) {
     const uint16_t* s = (const uint16_t*)src;
     for (int64_t i = 0; i < n; ++i) dst[i] = decode_bf16(s[i]);
+  } else if (t == KL_ORACLE_F16) {
+    const uint16_t* s = (const uint16_t*)src;
+    for (int64_t i = 0; i < n; ++i) dst[i] = decode_ieee(s[i], 5, 10);
+  } else if (t == KL_ORACLE_E5M2) {
+    const uint8_t* s = (const uint8_t*)src;
+    for (int64_t i = 0; i < n; ++i) dst[i] = decode_ieee(s[i], 5, 2);
   } else {
     const uint8_t* s = (const uint8_t*)src;
     for (int64_t i = 0; i < n; ++i) dst[i] = decode_e4m3(s[i]);
@@ -79,7 +109,7 @@ static void* f64_rows(void* arg) {
   job_t* j = (job_t*)arg;
   double* arow = (double*)malloc(sizeof(double) * (size_t)j->k);
   double* c = (double*)j->c;
-  const int esz = j->t == KL_ORACLE_BF16 ? 2 : 1;
+  const int esz = elem_size(j->t);
   for (int64_t i = j->row_begin; i < j->row_end; ++i) {
     kl_oracle_decode(j->t, (const char*)j->a + (size_t)(i * j->lda) * esz, j->k, arow);
     for (int64_t col = 0; col < j->n; ++col) {
@@ -110,7 +140,7 @@ static int clamp_threads(int threads, int64_t rows) {
 /* c[i*ldc + j] = scale * sum_k A[i,k] * B[j,k] in double, for rows [0, m). Returns 0 on success. */
 int kl_oracle_gemm_f64(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
                        int64_t k, double scale, double* c, int64_t ldc, int threads) {
-  const int esz = t == KL_ORACLE_BF16 ? 2 : 1;
+  const int esz = elem_size(t);
   double* bdec = (double*)malloc(sizeof(double) * (size_t)n * (size_t)(k > 0 ? k : 1));
   if (!bdec) return 1;
   for (int64_t r = 0; r < n; ++r) kl_oracle_decode(t, (const char*)b + (size_t)(r * ldb) * esz, k, bdec + r * k);
@@ -132,7 +162,7 @@ int kl_oracle_gemm_f64(int t, const void* a, int64_t lda, const void* b, int64_t
 #define KB 512
 static void* f32_rows(void* arg) {
   job_t* j = (job_t*)arg;
-  const int esz = j->t == KL_ORACLE_BF16 ? 2 : 1;
+  const int esz = elem_size(j->t);
   const int64_t k = j->k;
   float* c = (float*)j->c;
   float* ablk = (float*)malloc(sizeof(float) * 4 * (size_t)k);
@@ -167,7 +197,7 @@ static void* f32_rows(void* arg) {
 
 int kl_oracle_gemm_f32(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
                        int64_t k, double scale, float* c, int64_t ldc, int threads) {
-  const int esz = t == KL_ORACLE_BF16 ? 2 : 1;
+  const int esz = elem_size(t);
   float* bdec = (float*)malloc(sizeof(float) * (size_t)n * (size_t)(k > 0 ? k : 1));
   double* tmp = (double*)malloc(sizeof(double) * (size_t)(k > 0 ? k : 1));
   if (!bdec || !tmp) return 1;

@@ -33,6 +33,7 @@ template <> const char* tname<kl::f16>() { return "f16"; }
 template <> const char* tname<float>() { return "f32"; }
 template <> const char* tname<int8_t>() { return "i8"; }
 template <> const char* tname<kl::e4m3>() { return "e4m3"; }
+template <> const char* tname<kl::e5m2>() { return "e5m2"; }
 
 template <typename Tile>
 void dump_tile() {
@@ -161,6 +162,8 @@ int main(int argc, char** argv) {
   dump_tile<SmemTile<kl::bf16, 128, 32, kl::Swizzle64B>>();
   dump_tile<SmemTile<kl::bf16, 128, 32, kl::Swizzle32B>>();
   dump_tile<SmemTile<kl::bf16, 128, 16, kl::Swizzle32B>>();
+  dump_tile<SmemTile<kl::bf16, 128, 64, kl::Swizzle64B>>();  // 128 B of K as 2 or 4 atom columns
+  dump_tile<SmemTile<kl::bf16, 128, 64, kl::Swizzle32B>>();
   dump_tile<SmemTile<kl::bf16, 128, 8, kl::SwizzleNone>>();
   dump_tile<SmemTile<kl::bf16, 128, 16, kl::SwizzleNone>>();
   dump_tile<SmemTile<kl::bf16, 32, 64>>();
@@ -191,10 +194,15 @@ int main(int argc, char** argv) {
   dump_idesc_ref<kl::e4m3, kl::e4m3, float, 128, 256>();
   dump_idesc_ref<kl::e4m3, kl::e4m3, float, 128, 128>();
   dump_idesc_ref<kl::e4m3, kl::e4m3, float, 64, 64>();
+  dump_idesc_ref<kl::e5m2, kl::e5m2, float, 128, 256>();
+  dump_idesc_ref<kl::e5m2, kl::e5m2, float, 128, 128>();
+  dump_idesc_ref<kl::e4m3, kl::e5m2, float, 128, 256>();
   dump_idesc_cute<kl::bf16, kl::bf16, float, 256, 256>();
   dump_idesc_cute<kl::bf16, kl::bf16, float, 256, 128>();
   dump_idesc_cute<kl::e4m3, kl::e4m3, float, 256, 256>();
   dump_idesc_cute<kl::f16, kl::f16, float, 256, 64>();
+  dump_idesc_cute<kl::f16, kl::f16, float, 256, 256>();
+  dump_idesc_cute<kl::e5m2, kl::e5m2, float, 256, 256>();
   {  // MN-major operand bits (a_major / b_major = 1), CuTe's encoder.
     auto mn = [](auto d, const char* what) {
       begin_entry();

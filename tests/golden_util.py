@@ -8,7 +8,7 @@ from pathlib import Path
 import numpy as np
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-ELEM_BYTES = {"bf16": 2, "f16": 2, "f32": 4, "i8": 1, "e4m3": 1}
+ELEM_BYTES = {"bf16": 2, "f16": 2, "f32": 4, "i8": 1, "e4m3": 1, "e5m2": 1}
 
 
 @lru_cache(None)

@@ -11,7 +11,7 @@ import maia_b200 as kl
 from golden_util import ELEM_BYTES, idesc_majors, idescs, known_answers, mn_tiles, sha, tile_id, tiles
 
 HEADER = Path(__file__).resolve().parent.parent / "include" / "kl_gemm.h"
-TYPE = {"bf16": kl.KL_BF16, "f16": kl.KL_F16, "f32": kl.KL_F32, "i8": kl.KL_I8, "e4m3": kl.KL_E4M3}
+TYPE = {"bf16": kl.KL_BF16, "f16": kl.KL_F16, "f32": kl.KL_F32, "i8": kl.KL_I8, "e4m3": kl.KL_E4M3, "e5m2": kl.KL_E5M2}
 
 
 def declared_symbols():
@@ -131,3 +131,25 @@ def test_instr_desc_majors_match_cute():
     for d in got:
         m, n, am, bm = want[d["what"]]
         assert kl.mma_instr_desc_major(kl.KL_BF16, kl.KL_BF16, kl.KL_F32, m, n, am, bm) == int(d["value"], 16)
+
+
+def test_gemm_desc_layout_matches_the_c_header(tmp_path):
+    """The ctypes mirror of kl_gemm_desc has the C struct's field offsets and size (gcc, x86-64)."""
+    import shutil
+    import subprocess
+
+    gcc = shutil.which("gcc") or shutil.which("cc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    names = [f[0] for f in kl.GemmDesc._fields_]
+    src = tmp_path / "layout.c"
+    body = "".join(f'  printf("%s %zu\\n", "{n}", offsetof(kl_gemm_desc, {n}));\n' for n in names)
+    src.write_text('#include <stddef.h>\n#include <stdio.h>\n#include "kl_gemm.h"\nint main(void) {\n' + body +
+                   '  printf("sizeof %zu\\n", sizeof(kl_gemm_desc));\n  return 0;\n}\n')
+    exe = tmp_path / "layout"
+    subprocess.run([gcc, "-std=c11", "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    got = dict(line.split() for line in subprocess.run([str(exe)], check=True, capture_output=True,
+                                                       text=True).stdout.splitlines())
+    for n in names:
+        assert int(got[n]) == getattr(kl.GemmDesc, n).offset, n
+    assert int(got["sizeof"]) == ctypes.sizeof(kl.GemmDesc)

@@ -78,3 +78,47 @@ def test_rel_error_floor():
     assert abs(elem - 1e-5 / (1e-2 * np.sqrt(0.5))) < 1e-9 and abs(norm - 1e-3) < 1e-12
     elem, _ = og.rel_error(ref + np.array([1e-3, 0, 1e-6, 0]), ref, floor_frac=1e-3)
     assert abs(elem - 1e-6 / (1e-3 * np.sqrt(0.5))) < 1e-9
+
+
+def test_e5m2_table_and_decode():
+    v = wl.e5m2_values()
+    assert v[0x7B] == 57344.0 and v[0x01] == 2.0 ** -16 and v[0x3C] == 1.0 and v[0x7C] == np.inf
+    assert np.isnan(v[0x7D]) and v[0xBC] == -1.0 and v[0xFC] == -np.inf
+    got = og.decode(np.arange(256, dtype=np.uint8), "e5m2")
+    same = (got == v) | (np.isnan(got) & np.isnan(v))
+    assert same.all()
+
+
+def test_e5m2_fast_rounding_matches_nearest_search():
+    rng = np.random.default_rng(1)
+    x = np.concatenate([rng.standard_normal(200000).astype(np.float32) * s for s in (1e-5, 1e-2, 1.0, 300.0, 3e4)])
+    grid = wl.e5m2_values()[:0x7C].astype(np.float32)
+    mids = ((grid[1:] + grid[:-1]) / 2).astype(np.float32)  # exact ties
+    x = np.concatenate([x, grid, -grid, mids, -mids, np.array([57343.0, 57344.0, 61440.0, 1e6, 1e-9], np.float32)])
+    np.testing.assert_array_equal(wl.f32_to_e5m2_bits(x), wl.f32_to_e5m2_bits_nearest(x))
+    # 1 + 1/8 lies halfway between 1.0 (0x3C) and 1.25 (0x3D): ties to the even mantissa.
+    assert wl.f32_to_e5m2_bits(np.array([1.125, 1.375, 1e6, -1e6], np.float32)).tolist() == [0x3C, 0x3E, 0x7B, 0xFB]
+
+
+def test_f16_decode_matches_ieee_binary16():
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    want = bits.view(np.float16).astype(np.float64)
+    got = og.decode(bits, "f16")
+    assert ((got == want) | (np.isnan(got) & np.isnan(want))).all()
+    # float16 arrays are recognised without a kind.
+    np.testing.assert_array_equal(og.decode(np.array([1.5, -2.0], np.float16)), [1.5, -2.0])
+
+
+@pytest.mark.parametrize("dtype", ["f16", "e5m2"])
+def test_gemm_f64_other_formats(dtype):
+    from gpu_util import random_inputs
+
+    a, b, sa, sb = random_inputs(33, 17, 70, dtype, seed=5)
+    ref = og.decode(a, dtype) @ og.decode(b, dtype).T * (sa * sb)
+    np.testing.assert_allclose(og.gemm_f64(a, b, sa * sb, threads=2, kind=dtype), ref, rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(og.gemm_f32(a, b, sa * sb, threads=2, kind=dtype), ref, rtol=1e-4, atol=1e-4)
+
+
+def test_kind_must_match_the_bits():
+    with pytest.raises(TypeError):
+        og.decode(np.zeros(4, np.uint8), "f16")
