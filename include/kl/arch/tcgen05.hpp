@@ -81,6 +81,42 @@ KL_DEVICE void umma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uin
         : "memory");
 }
 
+// Block-scaled 8-bit float inputs (kind::mxf8f6f4.block_scale, one UE8M0 scale per 32 K-elements
+// of each row of A and B): D (+)= sum_k (A[m,k] * 2^(sfa[m, k/32] - 127)) * (B[n,k] * 2^(sfb[n,
+// k/32] - 127)). sfa_tmem / sfb_tmem are the TMEM columns holding the scales (layout written by
+// tmem_cp_32x128b_warpx4); which byte of each 32-bit scale word this MMA uses is the idesc's
+// a_sf_id / b_sf_id. With CtaGroup 2 each CTA of the pair holds the scales of its own 128 rows of
+// A and of all N rows of B, at the same TMEM columns.
+template <int CtaGroup>
+KL_DEVICE void umma_mxf8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t sfa_tmem,
+                            uint32_t sfb_tmem, uint32_t accumulate) {
+  if constexpr (CtaGroup == 1)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+}
+
+// Shared memory -> TMEM copy of 32 rows x 128 bits, replicated into all four 32-lane quarters
+// (lane q*32 + i, columns [col, col + 4) receive row i). `src_desc` is a no-swizzle K-major
+// matrix descriptor of the 32 rows (16 bytes each, 8-row groups 128 bytes apart). Ordered with the
+// tcgen05.mma issued after it by the same thread. With CtaGroup 2 the even CTA issues it and each
+// CTA of the pair copies from its own shared memory into its own TMEM.
+template <int CtaGroup>
+KL_DEVICE void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t src_desc) {
+  if constexpr (CtaGroup == 1)
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src_desc) : "memory");
+  else
+    asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src_desc) : "memory");
+}
+
 // Arrive once on `bar` (a shared::cluster address) when every tcgen05 operation this thread issued
 // so far has completed. With CtaGroup 2 the barrier may be in either CTA of the pair.
 template <int CtaGroup>

@@ -40,6 +40,10 @@ struct Problem {
   // 0: C = result. 1: C += result, by TMA reducing stores (fp32 add in the TMA unit, so fp32 C
   // only; every peer copy of C gets the same add; not with the direct-store epilogue).
   int c_reduce = 0;
+  // MXFP8 (configs with kMx): UE8M0 scales of A and B, one per 32 K-elements of each row, in the
+  // 128 x 4 blocked layout: ceil(rows / 128) x ceil(K / 128) atoms of 512 bytes, row-block major.
+  const void* sfa = nullptr;
+  const void* sfb = nullptr;
 };
 
 // Library defaults for the knobs a Problem leaves at 0.
@@ -184,6 +188,20 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   a.batch = int(pr.batch);
   a.batch_stride_c = pr.stride_c;
   a.c_reduce = pr.c_reduce;
+  if constexpr (Cfg::kMx) {
+    if (pr.sfa == nullptr || pr.sfb == nullptr) throw std::invalid_argument("kl::gemm: MXFP8 needs scales of A and B");
+    if (pr.batch > 1) throw std::invalid_argument("kl::gemm: MXFP8 is not batched");
+    // The blocked scale arrays as [row blocks][K blocks][128 words of 4 bytes].
+    const int64_t kb = (pr.k + 127) / 128;
+    auto sf_map = [&](CUtensorMap* map, void const* ptr, int64_t rows) {
+      const int64_t shape[3] = {(rows + 127) / 128, kb, 128};
+      const int64_t stride[3] = {kb * 128, 128, 1};
+      kl::detail::encode_tma_map(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, CU_TENSOR_MAP_SWIZZLE_NONE, 128, 1, ptr, 3,
+                                 shape, stride, TmaOptions{});
+    };
+    sf_map(&p.map_sfa, pr.sfa, pr.m);
+    sf_map(&p.map_sfb, pr.sfb, pr.n);
+  }
 
   const long long all_tiles = (long long)a.tiles_m * a.tiles_n * a.batch;
   if (all_tiles > INT32_MAX) throw std::invalid_argument("kl::gemm: too many tiles");

@@ -45,7 +45,7 @@ enum : int {
 };
 
 template <typename InT, typename OutT, int CtaGroup, int BlockN, int Stages, bool DirectStore = false,
-          bool AMn = false, bool BMn = false, class Sw = Swizzle128B>
+          bool AMn = false, bool BMn = false, class Sw = Swizzle128B, bool Mx = false>
 struct TnConfig {
   using in_type = InT;
   using out_type = OutT;
@@ -61,10 +61,25 @@ struct TnConfig {
   static constexpr int kBlockK = 128 / int(sizeof(InT));  // 128 bytes of K per stage
   static constexpr int kUmmaK = 32 / int(sizeof(InT));    // K of one tcgen05.mma
   static constexpr int kStages = Stages;
-  static constexpr int kNumAcc = 2;
+  // Block-scaled 8-bit inputs (MXFP8): one UE8M0 scale per 32 K-elements of every row of A and B,
+  // given in the 128 x 4 blocked layout (512-byte atoms: 128 rows x 4 scales, byte
+  // (r % 32) * 16 + (r / 32) * 4 + j for row r and K-group j). Each stage brings, by TMA, the atom
+  // of this CTA's 128 rows of A and the atoms of all the tile's rows of B (in both CTAs of a pair);
+  // the MMA thread moves them into TMEM (tcgen05.cp 32x128b.warpx4) ahead of the stage's
+  // block-scaled MMAs.
+  static constexpr bool kMx = Mx;
+  static constexpr int kSfbAtoms = Mx ? BlockN / 128 : 0;
+  static constexpr uint32_t kSfaBytes = Mx ? 512u : 0u;
+  static constexpr uint32_t kSfbBytes = 512u * kSfbAtoms;
+  // Two TMEM accumulators (epilogue of tile i overlaps the MMAs of tile i + 1), except for MXFP8
+  // with 256 columns: 2 x 256 accumulator columns would leave none for the scales.
+  static constexpr int kNumAcc = (Mx && BlockN == 256) ? 1 : 2;
   static constexpr int kAccCols = BlockN;              // fp32 accumulator columns per buffer
-  static constexpr int kTmemCols = (kAccCols * kNumAcc <= 32) ? 32 : (kAccCols * kNumAcc <= 64) ? 64
-                                 : (kAccCols * kNumAcc <= 128) ? 128 : (kAccCols * kNumAcc <= 256) ? 256 : 512;
+  static constexpr int kSfaCol = kAccCols * kNumAcc;   // TMEM columns of A's and B's scales
+  static constexpr int kSfbCol = kSfaCol + 4;
+  static constexpr int kTmemUsed = kAccCols * kNumAcc + (Mx ? 4 + 4 * kSfbAtoms : 0);
+  static constexpr int kTmemCols = (kTmemUsed <= 32) ? 32 : (kTmemUsed <= 64) ? 64
+                                 : (kTmemUsed <= 128) ? 128 : (kTmemUsed <= 256) ? 256 : 512;
   static constexpr int kChunkCols = 128 / int(sizeof(OutT));  // epilogue store box width (128 B)
   static constexpr int kChunks = BlockN / kChunkCols;
 
@@ -87,16 +102,26 @@ struct TnConfig {
   static constexpr uint32_t kOffA = 0;
   static constexpr uint32_t kOffB = kOffA + kStages * kABytes;
   static constexpr uint32_t kOffC = kOffB + kStages * kBBytes;
-  static constexpr uint32_t kOffBar = kOffC + (DirectStore ? 0u : 8u * kCBytes);  // 4 epilogue warps x 2 buffers
+  static constexpr uint32_t kOffSf = kOffC + (DirectStore ? 0u : 8u * kCBytes);  // 4 epilogue warps x 2 buffers
+  static constexpr uint32_t kOffSfb = kOffSf + kStages * kSfaBytes;
+  static constexpr uint32_t kOffBar = kOffSfb + kStages * kSfbBytes;
   static constexpr uint32_t kNumBars = 2 * kStages + 2 * kNumAcc + 1;
   static constexpr uint32_t kOffSlot = kOffBar + 8 * kNumBars;
   static constexpr uint32_t kSmemBytes = kOffSlot + 16 + 1024;  // + slack to align the base to 1 KB
 
   static constexpr bool kIsF8 = sizeof(InT) == 1;
-  static constexpr uint32_t kIdesc = mma_instr_desc<InT, InT, float, kTileM, BlockN, AMn ? UmmaMajor::MN : UmmaMajor::K,
-                                                    BMn ? UmmaMajor::MN : UmmaMajor::K>();
+  static constexpr uint32_t idesc() {
+    if constexpr (Mx)
+      return mma_instr_desc_block_scaled<InT, InT, kTileM, BlockN>();
+    else
+      return mma_instr_desc<InT, InT, float, kTileM, BlockN, AMn ? UmmaMajor::MN : UmmaMajor::K,
+                            BMn ? UmmaMajor::MN : UmmaMajor::K>();
+  }
+  static constexpr uint32_t kIdesc = idesc();
 
-  static_assert(kTmemCols <= 512 && kAccCols * kNumAcc <= 512, "accumulators exceed TMEM");
+  static_assert(kTmemUsed <= 512, "accumulators and scales exceed TMEM");
+  static_assert(!Mx || (sizeof(InT) == 1 && !AMn && !BMn && std::is_same_v<Sw, Swizzle128B> && BlockN % 128 == 0),
+                "MXFP8: 8-bit K-major operands, 128-byte swizzle, tile N a multiple of 128");
   static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
   static_assert(BlockN % (16 * CtaGroup) == 0 && BlockN <= 256, "UMMA N");
   static_assert(kCtaN % 8 == 0 && kCtaN <= 256, "B tile rows");
@@ -136,6 +161,10 @@ struct TnParams {
   // all-gather. Stores only; nothing in this kernel reads peer memory.
   CUtensorMap map_peer[kMaxPeers];
   int n_peers;
+  // MXFP8 scales (TnConfig::kMx): the blocked arrays of A and B as [row blocks, K blocks, 128]
+  // 32-bit words, box {128, 1, 1} = one 512-byte atom.
+  CUtensorMap map_sfa;
+  CUtensorMap map_sfb;
   TnArgs args;
 };
 
@@ -256,6 +285,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
   const uint32_t a_smem = base + Cfg::kOffA;
   const uint32_t b_smem = base + Cfg::kOffB;
   const uint32_t c_smem = base + Cfg::kOffC;
+  const uint32_t sfa_smem = base + Cfg::kOffSf;
+  const uint32_t sfb_smem = base + Cfg::kOffSfb;
   const uint32_t bar0 = base + Cfg::kOffBar;
   const uint32_t tmem_slot = base + Cfg::kOffSlot;
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
@@ -293,6 +324,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
     tma_prefetch_map(&p.map_a);
     tma_prefetch_map(&p.map_b);
     tma_prefetch_map(&p.map_c);
+    if constexpr (Cfg::kMx) {
+      tma_prefetch_map(&p.map_sfa);
+      tma_prefetch_map(&p.map_sfb);
+    }
   }
   if (warp == 1) {
     tmem_alloc<CG>(tmem_slot, Cfg::kTmemCols);
@@ -344,19 +379,38 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
           }
           const int kx = kb * Cfg::kBlockK;
           if constexpr (CG == 1) {
-            mbarrier_arrive_expect_tx(full_bar(stage), Cfg::kABytes + Cfg::kBBytes);
+            mbarrier_arrive_expect_tx(full_bar(stage), Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes + Cfg::kSfbBytes);
             load_operand<typename Cfg::ATile, Cfg::kAMn, 1>(a_smem + stage * Cfg::kABytes, &p.map_a, full_bar(stage),
                                                             kx, a_row, bz, batched);
             load_operand<typename Cfg::BTile, Cfg::kBMn, 1>(b_smem + stage * Cfg::kBBytes, &p.map_b, full_bar(stage),
                                                             kx, b_row, bz, batched);
+            if constexpr (Cfg::kMx) {
+              // K-block kb's scale atoms: A's row block (tm) and the tile's row blocks of B (a block
+              // past the end of B loads as zeros, for output columns that are never stored).
+              tma_load_3d(sfa_smem + stage * Cfg::kSfaBytes, &p.map_sfa, full_bar(stage), 0, kb, tm);
+#pragma unroll
+              for (int j = 0; j < Cfg::kSfbAtoms; ++j)
+                tma_load_3d(sfb_smem + stage * Cfg::kSfbBytes + 512u * j, &p.map_sfb, full_bar(stage), 0, kb,
+                            tn * Cfg::kSfbAtoms + j);
+            }
           } else {
             // The leader's barrier counts the bytes of both CTAs; only the leader arrives.
-            if (cta_rank == 0) mbarrier_arrive_expect_tx(full_bar(stage), 2u * (Cfg::kABytes + Cfg::kBBytes));
+            if (cta_rank == 0)
+              mbarrier_arrive_expect_tx(full_bar(stage),
+                                        2u * (Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes + Cfg::kSfbBytes));
             const uint32_t fb = leader_full0 + 8u * stage;
             load_operand<typename Cfg::ATile, Cfg::kAMn, 2>(a_smem + stage * Cfg::kABytes, &p.map_a, fb, kx, a_row, bz,
                                                             batched);
             load_operand<typename Cfg::BTile, Cfg::kBMn, 2>(b_smem + stage * Cfg::kBBytes, &p.map_b, fb, kx, b_row, bz,
                                                             batched);
+            if constexpr (Cfg::kMx) {
+              // Each CTA: the scales of its own 128 rows of A, and of all the tile's rows of B.
+              tma_load_3d_pair(sfa_smem + stage * Cfg::kSfaBytes, &p.map_sfa, fb, 0, kb, 2 * tm + int(cta_rank));
+#pragma unroll
+              for (int j = 0; j < Cfg::kSfbAtoms; ++j)
+                tma_load_3d_pair(sfb_smem + stage * Cfg::kSfbBytes + 512u * j, &p.map_sfb, fb, 0, kb,
+                                 tn * Cfg::kSfbAtoms + j);
+            }
           }
           if (++stage == S) {
             stage = 0;
@@ -379,8 +433,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
       uint32_t iter = 0;
       bool ok = true;
       for (int t = worker; ok && t < num_tiles; t += num_workers, ++iter) {
-        const uint32_t acc = iter & 1u;
-        const uint32_t acc_phase = (iter >> 1) & 1u;
+        const uint32_t acc = iter % Cfg::kNumAcc;
+        const uint32_t acc_phase = (iter / Cfg::kNumAcc) & 1u;
         if (!mbarrier_wait(tempty_bar(acc), acc_phase ^ 1u, args.timeout_ns)) {
           record_status(args.status, kStatusMmaTimeout);
           ok = false;
@@ -397,12 +451,28 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
           tcgen05_fence_after();
           const uint64_t a_desc = a_desc0 + ((stage * Cfg::kABytes) >> 4);
           const uint64_t b_desc = b_desc0 + ((stage * Cfg::kBBytes) >> 4);
+          if constexpr (Cfg::kMx) {
+            // The stage's scales into TMEM: one 32x128b copy (replicated to the four lane quarters)
+            // per 128 rows; the MMAs below are ordered after these copies.
+            tmem_cp_32x128b_warpx4<CG>(
+                tmem_base + Cfg::kSfaCol,
+                encode_smem_desc(sfa_smem + stage * Cfg::kSfaBytes, 0, 128, UmmaLayout::SWIZZLE_NONE));
+#pragma unroll
+            for (int j = 0; j < Cfg::kSfbAtoms; ++j)
+              tmem_cp_32x128b_warpx4<CG>(
+                  tmem_base + Cfg::kSfbCol + 4 * j,
+                  encode_smem_desc(sfb_smem + stage * Cfg::kSfbBytes + 512u * j, 0, 128, UmmaLayout::SWIZZLE_NONE));
+          }
 #pragma unroll
           for (int k = 0; k < Cfg::kBlockK / Cfg::kUmmaK; ++k) {
             const uint64_t ka = operand_kstep_16B<typename Cfg::ATile, Cfg::kAMn>(k);
             const uint64_t kb16 = operand_kstep_16B<typename Cfg::BTile, Cfg::kBMn>(k);
             const uint32_t accumulate = (kb | k) != 0;
-            if constexpr (Cfg::kIsF8)
+            if constexpr (Cfg::kMx)  // K-slice k reads byte k of every 32-bit scale word
+              umma_mxf8_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16,
+                               Cfg::kIdesc | (uint32_t(k) << 29) | (uint32_t(k) << 4), tmem_base + Cfg::kSfaCol,
+                               tmem_base + Cfg::kSfbCol, accumulate);
+            else if constexpr (Cfg::kIsF8)
               umma_f8_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16, Cfg::kIdesc, accumulate);
             else
               umma_f16_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16, Cfg::kIdesc, accumulate);
@@ -436,8 +506,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
     for (int t = worker; t < num_tiles; t += num_workers, ++iter) {
       int bz, tm, tn;
       tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, bz, tm, tn);
-      const uint32_t acc = iter & 1u;
-      const uint32_t acc_phase = (iter >> 1) & 1u;
+      const uint32_t acc = iter % Cfg::kNumAcc;
+      const uint32_t acc_phase = (iter / Cfg::kNumAcc) & 1u;
       if (!mbarrier_wait(tfull_bar(acc), acc_phase, args.timeout_ns)) {
         if (lane == 0) record_status(args.status, kStatusEpilogueTimeout);
         break;

@@ -227,4 +227,30 @@ KL_HOST_DEVICE constexpr uint32_t mma_instr_desc() {
                                static_cast<uint32_t>(BMajor));
 }
 
+namespace detail {
+// Block-scaled form (kind::mxf8f6f4.block_scale): no accumulator-format field (fp32 always);
+//   [4,6) B scale-factor id  [7,10) A format  [10,13) B format  [13] negate A  [14] negate B
+//   [15] A major  [16] B major  [17,23) N >> 3  [23] scale format (1 = UE8M0)  [24,29) M >> 4
+//   [29,31) A scale-factor id  [31] K size (0 = K32)
+// The scale-factor ids pick the byte of each 32-bit TMEM scale word an MMA reads.
+KL_HOST_DEVICE constexpr uint32_t instr_desc_block_scaled_rt(uint32_t a_fmt, uint32_t b_fmt, int m, int n,
+                                                             uint32_t a_sf_id = 0, uint32_t b_sf_id = 0,
+                                                             uint32_t a_major = 0, uint32_t b_major = 0) {
+  return (b_sf_id << 4) | (a_fmt << 7) | (b_fmt << 10) | (a_major << 15) | (b_major << 16) |
+         (uint32_t(n >> 3) << 17) | (1u << 23) | (uint32_t(m >> 4) << 24) | (a_sf_id << 29);
+}
+}  // namespace detail
+
+// 32-bit instruction descriptor for a block-scaled 8-bit MMA (MXFP8: e4m3 / e5m2 operands, one
+// UE8M0 scale per 32 K-elements), K-major operands, fp32 accumulate. No counterpart in the
+// reference; the field layout is CuTe's InstrDescriptorBlockScaled.
+template <typename A, typename B, int M, int N>
+KL_HOST_DEVICE constexpr uint32_t mma_instr_desc_block_scaled(uint32_t a_sf_id = 0, uint32_t b_sf_id = 0) {
+  static_assert(M == 128 || M == 256, "block-scaled tcgen05.mma: M = 128 (one CTA) or 256 (CTA pair)");
+  static_assert(N <= 256 && N >= 16 && N % 16 == 0, "N must be a multiple of 16, at most 256");
+  static_assert(bits_of<A> == 8 && bits_of<B> == 8, "MXFP8 operands are 8-bit floats");
+  return detail::instr_desc_block_scaled_rt(detail::umma_operand_format<A>(), detail::umma_operand_format<B>(), M, N,
+                                            a_sf_id, b_sf_id);
+}
+
 }  // namespace kl

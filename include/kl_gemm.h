@@ -99,7 +99,31 @@ typedef struct kl_gemm_desc {
    * stages hold the same 128 bytes of K as two or four swizzle atoms (one TMA box each); bf16
    * inputs with bf16 or f32 C, K-major operands. */
   int32_t swizzle;
+  /* Block scaling. 0: none. 1 (MX): ab_type KL_E4M3 or KL_E5M2 with one UE8M0 scale (value
+   * 2^(s - 127)) per 32 consecutive K-elements of every row of A and of B, in `sfa` / `sfb`
+   * (device), stored in the 128 x 4 blocked layout that kl_mx_pack_scales writes:
+   * kl_mx_scale_bytes(rows, k) bytes. C = alpha * sum_k (A[m,k] sfa[m,k/32]) (B[n,k] sfb[n,k/32])
+   * [* *scale_a * *scale_b]; C bf16 or f32; tile kernels only (KL_ALGO_2CTA: 256 x 256 tiles on a
+   * CTA pair; KL_ALGO_1CTA: variant 0/1 = 128 x 256 tiles, 2 = 128 x 128; KL_ALGO_AUTO picks the
+   * pair from 256 rows of A), K-major operands, 128-byte swizzle, batch 1. */
+  int32_t block_scale;
+  int32_t reserved; /* must be 0 */
+  const void* sfa;
+  const void* sfb;
 } kl_gemm_desc;
+
+/* ---- MXFP8 scale factors ------------------------------------------------------------------
+ * The blocked layout: rows in blocks of 128, K in blocks of 128 elements (4 scales); each
+ * (row block, K block) is a 512-byte atom, atoms stored row-block major ((rb * kb_count + kb) *
+ * 512), and inside an atom the scale of row r, K-group j sits at byte (r % 32) * 16 + (r / 32) * 4
+ * + j. Padding rows and K-groups hold 127 (a scale of 1). No counterpart in the reference. */
+
+/* Bytes of the blocked scale array for `rows` rows and `k` K-elements. */
+KL_API int64_t kl_mx_scale_bytes(int64_t rows, int64_t k);
+
+/* Device: repack row-major UE8M0 scales src[rows][ceil(k / 32)] (row pitch ld_src bytes) into
+ * the blocked layout at dst (kl_mx_scale_bytes(rows, k) bytes, 16-byte aligned). Stream-ordered. */
+KL_API kl_status kl_mx_pack_scales(const void* src, int64_t rows, int64_t k, int64_t ld_src, void* dst, void* stream);
 
 /* Library version: major * 10000 + minor * 100 + patch. */
 KL_API int32_t kl_version(void);
@@ -214,6 +238,13 @@ KL_API kl_status kl_umma_smem_desc(int32_t elem_bytes, int32_t rows, int32_t col
 /* 32-bit tcgen05.mma instruction descriptor, both operands K-major. M = 64/128 (one CTA) or 256
  * (CTA pair). kernel_lib/include/kl/layout/umma_desc.hpp:49-58 (mma_instr_desc, M <= 128 there). */
 KL_API kl_status kl_mma_instr_desc(int32_t a_type, int32_t b_type, int32_t acc_type, int32_t m, int32_t n, uint32_t* out);
+
+/* 32-bit instruction descriptor of a block-scaled (MXFP8, UE8M0 scales) tcgen05.mma:
+ * a_type / b_type KL_E4M3 or KL_E5M2, M = 128 or 256, K-major operands; a_sf_id / b_sf_id (0-3)
+ * select the byte of each TMEM scale word the MMA reads. No counterpart in the reference; pinned to
+ * CuTe's make_instr_desc_block_scaled / make_runtime_instr_desc_block_scaled. */
+KL_API kl_status kl_mma_instr_desc_block_scaled(int32_t a_type, int32_t b_type, int32_t m, int32_t n, int32_t a_sf_id,
+                                                int32_t b_sf_id, uint32_t* out);
 
 /* MN-major form of kl_umma_smem_desc: a tile stored k_rows x mn_cols (MN contiguous, swizzle
  * 32/64/128 bytes), K-slice `k_block`, MN columns [mn_col, mn_col + mn_extent) (0 = to the end).

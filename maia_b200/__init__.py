@@ -34,6 +34,7 @@ EXPORTED = (
     "kl_tma_box_geometry", "kl_tma_box_position", "kl_umma_smem_desc", "kl_mma_instr_desc",
     "kl_make_tma_desc", "kl_gemm_skinny_noalloc", "kl_gemm_host", "kl_gemm_clock_probe", "kl_gemm_gather",
     "kl_ipc_get_handle", "kl_ipc_open_handle", "kl_ipc_close", "kl_umma_smem_desc_mn", "kl_mma_instr_desc_major",
+    "kl_mma_instr_desc_block_scaled", "kl_mx_scale_bytes", "kl_mx_pack_scales",
 )
 
 
@@ -62,6 +63,8 @@ class GemmDesc(ctypes.Structure):
         ("stride_a", ctypes.c_int64), ("stride_b", ctypes.c_int64), ("stride_c", ctypes.c_int64),
         ("a_major", ctypes.c_int32), ("b_major", ctypes.c_int32),
         ("c_reduce", ctypes.c_int32), ("swizzle", ctypes.c_int32),
+        ("block_scale", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("sfa", ctypes.c_void_p), ("sfb", ctypes.c_void_p),
     ]
 
 
@@ -105,6 +108,9 @@ def lib() -> ctypes.CDLL:
             "kl_ipc_close": (i32, [vp]),
             "kl_umma_smem_desc_mn": (i32, [i32, i32, i32, i32, u32, i32, i32, i32, P(u64)]),
             "kl_mma_instr_desc_major": (i32, [i32, i32, i32, i32, i32, i32, i32, P(u32)]),
+            "kl_mma_instr_desc_block_scaled": (i32, [i32, i32, i32, i32, i32, i32, P(u32)]),
+            "kl_mx_scale_bytes": (i64, [i64, i64]),
+            "kl_mx_pack_scales": (i32, [vp, i64, i64, i64, vp, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -162,6 +168,12 @@ def mma_instr_desc_major(a_type, b_type, acc_type, m, n, a_major, b_major) -> in
     return out.value
 
 
+def mma_instr_desc_block_scaled(a_type, b_type, m, n, a_sf_id=0, b_sf_id=0) -> int:
+    out = ctypes.c_uint32()
+    check(lib().kl_mma_instr_desc_block_scaled(a_type, b_type, m, n, a_sf_id, b_sf_id, ctypes.byref(out)))
+    return out.value
+
+
 def mma_instr_desc(a_type, b_type, acc_type, m, n) -> int:
     out = ctypes.c_uint32()
     check(lib().kl_mma_instr_desc(a_type, b_type, acc_type, m, n, ctypes.byref(out)))
@@ -195,12 +207,13 @@ def _dtype_code(t) -> int:
 
 
 def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, group_m=0, max_ctas=0,
-              variant=0, prefetch=0, a_major=0, b_major=0, c_reduce=0, swizzle=0) -> GemmDesc:
+              variant=0, prefetch=0, a_major=0, b_major=0, c_reduce=0, swizzle=0, sfa=None, sfb=None) -> GemmDesc:
     """Descriptor for C = alpha * A . B^T on torch CUDA tensors: A [M,K], B [N,K], C [M,N], or the
     batched forms A [L,M,K], B [L,N,K], C [L,M,N] (L independent GEMMs). a_major / b_major = 1
     pass the operand MN-major: `a` as the stored [K, M] (A transposed in memory), `b` as [K, N].
     c_reduce = 1 adds the result into C instead of overwriting it; swizzle picks the operand
-    swizzle span in bytes (0 = 128, 64, 32)."""
+    swizzle span in bytes (0 = 128, 64, 32). sfa / sfb (uint8 device tensors in the blocked layout of
+    mx_pack_scales) make it an MXFP8 GEMM: one UE8M0 scale per 32 K-elements of each row."""
     for name, t in (("a", a), ("b", b), ("c", c)):
         if t.dim() not in (2, 3) or t.stride(-1) != 1:
             raise ValueError(f"{name} must be a 2-D or 3-D tensor with a contiguous last dimension")
@@ -218,14 +231,16 @@ def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, gr
                     scale_b=None if scale_b is None else scale_b.data_ptr(), algo=algo, group_m=group_m,
                     max_ctas=max_ctas, variant=variant, prefetch=prefetch, batch=batch, stride_a=bs[0],
                     stride_b=bs[1], stride_c=bs[2], a_major=a_major, b_major=b_major, c_reduce=int(c_reduce),
-                    swizzle=swizzle)
+                    swizzle=swizzle, block_scale=int(sfa is not None or sfb is not None),
+                    sfa=None if sfa is None else sfa.data_ptr(), sfb=None if sfb is None else sfb.data_ptr())
 
 
 def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
          group_m=0, max_ctas=0, variant=0, prefetch=0, a_major=0, b_major=0, accumulate=False, swizzle=0,
-         workspace=None, stream=None):
+         sfa=None, sfb=None, workspace=None, stream=None):
     """out = alpha * a @ b.T [* scale_a * scale_b] on the current CUDA stream, via kl_gemm.
-    accumulate=True: out += alpha * a @ b.T (out must be given)."""
+    accumulate=True: out += alpha * a @ b.T (out must be given). sfa/sfb: MXFP8 block scales
+    (see mx_pack_scales)."""
     import torch
 
     if accumulate and out is None:
@@ -236,13 +251,34 @@ def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=Non
         shape = (a.shape[0], m, n) if a.dim() == 3 else (m, n)
         out = torch.empty(shape, dtype=out_dtype or torch.bfloat16, device=a.device)
     d = gemm_desc(a, b, out, alpha, scale_a, scale_b, algo, group_m, max_ctas, variant, prefetch, a_major, b_major,
-                  int(bool(accumulate)), swizzle)
+                  int(bool(accumulate)), swizzle, sfa, sfb)
     s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
     if workspace is None:
         check(lib().kl_gemm(ctypes.byref(d), ctypes.c_void_p(s)))
     else:
         check(lib().kl_gemm_ws(ctypes.byref(d), ctypes.c_void_p(workspace.data_ptr()), workspace.numel() *
                                workspace.element_size(), ctypes.c_void_p(s)))
+    return out
+
+
+def mx_scale_bytes(rows: int, k: int) -> int:
+    """Bytes of the blocked MXFP8 scale array for `rows` rows of `k` K-elements."""
+    return int(lib().kl_mx_scale_bytes(int(rows), int(k)))
+
+
+def mx_pack_scales(scales, k: int, out=None, stream=None):
+    """Repack row-major UE8M0 scales (uint8 device tensor [rows, ceil(k/32)], unit stride in its
+    last dimension) into the blocked layout the MXFP8 GEMM reads; returns the uint8 tensor."""
+    import torch
+
+    rows = scales.shape[0]
+    if scales.dtype != torch.uint8 or scales.dim() != 2 or scales.stride(1) != 1:
+        raise ValueError("scales must be a 2-D uint8 tensor with a contiguous last dimension")
+    if out is None:
+        out = torch.empty(mx_scale_bytes(rows, k), dtype=torch.uint8, device=scales.device)
+    s = stream if stream is not None else torch.cuda.current_stream(scales.device).cuda_stream
+    check(lib().kl_mx_pack_scales(ctypes.c_void_p(scales.data_ptr()), rows, int(k), scales.stride(0),
+                                  ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(s)))
     return out
 
 

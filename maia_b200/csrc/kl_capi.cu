@@ -95,6 +95,15 @@ kl_status run_mn(Problem const& pr, bool pair, bool a_mn, bool b_mn, cudaStream_
 kl_status run_tile(kl_gemm_desc const& d, Problem const& pr, bool pair, cudaStream_t stream, LaunchInfo* info,
                    char const* who) {
   const bool a_mn = d.a_major == 1, b_mn = d.b_major == 1;
+  if (d.block_scale != 0) {
+    if (d.block_scale != 1) return fail(KL_ERR_INVALID_ARGUMENT, std::string(who) + ": block_scale must be 0 or 1 (MX)");
+    if (a_mn || b_mn || (d.swizzle != 0 && d.swizzle != 128) || pr.batch > 1)
+      return fail(KL_ERR_NOT_SUPPORTED, std::string(who) + ": MXFP8 takes K-major operands, 128-byte swizzle, batch 1");
+    bool handled = false;
+    kl_status s = kl::capi::run_tile_mx(d.ab_type, d.c_type, d.variant, pair, pr, stream, info, &handled);
+    if (handled) return s;
+    return fail(KL_ERR_NOT_SUPPORTED, std::string(who) + ": MXFP8 takes e4m3 or e5m2 inputs with bf16 or f32 C");
+  }
   const int32_t sw = d.swizzle == 0 ? 128 : d.swizzle;
   if (sw != 128 && sw != 64 && sw != 32)
     return fail(KL_ERR_INVALID_ARGUMENT, std::string(who) + ": swizzle must be 0 (default), 128, 64 or 32 bytes");
@@ -147,6 +156,8 @@ Problem problem_of(kl_gemm_desc const& d) {
   pr.stride_b = d.stride_b;
   pr.stride_c = d.stride_c;
   pr.c_reduce = d.c_reduce;
+  pr.sfa = d.sfa;
+  pr.sfb = d.sfb;
   return pr;
 }
 
@@ -227,10 +238,15 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
   if ((d->a_major != 0 && !a_mn) || (d->b_major != 0 && !b_mn))
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: a_major / b_major must be 0 (K) or 1 (MN)");
   const bool default_swizzle = d->swizzle == 0 || d->swizzle == 128;
+  if (d->reserved != 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: reserved must be 0");
   int algo = d->algo;
-  if (algo == KL_ALGO_AUTO)
+  if (algo == KL_ALGO_AUTO && d->block_scale != 0)
+    algo = d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA;
+  else if (algo == KL_ALGO_AUTO)
     algo = (batch > 1 || a_mn || b_mn || !default_swizzle) ? (d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA)
                                                            : kl::capi::choose_algo(*d);
+  if (algo == KL_ALGO_SKINNY && d->block_scale != 0)
+    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: MXFP8 runs on the tile kernels (KL_ALGO_1CTA / KL_ALGO_2CTA)");
   if (algo == KL_ALGO_SKINNY && batch > 1) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: KL_ALGO_SKINNY is not batched");
   if (algo == KL_ALGO_SKINNY && (a_mn || b_mn))
     return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: KL_ALGO_SKINNY takes K-major operands");
@@ -260,7 +276,8 @@ kl_status kl_gemm_gather(const kl_gemm_desc* d, void* const* peer_c, int32_t n_p
   for (int q = 0; q < n_peers; ++q)
     if (peer_c[q] == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: null peer C");
   int algo = d->algo;
-  if (algo == KL_ALGO_AUTO || algo == KL_ALGO_SKINNY) algo = d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA;
+  if (algo == KL_ALGO_AUTO || algo == KL_ALGO_SKINNY)
+    algo = d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA;
   if (algo != KL_ALGO_1CTA && algo != KL_ALGO_2CTA) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: unknown algo");
   if (d->c_reduce != 0 && d->c_reduce != 1)
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: c_reduce must be 0 (store) or 1 (add)");
@@ -458,6 +475,20 @@ kl_status kl_mma_instr_desc_major(int32_t a_type, int32_t b_type, int32_t acc_ty
   kl_status s = kl_mma_instr_desc(a_type, b_type, acc_type, m, n, out);
   if (s != KL_OK) return s;
   *out |= (uint32_t(a_major) << 15) | (uint32_t(b_major) << 16);
+  return KL_OK;
+}
+
+kl_status kl_mma_instr_desc_block_scaled(int32_t a_type, int32_t b_type, int32_t m, int32_t n, int32_t a_sf_id,
+                                         int32_t b_sf_id, uint32_t* out) {
+  if (out == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null output");
+  auto fmt = [](int32_t t) { return t == KL_E4M3 ? 0 : t == KL_E5M2 ? 1 : -1; };
+  const int fa = fmt(a_type), fb = fmt(b_type);
+  if (fa < 0 || fb < 0) return fail(KL_ERR_INVALID_ARGUMENT, "block-scaled operands must be e4m3 or e5m2");
+  if (m != 128 && m != 256) return fail(KL_ERR_INVALID_ARGUMENT, "block-scaled M must be 128 or 256");
+  if (n < 16 || n > 256 || n % 16 != 0) return fail(KL_ERR_INVALID_ARGUMENT, "N must be a multiple of 16 in [16, 256]");
+  if (a_sf_id < 0 || a_sf_id > 3 || b_sf_id < 0 || b_sf_id > 3)
+    return fail(KL_ERR_INVALID_ARGUMENT, "scale-factor ids are 0 to 3");
+  *out = kl::detail::instr_desc_block_scaled_rt(uint32_t(fa), uint32_t(fb), m, n, uint32_t(a_sf_id), uint32_t(b_sf_id));
   return KL_OK;
 }
 

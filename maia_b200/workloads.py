@@ -166,6 +166,28 @@ def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(x, dtype=np.float32).astype(np.float16).view(np.uint16)
 
 
+MX_EMAX = {"e4m3": 8, "e5m2": 15}  # exponent of the largest normal element value
+
+
+def mx_quantize(x: np.ndarray, kind: str = "e4m3") -> tuple[np.ndarray, np.ndarray]:
+    """MX quantisation (OCP Microscaling Formats v1.0) of float32 rows in blocks of 32 K-elements:
+    shared scale 2^(floor(log2(amax)) - emax) as UE8M0 bits, elements x / scale rounded to the
+    8-bit format (nearest, ties to even, saturating). Returns (element bits, scale bits
+    [rows, ceil(K/32)])."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, k = x.shape
+    groups = -(-k // 32)
+    padded = np.zeros((rows, groups * 32), dtype=np.float32)
+    padded[:, :k] = x
+    amax = np.abs(padded.reshape(rows, groups, 32)).max(axis=2).astype(np.float64)
+    e = np.where(amax > 0, np.floor(np.log2(np.where(amax > 0, amax, 1.0))), 0.0) - MX_EMAX[kind]
+    sbits = np.clip(e + 127, 0, 254).astype(np.uint8)
+    inv = np.exp2(127.0 - sbits.astype(np.float64))
+    q = (padded.reshape(rows, groups, 32) * inv[:, :, None]).reshape(rows, groups * 32)[:, :k].astype(np.float32)
+    enc = f32_to_e4m3_bits if kind == "e4m3" else f32_to_e5m2_bits
+    return enc(q), sbits
+
+
 def draw(w: Workload, tensor_id: int, rows: int, cols: int, scale: float) -> np.ndarray:
     rng = np.random.Generator(np.random.PCG64(w.seed * 1000 + tensor_id))
     if w.dist == "uniform":

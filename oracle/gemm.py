@@ -97,6 +97,37 @@ def gemm_f32(a: np.ndarray, b: np.ndarray, scale: float = 1.0, threads: int | No
     return c
 
 
+def e8m0_values(s: np.ndarray) -> np.ndarray:
+    """UE8M0 scales (OCP Microscaling Formats v1.0): value 2^(s - 127), s = 255 is NaN."""
+    s = np.asarray(s, dtype=np.float64)
+    return np.where(s == 255, np.nan, np.exp2(s - 127.0))
+
+
+def gemm_mx_f64(a: np.ndarray, b: np.ndarray, sfa: np.ndarray, sfb: np.ndarray, kind=None,
+                scale: float = 1.0) -> np.ndarray:
+    """MX block-scaled product in fp64: scale * sum_k (A[m,k] sfa[m, k/32]) (B[n,k] sfb[n, k/32]).
+
+    a, b: raw 8-bit element bits [M,K] / [N,K]; sfa, sfb: UE8M0 bits [M, ceil(K/32)] /
+    [N, ceil(K/32)], one scale per 32 consecutive K-elements (the OCP MX block size)."""
+    k = a.shape[1]
+    da = decode(a, kind) * np.repeat(e8m0_values(sfa), 32, axis=1)[:, :k]
+    db = decode(b, kind) * np.repeat(e8m0_values(sfb), 32, axis=1)[:, :k]
+    return (da @ db.T) * scale
+
+
+def pack_mx_scales(sf: np.ndarray, k: int) -> np.ndarray:
+    """The blocked scale layout of the MXFP8 GEMM, restated: rows in blocks of 128 and K in blocks
+    of 128 elements (4 scales) form 512-byte atoms stored row-block major; inside an atom the scale
+    of row r, K-group j is byte (r % 32) * 16 + (r / 32) * 4 + j. Padding holds 127 (a scale of 1).
+    This is the 128 x 4 scale-factor atom of CUTLASS's Sm1xxBlockScaledBasicChunk (K-major)."""
+    rows, groups = sf.shape
+    rb, kb = -(-rows // 128), -(-k // 128)
+    full = np.full((rb * 128, kb * 4), 127, dtype=np.uint8)
+    full[:rows, :groups] = sf
+    t = full.reshape(rb, 4, 32, kb, 4)                  # (row block, r / 32, r % 32, K block, j)
+    return np.ascontiguousarray(t.transpose(0, 3, 2, 1, 4)).reshape(-1)
+
+
 def rel_error(c: np.ndarray, ref: np.ndarray, floor_frac: float = 1e-2) -> tuple[float, float]:
     """(element-wise max of |c - r| / max(|r|, floor_frac * rms(r)), normwise max|c - r| / max|r|).
 

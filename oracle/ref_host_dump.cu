@@ -213,6 +213,28 @@ int main(int argc, char** argv) {
     mn(cute::UMMA::make_instr_desc<kl::bf16, kl::bf16, float, 128, 256, Major::K, Major::MN>(), "bf16 M128 N256 A=K B=MN");
     mn(cute::UMMA::make_instr_desc<kl::bf16, kl::bf16, float, 256, 256, Major::MN, Major::MN>(), "bf16 M256 N256 A=MN B=MN");
   }
+  {  // Block-scaled (MXFP8) instruction descriptors, CuTe's encoder: UE8M0 scales, K-major operands;
+     // the runtime form carries the scale-factor ids (TMEM byte of the scale word) in bits 29-30 / 4-5.
+    auto bs = [](uint32_t d, const char* a, const char* b, int m, int n, int a_sf, int b_sf) {
+      begin_entry();
+      std::fprintf(out, "{\"kind\": \"idesc_block_scaled\", \"a\": \"%s\", \"b\": \"%s\", \"m\": %d, \"n\": %d, "
+                   "\"a_sf_id\": %d, \"b_sf_id\": %d, \"value\": \"0x%08x\"}", a, b, m, n, a_sf, b_sf, (unsigned)d);
+    };
+    using cute::UMMA::Major;
+    using UE8 = cutlass::float_ue8m0_t;
+    using E4 = cutlass::float_e4m3_t;
+    using E5 = cutlass::float_e5m2_t;
+    bs(uint32_t(cute::UMMA::make_instr_desc_block_scaled<E4, E4, float, UE8, 128, 256, Major::K, Major::K>()), "e4m3", "e4m3", 128, 256, 0, 0);
+    bs(uint32_t(cute::UMMA::make_instr_desc_block_scaled<E4, E4, float, UE8, 128, 128, Major::K, Major::K>()), "e4m3", "e4m3", 128, 128, 0, 0);
+    bs(uint32_t(cute::UMMA::make_instr_desc_block_scaled<E5, E4, float, UE8, 128, 256, Major::K, Major::K>()), "e5m2", "e4m3", 128, 256, 0, 0);
+    bs(uint32_t(cute::UMMA::make_instr_desc_block_scaled<E5, E5, float, UE8, 256, 256, Major::K, Major::K>()), "e5m2", "e5m2", 256, 256, 0, 0);
+    for (int a_sf = 0; a_sf < 4; ++a_sf)
+      for (int b_sf = 0; b_sf < 4; ++b_sf) {
+        const uint64_t r = cute::UMMA::make_runtime_instr_desc_block_scaled<E4, E4, float, UE8, 128, 256, Major::K, Major::K>(
+            uint32_t(a_sf) << 30 | 0x100u, uint32_t(b_sf) << 30 | 0x108u);
+        bs(uint32_t(r >> 32), "e4m3", "e4m3", 128, 256, a_sf, b_sf);
+      }
+  }
   std::fprintf(out, "\n]\n");
   std::fclose(out);
   return 0;

@@ -10,7 +10,8 @@ CUTLASS/CuTe headers:
    (physical offsets through tile.tensor(), and the un-swizzled layout_b), TmaBox geometry,
    block_offset_16B, the UMMA smem descriptor body at shared address 0, and instruction
    descriptors; plus CuTe's own MN-major operand tiles and make_umma_desc<Major::MN> (the reference
-   is K-major only). Large offset arrays are stored as SHA-256 of their little-endian int64 bytes
+   is K-major only) and CuTe's block-scaled (MXFP8) instruction descriptors, with and without
+   scale-factor ids. Large offset arrays are stored as SHA-256 of their little-endian int64 bytes
    plus a 64-entry prefix.
 2. ref_test_known_answers.json: the known answers written into the reference's unit tests,
    extracted from the test sources as text (file:line recorded with each).

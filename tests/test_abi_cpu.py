@@ -153,3 +153,28 @@ def test_gemm_desc_layout_matches_the_c_header(tmp_path):
     for n in names:
         assert int(got[n]) == getattr(kl.GemmDesc, n).offset, n
     assert int(got["sizeof"]) == ctypes.sizeof(kl.GemmDesc)
+
+
+def test_block_scaled_instr_desc_matches_cute():
+    from golden_util import host_tables
+
+    rows = [t for t in host_tables() if t["kind"] == "idesc_block_scaled"]
+    assert len(rows) == 20
+    for d in rows:
+        got = kl.mma_instr_desc_block_scaled(TYPE[d["a"]], TYPE[d["b"]], d["m"], d["n"], d["a_sf_id"], d["b_sf_id"])
+        assert got == int(d["value"], 16), d
+
+
+def test_block_scaled_instr_desc_errors():
+    with pytest.raises(kl.KlError):
+        kl.mma_instr_desc_block_scaled(kl.KL_BF16, kl.KL_E4M3, 128, 256)
+    with pytest.raises(kl.KlError):
+        kl.mma_instr_desc_block_scaled(kl.KL_E4M3, kl.KL_E4M3, 64, 256)
+    with pytest.raises(kl.KlError):
+        kl.mma_instr_desc_block_scaled(kl.KL_E4M3, kl.KL_E4M3, 128, 256, 4, 0)
+
+
+@pytest.mark.parametrize("rows,k,want", [(1, 1, 512), (128, 128, 512), (129, 128, 1024), (128, 129, 1024),
+                                         (16384, 8192, 128 * 64 * 512), (0, 5, 0)])
+def test_mx_scale_bytes(rows, k, want):
+    assert kl.mx_scale_bytes(rows, k) == want

@@ -1,0 +1,146 @@
+"""MXFP8 (block-scaled e4m3 / e5m2) on the GPU against the fp64 oracle, and the scale repacking
+kernel against the oracle's restatement of the blocked layout.
+
+Inputs are MX-quantised (OCP MX v1.0: a UE8M0 scale per 32 K-elements, elements rounded to the
+8-bit format), so the oracle multiplies exactly the values the GPU sees; the tolerance (5e-2, as
+for every fp8 input) only has to cover fp32 accumulation and the rounding of C.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import maia_b200 as kl
+from maia_b200 import workloads as wl
+from oracle import gemm as og
+
+from gpu_util import TORCH_TYPES, to_device
+
+pytestmark = pytest.mark.gpu
+
+FP8_TOL = 5e-2
+
+
+def mx_inputs(m, n, k, kind, seed, spread=0.0):
+    """MX-quantised A, B; `spread` widens the per-block magnitudes by up to 2^spread."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    xa = rng.standard_normal((m, k), dtype=np.float32)
+    xb = rng.standard_normal((n, k), dtype=np.float32)
+    if spread:
+        xa *= np.exp2(rng.uniform(-spread, spread, (m, -(-k // 32)))).repeat(32, axis=1)[:, :k].astype(np.float32)
+        xb *= np.exp2(rng.uniform(-spread, spread, (n, -(-k // 32)))).repeat(32, axis=1)[:, :k].astype(np.float32)
+    qa, sa = wl.mx_quantize(xa, kind)
+    qb, sb = wl.mx_quantize(xb, kind)
+    return qa, sa, qb, sb
+
+
+def run_mx(qa, sa, qb, sb, kind, out, device, **kw):
+    k = qa.shape[1]
+    a, b = to_device(qa, kind, device), to_device(qb, kind, device)
+    psa = kl.mx_pack_scales(torch.from_numpy(sa).to(device), k)
+    psb = kl.mx_pack_scales(torch.from_numpy(sb).to(device), k)
+    c = kw.pop("c", None)
+    if c is None:
+        c = torch.full((qa.shape[0], qb.shape[0]), float("nan"), dtype=TORCH_TYPES[out], device=device)
+    kl.gemm(a, b, c, sfa=psa, sfb=psb, **kw)
+    torch.cuda.synchronize()
+    assert kl.read_status() == 0, "a device-side wait timed out"
+    return c.float().cpu().numpy()
+
+
+def check_mx(c, qa, sa, qb, sb, kind, tol=FP8_TOL, c0=None, scale=1.0):
+    ref = og.gemm_mx_f64(qa, qb, sa, sb, kind, scale)
+    if c0 is not None:
+        ref = ref + c0
+    assert not np.isnan(c).any(), "output has unwritten (NaN) entries"
+    elem, norm = og.rel_error(c, ref)
+    assert norm <= tol and elem <= tol, f"normwise {norm:.3e}, element-wise {elem:.3e} > {tol}"
+
+
+@pytest.mark.parametrize("rows,k", [(1, 1), (128, 128), (200, 300), (129, 1000), (1024, 4096), (300, 32)])
+def test_pack_scales_matches_the_blocked_layout(cuda, rows, k):
+    rng = np.random.default_rng(rows + k)
+    sf = rng.integers(0, 255, (rows, -(-k // 32)), dtype=np.uint8)
+    got = kl.mx_pack_scales(torch.from_numpy(sf).to(cuda), k).cpu().numpy()
+    assert got.size == kl.mx_scale_bytes(rows, k)
+    np.testing.assert_array_equal(got, og.pack_mx_scales(sf, k))
+
+
+def test_pack_scales_strided_source(cuda):
+    sf = np.random.default_rng(3).integers(100, 150, (256, 40), dtype=np.uint8)
+    src = torch.from_numpy(sf).to(cuda)[:, :32]  # row pitch 40, 32 groups = K 1024
+    got = kl.mx_pack_scales(src, 1024).cpu().numpy()
+    np.testing.assert_array_equal(got, og.pack_mx_scales(sf[:, :32], 1024))
+
+
+KERNELS = pytest.mark.parametrize("algo,variant", [(kl.ALGO_1CTA, 0), (kl.ALGO_1CTA, 2), (kl.ALGO_2CTA, 0)],
+                                  ids=["1cta_n256", "1cta_n128", "2cta"])
+
+
+@KERNELS
+@pytest.mark.parametrize("kind,out", [("e4m3", "bf16"), ("e4m3", "f32"), ("e5m2", "bf16"), ("e5m2", "f32")])
+@pytest.mark.parametrize("shape", [(128, 256, 128), (200, 304, 320), (256, 512, 1024), (1000, 1000, 1008)])
+def test_mx_gemm(cuda, algo, variant, kind, out, shape):
+    m, n, k = shape
+    qa, sa, qb, sb = mx_inputs(m, n, k, kind, seed=m + n + k)
+    c = run_mx(qa, sa, qb, sb, kind, out, cuda, algo=algo, variant=variant)
+    check_mx(c, qa, sa, qb, sb, kind)
+
+
+@KERNELS
+def test_mx_wide_scale_range(cuda, algo, variant):
+    """Block magnitudes spread over 2^-12 .. 2^12: every scale byte matters."""
+    qa, sa, qb, sb = mx_inputs(384, 512, 768, "e4m3", seed=5, spread=12.0)
+    assert sa.max() - sa.min() > 16 and sb.max() - sb.min() > 16
+    c = run_mx(qa, sa, qb, sb, "e4m3", "f32", cuda, algo=algo, variant=variant)
+    check_mx(c, qa, sa, qb, sb, "e4m3")
+
+
+@pytest.mark.parametrize("algo", [kl.ALGO_1CTA, kl.ALGO_2CTA], ids=["1cta", "2cta"])
+def test_mx_persistent_many_tiles(cuda, algo):
+    """More tiles than resident CTAs: each CTA walks several tiles through its accumulators."""
+    qa, sa, qb, sb = mx_inputs(2048, 4096, 512, "e4m3", seed=31)
+    c = run_mx(qa, sa, qb, sb, "e4m3", "bf16", cuda, algo=algo, max_ctas=16)
+    check_mx(c, qa, sa, qb, sb, "e4m3")
+
+
+@pytest.mark.parametrize("algo", [kl.ALGO_1CTA, kl.ALGO_2CTA], ids=["1cta", "2cta"])
+def test_mx_each_scale_is_applied_to_its_own_block(cuda, algo):
+    """Unit scales except one K-group of one row of A and one of B: only the matching outputs move."""
+    m, n, k = 256, 256, 512
+    rng = np.random.default_rng(8)
+    qa = wl.f32_to_e4m3_bits(rng.standard_normal((m, k)).astype(np.float32))
+    qb = wl.f32_to_e4m3_bits(rng.standard_normal((n, k)).astype(np.float32))
+    sa = np.full((m, k // 32), 127, np.uint8)
+    sb = np.full((n, k // 32), 127, np.uint8)
+    sa[77, 9] = 131   # x16 on A row 77, K [288, 320)
+    sb[200, 3] = 124  # /8 on B row 200, K [96, 128)
+    c = run_mx(qa, sa, qb, sb, "e4m3", "f32", cuda, algo=algo)
+    check_mx(c, qa, sa, qb, sb, "e4m3")
+
+
+def test_mx_with_tensor_scales_and_reduce(cuda):
+    m, n, k = 256, 256, 512
+    qa, sa, qb, sb = mx_inputs(m, n, k, "e4m3", seed=12)
+    c0 = np.random.default_rng(13).standard_normal((m, n)).astype(np.float32)
+    c = torch.from_numpy(c0).to(cuda)
+    two = torch.tensor([2.0], device=cuda)
+    half = torch.tensor([0.25], device=cuda)
+    got = run_mx(qa, sa, qb, sb, "e4m3", "f32", cuda, c=c, scale_a=two, scale_b=half, accumulate=True)
+    check_mx(got, qa, sa, qb, sb, "e4m3", c0=c0, scale=0.5)
+
+
+def test_mx_limits(cuda):
+    a = torch.zeros(256, 128, dtype=torch.float8_e4m3fn, device=cuda)
+    c = torch.zeros(256, 256, dtype=torch.bfloat16, device=cuda)
+    s = torch.full((kl.mx_scale_bytes(256, 128),), 127, dtype=torch.uint8, device=cuda)
+    with pytest.raises(kl.KlError) as e:
+        kl.gemm(a, a, c, sfa=s, sfb=s, algo=kl.ALGO_SKINNY)
+    assert e.value.status == kl.KL_ERR_NOT_SUPPORTED
+    with pytest.raises(kl.KlError) as e:
+        kl.gemm(a, a, c, sfa=s, algo=kl.ALGO_1CTA)  # no scales for B
+    assert e.value.status == kl.KL_ERR_INVALID_ARGUMENT
+    ab = torch.zeros(256, 128, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(kl.KlError) as e:
+        kl.gemm(ab, ab, c, sfa=s, sfb=s)
+    assert e.value.status == kl.KL_ERR_NOT_SUPPORTED

@@ -122,3 +122,36 @@ def test_gemm_f64_other_formats(dtype):
 def test_kind_must_match_the_bits():
     with pytest.raises(TypeError):
         og.decode(np.zeros(4, np.uint8), "f16")
+
+
+def test_mx_quantise_and_oracle():
+    """MX quantisation keeps every block within the element format, and the MX oracle equals the
+    plain fp64 product of the dequantised inputs."""
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((40, 200)).astype(np.float32) * np.float32(7.0)
+    for kind, fmax in (("e4m3", 448.0), ("e5m2", 57344.0)):
+        q, s = wl.mx_quantize(x, kind)
+        assert s.shape == (40, 7)
+        deq = og.decode(q, kind) * np.repeat(og.e8m0_values(s), 32, axis=1)[:, :200]
+        assert np.abs(og.decode(q, kind)).max() <= fmax
+        rel = np.abs(deq - x).max() / np.abs(x).max()
+        assert rel < (2.0 ** -3 if kind == "e4m3" else 2.0 ** -2)
+    qa, sa = wl.mx_quantize(x[:13], "e4m3")
+    qb, sb = wl.mx_quantize(x[13:], "e4m3")
+    da = og.decode(qa, "e4m3") * np.repeat(og.e8m0_values(sa), 32, axis=1)[:, :200]
+    db = og.decode(qb, "e4m3") * np.repeat(og.e8m0_values(sb), 32, axis=1)[:, :200]
+    np.testing.assert_allclose(og.gemm_mx_f64(qa, qb, sa, sb, "e4m3", 3.0), 3.0 * da @ db.T, rtol=1e-13)
+
+
+def test_pack_mx_scales_layout():
+    sf = np.arange(300 * 9, dtype=np.int64).reshape(300, 9).astype(np.uint8)
+    k = 9 * 32 - 5
+    pk = og.pack_mx_scales(sf, k)
+    kb = -(-k // 128)
+    assert pk.size == 3 * kb * 512
+    for r in (0, 31, 32, 127, 128, 200, 299):
+        for j in range(9):
+            rb, rr = divmod(r, 128)
+            kk, jj = divmod(j, 4)
+            assert pk[(rb * kb + kk) * 512 + (rr % 32) * 16 + (rr // 32) * 4 + jj] == sf[r, j]
+    assert pk[(2 * kb + 2) * 512 + 1 * 16 + 3 * 4 + 1] == 127  # row 2*128+97 >= 300: padding
