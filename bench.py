@@ -107,7 +107,10 @@ def cpu_baseline(w, budget_s: float = 6.0):
     while True:
         a, b, sa, sb = wl.make_inputs(w, rows_a=rows)
         t0 = time.perf_counter()
-        og.gemm_f32(a, b, sa * sb, threads=threads)
+        if w.dtype == "mxfp8":
+            og.gemm_mx_f32(a, b, sa, sb, "e4m3", threads=threads)
+        else:
+            og.gemm_f32(a, b, sa * sb, threads=threads)
         dt = time.perf_counter() - t0
         if dt >= budget_s / 3 or rows >= w.m:
             break
@@ -184,6 +187,9 @@ def main():
     a_bits, b_bits, sa, sb = wl.make_inputs(w)
     n_lo, n_hi = sharding.shard_range(w.n, world, rank, align=256)
     b_bits = np.ascontiguousarray(b_bits[n_lo:n_hi])
+    mx = w.dtype == "mxfp8"
+    if mx:
+        sb = np.ascontiguousarray(sb[n_lo:n_hi])
     nshard = n_hi - n_lo
     np_view = np.int16 if w.dtype == "bf16" else np.uint8
     tdt = torch.bfloat16 if w.dtype == "bf16" else torch.float8_e4m3fn
@@ -196,12 +202,19 @@ def main():
     c = torch.empty((w.m, nshard), dtype=odt, device=dev)
     c_host = torch.empty((w.m, nshard), dtype=odt).pin_memory()
     scale_a = scale_b = None
+    sfa = sfb = sfa_host = sfb_host = None
     if w.dtype == "e4m3":
         scale_a = torch.tensor([sa], dtype=torch.float32, device=dev)
         scale_b = torch.tensor([sb], dtype=torch.float32, device=dev)
+    if mx:
+        # MX block scales, repacked on the device into the blocked layout (untimed setup).
+        sfa = kl.mx_pack_scales(torch.from_numpy(sa).to(dev), w.k)
+        sfb = kl.mx_pack_scales(torch.from_numpy(sb).to(dev), w.k)
+        sfa_host = sfa.cpu().pin_memory()
+        sfb_host = sfb.cpu().pin_memory()
     stream = torch.cuda.current_stream(dev)
     kw = dict(scale_a=scale_a, scale_b=scale_b, algo=args.algo, group_m=args.group_m, prefetch=args.prefetch,
-              variant=args.variant)
+              variant=args.variant, sfa=sfa, sfb=sfb)
 
     def step():
         kl.gemm(a, b, c, **kw)
@@ -232,7 +245,8 @@ def main():
     if w.m > 256 and args.algo in (0, kl.ALGO_1CTA, kl.ALGO_2CTA):
         # One more launch, right after the timed ones, with every CTA stamping clock64 and
         # %globaltimer: the SM clock the kernel really ran at (NVML may report the boost target).
-        in_kernel = kl.clock_probe(a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo, group_m=args.group_m)
+        in_kernel = kl.clock_probe(a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo, group_m=args.group_m,
+                                   sfa=sfa, sfb=sfb)
     if kl.read_status() != 0:
         raise RuntimeError("a device-side wait timed out during the benchmark")
     dev_ms = max_over_ranks(dev_ms)
@@ -241,11 +255,14 @@ def main():
 
     # ---- end to end through the public API with host buffers
     h2d = a_host.numel() * a_host.element_size() + b_host.numel() * b_host.element_size()
+    if mx:
+        h2d += sfa_host.numel() + sfb_host.numel()
     d2h = c.numel() * c.element_size()
 
     def e2e_step():
         # The host-buffer entry point: copies in, GEMM and copy out, pipelined over column blocks.
-        kl.gemm_host(a_host, b_host, c_host, a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo)
+        kl.gemm_host(a_host, b_host, c_host, a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo,
+                     sfa=sfa_host, sfb=sfb_host)
 
     for _ in range(max(args.warmup, 3)):
         e2e_step()
@@ -285,7 +302,7 @@ def main():
         peers = shared.peer_ptrs(n_lo)
 
         def fused_step():
-            kl.gemm_gather(a, b, c_view, peers, scale_a=scale_a, scale_b=scale_b, algo=args.algo)
+            kl.gemm_gather(a, b, c_view, peers, scale_a=scale_a, scale_b=scale_b, algo=args.algo, sfa=sfa, sfb=sfb)
 
         for _ in range(max(args.warmup, 3)):
             fused_step()
@@ -307,7 +324,8 @@ def main():
     memory_bound = w.m <= 256
     if memory_bound:
         # Decode shapes: every operand byte moved once, against the measured copy bandwidth.
-        alg_bytes = (w.m * w.k + nshard * w.k) * w.in_bytes + w.m * nshard * w.out_bytes
+        alg_bytes = (w.m * w.k + nshard * w.k) * w.in_bytes + w.m * nshard * w.out_bytes + \
+            (w.m + nshard) * -(-w.k // 32) * (w.dtype == "mxfp8")
         roofline = {"bound": "hbm", "achieved": alg_bytes / (dev_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
                     "unit": "GB/s", "peak_source": f"{peak_src} hbm_gbs", "algorithmic_bytes_per_launch": alg_bytes}
     else:
@@ -315,7 +333,8 @@ def main():
         roofline = {"bound": "tensor", "achieved": per_rank_flops / (dev_ms * 1e-3) / 1e12, "peak": peak,
                     "unit": "TFLOP/s",
                     "peak_source": f"{peak_src} " + ("bf16_tflops (burst)" if w.dtype == "bf16" else
-                                                     "2 x bf16_tflops (burst; fp8 dense rate is twice bf16)"),
+                                                     "2 x bf16_tflops (burst; the fp8 and MXFP8 dense rate is "
+                                                     "twice bf16)"),
                     "algorithmic_flops_per_launch": per_rank_flops}
     roofline["frac"] = roofline["achieved"] / roofline["peak"]
     traffic = None

@@ -156,7 +156,10 @@ KL_API kl_status kl_gemm_ws(const kl_gemm_desc* desc, void* workspace, size_t wo
  * staging. The library copies A in, then streams B in `chunks` column blocks of C (0 = choose; a
  * block is a multiple of 256 columns) so that the copy in of block j+1, the GEMM of block j and
  * the copy back of block j-1 overlap. Ordered after the work already on `stream`; `stream` waits
- * for C to be on the host. The call only queues work: synchronise `stream` before reading C. */
+ * for C to be on the host. The call only queues work: synchronise `stream` before reading C.
+ * MXFP8 (block_scale = 1): desc->sfa / desc->sfb are HOST pointers to the blocked scale arrays;
+ * the library stages them in a device buffer of its own (one per device, grown on demand). K-major
+ * operands, C output only (c_reduce 0), one problem per call. */
 KL_API kl_status kl_gemm_host(const kl_gemm_desc* desc, void* dev_a, void* dev_b, void* dev_c, int32_t chunks,
                               void* stream);
 

@@ -283,13 +283,14 @@ def mx_pack_scales(scales, k: int, out=None, stream=None):
 
 
 def gemm_host(a_host, b_host, c_host, a_dev, b_dev, c_dev, *, alpha=1.0, scale_a=None, scale_b=None,
-              algo=ALGO_AUTO, chunks=0, stream=None):
+              algo=ALGO_AUTO, chunks=0, sfa=None, sfb=None, stream=None):
     """c_host = alpha * a_host @ b_host.T with host (ideally pinned) tensors, through kl_gemm_host:
     the copies in and out overlap the GEMM. a_dev/b_dev/c_dev are device staging tensors of the
-    same shapes. Returns c_host once the stream has been synchronised."""
+    same shapes; sfa/sfb: host MXFP8 scales in the blocked layout (staged by the library). Only
+    queues the work on the stream: synchronise it before reading c_host."""
     import torch
 
-    d = gemm_desc(a_host, b_host, c_host, alpha, scale_a, scale_b, algo)
+    d = gemm_desc(a_host, b_host, c_host, alpha, scale_a, scale_b, algo, sfa=sfa, sfb=sfb)
     s = stream if stream is not None else torch.cuda.current_stream(a_dev.device).cuda_stream
     check(lib().kl_gemm_host(ctypes.byref(d), ctypes.c_void_p(a_dev.data_ptr()), ctypes.c_void_p(b_dev.data_ptr()),
                              ctypes.c_void_p(c_dev.data_ptr()), int(chunks), ctypes.c_void_p(s)))
@@ -297,12 +298,12 @@ def gemm_host(a_host, b_host, c_host, a_dev, b_dev, c_dev, *, alpha=1.0, scale_a
 
 
 def gemm_gather(a, b, c_shard, peer_ptrs, *, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
-                group_m=0, stream=None):
+                group_m=0, sfa=None, sfb=None, stream=None):
     """c_shard = alpha * a @ b.T, and the same tiles written to each peer pointer (a view of the same
     columns in another GPU's copy of C, with c_shard's pitch), through kl_gemm_gather."""
     import torch
 
-    d = gemm_desc(a, b, c_shard, alpha, scale_a, scale_b, algo, group_m)
+    d = gemm_desc(a, b, c_shard, alpha, scale_a, scale_b, algo, group_m, sfa=sfa, sfb=sfb)
     arr = (ctypes.c_void_p * max(1, len(peer_ptrs)))(*[ctypes.c_void_p(p) for p in peer_ptrs])
     s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
     check(lib().kl_gemm_gather(ctypes.byref(d), arr, len(peer_ptrs), ctypes.c_void_p(s)))

@@ -2,7 +2,8 @@
 // device, then streams B in column blocks of C, so that the host-to-device copies of block j+1,
 // the GEMM of block j and the device-to-host copy of block j-1 run at the same time on three
 // streams (two copy engines and the SMs). Chained with events; ordered after and before the
-// caller's stream.
+// caller's stream. MXFP8 problems (block_scale = 1) also stage the blocked scale arrays: A's whole,
+// then B's row blocks along with each block of B.
 
 #include <cuda_runtime.h>
 
@@ -22,6 +23,8 @@ struct HostPipe {
   cudaStream_t in = nullptr, mm = nullptr, out = nullptr;
   cudaEvent_t start = nullptr, done = nullptr;
   std::vector<cudaEvent_t> loaded, computed;
+  void* scales = nullptr;  // device staging of MXFP8 scales, grown on demand
+  size_t scale_bytes = 0;
 };
 
 std::mutex g_pipe_mutex;
@@ -67,6 +70,9 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
   if (h->lda < h->k || h->ldb < h->k || h->ldc < h->n) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_host: leading dimension too small");
   if (h->batch > 1) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_host: one problem per call (batch must be 0 or 1)");
   if (h->c_reduce != 0) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_host: C is output only (c_reduce must be 0)");
+  const bool mx = h->block_scale != 0;
+  if (mx && (h->sfa == nullptr || h->sfb == nullptr))
+    return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_host: MXFP8 needs host scales of A and B (desc->sfa, desc->sfb)");
   if (h->a_major != 0 || h->b_major != 0)
     return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_host: K-major operands only (B is streamed by rows)");
   cudaStream_t caller = static_cast<cudaStream_t>(stream_ptr);
@@ -89,6 +95,23 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
   if (s != KL_OK) return s;
 
   const int eab = elem_bytes(h->ab_type), ec = elem_bytes(h->c_type);
+  // MXFP8 scales: blocked arrays, A's then B's, in one staging buffer.
+  const int64_t sfa_bytes = mx ? kl_mx_scale_bytes(h->m, h->k) : 0;
+  const int64_t sfb_bytes = mx ? kl_mx_scale_bytes(h->n, h->k) : 0;
+  const int64_t sf_row_block = ((h->k + 127) / 128) * 512;  // bytes per 128 rows
+  if (mx && p->scale_bytes < size_t(sfa_bytes + sfb_bytes)) {
+    if (p->scales != nullptr) {
+      if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+      cudaFree(p->scales);
+      p->scales = nullptr;
+      p->scale_bytes = 0;
+    }
+    if ((e = cudaMalloc(&p->scales, size_t(sfa_bytes + sfb_bytes))) != cudaSuccess)
+      return cuda_fail(e, "kl_gemm_host: cudaMalloc(scale staging)");
+    p->scale_bytes = size_t(sfa_bytes + sfb_bytes);
+  }
+  char* dsfa = static_cast<char*>(p->scales);
+  char* dsfb = dsfa + sfa_bytes;
   const char* ha = static_cast<const char*>(h->a);
   const char* hb = static_cast<const char*>(h->b);
   char* hc = static_cast<char*>(h->c);
@@ -101,11 +124,20 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
   if ((e = cudaStreamWaitEvent(p->in, p->start, 0)) != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
   if ((e = cudaMemcpyAsync(da, ha, size_t(h->m) * h->lda * eab, cudaMemcpyHostToDevice, p->in)) != cudaSuccess)
     return cuda_fail(e, "kl_gemm_host: copy of A");
+  if (mx && (e = cudaMemcpyAsync(dsfa, h->sfa, size_t(sfa_bytes), cudaMemcpyHostToDevice, p->in)) != cudaSuccess)
+    return cuda_fail(e, "kl_gemm_host: copy of A's scales");
   for (int j = 0; j < chunks; ++j) {
     const int64_t n0 = int64_t(j) * block, nj = std::min<int64_t>(block, h->n - n0);
     e = cudaMemcpyAsync(db + size_t(n0) * h->ldb * eab, hb + size_t(n0) * h->ldb * eab, size_t(nj) * h->ldb * eab,
                         cudaMemcpyHostToDevice, p->in);
     if (e != cudaSuccess) return cuda_fail(e, "kl_gemm_host: copy of B");
+    // Block j starts on a 256-row boundary of B, so its scales are whole 128-row blocks.
+    const int64_t sf_off = (n0 / 128) * sf_row_block, sf_len = ((nj + 127) / 128) * sf_row_block;
+    if (mx) {
+      e = cudaMemcpyAsync(dsfb + sf_off, static_cast<const char*>(h->sfb) + sf_off, size_t(sf_len),
+                          cudaMemcpyHostToDevice, p->in);
+      if (e != cudaSuccess) return cuda_fail(e, "kl_gemm_host: copy of B's scales");
+    }
     if ((e = cudaEventRecord(p->loaded[j], p->in)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
     if ((e = cudaStreamWaitEvent(p->mm, p->loaded[j], 0)) != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
     kl_gemm_desc d = *h;
@@ -113,6 +145,10 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
     d.a = da;
     d.b = db + size_t(n0) * h->ldb * eab;
     d.c = dc + size_t(n0) * ec;
+    if (mx) {
+      d.sfa = dsfa;
+      d.sfb = dsfb + sf_off;
+    }
     s = kl_gemm(&d, p->mm);
     if (s != KL_OK) return s;
     if ((e = cudaEventRecord(p->computed[j], p->mm)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord");

@@ -24,11 +24,15 @@ using Mx128 = TnConfig<InT, OutT, 1, 128, 5, false, false, false, kl::Swizzle128
 // CTA pair, 256 x 256 tiles: one accumulator per CTA, 5 stages of 33.5 KB per CTA.
 template <typename InT, typename OutT>
 using MxPair = TnConfig<InT, OutT, 2, 256, 5, false, false, false, kl::Swizzle128B, true>;
+// CTA pair, 256 x 128 tiles: two accumulators, 7 stages of 25 KB per CTA.
+template <typename InT, typename OutT>
+using MxPair128 = TnConfig<InT, OutT, 2, 128, 7, false, false, false, kl::Swizzle128B, true>;
 
 template <typename InT, typename OutT>
 kl_status run_mx(int32_t variant, bool pair, kl::gemm::Problem const& pr, cudaStream_t stream,
                  kl::gemm::LaunchInfo* info) {
-  if (pair) return run_cfg<MxPair<InT, OutT>>(pr, stream, info);
+  if (pair)
+    return variant == 2 ? run_cfg<MxPair128<InT, OutT>>(pr, stream, info) : run_cfg<MxPair<InT, OutT>>(pr, stream, info);
   return variant == 2 ? run_cfg<Mx128<InT, OutT>>(pr, stream, info) : run_cfg<Mx256<InT, OutT>>(pr, stream, info);
 }
 

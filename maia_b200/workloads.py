@@ -3,7 +3,8 @@
 Each tensor comes from its own numpy PCG64 stream seeded ``seed * 1000 + tensor_id`` (A = 0,
 B = 1), drawn in row-major order as float32, then rounded to the input type:
   * bf16: round-to-nearest-even of the float32 value;
-  * e4m3: per-tensor scale = amax / 448, q = RNE(x / scale) (|x / scale| <= 448, so no overflow).
+  * e4m3: per-tensor scale = amax / 448, q = RNE(x / scale) (|x / scale| <= 448, so no overflow);
+  * mxfp8: MX quantisation to e4m3 with a UE8M0 scale per 32 K-elements (mx_quantize).
 Inputs are returned as raw bits (uint16 / uint8 numpy arrays) so that the GPU and the CPU oracle
 see byte-identical operands.
 """
@@ -21,7 +22,7 @@ class Workload:
     m: int
     n: int
     k: int
-    dtype: str          # "bf16" or "e4m3"
+    dtype: str          # "bf16", "e4m3" or "mxfp8" (e4m3 elements with MX block scales)
     out: str            # "bf16" or "f32"
     dist: str           # "uniform" (on [-1, 1]) or "normal"
     a_scale: float      # multiplier of A's standard normal (normal) draws
@@ -37,13 +38,18 @@ class Workload:
         return 2 if self.dtype == "bf16" else 1
 
     @property
+    def scale_bytes(self) -> int:
+        """MX block scales: one byte per 32 K-elements of every row of A and B."""
+        return (self.m + self.n) * -(-self.k // 32) if self.dtype == "mxfp8" else 0
+
+    @property
     def out_bytes(self) -> int:
         return 2 if self.out == "bf16" else 4
 
     @property
     def bytes(self) -> int:
         """Algorithmic bytes: every matrix moved once."""
-        return (self.m * self.k + self.n * self.k) * self.in_bytes + self.m * self.n * self.out_bytes
+        return (self.m * self.k + self.n * self.k) * self.in_bytes + self.m * self.n * self.out_bytes + self.scale_bytes
 
 
 # C1..C5: the reference's GEMM contract at its benchmark shapes.
@@ -52,8 +58,11 @@ C2 = Workload("c2_4096_bf16", 4096, 4096, 4096, "bf16", "bf16", "normal", 0.05, 
 C3 = Workload("c3_8192_bf16", 8192, 8192, 8192, "bf16", "bf16", "normal", 0.02, 0.02, 2)
 C4 = Workload("c4_16384x16384x8192_e4m3", 16384, 16384, 8192, "e4m3", "bf16", "normal", 1.0, 1.0, 3)
 C5 = {m: Workload(f"c5_skinny_m{m}", m, 28672, 8192, "bf16", "bf16", "normal", 1.0, 0.02, 4) for m in (16, 64, 128)}
+# C4's shape and draws, MX-quantised instead of per-tensor scaled (block-scaled fp8); and C3's.
+C4MX = Workload("c4mx_16384x16384x8192_mxfp8", 16384, 16384, 8192, "mxfp8", "bf16", "normal", 1.0, 1.0, 3)
+C3MX = Workload("c3mx_8192_mxfp8", 8192, 8192, 8192, "mxfp8", "bf16", "normal", 0.02, 0.02, 2)
 
-ALL = {w.name: w for w in (C1, C2, C3, C4, *C5.values())}
+ALL = {w.name: w for w in (C1, C2, C3, C4, C4MX, C3MX, *C5.values())}
 
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
@@ -200,12 +209,17 @@ def draw(w: Workload, tensor_id: int, rows: int, cols: int, scale: float) -> np.
 
 
 def make_inputs(w: Workload, rows_a: int | None = None):
-    """(A bits, B bits, scale_a, scale_b). rows_a limits A to its first rows (a bounded CPU sample)."""
+    """(A bits, B bits, scale_a, scale_b). rows_a limits A to its first rows (a bounded CPU sample).
+    For mxfp8 the scales are the row-major UE8M0 arrays [rows, ceil(K/32)] of A and B."""
     ra = w.m if rows_a is None else min(rows_a, w.m)
     xa = draw(w, 0, w.m, w.k, w.a_scale)[:ra] if rows_a is not None else draw(w, 0, w.m, w.k, w.a_scale)
     xb = draw(w, 1, w.n, w.k, w.b_scale)
     if w.dtype == "bf16":
         return f32_to_bf16_bits(xa), f32_to_bf16_bits(xb), 1.0, 1.0
+    if w.dtype == "mxfp8":
+        qa, sfa = mx_quantize(xa, "e4m3")
+        qb, sfb = mx_quantize(xb, "e4m3")
+        return qa, qb, sfa, sfb
     # fp8: per-tensor scales from the full tensors' amax.
     sa = float(np.abs(draw(w, 0, w.m, w.k, w.a_scale)).max()) / 448.0 if rows_a is not None else float(np.abs(xa).max()) / 448.0
     sb = float(np.abs(xb).max()) / 448.0

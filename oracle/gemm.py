@@ -40,6 +40,11 @@ def lib():
         L.kl_oracle_gemm_f32.restype = i32
         L.kl_oracle_decode.argtypes = [i32, vp, i64, vp]
         L.kl_oracle_decode.restype = None
+        mx = [i32, vp, i64, vp, i64, i64, i64, i64, vp, i64, vp, i64, dbl, vp, i64, i32]
+        L.kl_oracle_gemm_mx_f64.argtypes = mx
+        L.kl_oracle_gemm_mx_f64.restype = i32
+        L.kl_oracle_gemm_mx_f32.argtypes = mx
+        L.kl_oracle_gemm_mx_f32.restype = i32
         _lib = L
     return _lib
 
@@ -103,16 +108,33 @@ def e8m0_values(s: np.ndarray) -> np.ndarray:
     return np.where(s == 255, np.nan, np.exp2(s - 127.0))
 
 
+def _mx_call(fn, out_dtype, a, b, sfa, sfb, kind, scale, threads):
+    a, b = np.ascontiguousarray(a), np.ascontiguousarray(b)
+    sfa, sfb = np.ascontiguousarray(sfa, dtype=np.uint8), np.ascontiguousarray(sfb, dtype=np.uint8)
+    m, k = a.shape
+    n = b.shape[0]
+    groups = -(-k // 32)
+    assert sfa.shape == (m, groups) and sfb.shape == (n, groups) and b.shape[1] == k
+    c = np.empty((m, n), dtype=out_dtype)
+    rc = fn(_kind(a, kind), a.ctypes.data, k, b.ctypes.data, k, m, n, k, sfa.ctypes.data, groups, sfb.ctypes.data,
+            groups, float(scale), c.ctypes.data, n, threads or threads_default())
+    assert rc == 0
+    return c
+
+
 def gemm_mx_f64(a: np.ndarray, b: np.ndarray, sfa: np.ndarray, sfb: np.ndarray, kind=None,
-                scale: float = 1.0) -> np.ndarray:
+                scale: float = 1.0, threads: int | None = None) -> np.ndarray:
     """MX block-scaled product in fp64: scale * sum_k (A[m,k] sfa[m, k/32]) (B[n,k] sfb[n, k/32]).
 
     a, b: raw 8-bit element bits [M,K] / [N,K]; sfa, sfb: UE8M0 bits [M, ceil(K/32)] /
     [N, ceil(K/32)], one scale per 32 consecutive K-elements (the OCP MX block size)."""
-    k = a.shape[1]
-    da = decode(a, kind) * np.repeat(e8m0_values(sfa), 32, axis=1)[:, :k]
-    db = decode(b, kind) * np.repeat(e8m0_values(sfb), 32, axis=1)[:, :k]
-    return (da @ db.T) * scale
+    return _mx_call(lib().kl_oracle_gemm_mx_f64, np.float64, a, b, sfa, sfb, kind, scale, threads)
+
+
+def gemm_mx_f32(a: np.ndarray, b: np.ndarray, sfa: np.ndarray, sfb: np.ndarray, kind=None,
+                scale: float = 1.0, threads: int | None = None) -> np.ndarray:
+    """The same with fp32 accumulation (the timed CPU baseline of the MX workload)."""
+    return _mx_call(lib().kl_oracle_gemm_mx_f32, np.float32, a, b, sfa, sfb, kind, scale, threads)
 
 
 def pack_mx_scales(sf: np.ndarray, k: int) -> np.ndarray:

@@ -16,6 +16,9 @@
  *                        baseline (the "CPU reference GEMM" of the benchmark's smallest config).
  *   kl_oracle_decode     element decoders (bf16, f16, e4m3, e5m2), exposed so tests can check
  *                        them.
+ *   kl_oracle_gemm_mx_f64 / _f32   the same with MX block scaling (OCP Microscaling Formats v1.0):
+ *                        element k of row r of A is multiplied by 2^(sfa[r][k/32] - 127) (UE8M0,
+ *                        one scale per 32 consecutive K-elements; 255 is NaN), likewise for B.
  *
  * Element decoding follows the formats' definitions: bf16 is the top half of an IEEE binary32;
  * f16 is IEEE binary16 (1 sign, 5 exponent bits with bias 15, 10 mantissa bits); e4m3 (OCP FP8,
@@ -103,15 +106,26 @@ typedef struct {
   int64_t row_begin, row_end;
   const double* bdec; /* decoded B, n x k (f64 path) */
   const float* bdecf; /* decoded B, n x k (f32 path) */
+  const uint8_t* sfa; /* optional MX scales of A, row-major [m][ldsfa] */
+  int64_t ldsfa;
 } job_t;
+
+static double e8m0(uint8_t s) { return s == 255 ? NAN : ldexp(1.0, (int)s - 127); }
+
+/* Decode row `r` of a matrix (k elements) and apply its MX scales when `sf` is given. */
+static void decode_row(int t, const void* base, int64_t ld, int64_t r, int64_t k, const uint8_t* sf, int64_t ldsf,
+                       double* out) {
+  kl_oracle_decode(t, (const char*)base + (size_t)(r * ld) * elem_size(t), k, out);
+  if (sf)
+    for (int64_t kk = 0; kk < k; ++kk) out[kk] *= e8m0(sf[r * ldsf + kk / 32]);
+}
 
 static void* f64_rows(void* arg) {
   job_t* j = (job_t*)arg;
   double* arow = (double*)malloc(sizeof(double) * (size_t)j->k);
   double* c = (double*)j->c;
-  const int esz = elem_size(j->t);
   for (int64_t i = j->row_begin; i < j->row_end; ++i) {
-    kl_oracle_decode(j->t, (const char*)j->a + (size_t)(i * j->lda) * esz, j->k, arow);
+    decode_row(j->t, j->a, j->lda, i, j->k, j->sfa, j->ldsfa, arow);
     for (int64_t col = 0; col < j->n; ++col) {
       const double* brow = j->bdec + (size_t)col * (size_t)j->k;
       double s0 = 0, s1 = 0, s2 = 0, s3 = 0;
@@ -137,18 +151,20 @@ static int clamp_threads(int threads, int64_t rows) {
   return threads;
 }
 
-/* c[i*ldc + j] = scale * sum_k A[i,k] * B[j,k] in double, for rows [0, m). Returns 0 on success. */
-int kl_oracle_gemm_f64(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
-                       int64_t k, double scale, double* c, int64_t ldc, int threads) {
-  const int esz = elem_size(t);
+/* c[i*ldc + j] = scale * sum_k A[i,k] * B[j,k] in double, for rows [0, m); with sfa / sfb (MX
+ * scales, row-major, row pitch ldsfa / ldsfb) each element is scaled first. Returns 0 on success. */
+int kl_oracle_gemm_mx_f64(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                          int64_t k, const uint8_t* sfa, int64_t ldsfa, const uint8_t* sfb, int64_t ldsfb,
+                          double scale, double* c, int64_t ldc, int threads) {
   double* bdec = (double*)malloc(sizeof(double) * (size_t)n * (size_t)(k > 0 ? k : 1));
   if (!bdec) return 1;
-  for (int64_t r = 0; r < n; ++r) kl_oracle_decode(t, (const char*)b + (size_t)(r * ldb) * esz, k, bdec + r * k);
+  for (int64_t r = 0; r < n; ++r) decode_row(t, b, ldb, r, k, sfb, ldsfb, bdec + r * k);
   threads = clamp_threads(threads, m);
   pthread_t tid[512];
   job_t jobs[512];
   for (int w = 0; w < threads; ++w) {
-    job_t j = {t, a, lda, b, ldb, m, n, k, scale, c, ldc, m * w / threads, m * (w + 1) / threads, bdec, NULL};
+    job_t j = {t, a, lda, b, ldb, m, n, k, scale, c, ldc, m * w / threads, m * (w + 1) / threads, bdec, NULL,
+               sfa, ldsfa};
     jobs[w] = j;
     pthread_create(&tid[w], NULL, f64_rows, &jobs[w]);
   }
@@ -157,12 +173,16 @@ int kl_oracle_gemm_f64(int t, const void* a, int64_t lda, const void* b, int64_t
   return 0;
 }
 
+int kl_oracle_gemm_f64(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                       int64_t k, double scale, double* c, int64_t ldc, int threads) {
+  return kl_oracle_gemm_mx_f64(t, a, lda, b, ldb, m, n, k, NULL, 0, NULL, 0, scale, c, ldc, threads);
+}
+
 /* fp32-accumulate baseline. Blocks of 4 rows of A against 4 rows of B, K in chunks that stay in
  * L1/L2, 8 independent fp32 partial sums per dot so the compiler can vectorise. */
 #define KB 512
 static void* f32_rows(void* arg) {
   job_t* j = (job_t*)arg;
-  const int esz = elem_size(j->t);
   const int64_t k = j->k;
   float* c = (float*)j->c;
   float* ablk = (float*)malloc(sizeof(float) * 4 * (size_t)k);
@@ -170,7 +190,7 @@ static void* f32_rows(void* arg) {
   for (int64_t i0 = j->row_begin; i0 < j->row_end; i0 += 4) {
     const int64_t ni = (j->row_end - i0) < 4 ? (j->row_end - i0) : 4;
     for (int64_t r = 0; r < ni; ++r) {
-      kl_oracle_decode(j->t, (const char*)j->a + (size_t)((i0 + r) * j->lda) * esz, k, tmp);
+      decode_row(j->t, j->a, j->lda, i0 + r, k, j->sfa, j->ldsfa, tmp);
       for (int64_t kk = 0; kk < k; ++kk) ablk[r * k + kk] = (float)tmp[kk];
     }
     for (int64_t r = ni; r < 4; ++r) memset(ablk + r * k, 0, sizeof(float) * (size_t)k);
@@ -195,14 +215,14 @@ static void* f32_rows(void* arg) {
   return NULL;
 }
 
-int kl_oracle_gemm_f32(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
-                       int64_t k, double scale, float* c, int64_t ldc, int threads) {
-  const int esz = elem_size(t);
+int kl_oracle_gemm_mx_f32(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                          int64_t k, const uint8_t* sfa, int64_t ldsfa, const uint8_t* sfb, int64_t ldsfb,
+                          double scale, float* c, int64_t ldc, int threads) {
   float* bdec = (float*)malloc(sizeof(float) * (size_t)n * (size_t)(k > 0 ? k : 1));
   double* tmp = (double*)malloc(sizeof(double) * (size_t)(k > 0 ? k : 1));
   if (!bdec || !tmp) return 1;
   for (int64_t r = 0; r < n; ++r) {
-    kl_oracle_decode(t, (const char*)b + (size_t)(r * ldb) * esz, k, tmp);
+    decode_row(t, b, ldb, r, k, sfb, ldsfb, tmp);
     for (int64_t kk = 0; kk < k; ++kk) bdec[r * k + kk] = (float)tmp[kk];
   }
   free(tmp);
@@ -214,11 +234,16 @@ int kl_oracle_gemm_f32(int t, const void* a, int64_t lda, const void* b, int64_t
     int64_t b0 = ((m + 3) / 4) * w / threads * 4, b1 = ((m + 3) / 4) * (w + 1) / threads * 4;
     if (b1 > m) b1 = m;
     if (b0 > m) b0 = m;
-    job_t j = {t, a, lda, b, ldb, m, n, k, scale, c, ldc, b0, b1, NULL, bdec};
+    job_t j = {t, a, lda, b, ldb, m, n, k, scale, c, ldc, b0, b1, NULL, bdec, sfa, ldsfa};
     jobs[w] = j;
     pthread_create(&tid[w], NULL, f32_rows, &jobs[w]);
   }
   for (int w = 0; w < threads; ++w) pthread_join(tid[w], NULL);
   free(bdec);
   return 0;
+}
+
+int kl_oracle_gemm_f32(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                       int64_t k, double scale, float* c, int64_t ldc, int threads) {
+  return kl_oracle_gemm_mx_f32(t, a, lda, b, ldb, m, n, k, NULL, 0, NULL, 0, scale, c, ldc, threads);
 }

@@ -38,3 +38,29 @@ def test_host_pipeline_matches_device_gemm(cuda, m, n, k, chunks, pinned):
         check(c_host.float().numpy(), a_bits, b_bits, 1.0, 1e-2)
         if m > 128:
             assert torch.equal(c_host.view(torch.int16), ref.cpu().view(torch.int16))
+
+
+@pytest.mark.parametrize("m, n, k, chunks", [(512, 4096, 1024, 0), (256, 3000, 640, 3), (1000, 1024, 512, 1)])
+def test_host_pipeline_mxfp8(cuda, m, n, k, chunks):
+    """MXFP8 through the host-buffer path: the blocked scales travel with their column blocks of B."""
+    from maia_b200 import workloads as wl
+    from oracle import gemm as og
+
+    rng = np.random.default_rng(m + n)
+    qa, sfa = wl.mx_quantize(rng.standard_normal((m, k)).astype(np.float32))
+    qb, sfb = wl.mx_quantize(rng.standard_normal((n, k)).astype(np.float32))
+    a_dev, b_dev = to_device(qa, "e4m3", cuda), to_device(qb, "e4m3", cuda)
+    psa = kl.mx_pack_scales(torch.from_numpy(sfa).to(cuda), k)
+    psb = kl.mx_pack_scales(torch.from_numpy(sfb).to(cuda), k)
+    ref = kl.gemm(a_dev, b_dev, sfa=psa, sfb=psb)
+    c_host = torch.full((m, n), float("nan"), dtype=torch.bfloat16).pin_memory()
+    kl.gemm_host(a_dev.cpu().pin_memory(), b_dev.cpu().pin_memory(), c_host, torch.empty_like(a_dev),
+                 torch.empty_like(b_dev), torch.empty((m, n), dtype=torch.bfloat16, device=cuda), chunks=chunks,
+                 sfa=psa.cpu().pin_memory(), sfb=psb.cpu().pin_memory())
+    torch.cuda.current_stream().synchronize()
+    assert kl.read_status() == 0
+    got = c_host.float().numpy()
+    want = og.gemm_mx_f64(qa, qb, sfa, sfb, "e4m3")
+    elem, norm = og.rel_error(got, want)
+    assert elem <= 5e-2 and norm <= 5e-2
+    assert torch.equal(c_host.view(torch.int16), ref.cpu().view(torch.int16))

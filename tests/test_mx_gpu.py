@@ -73,8 +73,9 @@ def test_pack_scales_strided_source(cuda):
     np.testing.assert_array_equal(got, og.pack_mx_scales(sf[:, :32], 1024))
 
 
-KERNELS = pytest.mark.parametrize("algo,variant", [(kl.ALGO_1CTA, 0), (kl.ALGO_1CTA, 2), (kl.ALGO_2CTA, 0)],
-                                  ids=["1cta_n256", "1cta_n128", "2cta"])
+KERNELS = pytest.mark.parametrize("algo,variant", [(kl.ALGO_1CTA, 0), (kl.ALGO_1CTA, 2), (kl.ALGO_2CTA, 0),
+                                                   (kl.ALGO_2CTA, 2)],
+                                  ids=["1cta_n256", "1cta_n128", "2cta_n256", "2cta_n128"])
 
 
 @KERNELS
