@@ -154,6 +154,7 @@ def main():
     ap.add_argument("--group-m", type=int, default=0)
     ap.add_argument("--prefetch", type=int, default=0, help="L2 prefetch distance (0 = library default, -1 = off)")
     ap.add_argument("--variant", type=int, default=0, help="kl_gemm_desc.variant (0 = library default)")
+    ap.add_argument("--max-ctas", type=int, default=0, help="cap on resident CTAs (0 = library default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
 
@@ -214,7 +215,7 @@ def main():
         sfb_host = sfb.cpu().pin_memory()
     stream = torch.cuda.current_stream(dev)
     kw = dict(scale_a=scale_a, scale_b=scale_b, algo=args.algo, group_m=args.group_m, prefetch=args.prefetch,
-              variant=args.variant, sfa=sfa, sfb=sfb)
+              variant=args.variant, max_ctas=args.max_ctas, sfa=sfa, sfb=sfb)
 
     def step():
         kl.gemm(a, b, c, **kw)
@@ -352,7 +353,7 @@ def main():
             "config": {"workload": w.name, "m": w.m, "n": w.n, "k": w.k, "out": w.out,
                        "parallelism": f"N-sharded x{world}", "output": "C[:, shard] per rank (no gather)",
                        "l2": "operands exceed L2 (no flush)", "algo": args.algo, "group_m": args.group_m,
-                       "prefetch": args.prefetch, "variant": args.variant},
+                       "prefetch": args.prefetch, "variant": args.variant, "max_ctas": args.max_ctas},
             "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "roofline": roofline,
