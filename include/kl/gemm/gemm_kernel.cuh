@@ -4,11 +4,11 @@
 // (both operands K-major, C row-major). No counterpart in the reference: kernel_lib ships the
 // descriptor encoders (tma_desc.hpp, umma_desc.hpp) this kernel is built from, but no kernel.
 //
-// Roles (192 threads, one CTA per SM):
+// Roles (192 threads, or 320 with eight epilogue warps; one CTA per SM):
 //   warp 0      TMA producer: fills a Stages-deep ring of (A, B) K-blocks in shared memory.
 //   warp 1      MMA issuer: one thread issues tcgen05.mma into a TMEM accumulator and commits
 //               each consumed stage back to the producer; warp 1 also owns the TMEM allocation.
-//   warps 2..5  epilogue: tcgen05.ld -> scale -> convert -> swizzled shared staging -> TMA store.
+//   warps 2..   epilogue: tcgen05.ld -> scale -> convert -> swizzled shared staging -> TMA store.
 // Two TMEM accumulators (2 x BlockN fp32 columns) let the epilogue of tile i overlap the main
 // loop of tile i + 1. Tiles are walked persistently in groups of `group_m` tile-rows so that the
 // CTAs running at the same time share A and B tiles in L2.
@@ -53,7 +53,6 @@ struct TnConfig {
   // true: the epilogue writes C straight from registers (16-byte vector stores per row) and the
   // shared memory that would stage TMA stores goes to the operand ring instead.
   static constexpr bool kDirectStore = DirectStore;
-  static constexpr int kThreads = 192;
   static constexpr int kCtaM = 128;                    // rows of A (= TMEM lanes) per CTA
   static constexpr int kTileM = kCtaM * CtaGroup;      // rows of C per tile
   static constexpr int kTileN = BlockN;                // columns of C per tile (UMMA N)
@@ -80,8 +79,17 @@ struct TnConfig {
   static constexpr int kTmemUsed = kAccCols * kNumAcc + (Mx ? 4 + 4 * kSfbAtoms : 0);
   static constexpr int kTmemCols = (kTmemUsed <= 32) ? 32 : (kTmemUsed <= 64) ? 64
                                  : (kTmemUsed <= 128) ? 128 : (kTmemUsed <= 256) ? 256 : 512;
+  // Epilogue warps. With two accumulators, 4 warps (one per TMEM lane quarter) drain a tile while
+  // the MMAs fill the other. With one, the MMAs wait for the drain, so 8 warps (two per quarter,
+  // each half of the columns) first load all their columns into registers, hand the accumulator
+  // back, and only then convert and store.
+  static constexpr int kEpiWarps = kNumAcc == 1 ? 8 : 4;
+  static constexpr bool kEarlyRelease = kNumAcc == 1;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kWarpCols = BlockN / (kEpiWarps / 4);  // accumulator columns per epilogue warp
   static constexpr int kChunkCols = 128 / int(sizeof(OutT));  // epilogue store box width (128 B)
-  static constexpr int kChunks = BlockN / kChunkCols;
+  static constexpr int kChunks = kWarpCols / kChunkCols;       // chunks per epilogue warp and tile
+  static constexpr int kStageBufs = kEpiWarps == 4 ? 2 : 1;    // C staging buffers per epilogue warp
 
   // Operand majors. K-major (the default): the operand is stored [rows, K] and its smem tile is
   // rows x K. MN-major: stored [K, rows] (A^T / B^T in memory), smem tile K x rows, MN contiguous,
@@ -102,7 +110,7 @@ struct TnConfig {
   static constexpr uint32_t kOffA = 0;
   static constexpr uint32_t kOffB = kOffA + kStages * kABytes;
   static constexpr uint32_t kOffC = kOffB + kStages * kBBytes;
-  static constexpr uint32_t kOffSf = kOffC + (DirectStore ? 0u : 8u * kCBytes);  // 4 epilogue warps x 2 buffers
+  static constexpr uint32_t kOffSf = kOffC + (DirectStore ? 0u : uint32_t(kEpiWarps * kStageBufs) * kCBytes);
   static constexpr uint32_t kOffSfb = kOffSf + kStages * kSfaBytes;
   static constexpr uint32_t kOffBar = kOffSfb + kStages * kSfbBytes;
   static constexpr uint32_t kNumBars = 2 * kStages + 2 * kNumAcc + 1;
@@ -125,7 +133,8 @@ struct TnConfig {
   static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
   static_assert(BlockN % (16 * CtaGroup) == 0 && BlockN <= 256, "UMMA N");
   static_assert(kCtaN % 8 == 0 && kCtaN <= 256, "B tile rows");
-  static_assert(BlockN % kChunkCols == 0, "epilogue chunking");
+  static_assert(kWarpCols % kChunkCols == 0, "epilogue chunking");
+  static_assert(!(kEarlyRelease && DirectStore), "the early-release epilogue stages through shared memory");
   static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "stages must keep 1 KB alignment");
   static_assert(std::is_same_v<Sw, Swizzle128B> || (!AMn && !BMn), "MN-major operands use 128-byte swizzle");
   static_assert(!std::is_same_v<Sw, SwizzleNone>, "operand tiles are swizzled");
@@ -315,7 +324,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
     }
     for (int a = 0; a < Cfg::kNumAcc; ++a) {
       mbarrier_init(tfull_bar(a), 1);
-      mbarrier_init(tempty_bar(a), 4 * CG);  // one arrival per epilogue warp of the pair
+      mbarrier_init(tempty_bar(a), Cfg::kEpiWarps * CG);  // one arrival per epilogue warp of the pair
     }
     mbarrier_init(drain_bar, 1);
     fence_barrier_init();
@@ -494,85 +503,53 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
       if (!mbarrier_wait(drain_bar, 0, args.timeout_ns)) record_status(args.status, kStatusDrainTimeout);
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    // ---------------------------------------------------------------- epilogue (warps 2..)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int ew = warp - 2;       // epilogue warp index -> staging buffers
+    const int wcol = (ew / 4) * Cfg::kWarpCols;  // this warp's first accumulator column
     const uint32_t lane_base = uint32_t(quarter * 32) << 16;
     float alpha = args.alpha;
     if (args.scale_a != nullptr) alpha *= *args.scale_a;
     if (args.scale_b != nullptr) alpha *= *args.scale_b;
     const uint32_t tempty_leader0 = (CG == 2) ? mapa_shared(tempty_bar(0), 0) : tempty_bar(0);
-    uint32_t iter = 0, nbuf = 0;
-    for (int t = worker; t < num_tiles; t += num_workers, ++iter) {
-      int bz, tm, tn;
-      tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, bz, tm, tn);
-      const uint32_t acc = iter % Cfg::kNumAcc;
-      const uint32_t acc_phase = (iter / Cfg::kNumAcc) & 1u;
-      if (!mbarrier_wait(tfull_bar(acc), acc_phase, args.timeout_ns)) {
-        if (lane == 0) record_status(args.status, kStatusEpilogueTimeout);
-        break;
-      }
-      tcgen05_fence_after();
-      const int row0 = tm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM + quarter * 32;
-      const int col0 = tn * Cfg::kTileN;
-#pragma unroll 1
-      for (int c = 0; c < Cfg::kChunks; ++c) {
-        uint32_t v[Cfg::kChunkCols];
-        const uint32_t taddr = tmem_base + lane_base + acc * Cfg::kAccCols + uint32_t(c * Cfg::kChunkCols);
-        if constexpr (Cfg::kChunkCols == 64) {
-          tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-          tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-        } else {
-          tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        }
-        tmem_wait_ld();
-        if (c == Cfg::kChunks - 1) {
-          // This warp is done with the accumulator: hand it back to the MMA issuer.
-          tcgen05_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            if constexpr (CG == 2)
-              mbarrier_arrive_cluster(tempty_leader0 + 8u * acc);
-            else
-              mbarrier_arrive(tempty_bar(acc));
-          }
-        }
-        const int col = col0 + c * Cfg::kChunkCols;
-        if constexpr (Cfg::kDirectStore) {
-          // Each thread owns one row of the chunk (128 bytes of C): eight 16-byte stores, or
-          // element by element on the ragged right edge.
-          const int row = row0 + lane;
-          if (row < args.m && col < args.n) {
-            OutT* dst = static_cast<OutT*>(args.c) + (long long)bz * args.batch_stride_c + (long long)row * args.ldc + col;
-            if (col + Cfg::kChunkCols <= args.n) {
+    uint32_t nbuf = 0;
+    int bz = 0, row0 = 0;
+
+    // Chunk `col` (kChunkCols fp32 accumulator columns of this thread's row, in v) scaled, converted
+    // and written to C: through a swizzled staging buffer and a TMA store (or reducing store), or
+    // straight from registers (direct-store configs).
+    auto emit_chunk = [&](const uint32_t* v, int col) {
+      if constexpr (Cfg::kDirectStore) {
+        // Each thread owns one row of the chunk (128 bytes of C): eight 16-byte stores, or
+        // element by element on the ragged right edge.
+        const int row = row0 + lane;
+        if (row < args.m && col < args.n) {
+          OutT* dst = static_cast<OutT*>(args.c) + (long long)bz * args.batch_stride_c + (long long)row * args.ldc + col;
+          if (col + Cfg::kChunkCols <= args.n) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                if constexpr (sizeof(OutT) == 2) {
-                  const float* f = reinterpret_cast<const float*>(&v[8 * j]);
-                  st_global_v4(dst + 8 * j, pack_out2<OutT>(f[0] * alpha, f[1] * alpha),
-                               pack_out2<OutT>(f[2] * alpha, f[3] * alpha), pack_out2<OutT>(f[4] * alpha, f[5] * alpha),
-                               pack_out2<OutT>(f[6] * alpha, f[7] * alpha));
-                } else {
-                  const float* f = reinterpret_cast<const float*>(&v[4 * j]);
-                  st_global_v4(dst + 4 * j, __float_as_uint(f[0] * alpha), __float_as_uint(f[1] * alpha),
-                               __float_as_uint(f[2] * alpha), __float_as_uint(f[3] * alpha));
-                }
-              }
-            } else {
-#pragma unroll
-              for (int e = 0; e < Cfg::kChunkCols; ++e) {  // unrolled: v stays in registers
-                if (col + e < args.n) {
-                  dst[e] = to_out<OutT>(__uint_as_float(v[e]) * alpha);
-                }
+            for (int j = 0; j < 8; ++j) {
+              if constexpr (sizeof(OutT) == 2) {
+                const float* f = reinterpret_cast<const float*>(&v[8 * j]);
+                st_global_v4(dst + 8 * j, pack_out2<OutT>(f[0] * alpha, f[1] * alpha),
+                             pack_out2<OutT>(f[2] * alpha, f[3] * alpha), pack_out2<OutT>(f[4] * alpha, f[5] * alpha),
+                             pack_out2<OutT>(f[6] * alpha, f[7] * alpha));
+              } else {
+                const float* f = reinterpret_cast<const float*>(&v[4 * j]);
+                st_global_v4(dst + 4 * j, __float_as_uint(f[0] * alpha), __float_as_uint(f[1] * alpha),
+                             __float_as_uint(f[2] * alpha), __float_as_uint(f[3] * alpha));
               }
             }
+          } else {
+#pragma unroll
+            for (int e = 0; e < Cfg::kChunkCols; ++e)  // unrolled: v stays in registers
+              if (col + e < args.n) dst[e] = to_out<OutT>(__uint_as_float(v[e]) * alpha);
           }
-          continue;
-        } else {
+        }
+      } else {
         const bool store = row0 < args.m && col < args.n;
-        const uint32_t buf = c_smem + uint32_t(ew * 2 + (nbuf & 1u)) * Cfg::kCBytes;
-        // The buffer's previous store (two chunks ago) must have finished reading it.
-        if (lane == 0) tma_store_wait_read<1>();
+        const uint32_t buf = c_smem + uint32_t(ew * Cfg::kStageBufs + (nbuf % Cfg::kStageBufs)) * Cfg::kCBytes;
+        // The buffer's previous store must have finished reading it.
+        if (lane == 0) tma_store_wait_read<Cfg::kStageBufs - 1>();
         __syncwarp();
         const uint32_t row_addr = buf + uint32_t(lane) * 128u;
         const uint32_t sw = uint32_t(lane & 7);
@@ -613,9 +590,58 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
               for (int q = 0; q < p.n_peers; ++q) tma_store_2d(&p.map_peer[q], buf, col, row0);
             }
           }
-          tma_store_commit();  // one group per chunk, empty or not, so wait_read<1> tracks buffers
+          tma_store_commit();  // one group per chunk, empty or not, so wait_read tracks buffers
         }
         ++nbuf;
+      }
+    };
+    // This warp is done reading the accumulator: hand it back to the MMA issuer.
+    auto release = [&](uint32_t acc) {
+      tcgen05_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (CG == 2)
+          mbarrier_arrive_cluster(tempty_leader0 + 8u * acc);
+        else
+          mbarrier_arrive(tempty_bar(acc));
+      }
+    };
+    auto load_chunk = [&](uint32_t taddr, uint32_t* v) {
+      tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      if constexpr (Cfg::kChunkCols == 64) tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+    };
+
+    uint32_t iter = 0;
+    for (int t = worker; t < num_tiles; t += num_workers, ++iter) {
+      int tm, tn;
+      tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, bz, tm, tn);
+      const uint32_t acc = iter % Cfg::kNumAcc;
+      const uint32_t acc_phase = (iter / Cfg::kNumAcc) & 1u;
+      if (!mbarrier_wait(tfull_bar(acc), acc_phase, args.timeout_ns)) {
+        if (lane == 0) record_status(args.status, kStatusEpilogueTimeout);
+        break;
+      }
+      tcgen05_fence_after();
+      row0 = tm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM + quarter * 32;
+      const int col0 = tn * Cfg::kTileN + wcol;
+      const uint32_t tcol = tmem_base + lane_base + acc * Cfg::kAccCols + uint32_t(wcol);
+      if constexpr (Cfg::kEarlyRelease) {
+        // All of this warp's columns into registers, accumulator back to the MMAs, then the stores.
+        uint32_t v[Cfg::kWarpCols];
+#pragma unroll
+        for (int c = 0; c < Cfg::kChunks; ++c) load_chunk(tcol + uint32_t(c * Cfg::kChunkCols), &v[c * Cfg::kChunkCols]);
+        tmem_wait_ld();
+        release(acc);
+#pragma unroll
+        for (int c = 0; c < Cfg::kChunks; ++c) emit_chunk(&v[c * Cfg::kChunkCols], col0 + c * Cfg::kChunkCols);
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < Cfg::kChunks; ++c) {
+          uint32_t v[Cfg::kChunkCols];
+          load_chunk(tcol + uint32_t(c * Cfg::kChunkCols), v);
+          tmem_wait_ld();
+          if (c == Cfg::kChunks - 1) release(acc);
+          emit_chunk(v, col0 + c * Cfg::kChunkCols);
         }
       }
     }
