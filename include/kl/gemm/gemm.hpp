@@ -40,8 +40,9 @@ struct Problem {
   // 0: C = result. 1: C += result, by TMA reducing stores (fp32 add in the TMA unit, so fp32 C
   // only; every peer copy of C gets the same add; not with the direct-store epilogue).
   int c_reduce = 0;
-  // MXFP8 (configs with kMx): UE8M0 scales of A and B, one per 32 K-elements of each row, in the
-  // 128 x 4 blocked layout: ceil(rows / 128) x ceil(K / 128) atoms of 512 bytes, row-block major.
+  // Block scaling (configs with kMx: MXFP8, or MXFP4 on packed fp4): UE8M0 scales of A and B, one
+  // per 32 K-elements of each row, in the 128 x 4 blocked layout: ceil(rows / 128) x ceil(K / 128)
+  // atoms of 512 bytes, row-block major.
   const void* sfa = nullptr;
   const void* sfb = nullptr;
 };
@@ -141,15 +142,24 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
     return g;
   };
   // A K-major operand is stored [rows, K]; an MN-major one [K, rows].
-  const int64_t a_rows = Cfg::kAMn ? pr.k : pr.m, a_cols = Cfg::kAMn ? pr.m : pr.k;
-  const int64_t b_rows = Cfg::kBMn ? pr.k : pr.n, b_cols = Cfg::kBMn ? pr.n : pr.k;
+  // Packed fp4 operands: K, leading dimensions and batch strides arrive in elements and are moved as
+  // bytes (element pairs).
+  constexpr int64_t kPack = Cfg::kFp4 ? 2 : 1;
+  if (pr.k % kPack != 0 || pr.lda % kPack != 0 || pr.ldb % kPack != 0 || pr.stride_a % kPack != 0 ||
+      pr.stride_b % kPack != 0)
+    throw std::invalid_argument("kl::gemm: packed fp4 needs even K, leading dimensions and batch strides");
+  const int64_t ku = pr.k / kPack, lda = pr.lda / kPack, ldb = pr.ldb / kPack;
+  const int64_t a_rows = Cfg::kAMn ? ku : pr.m, a_cols = Cfg::kAMn ? pr.m : ku;
+  const int64_t b_rows = Cfg::kBMn ? ku : pr.n, b_cols = Cfg::kBMn ? pr.n : ku;
   if (pr.batch > 1) {
-    p.map_a = make_tma_load<typename Cfg::ATile>(matrix(static_cast<InT const*>(pr.a), a_rows, a_cols, pr.lda, pr.stride_a)).map;
-    p.map_b = make_tma_load<typename Cfg::BTile>(matrix(static_cast<InT const*>(pr.b), b_rows, b_cols, pr.ldb, pr.stride_b)).map;
+    p.map_a = make_tma_load<typename Cfg::ATile>(
+                  matrix(static_cast<InT const*>(pr.a), a_rows, a_cols, lda, pr.stride_a / kPack)).map;
+    p.map_b = make_tma_load<typename Cfg::BTile>(
+                  matrix(static_cast<InT const*>(pr.b), b_rows, b_cols, ldb, pr.stride_b / kPack)).map;
     p.map_c = make_tma_store<typename Cfg::CBox>(matrix(static_cast<OutT*>(pr.c), pr.m, pr.n, pr.ldc, pr.stride_c)).map;
   } else {
-    p.map_a = make_tma_load<typename Cfg::ATile>(row_major_strided(static_cast<InT const*>(pr.a), a_rows, a_cols, pr.lda)).map;
-    p.map_b = make_tma_load<typename Cfg::BTile>(row_major_strided(static_cast<InT const*>(pr.b), b_rows, b_cols, pr.ldb)).map;
+    p.map_a = make_tma_load<typename Cfg::ATile>(row_major_strided(static_cast<InT const*>(pr.a), a_rows, a_cols, lda)).map;
+    p.map_b = make_tma_load<typename Cfg::BTile>(row_major_strided(static_cast<InT const*>(pr.b), b_rows, b_cols, ldb)).map;
     p.map_c = make_tma_store<typename Cfg::CBox>(row_major_strided(static_cast<OutT*>(pr.c), pr.m, pr.n, pr.ldc)).map;
   }
   if (pr.n_peers < 0 || pr.n_peers > kMaxPeers) throw std::invalid_argument("kl::gemm: at most 7 peer copies of C");
@@ -170,10 +180,10 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   TnArgs& a = p.args;
   a.m = int(pr.m);
   a.n = int(pr.n);
-  a.k = int(pr.k);
+  a.k = int(ku);
   a.tiles_m = int((pr.m + Cfg::kTileM - 1) / Cfg::kTileM);
   a.tiles_n = int((pr.n + Cfg::kTileN - 1) / Cfg::kTileN);
-  a.k_blocks = int((pr.k + Cfg::kBlockK - 1) / Cfg::kBlockK);
+  a.k_blocks = int((ku + Cfg::kBlockK - 1) / Cfg::kBlockK);
   a.group_m = pr.group_m > 0 ? pr.group_m : (Cfg::kCtaGroup == 2 ? 8 : 16);
   a.group_m = std::min(a.group_m, a.tiles_m);
   a.alpha = pr.alpha;
@@ -191,13 +201,14 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   if constexpr (Cfg::kMx) {
     if (pr.sfa == nullptr || pr.sfb == nullptr) throw std::invalid_argument("kl::gemm: MXFP8 needs scales of A and B");
     if (pr.batch > 1) throw std::invalid_argument("kl::gemm: MXFP8 is not batched");
-    // The blocked scale arrays as [row blocks][K blocks][128 words of 4 bytes].
+    // The blocked scale arrays as [row blocks][K blocks][128 words of 4 bytes]; a box is the
+    // kSfAtomsK atoms of one stage (K blocks of 128 elements).
     const int64_t kb = (pr.k + 127) / 128;
     auto sf_map = [&](CUtensorMap* map, void const* ptr, int64_t rows) {
       const int64_t shape[3] = {(rows + 127) / 128, kb, 128};
       const int64_t stride[3] = {kb * 128, 128, 1};
-      kl::detail::encode_tma_map(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, CU_TENSOR_MAP_SWIZZLE_NONE, 128, 1, ptr, 3,
-                                 shape, stride, TmaOptions{});
+      kl::detail::encode_tma_map(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, CU_TENSOR_MAP_SWIZZLE_NONE, 128,
+                                 uint32_t(Cfg::kSfAtomsK), ptr, 3, shape, stride, TmaOptions{});
     };
     sf_map(&p.map_sfa, pr.sfa, pr.m);
     sf_map(&p.map_sfb, pr.sfb, pr.n);

@@ -66,17 +66,23 @@ struct TnConfig {
   // of this CTA's 128 rows of A and the atoms of all the tile's rows of B (in both CTAs of a pair);
   // the MMA thread moves them into TMEM (tcgen05.cp 32x128b.warpx4) ahead of the stage's
   // block-scaled MMAs.
+  // Packed fp4 (e2m1x2, kind::mxf4): a stage's 128 bytes of K are 256 elements, so two scale atoms
+  // along K per 128 rows, and each MMA (64 elements) reads two scale bytes instead of one.
   static constexpr bool kMx = Mx;
-  static constexpr int kSfbAtoms = Mx ? BlockN / 128 : 0;
-  static constexpr uint32_t kSfaBytes = Mx ? 512u : 0u;
-  static constexpr uint32_t kSfbBytes = 512u * kSfbAtoms;
+  static constexpr bool kFp4 = std::is_same_v<InT, e2m1x2>;
+  static constexpr int kSfbAtoms = Mx ? BlockN / 128 : 0;   // 128-row scale blocks of B per tile
+  static constexpr int kSfAtomsK = Mx ? (kFp4 ? 2 : 1) : 0;  // scale atoms along K per stage
+  static constexpr int kMmasPerSfAtom = kFp4 ? 2 : 4;        // MMAs (32 bytes of K each) per atom
+  static constexpr uint32_t kSfIdStep = kFp4 ? 2u : 1u;      // scale bytes per MMA
+  static constexpr uint32_t kSfaBytes = 512u * kSfAtomsK;
+  static constexpr uint32_t kSfbBytes = 512u * kSfAtomsK * kSfbAtoms;
   // Two TMEM accumulators (epilogue of tile i overlaps the MMAs of tile i + 1), except for MXFP8
   // with 256 columns: 2 x 256 accumulator columns would leave none for the scales.
   static constexpr int kNumAcc = (Mx && BlockN == 256) ? 1 : 2;
   static constexpr int kAccCols = BlockN;              // fp32 accumulator columns per buffer
   static constexpr int kSfaCol = kAccCols * kNumAcc;   // TMEM columns of A's and B's scales
-  static constexpr int kSfbCol = kSfaCol + 4;
-  static constexpr int kTmemUsed = kAccCols * kNumAcc + (Mx ? 4 + 4 * kSfbAtoms : 0);
+  static constexpr int kSfbCol = kSfaCol + 4 * kSfAtomsK;
+  static constexpr int kTmemUsed = kAccCols * kNumAcc + 4 * kSfAtomsK * (1 + kSfbAtoms);
   static constexpr int kTmemCols = (kTmemUsed <= 32) ? 32 : (kTmemUsed <= 64) ? 64
                                  : (kTmemUsed <= 128) ? 128 : (kTmemUsed <= 256) ? 256 : 512;
   // Epilogue warps. With two accumulators, 4 warps (one per TMEM lane quarter) drain a tile while
@@ -129,7 +135,8 @@ struct TnConfig {
 
   static_assert(kTmemUsed <= 512, "accumulators and scales exceed TMEM");
   static_assert(!Mx || (sizeof(InT) == 1 && !AMn && !BMn && std::is_same_v<Sw, Swizzle128B> && BlockN % 128 == 0),
-                "MXFP8: 8-bit K-major operands, 128-byte swizzle, tile N a multiple of 128");
+                "block-scaled: 8-bit or packed fp4 K-major operands, 128-byte swizzle, tile N a multiple of 128");
+  static_assert(!kFp4 || Mx, "packed fp4 operands are block-scaled (kind::mxf4)");
   static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
   static_assert(BlockN % (16 * CtaGroup) == 0 && BlockN <= 256, "UMMA N");
   static_assert(kCtaN % 8 == 0 && kCtaN <= 256, "B tile rows");
@@ -396,11 +403,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
             if constexpr (Cfg::kMx) {
               // K-block kb's scale atoms: A's row block (tm) and the tile's row blocks of B (a block
               // past the end of B loads as zeros, for output columns that are never stored).
-              tma_load_3d(sfa_smem + stage * Cfg::kSfaBytes, &p.map_sfa, full_bar(stage), 0, kb, tm);
+              const int sy = kb * Cfg::kSfAtomsK;  // first K atom of this stage
+              tma_load_3d(sfa_smem + stage * Cfg::kSfaBytes, &p.map_sfa, full_bar(stage), 0, sy, tm);
 #pragma unroll
               for (int j = 0; j < Cfg::kSfbAtoms; ++j)
-                tma_load_3d(sfb_smem + stage * Cfg::kSfbBytes + 512u * j, &p.map_sfb, full_bar(stage), 0, kb,
-                            tn * Cfg::kSfbAtoms + j);
+                tma_load_3d(sfb_smem + stage * Cfg::kSfbBytes + 512u * Cfg::kSfAtomsK * j, &p.map_sfb, full_bar(stage),
+                            0, sy, tn * Cfg::kSfbAtoms + j);
             }
           } else {
             // The leader's barrier counts the bytes of both CTAs; only the leader arrives.
@@ -414,10 +422,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
                                                             batched);
             if constexpr (Cfg::kMx) {
               // Each CTA: the scales of its own 128 rows of A, and of all the tile's rows of B.
-              tma_load_3d_pair(sfa_smem + stage * Cfg::kSfaBytes, &p.map_sfa, fb, 0, kb, 2 * tm + int(cta_rank));
+              const int sy = kb * Cfg::kSfAtomsK;
+              tma_load_3d_pair(sfa_smem + stage * Cfg::kSfaBytes, &p.map_sfa, fb, 0, sy, 2 * tm + int(cta_rank));
 #pragma unroll
               for (int j = 0; j < Cfg::kSfbAtoms; ++j)
-                tma_load_3d_pair(sfb_smem + stage * Cfg::kSfbBytes + 512u * j, &p.map_sfb, fb, 0, kb,
+                tma_load_3d_pair(sfb_smem + stage * Cfg::kSfbBytes + 512u * Cfg::kSfAtomsK * j, &p.map_sfb, fb, 0, sy,
                                  tn * Cfg::kSfbAtoms + j);
             }
           }
@@ -463,24 +472,38 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
           if constexpr (Cfg::kMx) {
             // The stage's scales into TMEM: one 32x128b copy (replicated to the four lane quarters)
             // per 128 rows; the MMAs below are ordered after these copies.
-            tmem_cp_32x128b_warpx4<CG>(
-                tmem_base + Cfg::kSfaCol,
-                encode_smem_desc(sfa_smem + stage * Cfg::kSfaBytes, 0, 128, UmmaLayout::SWIZZLE_NONE));
+            // TMEM: A's atom q at kSfaCol + 4q; B's K atom q at kSfbCol + 4 * kSfbAtoms * q, its row blocks
+            // side by side (rows r of the tile in 32-bit word r / 32).
 #pragma unroll
-            for (int j = 0; j < Cfg::kSfbAtoms; ++j)
+            for (int q = 0; q < Cfg::kSfAtomsK; ++q) {
               tmem_cp_32x128b_warpx4<CG>(
-                  tmem_base + Cfg::kSfbCol + 4 * j,
-                  encode_smem_desc(sfb_smem + stage * Cfg::kSfbBytes + 512u * j, 0, 128, UmmaLayout::SWIZZLE_NONE));
+                  tmem_base + Cfg::kSfaCol + 4 * q,
+                  encode_smem_desc(sfa_smem + stage * Cfg::kSfaBytes + 512u * q, 0, 128, UmmaLayout::SWIZZLE_NONE));
+#pragma unroll
+              for (int j = 0; j < Cfg::kSfbAtoms; ++j)
+                tmem_cp_32x128b_warpx4<CG>(
+                    tmem_base + Cfg::kSfbCol + 4 * (q * Cfg::kSfbAtoms + j),
+                    encode_smem_desc(sfb_smem + stage * Cfg::kSfbBytes + 512u * (j * Cfg::kSfAtomsK + q), 0, 128,
+                                     UmmaLayout::SWIZZLE_NONE));
+            }
           }
 #pragma unroll
           for (int k = 0; k < Cfg::kBlockK / Cfg::kUmmaK; ++k) {
             const uint64_t ka = operand_kstep_16B<typename Cfg::ATile, Cfg::kAMn>(k);
             const uint64_t kb16 = operand_kstep_16B<typename Cfg::BTile, Cfg::kBMn>(k);
             const uint32_t accumulate = (kb | k) != 0;
-            if constexpr (Cfg::kMx)  // K-slice k reads byte k of every 32-bit scale word
-              umma_mxf8_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16,
-                               Cfg::kIdesc | (uint32_t(k) << 29) | (uint32_t(k) << 4), tmem_base + Cfg::kSfaCol,
-                               tmem_base + Cfg::kSfbCol, accumulate);
+            if constexpr (Cfg::kMx) {
+              // K-slice k: scale atom q, starting at byte `id` of every 32-bit scale word.
+              const int q = k / Cfg::kMmasPerSfAtom;
+              const uint32_t id = uint32_t(k % Cfg::kMmasPerSfAtom) * Cfg::kSfIdStep;
+              const uint32_t idesc = Cfg::kIdesc | (id << 29) | (id << 4);
+              const uint32_t sfa_t = tmem_base + Cfg::kSfaCol + 4 * q;
+              const uint32_t sfb_t = tmem_base + Cfg::kSfbCol + 4 * Cfg::kSfbAtoms * q;
+              if constexpr (Cfg::kFp4)
+                umma_mxf4_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16, idesc, sfa_t, sfb_t, accumulate);
+              else
+                umma_mxf8_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16, idesc, sfa_t, sfb_t, accumulate);
+            }
             else if constexpr (Cfg::kIsF8)
               umma_f8_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16, Cfg::kIdesc, accumulate);
             else

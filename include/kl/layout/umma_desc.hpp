@@ -186,6 +186,7 @@ KL_HOST_DEVICE constexpr uint32_t umma_operand_format() {
   else if constexpr (std::is_same_v<T, float>) return 2; // kind::tf32 (fp32 storage read as tf32)
   else if constexpr (std::is_same_v<T, e4m3>) return 0;  // kind::f8f6f4
   else if constexpr (std::is_same_v<T, e5m2>) return 1;  // kind::f8f6f4
+  else if constexpr (std::is_same_v<T, e2m1x2>) return 1;  // kind::mxf4 / mxf4nvf4 (packed e2m1)
   else if constexpr (std::is_same_v<T, uint8_t>) return 0;  // kind::i8
   else if constexpr (std::is_same_v<T, int8_t>) return 1;   // kind::i8
   else static_assert(sizeof(T) == 0, "no UMMA operand format for this element type");
@@ -248,7 +249,8 @@ template <typename A, typename B, int M, int N>
 KL_HOST_DEVICE constexpr uint32_t mma_instr_desc_block_scaled(uint32_t a_sf_id = 0, uint32_t b_sf_id = 0) {
   static_assert(M == 128 || M == 256, "block-scaled tcgen05.mma: M = 128 (one CTA) or 256 (CTA pair)");
   static_assert(N <= 256 && N >= 16 && N % 16 == 0, "N must be a multiple of 16, at most 256");
-  static_assert(bits_of<A> == 8 && bits_of<B> == 8, "MXFP8 operands are 8-bit floats");
+  static_assert(bits_of<A> == 8 && bits_of<B> == 8, "block-scaled operands are 8-bit floats or packed fp4 pairs");
+  static_assert(std::is_same_v<A, e2m1x2> == std::is_same_v<B, e2m1x2>, "fp4 (kind::mxf4) takes fp4 A and B");
   return detail::instr_desc_block_scaled_rt(detail::umma_operand_format<A>(), detail::umma_operand_format<B>(), M, N,
                                             a_sf_id, b_sf_id);
 }

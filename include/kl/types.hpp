@@ -16,7 +16,15 @@ using f16 = __half;
 using e4m3 = __nv_fp8_e4m3;
 using e5m2 = __nv_fp8_e5m2;
 
-// Width of one element in bits. Every type kl supports is a whole number of bytes.
+// Two e2m1 (fp4: 1 sign, 2 exponent bits with bias 1, 1 mantissa bit) values packed in one byte,
+// the first in the low nibble. kl moves fp4 as these byte pairs: tiles, tensor maps and K extents
+// of a packed operand count bytes, i.e. element pairs. (No counterpart in the reference, whose
+// types stop at 8 bits.)
+struct e2m1x2 {
+  uint8_t bits;
+};
+
+// Width of one element (of one storage unit, for e2m1x2) in bits.
 template <typename T>
 inline constexpr int bits_of = static_cast<int>(sizeof(T) * 8);
 

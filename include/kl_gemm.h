@@ -45,7 +45,10 @@ typedef enum kl_dtype {
   KL_F32 = 4,
   KL_I8 = 5,
   KL_U8 = 6,
-  KL_I32 = 7
+  KL_I32 = 7,
+  KL_E2M1 = 8,  /* fp4, two per byte (first in the low nibble); extents and pitches count elements */
+  KL_UE8M0 = 9, /* block-scale formats */
+  KL_UE4M3 = 10
 } kl_dtype;
 
 typedef enum kl_algo {
@@ -67,7 +70,8 @@ typedef struct kl_gemm_desc {
   int64_t ldb;
   void* c;       /* device, [m, ldc] */
   int64_t ldc;
-  int32_t ab_type;        /* kl_dtype of A and B: KL_BF16, KL_F16, KL_E4M3 or KL_E5M2 */
+  int32_t ab_type;        /* kl_dtype of A and B: KL_BF16, KL_F16, KL_E4M3, KL_E5M2, or KL_E2M1
+                             (packed fp4, with block_scale = 1 only) */
   int32_t c_type;         /* kl_dtype of C. (ab_type, c_type): (bf16, bf16), (bf16, f32), (f16, f16),
                              (f16, f32), (e4m3, bf16), (e4m3, f32), (e5m2, bf16), (e5m2, f32).
                              KL_ALGO_SKINNY: (bf16, bf16), (bf16, f32), (e4m3, bf16) */
@@ -99,7 +103,7 @@ typedef struct kl_gemm_desc {
    * stages hold the same 128 bytes of K as two or four swizzle atoms (one TMA box each); bf16
    * inputs with bf16 or f32 C, K-major operands. */
   int32_t swizzle;
-  /* Block scaling. 0: none. 1 (MX): ab_type KL_E4M3 or KL_E5M2 with one UE8M0 scale (value
+  /* Block scaling. 0: none. 1 (MX): ab_type KL_E4M3, KL_E5M2 or KL_E2M1 with one UE8M0 scale (value
    * 2^(s - 127)) per 32 consecutive K-elements of every row of A and of B, in `sfa` / `sfb`
    * (device), stored in the 128 x 4 blocked layout that kl_mx_pack_scales writes:
    * kl_mx_scale_bytes(rows, k) bytes. C = alpha * sum_k (A[m,k] sfa[m,k/32]) (B[n,k] sfb[n,k/32])
@@ -242,12 +246,13 @@ KL_API kl_status kl_umma_smem_desc(int32_t elem_bytes, int32_t rows, int32_t col
  * (CTA pair). kernel_lib/include/kl/layout/umma_desc.hpp:49-58 (mma_instr_desc, M <= 128 there). */
 KL_API kl_status kl_mma_instr_desc(int32_t a_type, int32_t b_type, int32_t acc_type, int32_t m, int32_t n, uint32_t* out);
 
-/* 32-bit instruction descriptor of a block-scaled (MXFP8, UE8M0 scales) tcgen05.mma:
- * a_type / b_type KL_E4M3 or KL_E5M2, M = 128 or 256, K-major operands; a_sf_id / b_sf_id (0-3)
- * select the byte of each TMEM scale word the MMA reads. No counterpart in the reference; pinned to
- * CuTe's make_instr_desc_block_scaled / make_runtime_instr_desc_block_scaled. */
-KL_API kl_status kl_mma_instr_desc_block_scaled(int32_t a_type, int32_t b_type, int32_t m, int32_t n, int32_t a_sf_id,
-                                                int32_t b_sf_id, uint32_t* out);
+/* 32-bit instruction descriptor of a block-scaled tcgen05.mma: a_type / b_type KL_E4M3 or
+ * KL_E5M2 (kind::mxf8f6f4) or KL_E2M1 (kind::mxf4 / mxf4nvf4), scale_type KL_UE8M0 or KL_UE4M3,
+ * M = 128 or 256, K-major operands; a_sf_id / b_sf_id (0-3) select the byte of each TMEM scale
+ * word the MMA reads first. No counterpart in the reference; pinned to CuTe's
+ * make_instr_desc_block_scaled / make_runtime_instr_desc_block_scaled. */
+KL_API kl_status kl_mma_instr_desc_block_scaled(int32_t a_type, int32_t b_type, int32_t scale_type, int32_t m,
+                                                int32_t n, int32_t a_sf_id, int32_t b_sf_id, uint32_t* out);
 
 /* MN-major form of kl_umma_smem_desc: a tile stored k_rows x mn_cols (MN contiguous, swizzle
  * 32/64/128 bytes), K-slice `k_block`, MN columns [mn_col, mn_col + mn_extent) (0 = to the end).

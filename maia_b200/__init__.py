@@ -23,7 +23,7 @@ KL_ERR_TIMEOUT = 4
 KL_ERR_NCCL = 5
 
 # kl_dtype
-KL_BF16, KL_F16, KL_E4M3, KL_E5M2, KL_F32, KL_I8, KL_U8, KL_I32 = range(8)
+KL_BF16, KL_F16, KL_E4M3, KL_E5M2, KL_F32, KL_I8, KL_U8, KL_I32, KL_E2M1, KL_UE8M0, KL_UE4M3 = range(11)
 
 # kl_algo
 ALGO_AUTO, ALGO_1CTA, ALGO_2CTA, ALGO_SKINNY = range(4)
@@ -108,7 +108,7 @@ def lib() -> ctypes.CDLL:
             "kl_ipc_close": (i32, [vp]),
             "kl_umma_smem_desc_mn": (i32, [i32, i32, i32, i32, u32, i32, i32, i32, P(u64)]),
             "kl_mma_instr_desc_major": (i32, [i32, i32, i32, i32, i32, i32, i32, P(u32)]),
-            "kl_mma_instr_desc_block_scaled": (i32, [i32, i32, i32, i32, i32, i32, P(u32)]),
+            "kl_mma_instr_desc_block_scaled": (i32, [i32, i32, i32, i32, i32, i32, i32, P(u32)]),
             "kl_mx_scale_bytes": (i64, [i64, i64]),
             "kl_mx_pack_scales": (i32, [vp, i64, i64, i64, vp, vp]),
         }
@@ -168,9 +168,9 @@ def mma_instr_desc_major(a_type, b_type, acc_type, m, n, a_major, b_major) -> in
     return out.value
 
 
-def mma_instr_desc_block_scaled(a_type, b_type, m, n, a_sf_id=0, b_sf_id=0) -> int:
+def mma_instr_desc_block_scaled(a_type, b_type, m, n, a_sf_id=0, b_sf_id=0, scale_type=KL_UE8M0) -> int:
     out = ctypes.c_uint32()
-    check(lib().kl_mma_instr_desc_block_scaled(a_type, b_type, m, n, a_sf_id, b_sf_id, ctypes.byref(out)))
+    check(lib().kl_mma_instr_desc_block_scaled(a_type, b_type, scale_type, m, n, a_sf_id, b_sf_id, ctypes.byref(out)))
     return out.value
 
 
@@ -202,7 +202,7 @@ def _dtype_code(t) -> int:
     if _TORCH_DTYPES is None:
         _TORCH_DTYPES = {torch.bfloat16: KL_BF16, torch.float16: KL_F16, torch.float8_e4m3fn: KL_E4M3,
                          torch.float8_e5m2: KL_E5M2, torch.float32: KL_F32, torch.int8: KL_I8,
-                         torch.uint8: KL_U8, torch.int32: KL_I32}
+                         torch.uint8: KL_U8, torch.int32: KL_I32, torch.float4_e2m1fn_x2: KL_E2M1}
     return _TORCH_DTYPES[t]
 
 
@@ -219,13 +219,19 @@ def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, gr
             raise ValueError(f"{name} must be a 2-D or 3-D tensor with a contiguous last dimension")
     if not a.dim() == b.dim() == c.dim():
         raise ValueError("a, b and c must all be 2-D or all 3-D")
-    m, k = (a.shape[-1], a.shape[-2]) if a_major else (a.shape[-2], a.shape[-1])
-    n, kb = (b.shape[-1], b.shape[-2]) if b_major else (b.shape[-2], b.shape[-1])
+    # Packed fp4 (torch.float4_e2m1fn_x2) holds two elements per storage unit: the descriptor counts
+    # elements, so K, the pitches and the batch strides of A and B double.
+    pa = 2 if _dtype_code(a.dtype) == KL_E2M1 else 1
+    pb = 2 if _dtype_code(b.dtype) == KL_E2M1 else 1
+    if (pa > 1 or pb > 1) and (a_major or b_major):
+        raise ValueError("packed fp4 operands are K-major")
+    m, k = (a.shape[-1], a.shape[-2]) if a_major else (a.shape[-2], a.shape[-1] * pa)
+    n, kb = (b.shape[-1], b.shape[-2]) if b_major else (b.shape[-2], b.shape[-1] * pb)
     batch = a.shape[0] if a.dim() == 3 else 0
     if kb != k or tuple(c.shape[-2:]) != (m, n) or (a.dim() == 3 and not (b.shape[0] == c.shape[0] == batch)):
         raise ValueError(f"shape mismatch: a {tuple(a.shape)}, b {tuple(b.shape)}, c {tuple(c.shape)}")
-    bs = (a.stride(0), b.stride(0), c.stride(0)) if a.dim() == 3 else (0, 0, 0)
-    return GemmDesc(m=m, n=n, k=k, a=a.data_ptr(), lda=a.stride(-2), b=b.data_ptr(), ldb=b.stride(-2),
+    bs = (a.stride(0) * pa, b.stride(0) * pb, c.stride(0)) if a.dim() == 3 else (0, 0, 0)
+    return GemmDesc(m=m, n=n, k=k, a=a.data_ptr(), lda=a.stride(-2) * pa, b=b.data_ptr(), ldb=b.stride(-2) * pb,
                     c=c.data_ptr(), ldc=c.stride(-2), ab_type=_dtype_code(a.dtype), c_type=_dtype_code(c.dtype),
                     alpha=float(alpha), scale_a=None if scale_a is None else scale_a.data_ptr(),
                     scale_b=None if scale_b is None else scale_b.data_ptr(), algo=algo, group_m=group_m,

@@ -478,17 +478,24 @@ kl_status kl_mma_instr_desc_major(int32_t a_type, int32_t b_type, int32_t acc_ty
   return KL_OK;
 }
 
-kl_status kl_mma_instr_desc_block_scaled(int32_t a_type, int32_t b_type, int32_t m, int32_t n, int32_t a_sf_id,
-                                         int32_t b_sf_id, uint32_t* out) {
+kl_status kl_mma_instr_desc_block_scaled(int32_t a_type, int32_t b_type, int32_t scale_type, int32_t m, int32_t n,
+                                         int32_t a_sf_id, int32_t b_sf_id, uint32_t* out) {
   if (out == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null output");
-  auto fmt = [](int32_t t) { return t == KL_E4M3 ? 0 : t == KL_E5M2 ? 1 : -1; };
+  // Operand formats: kind::mxf8f6f4 e4m3 = 0, e5m2 = 1; kind::mxf4 / mxf4nvf4 e2m1 = 1.
+  auto fmt = [](int32_t t) { return t == KL_E4M3 ? 0 : (t == KL_E5M2 || t == KL_E2M1) ? 1 : -1; };
   const int fa = fmt(a_type), fb = fmt(b_type);
-  if (fa < 0 || fb < 0) return fail(KL_ERR_INVALID_ARGUMENT, "block-scaled operands must be e4m3 or e5m2");
+  if (fa < 0 || fb < 0) return fail(KL_ERR_INVALID_ARGUMENT, "block-scaled operands must be e4m3, e5m2 or e2m1");
+  if ((a_type == KL_E2M1) != (b_type == KL_E2M1)) return fail(KL_ERR_INVALID_ARGUMENT, "e2m1 takes e2m1 A and B");
+  if (scale_type != KL_UE8M0 && scale_type != KL_UE4M3)
+    return fail(KL_ERR_INVALID_ARGUMENT, "scale_type must be KL_UE8M0 or KL_UE4M3");
+  if (scale_type == KL_UE4M3 && a_type != KL_E2M1)
+    return fail(KL_ERR_INVALID_ARGUMENT, "UE4M3 scales go with e2m1 operands (kind::mxf4nvf4)");
   if (m != 128 && m != 256) return fail(KL_ERR_INVALID_ARGUMENT, "block-scaled M must be 128 or 256");
   if (n < 16 || n > 256 || n % 16 != 0) return fail(KL_ERR_INVALID_ARGUMENT, "N must be a multiple of 16 in [16, 256]");
   if (a_sf_id < 0 || a_sf_id > 3 || b_sf_id < 0 || b_sf_id > 3)
     return fail(KL_ERR_INVALID_ARGUMENT, "scale-factor ids are 0 to 3");
   *out = kl::detail::instr_desc_block_scaled_rt(uint32_t(fa), uint32_t(fb), m, n, uint32_t(a_sf_id), uint32_t(b_sf_id));
+  if (scale_type == KL_UE4M3) *out &= ~(1u << 23);  // scale format bit: 1 = UE8M0, 0 = UE4M3
   return KL_OK;
 }
 

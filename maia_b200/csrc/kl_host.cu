@@ -94,7 +94,9 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
   kl_status s = get_pipe(dev, chunks, &p);
   if (s != KL_OK) return s;
 
-  const int eab = elem_bytes(h->ab_type), ec = elem_bytes(h->c_type);
+  const int ec = elem_bytes(h->c_type);
+  // Bytes of `elems` operand elements (packed fp4: two per byte).
+  auto ab_bytes = [&](int64_t elems) { return size_t(h->ab_type == KL_E2M1 ? elems / 2 : elems * elem_bytes(h->ab_type)); };
   // MXFP8 scales: blocked arrays, A's then B's, in one staging buffer.
   const int64_t sfa_bytes = mx ? kl_mx_scale_bytes(h->m, h->k) : 0;
   const int64_t sfb_bytes = mx ? kl_mx_scale_bytes(h->n, h->k) : 0;
@@ -122,13 +124,13 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
   // Start after everything already queued on the caller's stream.
   if ((e = cudaEventRecord(p->start, caller)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   if ((e = cudaStreamWaitEvent(p->in, p->start, 0)) != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
-  if ((e = cudaMemcpyAsync(da, ha, size_t(h->m) * h->lda * eab, cudaMemcpyHostToDevice, p->in)) != cudaSuccess)
+  if ((e = cudaMemcpyAsync(da, ha, ab_bytes(h->m * h->lda), cudaMemcpyHostToDevice, p->in)) != cudaSuccess)
     return cuda_fail(e, "kl_gemm_host: copy of A");
   if (mx && (e = cudaMemcpyAsync(dsfa, h->sfa, size_t(sfa_bytes), cudaMemcpyHostToDevice, p->in)) != cudaSuccess)
     return cuda_fail(e, "kl_gemm_host: copy of A's scales");
   for (int j = 0; j < chunks; ++j) {
     const int64_t n0 = int64_t(j) * block, nj = std::min<int64_t>(block, h->n - n0);
-    e = cudaMemcpyAsync(db + size_t(n0) * h->ldb * eab, hb + size_t(n0) * h->ldb * eab, size_t(nj) * h->ldb * eab,
+    e = cudaMemcpyAsync(db + ab_bytes(n0 * h->ldb), hb + ab_bytes(n0 * h->ldb), ab_bytes(nj * h->ldb),
                         cudaMemcpyHostToDevice, p->in);
     if (e != cudaSuccess) return cuda_fail(e, "kl_gemm_host: copy of B");
     // Block j starts on a 256-row boundary of B, so its scales are whole 128-row blocks.
@@ -143,7 +145,7 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
     kl_gemm_desc d = *h;
     d.n = nj;
     d.a = da;
-    d.b = db + size_t(n0) * h->ldb * eab;
+    d.b = db + ab_bytes(n0 * h->ldb);
     d.c = dc + size_t(n0) * ec;
     if (mx) {
       d.sfa = dsfa;

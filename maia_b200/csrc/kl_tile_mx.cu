@@ -1,5 +1,6 @@
-// MXFP8 tile kernels (block-scaled e4m3 / e5m2 through tcgen05.mma kind::mxf8f6f4.block_scale) and
-// the scale-factor repacking kernel.
+// Block-scaled tile kernels: MXFP8 (e4m3 / e5m2, tcgen05.mma kind::mxf8f6f4.block_scale) and MXFP4
+// (packed e2m1, kind::mxf4.block_scale.block32), UE8M0 scales per 32 K-elements; and the
+// scale-factor repacking kernel.
 
 #include <cuda_runtime.h>
 
@@ -65,6 +66,8 @@ kl_status run_tile_mx(int32_t ab, int32_t c, int32_t variant, bool pair, kl::gem
   if (ab == KL_E4M3 && c == KL_F32) return run_mx<kl::e4m3, float>(variant, pair, pr, stream, info);
   if (ab == KL_E5M2 && c == KL_BF16) return run_mx<kl::e5m2, kl::bf16>(variant, pair, pr, stream, info);
   if (ab == KL_E5M2 && c == KL_F32) return run_mx<kl::e5m2, float>(variant, pair, pr, stream, info);
+  if (ab == KL_E2M1 && c == KL_BF16) return run_mx<kl::e2m1x2, kl::bf16>(variant, pair, pr, stream, info);
+  if (ab == KL_E2M1 && c == KL_F32) return run_mx<kl::e2m1x2, float>(variant, pair, pr, stream, info);
   *handled = false;
   return KL_ERR_NOT_SUPPORTED;
 }

@@ -175,14 +175,34 @@ def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(x, dtype=np.float32).astype(np.float16).view(np.uint16)
 
 
-MX_EMAX = {"e4m3": 8, "e5m2": 15}  # exponent of the largest normal element value
+E2M1_GRID = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])  # the e2m1 magnitudes, by code 0..7
+
+
+def f32_to_e2m1_codes(x: np.ndarray) -> np.ndarray:
+    """Round float32 to the nearest e2m1 value (ties to the even code, i.e. mantissa 0), saturating
+    at +-6; returns 4-bit codes (sign in bit 3) as uint8."""
+    a = np.minimum(np.abs(np.asarray(x, dtype=np.float64)), 6.0)
+    idx = np.clip(np.searchsorted(E2M1_GRID, a), 1, 7)
+    lo, hi = E2M1_GRID[idx - 1], E2M1_GRID[idx]
+    pick_hi = (a - lo > hi - a) | ((a - lo == hi - a) & (idx % 2 == 0))
+    q = np.where(pick_hi, idx, idx - 1).astype(np.uint8)
+    return np.where(np.signbit(x) & (q != 0), q | 8, q).astype(np.uint8)
+
+
+def pack_e2m1(codes: np.ndarray) -> np.ndarray:
+    """Pack 4-bit codes [rows, K] (K even) two per byte, the first element in the low nibble."""
+    c = np.ascontiguousarray(codes, dtype=np.uint8)
+    return (c[..., 0::2] | (c[..., 1::2] << 4)).astype(np.uint8)
+
+
+MX_EMAX = {"e4m3": 8, "e5m2": 15, "e2m1": 2}  # exponent of the largest normal element value
 
 
 def mx_quantize(x: np.ndarray, kind: str = "e4m3") -> tuple[np.ndarray, np.ndarray]:
     """MX quantisation (OCP Microscaling Formats v1.0) of float32 rows in blocks of 32 K-elements:
     shared scale 2^(floor(log2(amax)) - emax) as UE8M0 bits, elements x / scale rounded to the
-    8-bit format (nearest, ties to even, saturating). Returns (element bits, scale bits
-    [rows, ceil(K/32)])."""
+    element format (nearest, ties to even, saturating). Returns (element bits, scale bits
+    [rows, ceil(K/32)]); e2m1 elements come packed two per byte ([rows, K/2], K even)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     rows, k = x.shape
     groups = -(-k // 32)
@@ -193,6 +213,8 @@ def mx_quantize(x: np.ndarray, kind: str = "e4m3") -> tuple[np.ndarray, np.ndarr
     sbits = np.clip(e + 127, 0, 254).astype(np.uint8)
     inv = np.exp2(127.0 - sbits.astype(np.float64))
     q = (padded.reshape(rows, groups, 32) * inv[:, :, None]).reshape(rows, groups * 32)[:, :k].astype(np.float32)
+    if kind == "e2m1":
+        return pack_e2m1(f32_to_e2m1_codes(q)), sbits
     enc = f32_to_e4m3_bits if kind == "e4m3" else f32_to_e5m2_bits
     return enc(q), sbits
 

@@ -24,7 +24,10 @@
  * f16 is IEEE binary16 (1 sign, 5 exponent bits with bias 15, 10 mantissa bits); e4m3 (OCP FP8,
  * "fn" variant) has 1 sign, 4 exponent (bias 7), 3 mantissa bits, no infinities, and S.1111.111 is
  * NaN; e5m2 (OCP FP8) has 1 sign, 5 exponent (bias 15), 2 mantissa bits, with IEEE infinities and
- * NaNs at exponent 31. Type codes follow the library's kl_dtype: bf16 0, f16 1, e4m3 2, e5m2 3.
+ * NaNs at exponent 31; e2m1 (OCP fp4) has 1 sign, 2 exponent (bias 1), 1 mantissa bit, no
+ * infinities or NaNs (values 0, 0.5, 1, 1.5, 2, 3, 4, 6), stored two per byte with the first
+ * element in the low nibble. Type codes follow the library's kl_dtype: bf16 0, f16 1, e4m3 2,
+ * e5m2 3, e2m1 8.
  */
 #include <math.h>
 #include <pthread.h>
@@ -36,8 +39,14 @@
 #define KL_ORACLE_F16 1
 #define KL_ORACLE_E4M3 2
 #define KL_ORACLE_E5M2 3
+#define KL_ORACLE_E2M1 8 /* two per byte, the first in the low nibble */
 
 static int elem_size(int t) { return (t == KL_ORACLE_BF16 || t == KL_ORACLE_F16) ? 2 : 1; }
+
+/* Bytes of `count` elements of type t (packed e2m1: two per byte; count even). */
+static size_t bytes_of(int t, int64_t count) {
+  return t == KL_ORACLE_E2M1 ? (size_t)(count / 2) : (size_t)count * (size_t)elem_size(t);
+}
 
 static double decode_bf16(uint16_t h) {
   uint32_t bits = (uint32_t)h << 16;
@@ -87,6 +96,13 @@ void kl_oracle_decode(int t, const void* src, int64_t n, double* dst) {
   } else if (t == KL_ORACLE_E5M2) {
     const uint8_t* s = (const uint8_t*)src;
     for (int64_t i = 0; i < n; ++i) dst[i] = decode_ieee(s[i], 5, 2);
+  } else if (t == KL_ORACLE_E2M1) {
+    const uint8_t* s = (const uint8_t*)src;
+    for (int64_t i = 0; i < n; ++i) {
+      const uint32_t v = (s[i / 2] >> (4 * (i & 1))) & 0xF;
+      const double mag = (v & 6) == 0 ? 0.5 * (v & 1) : ldexp(1.0 + 0.5 * (v & 1), (int)((v >> 1) & 3) - 1);
+      dst[i] = (v & 8) ? -mag : mag;
+    }
   } else {
     const uint8_t* s = (const uint8_t*)src;
     for (int64_t i = 0; i < n; ++i) dst[i] = decode_e4m3(s[i]);
@@ -115,7 +131,7 @@ static double e8m0(uint8_t s) { return s == 255 ? NAN : ldexp(1.0, (int)s - 127)
 /* Decode row `r` of a matrix (k elements) and apply its MX scales when `sf` is given. */
 static void decode_row(int t, const void* base, int64_t ld, int64_t r, int64_t k, const uint8_t* sf, int64_t ldsf,
                        double* out) {
-  kl_oracle_decode(t, (const char*)base + (size_t)(r * ld) * elem_size(t), k, out);
+  kl_oracle_decode(t, (const char*)base + bytes_of(t, r * ld), k, out);
   if (sf)
     for (int64_t kk = 0; kk < k; ++kk) out[kk] *= e8m0(sf[r * ldsf + kk / 32]);
 }

@@ -228,6 +228,16 @@ int main(int argc, char** argv) {
     bs(uint32_t(cute::UMMA::make_instr_desc_block_scaled<E4, E4, float, UE8, 128, 128, Major::K, Major::K>()), "e4m3", "e4m3", 128, 128, 0, 0);
     bs(uint32_t(cute::UMMA::make_instr_desc_block_scaled<E5, E4, float, UE8, 128, 256, Major::K, Major::K>()), "e5m2", "e4m3", 128, 256, 0, 0);
     bs(uint32_t(cute::UMMA::make_instr_desc_block_scaled<E5, E5, float, UE8, 256, 256, Major::K, Major::K>()), "e5m2", "e5m2", 256, 256, 0, 0);
+    using E2 = cutlass::float_e2m1_t;  // packed e2m1 (kind::mxf4 / mxf4nvf4)
+    using UE4 = cutlass::float_ue4m3_t;
+    bs(uint32_t(cute::UMMA::make_instr_desc_block_scaled<E2, E2, float, UE8, 128, 256, Major::K, Major::K>()), "e2m1", "e2m1", 128, 256, 0, 0);
+    bs(uint32_t(cute::UMMA::make_instr_desc_block_scaled<E2, E2, float, UE8, 256, 256, Major::K, Major::K>()), "e2m1", "e2m1", 256, 256, 0, 0);
+    {
+      const uint64_t r = cute::UMMA::make_runtime_instr_desc_block_scaled<E2, E2, float, UE8, 256, 256, Major::K, Major::K>(
+          2u << 30, 2u << 30);
+      bs(uint32_t(r >> 32), "e2m1", "e2m1", 256, 256, 2, 2);
+    }
+    bs(uint32_t(cute::UMMA::make_instr_desc_block_scaled<E2, E2, float, UE4, 128, 256, Major::K, Major::K>()), "e2m1/ue4m3", "e2m1/ue4m3", 128, 256, 0, 0);
     for (int a_sf = 0; a_sf < 4; ++a_sf)
       for (int b_sf = 0; b_sf < 4; ++b_sf) {
         const uint64_t r = cute::UMMA::make_runtime_instr_desc_block_scaled<E4, E4, float, UE8, 128, 256, Major::K, Major::K>(

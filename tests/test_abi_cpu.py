@@ -11,7 +11,8 @@ import maia_b200 as kl
 from golden_util import ELEM_BYTES, idesc_majors, idescs, known_answers, mn_tiles, sha, tile_id, tiles
 
 HEADER = Path(__file__).resolve().parent.parent / "include" / "kl_gemm.h"
-TYPE = {"bf16": kl.KL_BF16, "f16": kl.KL_F16, "f32": kl.KL_F32, "i8": kl.KL_I8, "e4m3": kl.KL_E4M3, "e5m2": kl.KL_E5M2}
+TYPE = {"bf16": kl.KL_BF16, "f16": kl.KL_F16, "f32": kl.KL_F32, "i8": kl.KL_I8, "e4m3": kl.KL_E4M3, "e5m2": kl.KL_E5M2,
+        "e2m1": kl.KL_E2M1}
 
 
 def declared_symbols():
@@ -159,9 +160,12 @@ def test_block_scaled_instr_desc_matches_cute():
     from golden_util import host_tables
 
     rows = [t for t in host_tables() if t["kind"] == "idesc_block_scaled"]
-    assert len(rows) == 20
+    assert len(rows) == 24
     for d in rows:
-        got = kl.mma_instr_desc_block_scaled(TYPE[d["a"]], TYPE[d["b"]], d["m"], d["n"], d["a_sf_id"], d["b_sf_id"])
+        a, _, sf = d["a"].partition("/")  # "e2m1/ue4m3": NVFP4 (UE4M3 scales); otherwise UE8M0
+        b = d["b"].partition("/")[0]
+        scale = kl.KL_UE4M3 if sf == "ue4m3" else kl.KL_UE8M0
+        got = kl.mma_instr_desc_block_scaled(TYPE[a], TYPE[b], d["m"], d["n"], d["a_sf_id"], d["b_sf_id"], scale)
         assert got == int(d["value"], 16), d
 
 
@@ -172,6 +176,10 @@ def test_block_scaled_instr_desc_errors():
         kl.mma_instr_desc_block_scaled(kl.KL_E4M3, kl.KL_E4M3, 64, 256)
     with pytest.raises(kl.KlError):
         kl.mma_instr_desc_block_scaled(kl.KL_E4M3, kl.KL_E4M3, 128, 256, 4, 0)
+    with pytest.raises(kl.KlError):  # fp4 with fp8
+        kl.mma_instr_desc_block_scaled(kl.KL_E2M1, kl.KL_E4M3, 128, 256)
+    with pytest.raises(kl.KlError):  # UE4M3 scales are for fp4 only
+        kl.mma_instr_desc_block_scaled(kl.KL_E4M3, kl.KL_E4M3, 128, 256, scale_type=kl.KL_UE4M3)
 
 
 @pytest.mark.parametrize("rows,k,want", [(1, 1, 512), (128, 128, 512), (129, 128, 1024), (128, 129, 1024),

@@ -35,7 +35,7 @@ def mx_inputs(m, n, k, kind, seed, spread=0.0):
 
 
 def run_mx(qa, sa, qb, sb, kind, out, device, **kw):
-    k = qa.shape[1]
+    k = qa.shape[1] * (2 if kind == "e2m1" else 1)
     a, b = to_device(qa, kind, device), to_device(qb, kind, device)
     psa = kl.mx_pack_scales(torch.from_numpy(sa).to(device), k)
     psb = kl.mx_pack_scales(torch.from_numpy(sb).to(device), k)
@@ -86,6 +86,25 @@ def test_mx_gemm(cuda, algo, variant, kind, out, shape):
     qa, sa, qb, sb = mx_inputs(m, n, k, kind, seed=m + n + k)
     c = run_mx(qa, sa, qb, sb, kind, out, cuda, algo=algo, variant=variant)
     check_mx(c, qa, sa, qb, sb, kind)
+
+
+@KERNELS
+@pytest.mark.parametrize("out", ["bf16", "f32"])
+@pytest.mark.parametrize("shape", [(128, 256, 256), (200, 304, 320), (256, 512, 1024), (1000, 1000, 1024),
+                                   (130, 264, 96)])
+def test_mxfp4_gemm(cuda, algo, variant, out, shape):
+    """Packed fp4 (e2m1, two per byte) with UE8M0 scales per 32 elements: kind::mxf4, 64 K-elements
+    and two scale bytes per MMA, two scale atoms along K per stage."""
+    m, n, k = shape
+    qa, sa, qb, sb = mx_inputs(m, n, k, "e2m1", seed=3 * m + n + k)
+    c = run_mx(qa, sa, qb, sb, "e2m1", out, cuda, algo=algo, variant=variant)
+    check_mx(c, qa, sa, qb, sb, "e2m1")
+
+
+def test_mxfp4_wide_scale_range(cuda):
+    qa, sa, qb, sb = mx_inputs(384, 512, 768, "e2m1", seed=6, spread=10.0)
+    c = run_mx(qa, sa, qb, sb, "e2m1", "f32", cuda, algo=kl.ALGO_2CTA)
+    check_mx(c, qa, sa, qb, sb, "e2m1")
 
 
 @KERNELS

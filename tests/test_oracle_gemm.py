@@ -155,3 +155,34 @@ def test_pack_mx_scales_layout():
             kk, jj = divmod(j, 4)
             assert pk[(rb * kb + kk) * 512 + (rr % 32) * 16 + (rr // 32) * 4 + jj] == sf[r, j]
     assert pk[(2 * kb + 2) * 512 + 1 * 16 + 3 * 4 + 1] == 127  # row 2*128+97 >= 300: padding
+
+
+def test_e2m1_rounding_packing_and_decode():
+    grid = wl.E2M1_GRID
+    # Every code decodes to its value; ties go to the even code (mantissa 0); saturation at 6.
+    codes = np.arange(16, dtype=np.uint8)
+    vals = np.where(codes & 8, -1.0, 1.0) * grid[codes & 7]
+    got = og.decode(wl.pack_e2m1(codes.reshape(1, 16)), "e2m1")[0]
+    np.testing.assert_array_equal(got, vals)
+    x = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 7.0, -5.0, 100.0], np.float32)
+    assert wl.f32_to_e2m1_codes(x).tolist() == [0, 2, 2, 4, 4, 6, 6, 7, 14, 7]
+    # Packing: the first element in the low nibble.
+    assert wl.pack_e2m1(np.array([[1, 2, 15, 0]], np.uint8)).tolist() == [[0x21, 0x0F]]
+    # Random values: the chosen code is a nearest grid point of the clipped value.
+    rng = np.random.default_rng(2)
+    y = np.clip(rng.standard_normal(5000).astype(np.float32) * 3, -6, 6)
+    c = wl.f32_to_e2m1_codes(y)
+    err = np.abs(np.where(c & 8, -1.0, 1.0) * grid[c & 7] - y)
+    nearest = np.abs(np.abs(y)[:, None] - grid[None, :]).min(axis=1)
+    np.testing.assert_allclose(err, nearest, atol=1e-7)
+
+
+def test_gemm_mx_f64_packed_fp4():
+    rng = np.random.default_rng(6)
+    qa, sa = wl.mx_quantize(rng.standard_normal((17, 96)).astype(np.float32), "e2m1")
+    qb, sb = wl.mx_quantize(rng.standard_normal((11, 96)).astype(np.float32), "e2m1")
+    assert qa.shape == (17, 48) and sa.shape == (17, 3)
+    da = og.decode(qa, "e2m1") * np.repeat(og.e8m0_values(sa), 32, axis=1)
+    db = og.decode(qb, "e2m1") * np.repeat(og.e8m0_values(sb), 32, axis=1)
+    np.testing.assert_allclose(og.gemm_mx_f64(qa, qb, sa, sb, "e2m1"), da @ db.T, rtol=1e-13, atol=1e-13)
+    np.testing.assert_allclose(og.gemm_mx_f32(qa, qb, sa, sb, "e2m1"), da @ db.T, rtol=1e-5, atol=1e-5)
