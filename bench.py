@@ -107,8 +107,8 @@ def cpu_baseline(w, budget_s: float = 6.0):
     while True:
         a, b, sa, sb = wl.make_inputs(w, rows_a=rows)
         t0 = time.perf_counter()
-        if w.dtype == "mxfp8":
-            og.gemm_mx_f32(a, b, sa, sb, "e4m3", threads=threads)
+        if w.dtype in ("mxfp8", "mxfp4"):
+            og.gemm_mx_f32(a, b, sa, sb, "e4m3" if w.dtype == "mxfp8" else "e2m1", threads=threads)
         else:
             og.gemm_f32(a, b, sa * sb, threads=threads)
         dt = time.perf_counter() - t0
@@ -188,12 +188,12 @@ def main():
     a_bits, b_bits, sa, sb = wl.make_inputs(w)
     n_lo, n_hi = sharding.shard_range(w.n, world, rank, align=256)
     b_bits = np.ascontiguousarray(b_bits[n_lo:n_hi])
-    mx = w.dtype == "mxfp8"
+    mx = w.dtype in ("mxfp8", "mxfp4")
     if mx:
         sb = np.ascontiguousarray(sb[n_lo:n_hi])
     nshard = n_hi - n_lo
     np_view = np.int16 if w.dtype == "bf16" else np.uint8
-    tdt = torch.bfloat16 if w.dtype == "bf16" else torch.float8_e4m3fn
+    tdt = {"bf16": torch.bfloat16, "mxfp4": torch.float4_e2m1fn_x2}.get(w.dtype, torch.float8_e4m3fn)
     odt = torch.bfloat16 if w.out == "bf16" else torch.float32
     a_host = torch.from_numpy(a_bits.view(np_view)).view(tdt).pin_memory()
     b_host = torch.from_numpy(b_bits.view(np_view)).view(tdt).pin_memory()
@@ -325,15 +325,17 @@ def main():
     memory_bound = w.m <= 256
     if memory_bound:
         # Decode shapes: every operand byte moved once, against the measured copy bandwidth.
-        alg_bytes = (w.m * w.k + nshard * w.k) * w.in_bytes + w.m * nshard * w.out_bytes + \
-            (w.m + nshard) * -(-w.k // 32) * (w.dtype == "mxfp8")
+        alg_bytes = int((w.m * w.k + nshard * w.k) * w.in_bytes) + w.m * nshard * w.out_bytes + \
+            (w.m + nshard) * -(-w.k // 32) * (w.dtype in ("mxfp8", "mxfp4"))
         roofline = {"bound": "hbm", "achieved": alg_bytes / (dev_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
                     "unit": "GB/s", "peak_source": f"{peak_src} hbm_gbs", "algorithmic_bytes_per_launch": alg_bytes}
     else:
-        peak = peaks["bf16_tflops"] if w.dtype == "bf16" else 2.0 * peaks["bf16_tflops"]
+        peak = peaks["bf16_tflops"] * {"bf16": 1.0, "mxfp4": 4.0}.get(w.dtype, 2.0)
         roofline = {"bound": "tensor", "achieved": per_rank_flops / (dev_ms * 1e-3) / 1e12, "peak": peak,
                     "unit": "TFLOP/s",
                     "peak_source": f"{peak_src} " + ("bf16_tflops (burst)" if w.dtype == "bf16" else
+                                                     "4 x bf16_tflops (burst; the dense fp4 rate is four times bf16)"
+                                                     if w.dtype == "mxfp4" else
                                                      "2 x bf16_tflops (burst; the fp8 and MXFP8 dense rate is "
                                                      "twice bf16)"),
                     "algorithmic_flops_per_launch": per_rank_flops}

@@ -22,7 +22,7 @@ class Workload:
     m: int
     n: int
     k: int
-    dtype: str          # "bf16", "e4m3" or "mxfp8" (e4m3 elements with MX block scales)
+    dtype: str          # "bf16", "e4m3", "mxfp8" (e4m3 elements with MX block scales) or "mxfp4" (e2m1)
     out: str            # "bf16" or "f32"
     dist: str           # "uniform" (on [-1, 1]) or "normal"
     a_scale: float      # multiplier of A's standard normal (normal) draws
@@ -34,13 +34,13 @@ class Workload:
         return 2.0 * self.m * self.n * self.k
 
     @property
-    def in_bytes(self) -> int:
-        return 2 if self.dtype == "bf16" else 1
+    def in_bytes(self) -> float:
+        return 2 if self.dtype == "bf16" else 0.5 if self.dtype == "mxfp4" else 1
 
     @property
     def scale_bytes(self) -> int:
         """MX block scales: one byte per 32 K-elements of every row of A and B."""
-        return (self.m + self.n) * -(-self.k // 32) if self.dtype == "mxfp8" else 0
+        return (self.m + self.n) * -(-self.k // 32) if self.dtype in ("mxfp8", "mxfp4") else 0
 
     @property
     def out_bytes(self) -> int:
@@ -49,7 +49,7 @@ class Workload:
     @property
     def bytes(self) -> int:
         """Algorithmic bytes: every matrix moved once."""
-        return (self.m * self.k + self.n * self.k) * self.in_bytes + self.m * self.n * self.out_bytes + self.scale_bytes
+        return int((self.m * self.k + self.n * self.k) * self.in_bytes) + self.m * self.n * self.out_bytes + self.scale_bytes
 
 
 # C1..C5: the reference's GEMM contract at its benchmark shapes.
@@ -61,8 +61,11 @@ C5 = {m: Workload(f"c5_skinny_m{m}", m, 28672, 8192, "bf16", "bf16", "normal", 1
 # C4's shape and draws, MX-quantised instead of per-tensor scaled (block-scaled fp8); and C3's.
 C4MX = Workload("c4mx_16384x16384x8192_mxfp8", 16384, 16384, 8192, "mxfp8", "bf16", "normal", 1.0, 1.0, 3)
 C3MX = Workload("c3mx_8192_mxfp8", 8192, 8192, 8192, "mxfp8", "bf16", "normal", 0.02, 0.02, 2)
+# The same shapes in MXFP4 (packed e2m1 elements, UE8M0 scales per 32).
+C3MXF4 = Workload("c3mxf4_8192_mxfp4", 8192, 8192, 8192, "mxfp4", "bf16", "normal", 0.02, 0.02, 2)
+C4MXF4 = Workload("c4mxf4_16384x16384x8192_mxfp4", 16384, 16384, 8192, "mxfp4", "bf16", "normal", 1.0, 1.0, 3)
 
-ALL = {w.name: w for w in (C1, C2, C3, C4, C4MX, C3MX, *C5.values())}
+ALL = {w.name: w for w in (C1, C2, C3, C4, C4MX, C3MX, C3MXF4, C4MXF4, *C5.values())}
 
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
@@ -238,9 +241,10 @@ def make_inputs(w: Workload, rows_a: int | None = None):
     xb = draw(w, 1, w.n, w.k, w.b_scale)
     if w.dtype == "bf16":
         return f32_to_bf16_bits(xa), f32_to_bf16_bits(xb), 1.0, 1.0
-    if w.dtype == "mxfp8":
-        qa, sfa = mx_quantize(xa, "e4m3")
-        qb, sfb = mx_quantize(xb, "e4m3")
+    if w.dtype in ("mxfp8", "mxfp4"):
+        kind = "e4m3" if w.dtype == "mxfp8" else "e2m1"
+        qa, sfa = mx_quantize(xa, kind)
+        qb, sfb = mx_quantize(xb, kind)
         return qa, qb, sfa, sfb
     # fp8: per-tensor scales from the full tensors' amax.
     sa = float(np.abs(draw(w, 0, w.m, w.k, w.a_scale)).max()) / 448.0 if rows_a is not None else float(np.abs(xa).max()) / 448.0

@@ -97,12 +97,13 @@ void kl_oracle_decode(int t, const void* src, int64_t n, double* dst) {
     const uint8_t* s = (const uint8_t*)src;
     for (int64_t i = 0; i < n; ++i) dst[i] = decode_ieee(s[i], 5, 2);
   } else if (t == KL_ORACLE_E2M1) {
-    const uint8_t* s = (const uint8_t*)src;
-    for (int64_t i = 0; i < n; ++i) {
-      const uint32_t v = (s[i / 2] >> (4 * (i & 1))) & 0xF;
+    double table[16];
+    for (uint32_t v = 0; v < 16; ++v) {
       const double mag = (v & 6) == 0 ? 0.5 * (v & 1) : ldexp(1.0 + 0.5 * (v & 1), (int)((v >> 1) & 3) - 1);
-      dst[i] = (v & 8) ? -mag : mag;
+      table[v] = (v & 8) ? -mag : mag;
     }
+    const uint8_t* s = (const uint8_t*)src;
+    for (int64_t i = 0; i < n; ++i) dst[i] = table[(s[i / 2] >> (4 * (i & 1))) & 0xF];
   } else {
     const uint8_t* s = (const uint8_t*)src;
     for (int64_t i = 0; i < n; ++i) dst[i] = decode_e4m3(s[i]);
@@ -126,12 +127,18 @@ typedef struct {
   int64_t ldsfa;
 } job_t;
 
-static double e8m0(uint8_t s) { return s == 255 ? NAN : ldexp(1.0, (int)s - 127); }
+static double e8m0_table[256];
+static pthread_once_t e8m0_once = PTHREAD_ONCE_INIT;
+static void e8m0_init(void) {
+  for (int s = 0; s < 256; ++s) e8m0_table[s] = s == 255 ? NAN : ldexp(1.0, s - 127);
+}
+static double e8m0(uint8_t s) { return e8m0_table[s]; }
 
 /* Decode row `r` of a matrix (k elements) and apply its MX scales when `sf` is given. */
 static void decode_row(int t, const void* base, int64_t ld, int64_t r, int64_t k, const uint8_t* sf, int64_t ldsf,
                        double* out) {
   kl_oracle_decode(t, (const char*)base + bytes_of(t, r * ld), k, out);
+  pthread_once(&e8m0_once, e8m0_init);
   if (sf)
     for (int64_t kk = 0; kk < k; ++kk) out[kk] *= e8m0(sf[r * ldsf + kk / 32]);
 }
