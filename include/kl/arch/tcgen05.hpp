@@ -124,6 +124,27 @@ KL_DEVICE void umma_mxf4_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, u
         : "memory");
 }
 
+// NVFP4: packed e2m1 with one UE4M3 scale per 16 K-elements (kind::mxf4nvf4.block_scale.block16);
+// each MMA (64 elements) reads a whole 32-bit scale word of every row (scale-factor id 0).
+template <int CtaGroup>
+KL_DEVICE void umma_nvf4_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t sfa_tmem,
+                            uint32_t sfb_tmem, uint32_t accumulate) {
+  if constexpr (CtaGroup == 1)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+            d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+            d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+}
+
 // Shared memory -> TMEM copy of 32 rows x 128 bits, replicated into all four 32-lane quarters
 // (lane q*32 + i, columns [col, col + 4) receive row i). `src_desc` is a no-swizzle K-major
 // matrix descriptor of the 32 rows (16 bytes each, 8-row groups 128 bytes apart). Ordered with the

@@ -40,9 +40,9 @@ struct Problem {
   // 0: C = result. 1: C += result, by TMA reducing stores (fp32 add in the TMA unit, so fp32 C
   // only; every peer copy of C gets the same add; not with the direct-store epilogue).
   int c_reduce = 0;
-  // Block scaling (configs with kMx: MXFP8, or MXFP4 on packed fp4): UE8M0 scales of A and B, one
-  // per 32 K-elements of each row, in the 128 x 4 blocked layout: ceil(rows / 128) x ceil(K / 128)
-  // atoms of 512 bytes, row-block major.
+  // Block scaling (configs with kMx: MXFP8 / MXFP4 with UE8M0 scales per 32 K-elements, NVFP4 with
+  // UE4M3 scales per 16): scales of A and B in the 128 x 4 blocked layout, ceil(rows / 128) x
+  // ceil(K / (4 * vec)) atoms of 512 bytes, row-block major.
   const void* sfa = nullptr;
   const void* sfb = nullptr;
 };
@@ -202,8 +202,8 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
     if (pr.sfa == nullptr || pr.sfb == nullptr) throw std::invalid_argument("kl::gemm: MXFP8 needs scales of A and B");
     if (pr.batch > 1) throw std::invalid_argument("kl::gemm: MXFP8 is not batched");
     // The blocked scale arrays as [row blocks][K blocks][128 words of 4 bytes]; a box is the
-    // kSfAtomsK atoms of one stage (K blocks of 128 elements).
-    const int64_t kb = (pr.k + 127) / 128;
+    // kSfAtomsK atoms of one stage (K blocks of 4 * kSfVec elements).
+    const int64_t kb = (pr.k + 4 * Cfg::kSfVec - 1) / (4 * Cfg::kSfVec);  // K blocks of 4 scales
     auto sf_map = [&](CUtensorMap* map, void const* ptr, int64_t rows) {
       const int64_t shape[3] = {(rows + 127) / 128, kb, 128};
       const int64_t stride[3] = {kb * 128, 128, 1};

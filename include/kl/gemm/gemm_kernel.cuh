@@ -45,7 +45,7 @@ enum : int {
 };
 
 template <typename InT, typename OutT, int CtaGroup, int BlockN, int Stages, bool DirectStore = false,
-          bool AMn = false, bool BMn = false, class Sw = Swizzle128B, bool Mx = false>
+          bool AMn = false, bool BMn = false, class Sw = Swizzle128B, int SfVec = 0>
 struct TnConfig {
   using in_type = InT;
   using out_type = OutT;
@@ -60,25 +60,28 @@ struct TnConfig {
   static constexpr int kBlockK = 128 / int(sizeof(InT));  // 128 bytes of K per stage
   static constexpr int kUmmaK = 32 / int(sizeof(InT));    // K of one tcgen05.mma
   static constexpr int kStages = Stages;
-  // Block-scaled 8-bit inputs (MXFP8): one UE8M0 scale per 32 K-elements of every row of A and B,
-  // given in the 128 x 4 blocked layout (512-byte atoms: 128 rows x 4 scales, byte
-  // (r % 32) * 16 + (r / 32) * 4 + j for row r and K-group j). Each stage brings, by TMA, the atom
-  // of this CTA's 128 rows of A and the atoms of all the tile's rows of B (in both CTAs of a pair);
-  // the MMA thread moves them into TMEM (tcgen05.cp 32x128b.warpx4) ahead of the stage's
-  // block-scaled MMAs.
-  // Packed fp4 (e2m1x2, kind::mxf4): a stage's 128 bytes of K are 256 elements, so two scale atoms
-  // along K per 128 rows, and each MMA (64 elements) reads two scale bytes instead of one.
-  static constexpr bool kMx = Mx;
+  // Block scaling (SfVec = K-elements per scale: 0 = none, 32 = MX with UE8M0 scales, 16 = NVFP4
+  // with UE4M3 scales): one scale per SfVec K-elements of every row of A and B, given in the
+  // 128 x 4 blocked layout (512-byte atoms: 128 rows x 4 scales, byte (r % 32) * 16 + (r / 32) * 4
+  // + j for row r and K-group j). Each stage brings, by TMA, the atoms of this CTA's 128 rows of A
+  // and of all the tile's rows of B (in both CTAs of a pair); the MMA thread moves them into TMEM
+  // (tcgen05.cp 32x128b.warpx4) ahead of the stage's block-scaled MMAs. A stage holds 128 bytes of
+  // K: 128 elements for fp8 (one atom along K, one scale byte per MMA), 256 for packed fp4 (two
+  // atoms and two scale bytes per MMA with SfVec 32, four atoms and a whole scale word per MMA
+  // with SfVec 16).
+  static constexpr int kSfVec = SfVec;
+  static constexpr bool kMx = SfVec != 0;
+  static constexpr bool kNv = SfVec == 16;
   static constexpr bool kFp4 = std::is_same_v<InT, e2m1x2>;
-  static constexpr int kSfbAtoms = Mx ? BlockN / 128 : 0;   // 128-row scale blocks of B per tile
-  static constexpr int kSfAtomsK = Mx ? (kFp4 ? 2 : 1) : 0;  // scale atoms along K per stage
-  static constexpr int kMmasPerSfAtom = kFp4 ? 2 : 4;        // MMAs (32 bytes of K each) per atom
-  static constexpr uint32_t kSfIdStep = kFp4 ? 2u : 1u;      // scale bytes per MMA
+  static constexpr int kSfbAtoms = kMx ? BlockN / 128 : 0;   // 128-row scale blocks of B per tile
+  static constexpr int kSfAtomsK = kMx ? (kFp4 ? 256 : 128) / (4 * SfVec) : 0;  // atoms along K per stage
+  static constexpr int kMmasPerSfAtom = kMx ? 4 / kSfAtomsK : 1;  // MMAs (32 bytes of K each) per atom
+  static constexpr uint32_t kSfIdStep = 4u / uint32_t(kMmasPerSfAtom);  // scale bytes per MMA
   static constexpr uint32_t kSfaBytes = 512u * kSfAtomsK;
   static constexpr uint32_t kSfbBytes = 512u * kSfAtomsK * kSfbAtoms;
-  // Two TMEM accumulators (epilogue of tile i overlaps the MMAs of tile i + 1), except for MXFP8
-  // with 256 columns: 2 x 256 accumulator columns would leave none for the scales.
-  static constexpr int kNumAcc = (Mx && BlockN == 256) ? 1 : 2;
+  // Two TMEM accumulators (epilogue of tile i overlaps the MMAs of tile i + 1), except for block
+  // scaling with 256 columns: 2 x 256 accumulator columns would leave none for the scales.
+  static constexpr int kNumAcc = (kMx && BlockN == 256) ? 1 : 2;
   static constexpr int kAccCols = BlockN;              // fp32 accumulator columns per buffer
   static constexpr int kSfaCol = kAccCols * kNumAcc;   // TMEM columns of A's and B's scales
   static constexpr int kSfbCol = kSfaCol + 4 * kSfAtomsK;
@@ -125,7 +128,9 @@ struct TnConfig {
 
   static constexpr bool kIsF8 = sizeof(InT) == 1;
   static constexpr uint32_t idesc() {
-    if constexpr (Mx)
+    if constexpr (kNv)  // scale format bit 23: 0 = UE4M3
+      return mma_instr_desc_block_scaled<InT, InT, kTileM, BlockN>() & ~(1u << 23);
+    else if constexpr (kMx)
       return mma_instr_desc_block_scaled<InT, InT, kTileM, BlockN>();
     else
       return mma_instr_desc<InT, InT, float, kTileM, BlockN, AMn ? UmmaMajor::MN : UmmaMajor::K,
@@ -134,9 +139,10 @@ struct TnConfig {
   static constexpr uint32_t kIdesc = idesc();
 
   static_assert(kTmemUsed <= 512, "accumulators and scales exceed TMEM");
-  static_assert(!Mx || (sizeof(InT) == 1 && !AMn && !BMn && std::is_same_v<Sw, Swizzle128B> && BlockN % 128 == 0),
+  static_assert(!kMx || (sizeof(InT) == 1 && !AMn && !BMn && std::is_same_v<Sw, Swizzle128B> && BlockN % 128 == 0),
                 "block-scaled: 8-bit or packed fp4 K-major operands, 128-byte swizzle, tile N a multiple of 128");
-  static_assert(!kFp4 || Mx, "packed fp4 operands are block-scaled (kind::mxf4)");
+  static_assert(SfVec == 0 || SfVec == 32 || (SfVec == 16 && kFp4), "scales per 32 elements, or per 16 for fp4");
+  static_assert(!kFp4 || kMx, "packed fp4 operands are block-scaled (kind::mxf4 / mxf4nvf4)");
   static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
   static_assert(BlockN % (16 * CtaGroup) == 0 && BlockN <= 256, "UMMA N");
   static_assert(kCtaN % 8 == 0 && kCtaN <= 256, "B tile rows");
@@ -499,7 +505,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
               const uint32_t idesc = Cfg::kIdesc | (id << 29) | (id << 4);
               const uint32_t sfa_t = tmem_base + Cfg::kSfaCol + 4 * q;
               const uint32_t sfb_t = tmem_base + Cfg::kSfbCol + 4 * Cfg::kSfbAtoms * q;
-              if constexpr (Cfg::kFp4)
+              if constexpr (Cfg::kNv)
+                umma_nvf4_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16, idesc, sfa_t, sfb_t, accumulate);
+              else if constexpr (Cfg::kFp4)
                 umma_mxf4_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16, idesc, sfa_t, sfb_t, accumulate);
               else
                 umma_mxf8_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16, idesc, sfa_t, sfb_t, accumulate);

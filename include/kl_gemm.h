@@ -103,7 +103,9 @@ typedef struct kl_gemm_desc {
    * stages hold the same 128 bytes of K as two or four swizzle atoms (one TMA box each); bf16
    * inputs with bf16 or f32 C, K-major operands. */
   int32_t swizzle;
-  /* Block scaling. 0: none. 1 (MX): ab_type KL_E4M3, KL_E5M2 or KL_E2M1 with one UE8M0 scale (value
+  /* Block scaling. 2 (NVFP4): ab_type KL_E2M1 with one UE4M3 scale (an e4m3 value, sign 0) per 16
+   * K-elements, blocked by kl_pack_block_scales(vec 16); otherwise as for 1.
+   * 0: none. 1 (MX): ab_type KL_E4M3, KL_E5M2 or KL_E2M1 with one UE8M0 scale (value
    * 2^(s - 127)) per 32 consecutive K-elements of every row of A and of B, in `sfa` / `sfb`
    * (device), stored in the 128 x 4 blocked layout that kl_mx_pack_scales writes:
    * kl_mx_scale_bytes(rows, k) bytes. C = alpha * sum_k (A[m,k] sfa[m,k/32]) (B[n,k] sfb[n,k/32])
@@ -122,12 +124,18 @@ typedef struct kl_gemm_desc {
  * 512), and inside an atom the scale of row r, K-group j sits at byte (r % 32) * 16 + (r / 32) * 4
  * + j. Padding rows and K-groups hold 127 (a scale of 1). No counterpart in the reference. */
 
-/* Bytes of the blocked scale array for `rows` rows and `k` K-elements. */
-KL_API int64_t kl_mx_scale_bytes(int64_t rows, int64_t k);
+/* Bytes of the blocked scale array for `rows` rows and `k` K-elements, one scale per `vec` (32 for
+ * MX, 16 for NVFP4) elements: ceil(rows / 128) * ceil(k / (4 * vec)) * 512. */
+KL_API int64_t kl_block_scale_bytes(int64_t rows, int64_t k, int32_t vec);
+KL_API int64_t kl_mx_scale_bytes(int64_t rows, int64_t k); /* vec = 32 */
 
-/* Device: repack row-major UE8M0 scales src[rows][ceil(k / 32)] (row pitch ld_src bytes) into
- * the blocked layout at dst (kl_mx_scale_bytes(rows, k) bytes, 16-byte aligned). Stream-ordered. */
-KL_API kl_status kl_mx_pack_scales(const void* src, int64_t rows, int64_t k, int64_t ld_src, void* dst, void* stream);
+/* Device: repack row-major scales src[rows][ceil(k / vec)] (one byte each, row pitch ld_src
+ * bytes) into the blocked layout at dst (kl_block_scale_bytes bytes, 16-byte aligned); padding
+ * holds a scale of 1 (UE8M0 127 for vec 32, UE4M3 0x38 for vec 16). Stream-ordered. */
+KL_API kl_status kl_pack_block_scales(const void* src, int64_t rows, int64_t k, int32_t vec, int64_t ld_src,
+                                      void* dst, void* stream);
+KL_API kl_status kl_mx_pack_scales(const void* src, int64_t rows, int64_t k, int64_t ld_src, void* dst,
+                                   void* stream); /* vec = 32 */
 
 /* Library version: major * 10000 + minor * 100 + patch. */
 KL_API int32_t kl_version(void);

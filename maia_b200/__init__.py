@@ -34,7 +34,8 @@ EXPORTED = (
     "kl_tma_box_geometry", "kl_tma_box_position", "kl_umma_smem_desc", "kl_mma_instr_desc",
     "kl_make_tma_desc", "kl_gemm_skinny_noalloc", "kl_gemm_host", "kl_gemm_clock_probe", "kl_gemm_gather",
     "kl_ipc_get_handle", "kl_ipc_open_handle", "kl_ipc_close", "kl_umma_smem_desc_mn", "kl_mma_instr_desc_major",
-    "kl_mma_instr_desc_block_scaled", "kl_mx_scale_bytes", "kl_mx_pack_scales",
+    "kl_mma_instr_desc_block_scaled", "kl_mx_scale_bytes", "kl_mx_pack_scales", "kl_block_scale_bytes",
+    "kl_pack_block_scales",
 )
 
 
@@ -111,6 +112,8 @@ def lib() -> ctypes.CDLL:
             "kl_mma_instr_desc_block_scaled": (i32, [i32, i32, i32, i32, i32, i32, i32, P(u32)]),
             "kl_mx_scale_bytes": (i64, [i64, i64]),
             "kl_mx_pack_scales": (i32, [vp, i64, i64, i64, vp, vp]),
+            "kl_block_scale_bytes": (i64, [i64, i64, i32]),
+            "kl_pack_block_scales": (i32, [vp, i64, i64, i32, i64, vp, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -207,13 +210,15 @@ def _dtype_code(t) -> int:
 
 
 def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, group_m=0, max_ctas=0,
-              variant=0, prefetch=0, a_major=0, b_major=0, c_reduce=0, swizzle=0, sfa=None, sfb=None) -> GemmDesc:
+              variant=0, prefetch=0, a_major=0, b_major=0, c_reduce=0, swizzle=0, sfa=None, sfb=None,
+              scale_vec=32) -> GemmDesc:
     """Descriptor for C = alpha * A . B^T on torch CUDA tensors: A [M,K], B [N,K], C [M,N], or the
     batched forms A [L,M,K], B [L,N,K], C [L,M,N] (L independent GEMMs). a_major / b_major = 1
     pass the operand MN-major: `a` as the stored [K, M] (A transposed in memory), `b` as [K, N].
     c_reduce = 1 adds the result into C instead of overwriting it; swizzle picks the operand
     swizzle span in bytes (0 = 128, 64, 32). sfa / sfb (uint8 device tensors in the blocked layout of
-    mx_pack_scales) make it an MXFP8 GEMM: one UE8M0 scale per 32 K-elements of each row."""
+    pack_block_scales) make it a block-scaled GEMM: one UE8M0 scale per 32 K-elements of each row
+    (MX, scale_vec 32) or one UE4M3 scale per 16 (NVFP4, scale_vec 16, fp4 operands)."""
     for name, t in (("a", a), ("b", b), ("c", c)):
         if t.dim() not in (2, 3) or t.stride(-1) != 1:
             raise ValueError(f"{name} must be a 2-D or 3-D tensor with a contiguous last dimension")
@@ -237,13 +242,14 @@ def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, gr
                     scale_b=None if scale_b is None else scale_b.data_ptr(), algo=algo, group_m=group_m,
                     max_ctas=max_ctas, variant=variant, prefetch=prefetch, batch=batch, stride_a=bs[0],
                     stride_b=bs[1], stride_c=bs[2], a_major=a_major, b_major=b_major, c_reduce=int(c_reduce),
-                    swizzle=swizzle, block_scale=int(sfa is not None or sfb is not None),
+                    swizzle=swizzle,
+                    block_scale=0 if sfa is None and sfb is None else (2 if scale_vec == 16 else 1),
                     sfa=None if sfa is None else sfa.data_ptr(), sfb=None if sfb is None else sfb.data_ptr())
 
 
 def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
          group_m=0, max_ctas=0, variant=0, prefetch=0, a_major=0, b_major=0, accumulate=False, swizzle=0,
-         sfa=None, sfb=None, workspace=None, stream=None):
+         sfa=None, sfb=None, scale_vec=32, workspace=None, stream=None):
     """out = alpha * a @ b.T [* scale_a * scale_b] on the current CUDA stream, via kl_gemm.
     accumulate=True: out += alpha * a @ b.T (out must be given). sfa/sfb: MXFP8 block scales
     (see mx_pack_scales)."""
@@ -257,7 +263,7 @@ def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=Non
         shape = (a.shape[0], m, n) if a.dim() == 3 else (m, n)
         out = torch.empty(shape, dtype=out_dtype or torch.bfloat16, device=a.device)
     d = gemm_desc(a, b, out, alpha, scale_a, scale_b, algo, group_m, max_ctas, variant, prefetch, a_major, b_major,
-                  int(bool(accumulate)), swizzle, sfa, sfb)
+                  int(bool(accumulate)), swizzle, sfa, sfb, scale_vec)
     s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
     if workspace is None:
         check(lib().kl_gemm(ctypes.byref(d), ctypes.c_void_p(s)))
@@ -267,36 +273,45 @@ def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=Non
     return out
 
 
+def block_scale_bytes(rows: int, k: int, vec: int = 32) -> int:
+    """Bytes of the blocked scale array for `rows` rows of `k` K-elements, one scale per `vec`."""
+    return int(lib().kl_block_scale_bytes(int(rows), int(k), int(vec)))
+
+
 def mx_scale_bytes(rows: int, k: int) -> int:
-    """Bytes of the blocked MXFP8 scale array for `rows` rows of `k` K-elements."""
-    return int(lib().kl_mx_scale_bytes(int(rows), int(k)))
+    return block_scale_bytes(rows, k, 32)
 
 
-def mx_pack_scales(scales, k: int, out=None, stream=None):
-    """Repack row-major UE8M0 scales (uint8 device tensor [rows, ceil(k/32)], unit stride in its
-    last dimension) into the blocked layout the MXFP8 GEMM reads; returns the uint8 tensor."""
+def pack_block_scales(scales, k: int, vec: int = 32, out=None, stream=None):
+    """Repack row-major scales (uint8 device tensor [rows, ceil(k/vec)], unit stride in its last
+    dimension) into the blocked layout the block-scaled GEMMs read; returns the uint8 tensor."""
     import torch
 
     rows = scales.shape[0]
     if scales.dtype != torch.uint8 or scales.dim() != 2 or scales.stride(1) != 1:
         raise ValueError("scales must be a 2-D uint8 tensor with a contiguous last dimension")
     if out is None:
-        out = torch.empty(mx_scale_bytes(rows, k), dtype=torch.uint8, device=scales.device)
+        out = torch.empty(block_scale_bytes(rows, k, vec), dtype=torch.uint8, device=scales.device)
     s = stream if stream is not None else torch.cuda.current_stream(scales.device).cuda_stream
-    check(lib().kl_mx_pack_scales(ctypes.c_void_p(scales.data_ptr()), rows, int(k), scales.stride(0),
-                                  ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(s)))
+    check(lib().kl_pack_block_scales(ctypes.c_void_p(scales.data_ptr()), rows, int(k), int(vec), scales.stride(0),
+                                     ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(s)))
     return out
 
 
+def mx_pack_scales(scales, k: int, out=None, stream=None):
+    """pack_block_scales for MX (UE8M0 scales per 32 elements)."""
+    return pack_block_scales(scales, k, 32, out, stream)
+
+
 def gemm_host(a_host, b_host, c_host, a_dev, b_dev, c_dev, *, alpha=1.0, scale_a=None, scale_b=None,
-              algo=ALGO_AUTO, chunks=0, sfa=None, sfb=None, stream=None):
+              algo=ALGO_AUTO, chunks=0, sfa=None, sfb=None, scale_vec=32, stream=None):
     """c_host = alpha * a_host @ b_host.T with host (ideally pinned) tensors, through kl_gemm_host:
     the copies in and out overlap the GEMM. a_dev/b_dev/c_dev are device staging tensors of the
     same shapes; sfa/sfb: host MXFP8 scales in the blocked layout (staged by the library). Only
     queues the work on the stream: synchronise it before reading c_host."""
     import torch
 
-    d = gemm_desc(a_host, b_host, c_host, alpha, scale_a, scale_b, algo, sfa=sfa, sfb=sfb)
+    d = gemm_desc(a_host, b_host, c_host, alpha, scale_a, scale_b, algo, sfa=sfa, sfb=sfb, scale_vec=scale_vec)
     s = stream if stream is not None else torch.cuda.current_stream(a_dev.device).cuda_stream
     check(lib().kl_gemm_host(ctypes.byref(d), ctypes.c_void_p(a_dev.data_ptr()), ctypes.c_void_p(b_dev.data_ptr()),
                              ctypes.c_void_p(c_dev.data_ptr()), int(chunks), ctypes.c_void_p(s)))

@@ -96,13 +96,16 @@ kl_status run_tile(kl_gemm_desc const& d, Problem const& pr, bool pair, cudaStre
                    char const* who) {
   const bool a_mn = d.a_major == 1, b_mn = d.b_major == 1;
   if (d.block_scale != 0) {
-    if (d.block_scale != 1) return fail(KL_ERR_INVALID_ARGUMENT, std::string(who) + ": block_scale must be 0 or 1 (MX)");
+    if (d.block_scale != 1 && d.block_scale != 2)
+      return fail(KL_ERR_INVALID_ARGUMENT, std::string(who) + ": block_scale must be 0, 1 (MX) or 2 (NVFP4)");
     if (a_mn || b_mn || (d.swizzle != 0 && d.swizzle != 128) || pr.batch > 1)
       return fail(KL_ERR_NOT_SUPPORTED, std::string(who) + ": MXFP8 takes K-major operands, 128-byte swizzle, batch 1");
     bool handled = false;
-    kl_status s = kl::capi::run_tile_mx(d.ab_type, d.c_type, d.variant, pair, pr, stream, info, &handled);
+    kl_status s = kl::capi::run_tile_mx(d.block_scale, d.ab_type, d.c_type, d.variant, pair, pr, stream, info, &handled);
     if (handled) return s;
-    return fail(KL_ERR_NOT_SUPPORTED, std::string(who) + ": MXFP8 takes e4m3 or e5m2 inputs with bf16 or f32 C");
+    return fail(KL_ERR_NOT_SUPPORTED, std::string(who) + (d.block_scale == 2
+                                                              ? ": NVFP4 takes e2m1 inputs with bf16 or f32 C"
+                                                              : ": MX takes e4m3, e5m2 or e2m1 inputs with bf16 or f32 C"));
   }
   const int32_t sw = d.swizzle == 0 ? 128 : d.swizzle;
   if (sw != 128 && sw != 64 && sw != 32)

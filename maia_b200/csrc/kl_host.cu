@@ -2,7 +2,7 @@
 // device, then streams B in column blocks of C, so that the host-to-device copies of block j+1,
 // the GEMM of block j and the device-to-host copy of block j-1 run at the same time on three
 // streams (two copy engines and the SMs). Chained with events; ordered after and before the
-// caller's stream. MXFP8 problems (block_scale = 1) also stage the blocked scale arrays: A's whole,
+// caller's stream. Block-scaled problems (block_scale 1 or 2) also stage the blocked scale arrays: A's whole,
 // then B's row blocks along with each block of B.
 
 #include <cuda_runtime.h>
@@ -98,9 +98,10 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
   // Bytes of `elems` operand elements (packed fp4: two per byte).
   auto ab_bytes = [&](int64_t elems) { return size_t(h->ab_type == KL_E2M1 ? elems / 2 : elems * elem_bytes(h->ab_type)); };
   // MXFP8 scales: blocked arrays, A's then B's, in one staging buffer.
-  const int64_t sfa_bytes = mx ? kl_mx_scale_bytes(h->m, h->k) : 0;
-  const int64_t sfb_bytes = mx ? kl_mx_scale_bytes(h->n, h->k) : 0;
-  const int64_t sf_row_block = ((h->k + 127) / 128) * 512;  // bytes per 128 rows
+  const int32_t vec = h->block_scale == 2 ? 16 : 32;
+  const int64_t sfa_bytes = mx ? kl_block_scale_bytes(h->m, h->k, vec) : 0;
+  const int64_t sfb_bytes = mx ? kl_block_scale_bytes(h->n, h->k, vec) : 0;
+  const int64_t sf_row_block = ((h->k + 4 * vec - 1) / (4 * vec)) * 512;  // bytes per 128 rows
   if (mx && p->scale_bytes < size_t(sfa_bytes + sfb_bytes)) {
     if (p->scales != nullptr) {
       if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");

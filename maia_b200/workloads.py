@@ -222,6 +222,27 @@ def mx_quantize(x: np.ndarray, kind: str = "e4m3") -> tuple[np.ndarray, np.ndarr
     return enc(q), sbits
 
 
+def nv_quantize(x: np.ndarray) -> tuple[np.ndarray, np.ndarray, float]:
+    """NVFP4 quantisation of float32 rows: a per-tensor scale g = amax / (448 * 6), then per block
+    of 16 K-elements a UE4M3 scale s = e4m3(amax_block / (6 g)) (round to nearest, saturating),
+    elements e2m1(x / (s g)). Returns (packed e2m1 [rows, K/2], UE4M3 bits [rows, ceil(K/16)], g);
+    x ~ g * s * e2m1."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, k = x.shape
+    groups = -(-k // 16)
+    padded = np.zeros((rows, groups * 16), dtype=np.float32)
+    padded[:, :k] = x
+    amax = float(np.abs(x).max()) if x.size else 0.0
+    g = amax / (448.0 * 6.0) if amax > 0 else 1.0
+    bmax = np.abs(padded.reshape(rows, groups, 16)).max(axis=2)
+    sbits = f32_to_e4m3_bits((bmax / (6.0 * g)).astype(np.float32)) & np.uint8(0x7F)
+    s = e4m3_values()[sbits].astype(np.float64)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        inv = np.where(s > 0, 1.0 / (s * g), 0.0)
+    q = (padded.reshape(rows, groups, 16) * inv[:, :, None]).reshape(rows, groups * 16)[:, :k].astype(np.float32)
+    return pack_e2m1(f32_to_e2m1_codes(q)), sbits, g
+
+
 def draw(w: Workload, tensor_id: int, rows: int, cols: int, scale: float) -> np.ndarray:
     rng = np.random.Generator(np.random.PCG64(w.seed * 1000 + tensor_id))
     if w.dist == "uniform":

@@ -41,11 +41,11 @@ def lib():
         L.kl_oracle_gemm_f32.restype = i32
         L.kl_oracle_decode.argtypes = [i32, vp, i64, vp]
         L.kl_oracle_decode.restype = None
-        mx = [i32, vp, i64, vp, i64, i64, i64, i64, vp, i64, vp, i64, dbl, vp, i64, i32]
-        L.kl_oracle_gemm_mx_f64.argtypes = mx
-        L.kl_oracle_gemm_mx_f64.restype = i32
-        L.kl_oracle_gemm_mx_f32.argtypes = mx
-        L.kl_oracle_gemm_mx_f32.restype = i32
+        bs = [i32, vp, i64, vp, i64, i64, i64, i64, vp, i64, vp, i64, i32, i32, dbl, vp, i64, i32]
+        L.kl_oracle_gemm_bs_f64.argtypes = bs
+        L.kl_oracle_gemm_bs_f64.restype = i32
+        L.kl_oracle_gemm_bs_f32.argtypes = bs
+        L.kl_oracle_gemm_bs_f32.restype = i32
         _lib = L
     return _lib
 
@@ -115,16 +115,16 @@ def e8m0_values(s: np.ndarray) -> np.ndarray:
     return np.where(s == 255, np.nan, np.exp2(s - 127.0))
 
 
-def _mx_call(fn, out_dtype, a, b, sfa, sfb, kind, scale, threads):
+def _mx_call(fn, out_dtype, a, b, sfa, sfb, kind, scale, threads, vec=32, sf_format="ue8m0"):
     a, b = np.ascontiguousarray(a), np.ascontiguousarray(b)
     sfa, sfb = np.ascontiguousarray(sfa, dtype=np.uint8), np.ascontiguousarray(sfb, dtype=np.uint8)
     m, k = a.shape[0], a.shape[1] * _per_unit(kind)
     n = b.shape[0]
-    groups = -(-k // 32)
+    groups = -(-k // vec)
     assert sfa.shape == (m, groups) and sfb.shape == (n, groups) and b.shape[1] == a.shape[1]
     c = np.empty((m, n), dtype=out_dtype)
     rc = fn(_kind(a, kind), a.ctypes.data, k, b.ctypes.data, k, m, n, k, sfa.ctypes.data, groups, sfb.ctypes.data,
-            groups, float(scale), c.ctypes.data, n, threads or threads_default())
+            groups, int(vec), int(sf_format == "ue4m3"), float(scale), c.ctypes.data, n, threads or threads_default())
     assert rc == 0
     return c
 
@@ -135,23 +135,36 @@ def gemm_mx_f64(a: np.ndarray, b: np.ndarray, sfa: np.ndarray, sfb: np.ndarray, 
 
     a, b: raw 8-bit element bits [M,K] / [N,K]; sfa, sfb: UE8M0 bits [M, ceil(K/32)] /
     [N, ceil(K/32)], one scale per 32 consecutive K-elements (the OCP MX block size)."""
-    return _mx_call(lib().kl_oracle_gemm_mx_f64, np.float64, a, b, sfa, sfb, kind, scale, threads)
+    return _mx_call(lib().kl_oracle_gemm_bs_f64, np.float64, a, b, sfa, sfb, kind, scale, threads)
 
 
 def gemm_mx_f32(a: np.ndarray, b: np.ndarray, sfa: np.ndarray, sfb: np.ndarray, kind=None,
                 scale: float = 1.0, threads: int | None = None) -> np.ndarray:
     """The same with fp32 accumulation (the timed CPU baseline of the MX workload)."""
-    return _mx_call(lib().kl_oracle_gemm_mx_f32, np.float32, a, b, sfa, sfb, kind, scale, threads)
+    return _mx_call(lib().kl_oracle_gemm_bs_f32, np.float32, a, b, sfa, sfb, kind, scale, threads)
 
 
-def pack_mx_scales(sf: np.ndarray, k: int) -> np.ndarray:
-    """The blocked scale layout of the MXFP8 GEMM, restated: rows in blocks of 128 and K in blocks
-    of 128 elements (4 scales) form 512-byte atoms stored row-block major; inside an atom the scale
-    of row r, K-group j is byte (r % 32) * 16 + (r / 32) * 4 + j. Padding holds 127 (a scale of 1).
-    This is the 128 x 4 scale-factor atom of CUTLASS's Sm1xxBlockScaledBasicChunk (K-major)."""
+def gemm_nv_f64(a: np.ndarray, b: np.ndarray, sfa: np.ndarray, sfb: np.ndarray, scale: float = 1.0,
+                threads: int | None = None) -> np.ndarray:
+    """NVFP4 product in fp64: packed e2m1 A [M, K/2], B [N, K/2] with UE4M3 scales [rows,
+    ceil(K/16)], one per 16 consecutive K-elements (an e4m3 byte read as a magnitude), times the
+    product of the per-tensor scales `scale`."""
+    return _mx_call(lib().kl_oracle_gemm_bs_f64, np.float64, a, b, sfa, sfb, "e2m1", scale, threads, 16, "ue4m3")
+
+
+def gemm_nv_f32(a, b, sfa, sfb, scale: float = 1.0, threads: int | None = None) -> np.ndarray:
+    return _mx_call(lib().kl_oracle_gemm_bs_f32, np.float32, a, b, sfa, sfb, "e2m1", scale, threads, 16, "ue4m3")
+
+
+def pack_mx_scales(sf: np.ndarray, k: int, vec: int = 32) -> np.ndarray:
+    """The blocked scale layout of the block-scaled GEMMs, restated: rows in blocks of 128 and K in
+    blocks of 4 scales (4 * vec elements) form 512-byte atoms stored row-block major; inside an atom
+    the scale of row r, K-group j is byte (r % 32) * 16 + (r / 32) * 4 + j. Padding holds a scale of
+    1 (UE8M0 127 for vec 32, UE4M3 0x38 for vec 16). This is the 128 x 4 scale-factor atom of
+    CUTLASS's Sm1xxBlockScaledBasicChunk (K-major)."""
     rows, groups = sf.shape
-    rb, kb = -(-rows // 128), -(-k // 128)
-    full = np.full((rb * 128, kb * 4), 127, dtype=np.uint8)
+    rb, kb = -(-rows // 128), -(-k // (4 * vec))
+    full = np.full((rb * 128, kb * 4), 127 if vec == 32 else 0x38, dtype=np.uint8)
     full[:rows, :groups] = sf
     t = full.reshape(rb, 4, 32, kb, 4)                  # (row block, r / 32, r % 32, K block, j)
     return np.ascontiguousarray(t.transpose(0, 3, 2, 1, 4)).reshape(-1)

@@ -19,6 +19,9 @@
  *   kl_oracle_gemm_mx_f64 / _f32   the same with MX block scaling (OCP Microscaling Formats v1.0):
  *                        element k of row r of A is multiplied by 2^(sfa[r][k/32] - 127) (UE8M0,
  *                        one scale per 32 consecutive K-elements; 255 is NaN), likewise for B.
+ *   kl_oracle_gemm_bs_f64 / _f32   block scaling with `vec` elements per scale and the scale
+ *                        format given: UE8M0 as above, or UE4M3 (NVFP4: an e4m3 byte read as a
+ *                        magnitude, one scale per 16 K-elements).
  *
  * Element decoding follows the formats' definitions: bf16 is the top half of an IEEE binary32;
  * f16 is IEEE binary16 (1 sign, 5 exponent bits with bias 15, 10 mantissa bits); e4m3 (OCP FP8,
@@ -123,8 +126,10 @@ typedef struct {
   int64_t row_begin, row_end;
   const double* bdec; /* decoded B, n x k (f64 path) */
   const float* bdecf; /* decoded B, n x k (f32 path) */
-  const uint8_t* sfa; /* optional MX scales of A, row-major [m][ldsfa] */
+  const uint8_t* sfa; /* optional block scales of A, row-major [m][ldsfa] */
   int64_t ldsfa;
+  int vec;            /* K-elements per scale */
+  int sf_ue4m3;       /* scale format: 0 = UE8M0, 1 = UE4M3 */
 } job_t;
 
 static double e8m0_table[256];
@@ -134,13 +139,18 @@ static void e8m0_init(void) {
 }
 static double e8m0(uint8_t s) { return e8m0_table[s]; }
 
-/* Decode row `r` of a matrix (k elements) and apply its MX scales when `sf` is given. */
+static double ue4m3(uint8_t s) { return decode_e4m3((uint8_t)(s & 0x7F)); }
+
+/* Decode row `r` of a matrix (k elements) and apply its block scales when `sf` is given. */
 static void decode_row(int t, const void* base, int64_t ld, int64_t r, int64_t k, const uint8_t* sf, int64_t ldsf,
-                       double* out) {
+                       int vec, int sf_ue4m3, double* out) {
   kl_oracle_decode(t, (const char*)base + bytes_of(t, r * ld), k, out);
   pthread_once(&e8m0_once, e8m0_init);
   if (sf)
-    for (int64_t kk = 0; kk < k; ++kk) out[kk] *= e8m0(sf[r * ldsf + kk / 32]);
+    for (int64_t kk = 0; kk < k; ++kk) {
+      const uint8_t v = sf[r * ldsf + kk / vec];
+      out[kk] *= sf_ue4m3 ? ue4m3(v) : e8m0(v);
+    }
 }
 
 static void* f64_rows(void* arg) {
@@ -148,7 +158,7 @@ static void* f64_rows(void* arg) {
   double* arow = (double*)malloc(sizeof(double) * (size_t)j->k);
   double* c = (double*)j->c;
   for (int64_t i = j->row_begin; i < j->row_end; ++i) {
-    decode_row(j->t, j->a, j->lda, i, j->k, j->sfa, j->ldsfa, arow);
+    decode_row(j->t, j->a, j->lda, i, j->k, j->sfa, j->ldsfa, j->vec, j->sf_ue4m3, arow);
     for (int64_t col = 0; col < j->n; ++col) {
       const double* brow = j->bdec + (size_t)col * (size_t)j->k;
       double s0 = 0, s1 = 0, s2 = 0, s3 = 0;
@@ -176,24 +186,31 @@ static int clamp_threads(int threads, int64_t rows) {
 
 /* c[i*ldc + j] = scale * sum_k A[i,k] * B[j,k] in double, for rows [0, m); with sfa / sfb (MX
  * scales, row-major, row pitch ldsfa / ldsfb) each element is scaled first. Returns 0 on success. */
-int kl_oracle_gemm_mx_f64(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
-                          int64_t k, const uint8_t* sfa, int64_t ldsfa, const uint8_t* sfb, int64_t ldsfb,
-                          double scale, double* c, int64_t ldc, int threads) {
+int kl_oracle_gemm_bs_f64(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                          int64_t k, const uint8_t* sfa, int64_t ldsfa, const uint8_t* sfb, int64_t ldsfb, int vec,
+                          int sf_ue4m3, double scale, double* c, int64_t ldc, int threads) {
+  if (vec <= 0) return 2;
   double* bdec = (double*)malloc(sizeof(double) * (size_t)n * (size_t)(k > 0 ? k : 1));
   if (!bdec) return 1;
-  for (int64_t r = 0; r < n; ++r) decode_row(t, b, ldb, r, k, sfb, ldsfb, bdec + r * k);
+  for (int64_t r = 0; r < n; ++r) decode_row(t, b, ldb, r, k, sfb, ldsfb, vec, sf_ue4m3, bdec + r * k);
   threads = clamp_threads(threads, m);
   pthread_t tid[512];
   job_t jobs[512];
   for (int w = 0; w < threads; ++w) {
     job_t j = {t, a, lda, b, ldb, m, n, k, scale, c, ldc, m * w / threads, m * (w + 1) / threads, bdec, NULL,
-               sfa, ldsfa};
+               sfa, ldsfa, vec, sf_ue4m3};
     jobs[w] = j;
     pthread_create(&tid[w], NULL, f64_rows, &jobs[w]);
   }
   for (int w = 0; w < threads; ++w) pthread_join(tid[w], NULL);
   free(bdec);
   return 0;
+}
+
+int kl_oracle_gemm_mx_f64(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                          int64_t k, const uint8_t* sfa, int64_t ldsfa, const uint8_t* sfb, int64_t ldsfb,
+                          double scale, double* c, int64_t ldc, int threads) {
+  return kl_oracle_gemm_bs_f64(t, a, lda, b, ldb, m, n, k, sfa, ldsfa, sfb, ldsfb, 32, 0, scale, c, ldc, threads);
 }
 
 int kl_oracle_gemm_f64(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
@@ -213,7 +230,7 @@ static void* f32_rows(void* arg) {
   for (int64_t i0 = j->row_begin; i0 < j->row_end; i0 += 4) {
     const int64_t ni = (j->row_end - i0) < 4 ? (j->row_end - i0) : 4;
     for (int64_t r = 0; r < ni; ++r) {
-      decode_row(j->t, j->a, j->lda, i0 + r, k, j->sfa, j->ldsfa, tmp);
+      decode_row(j->t, j->a, j->lda, i0 + r, k, j->sfa, j->ldsfa, j->vec, j->sf_ue4m3, tmp);
       for (int64_t kk = 0; kk < k; ++kk) ablk[r * k + kk] = (float)tmp[kk];
     }
     for (int64_t r = ni; r < 4; ++r) memset(ablk + r * k, 0, sizeof(float) * (size_t)k);
@@ -238,14 +255,15 @@ static void* f32_rows(void* arg) {
   return NULL;
 }
 
-int kl_oracle_gemm_mx_f32(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
-                          int64_t k, const uint8_t* sfa, int64_t ldsfa, const uint8_t* sfb, int64_t ldsfb,
-                          double scale, float* c, int64_t ldc, int threads) {
+int kl_oracle_gemm_bs_f32(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                          int64_t k, const uint8_t* sfa, int64_t ldsfa, const uint8_t* sfb, int64_t ldsfb, int vec,
+                          int sf_ue4m3, double scale, float* c, int64_t ldc, int threads) {
+  if (vec <= 0) return 2;
   float* bdec = (float*)malloc(sizeof(float) * (size_t)n * (size_t)(k > 0 ? k : 1));
   double* tmp = (double*)malloc(sizeof(double) * (size_t)(k > 0 ? k : 1));
   if (!bdec || !tmp) return 1;
   for (int64_t r = 0; r < n; ++r) {
-    decode_row(t, b, ldb, r, k, sfb, ldsfb, tmp);
+    decode_row(t, b, ldb, r, k, sfb, ldsfb, vec, sf_ue4m3, tmp);
     for (int64_t kk = 0; kk < k; ++kk) bdec[r * k + kk] = (float)tmp[kk];
   }
   free(tmp);
@@ -257,13 +275,19 @@ int kl_oracle_gemm_mx_f32(int t, const void* a, int64_t lda, const void* b, int6
     int64_t b0 = ((m + 3) / 4) * w / threads * 4, b1 = ((m + 3) / 4) * (w + 1) / threads * 4;
     if (b1 > m) b1 = m;
     if (b0 > m) b0 = m;
-    job_t j = {t, a, lda, b, ldb, m, n, k, scale, c, ldc, b0, b1, NULL, bdec, sfa, ldsfa};
+    job_t j = {t, a, lda, b, ldb, m, n, k, scale, c, ldc, b0, b1, NULL, bdec, sfa, ldsfa, vec, sf_ue4m3};
     jobs[w] = j;
     pthread_create(&tid[w], NULL, f32_rows, &jobs[w]);
   }
   for (int w = 0; w < threads; ++w) pthread_join(tid[w], NULL);
   free(bdec);
   return 0;
+}
+
+int kl_oracle_gemm_mx_f32(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                          int64_t k, const uint8_t* sfa, int64_t ldsfa, const uint8_t* sfb, int64_t ldsfb,
+                          double scale, float* c, int64_t ldc, int threads) {
+  return kl_oracle_gemm_bs_f32(t, a, lda, b, ldb, m, n, k, sfa, ldsfa, sfb, ldsfb, 32, 0, scale, c, ldc, threads);
 }
 
 int kl_oracle_gemm_f32(int t, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,

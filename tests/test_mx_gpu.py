@@ -164,3 +164,43 @@ def test_mx_limits(cuda):
     with pytest.raises(kl.KlError) as e:
         kl.gemm(ab, ab, c, sfa=s, sfb=s)
     assert e.value.status == kl.KL_ERR_NOT_SUPPORTED
+
+
+@pytest.mark.parametrize("rows,k", [(1, 16), (128, 64), (200, 320), (129, 1000)])
+def test_pack_scales_nvfp4_layout(cuda, rows, k):
+    rng = np.random.default_rng(rows + 3 * k)
+    sf = rng.integers(0, 127, (rows, -(-k // 16)), dtype=np.uint8)
+    got = kl.pack_block_scales(torch.from_numpy(sf).to(cuda), k, 16).cpu().numpy()
+    assert got.size == kl.block_scale_bytes(rows, k, 16)
+    np.testing.assert_array_equal(got, og.pack_mx_scales(sf, k, 16))
+
+
+def run_nv(m, n, k, out, device, seed, **kw):
+    rng = np.random.Generator(np.random.PCG64(seed))
+    qa, sa, ga = wl.nv_quantize(rng.standard_normal((m, k), dtype=np.float32))
+    qb, sb, gb = wl.nv_quantize(rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.1))
+    a, b = to_device(qa, "e2m1", device), to_device(qb, "e2m1", device)
+    psa = kl.pack_block_scales(torch.from_numpy(sa).to(device), k, 16)
+    psb = kl.pack_block_scales(torch.from_numpy(sb).to(device), k, 16)
+    c = torch.full((m, n), float("nan"), dtype=TORCH_TYPES[out], device=device)
+    dga = torch.tensor([ga], dtype=torch.float32, device=device)
+    dgb = torch.tensor([gb], dtype=torch.float32, device=device)
+    kl.gemm(a, b, c, sfa=psa, sfb=psb, scale_vec=16, scale_a=dga, scale_b=dgb, **kw)
+    torch.cuda.synchronize()
+    assert kl.read_status() == 0, "a device-side wait timed out"
+    ref = og.gemm_nv_f64(qa, qb, sa, sb, ga * gb)
+    return c.float().cpu().numpy(), ref
+
+
+@KERNELS
+@pytest.mark.parametrize("out", ["bf16", "f32"])
+@pytest.mark.parametrize("shape", [(128, 256, 256), (200, 304, 320), (256, 512, 1024), (1000, 1000, 1024),
+                                   (130, 264, 96)])
+def test_nvfp4_gemm(cuda, algo, variant, out, shape):
+    """NVFP4: packed e2m1 with UE4M3 scales per 16 elements and per-tensor fp32 scales
+    (kind::mxf4nvf4.block16: four scale atoms along K per stage, a whole scale word per MMA)."""
+    m, n, k = shape
+    c, ref = run_nv(m, n, k, out, cuda, seed=m + 7 * n + k, algo=algo, variant=variant)
+    assert not np.isnan(c).any()
+    elem, norm = og.rel_error(c, ref)
+    assert norm <= FP8_TOL and elem <= FP8_TOL, f"normwise {norm:.3e}, element-wise {elem:.3e}"
