@@ -107,7 +107,9 @@ def cpu_baseline(w, budget_s: float = 6.0):
     while True:
         a, b, sa, sb = wl.make_inputs(w, rows_a=rows)
         t0 = time.perf_counter()
-        if w.dtype in ("mxfp8", "mxfp4"):
+        if w.dtype == "nvfp4":
+            og.gemm_nv_f32(a, b, sa[0], sb[0], sa[1] * sb[1], threads=threads)
+        elif w.dtype in ("mxfp8", "mxfp4"):
             og.gemm_mx_f32(a, b, sa, sb, "e4m3" if w.dtype == "mxfp8" else "e2m1", threads=threads)
         else:
             og.gemm_f32(a, b, sa * sb, threads=threads)
@@ -188,12 +190,18 @@ def main():
     a_bits, b_bits, sa, sb = wl.make_inputs(w)
     n_lo, n_hi = sharding.shard_range(w.n, world, rank, align=256)
     b_bits = np.ascontiguousarray(b_bits[n_lo:n_hi])
-    mx = w.dtype in ("mxfp8", "mxfp4")
+    mx = w.dtype in ("mxfp8", "mxfp4", "nvfp4")
+    vec = 16 if w.dtype == "nvfp4" else 32
+    gscale = None
+    if w.dtype == "nvfp4":  # (block scales, per-tensor scale) pairs
+        (sa, ga), (sb, gb) = sa, sb
+        gscale = (ga, gb)
     if mx:
         sb = np.ascontiguousarray(sb[n_lo:n_hi])
     nshard = n_hi - n_lo
     np_view = np.int16 if w.dtype == "bf16" else np.uint8
-    tdt = {"bf16": torch.bfloat16, "mxfp4": torch.float4_e2m1fn_x2}.get(w.dtype, torch.float8_e4m3fn)
+    tdt = {"bf16": torch.bfloat16, "mxfp4": torch.float4_e2m1fn_x2, "nvfp4": torch.float4_e2m1fn_x2}.get(
+        w.dtype, torch.float8_e4m3fn)
     odt = torch.bfloat16 if w.out == "bf16" else torch.float32
     a_host = torch.from_numpy(a_bits.view(np_view)).view(tdt).pin_memory()
     b_host = torch.from_numpy(b_bits.view(np_view)).view(tdt).pin_memory()
@@ -207,15 +215,18 @@ def main():
     if w.dtype == "e4m3":
         scale_a = torch.tensor([sa], dtype=torch.float32, device=dev)
         scale_b = torch.tensor([sb], dtype=torch.float32, device=dev)
+    if gscale is not None:
+        scale_a = torch.tensor([gscale[0]], dtype=torch.float32, device=dev)
+        scale_b = torch.tensor([gscale[1]], dtype=torch.float32, device=dev)
     if mx:
-        # MX block scales, repacked on the device into the blocked layout (untimed setup).
-        sfa = kl.mx_pack_scales(torch.from_numpy(sa).to(dev), w.k)
-        sfb = kl.mx_pack_scales(torch.from_numpy(sb).to(dev), w.k)
+        # Block scales, repacked on the device into the blocked layout (untimed setup).
+        sfa = kl.pack_block_scales(torch.from_numpy(sa).to(dev), w.k, vec)
+        sfb = kl.pack_block_scales(torch.from_numpy(sb).to(dev), w.k, vec)
         sfa_host = sfa.cpu().pin_memory()
         sfb_host = sfb.cpu().pin_memory()
     stream = torch.cuda.current_stream(dev)
     kw = dict(scale_a=scale_a, scale_b=scale_b, algo=args.algo, group_m=args.group_m, prefetch=args.prefetch,
-              variant=args.variant, max_ctas=args.max_ctas, sfa=sfa, sfb=sfb)
+              variant=args.variant, max_ctas=args.max_ctas, sfa=sfa, sfb=sfb, scale_vec=vec)
 
     def step():
         kl.gemm(a, b, c, **kw)
@@ -247,7 +258,7 @@ def main():
         # One more launch, right after the timed ones, with every CTA stamping clock64 and
         # %globaltimer: the SM clock the kernel really ran at (NVML may report the boost target).
         in_kernel = kl.clock_probe(a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo, group_m=args.group_m,
-                                   sfa=sfa, sfb=sfb)
+                                   sfa=sfa, sfb=sfb, scale_vec=vec)
     if kl.read_status() != 0:
         raise RuntimeError("a device-side wait timed out during the benchmark")
     dev_ms = max_over_ranks(dev_ms)
@@ -263,7 +274,7 @@ def main():
     def e2e_step():
         # The host-buffer entry point: copies in, GEMM and copy out, pipelined over column blocks.
         kl.gemm_host(a_host, b_host, c_host, a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo,
-                     sfa=sfa_host, sfb=sfb_host)
+                     sfa=sfa_host, sfb=sfb_host, scale_vec=vec)
 
     for _ in range(max(args.warmup, 3)):
         e2e_step()
@@ -303,7 +314,8 @@ def main():
         peers = shared.peer_ptrs(n_lo)
 
         def fused_step():
-            kl.gemm_gather(a, b, c_view, peers, scale_a=scale_a, scale_b=scale_b, algo=args.algo, sfa=sfa, sfb=sfb)
+            kl.gemm_gather(a, b, c_view, peers, scale_a=scale_a, scale_b=scale_b, algo=args.algo, sfa=sfa, sfb=sfb,
+                           scale_vec=vec)
 
         for _ in range(max(args.warmup, 3)):
             fused_step()
@@ -326,16 +338,16 @@ def main():
     if memory_bound:
         # Decode shapes: every operand byte moved once, against the measured copy bandwidth.
         alg_bytes = int((w.m * w.k + nshard * w.k) * w.in_bytes) + w.m * nshard * w.out_bytes + \
-            (w.m + nshard) * -(-w.k // 32) * (w.dtype in ("mxfp8", "mxfp4"))
+            (w.m + nshard) * -(-w.k // vec) * mx
         roofline = {"bound": "hbm", "achieved": alg_bytes / (dev_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
                     "unit": "GB/s", "peak_source": f"{peak_src} hbm_gbs", "algorithmic_bytes_per_launch": alg_bytes}
     else:
-        peak = peaks["bf16_tflops"] * {"bf16": 1.0, "mxfp4": 4.0}.get(w.dtype, 2.0)
+        peak = peaks["bf16_tflops"] * {"bf16": 1.0, "mxfp4": 4.0, "nvfp4": 4.0}.get(w.dtype, 2.0)
         roofline = {"bound": "tensor", "achieved": per_rank_flops / (dev_ms * 1e-3) / 1e12, "peak": peak,
                     "unit": "TFLOP/s",
                     "peak_source": f"{peak_src} " + ("bf16_tflops (burst)" if w.dtype == "bf16" else
                                                      "4 x bf16_tflops (burst; the dense fp4 rate is four times bf16)"
-                                                     if w.dtype == "mxfp4" else
+                                                     if w.dtype in ("mxfp4", "nvfp4") else
                                                      "2 x bf16_tflops (burst; the fp8 and MXFP8 dense rate is "
                                                      "twice bf16)"),
                     "algorithmic_flops_per_launch": per_rank_flops}

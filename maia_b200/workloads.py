@@ -22,7 +22,7 @@ class Workload:
     m: int
     n: int
     k: int
-    dtype: str          # "bf16", "e4m3", "mxfp8" (e4m3 elements with MX block scales) or "mxfp4" (e2m1)
+    dtype: str          # "bf16", "e4m3", "mxfp8" (e4m3 elements with MX block scales), "mxfp4" or "nvfp4" (e2m1)
     out: str            # "bf16" or "f32"
     dist: str           # "uniform" (on [-1, 1]) or "normal"
     a_scale: float      # multiplier of A's standard normal (normal) draws
@@ -35,11 +35,13 @@ class Workload:
 
     @property
     def in_bytes(self) -> float:
-        return 2 if self.dtype == "bf16" else 0.5 if self.dtype == "mxfp4" else 1
+        return 2 if self.dtype == "bf16" else 0.5 if self.dtype in ("mxfp4", "nvfp4") else 1
 
     @property
     def scale_bytes(self) -> int:
         """MX block scales: one byte per 32 K-elements of every row of A and B."""
+        if self.dtype == "nvfp4":
+            return (self.m + self.n) * -(-self.k // 16)
         return (self.m + self.n) * -(-self.k // 32) if self.dtype in ("mxfp8", "mxfp4") else 0
 
     @property
@@ -64,8 +66,9 @@ C3MX = Workload("c3mx_8192_mxfp8", 8192, 8192, 8192, "mxfp8", "bf16", "normal", 
 # The same shapes in MXFP4 (packed e2m1 elements, UE8M0 scales per 32).
 C3MXF4 = Workload("c3mxf4_8192_mxfp4", 8192, 8192, 8192, "mxfp4", "bf16", "normal", 0.02, 0.02, 2)
 C4MXF4 = Workload("c4mxf4_16384x16384x8192_mxfp4", 16384, 16384, 8192, "mxfp4", "bf16", "normal", 1.0, 1.0, 3)
+C3NVF4 = Workload("c3nvf4_8192_nvfp4", 8192, 8192, 8192, "nvfp4", "bf16", "normal", 0.02, 0.02, 2)
 
-ALL = {w.name: w for w in (C1, C2, C3, C4, C4MX, C3MX, C3MXF4, C4MXF4, *C5.values())}
+ALL = {w.name: w for w in (C1, C2, C3, C4, C4MX, C3MX, C3MXF4, C4MXF4, C3NVF4, *C5.values())}
 
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
@@ -256,12 +259,17 @@ def draw(w: Workload, tensor_id: int, rows: int, cols: int, scale: float) -> np.
 
 def make_inputs(w: Workload, rows_a: int | None = None):
     """(A bits, B bits, scale_a, scale_b). rows_a limits A to its first rows (a bounded CPU sample).
-    For mxfp8 the scales are the row-major UE8M0 arrays [rows, ceil(K/32)] of A and B."""
+    For mxfp8 / mxfp4 the scales are the row-major UE8M0 arrays [rows, ceil(K/32)] of A and B; for
+    nvfp4 they are (UE4M3 array [rows, ceil(K/16)], per-tensor fp32 scale) pairs."""
     ra = w.m if rows_a is None else min(rows_a, w.m)
     xa = draw(w, 0, w.m, w.k, w.a_scale)[:ra] if rows_a is not None else draw(w, 0, w.m, w.k, w.a_scale)
     xb = draw(w, 1, w.n, w.k, w.b_scale)
     if w.dtype == "bf16":
         return f32_to_bf16_bits(xa), f32_to_bf16_bits(xb), 1.0, 1.0
+    if w.dtype == "nvfp4":
+        qa, sfa, ga = nv_quantize(xa)
+        qb, sfb, gb = nv_quantize(xb)
+        return qa, qb, (sfa, ga), (sfb, gb)
     if w.dtype in ("mxfp8", "mxfp4"):
         kind = "e4m3" if w.dtype == "mxfp8" else "e2m1"
         qa, sfa = mx_quantize(xa, kind)
