@@ -17,3 +17,15 @@ def test_fake_tensor_shapes():
         s = torch.empty((1,), dtype=torch.float32)
         c8 = torch.ops.kl.gemm_fp8(a8, b8, s, s)
         assert c8.shape == (8, 24) and c8.dtype == torch.bfloat16
+
+
+def test_fake_block_scaled_shapes():
+    import maia_b200.torch_ops  # noqa: F401
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        a = torch.empty((256, 64), dtype=torch.float4_e2m1fn_x2)   # K = 128 packed
+        b = torch.empty((128, 64), dtype=torch.float4_e2m1fn_x2)
+        sf = torch.empty((1024,), dtype=torch.uint8)
+        c = torch.ops.kl.gemm_block_scaled(a, b, sf, sf, 16, torch.float32)
+        assert c.shape == (256, 128) and c.dtype == torch.float32

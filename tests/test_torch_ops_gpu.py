@@ -33,3 +33,37 @@ def test_kl_gemm_fp8_op(cuda):
     b = (xb / sb).to(torch.float8_e4m3fn)
     ref = (a.float() @ b.float().T) * sa * sb
     assert rel(torch.ops.kl.gemm_fp8(a, b, sa.reshape(1), sb.reshape(1)), ref) < 5e-2
+
+
+@pytest.mark.parametrize("kind,vec", [("e4m3", 32), ("e2m1", 32), ("e2m1", 16)])
+def test_kl_gemm_block_scaled_op(cuda, kind, vec):
+    """torch.ops.kl.gemm_block_scaled against the fp64 oracle (MXFP8, MXFP4, NVFP4)."""
+    import numpy as np
+
+    import maia_b200 as kl
+    import maia_b200.torch_ops  # noqa: F401
+    from maia_b200 import workloads as wl
+    from oracle import gemm as og
+
+    from gpu_util import to_device
+
+    rng = np.random.default_rng(vec)
+    xa = rng.standard_normal((384, 512)).astype(np.float32)
+    xb = rng.standard_normal((256, 512)).astype(np.float32)
+    if vec == 16:
+        qa, sa, ga = wl.nv_quantize(xa)
+        qb, sb, gb = wl.nv_quantize(xb)
+        ref = og.gemm_nv_f64(qa, qb, sa, sb, ga * gb)
+        scales = dict(scale_a=torch.tensor([ga], device=cuda), scale_b=torch.tensor([gb], device=cuda))
+    else:
+        qa, sa = wl.mx_quantize(xa, kind)
+        qb, sb = wl.mx_quantize(xb, kind)
+        ref = og.gemm_mx_f64(qa, qb, sa, sb, kind)
+        scales = {}
+    psa = kl.pack_block_scales(torch.from_numpy(sa).to(cuda), 512, vec)
+    psb = kl.pack_block_scales(torch.from_numpy(sb).to(cuda), 512, vec)
+    c = torch.ops.kl.gemm_block_scaled(to_device(qa, kind, cuda), to_device(qb, kind, cuda), psa, psb, vec,
+                                       torch.float32, **scales)
+    torch.cuda.synchronize()
+    got = c.cpu().numpy()
+    assert np.abs(got - ref).max() / np.abs(ref).max() < 1e-3
