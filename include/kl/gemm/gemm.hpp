@@ -199,8 +199,8 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   a.batch_stride_c = pr.stride_c;
   a.c_reduce = pr.c_reduce;
   if constexpr (Cfg::kMx) {
-    if (pr.sfa == nullptr || pr.sfb == nullptr) throw std::invalid_argument("kl::gemm: MXFP8 needs scales of A and B");
-    if (pr.batch > 1) throw std::invalid_argument("kl::gemm: MXFP8 is not batched");
+    if (pr.sfa == nullptr || pr.sfb == nullptr) throw std::invalid_argument("kl::gemm: block scaling needs scales of A and B");
+    if (pr.batch > 1) throw std::invalid_argument("kl::gemm: block-scaled GEMMs are not batched");
     // The blocked scale arrays as [row blocks][K blocks][128 words of 4 bytes]; a box is the
     // kSfAtomsK atoms of one stage (K blocks of 4 * kSfVec elements).
     const int64_t kb = (pr.k + 4 * Cfg::kSfVec - 1) / (4 * Cfg::kSfVec);  // K blocks of 4 scales

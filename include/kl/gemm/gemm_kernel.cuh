@@ -183,7 +183,7 @@ struct TnParams {
   // all-gather. Stores only; nothing in this kernel reads peer memory.
   CUtensorMap map_peer[kMaxPeers];
   int n_peers;
-  // MXFP8 scales (TnConfig::kMx): the blocked arrays of A and B as [row blocks, K blocks, 128]
+  // Block scales (TnConfig::kMx): the blocked arrays of A and B as [row blocks, K blocks, 128]
   // 32-bit words, box {128, 1, 1} = one 512-byte atom.
   CUtensorMap map_sfa;
   CUtensorMap map_sfb;

@@ -118,11 +118,11 @@ typedef struct kl_gemm_desc {
   const void* sfb;
 } kl_gemm_desc;
 
-/* ---- MXFP8 scale factors ------------------------------------------------------------------
- * The blocked layout: rows in blocks of 128, K in blocks of 128 elements (4 scales); each
+/* ---- block scale factors (MX, NVFP4) ------------------------------------------------------
+ * The blocked layout: rows in blocks of 128, K in blocks of 4 scales (4 * vec elements); each
  * (row block, K block) is a 512-byte atom, atoms stored row-block major ((rb * kb_count + kb) *
  * 512), and inside an atom the scale of row r, K-group j sits at byte (r % 32) * 16 + (r / 32) * 4
- * + j. Padding rows and K-groups hold 127 (a scale of 1). No counterpart in the reference. */
+ * + j. Padding rows and K-groups hold a scale of 1. No counterpart in the reference. */
 
 /* Bytes of the blocked scale array for `rows` rows and `k` K-elements, one scale per `vec` (32 for
  * MX, 16 for NVFP4) elements: ceil(rows / 128) * ceil(k / (4 * vec)) * 512. */
@@ -169,7 +169,7 @@ KL_API kl_status kl_gemm_ws(const kl_gemm_desc* desc, void* workspace, size_t wo
  * block is a multiple of 256 columns) so that the copy in of block j+1, the GEMM of block j and
  * the copy back of block j-1 overlap. Ordered after the work already on `stream`; `stream` waits
  * for C to be on the host. The call only queues work: synchronise `stream` before reading C.
- * MXFP8 (block_scale = 1): desc->sfa / desc->sfb are HOST pointers to the blocked scale arrays;
+ * Block scaling (block_scale 1 or 2): desc->sfa / desc->sfb are HOST pointers to the blocked scale arrays;
  * the library stages them in a device buffer of its own (one per device, grown on demand). K-major
  * operands, C output only (c_reduce 0), one problem per call. */
 KL_API kl_status kl_gemm_host(const kl_gemm_desc* desc, void* dev_a, void* dev_b, void* dev_c, int32_t chunks,

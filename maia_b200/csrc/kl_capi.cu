@@ -99,7 +99,7 @@ kl_status run_tile(kl_gemm_desc const& d, Problem const& pr, bool pair, cudaStre
     if (d.block_scale != 1 && d.block_scale != 2)
       return fail(KL_ERR_INVALID_ARGUMENT, std::string(who) + ": block_scale must be 0, 1 (MX) or 2 (NVFP4)");
     if (a_mn || b_mn || (d.swizzle != 0 && d.swizzle != 128) || pr.batch > 1)
-      return fail(KL_ERR_NOT_SUPPORTED, std::string(who) + ": MXFP8 takes K-major operands, 128-byte swizzle, batch 1");
+      return fail(KL_ERR_NOT_SUPPORTED, std::string(who) + ": block-scaled GEMMs take K-major operands, 128-byte swizzle, batch 1");
     bool handled = false;
     kl_status s = kl::capi::run_tile_mx(d.block_scale, d.ab_type, d.c_type, d.variant, pair, pr, stream, info, &handled);
     if (handled) return s;
@@ -249,7 +249,7 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
     algo = (batch > 1 || a_mn || b_mn || !default_swizzle) ? (d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA)
                                                            : kl::capi::choose_algo(*d);
   if (algo == KL_ALGO_SKINNY && d->block_scale != 0)
-    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: MXFP8 runs on the tile kernels (KL_ALGO_1CTA / KL_ALGO_2CTA)");
+    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: block-scaled GEMMs run on the tile kernels (KL_ALGO_1CTA / KL_ALGO_2CTA)");
   if (algo == KL_ALGO_SKINNY && batch > 1) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: KL_ALGO_SKINNY is not batched");
   if (algo == KL_ALGO_SKINNY && (a_mn || b_mn))
     return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: KL_ALGO_SKINNY takes K-major operands");

@@ -23,7 +23,7 @@ struct HostPipe {
   cudaStream_t in = nullptr, mm = nullptr, out = nullptr;
   cudaEvent_t start = nullptr, done = nullptr;
   std::vector<cudaEvent_t> loaded, computed;
-  void* scales = nullptr;  // device staging of MXFP8 scales, grown on demand
+  void* scales = nullptr;  // device staging of block scales, grown on demand
   size_t scale_bytes = 0;
 };
 
@@ -72,7 +72,7 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
   if (h->c_reduce != 0) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_host: C is output only (c_reduce must be 0)");
   const bool mx = h->block_scale != 0;
   if (mx && (h->sfa == nullptr || h->sfb == nullptr))
-    return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_host: MXFP8 needs host scales of A and B (desc->sfa, desc->sfb)");
+    return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_host: block scaling needs host scales of A and B (desc->sfa, desc->sfb)");
   if (h->a_major != 0 || h->b_major != 0)
     return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_host: K-major operands only (B is streamed by rows)");
   cudaStream_t caller = static_cast<cudaStream_t>(stream_ptr);
@@ -97,7 +97,7 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
   const int ec = elem_bytes(h->c_type);
   // Bytes of `elems` operand elements (packed fp4: two per byte).
   auto ab_bytes = [&](int64_t elems) { return size_t(h->ab_type == KL_E2M1 ? elems / 2 : elems * elem_bytes(h->ab_type)); };
-  // MXFP8 scales: blocked arrays, A's then B's, in one staging buffer.
+  // Block scales: blocked arrays, A's then B's, in one staging buffer.
   const int32_t vec = h->block_scale == 2 ? 16 : 32;
   const int64_t sfa_bytes = mx ? kl_block_scale_bytes(h->m, h->k, vec) : 0;
   const int64_t sfb_bytes = mx ? kl_block_scale_bytes(h->n, h->k, vec) : 0;

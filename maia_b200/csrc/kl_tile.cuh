@@ -32,7 +32,7 @@ kl_status run_tile_types(int32_t ab_type, int32_t c_type, kl::gemm::Problem cons
 kl_status run_tile_swizzle(int32_t swizzle, int32_t ab_type, int32_t c_type, kl::gemm::Problem const& pr, bool pair,
                            cudaStream_t stream, kl::gemm::LaunchInfo* info, bool* handled);
 
-// kl_tile_mx.cu: MXFP8 (block-scaled e4m3 / e5m2), bf16 or f32 C. `pair`: 256 x 256 tiles on a
+// kl_tile_mx.cu: block-scaled GEMMs (MXFP8, MXFP4, NVFP4), bf16 or f32 C. `pair`: 256 x 256 tiles on a
 // CTA pair; one CTA: variant 0/1 = 128 x 256 tiles with one accumulator, 2 = 128 x 128 with two.
 // mode: 1 = MX (UE8M0 scales per 32 elements), 2 = NVFP4 (UE4M3 per 16, e2m1 only).
 kl_status run_tile_mx(int32_t mode, int32_t ab_type, int32_t c_type, int32_t variant, bool pair,
