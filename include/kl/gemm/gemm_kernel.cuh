@@ -73,7 +73,12 @@ struct TnConfig {
   static constexpr bool kMx = SfVec != 0;
   static constexpr bool kNv = SfVec == 16;
   static constexpr bool kFp4 = std::is_same_v<InT, e2m1x2>;
-  static constexpr int kSfbAtoms = kMx ? BlockN / 128 : 0;   // 128-row scale blocks of B per tile
+  // A tile of B rows [tn * BlockN, +BlockN) starts r = (tn * BlockN) % 128 rows into a 128-row
+  // scale block, r a multiple of gcd(BlockN, 128) >= 32: the tile's scales span kSfbAtoms blocks,
+  // copied to TMEM side by side, and the MMAs read them from word r / 32 on (row r + j of the first
+  // block sits in lane j % 32, word (r + j) / 32). So BlockN = 192 works with 128-row scale blocks.
+  static constexpr int kSfbGcd = (BlockN % 128 == 0) ? 128 : (BlockN % 64 == 0) ? 64 : 32;
+  static constexpr int kSfbAtoms = kMx ? (128 - kSfbGcd + BlockN + 127) / 128 : 0;  // 128-row scale blocks of B per tile
   static constexpr int kSfAtomsK = kMx ? (kFp4 ? 256 : 128) / (4 * SfVec) : 0;  // atoms along K per stage
   static constexpr int kMmasPerSfAtom = kMx ? 4 / kSfAtomsK : 1;  // MMAs (32 bytes of K each) per atom
   static constexpr uint32_t kSfIdStep = 4u / uint32_t(kMmasPerSfAtom);  // scale bytes per MMA
@@ -139,8 +144,8 @@ struct TnConfig {
   static constexpr uint32_t kIdesc = idesc();
 
   static_assert(kTmemUsed <= 512, "accumulators and scales exceed TMEM");
-  static_assert(!kMx || (sizeof(InT) == 1 && !AMn && !BMn && std::is_same_v<Sw, Swizzle128B> && BlockN % 128 == 0),
-                "block-scaled: 8-bit or packed fp4 K-major operands, 128-byte swizzle, tile N a multiple of 128");
+  static_assert(!kMx || (sizeof(InT) == 1 && !AMn && !BMn && std::is_same_v<Sw, Swizzle128B> && BlockN % 32 == 0),
+                "block-scaled: 8-bit or packed fp4 K-major operands, 128-byte swizzle, tile N a multiple of 32");
   static_assert(SfVec == 0 || SfVec == 32 || (SfVec == 16 && kFp4), "scales per 32 elements, or per 16 for fp4");
   static_assert(!kFp4 || kMx, "packed fp4 operands are block-scaled (kind::mxf4 / mxf4nvf4)");
   static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
@@ -414,7 +419,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
 #pragma unroll
               for (int j = 0; j < Cfg::kSfbAtoms; ++j)
                 tma_load_3d(sfb_smem + stage * Cfg::kSfbBytes + 512u * Cfg::kSfAtomsK * j, &p.map_sfb, full_bar(stage),
-                            0, sy, tn * Cfg::kSfbAtoms + j);
+                            0, sy, (tn * Cfg::kTileN) / 128 + j);
             }
           } else {
             // The leader's barrier counts the bytes of both CTAs; only the leader arrives.
@@ -433,7 +438,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
 #pragma unroll
               for (int j = 0; j < Cfg::kSfbAtoms; ++j)
                 tma_load_3d_pair(sfb_smem + stage * Cfg::kSfbBytes + 512u * Cfg::kSfAtomsK * j, &p.map_sfb, fb, 0, sy,
-                                 tn * Cfg::kSfbAtoms + j);
+                                 (tn * Cfg::kTileN) / 128 + j);
             }
           }
           if (++stage == S) {
@@ -466,6 +471,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         }
         tcgen05_fence_after();
         const uint32_t d_tmem = tmem_base + acc * Cfg::kAccCols;
+        uint32_t sfb_word = 0;  // first TMEM word of B's scales for this tile's rows
+        if constexpr (Cfg::kMx) {
+          int tbz, ttm, ttn;
+          tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, tbz, ttm, ttn);
+          sfb_word = uint32_t(((ttn * Cfg::kTileN) % 128) / 32);
+        }
         for (int kb = 0; kb < args.k_blocks; ++kb) {
           if (!mbarrier_wait(full_bar(stage), phase, args.timeout_ns)) {
             record_status(args.status, kStatusMmaTimeout);
@@ -504,7 +515,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
               const uint32_t id = uint32_t(k % Cfg::kMmasPerSfAtom) * Cfg::kSfIdStep;
               const uint32_t idesc = Cfg::kIdesc | (id << 29) | (id << 4);
               const uint32_t sfa_t = tmem_base + Cfg::kSfaCol + 4 * q;
-              const uint32_t sfb_t = tmem_base + Cfg::kSfbCol + 4 * Cfg::kSfbAtoms * q;
+              const uint32_t sfb_t = tmem_base + Cfg::kSfbCol + 4 * Cfg::kSfbAtoms * q + sfb_word;
               if constexpr (Cfg::kNv)
                 umma_nvf4_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16, idesc, sfa_t, sfb_t, accumulate);
               else if constexpr (Cfg::kFp4)

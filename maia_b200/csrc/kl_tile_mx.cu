@@ -25,6 +25,11 @@ using Mx128 = TnConfig<InT, OutT, 1, 128, 5, false, false, false, kl::Swizzle128
 // CTA pair, 256 x 256 tiles: one accumulator per CTA, 5 stages of 33.5 KB per CTA (fp8).
 template <typename InT, typename OutT, int V>
 using MxPair = TnConfig<InT, OutT, 2, 256, 5, false, false, false, kl::Swizzle128B, V>;
+// CTA pair, 256 x 192 tiles: two accumulators (2 x 192 columns leave room for the scales), 6 stages
+// of 29.5 KB per CTA (fp8; 5 for NVFP4's larger scale tiles). B's 192-row tiles start 0 or 64 rows
+// into a 128-row scale block.
+template <typename InT, typename OutT, int V>
+using MxPair192 = TnConfig<InT, OutT, 2, 192, V == 16 ? 5 : 6, false, false, false, kl::Swizzle128B, V>;
 // CTA pair, 256 x 128 tiles: two accumulators, 7 stages of 25 KB per CTA (fp8).
 template <typename InT, typename OutT, int V>
 using MxPair128 = TnConfig<InT, OutT, 2, 128, V == 16 ? 6 : 7, false, false, false, kl::Swizzle128B, V>;
@@ -33,8 +38,9 @@ template <typename InT, typename OutT, int V = 32>
 kl_status run_mx(int32_t variant, bool pair, kl::gemm::Problem const& pr, cudaStream_t stream,
                  kl::gemm::LaunchInfo* info) {
   if (pair)
-    return variant == 2 ? run_cfg<MxPair128<InT, OutT, V>>(pr, stream, info)
-                        : run_cfg<MxPair<InT, OutT, V>>(pr, stream, info);
+    return variant == 2   ? run_cfg<MxPair128<InT, OutT, V>>(pr, stream, info)
+           : variant == 3 ? run_cfg<MxPair192<InT, OutT, V>>(pr, stream, info)
+                          : run_cfg<MxPair<InT, OutT, V>>(pr, stream, info);
   return variant == 2 ? run_cfg<Mx128<InT, OutT, V>>(pr, stream, info) : run_cfg<Mx256<InT, OutT, V>>(pr, stream, info);
 }
 
@@ -65,8 +71,9 @@ __global__ void pack_scales_kernel(const uint8_t* __restrict__ src, long long ro
 kl_status run_tile_mx(int32_t mode, int32_t ab, int32_t c, int32_t variant, bool pair, kl::gemm::Problem const& pr,
                       cudaStream_t stream, kl::gemm::LaunchInfo* info, bool* handled) {
   *handled = true;
-  if (variant < 0 || variant > 2)
-    return fail(KL_ERR_INVALID_ARGUMENT, "block-scaled variant must be 0, 1 (256-column tiles) or 2 (128)");
+  if (variant < 0 || variant > 3 || (variant == 3 && !pair))
+    return fail(KL_ERR_INVALID_ARGUMENT,
+                "block-scaled variant must be 0, 1 (256-column tiles), 2 (128) or, on a CTA pair, 3 (192)");
   if (mode == 2) {  // NVFP4: UE4M3 scales per 16 elements
     if (ab == KL_E2M1 && c == KL_BF16) return run_mx<kl::e2m1x2, kl::bf16, 16>(variant, pair, pr, stream, info);
     if (ab == KL_E2M1 && c == KL_F32) return run_mx<kl::e2m1x2, float, 16>(variant, pair, pr, stream, info);

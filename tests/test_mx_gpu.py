@@ -74,8 +74,8 @@ def test_pack_scales_strided_source(cuda):
 
 
 KERNELS = pytest.mark.parametrize("algo,variant", [(kl.ALGO_1CTA, 0), (kl.ALGO_1CTA, 2), (kl.ALGO_2CTA, 0),
-                                                   (kl.ALGO_2CTA, 2)],
-                                  ids=["1cta_n256", "1cta_n128", "2cta_n256", "2cta_n128"])
+                                                   (kl.ALGO_2CTA, 2), (kl.ALGO_2CTA, 3)],
+                                  ids=["1cta_n256", "1cta_n128", "2cta_n256", "2cta_n128", "2cta_n192"])
 
 
 @KERNELS
