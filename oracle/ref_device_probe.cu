@@ -142,6 +142,35 @@ extern "C" int kl_ref_tma_desc_batched(void* gmem, int64_t b, int64_t m, int64_t
   return 0;
 }
 
+// Rank-4 and rank-5 tensors (two or three outer modes), row-major: the reference's
+// make_tma_load<bf16 128x64>(row_major(p, extents...)) and CuTe's make_tma_copy of the same tensor
+// with the outer modes last (the order CuTe tiles in).
+extern "C" int kl_ref_tma_desc_rank(void* gmem, int rank, const int64_t* e, void* kl_map, void* cute_map) {
+  auto* p = static_cast<kl::bf16*>(gmem);
+  using Tile = kl::SmemTile<kl::bf16, 128, 64>;
+  if (rank == 4) {
+    auto ours = kl::make_tma_load<Tile>(kl::row_major(p, e[0], e[1], e[2], e[3]));
+    std::memcpy(kl_map, &ours.map, sizeof(CUtensorMap));
+    const int64_t mk = e[2] * e[3];
+    auto ref = cute::make_tensor(cute::make_gmem_ptr(p), cute::make_shape(e[2], e[3], e[1], e[0]),
+                                 cute::make_stride(e[3], cute::_1{}, mk, mk * e[1]));
+    auto theirs = cute::make_tma_copy(cute::SM90_TMA_LOAD{}, ref, typename Tile::layout_type{});
+    std::memcpy(cute_map, theirs.get_tma_descriptor(), sizeof(CUtensorMap));
+    return 0;
+  }
+  if (rank == 5) {
+    auto ours = kl::make_tma_load<Tile>(kl::row_major(p, e[0], e[1], e[2], e[3], e[4]));
+    std::memcpy(kl_map, &ours.map, sizeof(CUtensorMap));
+    const int64_t mk = e[3] * e[4];
+    auto ref = cute::make_tensor(cute::make_gmem_ptr(p), cute::make_shape(e[3], e[4], e[2], e[1], e[0]),
+                                 cute::make_stride(e[4], cute::_1{}, mk, mk * e[2], mk * e[2] * e[1]));
+    auto theirs = cute::make_tma_copy(cute::SM90_TMA_LOAD{}, ref, typename Tile::layout_type{});
+    std::memcpy(cute_map, theirs.get_tma_descriptor(), sizeof(CUtensorMap));
+    return 0;
+  }
+  return 1;
+}
+
 // The reference's message for make_tma_load<bf16 128x64> on (ptr, rows, cols, row_stride), or "".
 extern "C" int kl_ref_tma_error(void* gmem, int64_t rows, int64_t cols, int64_t row_stride, char* msg, int cap) {
   using Tile = kl::SmemTile<kl::bf16, 128, 64>;

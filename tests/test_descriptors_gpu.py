@@ -52,6 +52,8 @@ def ref():
                                           ctypes.c_void_p, ctypes.c_void_p]
     L.kl_ref_tma_error.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_char_p,
                                    ctypes.c_int]
+    L.kl_ref_tma_desc_rank.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int64), ctypes.c_void_p,
+                                       ctypes.c_void_p]
     return L
 
 
@@ -119,6 +121,28 @@ def test_batched_rank3_map_matches_reference(cuda, ref):
     kl_map, cute_map = ctypes.create_string_buffer(128), ctypes.create_string_buffer(128)
     assert ref.kl_ref_tma_desc_batched(ctypes.c_void_p(buf.data_ptr()), B, M, K, kl_map, cute_map) == 0
     assert ours == kl_map.raw == cute_map.raw
+
+
+@pytest.mark.parametrize("shape", [(3, 4, 512, 256), (2, 3, 4, 256, 512), (1, 1, 2, 128, 64)])
+def test_rank4_rank5_maps_match_reference(cuda, ref, shape):
+    """Outer modes beyond one batch mode (tma_desc.hpp allows rank 2..5): ours = the reference's
+    make_tma_load(row_major(p, extents...)) = CuTe's make_tma_copy."""
+    import torch
+
+    n = 1
+    for e in shape:
+        n *= e
+    buf = torch.empty(n, dtype=torch.bfloat16, device=cuda)
+    strides, acc = [], 1
+    for e in reversed(shape):
+        strides.insert(0, acc)
+        acc *= e
+    ours = kl.make_tma_desc(kl.KL_BF16, 128, 64, 128, buf.data_ptr(), shape, strides)
+    kl_map, cute_map = ctypes.create_string_buffer(128), ctypes.create_string_buffer(128)
+    ext = (ctypes.c_int64 * len(shape))(*shape)
+    assert ref.kl_ref_tma_desc_rank(ctypes.c_void_p(buf.data_ptr()), len(shape), ext, kl_map, cute_map) == 0
+    assert ours == kl_map.raw, "tensor map differs from the reference's make_tma_load"
+    assert ours == cute_map.raw, "tensor map differs from CuTe's make_tma_copy"
 
 
 @pytest.mark.parametrize("offset, rows, cols, stride", [
