@@ -157,6 +157,7 @@ def main():
     ap.add_argument("--prefetch", type=int, default=0, help="L2 prefetch distance (0 = library default, -1 = off)")
     ap.add_argument("--variant", type=int, default=0, help="kl_gemm_desc.variant (0 = library default)")
     ap.add_argument("--max-ctas", type=int, default=0, help="cap on resident CTAs (0 = library default)")
+    ap.add_argument("--chunks", type=int, default=0, help="e2e column blocks of kl_gemm_host (0 = library default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
 
@@ -274,7 +275,7 @@ def main():
     def e2e_step():
         # The host-buffer entry point: copies in, GEMM and copy out, pipelined over column blocks.
         kl.gemm_host(a_host, b_host, c_host, a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo,
-                     sfa=sfa_host, sfb=sfb_host, scale_vec=vec)
+                     sfa=sfa_host, sfb=sfb_host, scale_vec=vec, chunks=args.chunks)
 
     for _ in range(max(args.warmup, 3)):
         e2e_step()
