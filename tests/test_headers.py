@@ -36,3 +36,24 @@ def test_product_headers_pull_in_no_cutlass():
     assert any("kl/gemm/gemm_kernel.cuh" in d for d in deps)
     bad = [d for d in deps if "/cute/" in d or "/cutlass/" in d or "cublas" in d.lower()]
     assert not bad, bad
+
+
+def test_cmake_consumer_builds_against_kl_target(tmp_path):
+    """A C++ consumer links kl::kl from the repository's CMakeLists.txt (the reference exports the
+    same INTERFACE target name) and runs the header checks."""
+    import shutil
+    import subprocess
+
+    cmake = shutil.which("cmake")
+    if cmake is None:
+        pytest.skip("cmake not installed")
+    build = tmp_path / "build"
+    cfg = subprocess.run([cmake, "-S", str(ROOT), "-B", str(build), "-DKL_BUILD_LIBRARY=OFF", "-DKL_BUILD_EXAMPLES=ON",
+                          "-DCMAKE_BUILD_TYPE=Release"], capture_output=True, text=True)
+    if cfg.returncode != 0 and "CUDA" in (cfg.stderr + cfg.stdout) and "not" in (cfg.stderr + cfg.stdout):
+        pytest.skip("CMake found no usable CUDA toolkit here")
+    assert cfg.returncode == 0, cfg.stdout + cfg.stderr
+    bld = subprocess.run([cmake, "--build", str(build), "--target", "kl_header_example"], capture_output=True, text=True)
+    assert bld.returncode == 0, bld.stdout + bld.stderr
+    run = subprocess.run([str(build / "kl_header_example")], capture_output=True, text=True)
+    assert run.returncode == 0, run.stdout + run.stderr
