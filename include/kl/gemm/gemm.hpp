@@ -37,8 +37,10 @@ struct Problem {
   // Batched GEMM: `batch` independent problems, A/B/C matrix b at a/b/c + b * stride_*.
   int64_t batch = 1;
   int64_t stride_a = 0, stride_b = 0, stride_c = 0;  // elements
-  // 0: C = result. 1: C += result, by TMA reducing stores (fp32 add in the TMA unit, so fp32 C
-  // only; every peer copy of C gets the same add; not with the direct-store epilogue).
+  // 0: C = result. 1: C += result: on an fp32 C by TMA reducing stores (the add happens in the TMA
+  // unit, also on every peer copy of C); on a bf16 / f16 C the epilogue reads this GPU's C, adds in
+  // fp32 and stores the sum (rounded once) to C and its peer copies. Not with the direct-store
+  // epilogue.
   int c_reduce = 0;
   // Block scaling (configs with kMx: MXFP8 / MXFP4 with UE8M0 scales per 32 K-elements, NVFP4 with
   // UE4M3 scales per 16): scales of A and B in the 128 x 4 blocked layout, ceil(rows / 128) x
@@ -168,8 +170,6 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   if (pr.c_reduce != 0 && pr.c_reduce != 1) throw std::invalid_argument("kl::gemm: c_reduce must be 0 (store) or 1 (add)");
   if (pr.c_reduce && Cfg::kDirectStore)
     throw std::invalid_argument("kl::gemm: reducing stores need the TMA-store epilogue");
-  if (pr.c_reduce && !std::is_same_v<OutT, float>)
-    throw std::invalid_argument("kl::gemm: reducing stores (C += result) need an fp32 C");
   for (int q = 0; q < pr.n_peers; ++q) {
     auto* pc = static_cast<OutT*>(pr.peer_c[q]);
     p.map_peer[q] = pr.batch > 1 ? make_tma_store<typename Cfg::CBox>(matrix(pc, pr.m, pr.n, pr.ldc, pr.stride_c)).map

@@ -173,7 +173,7 @@ struct TnArgs {
   unsigned long long* clock_probe;  // optional: per CTA {clock64, globaltimer} at start and end
   int batch;                    // independent GEMMs (rank-3 tensor maps when > 1)
   long long batch_stride_c;     // elements between the C matrices (direct-store epilogue)
-  int c_reduce;                 // 0: C = result; 1: C += result (TMA reducing stores, fp32 add)
+  int c_reduce;                 // 0: C = result; 1: C += result (fp32 C: TMA reducing stores; 16-bit C: read, add, store)
 };
 
 // Most peers an epilogue can push C tiles to (one NVLink/NVSwitch domain of 8 GPUs).
@@ -245,6 +245,21 @@ KL_DEVICE uint32_t pack_out2(float lo, float hi) {
   } else {
     return pack_bf16x2(lo, hi);
   }
+}
+
+// Two 16-bit values (low first) widened to fp32.
+template <typename OutT>
+KL_DEVICE float2 unpack_out2(uint32_t u) {
+  if constexpr (std::is_same_v<OutT, __half>)
+    return __half22float2(*reinterpret_cast<__half2*>(&u));
+  else
+    return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u));
+}
+
+KL_DEVICE uint4 ld_global_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
 }
 
 template <typename OutT>
@@ -596,12 +611,35 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         const uint32_t row_addr = buf + uint32_t(lane) * 128u;
         const uint32_t sw = uint32_t(lane & 7);
         if constexpr (sizeof(OutT) == 2) {
+          // C += result on a 16-bit C: the TMA unit's reducing store would round twice, so each thread
+          // reads its row of the chunk, 16 bytes at a time, adds in fp32 and the sum is stored, rounded
+          // once.
+          const int row = row0 + lane;
+          const bool add = args.c_reduce && row < args.m && col < args.n;
+          const OutT* src =
+              static_cast<const OutT*>(args.c) + (long long)bz * args.batch_stride_c + (long long)row * args.ldc + col;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
+            uint4 old = make_uint4(0u, 0u, 0u, 0u);
+            if (add) {
+              if (col + 8 * j + 8 <= args.n) {
+                old = ld_global_v4(src + 8 * j);
+              } else {
+                uint16_t h[8] = {};
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                  if (col + 8 * j + e < args.n) h[e] = reinterpret_cast<const uint16_t*>(src)[8 * j + e];
+                old = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
+                                 h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
+              }
+            }
             const float* f = reinterpret_cast<const float*>(&v[8 * j]);
-            st_shared_v4(row_addr + ((uint32_t(j) ^ sw) << 4), pack_out2<OutT>(f[0] * alpha, f[1] * alpha),
-                         pack_out2<OutT>(f[2] * alpha, f[3] * alpha), pack_out2<OutT>(f[4] * alpha, f[5] * alpha),
-                         pack_out2<OutT>(f[6] * alpha, f[7] * alpha));
+            const float2 o0 = unpack_out2<OutT>(old.x), o1 = unpack_out2<OutT>(old.y);
+            const float2 o2 = unpack_out2<OutT>(old.z), o3 = unpack_out2<OutT>(old.w);
+            st_shared_v4(row_addr + ((uint32_t(j) ^ sw) << 4), pack_out2<OutT>(f[0] * alpha + o0.x, f[1] * alpha + o0.y),
+                         pack_out2<OutT>(f[2] * alpha + o1.x, f[3] * alpha + o1.y),
+                         pack_out2<OutT>(f[4] * alpha + o2.x, f[5] * alpha + o2.y),
+                         pack_out2<OutT>(f[6] * alpha + o3.x, f[7] * alpha + o3.y));
           }
         } else {
 #pragma unroll
@@ -615,8 +653,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         __syncwarp();
         if (lane == 0) {
           if (store) {
-            if (args.c_reduce) {
-              // C += tile: the TMA unit reads C, adds the staged values and writes the sum back.
+            if (args.c_reduce && sizeof(OutT) == 4) {
+              // C += tile on an fp32 C: the TMA unit reads C, adds the staged values and writes back.
               if (batched) {
                 tma_reduce_add_3d(&p.map_c, buf, col, row0, bz);
                 for (int q = 0; q < p.n_peers; ++q) tma_reduce_add_3d(&p.map_peer[q], buf, col, row0, bz);

@@ -83,7 +83,7 @@ struct SkinnyArgs {
   int* status;
   unsigned long long timeout_ns;
   int prefetch;           // L2 prefetch distance for weight tiles, in units (0 = off)
-  int c_reduce;           // 0: C = result; 1: C += result (fp32 C)
+  int c_reduce;           // 0: C = result; 1: C += result
 };
 
 struct SkinnyParams {
@@ -115,8 +115,9 @@ KL_DEVICE void st_global_b16(void* p, uint16_t v) {
 }
 
 // C[j0 + q][col] = alpha * r[q] for the tokens q < W that exist (one C column per thread: a warp
-// writes 32 consecutive columns of each token row). With args.c_reduce (fp32 C only) the result
-// is added to C; exactly one thread writes each element, so the read-modify-write needs no atomics.
+// writes 32 consecutive columns of each token row). With args.c_reduce the result is added to C
+// in fp32 and rounded once; exactly one thread writes each element, so the read-modify-write needs
+// no atomics.
 template <typename OutT, int W>
 KL_DEVICE void store_c_column(SkinnyArgs const& args, const uint32_t (&r)[32], int j0, int col, float alpha) {
 #pragma unroll
@@ -125,8 +126,9 @@ KL_DEVICE void store_c_column(SkinnyArgs const& args, const uint32_t (&r)[32], i
     if (j < args.m) {
       const float v = __uint_as_float(r[q]) * alpha;
       if constexpr (sizeof(OutT) == 2) {
-        __nv_bfloat16 h = __float2bfloat16_rn(v);
-        st_global_b16(static_cast<uint16_t*>(args.c) + (long long)j * args.ldc + col, *reinterpret_cast<uint16_t*>(&h));
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(args.c) + (long long)j * args.ldc + col;
+        __nv_bfloat16 h = __float2bfloat16_rn(args.c_reduce ? __bfloat162float(*dst) + v : v);
+        st_global_b16(dst, *reinterpret_cast<uint16_t*>(&h));
       } else {
         float* dst = static_cast<float*>(args.c) + (long long)j * args.ldc + col;
         *dst = args.c_reduce ? *dst + v : v;

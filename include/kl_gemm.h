@@ -93,11 +93,11 @@ typedef struct kl_gemm_desc {
    * [K, M] with M contiguous, B stored [K, N]); lda / ldb are then the pitch of the stored
    * matrix. MN-major operands: bf16 inputs with bf16 C on the tile kernels. */
   int32_t a_major, b_major;
-  /* 0: C = result. 1 (add): C += result, in fp32 (c_type must be KL_F32): split-K partial sums,
-   * accumulation into a residual. The tile kernels add with TMA reducing stores
-   * (cp.reduce.async.bulk.tensor .add, performed by the TMA unit), the skinny kernel with a
-   * read-modify-write by the one thread that owns each element. Calls that add into one C from
-   * the same stream are ordered; concurrent calls race on the skinny path. */
+  /* 0: C = result. 1 (add): C += result (split-K partial sums, a residual add). fp32 C: the tile
+   * kernels add with TMA reducing stores (cp.reduce.async.bulk.tensor .add, performed by the TMA
+   * unit). bf16 / f16 C: the epilogue reads C, adds in fp32 and stores the sum, rounded once. The
+   * skinny kernel: a read-modify-write by the one thread that owns each element. Calls that add
+   * into one C from the same stream are ordered; concurrent calls race. */
   int32_t c_reduce;
   /* Operand swizzle span in bytes: 0 (= 128), 128, 64 or 32. 64 and 32 select tile kernels whose
    * stages hold the same 128 bytes of K as two or four swizzle atoms (one TMA box each); bf16

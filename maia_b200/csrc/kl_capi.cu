@@ -218,7 +218,6 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   if (d->m < 0 || d->n < 0 || d->k < 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: negative extent");
   if (d->c_reduce != 0 && d->c_reduce != 1) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: c_reduce must be 0 (store) or 1 (add)");
-  if (d->c_reduce && d->c_type != KL_F32) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: c_reduce (C += result) needs an fp32 C");
   if (d->m == 0 || d->n == 0) return KL_OK;
   if (d->c == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: null C");
   const int c_bytes = elem_bytes_of(d->c_type);
@@ -284,8 +283,6 @@ kl_status kl_gemm_gather(const kl_gemm_desc* d, void* const* peer_c, int32_t n_p
   if (algo != KL_ALGO_1CTA && algo != KL_ALGO_2CTA) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: unknown algo");
   if (d->c_reduce != 0 && d->c_reduce != 1)
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: c_reduce must be 0 (store) or 1 (add)");
-  if (d->c_reduce && d->c_type != KL_F32)
-    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_gather: c_reduce (C += result) needs an fp32 C");
   Problem pr = problem_of(*d);
   pr.peer_c = peer_c;
   pr.n_peers = n_peers;

@@ -135,8 +135,6 @@ extern "C" kl_status kl_gemm_skinny_noalloc(const kl_gemm_desc* d, void* stream_
     return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_skinny_noalloc: K-major operands with the 128-byte swizzle only");
   if (d->c_reduce != 0 && d->c_reduce != 1)
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_skinny_noalloc: c_reduce must be 0 (store) or 1 (add)");
-  if (d->c_reduce && d->c_type != KL_F32)
-    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_skinny_noalloc: c_reduce (C += result) needs an fp32 C");
   if (d->n > INT32_MAX || d->k > INT32_MAX)
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_skinny_noalloc: extents must fit in 32 bits");
   if (d->a == nullptr || d->b == nullptr || d->c == nullptr)

@@ -161,12 +161,28 @@ def test_reduce_add_k_zero_leaves_c(cuda):
     assert torch.equal(c, before)
 
 
-def test_reduce_add_needs_fp32_c(cuda):
+@pytest.mark.parametrize("algo", [kl.ALGO_1CTA, kl.ALGO_2CTA, kl.ALGO_SKINNY], ids=["1cta", "2cta", "skinny"])
+@pytest.mark.parametrize("out", ["bf16", "f16"])
+@pytest.mark.parametrize("shape", [(16, 1024, 512), (100, 520, 200), (256, 776, 1024)])
+def test_reduce_add_into_16bit_c(cuda, algo, out, shape):
+    """C += A . B^T on a bf16 / f16 C (a residual add): the epilogue reads C, adds in fp32 and the
+    sum is rounded once; ragged right edges (N not a multiple of 64) included."""
+    m, n, k = shape
+    if algo == kl.ALGO_SKINNY and out == "f16":
+        pytest.skip("the skinny kernel writes bf16 or f32 C")
+    dtype = "bf16" if out == "bf16" or algo == kl.ALGO_SKINNY else "f16"
+    a, b, _, _ = random_inputs(m, n, k, dtype, seed=m + n + 2 * k)
+    tdt = torch.bfloat16 if out == "bf16" else torch.float16
+    c = (torch.randn(m, n, generator=torch.Generator().manual_seed(m)) * 4).to(tdt)
+    c0 = c.float().numpy().astype(np.float64)
+    c = c.to(cuda)
+    kl.gemm(to_device(a, dtype, cuda), to_device(b, dtype, cuda), c, algo=algo, accumulate=True)
+    torch.cuda.synchronize()
+    assert kl.read_status() == 0
+    check(c.float().cpu().numpy(), a, b, 1.0, TOL16, kind=dtype, c0=c0)
+
+
+def test_reduce_add_needs_out(cuda):
     a = torch.zeros(256, 64, dtype=torch.bfloat16, device=cuda)
-    c = torch.zeros(256, 256, dtype=torch.bfloat16, device=cuda)
-    for algo in (kl.ALGO_1CTA, kl.ALGO_SKINNY):
-        with pytest.raises(kl.KlError) as e:
-            kl.gemm(a, a, c, algo=algo, accumulate=True)
-        assert e.value.status == kl.KL_ERR_NOT_SUPPORTED
     with pytest.raises(ValueError):
         kl.gemm(a, a, accumulate=True)
