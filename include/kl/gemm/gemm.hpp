@@ -47,6 +47,11 @@ struct Problem {
   // ceil(K / (4 * vec)) atoms of 512 bytes, row-block major.
   const void* sfa = nullptr;
   const void* sfb = nullptr;
+  // m-grouped GEMM (one-CTA configs): `groups` B matrices [groups, N, K] (stride_b elements apart);
+  // A [M, K] and C [M, N] are single matrices whose 128-row blocks each use the B named by
+  // m_block_group[block] (device, ceil(M / 128) entries; -1 = padding, computed with B = 0).
+  int groups = 0;
+  const int* m_block_group = nullptr;
 };
 
 // Library defaults for the knobs a Problem leaves at 0.
@@ -153,7 +158,25 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   const int64_t ku = pr.k / kPack, lda = pr.lda / kPack, ldb = pr.ldb / kPack;
   const int64_t a_rows = Cfg::kAMn ? ku : pr.m, a_cols = Cfg::kAMn ? pr.m : ku;
   const int64_t b_rows = Cfg::kBMn ? ku : pr.n, b_cols = Cfg::kBMn ? pr.n : ku;
-  if (pr.batch > 1) {
+  const bool grouped = pr.m_block_group != nullptr;
+  if (grouped) {
+    if (Cfg::kCtaGroup != 1 || Cfg::kAMn || Cfg::kBMn || Cfg::kMx || pr.batch > 1)
+      throw std::invalid_argument("kl::gemm: m-grouped GEMMs run on the one-CTA kernel, K-major, batch 1");
+    if (pr.groups < 1 || pr.groups > 65535) throw std::invalid_argument("kl::gemm: groups must be in [1, 65535]");
+  }
+  if (grouped) {
+    p.map_a = make_tma_load<typename Cfg::ATile>(row_major_strided(static_cast<InT const*>(pr.a), a_rows, a_cols, lda)).map;
+    GmemTensor<InT const, 3> gb;
+    gb.ptr = static_cast<InT const*>(pr.b);
+    gb.shape[0] = pr.groups;
+    gb.shape[1] = b_rows;
+    gb.shape[2] = b_cols;
+    gb.stride[0] = pr.stride_b / kPack;
+    gb.stride[1] = ldb;
+    gb.stride[2] = 1;
+    p.map_b = make_tma_load<typename Cfg::BTile>(gb).map;
+    p.map_c = make_tma_store<typename Cfg::CBox>(row_major_strided(static_cast<OutT*>(pr.c), pr.m, pr.n, pr.ldc)).map;
+  } else if (pr.batch > 1) {
     p.map_a = make_tma_load<typename Cfg::ATile>(
                   matrix(static_cast<InT const*>(pr.a), a_rows, a_cols, lda, pr.stride_a / kPack)).map;
     p.map_b = make_tma_load<typename Cfg::BTile>(
@@ -198,6 +221,7 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   a.batch = int(pr.batch);
   a.batch_stride_c = pr.stride_c;
   a.c_reduce = pr.c_reduce;
+  a.m_block_group = pr.m_block_group;
   if constexpr (Cfg::kMx) {
     if (pr.sfa == nullptr || pr.sfb == nullptr) throw std::invalid_argument("kl::gemm: block scaling needs scales of A and B");
     if (pr.batch > 1) throw std::invalid_argument("kl::gemm: block-scaled GEMMs are not batched");

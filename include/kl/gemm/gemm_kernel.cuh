@@ -174,6 +174,7 @@ struct TnArgs {
   int batch;                    // independent GEMMs (rank-3 tensor maps when > 1)
   long long batch_stride_c;     // elements between the C matrices (direct-store epilogue)
   int c_reduce;                 // 0: C = result; 1: C += result (fp32 C: TMA reducing stores; 16-bit C: read, add, store)
+  const int* m_block_group;     // m-grouped GEMM (one CTA per tile): B matrix of each 128-row block of A / C
 };
 
 // Most peers an epilogue can push C tiles to (one NVLink/NVSwitch domain of 8 GPUs).
@@ -399,7 +400,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         if (t >= num_tiles) return;
         int pbz, ptm, ptn;
         tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, pbz, ptm, ptn);
-        if (batched || Cfg::kAMn || Cfg::kBMn) return;  // 2-D, K-major maps only
+        if (batched || Cfg::kAMn || Cfg::kBMn || args.m_block_group != nullptr) return;  // 2-D, K-major maps only
         tma_prefetch_l2_2d(&p.map_a, kb * Cfg::kBlockK, ptm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM);
         tma_prefetch_l2_2d(&p.map_b, kb * Cfg::kBlockK, ptn * Cfg::kTileN + int(cta_rank) * Cfg::kCtaN);
       };
@@ -412,6 +413,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, bz, tm, tn);
         const int a_row = tm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM;
         const int b_row = tn * Cfg::kTileN + int(cta_rank) * Cfg::kCtaN;
+        // m-grouped: A and C are one [M, *] matrix, B one of a rank-3 stack, chosen per 128-row block
+        // (a block marked -1 loads B as zeros: padding rows come out 0).
+        const int gz = args.m_block_group != nullptr ? __ldg(args.m_block_group + tm) : 0;
         for (int kb = 0; kb < args.k_blocks; ++kb) {
           if (pf > 0) prefetch_unit(t, kb + pf);
           if (!mbarrier_wait(empty_bar(stage), phase ^ 1u, args.timeout_ns)) {
@@ -424,8 +428,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
             mbarrier_arrive_expect_tx(full_bar(stage), Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes + Cfg::kSfbBytes);
             load_operand<typename Cfg::ATile, Cfg::kAMn, 1>(a_smem + stage * Cfg::kABytes, &p.map_a, full_bar(stage),
                                                             kx, a_row, bz, batched);
-            load_operand<typename Cfg::BTile, Cfg::kBMn, 1>(b_smem + stage * Cfg::kBBytes, &p.map_b, full_bar(stage),
-                                                            kx, b_row, bz, batched);
+            if (args.m_block_group != nullptr)
+              load_operand<typename Cfg::BTile, Cfg::kBMn, 1>(b_smem + stage * Cfg::kBBytes, &p.map_b, full_bar(stage),
+                                                              kx, b_row, gz, true);
+            else
+              load_operand<typename Cfg::BTile, Cfg::kBMn, 1>(b_smem + stage * Cfg::kBBytes, &p.map_b, full_bar(stage),
+                                                              kx, b_row, bz, batched);
             if constexpr (Cfg::kMx) {
               // K-block kb's scale atoms: A's row block (tm) and the tile's row blocks of B (a block
               // past the end of B loads as zeros, for output columns that are never stored).

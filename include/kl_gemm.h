@@ -117,6 +117,15 @@ typedef struct kl_gemm_desc {
   int32_t reserved; /* must be 0 */
   const void* sfa;
   const void* sfb;
+  /* m-grouped GEMM (mixture-of-experts layout): m_block_group non-NULL makes B a stack of `groups`
+   * matrices [groups, N, K] (stride_b elements apart) while A [M, K] and C [M, N] stay single
+   * matrices whose rows are the groups' rows back to back, each group padded to a multiple of 128
+   * rows. m_block_group (device, ceil(M / 128) int32) names the B of every 128-row block; -1 marks
+   * a padding block (its C rows come out 0, or C + 0). One-CTA tile kernel (KL_ALGO_AUTO or
+   * KL_ALGO_1CTA), K-major, batch 1, no block scaling. */
+  int32_t groups;
+  int32_t reserved2; /* must be 0 */
+  const int32_t* m_block_group;
 } kl_gemm_desc;
 
 /* ---- block scale factors (MX, NVFP4) ------------------------------------------------------

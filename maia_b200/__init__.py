@@ -66,6 +66,8 @@ class GemmDesc(ctypes.Structure):
         ("c_reduce", ctypes.c_int32), ("swizzle", ctypes.c_int32),
         ("block_scale", ctypes.c_int32), ("reserved", ctypes.c_int32),
         ("sfa", ctypes.c_void_p), ("sfb", ctypes.c_void_p),
+        ("groups", ctypes.c_int32), ("reserved2", ctypes.c_int32),
+        ("m_block_group", ctypes.c_void_p),
     ]
 
 
@@ -276,6 +278,32 @@ def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=Non
 def block_scale_bytes(rows: int, k: int, vec: int = 32) -> int:
     """Bytes of the blocked scale array for `rows` rows of `k` K-elements, one scale per `vec`."""
     return int(lib().kl_block_scale_bytes(int(rows), int(k), int(vec)))
+
+
+def gemm_grouped(a, b, m_block_group, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=None,
+                 accumulate=False, stream=None):
+    """m-grouped GEMM (mixture-of-experts layout): a [M, K] holds the groups' rows back to back,
+    each group padded to a multiple of 128 rows; b [G, N, K] holds one matrix per group;
+    m_block_group is an int32 device tensor of ceil(M / 128) entries naming the group of every
+    128-row block (-1 = padding). out[rows of block i] = a[rows] @ b[m_block_group[i]].T."""
+    import torch
+
+    if b.dim() != 3 or a.dim() != 2 or b.shape[2] != a.shape[1]:
+        raise ValueError("a must be [M, K] and b [G, N, K]")
+    if m_block_group.dtype != torch.int32 or m_block_group.numel() < -(-a.shape[0] // 128):
+        raise ValueError("m_block_group must be int32 with ceil(M / 128) entries")
+    if accumulate and out is None:
+        raise ValueError("accumulate=True adds into `out`, which must be given")
+    if out is None:
+        out = torch.empty((a.shape[0], b.shape[1]), dtype=out_dtype or torch.bfloat16, device=a.device)
+    d = gemm_desc(a, b[0], out, alpha, scale_a, scale_b, ALGO_1CTA, c_reduce=int(bool(accumulate)))
+    pb = 2 if _dtype_code(b.dtype) == KL_E2M1 else 1
+    d.groups = b.shape[0]
+    d.stride_b = b.stride(0) * pb
+    d.m_block_group = m_block_group.data_ptr()
+    s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
+    check(lib().kl_gemm(ctypes.byref(d), ctypes.c_void_p(s)))
+    return out
 
 
 def mx_scale_bytes(rows: int, k: int) -> int:

@@ -161,6 +161,8 @@ Problem problem_of(kl_gemm_desc const& d) {
   pr.c_reduce = d.c_reduce;
   pr.sfa = d.sfa;
   pr.sfb = d.sfb;
+  pr.groups = d.groups;
+  pr.m_block_group = d.m_block_group;
   return pr;
 }
 
@@ -240,8 +242,15 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
   if ((d->a_major != 0 && !a_mn) || (d->b_major != 0 && !b_mn))
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: a_major / b_major must be 0 (K) or 1 (MN)");
   const bool default_swizzle = d->swizzle == 0 || d->swizzle == 128;
-  if (d->reserved != 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: reserved must be 0");
+  if (d->reserved != 0 || d->reserved2 != 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: reserved fields must be 0");
   int algo = d->algo;
+  if (d->m_block_group != nullptr) {
+    if (algo != KL_ALGO_AUTO && algo != KL_ALGO_1CTA)
+      return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: m-grouped GEMMs run on the one-CTA tile kernel (KL_ALGO_1CTA)");
+    if (batch > 1 || d->block_scale != 0 || a_mn || b_mn)
+      return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: m-grouped GEMMs take K-major operands, batch 1, no block scaling");
+    algo = KL_ALGO_1CTA;
+  }
   if (algo == KL_ALGO_AUTO && d->block_scale != 0)
     algo = d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA;
   else if (algo == KL_ALGO_AUTO)
