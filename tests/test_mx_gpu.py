@@ -204,3 +204,14 @@ def test_nvfp4_gemm(cuda, algo, variant, out, shape):
     assert not np.isnan(c).any()
     elem, norm = og.rel_error(c, ref)
     assert norm <= FP8_TOL and elem <= FP8_TOL, f"normwise {norm:.3e}, element-wise {elem:.3e}"
+
+
+@pytest.mark.parametrize("algo", [kl.ALGO_1CTA, kl.ALGO_2CTA], ids=["1cta", "2cta"])
+def test_mx_reduce_into_bf16_c(cuda, algo):
+    """Block-scaled GEMM adding into a bf16 C (the one-accumulator, eight-warp epilogue path)."""
+    m, n, k = 384, 520, 512
+    qa, sa, qb, sb = mx_inputs(m, n, k, "e4m3", seed=19)
+    c0 = torch.randn(m, n, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
+    c = c0.to(cuda)
+    got = run_mx(qa, sa, qb, sb, "e4m3", "bf16", cuda, c=c, algo=algo, accumulate=True)
+    check_mx(got, qa, sa, qb, sb, "e4m3", c0=c0.float().numpy().astype(np.float64))
