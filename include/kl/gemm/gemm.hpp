@@ -47,9 +47,10 @@ struct Problem {
   // ceil(K / (4 * vec)) atoms of 512 bytes, row-block major.
   const void* sfa = nullptr;
   const void* sfb = nullptr;
-  // m-grouped GEMM (one-CTA configs): `groups` B matrices [groups, N, K] (stride_b elements apart);
-  // A [M, K] and C [M, N] are single matrices whose 128-row blocks each use the B named by
-  // m_block_group[block] (device, ceil(M / 128) entries; -1 = padding, computed with B = 0).
+  // m-grouped GEMM: `groups` B matrices [groups, N, K] (stride_b elements apart); A [M, K] and
+  // C [M, N] are single matrices whose 128-row blocks each use the B named by m_block_group[block]
+  // (device, ceil(M / 128) entries; -1 = padding, computed with B = 0). CTA-pair configs use the
+  // group of each 256-row tile's first block, so there blocks 2i and 2i + 1 must agree.
   int groups = 0;
   const int* m_block_group = nullptr;
 };
@@ -160,8 +161,8 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   const int64_t b_rows = Cfg::kBMn ? ku : pr.n, b_cols = Cfg::kBMn ? pr.n : ku;
   const bool grouped = pr.m_block_group != nullptr;
   if (grouped) {
-    if (Cfg::kCtaGroup != 1 || Cfg::kAMn || Cfg::kBMn || Cfg::kMx || pr.batch > 1)
-      throw std::invalid_argument("kl::gemm: m-grouped GEMMs run on the one-CTA kernel, K-major, batch 1");
+    if (Cfg::kAMn || Cfg::kBMn || Cfg::kMx || pr.batch > 1)
+      throw std::invalid_argument("kl::gemm: m-grouped GEMMs take K-major operands, batch 1, no block scaling");
     if (pr.groups < 1 || pr.groups > 65535) throw std::invalid_argument("kl::gemm: groups must be in [1, 65535]");
   }
   if (grouped) {

@@ -174,7 +174,7 @@ struct TnArgs {
   int batch;                    // independent GEMMs (rank-3 tensor maps when > 1)
   long long batch_stride_c;     // elements between the C matrices (direct-store epilogue)
   int c_reduce;                 // 0: C = result; 1: C += result (fp32 C: TMA reducing stores; 16-bit C: read, add, store)
-  const int* m_block_group;     // m-grouped GEMM (one CTA per tile): B matrix of each 128-row block of A / C
+  const int* m_block_group;     // m-grouped GEMM: B matrix of each 128-row block of A / C (-1 = padding)
 };
 
 // Most peers an epilogue can push C tiles to (one NVLink/NVSwitch domain of 8 GPUs).
@@ -414,8 +414,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         const int a_row = tm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM;
         const int b_row = tn * Cfg::kTileN + int(cta_rank) * Cfg::kCtaN;
         // m-grouped: A and C are one [M, *] matrix, B one of a rank-3 stack, chosen per 128-row block
-        // (a block marked -1 loads B as zeros: padding rows come out 0).
-        const int gz = args.m_block_group != nullptr ? __ldg(args.m_block_group + tm) : 0;
+        // (a block marked -1 loads B as zeros: padding rows come out 0). A CTA pair's 256-row tile
+        // uses the group of its first block: both blocks must name the same group.
+        const int gz = args.m_block_group != nullptr ? __ldg(args.m_block_group + tm * CG) : 0;
         for (int kb = 0; kb < args.k_blocks; ++kb) {
           if (pf > 0) prefetch_unit(t, kb + pf);
           if (!mbarrier_wait(empty_bar(stage), phase ^ 1u, args.timeout_ns)) {
@@ -452,8 +453,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
             const uint32_t fb = leader_full0 + 8u * stage;
             load_operand<typename Cfg::ATile, Cfg::kAMn, 2>(a_smem + stage * Cfg::kABytes, &p.map_a, fb, kx, a_row, bz,
                                                             batched);
-            load_operand<typename Cfg::BTile, Cfg::kBMn, 2>(b_smem + stage * Cfg::kBBytes, &p.map_b, fb, kx, b_row, bz,
-                                                            batched);
+            if (args.m_block_group != nullptr)
+              load_operand<typename Cfg::BTile, Cfg::kBMn, 2>(b_smem + stage * Cfg::kBBytes, &p.map_b, fb, kx, b_row,
+                                                              gz, true);
+            else
+              load_operand<typename Cfg::BTile, Cfg::kBMn, 2>(b_smem + stage * Cfg::kBBytes, &p.map_b, fb, kx, b_row,
+                                                              bz, batched);
             if constexpr (Cfg::kMx) {
               // Each CTA: the scales of its own 128 rows of A, and of all the tile's rows of B.
               const int sy = kb * Cfg::kSfAtomsK;

@@ -121,8 +121,10 @@ typedef struct kl_gemm_desc {
    * matrices [groups, N, K] (stride_b elements apart) while A [M, K] and C [M, N] stay single
    * matrices whose rows are the groups' rows back to back, each group padded to a multiple of 128
    * rows. m_block_group (device, ceil(M / 128) int32) names the B of every 128-row block; -1 marks
-   * a padding block (its C rows come out 0, or C + 0). One-CTA tile kernel (KL_ALGO_AUTO or
-   * KL_ALGO_1CTA), K-major, batch 1, no block scaling. */
+   * a padding block (its C rows come out 0, or C + 0). KL_ALGO_AUTO / KL_ALGO_1CTA: the one-CTA
+   * tile kernel, any such layout; KL_ALGO_2CTA: the CTA pair, which takes each 256-row tile's
+   * group from its first block, so groups must be padded to 256 rows (blocks 2i and 2i + 1 name the
+   * same group). K-major, batch 1, no block scaling. */
   int32_t groups;
   int32_t reserved2; /* must be 0 */
   const int32_t* m_block_group;

@@ -245,11 +245,13 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
   if (d->reserved != 0 || d->reserved2 != 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: reserved fields must be 0");
   int algo = d->algo;
   if (d->m_block_group != nullptr) {
-    if (algo != KL_ALGO_AUTO && algo != KL_ALGO_1CTA)
-      return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: m-grouped GEMMs run on the one-CTA tile kernel (KL_ALGO_1CTA)");
+    // The one-CTA kernel takes any 128-row grouping; the CTA pair needs groups padded to 256 rows
+    // (it reads the group of each tile's first block), so it is used only when asked for.
+    if (algo != KL_ALGO_AUTO && algo != KL_ALGO_1CTA && algo != KL_ALGO_2CTA)
+      return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: m-grouped GEMMs run on the tile kernels (KL_ALGO_1CTA / 2CTA)");
     if (batch > 1 || d->block_scale != 0 || a_mn || b_mn)
       return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: m-grouped GEMMs take K-major operands, batch 1, no block scaling");
-    algo = KL_ALGO_1CTA;
+    if (algo == KL_ALGO_AUTO) algo = KL_ALGO_1CTA;
   }
   if (algo == KL_ALGO_AUTO && d->block_scale != 0)
     algo = d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA;

@@ -70,11 +70,37 @@ def test_grouped_gemm_fp8_and_accumulate(cuda):
         r0 += rp
 
 
+@pytest.mark.parametrize("sizes,n,k", [([256, 512, 200, 256], 512, 384), ([300, 100], 1000, 520)])
+def test_grouped_gemm_cta_pair(cuda, sizes, n, k):
+    """The CTA-pair kernel with groups padded to 256 rows (each 256-row tile within one group)."""
+    rows = [-(-s // 256) * 256 for s in sizes]
+    a_bits = np.zeros((sum(rows), k), dtype=np.uint16)
+    b_list, blocks, r0 = [], [], 0
+    for g, (s, rp) in enumerate(zip(sizes, rows)):
+        a, b, _, _ = random_inputs(s, n, k, "bf16", seed=11 * g + s)
+        a_bits[r0:r0 + s] = a
+        b_list.append(b)
+        blocks += [g] * (rp // 128)
+        r0 += rp
+    b_bits = np.stack(b_list)
+    a, b = to_device(a_bits, "bf16", cuda), to_device(b_bits, "bf16", cuda)
+    c = torch.full((a.shape[0], n), float("nan"), dtype=torch.float32, device=cuda)
+    kl.gemm_grouped(a, b, torch.tensor(blocks, dtype=torch.int32, device=cuda), c, algo=kl.ALGO_2CTA)
+    torch.cuda.synchronize()
+    assert kl.read_status() == 0
+    got = c.cpu().numpy()
+    r0 = 0
+    for g, (s, rp) in enumerate(zip(sizes, rows)):
+        elem, norm = og.rel_error(got[r0:r0 + s], og.gemm_f64(a_bits[r0:r0 + s], b_bits[g]))
+        assert elem <= 1e-2 and norm <= 1e-2, f"group {g}: {elem:.3e} / {norm:.3e}"
+        r0 += rp
+
+
 def test_grouped_gemm_limits(cuda):
     a = torch.zeros(256, 64, dtype=torch.bfloat16, device=cuda)
     b = torch.zeros(2, 128, 64, dtype=torch.bfloat16, device=cuda)
     blocks = torch.zeros(2, dtype=torch.int32, device=cuda)
-    d = kl.gemm_desc(a, b[0], torch.zeros(256, 128, dtype=torch.bfloat16, device=cuda), algo=kl.ALGO_2CTA)
+    d = kl.gemm_desc(a, b[0], torch.zeros(256, 128, dtype=torch.bfloat16, device=cuda), algo=kl.ALGO_SKINNY)
     d.groups, d.stride_b, d.m_block_group = 2, b.stride(0), blocks.data_ptr()
     with pytest.raises(kl.KlError) as e:
         kl.check(kl.lib().kl_gemm(kl.ctypes.byref(d), kl.ctypes.c_void_p(0)))
