@@ -1,5 +1,5 @@
-"""PyTorch operators over the C ABI: torch.ops.kl.gemm, torch.ops.kl.gemm_fp8 and
-torch.ops.kl.gemm_block_scaled.
+"""PyTorch operators over the C ABI: torch.ops.kl.gemm, torch.ops.kl.gemm_fp8,
+torch.ops.kl.gemm_block_scaled and torch.ops.kl.gemm_grouped.
 
 Registered with torch.library so they compose with the rest of a PyTorch program (fake tensors
 for shape inference, the dispatcher, torch.compile graphs that call them as opaque ops). The work
@@ -12,7 +12,7 @@ from typing import Optional
 
 import torch
 
-from . import ALGO_AUTO, gemm as _kl_gemm
+from . import ALGO_1CTA, ALGO_2CTA, ALGO_AUTO, gemm as _kl_gemm, gemm_grouped as _kl_gemm_grouped
 
 
 @torch.library.custom_op("kl::gemm", mutates_args=())
@@ -61,3 +61,18 @@ def gemm_block_scaled(a: torch.Tensor, b: torch.Tensor, sfa: torch.Tensor, sfb: 
 @gemm_block_scaled.register_fake
 def _(a, b, sfa, sfb, scale_vec=32, out_dtype=torch.bfloat16, scale_a=None, scale_b=None):
     return a.new_empty((a.shape[0], b.shape[0]), dtype=out_dtype)
+
+
+@torch.library.custom_op("kl::gemm_grouped", mutates_args=())
+def gemm_grouped(a: torch.Tensor, b: torch.Tensor, m_block_group: torch.Tensor,
+                 out_dtype: torch.dtype = torch.bfloat16, pairs: bool = False) -> torch.Tensor:
+    """m-grouped a @ b[g].T (mixture-of-experts layout): a [M, K] with the groups' rows back to back
+    (each group padded to 128 rows, or 256 with pairs=True for the CTA-pair kernel), b [G, N, K],
+    m_block_group int32 [ceil(M / 128)] naming each 128-row block's group (-1 = padding)."""
+    out = torch.empty((a.shape[0], b.shape[1]), dtype=out_dtype, device=a.device)
+    return _kl_gemm_grouped(a, b, m_block_group, out, algo=ALGO_2CTA if pairs else ALGO_1CTA)
+
+
+@gemm_grouped.register_fake
+def _(a, b, m_block_group, out_dtype=torch.bfloat16, pairs=False):
+    return a.new_empty((a.shape[0], b.shape[1]), dtype=out_dtype)

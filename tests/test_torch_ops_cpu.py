@@ -29,3 +29,15 @@ def test_fake_block_scaled_shapes():
         sf = torch.empty((1024,), dtype=torch.uint8)
         c = torch.ops.kl.gemm_block_scaled(a, b, sf, sf, 16, torch.float32)
         assert c.shape == (256, 128) and c.dtype == torch.float32
+
+
+def test_fake_grouped_shapes():
+    import maia_b200.torch_ops  # noqa: F401
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        a = torch.empty((512, 64), dtype=torch.bfloat16)
+        b = torch.empty((3, 96, 64), dtype=torch.bfloat16)
+        blocks = torch.empty((4,), dtype=torch.int32)
+        c = torch.ops.kl.gemm_grouped(a, b, blocks)
+        assert c.shape == (512, 96) and c.dtype == torch.bfloat16

@@ -67,3 +67,16 @@ def test_kl_gemm_block_scaled_op(cuda, kind, vec):
     torch.cuda.synchronize()
     got = c.cpu().numpy()
     assert np.abs(got - ref).max() / np.abs(ref).max() < 1e-3
+
+
+def test_kl_gemm_grouped_op(cuda):
+    import maia_b200.torch_ops  # noqa: F401
+
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.randn((512, 256), device=cuda, generator=g).to(torch.bfloat16)
+    b = torch.randn((2, 384, 256), device=cuda, generator=g).to(torch.bfloat16)
+    blocks = torch.tensor([0, 0, 1, 1], dtype=torch.int32, device=cuda)
+    for pairs in (False, True):
+        c = torch.ops.kl.gemm_grouped(a, b, blocks, torch.float32, pairs)
+        ref = torch.cat([a[:256].float() @ b[0].float().T, a[256:].float() @ b[1].float().T])
+        assert rel(c, ref) < 1e-5
