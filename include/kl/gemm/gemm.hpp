@@ -161,8 +161,8 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   const int64_t b_rows = Cfg::kBMn ? ku : pr.n, b_cols = Cfg::kBMn ? pr.n : ku;
   const bool grouped = pr.m_block_group != nullptr;
   if (grouped) {
-    if (Cfg::kAMn || Cfg::kBMn || Cfg::kMx || pr.batch > 1)
-      throw std::invalid_argument("kl::gemm: m-grouped GEMMs take K-major operands, batch 1, no block scaling");
+    if (Cfg::kAMn || Cfg::kBMn || pr.batch > 1)
+      throw std::invalid_argument("kl::gemm: m-grouped GEMMs take K-major operands, batch 1");
     if (pr.groups < 1 || pr.groups > 65535) throw std::invalid_argument("kl::gemm: groups must be in [1, 65535]");
   }
   if (grouped) {
@@ -229,14 +229,18 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
     // The blocked scale arrays as [row blocks][K blocks][128 words of 4 bytes]; a box is the
     // kSfAtomsK atoms of one stage (K blocks of 4 * kSfVec elements).
     const int64_t kb = (pr.k + 4 * Cfg::kSfVec - 1) / (4 * Cfg::kSfVec);  // K blocks of 4 scales
-    auto sf_map = [&](CUtensorMap* map, void const* ptr, int64_t rows) {
-      const int64_t shape[3] = {(rows + 127) / 128, kb, 128};
+    auto sf_map = [&](CUtensorMap* map, void const* ptr, int64_t row_blocks) {
+      const int64_t shape[3] = {row_blocks, kb, 128};
       const int64_t stride[3] = {kb * 128, 128, 1};
       kl::detail::encode_tma_map(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, CU_TENSOR_MAP_SWIZZLE_NONE, 128,
                                  uint32_t(Cfg::kSfAtomsK), ptr, 3, shape, stride, TmaOptions{});
     };
-    sf_map(&p.map_sfa, pr.sfa, pr.m);
-    sf_map(&p.map_sfb, pr.sfb, pr.n);
+    // m-grouped: B's scales are the groups' blocked arrays back to back, ceil(N / 128) row blocks
+    // each.
+    const int64_t nb = (pr.n + 127) / 128;
+    sf_map(&p.map_sfa, pr.sfa, (pr.m + 127) / 128);
+    sf_map(&p.map_sfb, pr.sfb, grouped ? nb * pr.groups : nb);
+    a.sfb_group_blocks = grouped ? int(nb) : 0;
   }
 
   const long long all_tiles = (long long)a.tiles_m * a.tiles_n * a.batch;

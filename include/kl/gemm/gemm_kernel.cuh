@@ -175,6 +175,7 @@ struct TnArgs {
   long long batch_stride_c;     // elements between the C matrices (direct-store epilogue)
   int c_reduce;                 // 0: C = result; 1: C += result (fp32 C: TMA reducing stores; 16-bit C: read, add, store)
   const int* m_block_group;     // m-grouped GEMM: B matrix of each 128-row block of A / C (-1 = padding)
+  int sfb_group_blocks;         // m-grouped block-scaled: 128-row scale blocks of each group's B
 };
 
 // Most peers an epilogue can push C tiles to (one NVLink/NVSwitch domain of 8 GPUs).
@@ -443,7 +444,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
 #pragma unroll
               for (int j = 0; j < Cfg::kSfbAtoms; ++j)
                 tma_load_3d(sfb_smem + stage * Cfg::kSfbBytes + 512u * Cfg::kSfAtomsK * j, &p.map_sfb, full_bar(stage),
-                            0, sy, (tn * Cfg::kTileN) / 128 + j);
+                            0, sy, gz * args.sfb_group_blocks + (tn * Cfg::kTileN) / 128 + j);
             }
           } else {
             // The leader's barrier counts the bytes of both CTAs; only the leader arrives.
@@ -466,7 +467,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
 #pragma unroll
               for (int j = 0; j < Cfg::kSfbAtoms; ++j)
                 tma_load_3d_pair(sfb_smem + stage * Cfg::kSfbBytes + 512u * Cfg::kSfAtomsK * j, &p.map_sfb, fb, 0, sy,
-                                 (tn * Cfg::kTileN) / 128 + j);
+                                 gz * args.sfb_group_blocks + (tn * Cfg::kTileN) / 128 + j);
             }
           }
           if (++stage == S) {

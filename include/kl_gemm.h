@@ -124,7 +124,8 @@ typedef struct kl_gemm_desc {
    * a padding block (its C rows come out 0, or C + 0). KL_ALGO_AUTO / KL_ALGO_1CTA: the one-CTA
    * tile kernel, any such layout; KL_ALGO_2CTA: the CTA pair, which takes each 256-row tile's
    * group from its first block, so groups must be padded to 256 rows (blocks 2i and 2i + 1 name the
-   * same group). K-major, batch 1, no block scaling. */
+   * same group). K-major, batch 1. With block scaling, sfb holds the groups' blocked scale arrays
+   * back to back (kl_block_scale_bytes(N, K, vec) bytes each) and sfa A's. */
   int32_t groups;
   int32_t reserved2; /* must be 0 */
   const int32_t* m_block_group;

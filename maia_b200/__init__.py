@@ -281,12 +281,13 @@ def block_scale_bytes(rows: int, k: int, vec: int = 32) -> int:
 
 
 def gemm_grouped(a, b, m_block_group, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=None,
-                 accumulate=False, algo=ALGO_1CTA, stream=None):
+                 accumulate=False, algo=ALGO_1CTA, sfa=None, sfb=None, scale_vec=32, stream=None):
     """m-grouped GEMM (mixture-of-experts layout): a [M, K] holds the groups' rows back to back,
     each group padded to a multiple of 128 rows; b [G, N, K] holds one matrix per group;
     m_block_group is an int32 device tensor of ceil(M / 128) entries naming the group of every
     128-row block (-1 = padding). out[rows of block i] = a[rows] @ b[m_block_group[i]].T.
-    algo=ALGO_2CTA runs the CTA-pair kernel, which needs the groups padded to 256 rows."""
+    algo=ALGO_2CTA runs the CTA-pair kernel, which needs the groups padded to 256 rows. Block
+    scaling: sfa = A's blocked scales, sfb = the groups' blocked scales concatenated."""
     import torch
 
     if b.dim() != 3 or a.dim() != 2 or b.shape[2] != a.shape[1]:
@@ -297,7 +298,8 @@ def gemm_grouped(a, b, m_block_group, out=None, *, out_dtype=None, alpha=1.0, sc
         raise ValueError("accumulate=True adds into `out`, which must be given")
     if out is None:
         out = torch.empty((a.shape[0], b.shape[1]), dtype=out_dtype or torch.bfloat16, device=a.device)
-    d = gemm_desc(a, b[0], out, alpha, scale_a, scale_b, algo, c_reduce=int(bool(accumulate)))
+    d = gemm_desc(a, b[0], out, alpha, scale_a, scale_b, algo, c_reduce=int(bool(accumulate)), sfa=sfa, sfb=sfb,
+                  scale_vec=scale_vec)
     pb = 2 if _dtype_code(b.dtype) == KL_E2M1 else 1
     d.groups = b.shape[0]
     d.stride_b = b.stride(0) * pb

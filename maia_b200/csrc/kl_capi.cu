@@ -249,8 +249,8 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
     // (it reads the group of each tile's first block), so it is used only when asked for.
     if (algo != KL_ALGO_AUTO && algo != KL_ALGO_1CTA && algo != KL_ALGO_2CTA)
       return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: m-grouped GEMMs run on the tile kernels (KL_ALGO_1CTA / 2CTA)");
-    if (batch > 1 || d->block_scale != 0 || a_mn || b_mn)
-      return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: m-grouped GEMMs take K-major operands, batch 1, no block scaling");
+    if (batch > 1 || a_mn || b_mn)
+      return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: m-grouped GEMMs take K-major operands, batch 1");
     if (algo == KL_ALGO_AUTO) algo = KL_ALGO_1CTA;
   }
   if (algo == KL_ALGO_AUTO && d->block_scale != 0)

@@ -107,3 +107,37 @@ def test_grouped_gemm_limits(cuda):
     assert e.value.status == kl.KL_ERR_NOT_SUPPORTED
     with pytest.raises(ValueError):
         kl.gemm_grouped(a, b, torch.zeros(1, dtype=torch.int32, device=cuda))  # too few block entries
+
+
+@pytest.mark.parametrize("algo", [kl.ALGO_1CTA, kl.ALGO_2CTA], ids=["1cta", "2cta"])
+@pytest.mark.parametrize("kind", ["e4m3", "e2m1"])
+def test_grouped_block_scaled(cuda, algo, kind):
+    """MoE experts in MX formats: B's block scales are the groups' blocked arrays back to back."""
+    from maia_b200 import workloads as wl
+
+    sizes, n, k = [256, 512, 256], 320, 512
+    rng = np.random.default_rng(len(kind))
+    qa_parts, sa_parts, qb, sb = [], [], [], []
+    for s in sizes:
+        q, sc = wl.mx_quantize(rng.standard_normal((s, k)).astype(np.float32), kind)
+        qa_parts.append(q)
+        sa_parts.append(sc)
+    for _ in sizes:
+        q, sc = wl.mx_quantize(rng.standard_normal((n, k)).astype(np.float32), kind)
+        qb.append(q)
+        sb.append(sc)
+    qa, sa = np.concatenate(qa_parts), np.concatenate(sa_parts)
+    blocks = np.repeat(np.arange(len(sizes), dtype=np.int32), [s // 128 for s in sizes])
+    a, b = to_device(qa, kind, cuda), to_device(np.stack(qb), kind, cuda)
+    psa = kl.pack_block_scales(torch.from_numpy(sa).to(cuda), k)
+    psb = torch.cat([kl.pack_block_scales(torch.from_numpy(x).to(cuda), k) for x in sb])
+    c = torch.full((qa.shape[0], n), float("nan"), dtype=torch.float32, device=cuda)
+    kl.gemm_grouped(a, b, torch.from_numpy(blocks).to(cuda), c, algo=algo, sfa=psa, sfb=psb)
+    torch.cuda.synchronize()
+    assert kl.read_status() == 0
+    got, r0 = c.cpu().numpy(), 0
+    for g, s in enumerate(sizes):
+        ref = og.gemm_mx_f64(qa_parts[g], qb[g], sa_parts[g], sb[g], kind)
+        elem, norm = og.rel_error(got[r0:r0 + s], ref)
+        assert elem <= 5e-2 and norm <= 5e-2, f"group {g}: {elem:.3e} / {norm:.3e}"
+        r0 += s
