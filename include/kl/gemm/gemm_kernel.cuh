@@ -1,17 +1,20 @@
 #pragma once
 
-// Persistent, warp-specialised dense GEMM for sm_100a:  C[M,N] = alpha * A[M,K] . B[N,K]^T
-// (both operands K-major, C row-major). No counterpart in the reference: kernel_lib ships the
-// descriptor encoders (tma_desc.hpp, umma_desc.hpp) this kernel is built from, but no kernel.
+// Persistent, warp-specialised dense GEMM for sm_100a:  C[M,N] (+)= alpha * A[M,K] . B[N,K]^T
+// (K-major operands by default, MN-major ones as options; C row-major), in bf16 / f16 / fp8 / fp4,
+// optionally block-scaled (MX, NVFP4), batched or m-grouped. No counterpart in the reference:
+// kernel_lib ships the descriptor encoders (tma_desc.hpp, umma_desc.hpp) this kernel is built
+// from, but no kernel.
 //
 // Roles (192 threads, or 320 with eight epilogue warps; one CTA per SM):
-//   warp 0      TMA producer: fills a Stages-deep ring of (A, B) K-blocks in shared memory.
+//   warp 0      TMA producer: fills a Stages-deep ring of (A, B[, scales]) K-blocks in shared memory.
 //   warp 1      MMA issuer: one thread issues tcgen05.mma into a TMEM accumulator and commits
 //               each consumed stage back to the producer; warp 1 also owns the TMEM allocation.
 //   warps 2..   epilogue: tcgen05.ld -> scale -> convert -> swizzled shared staging -> TMA store.
 // Two TMEM accumulators (2 x BlockN fp32 columns) let the epilogue of tile i overlap the main
-// loop of tile i + 1. Tiles are walked persistently in groups of `group_m` tile-rows so that the
-// CTAs running at the same time share A and B tiles in L2.
+// loop of tile i + 1 (block-scaled 256-column tiles keep one; see kNumAcc). Tiles are walked
+// persistently in groups of `group_m` tile-rows so that the CTAs running at the same time share A
+// and B tiles in L2.
 //
 // CtaGroup = 2 runs a CTA pair (cluster of 2) on a 256-row tile with cta_group::2 MMAs: each CTA
 // loads its own 128 rows of A and its own half of B (no multicast), the even CTA issues the MMAs,
@@ -168,11 +171,11 @@ struct TnArgs {
   int* status;                  // device word; timeout bits are ORed in
   unsigned long long timeout_ns;
   int prefetch;                 // L2 prefetch distance, in K-blocks of the producer's sequence (0 = off)
-  void* c;                      // C and its row pitch in elements, for the direct-store epilogue
+  void* c;                      // C and its row pitch in elements (direct-store epilogue; read for C += result)
   long long ldc;
   unsigned long long* clock_probe;  // optional: per CTA {clock64, globaltimer} at start and end
   int batch;                    // independent GEMMs (rank-3 tensor maps when > 1)
-  long long batch_stride_c;     // elements between the C matrices (direct-store epilogue)
+  long long batch_stride_c;     // elements between the C matrices (direct stores and C reads)
   int c_reduce;                 // 0: C = result; 1: C += result (fp32 C: TMA reducing stores; 16-bit C: read, add, store)
   const int* m_block_group;     // m-grouped GEMM: B matrix of each 128-row block of A / C (-1 = padding)
   int sfb_group_blocks;         // m-grouped block-scaled: 128-row scale blocks of each group's B
@@ -183,7 +186,7 @@ inline constexpr int kMaxPeers = 7;
 
 struct TnParams {
   CUtensorMap map_a;  // A [M, K], box {kBlockK, 128}
-  CUtensorMap map_b;  // B [N, K], box {kBlockK, kCtaN}
+  CUtensorMap map_b;  // B [N, K], box {kBlockK, kCtaN} (rank 3 [batch or groups, N, K] when batched / grouped)
   CUtensorMap map_c;  // C [M, N], box {kChunkCols, 32}
   // The same C block in other GPUs' memory (peer-mapped pointers): every finished tile is also
   // TMA-stored there, so a column-sharded GEMM leaves the whole C on every GPU with no separate
@@ -191,7 +194,7 @@ struct TnParams {
   CUtensorMap map_peer[kMaxPeers];
   int n_peers;
   // Block scales (TnConfig::kMx): the blocked arrays of A and B as [row blocks, K blocks, 128]
-  // 32-bit words, box {128, 1, 1} = one 512-byte atom.
+  // 32-bit words, box {128, kSfAtomsK, 1} = one stage's atoms of 128 rows.
   CUtensorMap map_sfa;
   CUtensorMap map_sfb;
   TnArgs args;
