@@ -289,8 +289,8 @@ kl_status kl_gemm_gather(const kl_gemm_desc* d, void* const* peer_c, int32_t n_p
   for (int q = 0; q < n_peers; ++q)
     if (peer_c[q] == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: null peer C");
   int algo = d->algo;
-  if (algo == KL_ALGO_AUTO || algo == KL_ALGO_SKINNY)
-    algo = d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA;
+  if (algo == KL_ALGO_AUTO || algo == KL_ALGO_SKINNY)  // m-grouped: the pair needs 256-row groups, so ask for it
+    algo = (d->m >= 256 && d->m_block_group == nullptr) ? KL_ALGO_2CTA : KL_ALGO_1CTA;
   if (algo != KL_ALGO_1CTA && algo != KL_ALGO_2CTA) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: unknown algo");
   if (d->c_reduce != 0 && d->c_reduce != 1)
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather: c_reduce must be 0 (store) or 1 (add)");

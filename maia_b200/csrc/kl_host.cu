@@ -75,6 +75,8 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_host: block scaling needs host scales of A and B (desc->sfa, desc->sfb)");
   if (h->a_major != 0 || h->b_major != 0)
     return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_host: K-major operands only (B is streamed by rows)");
+  if (h->m_block_group != nullptr)
+    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_host: m-grouped GEMMs take device buffers (kl_gemm)");
   cudaStream_t caller = static_cast<cudaStream_t>(stream_ptr);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -131,6 +131,8 @@ extern "C" kl_status kl_gemm_skinny_noalloc(const kl_gemm_desc* d, void* stream_
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_skinny_noalloc: m, n and k must be positive");
   if (d->m > 256) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_skinny_noalloc: at most 256 rows of A");
   if (d->batch > 1) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_skinny_noalloc: one problem per call");
+  if (d->m_block_group != nullptr || d->block_scale != 0)
+    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_skinny_noalloc: plain (not grouped, not block-scaled) GEMMs only");
   if (d->a_major != 0 || d->b_major != 0 || (d->swizzle != 0 && d->swizzle != 128))
     return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_skinny_noalloc: K-major operands with the 128-byte swizzle only");
   if (d->c_reduce != 0 && d->c_reduce != 1)
