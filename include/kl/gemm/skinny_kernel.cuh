@@ -17,6 +17,10 @@
 //
 // Roles as in gemm_kernel.cuh: warp 0 TMA producer (weights streamed with an L2 evict-first hint,
 // the small activation tile with evict-last), warp 1 MMA issuer, warps 2..5 epilogue.
+//
+// Block-scaled inputs (SfVec 32: MXFP8 / MXFP4, 16: NVFP4) work as in the tile kernels: each unit
+// brings the scale atoms of its 128 weight rows (the MMA's A) and of the tokens (the MMA's B) with
+// the K-block, and the MMA thread copies them into TMEM ahead of the block-scaled MMAs.
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -32,7 +36,7 @@
 
 namespace kl::gemm {
 
-template <typename InT, typename OutT, int TokPad, int Stages, int WSub = 1>
+template <typename InT, typename OutT, int TokPad, int Stages, int WSub = 1, int SfVec = 0>
 struct SkinnyConfig {
   using in_type = InT;
   using out_type = OutT;
@@ -45,8 +49,22 @@ struct SkinnyConfig {
   static constexpr int kStages = Stages;
   static constexpr int kNumAcc = 2;
   static constexpr int kAccCols = TokPad * WSub;           // one accumulator: WSub blocks of TokPad columns
-  static constexpr int kTmemCols = (kAccCols * 2 <= 32) ? 32 : (kAccCols * 2 <= 64) ? 64 : (kAccCols * 2 <= 128) ? 128
-                                 : (kAccCols * 2 <= 256) ? 256 : 512;
+  // Block scales: atoms along K per stage, token atoms (128 tokens each), MMAs per atom, bytes.
+  static constexpr int kSfVecSize = SfVec;
+  static constexpr bool kMx = SfVec != 0;
+  static constexpr bool kNv = SfVec == 16;
+  static constexpr bool kFp4 = std::is_same_v<InT, e2m1x2>;
+  static constexpr int kSfAtomsK = kMx ? (kFp4 ? 256 : 128) / (4 * SfVec) : 0;
+  static constexpr int kXAtoms = kMx ? (TokPad + 127) / 128 : 0;
+  static constexpr int kMmasPerSfAtom = kMx ? 4 / kSfAtomsK : 1;
+  static constexpr uint32_t kSfIdStep = 4u / uint32_t(kMmasPerSfAtom);
+  static constexpr uint32_t kSfwBytes = 512u * kSfAtomsK * WSub;
+  static constexpr uint32_t kSfxBytes = 512u * kSfAtomsK * kXAtoms;
+  static constexpr int kSfwCol = kAccCols * kNumAcc;       // TMEM columns of the weights' and tokens' scales
+  static constexpr int kSfxCol = kSfwCol + 4 * kSfAtomsK * WSub;
+  static constexpr int kTmemUsed = kAccCols * kNumAcc + 4 * kSfAtomsK * (WSub + kXAtoms);
+  static constexpr int kTmemCols = (kTmemUsed <= 32) ? 32 : (kTmemUsed <= 64) ? 64 : (kTmemUsed <= 128) ? 128
+                                 : (kTmemUsed <= 256) ? 256 : 512;
   using WTile = SmemTile<InT, 128, kBlockK>;               // one UMMA M = 128 box
   using XTile = SmemTile<InT, kTok, kBlockK>;
   static constexpr uint32_t kWBoxBytes = WTile::bytes;
@@ -54,15 +72,27 @@ struct SkinnyConfig {
   static constexpr uint32_t kXBytes = XTile::bytes;
   static constexpr uint32_t kOffW = 0;
   static constexpr uint32_t kOffX = kStages * kWBytes;
-  static constexpr uint32_t kOffBar = kOffX + kStages * kXBytes;
+  static constexpr uint32_t kOffSfw = kOffX + kStages * kXBytes;
+  static constexpr uint32_t kOffSfx = kOffSfw + kStages * kSfwBytes;
+  static constexpr uint32_t kOffBar = kOffSfx + kStages * kSfxBytes;
   static constexpr uint32_t kNumBars = 2 * kStages + 2 * kNumAcc + 1;
   static constexpr uint32_t kOffSlot = kOffBar + 8 * kNumBars;
   static constexpr uint32_t kSmemBytes = kOffSlot + 16 + 1024;
   static constexpr bool kIsF8 = sizeof(InT) == 1;
-  static constexpr uint32_t kIdesc = mma_instr_desc<InT, InT, float, 128, kTok>();
+  static constexpr uint32_t idesc() {
+    if constexpr (kNv)  // scale format bit 23: 0 = UE4M3
+      return mma_instr_desc_block_scaled<InT, InT, 128, kTok>() & ~(1u << 23);
+    else if constexpr (kMx)
+      return mma_instr_desc_block_scaled<InT, InT, 128, kTok>();
+    else
+      return mma_instr_desc<InT, InT, float, 128, kTok>();
+  }
+  static constexpr uint32_t kIdesc = idesc();
 
   static_assert(WSub == 1 || WSub == 2, "one or two 128-row weight boxes per tile");
-  static_assert(kAccCols * 2 <= 512, "two accumulators must fit in TMEM");
+  static_assert(kTmemUsed <= 512, "two accumulators (and the scales) must fit in TMEM");
+  static_assert(SfVec == 0 || SfVec == 32 || (SfVec == 16 && kFp4), "scales per 32 elements, or per 16 for fp4");
+  static_assert(!kFp4 || kMx, "packed fp4 operands are block-scaled");
   static_assert(TokPad == 16 || (TokPad % 32 == 0 && TokPad <= 256), "token tile: 16 or a multiple of 32 up to 256");
   static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
   static_assert(kWBytes % 1024 == 0 && kXBytes % 1024 == 0, "stages keep 1 KB alignment");
@@ -89,6 +119,8 @@ struct SkinnyArgs {
 struct SkinnyParams {
   CUtensorMap map_w;  // B [N, K], box {kBlockK, 128} (kSub boxes per tile)
   CUtensorMap map_x;  // A [M, K], box {kBlockK, TokPad}
+  CUtensorMap map_sfw;  // block scales of B and A (blocked arrays as [row blocks, K blocks, 128] words)
+  CUtensorMap map_sfx;
   SkinnyArgs args;
 };
 
@@ -149,6 +181,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_skinny_kernel(const __g
   const uint32_t base = (raw + 1023u) & ~1023u;
   const uint32_t w_smem = base + Cfg::kOffW;
   const uint32_t x_smem = base + Cfg::kOffX;
+  const uint32_t sfw_smem = base + Cfg::kOffSfw;
+  const uint32_t sfx_smem = base + Cfg::kOffSfx;
   const uint32_t bar0 = base + Cfg::kOffBar;
   const uint32_t tmem_slot = base + Cfg::kOffSlot;
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
@@ -214,13 +248,24 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_skinny_kernel(const __g
           ok = false;
           break;
         }
-        mbarrier_arrive_expect_tx(full_bar(stage), Cfg::kWBytes + Cfg::kXBytes);
+        mbarrier_arrive_expect_tx(full_bar(stage), Cfg::kWBytes + Cfg::kXBytes + Cfg::kSfwBytes + Cfg::kSfxBytes);
         const int kx = kb * Cfg::kBlockK;
 #pragma unroll
         for (int sub = 0; sub < Cfg::kSub; ++sub)
           tma_load_2d_hint(w_smem + stage * Cfg::kWBytes + sub * Cfg::kWBoxBytes, &p.map_w, full_bar(stage), kx,
                            tile * Cfg::kTileW + sub * 128, stream_policy);
         tma_load_2d_hint(x_smem + stage * Cfg::kXBytes, &p.map_x, full_bar(stage), kx, 0, keep_policy);
+        if constexpr (Cfg::kMx) {
+          const int sy = kb * Cfg::kSfAtomsK;
+#pragma unroll
+          for (int sub = 0; sub < Cfg::kSub; ++sub)
+            tma_load_3d(sfw_smem + stage * Cfg::kSfwBytes + 512u * Cfg::kSfAtomsK * sub, &p.map_sfw, full_bar(stage), 0,
+                        sy, tile * Cfg::kSub + sub);
+#pragma unroll
+          for (int j = 0; j < Cfg::kXAtoms; ++j)
+            tma_load_3d(sfx_smem + stage * Cfg::kSfxBytes + 512u * Cfg::kSfAtomsK * j, &p.map_sfx, full_bar(stage), 0,
+                        sy, j);
+        }
         if (++stage == S) {
           stage = 0;
           phase ^= 1u;
@@ -257,6 +302,25 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_skinny_kernel(const __g
           tcgen05_fence_after();
           const uint64_t w_desc = w_desc0 + ((stage * Cfg::kWBytes) >> 4);
           const uint64_t x_desc = x_desc0 + ((stage * Cfg::kXBytes) >> 4);
+          if constexpr (Cfg::kMx) {
+            // Scales to TMEM: weights' atom (sub, q) at kSfwCol + 4 (q * kSub + sub), tokens' (j, q)
+            // at kSfxCol + 4 (q * kXAtoms + j).
+#pragma unroll
+            for (int q = 0; q < Cfg::kSfAtomsK; ++q) {
+#pragma unroll
+              for (int sub = 0; sub < Cfg::kSub; ++sub)
+                tmem_cp_32x128b_warpx4<1>(tmem_base + Cfg::kSfwCol + 4 * (q * Cfg::kSub + sub),
+                                          encode_smem_desc(sfw_smem + stage * Cfg::kSfwBytes +
+                                                               512u * (sub * Cfg::kSfAtomsK + q),
+                                                           0, 128, UmmaLayout::SWIZZLE_NONE));
+#pragma unroll
+              for (int j = 0; j < Cfg::kXAtoms; ++j)
+                tmem_cp_32x128b_warpx4<1>(tmem_base + Cfg::kSfxCol + 4 * (q * Cfg::kXAtoms + j),
+                                          encode_smem_desc(sfx_smem + stage * Cfg::kSfxBytes +
+                                                               512u * (j * Cfg::kSfAtomsK + q),
+                                                           0, 128, UmmaLayout::SWIZZLE_NONE));
+            }
+          }
 #pragma unroll
           for (int k = 0; k < Cfg::kBlockK / Cfg::kUmmaK; ++k) {
             const uint64_t koff = block_offset_16B<typename Cfg::WTile>(k);
@@ -264,7 +328,19 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_skinny_kernel(const __g
 #pragma unroll
             for (int sub = 0; sub < Cfg::kSub; ++sub) {
               const uint64_t wd = w_desc + ((sub * Cfg::kWBoxBytes) >> 4) + koff;
-              if constexpr (Cfg::kIsF8)
+              if constexpr (Cfg::kMx) {
+                const int q = k / Cfg::kMmasPerSfAtom;
+                const uint32_t id = uint32_t(k % Cfg::kMmasPerSfAtom) * Cfg::kSfIdStep;
+                const uint32_t idesc = Cfg::kIdesc | (id << 29) | (id << 4);
+                const uint32_t sfw_t = tmem_base + Cfg::kSfwCol + 4 * (q * Cfg::kSub + sub);
+                const uint32_t sfx_t = tmem_base + Cfg::kSfxCol + 4 * Cfg::kXAtoms * q;
+                if constexpr (Cfg::kNv)
+                  umma_nvf4_ss<1>(d_tmem + sub * TOK, wd, x_desc + koff, idesc, sfw_t, sfx_t, accumulate);
+                else if constexpr (Cfg::kFp4)
+                  umma_mxf4_ss<1>(d_tmem + sub * TOK, wd, x_desc + koff, idesc, sfw_t, sfx_t, accumulate);
+                else
+                  umma_mxf8_ss<1>(d_tmem + sub * TOK, wd, x_desc + koff, idesc, sfw_t, sfx_t, accumulate);
+              } else if constexpr (Cfg::kIsF8)
                 umma_f8_ss<1>(d_tmem + sub * TOK, wd, x_desc + koff, Cfg::kIdesc, accumulate);
               else
                 umma_f16_ss<1>(d_tmem + sub * TOK, wd, x_desc + koff, Cfg::kIdesc, accumulate);

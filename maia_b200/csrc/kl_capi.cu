@@ -254,12 +254,10 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
     if (algo == KL_ALGO_AUTO) algo = KL_ALGO_1CTA;
   }
   if (algo == KL_ALGO_AUTO && d->block_scale != 0)
-    algo = d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA;
+    algo = kl::capi::choose_algo(*d);
   else if (algo == KL_ALGO_AUTO)
     algo = (batch > 1 || a_mn || b_mn || !default_swizzle) ? (d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA)
                                                            : kl::capi::choose_algo(*d);
-  if (algo == KL_ALGO_SKINNY && d->block_scale != 0)
-    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: block-scaled GEMMs run on the tile kernels (KL_ALGO_1CTA / KL_ALGO_2CTA)");
   if (algo == KL_ALGO_SKINNY && batch > 1) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: KL_ALGO_SKINNY is not batched");
   if (algo == KL_ALGO_SKINNY && (a_mn || b_mn))
     return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: KL_ALGO_SKINNY takes K-major operands");

@@ -35,6 +35,17 @@ constexpr int skinny_stages(int tok, int sub) {
 template <typename InT, typename OutT, int Tok, int Sub>
 using Skinny = SkinnyConfig<InT, OutT, Tok, skinny_stages(Tok, Sub), Sub>;
 
+// Block-scaled (SfVec V): the bf16/fp8 stage counts, fewer where the scale atoms (512 bytes per 128
+// rows and atom along K) push a stage past the ~200 KB budget.
+constexpr int skinny_mx_stages(int tok, bool fp4, int vec) {
+  const int atoms_k = (fp4 ? 256 : 128) / (4 * vec);
+  const int stage = 16384 + tok * 128 + 512 * atoms_k * (1 + (tok + 127) / 128);
+  const int fit = 204800 / stage;
+  return fit < skinny_stages(tok, 1) ? fit : skinny_stages(tok, 1);
+}
+template <typename InT, typename OutT, int Tok, int V>
+using SkinnyMx = SkinnyConfig<InT, OutT, Tok, skinny_mx_stages(Tok, std::is_same_v<InT, kl::e2m1x2>, V), 1, V>;
+
 struct Plan {
   int tok = 0;
   int sub = 1;  // 128-row weight boxes per tile
@@ -52,10 +63,13 @@ kl_status make_plan(kl_gemm_desc const& d, Plan* p) {
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
-  const int elem = d.ab_type == KL_E4M3 ? 1 : 2;
-  const int block_k = 128 / elem;
+  // Elements per 128-byte K-block: 64 (16-bit), 128 (8-bit), 256 (packed fp4).
+  const int block_k = d.ab_type == KL_E2M1 ? 256 : (d.ab_type == KL_E4M3 || d.ab_type == KL_E5M2) ? 128 : 64;
+  if (d.block_scale != 0 && d.m > 128)
+    return fail(KL_ERR_INVALID_ARGUMENT, "KL_ALGO_SKINNY with block scaling handles at most 128 rows of A");
   p->tok = token_tile(d.m);
   p->sub = d.variant == 2 ? 2 : d.variant == 1 ? 1 : kDefaultSkinnySub;
+  if (d.block_scale != 0) p->sub = 1;
   if (p->sub == 2 && p->tok > 128) p->sub = 1;  // two 256-token accumulators would not fit in TMEM
   if (d.variant < 0 || d.variant > 2) return fail(KL_ERR_INVALID_ARGUMENT, "KL_ALGO_SKINNY variant must be 0, 1 or 2");
   p->n_tiles = int((d.n + 128 * p->sub - 1) / (128 * p->sub));
@@ -84,8 +98,26 @@ kl_status launch(kl_gemm_desc const& d, Plan const& pl, void* ws, cudaStream_t s
     configured[dev] = 1;
   }
   SkinnyParams p{};
-  p.map_w = make_tma_load<typename Cfg::WTile>(row_major_strided(static_cast<InT const*>(d.b), d.n, d.k, d.ldb)).map;
-  p.map_x = make_tma_load<typename Cfg::XTile>(row_major_strided(static_cast<InT const*>(d.a), d.m, d.k, d.lda)).map;
+  // Packed fp4: K and the pitches count elements, the maps bytes.
+  constexpr int64_t pack = Cfg::kFp4 ? 2 : 1;
+  if (d.k % pack != 0 || d.lda % pack != 0 || d.ldb % pack != 0)
+    throw std::invalid_argument("kl::gemm: packed fp4 needs even K and leading dimensions");
+  p.map_w = make_tma_load<typename Cfg::WTile>(
+                row_major_strided(static_cast<InT const*>(d.b), d.n, d.k / pack, d.ldb / pack)).map;
+  p.map_x = make_tma_load<typename Cfg::XTile>(
+                row_major_strided(static_cast<InT const*>(d.a), d.m, d.k / pack, d.lda / pack)).map;
+  if constexpr (Cfg::kMx) {
+    if (d.sfa == nullptr || d.sfb == nullptr) throw std::invalid_argument("kl::gemm: block scaling needs scales of A and B");
+    const int64_t kb = (d.k + 4 * Cfg::kSfVecSize - 1) / (4 * Cfg::kSfVecSize);
+    auto sf_map = [&](CUtensorMap* map, void const* ptr, int64_t rows) {
+      const int64_t shape[3] = {(rows + 127) / 128, kb, 128};
+      const int64_t stride[3] = {kb * 128, 128, 1};
+      kl::detail::encode_tma_map(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, CU_TENSOR_MAP_SWIZZLE_NONE, 128,
+                                 uint32_t(Cfg::kSfAtomsK), ptr, 3, shape, stride, TmaOptions{});
+    };
+    sf_map(&p.map_sfw, d.sfb, d.n);
+    sf_map(&p.map_sfx, d.sfa, d.m);
+  }
   if (d.ldc < d.n) throw std::invalid_argument("kl_gemm: ldc < n");
   if (reinterpret_cast<uintptr_t>(d.c) % (d.c_type == KL_F32 ? 4 : 2) != 0)
     throw std::invalid_argument("kl_gemm: C is not aligned to its element size");
@@ -129,6 +161,16 @@ kl_status dispatch_tok(kl_gemm_desc const& d, Plan const& pl, void* ws, cudaStre
     case 64: return launch<Skinny<InT, OutT, 64, 1>>(d, pl, ws, stream);
     case 128: return launch<Skinny<InT, OutT, 128, 1>>(d, pl, ws, stream);
     default: return launch<Skinny<InT, OutT, 256, 1>>(d, pl, ws, stream);
+  }
+}
+
+template <typename InT, typename OutT, int V>
+kl_status dispatch_tok_mx(kl_gemm_desc const& d, Plan const& pl, void* ws, cudaStream_t stream) {
+  switch (pl.tok) {
+    case 16: return launch<SkinnyMx<InT, OutT, 16, V>>(d, pl, ws, stream);
+    case 32: return launch<SkinnyMx<InT, OutT, 32, V>>(d, pl, ws, stream);
+    case 64: return launch<SkinnyMx<InT, OutT, 64, V>>(d, pl, ws, stream);
+    default: return launch<SkinnyMx<InT, OutT, 128, V>>(d, pl, ws, stream);
   }
 }
 
@@ -197,6 +239,13 @@ int choose_algo(kl_gemm_desc const& d) {
   // 64 rows (the one-CTA tile kernel 5.90), but at 128 rows its MMAs no longer hide behind the
   // stream and the one-CTA tile kernel (112 weight bands of 256 rows) is ahead, 5.88 vs 5.68 TB/s.
   // fp8 halves the MMA work per byte, so it stays on the skinny kernel up to 128 rows.
+  if (d.block_scale != 0) {
+    // Block-scaled decode shapes (MXFP8 / MXFP4 / NVFP4 weights, bf16 C) stream on the skinny
+    // kernel up to 128 rows.
+    const bool bs_skinny = d.c_type == KL_BF16 && (d.ab_type == KL_E2M1 || (d.ab_type == KL_E4M3 && d.block_scale == 1));
+    if (bs_skinny && d.m <= 128 && d.m_block_group == nullptr) return KL_ALGO_SKINNY;
+    return d.m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA;
+  }
   const bool bf16_skinny = d.ab_type == KL_BF16 && (d.c_type == KL_BF16 || d.c_type == KL_F32);
   const bool fp8_skinny = d.ab_type == KL_E4M3 && d.c_type == KL_BF16;
   if ((bf16_skinny && d.m <= 64) || (fp8_skinny && d.m <= 128)) return KL_ALGO_SKINNY;
@@ -225,6 +274,15 @@ kl_status run_skinny(kl_gemm_desc const& d, void* workspace, size_t workspace_by
                 "kl_gemm_ws: workspace of " + std::to_string(workspace_bytes) + " bytes, need " + std::to_string(need));
   } else if (reinterpret_cast<uintptr_t>(ws) % 16 != 0) {
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_ws: workspace must be 16-byte aligned");
+  }
+  if (d.block_scale == 1) {
+    if (d.ab_type == KL_E4M3 && d.c_type == KL_BF16) return dispatch_tok_mx<kl::e4m3, kl::bf16, 32>(d, pl, ws, stream);
+    if (d.ab_type == KL_E2M1 && d.c_type == KL_BF16) return dispatch_tok_mx<kl::e2m1x2, kl::bf16, 32>(d, pl, ws, stream);
+    return fail(KL_ERR_NOT_SUPPORTED, "KL_ALGO_SKINNY with MX scales supports (A/B, C) = (e4m3, bf16), (e2m1, bf16)");
+  }
+  if (d.block_scale == 2) {
+    if (d.ab_type == KL_E2M1 && d.c_type == KL_BF16) return dispatch_tok_mx<kl::e2m1x2, kl::bf16, 16>(d, pl, ws, stream);
+    return fail(KL_ERR_NOT_SUPPORTED, "KL_ALGO_SKINNY with NVFP4 scales supports (A/B, C) = (e2m1, bf16)");
   }
   if (d.ab_type == KL_BF16 && d.c_type == KL_BF16) return dispatch_tok<kl::bf16, kl::bf16>(d, pl, ws, stream);
   if (d.ab_type == KL_BF16 && d.c_type == KL_F32) return dispatch_tok<kl::bf16, float>(d, pl, ws, stream);

@@ -215,3 +215,36 @@ def test_mx_reduce_into_bf16_c(cuda, algo):
     c = c0.to(cuda)
     got = run_mx(qa, sa, qb, sb, "e4m3", "bf16", cuda, c=c, algo=algo, accumulate=True)
     check_mx(got, qa, sa, qb, sb, "e4m3", c0=c0.float().numpy().astype(np.float64))
+
+
+@pytest.mark.parametrize("kind,vec", [("e4m3", 32), ("e2m1", 32), ("e2m1", 16)], ids=["mxfp8", "mxfp4", "nvfp4"])
+@pytest.mark.parametrize("m", [1, 16, 40, 64, 128])
+def test_block_scaled_decode_skinny(cuda, kind, vec, m):
+    """Decode shapes on the stream-K skinny kernel with block scales (weights' scales on the MMA's A
+    side, the tokens' on its B side); K split across CTAs for the 3200-row weight matrix."""
+    n, k = 3200, 2048
+    rng = np.random.default_rng(m + vec)
+    xa = rng.standard_normal((m, k)).astype(np.float32)
+    xb = (rng.standard_normal((n, k)) * 0.05).astype(np.float32)
+    if vec == 16:
+        qa, sa, ga = wl.nv_quantize(xa)
+        qb, sb, gb = wl.nv_quantize(xb)
+        ref = og.gemm_nv_f64(qa, qb, sa, sb, ga * gb)
+        scales = dict(scale_a=torch.tensor([ga], device=cuda), scale_b=torch.tensor([gb], device=cuda))
+    else:
+        qa, sa = wl.mx_quantize(xa, kind)
+        qb, sb = wl.mx_quantize(xb, kind)
+        ref = og.gemm_mx_f64(qa, qb, sa, sb, kind)
+        scales = {}
+    psa = kl.pack_block_scales(torch.from_numpy(sa).to(cuda), k, vec)
+    psb = kl.pack_block_scales(torch.from_numpy(sb).to(cuda), k, vec)
+    a, b = to_device(qa, kind, cuda), to_device(qb, kind, cuda)
+    for algo in (kl.ALGO_SKINNY, kl.ALGO_AUTO):
+        c = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=cuda)
+        kl.gemm(a, b, c, sfa=psa, sfb=psb, scale_vec=vec, algo=algo, **scales)
+        torch.cuda.synchronize()
+        assert kl.read_status() == 0
+        got = c.float().cpu().numpy()
+        assert not np.isnan(got).any()
+        elem, norm = og.rel_error(got, ref)
+        assert elem <= FP8_TOL and norm <= FP8_TOL, f"algo {algo}: {elem:.3e} / {norm:.3e}"
