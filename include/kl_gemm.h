@@ -150,6 +150,15 @@ KL_API kl_status kl_pack_block_scales(const void* src, int64_t rows, int64_t k, 
 KL_API kl_status kl_mx_pack_scales(const void* src, int64_t rows, int64_t k, int64_t ld_src, void* dst,
                                    void* stream); /* vec = 32 */
 
+/* Device: MX quantisation (OCP Microscaling Formats v1.0) of x [rows, k] (KL_F32 or KL_BF16, row
+ * pitch ldx elements; k a multiple of 32) into q (KL_E4M3: [rows, ldq] bytes; KL_E2M1: packed,
+ * ldq elements = ldq / 2 bytes per row) and the blocked UE8M0 scales (kl_block_scale_bytes(rows,
+ * k, 32) bytes, padding included): per 32 elements, scale 2^(floor(log2(amax)) - emax) with emax 8
+ * (e4m3) or 2 (e2m1), elements x / scale rounded to nearest even, saturating. Stream-ordered; the
+ * outputs feed kl_gemm with block_scale = 1 directly. */
+KL_API kl_status kl_mx_quantize(const void* x, int32_t x_type, int64_t rows, int64_t k, int64_t ldx, int32_t q_type,
+                                void* q, int64_t ldq, void* scales, void* stream);
+
 /* Library version: major * 10000 + minor * 100 + patch. */
 KL_API int32_t kl_version(void);
 

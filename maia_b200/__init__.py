@@ -35,7 +35,7 @@ EXPORTED = (
     "kl_make_tma_desc", "kl_gemm_skinny_noalloc", "kl_gemm_host", "kl_gemm_clock_probe", "kl_gemm_gather",
     "kl_ipc_get_handle", "kl_ipc_open_handle", "kl_ipc_close", "kl_umma_smem_desc_mn", "kl_mma_instr_desc_major",
     "kl_mma_instr_desc_block_scaled", "kl_mx_scale_bytes", "kl_mx_pack_scales", "kl_block_scale_bytes",
-    "kl_pack_block_scales",
+    "kl_pack_block_scales", "kl_mx_quantize",
 )
 
 
@@ -116,6 +116,7 @@ def lib() -> ctypes.CDLL:
             "kl_mx_pack_scales": (i32, [vp, i64, i64, i64, vp, vp]),
             "kl_block_scale_bytes": (i64, [i64, i64, i32]),
             "kl_pack_block_scales": (i32, [vp, i64, i64, i32, i64, vp, vp]),
+            "kl_mx_quantize": (i32, [vp, i32, i64, i64, i64, i32, vp, i64, vp, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -327,6 +328,25 @@ def pack_block_scales(scales, k: int, vec: int = 32, out=None, stream=None):
     check(lib().kl_pack_block_scales(ctypes.c_void_p(scales.data_ptr()), rows, int(k), int(vec), scales.stride(0),
                                      ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(s)))
     return out
+
+
+def mx_quantize(x, kind: str = "e4m3", stream=None):
+    """MX-quantise x (fp32 or bf16 device tensor [rows, K], K a multiple of 32) on the device:
+    returns (q, scales) with q float8_e4m3fn [rows, K] or float4_e2m1fn_x2 [rows, K/2] and scales
+    the blocked UE8M0 array, ready for gemm(..., sfa=scales)."""
+    import torch
+
+    rows, k = x.shape
+    if x.stride(1) != 1:
+        raise ValueError("x must have a contiguous last dimension")
+    fp4 = kind == "e2m1"
+    q = torch.empty((rows, k // 2 if fp4 else k), dtype=torch.uint8, device=x.device)
+    sc = torch.empty(block_scale_bytes(rows, k, 32), dtype=torch.uint8, device=x.device)
+    s = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
+    check(lib().kl_mx_quantize(ctypes.c_void_p(x.data_ptr()), _dtype_code(x.dtype), rows, k, x.stride(0),
+                               KL_E2M1 if fp4 else KL_E4M3, ctypes.c_void_p(q.data_ptr()), k, ctypes.c_void_p(sc.data_ptr()),
+                               ctypes.c_void_p(s)))
+    return q.view(torch.float4_e2m1fn_x2 if fp4 else torch.float8_e4m3fn), sc
 
 
 def mx_pack_scales(scales, k: int, out=None, stream=None):

@@ -248,3 +248,43 @@ def test_block_scaled_decode_skinny(cuda, kind, vec, m):
         assert not np.isnan(got).any()
         elem, norm = og.rel_error(got, ref)
         assert elem <= FP8_TOL and norm <= FP8_TOL, f"algo {algo}: {elem:.3e} / {norm:.3e}"
+
+
+@pytest.mark.parametrize("kind", ["e4m3", "e2m1"])
+@pytest.mark.parametrize("src", ["f32", "bf16"])
+@pytest.mark.parametrize("rows,k", [(1, 32), (200, 320), (129, 1024)])
+def test_device_mx_quantize_matches_reference(cuda, kind, src, rows, k):
+    """kl_mx_quantize = the OCP MX quantisation restated in maia_b200.workloads.mx_quantize: the same
+    scales bit for bit, the same element values (compared as values: the device may encode a
+    negative value that rounds to zero as -0)."""
+    rng = np.random.default_rng(rows + k)
+    x = (rng.standard_normal((rows, k)) * np.exp2(rng.uniform(-8, 8, (rows, 1)))).astype(np.float32)
+    if src == "bf16":
+        x = wl.bf16_bits_to_f32(wl.f32_to_bf16_bits(x))
+    xt = torch.from_numpy(x).to(cuda)
+    if src == "bf16":
+        xt = xt.to(torch.bfloat16)
+    q, sc = kl.mx_quantize(xt, kind)
+    torch.cuda.synchronize()
+    want_q, want_s = wl.mx_quantize(x, kind)
+    np.testing.assert_array_equal(sc.cpu().numpy(), og.pack_mx_scales(want_s, k))
+    got_v = og.decode(q.view(torch.uint8).cpu().numpy(), kind)
+    np.testing.assert_array_equal(got_v, og.decode(want_q, kind))
+
+
+@pytest.mark.parametrize("kind", ["e4m3", "e2m1"])
+def test_device_quantize_then_gemm(cuda, kind):
+    """Activations and weights quantised on the device feed the block-scaled GEMM directly."""
+    rng = np.random.default_rng(9)
+    xa = rng.standard_normal((256, 512)).astype(np.float32)
+    xb = rng.standard_normal((384, 512)).astype(np.float32)
+    qa, sa = kl.mx_quantize(torch.from_numpy(xa).to(cuda), kind)
+    qb, sb = kl.mx_quantize(torch.from_numpy(xb).to(cuda), kind)
+    c = kl.gemm(qa, qb, sfa=sa, sfb=sb, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert kl.read_status() == 0
+    ra, rsa = wl.mx_quantize(xa, kind)
+    rb, rsb = wl.mx_quantize(xb, kind)
+    ref = og.gemm_mx_f64(ra, rb, rsa, rsb, kind)
+    elem, norm = og.rel_error(c.cpu().numpy(), ref)
+    assert elem <= FP8_TOL and norm <= FP8_TOL
