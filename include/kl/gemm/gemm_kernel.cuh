@@ -76,6 +76,10 @@ struct TnConfig {
   static constexpr bool kMx = SfVec != 0;
   static constexpr bool kNv = SfVec == 16;
   static constexpr bool kFp4 = std::is_same_v<InT, e2m1x2>;
+  // Packed fp6 (e3m2 / e2m3): one element per shared-memory byte like fp8 (TMA's 16U6 type unpacks
+  // 12 bytes into each 16-byte slot), consumed by kind::mxf8f6f4 like MXFP8; a stage's TMA
+  // transactions count the packed bytes, 3/4 of the tile's shared-memory footprint.
+  static constexpr bool kFp6 = is_fp6<InT>;
   // A tile of B rows [tn * BlockN, +BlockN) starts r = (tn * BlockN) % 128 rows into a 128-row
   // scale block, r a multiple of gcd(BlockN, 128) >= 32: the tile's scales span kSfbAtoms blocks,
   // copied to TMEM side by side, and the MMAs read them from word r / 32 on (row r + j of the first
@@ -123,6 +127,7 @@ struct TnConfig {
 
   static constexpr uint32_t kABytes = ATile::bytes;
   static constexpr uint32_t kBBytes = BTile::bytes;
+  static constexpr uint32_t kStageTx = (kFp6 ? (kABytes + kBBytes) / 4 * 3 : kABytes + kBBytes) + kSfaBytes + kSfbBytes;
   static constexpr uint32_t kCBytes = CBox::bytes;     // 4 KB per staging buffer
   static constexpr uint32_t kOffA = 0;
   static constexpr uint32_t kOffB = kOffA + kStages * kABytes;
@@ -151,6 +156,7 @@ struct TnConfig {
                 "block-scaled: 8-bit or packed fp4 K-major operands, 128-byte swizzle, tile N a multiple of 32");
   static_assert(SfVec == 0 || SfVec == 32 || (SfVec == 16 && kFp4), "scales per 32 elements, or per 16 for fp4");
   static_assert(!kFp4 || kMx, "packed fp4 operands are block-scaled (kind::mxf4 / mxf4nvf4)");
+  static_assert(!kFp6 || SfVec == 32, "fp6 operands are MX block-scaled (kind::mxf8f6f4, a scale per 32)");
   static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
   static_assert(BlockN % (16 * CtaGroup) == 0 && BlockN <= 256, "UMMA N");
   static_assert(kCtaN % 8 == 0 && kCtaN <= 256, "B tile rows");
@@ -430,7 +436,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
           }
           const int kx = kb * Cfg::kBlockK;
           if constexpr (CG == 1) {
-            mbarrier_arrive_expect_tx(full_bar(stage), Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes + Cfg::kSfbBytes);
+            mbarrier_arrive_expect_tx(full_bar(stage), Cfg::kStageTx);
             load_operand<typename Cfg::ATile, Cfg::kAMn, 1>(a_smem + stage * Cfg::kABytes, &p.map_a, full_bar(stage),
                                                             kx, a_row, bz, batched);
             if (args.m_block_group != nullptr)
@@ -452,8 +458,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
           } else {
             // The leader's barrier counts the bytes of both CTAs; only the leader arrives.
             if (cta_rank == 0)
-              mbarrier_arrive_expect_tx(full_bar(stage),
-                                        2u * (Cfg::kABytes + Cfg::kBBytes + Cfg::kSfaBytes + Cfg::kSfbBytes));
+              mbarrier_arrive_expect_tx(full_bar(stage), 2u * Cfg::kStageTx);
             const uint32_t fb = leader_full0 + 8u * stage;
             load_operand<typename Cfg::ATile, Cfg::kAMn, 2>(a_smem + stage * Cfg::kABytes, &p.map_a, fb, kx, a_row, bz,
                                                             batched);

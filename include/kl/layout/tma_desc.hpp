@@ -191,6 +191,47 @@ inline void encode_tma_map(CUtensorMap* out, CUtensorMapDataType dtype, int elem
   if (res != CUDA_SUCCESS) tma_fail("cuTensorMapEncodeTiled failed with CUresult " + std::to_string(int(res)));
 }
 
+// The same for packed fp6 (kl::e3m2 / kl::e2m3): TMA's 16U6_ALIGN16B data type reads 16 elements
+// (12 bytes) of global memory into every 16-byte slot of shared memory. Shapes, strides and boxes
+// count elements; the driver's rules for this type (cuTensorMapEncodeTiled, CUDA 12.8+): the base
+// 32-byte aligned, the innermost extent a multiple of 128 elements, every stride a multiple of 32
+// bytes (= 128 elements), the box 128 elements wide, and 128-byte swizzle (or none). A tile's x
+// coordinate is then always a multiple of 128 elements (96 bytes).
+inline void encode_tma_map_u6(CUtensorMap* out, CUtensorMapSwizzle swizzle, uint32_t box_inner, uint32_t box_outer,
+                              void const* gmem, int R, int64_t const* shape, int64_t const* stride,
+                              TmaOptions const& opt) {
+  if (R < 2 || R > 5) tma_fail("TMA tensors have 2 to 5 modes");
+  if (box_inner != 128) tma_fail("packed fp6 boxes are 128 elements wide");
+  if (swizzle != CU_TENSOR_MAP_SWIZZLE_128B && swizzle != CU_TENSOR_MAP_SWIZZLE_NONE)
+    tma_fail("packed fp6 tiles use 128-byte swizzle");
+  if (reinterpret_cast<uintptr_t>(gmem) % 32 != 0) tma_fail("packed fp6: global address must be 32-byte aligned");
+  if (shape[R - 1] % 128 != 0) tma_fail("packed fp6: the innermost extent must be a multiple of 128 elements");
+  for (int i = 0; i < R - 1; ++i)
+    if (stride[i] <= 0 || stride[i] % 128 != 0)
+      tma_fail("packed fp6: outer strides must be positive multiples of 128 elements (32 bytes)");
+  if (stride[R - 1] != 1) tma_fail("the last mode must be contiguous (stride 1)");
+  if (stride[R - 2] < shape[R - 1]) tma_fail("rows overlap: the row stride is smaller than cols");
+  uint64_t dims[5], strides[4];
+  uint32_t box[5], elem_strides[5];
+  for (int i = 0; i < R; ++i) {
+    if (shape[i] < 1 || shape[i] > (int64_t(1) << 32)) tma_fail("extents must be in [1, 2^32]");
+    dims[i] = static_cast<uint64_t>(shape[R - 1 - i]);
+    box[i] = i == 0 ? box_inner : i == 1 ? box_outer : 1;
+    elem_strides[i] = 1;
+  }
+  for (int i = 1; i < R; ++i) {
+    strides[i - 1] = static_cast<uint64_t>(stride[R - 1 - i]) * 3 / 4;  // 6 bits per element
+    if (strides[i - 1] >= (uint64_t(1) << 40)) tma_fail("outer strides must be below 2^40 bytes");
+  }
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) tma_fail("cuTensorMapEncodeTiled is unavailable (no CUDA driver)");
+  *out = CUtensorMap{};
+  CUresult res = encode(out, CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B, static_cast<cuuint32_t>(R), const_cast<void*>(gmem),
+                        dims, strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, opt.l2_promotion,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (res != CUDA_SUCCESS) tma_fail("cuTensorMapEncodeTiled failed with CUresult " + std::to_string(int(res)));
+}
+
 }  // namespace detail
 
 // Describe a global tensor for TMA (build it with kl::row_major / row_major_strided). The last mode
@@ -205,8 +246,14 @@ TmaDesc<Tile, Direction, R> make_tma_desc(GmemTensor<G, R> const& g, TmaOptions 
   static_assert(R >= 2 && R <= 5, "TMA tensors have 2 to 5 modes");
   static_assert(!(std::is_same_v<Direction, TmaStoreTag> && std::is_const_v<G>), "a TMA store needs a non-const tensor");
   TmaDesc<Tile, Direction, R> desc{};
-  detail::encode_tma_map(&desc.map, tma_dtype<T>(), bits_of<T> / 8, tma_swizzle<typename Tile::swizzle>(), Box::inner,
-                         Box::outer, g.ptr, R, g.shape, g.stride, opt);
+  if constexpr (is_fp6<T>) {
+    static_assert(std::is_same_v<Direction, TmaLoadTag>, "packed fp6 tensors are read-only here");
+    detail::encode_tma_map_u6(&desc.map, tma_swizzle<typename Tile::swizzle>(), Box::inner, Box::outer, g.ptr, R,
+                              g.shape, g.stride, opt);
+  } else {
+    detail::encode_tma_map(&desc.map, tma_dtype<T>(), bits_of<T> / 8, tma_swizzle<typename Tile::swizzle>(),
+                           Box::inner, Box::outer, g.ptr, R, g.shape, g.stride, opt);
+  }
   return desc;
 }
 

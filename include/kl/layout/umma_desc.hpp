@@ -186,6 +186,8 @@ KL_HOST_DEVICE constexpr uint32_t umma_operand_format() {
   else if constexpr (std::is_same_v<T, float>) return 2; // kind::tf32 (fp32 storage read as tf32)
   else if constexpr (std::is_same_v<T, e4m3>) return 0;  // kind::f8f6f4
   else if constexpr (std::is_same_v<T, e5m2>) return 1;  // kind::f8f6f4
+  else if constexpr (std::is_same_v<T, e2m3>) return 3;  // kind::f8f6f4 / mxf8f6f4
+  else if constexpr (std::is_same_v<T, e3m2>) return 4;  // kind::f8f6f4 / mxf8f6f4
   else if constexpr (std::is_same_v<T, e2m1x2>) return 1;  // kind::mxf4 / mxf4nvf4 (packed e2m1)
   else if constexpr (std::is_same_v<T, uint8_t>) return 0;  // kind::i8
   else if constexpr (std::is_same_v<T, int8_t>) return 1;   // kind::i8

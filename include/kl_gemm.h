@@ -48,7 +48,10 @@ typedef enum kl_dtype {
   KL_I32 = 7,
   KL_E2M1 = 8,  /* fp4, two per byte (first in the low nibble); extents and pitches count elements */
   KL_UE8M0 = 9, /* block-scale formats */
-  KL_UE4M3 = 10
+  KL_UE4M3 = 10,
+  KL_E3M2 = 11, /* fp6, packed: element i of a row at bits [6i, 6i + 6) of its bytes (four in three);
+                 * extents and pitches count elements */
+  KL_E2M3 = 12
 } kl_dtype;
 
 typedef enum kl_algo {
@@ -70,8 +73,9 @@ typedef struct kl_gemm_desc {
   int64_t ldb;
   void* c;       /* device, [m, ldc] */
   int64_t ldc;
-  int32_t ab_type;        /* kl_dtype of A and B: KL_BF16, KL_F16, KL_E4M3, KL_E5M2, or KL_E2M1
-                             (packed fp4, with block_scale = 1 only) */
+  int32_t ab_type;        /* kl_dtype of A and B: KL_BF16, KL_F16, KL_E4M3, KL_E5M2, KL_E2M1
+                             (packed fp4, block-scaled only) or KL_E3M2 / KL_E2M3 (packed fp6,
+                             block_scale = 1 only) */
   int32_t c_type;         /* kl_dtype of C. (ab_type, c_type): (bf16, bf16), (bf16, f32), (f16, f16),
                              (f16, f32), (e4m3, bf16), (e4m3, f32), (e5m2, bf16), (e5m2, f32).
                              KL_ALGO_SKINNY: (bf16, bf16), (bf16, f32), (e4m3, bf16) */
@@ -105,14 +109,16 @@ typedef struct kl_gemm_desc {
   int32_t swizzle;
   /* Block scaling. 2 (NVFP4): ab_type KL_E2M1 with one UE4M3 scale (an e4m3 value, sign 0) per 16
    * K-elements, blocked by kl_pack_block_scales(vec 16); otherwise as for 1.
-   * 0: none. 1 (MX): ab_type KL_E4M3, KL_E5M2 or KL_E2M1 with one UE8M0 scale (value
+   * 0: none. 1 (MX): ab_type KL_E4M3, KL_E5M2, KL_E2M1, KL_E3M2 or KL_E2M3 with one UE8M0 scale (value
    * 2^(s - 127)) per 32 consecutive K-elements of every row of A and of B, in `sfa` / `sfb`
    * (device), stored in the 128 x 4 blocked layout that kl_mx_pack_scales writes:
    * kl_mx_scale_bytes(rows, k) bytes. C = alpha * sum_k (A[m,k] sfa[m,k/32]) (B[n,k] sfb[n,k/32])
    * [* *scale_a * *scale_b]; C bf16 or f32 (KL_ALGO_2CTA: variant 0/1 = 256 x 256 tiles on a CTA
    * pair, 2 = 256 x 128, 3 = 256 x 192; KL_ALGO_1CTA: variant 0/1 = 128 x 256, 2 = 128 x 128;
    * KL_ALGO_SKINNY: up to 128 rows of A, bf16 C, e4m3 or e2m1; KL_ALGO_AUTO: skinny up to 128 rows,
-   * the pair from 256), K-major operands, 128-byte swizzle, batch 1. */
+   * the pair from 256), K-major operands, 128-byte swizzle, batch 1. fp6 (KL_E3M2 / KL_E2M3, tile
+   * kernels only): K, lda, ldb and stride_b multiples of 128 elements (96 bytes), A and B 32-byte
+   * aligned. */
   int32_t block_scale;
   int32_t reserved; /* must be 0 */
   const void* sfa;
@@ -152,10 +158,11 @@ KL_API kl_status kl_mx_pack_scales(const void* src, int64_t rows, int64_t k, int
 
 /* Device: MX quantisation (OCP Microscaling Formats v1.0) of x [rows, k] (KL_F32 or KL_BF16, row
  * pitch ldx elements; k a multiple of 32) into q (KL_E4M3: [rows, ldq] bytes; KL_E2M1: packed,
- * ldq elements = ldq / 2 bytes per row) and the blocked UE8M0 scales (kl_block_scale_bytes(rows,
- * k, 32) bytes, padding included): per 32 elements, scale 2^(floor(log2(amax)) - emax) with emax 8
- * (e4m3) or 2 (e2m1), elements x / scale rounded to nearest even, saturating. Stream-ordered; the
- * outputs feed kl_gemm with block_scale = 1 directly. */
+ * ldq elements = ldq / 2 bytes per row; KL_E3M2 / KL_E2M3: packed fp6, ldq a multiple of 128
+ * elements = 3 ldq / 4 bytes per row) and the blocked UE8M0 scales (kl_block_scale_bytes(rows, k,
+ * 32) bytes, padding included): per 32 elements, scale 2^(floor(log2(amax)) - emax) with emax 8
+ * (e4m3), 4 (e3m2) or 2 (e2m1, e2m3), elements x / scale rounded to nearest even, saturating.
+ * Stream-ordered; the outputs feed kl_gemm with block_scale = 1 directly. */
 KL_API kl_status kl_mx_quantize(const void* x, int32_t x_type, int64_t rows, int64_t k, int64_t ldx, int32_t q_type,
                                 void* q, int64_t ldq, void* scales, void* stream);
 
@@ -276,8 +283,8 @@ KL_API kl_status kl_umma_smem_desc(int32_t elem_bytes, int32_t rows, int32_t col
  * (CTA pair). kernel_lib/include/kl/layout/umma_desc.hpp:49-58 (mma_instr_desc, M <= 128 there). */
 KL_API kl_status kl_mma_instr_desc(int32_t a_type, int32_t b_type, int32_t acc_type, int32_t m, int32_t n, uint32_t* out);
 
-/* 32-bit instruction descriptor of a block-scaled tcgen05.mma: a_type / b_type KL_E4M3 or
- * KL_E5M2 (kind::mxf8f6f4) or KL_E2M1 (kind::mxf4 / mxf4nvf4), scale_type KL_UE8M0 or KL_UE4M3,
+/* 32-bit instruction descriptor of a block-scaled tcgen05.mma: a_type / b_type KL_E4M3, KL_E5M2,
+ * KL_E3M2 or KL_E2M3 (kind::mxf8f6f4) or KL_E2M1 (kind::mxf4 / mxf4nvf4), scale_type KL_UE8M0 or KL_UE4M3,
  * M = 128 or 256, K-major operands; a_sf_id / b_sf_id (0-3) select the byte of each TMEM scale
  * word the MMA reads first. No counterpart in the reference; pinned to CuTe's
  * make_instr_desc_block_scaled / make_runtime_instr_desc_block_scaled. */

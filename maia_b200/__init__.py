@@ -23,7 +23,8 @@ KL_ERR_TIMEOUT = 4
 KL_ERR_NCCL = 5
 
 # kl_dtype
-KL_BF16, KL_F16, KL_E4M3, KL_E5M2, KL_F32, KL_I8, KL_U8, KL_I32, KL_E2M1, KL_UE8M0, KL_UE4M3 = range(11)
+KL_BF16, KL_F16, KL_E4M3, KL_E5M2, KL_F32, KL_I8, KL_U8, KL_I32, KL_E2M1, KL_UE8M0, KL_UE4M3, KL_E3M2, KL_E2M3 = range(13)
+FP6_TYPES = {"e3m2": KL_E3M2, "e2m3": KL_E2M3}
 
 # kl_algo
 ALGO_AUTO, ALGO_1CTA, ALGO_2CTA, ALGO_SKINNY = range(4)
@@ -212,35 +213,62 @@ def _dtype_code(t) -> int:
     return _TORCH_DTYPES[t]
 
 
+def _operand_type(x, ab_type) -> int:
+    """kl_dtype of an A / B tensor: from its torch dtype, or `ab_type` (KL_E3M2 / KL_E2M3, or
+    "e3m2" / "e2m3") for packed fp6, which torch has no dtype for and which travels as uint8."""
+    import torch
+
+    if ab_type is None:
+        return _dtype_code(x.dtype)
+    code = FP6_TYPES[ab_type] if isinstance(ab_type, str) else int(ab_type)
+    if code not in (KL_E3M2, KL_E2M3) or x.dtype != torch.uint8:
+        raise ValueError("ab_type names packed fp6 (KL_E3M2 / KL_E2M3) on uint8 tensors")
+    return code
+
+
+def _elements(code: int, units: int) -> int:
+    """Elements in `units` storage units: two per byte for packed fp4, four per three bytes for
+    packed fp6, else one."""
+    if code == KL_E2M1:
+        return 2 * units
+    if code in (KL_E3M2, KL_E2M3):
+        if units % 3:
+            raise ValueError("packed fp6 extents and strides are whole groups of 3 bytes (4 elements)")
+        return units // 3 * 4
+    return units
+
+
 def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, group_m=0, max_ctas=0,
               variant=0, prefetch=0, a_major=0, b_major=0, c_reduce=0, swizzle=0, sfa=None, sfb=None,
-              scale_vec=32) -> GemmDesc:
+              scale_vec=32, ab_type=None) -> GemmDesc:
     """Descriptor for C = alpha * A . B^T on torch CUDA tensors: A [M,K], B [N,K], C [M,N], or the
     batched forms A [L,M,K], B [L,N,K], C [L,M,N] (L independent GEMMs). a_major / b_major = 1
     pass the operand MN-major: `a` as the stored [K, M] (A transposed in memory), `b` as [K, N].
     c_reduce = 1 adds the result into C instead of overwriting it; swizzle picks the operand
     swizzle span in bytes (0 = 128, 64, 32). sfa / sfb (uint8 device tensors in the blocked layout of
     pack_block_scales) make it a block-scaled GEMM: one UE8M0 scale per 32 K-elements of each row
-    (MX, scale_vec 32) or one UE4M3 scale per 16 (NVFP4, scale_vec 16, fp4 operands)."""
+    (MX, scale_vec 32) or one UE4M3 scale per 16 (NVFP4, scale_vec 16, fp4 operands). ab_type =
+    KL_E3M2 / KL_E2M3 passes uint8 `a` / `b` as packed fp6 ([rows, 3 K / 4] bytes)."""
     for name, t in (("a", a), ("b", b), ("c", c)):
         if t.dim() not in (2, 3) or t.stride(-1) != 1:
             raise ValueError(f"{name} must be a 2-D or 3-D tensor with a contiguous last dimension")
     if not a.dim() == b.dim() == c.dim():
         raise ValueError("a, b and c must all be 2-D or all 3-D")
-    # Packed fp4 (torch.float4_e2m1fn_x2) holds two elements per storage unit: the descriptor counts
-    # elements, so K, the pitches and the batch strides of A and B double.
-    pa = 2 if _dtype_code(a.dtype) == KL_E2M1 else 1
-    pb = 2 if _dtype_code(b.dtype) == KL_E2M1 else 1
-    if (pa > 1 or pb > 1) and (a_major or b_major):
-        raise ValueError("packed fp4 operands are K-major")
-    m, k = (a.shape[-1], a.shape[-2]) if a_major else (a.shape[-2], a.shape[-1] * pa)
-    n, kb = (b.shape[-1], b.shape[-2]) if b_major else (b.shape[-2], b.shape[-1] * pb)
+    # Packed fp4 (torch.float4_e2m1fn_x2) holds two elements per storage unit, packed fp6 four per
+    # three bytes: the descriptor counts elements, so K, the pitches and the batch strides of A and B
+    # are converted.
+    ta, tb = _operand_type(a, ab_type), _operand_type(b, ab_type)
+    if {ta, tb} & {KL_E2M1, KL_E3M2, KL_E2M3} and (a_major or b_major):
+        raise ValueError("packed fp4 / fp6 operands are K-major")
+    m, k = (a.shape[-1], a.shape[-2]) if a_major else (a.shape[-2], _elements(ta, a.shape[-1]))
+    n, kb = (b.shape[-1], b.shape[-2]) if b_major else (b.shape[-2], _elements(tb, b.shape[-1]))
     batch = a.shape[0] if a.dim() == 3 else 0
     if kb != k or tuple(c.shape[-2:]) != (m, n) or (a.dim() == 3 and not (b.shape[0] == c.shape[0] == batch)):
         raise ValueError(f"shape mismatch: a {tuple(a.shape)}, b {tuple(b.shape)}, c {tuple(c.shape)}")
-    bs = (a.stride(0) * pa, b.stride(0) * pb, c.stride(0)) if a.dim() == 3 else (0, 0, 0)
-    return GemmDesc(m=m, n=n, k=k, a=a.data_ptr(), lda=a.stride(-2) * pa, b=b.data_ptr(), ldb=b.stride(-2) * pb,
-                    c=c.data_ptr(), ldc=c.stride(-2), ab_type=_dtype_code(a.dtype), c_type=_dtype_code(c.dtype),
+    bs = (_elements(ta, a.stride(0)), _elements(tb, b.stride(0)), c.stride(0)) if a.dim() == 3 else (0, 0, 0)
+    return GemmDesc(m=m, n=n, k=k, a=a.data_ptr(), lda=_elements(ta, a.stride(-2)), b=b.data_ptr(),
+                    ldb=_elements(tb, b.stride(-2)), c=c.data_ptr(), ldc=c.stride(-2), ab_type=ta,
+                    c_type=_dtype_code(c.dtype),
                     alpha=float(alpha), scale_a=None if scale_a is None else scale_a.data_ptr(),
                     scale_b=None if scale_b is None else scale_b.data_ptr(), algo=algo, group_m=group_m,
                     max_ctas=max_ctas, variant=variant, prefetch=prefetch, batch=batch, stride_a=bs[0],
@@ -252,10 +280,10 @@ def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, gr
 
 def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
          group_m=0, max_ctas=0, variant=0, prefetch=0, a_major=0, b_major=0, accumulate=False, swizzle=0,
-         sfa=None, sfb=None, scale_vec=32, workspace=None, stream=None):
+         sfa=None, sfb=None, scale_vec=32, ab_type=None, workspace=None, stream=None):
     """out = alpha * a @ b.T [* scale_a * scale_b] on the current CUDA stream, via kl_gemm.
-    accumulate=True: out += alpha * a @ b.T (out must be given). sfa/sfb: MXFP8 block scales
-    (see mx_pack_scales)."""
+    accumulate=True: out += alpha * a @ b.T (out must be given). sfa/sfb: block scales (see
+    pack_block_scales). ab_type="e3m2" / "e2m3": a and b are uint8 packed fp6."""
     import torch
 
     if accumulate and out is None:
@@ -266,7 +294,7 @@ def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=Non
         shape = (a.shape[0], m, n) if a.dim() == 3 else (m, n)
         out = torch.empty(shape, dtype=out_dtype or torch.bfloat16, device=a.device)
     d = gemm_desc(a, b, out, alpha, scale_a, scale_b, algo, group_m, max_ctas, variant, prefetch, a_major, b_major,
-                  int(bool(accumulate)), swizzle, sfa, sfb, scale_vec)
+                  int(bool(accumulate)), swizzle, sfa, sfb, scale_vec, ab_type)
     s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
     if workspace is None:
         check(lib().kl_gemm(ctypes.byref(d), ctypes.c_void_p(s)))
@@ -282,7 +310,7 @@ def block_scale_bytes(rows: int, k: int, vec: int = 32) -> int:
 
 
 def gemm_grouped(a, b, m_block_group, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=None,
-                 accumulate=False, algo=ALGO_1CTA, sfa=None, sfb=None, scale_vec=32, stream=None):
+                 accumulate=False, algo=ALGO_1CTA, sfa=None, sfb=None, scale_vec=32, ab_type=None, stream=None):
     """m-grouped GEMM (mixture-of-experts layout): a [M, K] holds the groups' rows back to back,
     each group padded to a multiple of 128 rows; b [G, N, K] holds one matrix per group;
     m_block_group is an int32 device tensor of ceil(M / 128) entries naming the group of every
@@ -300,10 +328,9 @@ def gemm_grouped(a, b, m_block_group, out=None, *, out_dtype=None, alpha=1.0, sc
     if out is None:
         out = torch.empty((a.shape[0], b.shape[1]), dtype=out_dtype or torch.bfloat16, device=a.device)
     d = gemm_desc(a, b[0], out, alpha, scale_a, scale_b, algo, c_reduce=int(bool(accumulate)), sfa=sfa, sfb=sfb,
-                  scale_vec=scale_vec)
-    pb = 2 if _dtype_code(b.dtype) == KL_E2M1 else 1
+                  scale_vec=scale_vec, ab_type=ab_type)
     d.groups = b.shape[0]
-    d.stride_b = b.stride(0) * pb
+    d.stride_b = _elements(_operand_type(b, ab_type), b.stride(0))
     d.m_block_group = m_block_group.data_ptr()
     s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
     check(lib().kl_gemm(ctypes.byref(d), ctypes.c_void_p(s)))
@@ -332,21 +359,27 @@ def pack_block_scales(scales, k: int, vec: int = 32, out=None, stream=None):
 
 def mx_quantize(x, kind: str = "e4m3", stream=None):
     """MX-quantise x (fp32 or bf16 device tensor [rows, K], K a multiple of 32) on the device:
-    returns (q, scales) with q float8_e4m3fn [rows, K] or float4_e2m1fn_x2 [rows, K/2] and scales
-    the blocked UE8M0 array, ready for gemm(..., sfa=scales)."""
+    returns (q, scales) with q float8_e4m3fn [rows, K], float4_e2m1fn_x2 [rows, K/2], or for
+    kind "e3m2" / "e2m3" uint8 packed fp6 [rows, 3 K / 4] (K a multiple of 128), and scales the
+    blocked UE8M0 array, ready for gemm(..., sfa=scales) (with ab_type=kind for fp6)."""
     import torch
 
     rows, k = x.shape
     if x.stride(1) != 1:
         raise ValueError("x must have a contiguous last dimension")
-    fp4 = kind == "e2m1"
-    q = torch.empty((rows, k // 2 if fp4 else k), dtype=torch.uint8, device=x.device)
+    code = {"e4m3": KL_E4M3, "e2m1": KL_E2M1, **FP6_TYPES}[kind]
+    if code in (KL_E3M2, KL_E2M3) and k % 128:
+        raise ValueError("packed fp6 rows are whole 128-element (96-byte) blocks")
+    width = k // 2 if code == KL_E2M1 else k // 4 * 3 if code in (KL_E3M2, KL_E2M3) else k
+    q = torch.empty((rows, width), dtype=torch.uint8, device=x.device)
     sc = torch.empty(block_scale_bytes(rows, k, 32), dtype=torch.uint8, device=x.device)
     s = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
     check(lib().kl_mx_quantize(ctypes.c_void_p(x.data_ptr()), _dtype_code(x.dtype), rows, k, x.stride(0),
-                               KL_E2M1 if fp4 else KL_E4M3, ctypes.c_void_p(q.data_ptr()), k, ctypes.c_void_p(sc.data_ptr()),
+                               code, ctypes.c_void_p(q.data_ptr()), k, ctypes.c_void_p(sc.data_ptr()),
                                ctypes.c_void_p(s)))
-    return q.view(torch.float4_e2m1fn_x2 if fp4 else torch.float8_e4m3fn), sc
+    if code == KL_E2M1:
+        return q.view(torch.float4_e2m1fn_x2), sc
+    return (q, sc) if code != KL_E4M3 else (q.view(torch.float8_e4m3fn), sc)
 
 
 def mx_pack_scales(scales, k: int, out=None, stream=None):
@@ -355,14 +388,15 @@ def mx_pack_scales(scales, k: int, out=None, stream=None):
 
 
 def gemm_host(a_host, b_host, c_host, a_dev, b_dev, c_dev, *, alpha=1.0, scale_a=None, scale_b=None,
-              algo=ALGO_AUTO, chunks=0, sfa=None, sfb=None, scale_vec=32, stream=None):
+              algo=ALGO_AUTO, chunks=0, sfa=None, sfb=None, scale_vec=32, ab_type=None, stream=None):
     """c_host = alpha * a_host @ b_host.T with host (ideally pinned) tensors, through kl_gemm_host:
     the copies in and out overlap the GEMM. a_dev/b_dev/c_dev are device staging tensors of the
     same shapes; sfa/sfb: host MXFP8 scales in the blocked layout (staged by the library). Only
     queues the work on the stream: synchronise it before reading c_host."""
     import torch
 
-    d = gemm_desc(a_host, b_host, c_host, alpha, scale_a, scale_b, algo, sfa=sfa, sfb=sfb, scale_vec=scale_vec)
+    d = gemm_desc(a_host, b_host, c_host, alpha, scale_a, scale_b, algo, sfa=sfa, sfb=sfb, scale_vec=scale_vec,
+                  ab_type=ab_type)
     s = stream if stream is not None else torch.cuda.current_stream(a_dev.device).cuda_stream
     check(lib().kl_gemm_host(ctypes.byref(d), ctypes.c_void_p(a_dev.data_ptr()), ctypes.c_void_p(b_dev.data_ptr()),
                              ctypes.c_void_p(c_dev.data_ptr()), int(chunks), ctypes.c_void_p(s)))
@@ -370,12 +404,13 @@ def gemm_host(a_host, b_host, c_host, a_dev, b_dev, c_dev, *, alpha=1.0, scale_a
 
 
 def gemm_gather(a, b, c_shard, peer_ptrs, *, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
-                group_m=0, sfa=None, sfb=None, scale_vec=32, stream=None):
+                group_m=0, sfa=None, sfb=None, scale_vec=32, ab_type=None, stream=None):
     """c_shard = alpha * a @ b.T, and the same tiles written to each peer pointer (a view of the same
     columns in another GPU's copy of C, with c_shard's pitch), through kl_gemm_gather."""
     import torch
 
-    d = gemm_desc(a, b, c_shard, alpha, scale_a, scale_b, algo, group_m, sfa=sfa, sfb=sfb, scale_vec=scale_vec)
+    d = gemm_desc(a, b, c_shard, alpha, scale_a, scale_b, algo, group_m, sfa=sfa, sfb=sfb, scale_vec=scale_vec,
+                  ab_type=ab_type)
     arr = (ctypes.c_void_p * max(1, len(peer_ptrs)))(*[ctypes.c_void_p(p) for p in peer_ptrs])
     s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
     check(lib().kl_gemm_gather(ctypes.byref(d), arr, len(peer_ptrs), ctypes.c_void_p(s)))

@@ -105,7 +105,7 @@ kl_status run_tile(kl_gemm_desc const& d, Problem const& pr, bool pair, cudaStre
     if (handled) return s;
     return fail(KL_ERR_NOT_SUPPORTED, std::string(who) + (d.block_scale == 2
                                                               ? ": NVFP4 takes e2m1 inputs with bf16 or f32 C"
-                                                              : ": MX takes e4m3, e5m2 or e2m1 inputs with bf16 or f32 C"));
+                                                              : ": MX takes e4m3, e5m2, e3m2, e2m3 or e2m1 inputs with bf16 or f32 C"));
   }
   const int32_t sw = d.swizzle == 0 ? 128 : d.swizzle;
   if (sw != 128 && sw != 64 && sw != 32)
@@ -490,10 +490,21 @@ kl_status kl_mma_instr_desc_major(int32_t a_type, int32_t b_type, int32_t acc_ty
 kl_status kl_mma_instr_desc_block_scaled(int32_t a_type, int32_t b_type, int32_t scale_type, int32_t m, int32_t n,
                                          int32_t a_sf_id, int32_t b_sf_id, uint32_t* out) {
   if (out == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null output");
-  // Operand formats: kind::mxf8f6f4 e4m3 = 0, e5m2 = 1; kind::mxf4 / mxf4nvf4 e2m1 = 1.
-  auto fmt = [](int32_t t) { return t == KL_E4M3 ? 0 : (t == KL_E5M2 || t == KL_E2M1) ? 1 : -1; };
+  // Operand formats: kind::mxf8f6f4 e4m3 = 0, e5m2 = 1, e2m3 = 3, e3m2 = 4; kind::mxf4 / mxf4nvf4
+  // e2m1 = 1.
+  auto fmt = [](int32_t t) {
+    switch (t) {
+      case KL_E4M3: return 0;
+      case KL_E5M2:
+      case KL_E2M1: return 1;
+      case KL_E2M3: return 3;
+      case KL_E3M2: return 4;
+      default: return -1;
+    }
+  };
   const int fa = fmt(a_type), fb = fmt(b_type);
-  if (fa < 0 || fb < 0) return fail(KL_ERR_INVALID_ARGUMENT, "block-scaled operands must be e4m3, e5m2 or e2m1");
+  if (fa < 0 || fb < 0)
+    return fail(KL_ERR_INVALID_ARGUMENT, "block-scaled operands must be e4m3, e5m2, e3m2, e2m3 or e2m1");
   if ((a_type == KL_E2M1) != (b_type == KL_E2M1)) return fail(KL_ERR_INVALID_ARGUMENT, "e2m1 takes e2m1 A and B");
   if (scale_type != KL_UE8M0 && scale_type != KL_UE4M3)
     return fail(KL_ERR_INVALID_ARGUMENT, "scale_type must be KL_UE8M0 or KL_UE4M3");
@@ -517,6 +528,8 @@ kl_status kl_mma_instr_desc(int32_t a_type, int32_t b_type, int32_t acc_type, in
       case KL_F32: *kind = 1; return 2;  // tf32
       case KL_E4M3: *kind = 2; return 0;
       case KL_E5M2: *kind = 2; return 1;
+      case KL_E2M3: *kind = 2; return 3;
+      case KL_E3M2: *kind = 2; return 4;
       case KL_U8: *kind = 3; return 0;
       case KL_I8: *kind = 3; return 1;
       default: return -1;

@@ -97,8 +97,12 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
   if (s != KL_OK) return s;
 
   const int ec = elem_bytes(h->c_type);
-  // Bytes of `elems` operand elements (packed fp4: two per byte).
-  auto ab_bytes = [&](int64_t elems) { return size_t(h->ab_type == KL_E2M1 ? elems / 2 : elems * elem_bytes(h->ab_type)); };
+  // Bytes of `elems` operand elements.
+  auto ab_bytes = [&](int64_t elems) {
+    if (h->ab_type == KL_E2M1) return size_t(elems / 2);                           // packed fp4
+    if (h->ab_type == KL_E3M2 || h->ab_type == KL_E2M3) return size_t(elems / 4 * 3);  // packed fp6
+    return size_t(elems * elem_bytes(h->ab_type));
+  };
   // Block scales: blocked arrays, A's then B's, in one staging buffer.
   const int32_t vec = h->block_scale == 2 ? 16 : 32;
   const int64_t sfa_bytes = mx ? kl_block_scale_bytes(h->m, h->k, vec) : 0;

@@ -5,6 +5,9 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <type_traits>
+
+#include <cuda_fp6.h>
 
 #include <kl/gemm/gemm.hpp>
 
@@ -12,37 +15,9 @@
 
 namespace kl::capi {
 
+using mx::run_mx;
+
 namespace {
-
-using kl::gemm::TnConfig;
-
-// One CTA, 128 x 256 tiles: one TMEM accumulator (the scales take the rest), 3 stages of 49.5 KB.
-template <typename InT, typename OutT, int V>
-using Mx256 = TnConfig<InT, OutT, 1, 256, 3, false, false, false, kl::Swizzle128B, V>;
-// One CTA, 128 x 128 tiles: two accumulators (epilogue overlapped), 5 stages of 33 KB.
-template <typename InT, typename OutT, int V>
-using Mx128 = TnConfig<InT, OutT, 1, 128, 5, false, false, false, kl::Swizzle128B, V>;
-// CTA pair, 256 x 256 tiles: one accumulator per CTA, 5 stages of 33.5 KB per CTA (fp8).
-template <typename InT, typename OutT, int V>
-using MxPair = TnConfig<InT, OutT, 2, 256, 5, false, false, false, kl::Swizzle128B, V>;
-// CTA pair, 256 x 192 tiles: two accumulators (2 x 192 columns leave room for the scales), 6 stages
-// of 29.5 KB per CTA (fp8; 5 for NVFP4's larger scale tiles). B's 192-row tiles start 0 or 64 rows
-// into a 128-row scale block.
-template <typename InT, typename OutT, int V>
-using MxPair192 = TnConfig<InT, OutT, 2, 192, V == 16 ? 5 : 6, false, false, false, kl::Swizzle128B, V>;
-// CTA pair, 256 x 128 tiles: two accumulators, 7 stages of 25 KB per CTA (fp8).
-template <typename InT, typename OutT, int V>
-using MxPair128 = TnConfig<InT, OutT, 2, 128, V == 16 ? 6 : 7, false, false, false, kl::Swizzle128B, V>;
-
-template <typename InT, typename OutT, int V = 32>
-kl_status run_mx(int32_t variant, bool pair, kl::gemm::Problem const& pr, cudaStream_t stream,
-                 kl::gemm::LaunchInfo* info) {
-  if (pair)
-    return variant == 2   ? run_cfg<MxPair128<InT, OutT, V>>(pr, stream, info)
-           : variant == 3 ? run_cfg<MxPair192<InT, OutT, V>>(pr, stream, info)
-                          : run_cfg<MxPair<InT, OutT, V>>(pr, stream, info);
-  return variant == 2 ? run_cfg<Mx128<InT, OutT, V>>(pr, stream, info) : run_cfg<Mx256<InT, OutT, V>>(pr, stream, info);
-}
 
 // One thread per 32-bit word of the blocked layout: the four K-group scales of one row. Padding
 // (rows past `rows`, K-groups past `groups`) holds `pad`, a finite scale of 1 in the scale format
@@ -80,6 +55,7 @@ kl_status run_tile_mx(int32_t mode, int32_t ab, int32_t c, int32_t variant, bool
     *handled = false;
     return KL_ERR_NOT_SUPPORTED;
   }
+  if (ab == KL_E3M2 || ab == KL_E2M3) return run_tile_fp6(ab, c, variant, pair, pr, stream, info, handled);
   if (ab == KL_E4M3 && c == KL_BF16) return run_mx<kl::e4m3, kl::bf16>(variant, pair, pr, stream, info);
   if (ab == KL_E4M3 && c == KL_F32) return run_mx<kl::e4m3, float>(variant, pair, pr, stream, info);
   if (ab == KL_E5M2 && c == KL_BF16) return run_mx<kl::e5m2, kl::bf16>(variant, pair, pr, stream, info);
@@ -134,7 +110,7 @@ kl_status kl_mx_pack_scales(const void* src, int64_t rows, int64_t k, int64_t ld
 namespace kl::capi {
 namespace {
 
-// Two fp32 values rounded (nearest, ties to even, saturating) to e4m3 / e2m1, `lo` in the low
+// Two fp32 values rounded (nearest, ties to even, saturating) to e4m3 / e2m1 / fp6, `lo` in the low
 // byte / nibble.
 __device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
   uint16_t r;
@@ -146,11 +122,22 @@ __device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
   asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u16.u8 %0, t;\n\t}" : "=h"(r) : "f"(hi), "f"(lo));
   return r;
 }
+// fp6 (CUDA's fp6 conversion): each value in the low 6 bits of its byte.
+template <int QT>
+__device__ __forceinline__ uint32_t cvt_fp6x2(float lo, float hi) {
+  return __nv_cvt_float2_to_fp6x2(make_float2(lo, hi), QT == KL_E3M2 ? __NV_E3M2 : __NV_E2M3, cudaRoundNearest);
+}
+// Element format constants: exponent of the largest normal value (OCP MX emax) and bytes per 32
+// elements.
+template <int QT>
+inline constexpr int kQEmax = QT == KL_E4M3 ? 8 : QT == KL_E3M2 ? 4 : 2;
+template <int QT>
+inline constexpr int kQGroupBytes = QT == KL_E4M3 ? 32 : QT == KL_E2M1 ? 16 : 24;
 
 // One thread per (row, 32-element group) of the padded blocked layout: the group's UE8M0 scale
 // 2^(floor(log2(amax)) - emax) (OCP MX v1.0) goes to its blocked position, the elements x * 2^-e
 // (exact: a power of two) are rounded to the element format. Padding positions get scale 127.
-template <typename XT, bool Fp4>
+template <typename XT, int QT>
 __global__ void mx_quantize_kernel(const XT* __restrict__ x, long long ldx, long long rows, long long groups,
                                    uint8_t* __restrict__ q, long long ldq_bytes, uint8_t* __restrict__ sf,
                                    long long k_blocks, long long rows_pad) {
@@ -186,13 +173,30 @@ __global__ void mx_quantize_kernel(const XT* __restrict__ x, long long ldx, long
   float amax = 0.0f;
 #pragma unroll
   for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-  constexpr int emax = Fp4 ? 2 : 8;  // exponent of the element format's largest normal value
-  const int e = (amax > 0.0f ? ilogbf(amax) : 0) - emax;
+  const int e = (amax > 0.0f ? ilogbf(amax) : 0) - kQEmax<QT>;
   const int s = e + 127 < 0 ? 0 : e + 127 > 254 ? 254 : e + 127;
   *sfp = uint8_t(s);
   const float inv = ldexpf(1.0f, 127 - s);
-  uint8_t* dst = q + r * ldq_bytes + g * (Fp4 ? 16 : 32);
-  if constexpr (Fp4) {
+  uint8_t* dst = q + r * ldq_bytes + g * kQGroupBytes<QT>;
+  if constexpr (QT == KL_E3M2 || QT == KL_E2M3) {
+    // 32 six-bit codes as one 192-bit little-endian stream: element i at bits [6i, 6i + 6).
+    uint32_t w[6] = {0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      const uint32_t pair = cvt_fp6x2<QT>(v[i] * inv, v[i + 1] * inv);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t c = (pair >> (8 * h)) & 63u;
+        const int bit = 6 * (i + h), word = bit >> 5, off = bit & 31;
+        w[word] |= c << off;
+        if (off > 26) w[word + 1] |= c >> (32 - off);
+      }
+    }
+    // 24 bytes at an 8-byte-aligned address (row pitches are multiples of 96 bytes).
+    reinterpret_cast<uint2*>(dst)[0] = make_uint2(w[0], w[1]);
+    reinterpret_cast<uint2*>(dst)[1] = make_uint2(w[2], w[3]);
+    reinterpret_cast<uint2*>(dst)[2] = make_uint2(w[4], w[5]);
+  } else if constexpr (QT == KL_E2M1) {
     uint32_t w[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -221,39 +225,47 @@ extern "C" kl_status kl_mx_quantize(const void* x, int32_t x_type, int64_t rows,
   if (rows == 0 || k == 0) return KL_OK;
   if (x == nullptr || q == nullptr || scales == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "kl_mx_quantize: null pointer");
   if (x_type != KL_F32 && x_type != KL_BF16) return fail(KL_ERR_NOT_SUPPORTED, "kl_mx_quantize: x must be f32 or bf16");
-  if (q_type != KL_E4M3 && q_type != KL_E2M1) return fail(KL_ERR_NOT_SUPPORTED, "kl_mx_quantize: q must be e4m3 or e2m1");
+  if (q_type != KL_E4M3 && q_type != KL_E2M1 && q_type != KL_E3M2 && q_type != KL_E2M3)
+    return fail(KL_ERR_NOT_SUPPORTED, "kl_mx_quantize: q must be e4m3, e2m1, e3m2 or e2m3");
   if (k % 32 != 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_mx_quantize: k must be a multiple of 32");
   const int xb = x_type == KL_F32 ? 4 : 2;
-  const bool fp4 = q_type == KL_E2M1;
+  const bool fp6 = q_type == KL_E3M2 || q_type == KL_E2M3;
   if (ldx < k || (ldx * xb) % 16 != 0 || reinterpret_cast<uintptr_t>(x) % 16 != 0)
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_mx_quantize: x must be 16-byte aligned with a 16-byte-multiple row pitch >= k");
-  if (ldq < k || (fp4 && ldq % 32 != 0) || (!fp4 && ldq % 16 != 0) || reinterpret_cast<uintptr_t>(q) % 16 != 0)
-    return fail(KL_ERR_INVALID_ARGUMENT, "kl_mx_quantize: q must be 16-byte aligned with a 16-byte-multiple row pitch >= k");
+  // Row pitch of q in bytes: e4m3 one per element, e2m1 two per byte, fp6 four per three bytes.
+  const long long ldq_bytes = q_type == KL_E2M1 ? ldq / 2 : fp6 ? ldq / 4 * 3 : ldq;
+  // Pitch granule, in elements: 16 bytes, or for fp6 96 bytes (128 elements, the GEMM's own rule).
+  const long long ldq_unit = q_type == KL_E2M1 ? 32 : fp6 ? 128 : 16;
+  if (ldq < k || ldq % ldq_unit != 0 || reinterpret_cast<uintptr_t>(q) % 16 != 0)
+    return fail(KL_ERR_INVALID_ARGUMENT,
+                fp6 ? "kl_mx_quantize: fp6 q must be 16-byte aligned with a row pitch >= k, a multiple of 128 elements"
+                    : "kl_mx_quantize: q must be 16-byte aligned with a 16-byte-multiple row pitch >= k");
   if (reinterpret_cast<uintptr_t>(scales) % 16 != 0)
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_mx_quantize: scales must be 16-byte aligned");
   const long long k_blocks = (k + 127) / 128, rows_pad = (rows + 127) / 128 * 128;
   const long long threads = rows_pad * k_blocks * 4;
   const long long blocks = (threads + 255) / 256;
   if (blocks > INT32_MAX) return fail(KL_ERR_INVALID_ARGUMENT, "kl_mx_quantize: too large");
-  const long long ldq_bytes = fp4 ? ldq / 2 : ldq;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto* qp = static_cast<uint8_t*>(q);
   auto* sp = static_cast<uint8_t*>(scales);
-  if (x_type == KL_F32) {
-    if (fp4)
-      kl::capi::mx_quantize_kernel<float, true><<<unsigned(blocks), 256, 0, s>>>(
-          static_cast<const float*>(x), ldx, rows, k / 32, qp, ldq_bytes, sp, k_blocks, rows_pad);
-    else
-      kl::capi::mx_quantize_kernel<float, false><<<unsigned(blocks), 256, 0, s>>>(
-          static_cast<const float*>(x), ldx, rows, k / 32, qp, ldq_bytes, sp, k_blocks, rows_pad);
-  } else {
-    if (fp4)
-      kl::capi::mx_quantize_kernel<uint16_t, true><<<unsigned(blocks), 256, 0, s>>>(
-          static_cast<const uint16_t*>(x), ldx, rows, k / 32, qp, ldq_bytes, sp, k_blocks, rows_pad);
-    else
-      kl::capi::mx_quantize_kernel<uint16_t, false><<<unsigned(blocks), 256, 0, s>>>(
-          static_cast<const uint16_t*>(x), ldx, rows, k / 32, qp, ldq_bytes, sp, k_blocks, rows_pad);
-  }
+  auto launch = [&](auto const* xp, auto qt) {
+    using XT = std::remove_cv_t<std::remove_pointer_t<decltype(xp)>>;
+    kl::capi::mx_quantize_kernel<XT, decltype(qt)::value><<<unsigned(blocks), 256, 0, s>>>(
+        xp, ldx, rows, k / 32, qp, ldq_bytes, sp, k_blocks, rows_pad);
+  };
+  auto by_q = [&](auto const* xp) {
+    switch (q_type) {
+      case KL_E4M3: launch(xp, std::integral_constant<int, KL_E4M3>{}); break;
+      case KL_E2M1: launch(xp, std::integral_constant<int, KL_E2M1>{}); break;
+      case KL_E3M2: launch(xp, std::integral_constant<int, KL_E3M2>{}); break;
+      default: launch(xp, std::integral_constant<int, KL_E2M3>{}); break;
+    }
+  };
+  if (x_type == KL_F32)
+    by_q(static_cast<const float*>(x));
+  else
+    by_q(static_cast<const uint16_t*>(x));
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? KL_OK : kl::capi::cuda_fail(e, "kl_mx_quantize launch");
 }

@@ -22,7 +22,8 @@ class Workload:
     m: int
     n: int
     k: int
-    dtype: str          # "bf16", "e4m3", "mxfp8" (e4m3 elements with MX block scales), "mxfp4" or "nvfp4" (e2m1)
+    dtype: str          # "bf16", "e4m3", "mxfp8" (e4m3 elements with MX block scales), "mxfp6" (e2m3),
+                        # "mxfp4" or "nvfp4" (e2m1)
     out: str            # "bf16" or "f32"
     dist: str           # "uniform" (on [-1, 1]) or "normal"
     a_scale: float      # multiplier of A's standard normal (normal) draws
@@ -35,14 +36,14 @@ class Workload:
 
     @property
     def in_bytes(self) -> float:
-        return 2 if self.dtype == "bf16" else 0.5 if self.dtype in ("mxfp4", "nvfp4") else 1
+        return 2 if self.dtype == "bf16" else 0.5 if self.dtype in ("mxfp4", "nvfp4") else 0.75 if self.dtype == "mxfp6" else 1
 
     @property
     def scale_bytes(self) -> int:
         """MX block scales: one byte per 32 K-elements of every row of A and B."""
         if self.dtype == "nvfp4":
             return (self.m + self.n) * -(-self.k // 16)
-        return (self.m + self.n) * -(-self.k // 32) if self.dtype in ("mxfp8", "mxfp4") else 0
+        return (self.m + self.n) * -(-self.k // 32) if self.dtype in ("mxfp8", "mxfp6", "mxfp4") else 0
 
     @property
     def out_bytes(self) -> int:
@@ -67,8 +68,11 @@ C3MX = Workload("c3mx_8192_mxfp8", 8192, 8192, 8192, "mxfp8", "bf16", "normal", 
 C3MXF4 = Workload("c3mxf4_8192_mxfp4", 8192, 8192, 8192, "mxfp4", "bf16", "normal", 0.02, 0.02, 2)
 C4MXF4 = Workload("c4mxf4_16384x16384x8192_mxfp4", 16384, 16384, 8192, "mxfp4", "bf16", "normal", 1.0, 1.0, 3)
 C3NVF4 = Workload("c3nvf4_8192_nvfp4", 8192, 8192, 8192, "nvfp4", "bf16", "normal", 0.02, 0.02, 2)
+# C3's shape in MXFP6 (packed e2m3 elements, UE8M0 scales per 32; kind::mxf8f6f4 at the fp8 rate).
+C3MXF6 = Workload("c3mxf6_8192_mxfp6", 8192, 8192, 8192, "mxfp6", "bf16", "normal", 0.02, 0.02, 2)
 
-ALL = {w.name: w for w in (C1, C2, C3, C4, C4MX, C3MX, C3MXF4, C4MXF4, C3NVF4, *C5.values())}
+ALL = {w.name: w for w in (C1, C2, C3, C4, C4MX, C3MX, C3MXF4, C4MXF4, C3NVF4, C3MXF6, *C5.values())}
+MX_ELEMENT = {"mxfp8": "e4m3", "mxfp6": "e2m3", "mxfp4": "e2m1"}  # element format of each MX workload dtype
 
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
@@ -201,14 +205,56 @@ def pack_e2m1(codes: np.ndarray) -> np.ndarray:
     return (c[..., 0::2] | (c[..., 1::2] << 4)).astype(np.uint8)
 
 
-MX_EMAX = {"e4m3": 8, "e5m2": 15, "e2m1": 2}  # exponent of the largest normal element value
+def _fp6_grid(eb: int) -> np.ndarray:
+    """The 32 magnitudes of an fp6 format with `eb` exponent bits (bias 2^(eb-1) - 1) and 5 - eb
+    mantissa bits, by code (exponent in the high bits): increasing, no special values."""
+    mb, bias = 5 - eb, (1 << (eb - 1)) - 1
+    c = np.arange(32)
+    e, m = c >> mb, c & ((1 << mb) - 1)
+    return np.where(e == 0, m * 2.0 ** (1 - bias - mb), (m + (1 << mb)) * 2.0 ** (e - bias - mb))
+
+
+FP6_GRID = {"e3m2": _fp6_grid(3), "e2m3": _fp6_grid(2)}  # largest 28 and 7.5
+
+
+def f32_to_fp6_codes(x: np.ndarray, kind: str) -> np.ndarray:
+    """Round float32 to the nearest fp6 (e3m2 or e2m3) value, ties to the even code (mantissa LSB
+    0), saturating at the largest magnitude; returns 6-bit codes (sign in bit 5) as uint8."""
+    grid = FP6_GRID[kind]
+    a = np.minimum(np.abs(np.asarray(x, dtype=np.float64)), grid[-1])
+    idx = np.clip(np.searchsorted(grid, a), 1, 31)
+    lo, hi = grid[idx - 1], grid[idx]
+    pick_hi = (a - lo > hi - a) | ((a - lo == hi - a) & (idx % 2 == 0))
+    q = np.where(pick_hi, idx, idx - 1).astype(np.uint8)
+    return np.where(np.signbit(x) & (q != 0), q | 32, q).astype(np.uint8)
+
+
+def pack_fp6(codes: np.ndarray) -> np.ndarray:
+    """Pack 6-bit codes [rows, K] (K a multiple of 4) into [rows, 3 K / 4] bytes: element i at bits
+    [6i, 6i + 6) of the row, least significant bit first (four elements per three bytes)."""
+    c = np.ascontiguousarray(codes, dtype=np.uint32)
+    w = c[..., 0::4] | (c[..., 1::4] << 6) | (c[..., 2::4] << 12) | (c[..., 3::4] << 18)
+    out = np.stack([w & 0xFF, (w >> 8) & 0xFF, (w >> 16) & 0xFF], axis=-1).astype(np.uint8)
+    return out.reshape(c.shape[:-1] + (c.shape[-1] // 4 * 3,))
+
+
+def unpack_fp6(packed: np.ndarray) -> np.ndarray:
+    """Inverse of pack_fp6: [rows, 3 K / 4] bytes to 6-bit codes [rows, K]."""
+    b = np.ascontiguousarray(packed, dtype=np.uint32).reshape(packed.shape[:-1] + (-1, 3))
+    w = b[..., 0] | (b[..., 1] << 8) | (b[..., 2] << 16)
+    out = np.stack([(w >> (6 * j)) & 63 for j in range(4)], axis=-1).astype(np.uint8)
+    return out.reshape(packed.shape[:-1] + (-1,))
+
+
+MX_EMAX = {"e4m3": 8, "e5m2": 15, "e2m1": 2, "e3m2": 4, "e2m3": 2}  # exponent of the largest normal element value
 
 
 def mx_quantize(x: np.ndarray, kind: str = "e4m3") -> tuple[np.ndarray, np.ndarray]:
     """MX quantisation (OCP Microscaling Formats v1.0) of float32 rows in blocks of 32 K-elements:
     shared scale 2^(floor(log2(amax)) - emax) as UE8M0 bits, elements x / scale rounded to the
     element format (nearest, ties to even, saturating). Returns (element bits, scale bits
-    [rows, ceil(K/32)]); e2m1 elements come packed two per byte ([rows, K/2], K even)."""
+    [rows, ceil(K/32)]); e2m1 elements come packed two per byte ([rows, K/2], K even), e3m2 /
+    e2m3 elements four per three bytes ([rows, 3 K / 4], K a multiple of 4)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     rows, k = x.shape
     groups = -(-k // 32)
@@ -221,6 +267,8 @@ def mx_quantize(x: np.ndarray, kind: str = "e4m3") -> tuple[np.ndarray, np.ndarr
     q = (padded.reshape(rows, groups, 32) * inv[:, :, None]).reshape(rows, groups * 32)[:, :k].astype(np.float32)
     if kind == "e2m1":
         return pack_e2m1(f32_to_e2m1_codes(q)), sbits
+    if kind in FP6_GRID:
+        return pack_fp6(f32_to_fp6_codes(q, kind)), sbits
     enc = f32_to_e4m3_bits if kind == "e4m3" else f32_to_e5m2_bits
     return enc(q), sbits
 
@@ -270,8 +318,8 @@ def make_inputs(w: Workload, rows_a: int | None = None):
         qa, sfa, ga = nv_quantize(xa)
         qb, sfb, gb = nv_quantize(xb)
         return qa, qb, (sfa, ga), (sfb, gb)
-    if w.dtype in ("mxfp8", "mxfp4"):
-        kind = "e4m3" if w.dtype == "mxfp8" else "e2m1"
+    if w.dtype in MX_ELEMENT:
+        kind = MX_ELEMENT[w.dtype]
         qa, sfa = mx_quantize(xa, kind)
         qb, sfb = mx_quantize(xb, kind)
         return qa, qb, sfa, sfb

@@ -3,7 +3,9 @@
 Inputs are raw element bits as numpy arrays, row-major: uint16 for bf16, uint8 for e4m3 (the
 defaults), np.float16 for f16; pass `kind` for the other formats (F16 on uint16 bits, E5M2 on
 uint8 bits, E2M1 on uint8 bytes that each hold two fp4 elements, the first in the low nibble, so a
-row of K elements is K / 2 bytes). Type codes follow the library's kl_dtype.
+row of K elements is K / 2 bytes; E3M2 / E2M3 on uint8 bytes of packed fp6, element i of a row at
+bits [6i, 6i + 6), least significant bit first, so a row of K elements is 3 K / 4 bytes). Type codes
+follow the library's kl_dtype.
 """
 
 from __future__ import annotations
@@ -17,8 +19,8 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libkl_oracle.so"
-BF16, F16, E4M3, E5M2, E2M1 = 0, 1, 2, 3, 8
-KINDS = {"bf16": BF16, "f16": F16, "e4m3": E4M3, "e5m2": E5M2, "e2m1": E2M1}
+BF16, F16, E4M3, E5M2, E2M1, E3M2, E2M3 = 0, 1, 2, 3, 8, 11, 12
+KINDS = {"bf16": BF16, "f16": F16, "e4m3": E4M3, "e5m2": E5M2, "e2m1": E2M1, "e3m2": E3M2, "e2m3": E2M3}
 _lib = None
 
 
@@ -69,16 +71,28 @@ def threads_default() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
 
 
-def _per_unit(kind) -> int:
-    """Elements per storage unit: 2 for packed e2m1, else 1."""
-    return 2 if kind is not None and (KINDS.get(kind) if isinstance(kind, str) else int(kind)) == E2M1 else 1
+def elements(kind, units: int) -> int:
+    """Elements in `units` storage units of a row: two per byte for packed e2m1, four per three
+    bytes for packed fp6 (units a multiple of 3), else one."""
+    code = None if kind is None else (KINDS.get(kind) if isinstance(kind, str) else int(kind))
+    if code == E2M1:
+        return 2 * units
+    if code in (E3M2, E2M3):
+        if units % 3:
+            raise ValueError("packed fp6 rows are whole groups of 3 bytes (4 elements)")
+        return units // 3 * 4
+    return units
 
 
 def decode(bits: np.ndarray, kind=None) -> np.ndarray:
     bits = np.ascontiguousarray(bits)
-    per = _per_unit(kind)
-    out = np.empty(bits.shape[:-1] + (bits.shape[-1] * per,) if bits.ndim else bits.shape, dtype=np.float64)
-    lib().kl_oracle_decode(_kind(bits, kind), bits.ctypes.data, bits.size * per, out.ctypes.data)
+    if bits.ndim == 0:
+        bits = bits.reshape(1)
+    n = elements(kind, bits.shape[-1])
+    out = np.empty(bits.shape[:-1] + (n,), dtype=np.float64)
+    rows = bits.size // bits.shape[-1] if bits.shape[-1] else 0
+    for r, row in enumerate(bits.reshape(rows, bits.shape[-1])):  # one call per row: fp6 rows pack apart
+        lib().kl_oracle_decode(_kind(bits, kind), row.ctypes.data, n, out.reshape(rows, n)[r].ctypes.data)
     return out
 
 
@@ -87,7 +101,7 @@ def gemm_f64(a: np.ndarray, b: np.ndarray, scale: float = 1.0, threads: int | No
     a = np.ascontiguousarray(a)
     b = np.ascontiguousarray(b)
     assert a.dtype == b.dtype and a.shape[1] == b.shape[1]
-    m, k = a.shape[0], a.shape[1] * _per_unit(kind)
+    m, k = a.shape[0], elements(kind, a.shape[1])
     n = b.shape[0]
     c = np.empty((m, n), dtype=np.float64)
     rc = lib().kl_oracle_gemm_f64(_kind(a, kind), a.ctypes.data, k, b.ctypes.data, k, m, n, k, float(scale),
@@ -100,7 +114,7 @@ def gemm_f32(a: np.ndarray, b: np.ndarray, scale: float = 1.0, threads: int | No
     """scale * A . B^T with fp32 accumulation (the timed CPU baseline)."""
     a = np.ascontiguousarray(a)
     b = np.ascontiguousarray(b)
-    m, k = a.shape[0], a.shape[1] * _per_unit(kind)
+    m, k = a.shape[0], elements(kind, a.shape[1])
     n = b.shape[0]
     c = np.empty((m, n), dtype=np.float32)
     rc = lib().kl_oracle_gemm_f32(_kind(a, kind), a.ctypes.data, k, b.ctypes.data, k, m, n, k, float(scale),
@@ -118,7 +132,7 @@ def e8m0_values(s: np.ndarray) -> np.ndarray:
 def _mx_call(fn, out_dtype, a, b, sfa, sfb, kind, scale, threads, vec=32, sf_format="ue8m0"):
     a, b = np.ascontiguousarray(a), np.ascontiguousarray(b)
     sfa, sfb = np.ascontiguousarray(sfa, dtype=np.uint8), np.ascontiguousarray(sfb, dtype=np.uint8)
-    m, k = a.shape[0], a.shape[1] * _per_unit(kind)
+    m, k = a.shape[0], elements(kind, a.shape[1])
     n = b.shape[0]
     groups = -(-k // vec)
     assert sfa.shape == (m, groups) and sfb.shape == (n, groups) and b.shape[1] == a.shape[1]

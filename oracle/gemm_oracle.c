@@ -29,8 +29,11 @@
  * NaN; e5m2 (OCP FP8) has 1 sign, 5 exponent (bias 15), 2 mantissa bits, with IEEE infinities and
  * NaNs at exponent 31; e2m1 (OCP fp4) has 1 sign, 2 exponent (bias 1), 1 mantissa bit, no
  * infinities or NaNs (values 0, 0.5, 1, 1.5, 2, 3, 4, 6), stored two per byte with the first
- * element in the low nibble. Type codes follow the library's kl_dtype: bf16 0, f16 1, e4m3 2,
- * e5m2 3, e2m1 8.
+ * element in the low nibble. e3m2 and e2m3 (OCP fp6) have 1 sign, 3 exponent (bias 3) and 2
+ * mantissa bits, or 2 exponent (bias 1) and 3 mantissa bits, no infinities or NaNs (largest 28 and
+ * 7.5), packed four to three bytes: element i of a row at bits [6i, 6i + 6) of its bytes, least
+ * significant bit first. Type codes follow the library's kl_dtype: bf16 0, f16 1, e4m3 2, e5m2 3,
+ * e2m1 8, e3m2 11, e2m3 12.
  */
 #include <math.h>
 #include <pthread.h>
@@ -43,12 +46,28 @@
 #define KL_ORACLE_E4M3 2
 #define KL_ORACLE_E5M2 3
 #define KL_ORACLE_E2M1 8 /* two per byte, the first in the low nibble */
+#define KL_ORACLE_E3M2 11 /* four per three bytes, least significant bits first */
+#define KL_ORACLE_E2M3 12
 
 static int elem_size(int t) { return (t == KL_ORACLE_BF16 || t == KL_ORACLE_F16) ? 2 : 1; }
 
-/* Bytes of `count` elements of type t (packed e2m1: two per byte; count even). */
+/* Bytes of `count` elements of type t (packed e2m1: two per byte, count even; packed fp6: four
+ * per three bytes, count a multiple of 4). */
 static size_t bytes_of(int t, int64_t count) {
-  return t == KL_ORACLE_E2M1 ? (size_t)(count / 2) : (size_t)count * (size_t)elem_size(t);
+  if (t == KL_ORACLE_E2M1) return (size_t)(count / 2);
+  if (t == KL_ORACLE_E3M2 || t == KL_ORACLE_E2M3) return (size_t)(count / 4 * 3);
+  return (size_t)count * (size_t)elem_size(t);
+}
+
+/* A sign-magnitude minifloat with `eb` exponent bits (bias 2^(eb-1) - 1), `mb` mantissa bits and
+ * no special values: fp6 e3m2 (3, 2) and e2m3 (2, 3). */
+static double decode_finite(uint32_t v, int eb, int mb) {
+  const int sign = (v >> (eb + mb)) & 1;
+  const int exp = (v >> mb) & ((1 << eb) - 1);
+  const uint32_t man = v & ((1u << mb) - 1);
+  const int bias = (1 << (eb - 1)) - 1;
+  const double x = exp == 0 ? ldexp((double)man, 1 - bias - mb) : ldexp((double)((1u << mb) | man), exp - bias - mb);
+  return sign ? -x : x;
 }
 
 static double decode_bf16(uint16_t h) {
@@ -99,6 +118,16 @@ void kl_oracle_decode(int t, const void* src, int64_t n, double* dst) {
   } else if (t == KL_ORACLE_E5M2) {
     const uint8_t* s = (const uint8_t*)src;
     for (int64_t i = 0; i < n; ++i) dst[i] = decode_ieee(s[i], 5, 2);
+  } else if (t == KL_ORACLE_E3M2 || t == KL_ORACLE_E2M3) {
+    const int eb = t == KL_ORACLE_E3M2 ? 3 : 2;
+    const uint8_t* s = (const uint8_t*)src;
+    for (int64_t i = 0; i < n; ++i) {
+      const int64_t bit = 6 * i, byte = bit >> 3;
+      const int shift = (int)(bit & 7);
+      uint32_t w = s[byte];
+      if (shift > 2) w |= (uint32_t)s[byte + 1] << 8; /* the element spills into the next byte */
+      dst[i] = decode_finite((w >> shift) & 63u, eb, 5 - eb);
+    }
   } else if (t == KL_ORACLE_E2M1) {
     double table[16];
     for (uint32_t v = 0; v < 16; ++v) {

@@ -238,6 +238,18 @@ int main(int argc, char** argv) {
       bs(uint32_t(r >> 32), "e2m1", "e2m1", 256, 256, 2, 2);
     }
     bs(uint32_t(cute::UMMA::make_instr_desc_block_scaled<E2, E2, float, UE4, 128, 256, Major::K, Major::K>()), "e2m1/ue4m3", "e2m1/ue4m3", 128, 256, 0, 0);
+    // fp6 through kind::mxf8f6f4 (CuTe's shared-memory element types for TMA-unpacked fp6).
+    using F6a = cutlass::detail::float_e3m2_unpacksmem_t;
+    using F6b = cutlass::detail::float_e2m3_unpacksmem_t;
+    bs(uint32_t(cute::UMMA::make_instr_desc_block_scaled<F6a, F6a, float, UE8, 128, 256, Major::K, Major::K>()), "e3m2", "e3m2", 128, 256, 0, 0);
+    bs(uint32_t(cute::UMMA::make_instr_desc_block_scaled<F6b, F6b, float, UE8, 256, 256, Major::K, Major::K>()), "e2m3", "e2m3", 256, 256, 0, 0);
+    bs(uint32_t(cute::UMMA::make_instr_desc_block_scaled<F6b, F6a, float, UE8, 256, 192, Major::K, Major::K>()), "e2m3", "e3m2", 256, 192, 0, 0);
+    bs(uint32_t(cute::UMMA::make_instr_desc_block_scaled<E4, F6a, float, UE8, 128, 128, Major::K, Major::K>()), "e4m3", "e3m2", 128, 128, 0, 0);
+    {
+      const uint64_t r = cute::UMMA::make_runtime_instr_desc_block_scaled<F6a, F6a, float, UE8, 256, 256, Major::K, Major::K>(
+          3u << 30, 1u << 30);
+      bs(uint32_t(r >> 32), "e3m2", "e3m2", 256, 256, 3, 1);
+    }
     for (int a_sf = 0; a_sf < 4; ++a_sf)
       for (int b_sf = 0; b_sf < 4; ++b_sf) {
         const uint64_t r = cute::UMMA::make_runtime_instr_desc_block_scaled<E4, E4, float, UE8, 128, 256, Major::K, Major::K>(

@@ -9,7 +9,8 @@ from oracle import gemm as og
 
 
 TORCH_TYPES = {"bf16": torch.bfloat16, "f16": torch.float16, "e4m3": torch.float8_e4m3fn,
-               "e5m2": torch.float8_e5m2, "f32": torch.float32, "e2m1": torch.float4_e2m1fn_x2}
+               "e5m2": torch.float8_e5m2, "f32": torch.float32, "e2m1": torch.float4_e2m1fn_x2,
+               "e3m2": torch.uint8, "e2m3": torch.uint8}  # packed fp6 travels as bytes
 FP8_MAX = {"e4m3": 448.0, "e5m2": 57344.0}
 
 

@@ -12,7 +12,7 @@ from golden_util import ELEM_BYTES, idesc_majors, idescs, known_answers, mn_tile
 
 HEADER = Path(__file__).resolve().parent.parent / "include" / "kl_gemm.h"
 TYPE = {"bf16": kl.KL_BF16, "f16": kl.KL_F16, "f32": kl.KL_F32, "i8": kl.KL_I8, "e4m3": kl.KL_E4M3, "e5m2": kl.KL_E5M2,
-        "e2m1": kl.KL_E2M1}
+        "e2m1": kl.KL_E2M1, "e3m2": kl.KL_E3M2, "e2m3": kl.KL_E2M3}
 
 
 def declared_symbols():
@@ -160,7 +160,7 @@ def test_block_scaled_instr_desc_matches_cute():
     from golden_util import host_tables
 
     rows = [t for t in host_tables() if t["kind"] == "idesc_block_scaled"]
-    assert len(rows) == 24
+    assert len(rows) == 29
     for d in rows:
         a, _, sf = d["a"].partition("/")  # "e2m1/ue4m3": NVFP4 (UE4M3 scales); otherwise UE8M0
         b = d["b"].partition("/")[0]

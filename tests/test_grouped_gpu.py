@@ -110,9 +110,10 @@ def test_grouped_gemm_limits(cuda):
 
 
 @pytest.mark.parametrize("algo", [kl.ALGO_1CTA, kl.ALGO_2CTA], ids=["1cta", "2cta"])
-@pytest.mark.parametrize("kind", ["e4m3", "e2m1"])
+@pytest.mark.parametrize("kind", ["e4m3", "e2m1", "e2m3"])
 def test_grouped_block_scaled(cuda, algo, kind):
-    """MoE experts in MX formats: B's block scales are the groups' blocked arrays back to back."""
+    """MoE experts in MX formats: B's block scales are the groups' blocked arrays back to back
+    (packed fp6 experts: a rank-3 16U6 tensor map over the stack)."""
     from maia_b200 import workloads as wl
 
     sizes, n, k = [256, 512, 256], 320, 512
@@ -132,7 +133,8 @@ def test_grouped_block_scaled(cuda, algo, kind):
     psa = kl.pack_block_scales(torch.from_numpy(sa).to(cuda), k)
     psb = torch.cat([kl.pack_block_scales(torch.from_numpy(x).to(cuda), k) for x in sb])
     c = torch.full((qa.shape[0], n), float("nan"), dtype=torch.float32, device=cuda)
-    kl.gemm_grouped(a, b, torch.from_numpy(blocks).to(cuda), c, algo=algo, sfa=psa, sfb=psb)
+    kl.gemm_grouped(a, b, torch.from_numpy(blocks).to(cuda), c, algo=algo, sfa=psa, sfb=psb,
+                    ab_type=kind if kind in kl.FP6_TYPES else None)
     torch.cuda.synchronize()
     assert kl.read_status() == 0
     got, r0 = c.cpu().numpy(), 0

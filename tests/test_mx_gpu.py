@@ -34,9 +34,14 @@ def mx_inputs(m, n, k, kind, seed, spread=0.0):
     return qa, sa, qb, sb
 
 
+FP6 = ("e3m2", "e2m3")
+
+
 def run_mx(qa, sa, qb, sb, kind, out, device, **kw):
-    k = qa.shape[1] * (2 if kind == "e2m1" else 1)
+    k = og.elements(kind, qa.shape[1])
     a, b = to_device(qa, kind, device), to_device(qb, kind, device)
+    if kind in FP6:
+        kw.setdefault("ab_type", kind)
     psa = kl.mx_pack_scales(torch.from_numpy(sa).to(device), k)
     psb = kl.mx_pack_scales(torch.from_numpy(sb).to(device), k)
     c = kw.pop("c", None)
@@ -105,6 +110,74 @@ def test_mxfp4_wide_scale_range(cuda):
     qa, sa, qb, sb = mx_inputs(384, 512, 768, "e2m1", seed=6, spread=10.0)
     c = run_mx(qa, sa, qb, sb, "e2m1", "f32", cuda, algo=kl.ALGO_2CTA)
     check_mx(c, qa, sa, qb, sb, "e2m1")
+
+
+@KERNELS
+@pytest.mark.parametrize("kind", FP6)
+@pytest.mark.parametrize("out", ["bf16", "f32"])
+@pytest.mark.parametrize("shape", [(128, 256, 128), (200, 304, 384), (1000, 1000, 1024)])
+def test_mxfp6_gemm(cuda, algo, variant, kind, out, shape):
+    """Packed fp6 (four elements per three bytes) read through TMA's 16U6 type, which gives every 16
+    elements a 16-byte shared-memory slot, into kind::mxf8f6f4 MMAs with UE8M0 scales per 32."""
+    m, n, k = shape
+    qa, sa, qb, sb = mx_inputs(m, n, k, kind, seed=5 * m + n + k)
+    c = run_mx(qa, sa, qb, sb, kind, out, cuda, algo=algo, variant=variant)
+    check_mx(c, qa, sa, qb, sb, kind)
+
+
+@pytest.mark.parametrize("kind", FP6)
+@pytest.mark.parametrize("algo", [kl.ALGO_1CTA, kl.ALGO_2CTA], ids=["1cta", "2cta"])
+def test_mxfp6_equals_mxfp8_on_the_same_values(cuda, kind, algo):
+    """Every e3m2 and e2m3 value is an e4m3 value: the fp6 kernel and the MXFP8 kernel, given the
+    same values and scales, run the same MMA kind in the same order and agree bit for bit."""
+    qa, sa, qb, sb = mx_inputs(384, 512, 768, kind, seed=11)
+    c6 = run_mx(qa, sa, qb, sb, kind, "f32", cuda, algo=algo)
+    to8 = lambda q: wl.f32_to_e4m3_bits(og.decode(q, kind).astype(np.float32))
+    assert np.array_equal(og.decode(to8(qa), "e4m3"), og.decode(qa, kind))
+    c8 = run_mx(to8(qa), sa, to8(qb), sb, "e4m3", "f32", cuda, algo=algo)
+    assert np.array_equal(c6, c8)
+
+
+@pytest.mark.parametrize("kind", FP6)
+def test_mxfp6_wide_scale_range(cuda, kind):
+    qa, sa, qb, sb = mx_inputs(384, 512, 768, kind, seed=7, spread=10.0)
+    c = run_mx(qa, sa, qb, sb, kind, "f32", cuda, algo=kl.ALGO_2CTA, variant=3)
+    check_mx(c, qa, sa, qb, sb, kind)
+
+
+def test_mxfp6_auto_small_m_uses_a_tile_kernel(cuda):
+    """No skinny kernel for fp6: KL_ALGO_AUTO sends 16 rows to a tile kernel; KL_ALGO_SKINNY says
+    it cannot."""
+    qa, sa, qb, sb = mx_inputs(16, 1024, 512, "e3m2", seed=8)
+    check_mx(run_mx(qa, sa, qb, sb, "e3m2", "bf16", cuda, algo=kl.ALGO_AUTO), qa, sa, qb, sb, "e3m2")
+    with pytest.raises(kl.KlError) as e:
+        run_mx(qa, sa, qb, sb, "e3m2", "bf16", cuda, algo=kl.ALGO_SKINNY)
+    assert e.value.status == kl.KL_ERR_NOT_SUPPORTED
+
+
+def test_mxfp6_limits(cuda):
+    """The 16U6 tensor maps' rules, checked on the host before any launch: K, pitches and strides
+    in whole 128-element (96-byte) blocks, A and B 32-byte aligned."""
+    c = torch.zeros(128, 128, dtype=torch.bfloat16, device=cuda)
+    sf = torch.full((kl.block_scale_bytes(128, 256),), 127, dtype=torch.uint8, device=cuda)
+    a = torch.zeros(128, 120, dtype=torch.uint8, device=cuda)  # K = 160
+    with pytest.raises(kl.KlError) as e:
+        kl.gemm(a, a, c, sfa=sf, sfb=sf, ab_type="e3m2", algo=kl.ALGO_1CTA)
+    assert e.value.status == kl.KL_ERR_INVALID_ARGUMENT
+    buf = torch.zeros(128 * 96 + 64, dtype=torch.uint8, device=cuda)
+    assert buf.data_ptr() % 32 == 0
+    shifted = buf[16:16 + 128 * 96].view(128, 96)  # 16-byte but not 32-byte aligned
+    with pytest.raises(kl.KlError) as e:
+        kl.gemm(shifted, buf[:128 * 96].view(128, 96), c, sfa=sf, sfb=sf, ab_type="e2m3", algo=kl.ALGO_2CTA)
+    assert e.value.status == kl.KL_ERR_INVALID_ARGUMENT
+    with pytest.raises(ValueError):
+        kl.gemm(torch.zeros(128, 95, dtype=torch.uint8, device=cuda), a, c, sfa=sf, sfb=sf, ab_type="e3m2")
+    with pytest.raises(kl.KlError) as e:  # fp6 is MX-only
+        kl.gemm(buf[:128 * 96].view(128, 96), buf[:128 * 96].view(128, 96), c, sfa=sf, sfb=sf, scale_vec=16,
+                ab_type="e3m2")
+    assert e.value.status == kl.KL_ERR_NOT_SUPPORTED
+    torch.cuda.synchronize()
+    assert kl.read_status() == 0
 
 
 @KERNELS
@@ -250,13 +323,15 @@ def test_block_scaled_decode_skinny(cuda, kind, vec, m):
         assert elem <= FP8_TOL and norm <= FP8_TOL, f"algo {algo}: {elem:.3e} / {norm:.3e}"
 
 
-@pytest.mark.parametrize("kind", ["e4m3", "e2m1"])
+@pytest.mark.parametrize("kind", ["e4m3", "e2m1", "e3m2", "e2m3"])
 @pytest.mark.parametrize("src", ["f32", "bf16"])
 @pytest.mark.parametrize("rows,k", [(1, 32), (200, 320), (129, 1024)])
 def test_device_mx_quantize_matches_reference(cuda, kind, src, rows, k):
     """kl_mx_quantize = the OCP MX quantisation restated in maia_b200.workloads.mx_quantize: the same
     scales bit for bit, the same element values (compared as values: the device may encode a
-    negative value that rounds to zero as -0)."""
+    negative value that rounds to zero as -0). Packed fp6 rows are whole 128-element blocks."""
+    if kind in FP6:
+        k = -(-k // 128) * 128
     rng = np.random.default_rng(rows + k)
     x = (rng.standard_normal((rows, k)) * np.exp2(rng.uniform(-8, 8, (rows, 1)))).astype(np.float32)
     if src == "bf16":
@@ -272,7 +347,7 @@ def test_device_mx_quantize_matches_reference(cuda, kind, src, rows, k):
     np.testing.assert_array_equal(got_v, og.decode(want_q, kind))
 
 
-@pytest.mark.parametrize("kind", ["e4m3", "e2m1"])
+@pytest.mark.parametrize("kind", ["e4m3", "e2m1", "e3m2", "e2m3"])
 def test_device_quantize_then_gemm(cuda, kind):
     """Activations and weights quantised on the device feed the block-scaled GEMM directly."""
     rng = np.random.default_rng(9)
@@ -280,7 +355,7 @@ def test_device_quantize_then_gemm(cuda, kind):
     xb = rng.standard_normal((384, 512)).astype(np.float32)
     qa, sa = kl.mx_quantize(torch.from_numpy(xa).to(cuda), kind)
     qb, sb = kl.mx_quantize(torch.from_numpy(xb).to(cuda), kind)
-    c = kl.gemm(qa, qb, sfa=sa, sfb=sb, out_dtype=torch.float32)
+    c = kl.gemm(qa, qb, sfa=sa, sfb=sb, out_dtype=torch.float32, ab_type=kind if kind in FP6 else None)
     torch.cuda.synchronize()
     assert kl.read_status() == 0
     ra, rsa = wl.mx_quantize(xa, kind)
