@@ -109,8 +109,8 @@ def cpu_baseline(w, budget_s: float = 6.0):
         t0 = time.perf_counter()
         if w.dtype == "nvfp4":
             og.gemm_nv_f32(a, b, sa[0], sb[0], sa[1] * sb[1], threads=threads)
-        elif w.dtype in ("mxfp8", "mxfp4"):
-            og.gemm_mx_f32(a, b, sa, sb, "e4m3" if w.dtype == "mxfp8" else "e2m1", threads=threads)
+        elif w.dtype in wl.MX_ELEMENT:
+            og.gemm_mx_f32(a, b, sa, sb, wl.MX_ELEMENT[w.dtype], threads=threads)
         else:
             og.gemm_f32(a, b, sa * sb, threads=threads)
         dt = time.perf_counter() - t0
@@ -191,7 +191,7 @@ def main():
     a_bits, b_bits, sa, sb = wl.make_inputs(w)
     n_lo, n_hi = sharding.shard_range(w.n, world, rank, align=256)
     b_bits = np.ascontiguousarray(b_bits[n_lo:n_hi])
-    mx = w.dtype in ("mxfp8", "mxfp4", "nvfp4")
+    mx = w.dtype in ("mxfp8", "mxfp6", "mxfp4", "nvfp4")
     vec = 16 if w.dtype == "nvfp4" else 32
     gscale = None
     if w.dtype == "nvfp4":  # (block scales, per-tensor scale) pairs
@@ -201,8 +201,9 @@ def main():
         sb = np.ascontiguousarray(sb[n_lo:n_hi])
     nshard = n_hi - n_lo
     np_view = np.int16 if w.dtype == "bf16" else np.uint8
-    tdt = {"bf16": torch.bfloat16, "mxfp4": torch.float4_e2m1fn_x2, "nvfp4": torch.float4_e2m1fn_x2}.get(
-        w.dtype, torch.float8_e4m3fn)
+    # Packed fp6 has no torch dtype: its bytes travel as uint8 with ab_type naming the format.
+    tdt = {"bf16": torch.bfloat16, "mxfp4": torch.float4_e2m1fn_x2, "nvfp4": torch.float4_e2m1fn_x2,
+           "mxfp6": torch.uint8}.get(w.dtype, torch.float8_e4m3fn)
     odt = torch.bfloat16 if w.out == "bf16" else torch.float32
     a_host = torch.from_numpy(a_bits.view(np_view)).view(tdt).pin_memory()
     b_host = torch.from_numpy(b_bits.view(np_view)).view(tdt).pin_memory()
@@ -227,7 +228,8 @@ def main():
         sfb_host = sfb.cpu().pin_memory()
     stream = torch.cuda.current_stream(dev)
     kw = dict(scale_a=scale_a, scale_b=scale_b, algo=args.algo, group_m=args.group_m, prefetch=args.prefetch,
-              variant=args.variant, max_ctas=args.max_ctas, sfa=sfa, sfb=sfb, scale_vec=vec)
+              variant=args.variant, max_ctas=args.max_ctas, sfa=sfa, sfb=sfb, scale_vec=vec,
+              ab_type=wl.MX_ELEMENT[w.dtype] if w.dtype == "mxfp6" else None)
 
     def step():
         kl.gemm(a, b, c, **kw)
@@ -259,7 +261,7 @@ def main():
         # One more launch, right after the timed ones, with every CTA stamping clock64 and
         # %globaltimer: the SM clock the kernel really ran at (NVML may report the boost target).
         in_kernel = kl.clock_probe(a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo, group_m=args.group_m,
-                                   sfa=sfa, sfb=sfb, scale_vec=vec)
+                                   sfa=sfa, sfb=sfb, scale_vec=vec, ab_type=kw["ab_type"])
     if kl.read_status() != 0:
         raise RuntimeError("a device-side wait timed out during the benchmark")
     dev_ms = max_over_ranks(dev_ms)
@@ -275,7 +277,7 @@ def main():
     def e2e_step():
         # The host-buffer entry point: copies in, GEMM and copy out, pipelined over column blocks.
         kl.gemm_host(a_host, b_host, c_host, a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo,
-                     sfa=sfa_host, sfb=sfb_host, scale_vec=vec, chunks=args.chunks)
+                     sfa=sfa_host, sfb=sfb_host, scale_vec=vec, chunks=args.chunks, ab_type=kw["ab_type"])
 
     for _ in range(max(args.warmup, 3)):
         e2e_step()
@@ -349,8 +351,8 @@ def main():
                     "peak_source": f"{peak_src} " + ("bf16_tflops (burst)" if w.dtype == "bf16" else
                                                      "4 x bf16_tflops (burst; the dense fp4 rate is four times bf16)"
                                                      if w.dtype in ("mxfp4", "nvfp4") else
-                                                     "2 x bf16_tflops (burst; the fp8 and MXFP8 dense rate is "
-                                                     "twice bf16)"),
+                                                     "2 x bf16_tflops (burst; the fp8, MXFP8 and MXFP6 dense "
+                                                     "rate is twice bf16)"),
                     "algorithmic_flops_per_launch": per_rank_flops}
     roofline["frac"] = roofline["achieved"] / roofline["peak"]
     traffic = None
