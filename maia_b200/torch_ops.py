@@ -47,19 +47,21 @@ def _(a, b, scale_a, scale_b):
 @torch.library.custom_op("kl::gemm_block_scaled", mutates_args=())
 def gemm_block_scaled(a: torch.Tensor, b: torch.Tensor, sfa: torch.Tensor, sfb: torch.Tensor, scale_vec: int = 32,
                       out_dtype: torch.dtype = torch.bfloat16, scale_a: Optional[torch.Tensor] = None,
-                      scale_b: Optional[torch.Tensor] = None) -> torch.Tensor:
+                      scale_b: Optional[torch.Tensor] = None, fp6: str = "") -> torch.Tensor:
     """Block-scaled a @ b.T: a [M, K] and b [N, K] in float8_e4m3fn / float8_e5m2 (MXFP8, scale_vec
-    32) or float4_e2m1fn_x2 ([M, K/2]; MXFP4 with scale_vec 32, NVFP4 with scale_vec 16), sfa / sfb
-    the uint8 scales in the blocked layout of maia_b200.pack_block_scales, optional fp32 scalar
-    per-tensor scales; bf16 or fp32 out."""
+    32) or float4_e2m1fn_x2 ([M, K/2]; MXFP4 with scale_vec 32, NVFP4 with scale_vec 16), or with
+    fp6 = "e3m2" / "e2m3" uint8 packed fp6 ([M, 3K/4], MXFP6); sfa / sfb the uint8 scales in the
+    blocked layout of maia_b200.pack_block_scales, optional fp32 scalar per-tensor scales; bf16 or
+    fp32 out."""
     out = torch.empty((a.shape[0], b.shape[0]), dtype=out_dtype, device=a.device)
     return _kl_gemm(a, b, out, sfa=sfa, sfb=sfb, scale_vec=scale_vec,
                     scale_a=None if scale_a is None else scale_a.float().contiguous(),
-                    scale_b=None if scale_b is None else scale_b.float().contiguous(), algo=ALGO_AUTO)
+                    scale_b=None if scale_b is None else scale_b.float().contiguous(), algo=ALGO_AUTO,
+                    ab_type=fp6 or None)
 
 
 @gemm_block_scaled.register_fake
-def _(a, b, sfa, sfb, scale_vec=32, out_dtype=torch.bfloat16, scale_a=None, scale_b=None):
+def _(a, b, sfa, sfb, scale_vec=32, out_dtype=torch.bfloat16, scale_a=None, scale_b=None, fp6=""):
     return a.new_empty((a.shape[0], b.shape[0]), dtype=out_dtype)
 
 

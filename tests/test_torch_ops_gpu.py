@@ -35,9 +35,9 @@ def test_kl_gemm_fp8_op(cuda):
     assert rel(torch.ops.kl.gemm_fp8(a, b, sa.reshape(1), sb.reshape(1)), ref) < 5e-2
 
 
-@pytest.mark.parametrize("kind,vec", [("e4m3", 32), ("e2m1", 32), ("e2m1", 16)])
+@pytest.mark.parametrize("kind,vec", [("e4m3", 32), ("e2m1", 32), ("e2m1", 16), ("e2m3", 32)])
 def test_kl_gemm_block_scaled_op(cuda, kind, vec):
-    """torch.ops.kl.gemm_block_scaled against the fp64 oracle (MXFP8, MXFP4, NVFP4)."""
+    """torch.ops.kl.gemm_block_scaled against the fp64 oracle (MXFP8, MXFP4, NVFP4, MXFP6)."""
     import numpy as np
 
     import maia_b200 as kl
@@ -59,7 +59,7 @@ def test_kl_gemm_block_scaled_op(cuda, kind, vec):
         qa, sa = wl.mx_quantize(xa, kind)
         qb, sb = wl.mx_quantize(xb, kind)
         ref = og.gemm_mx_f64(qa, qb, sa, sb, kind)
-        scales = {}
+        scales = {"fp6": kind} if kind in ("e3m2", "e2m3") else {}
     psa = kl.pack_block_scales(torch.from_numpy(sa).to(cuda), 512, vec)
     psb = kl.pack_block_scales(torch.from_numpy(sb).to(cuda), 512, vec)
     c = torch.ops.kl.gemm_block_scaled(to_device(qa, kind, cuda), to_device(qb, kind, cuda), psa, psb, vec,
