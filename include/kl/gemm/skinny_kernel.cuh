@@ -54,6 +54,9 @@ struct SkinnyConfig {
   static constexpr bool kMx = SfVec != 0;
   static constexpr bool kNv = SfVec == 16;
   static constexpr bool kFp4 = std::is_same_v<InT, e2m1x2>;
+  // Packed fp6 (e3m2 / e2m3): TMA's 16U6 type gives each element a shared-memory byte, so the tiles
+  // are fp8's; transactions count the packed bytes (3/4 of the tiles).
+  static constexpr bool kFp6 = is_fp6<InT>;
   static constexpr int kSfAtomsK = kMx ? (kFp4 ? 256 : 128) / (4 * SfVec) : 0;
   static constexpr int kXAtoms = kMx ? (TokPad + 127) / 128 : 0;
   static constexpr int kMmasPerSfAtom = kMx ? 4 / kSfAtomsK : 1;
@@ -70,6 +73,7 @@ struct SkinnyConfig {
   static constexpr uint32_t kWBoxBytes = WTile::bytes;
   static constexpr uint32_t kWBytes = WTile::bytes * WSub;
   static constexpr uint32_t kXBytes = XTile::bytes;
+  static constexpr uint32_t kStageTx = (kFp6 ? (kWBytes + kXBytes) / 4 * 3 : kWBytes + kXBytes) + kSfwBytes + kSfxBytes;
   static constexpr uint32_t kOffW = 0;
   static constexpr uint32_t kOffX = kStages * kWBytes;
   static constexpr uint32_t kOffSfw = kOffX + kStages * kXBytes;
@@ -93,6 +97,7 @@ struct SkinnyConfig {
   static_assert(kTmemUsed <= 512, "two accumulators (and the scales) must fit in TMEM");
   static_assert(SfVec == 0 || SfVec == 32 || (SfVec == 16 && kFp4), "scales per 32 elements, or per 16 for fp4");
   static_assert(!kFp4 || kMx, "packed fp4 operands are block-scaled");
+  static_assert(!kFp6 || SfVec == 32, "fp6 operands are MX block-scaled (kind::mxf8f6f4)");
   static_assert(TokPad == 16 || (TokPad % 32 == 0 && TokPad <= 256), "token tile: 16 or a multiple of 32 up to 256");
   static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
   static_assert(kWBytes % 1024 == 0 && kXBytes % 1024 == 0, "stages keep 1 KB alignment");
@@ -248,7 +253,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_skinny_kernel(const __g
           ok = false;
           break;
         }
-        mbarrier_arrive_expect_tx(full_bar(stage), Cfg::kWBytes + Cfg::kXBytes + Cfg::kSfwBytes + Cfg::kSfxBytes);
+        mbarrier_arrive_expect_tx(full_bar(stage), Cfg::kStageTx);
         const int kx = kb * Cfg::kBlockK;
 #pragma unroll
         for (int sub = 0; sub < Cfg::kSub; ++sub)

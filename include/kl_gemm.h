@@ -115,10 +115,9 @@ typedef struct kl_gemm_desc {
    * kl_mx_scale_bytes(rows, k) bytes. C = alpha * sum_k (A[m,k] sfa[m,k/32]) (B[n,k] sfb[n,k/32])
    * [* *scale_a * *scale_b]; C bf16 or f32 (KL_ALGO_2CTA: variant 0/1 = 256 x 256 tiles on a CTA
    * pair, 2 = 256 x 128, 3 = 256 x 192; KL_ALGO_1CTA: variant 0/1 = 128 x 256, 2 = 128 x 128;
-   * KL_ALGO_SKINNY: up to 128 rows of A, bf16 C, e4m3 or e2m1; KL_ALGO_AUTO: skinny up to 128 rows,
-   * the pair from 256), K-major operands, 128-byte swizzle, batch 1. fp6 (KL_E3M2 / KL_E2M3, tile
-   * kernels only): K, lda, ldb and stride_b multiples of 128 elements (96 bytes), A and B 32-byte
-   * aligned. */
+   * KL_ALGO_SKINNY: up to 128 rows of A, bf16 C, e4m3, e3m2, e2m3 or e2m1; KL_ALGO_AUTO: skinny up to 128 rows,
+   * the pair from 256), K-major operands, 128-byte swizzle, batch 1. fp6 (KL_E3M2 / KL_E2M3): K,
+   * lda, ldb and stride_b multiples of 128 elements (96 bytes), A and B 32-byte aligned. */
   int32_t block_scale;
   int32_t reserved; /* must be 0 */
   const void* sfa;

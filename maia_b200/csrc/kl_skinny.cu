@@ -63,8 +63,10 @@ kl_status make_plan(kl_gemm_desc const& d, Plan* p) {
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
-  // Elements per 128-byte K-block: 64 (16-bit), 128 (8-bit), 256 (packed fp4).
-  const int block_k = d.ab_type == KL_E2M1 ? 256 : (d.ab_type == KL_E4M3 || d.ab_type == KL_E5M2) ? 128 : 64;
+  // Elements per 128-byte K-block: 64 (16-bit), 128 (8-bit, and fp6 whose tiles hold a byte per
+  // element), 256 (packed fp4).
+  const bool one_byte = d.ab_type == KL_E4M3 || d.ab_type == KL_E5M2 || d.ab_type == KL_E3M2 || d.ab_type == KL_E2M3;
+  const int block_k = d.ab_type == KL_E2M1 ? 256 : one_byte ? 128 : 64;
   if (d.block_scale != 0 && d.m > 128)
     return fail(KL_ERR_INVALID_ARGUMENT, "KL_ALGO_SKINNY with block scaling handles at most 128 rows of A");
   p->tok = token_tile(d.m);
@@ -75,7 +77,12 @@ kl_status make_plan(kl_gemm_desc const& d, Plan* p) {
   p->n_tiles = int((d.n + 128 * p->sub - 1) / (128 * p->sub));
   p->k_blocks = int((d.k + block_k - 1) / block_k);
   p->total = (long long)p->n_tiles * p->k_blocks;
-  int cap = d.max_ctas > 0 ? std::min(d.max_ctas, sms) : skinny_default_ctas(sms);
+  // Packed fp6 brings 3/4 of fp8's bytes per shared-memory stage (the 16U6 tiles hold a byte per
+  // element), so a latency-bound weight stream keeps fewer bytes in flight per CTA: at 16 tokens it
+  // runs on every SM. Measured on B200 (N = 28672, K = 8192, MXFP6): 16 tokens 36.6 us with 148
+  // CTAs vs 40.8 us with 112; 64 tokens 43.2 us both; 128 tokens 112 CTAs ahead (47.3 vs 53.3 us).
+  const bool fp6 = d.ab_type == KL_E3M2 || d.ab_type == KL_E2M3;
+  int cap = d.max_ctas > 0 ? std::min(d.max_ctas, sms) : (fp6 && d.m <= 16) ? sms : skinny_default_ctas(sms);
   p->grid = int(std::min<long long>(cap, p->total));
   p->ticket_bytes = round_up(size_t(p->n_tiles) * 4 * sizeof(int));
   p->slot_bytes = size_t(p->n_tiles + p->grid - 1) * size_t(p->tok) * 128 * p->sub * sizeof(float);
@@ -240,9 +247,10 @@ int choose_algo(kl_gemm_desc const& d) {
   // stream and the one-CTA tile kernel (112 weight bands of 256 rows) is ahead, 5.88 vs 5.68 TB/s.
   // fp8 halves the MMA work per byte, so it stays on the skinny kernel up to 128 rows.
   if (d.block_scale != 0) {
-    // Block-scaled decode shapes (MXFP8 / MXFP4 / NVFP4 weights, bf16 C) stream on the skinny
-    // kernel up to 128 rows.
-    const bool bs_skinny = d.c_type == KL_BF16 && (d.ab_type == KL_E2M1 || (d.ab_type == KL_E4M3 && d.block_scale == 1));
+    // Block-scaled decode shapes (MXFP8 / MXFP6 / MXFP4 / NVFP4 weights, bf16 C) stream on the
+    // skinny kernel up to 128 rows.
+    const bool mx_8_6 = d.ab_type == KL_E4M3 || d.ab_type == KL_E3M2 || d.ab_type == KL_E2M3;
+    const bool bs_skinny = d.c_type == KL_BF16 && (d.ab_type == KL_E2M1 || (mx_8_6 && d.block_scale == 1));
     if (bs_skinny && d.m <= 128 && d.m_block_group == nullptr) return KL_ALGO_SKINNY;
     return d.m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA;
   }
@@ -278,7 +286,10 @@ kl_status run_skinny(kl_gemm_desc const& d, void* workspace, size_t workspace_by
   if (d.block_scale == 1) {
     if (d.ab_type == KL_E4M3 && d.c_type == KL_BF16) return dispatch_tok_mx<kl::e4m3, kl::bf16, 32>(d, pl, ws, stream);
     if (d.ab_type == KL_E2M1 && d.c_type == KL_BF16) return dispatch_tok_mx<kl::e2m1x2, kl::bf16, 32>(d, pl, ws, stream);
-    return fail(KL_ERR_NOT_SUPPORTED, "KL_ALGO_SKINNY with MX scales supports (A/B, C) = (e4m3, bf16), (e2m1, bf16)");
+    if (d.ab_type == KL_E3M2 && d.c_type == KL_BF16) return dispatch_tok_mx<kl::e3m2, kl::bf16, 32>(d, pl, ws, stream);
+    if (d.ab_type == KL_E2M3 && d.c_type == KL_BF16) return dispatch_tok_mx<kl::e2m3, kl::bf16, 32>(d, pl, ws, stream);
+    return fail(KL_ERR_NOT_SUPPORTED,
+                "KL_ALGO_SKINNY with MX scales supports (A/B, C) = (e4m3, bf16), (e3m2, bf16), (e2m3, bf16), (e2m1, bf16)");
   }
   if (d.block_scale == 2) {
     if (d.ab_type == KL_E2M1 && d.c_type == KL_BF16) return dispatch_tok_mx<kl::e2m1x2, kl::bf16, 16>(d, pl, ws, stream);

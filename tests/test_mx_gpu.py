@@ -145,13 +145,14 @@ def test_mxfp6_wide_scale_range(cuda, kind):
     check_mx(c, qa, sa, qb, sb, kind)
 
 
-def test_mxfp6_auto_small_m_uses_a_tile_kernel(cuda):
-    """No skinny kernel for fp6: KL_ALGO_AUTO sends 16 rows to a tile kernel; KL_ALGO_SKINNY says
-    it cannot."""
+def test_mxfp6_decode_kernels_agree(cuda):
+    """16 rows of fp6 on the skinny kernel (the KL_ALGO_AUTO choice) and on the one-CTA tile kernel:
+    both within tolerance of the oracle; the skinny kernel writes bf16 C only."""
     qa, sa, qb, sb = mx_inputs(16, 1024, 512, "e3m2", seed=8)
-    check_mx(run_mx(qa, sa, qb, sb, "e3m2", "bf16", cuda, algo=kl.ALGO_AUTO), qa, sa, qb, sb, "e3m2")
+    for algo in (kl.ALGO_AUTO, kl.ALGO_SKINNY, kl.ALGO_1CTA):
+        check_mx(run_mx(qa, sa, qb, sb, "e3m2", "bf16", cuda, algo=algo), qa, sa, qb, sb, "e3m2")
     with pytest.raises(kl.KlError) as e:
-        run_mx(qa, sa, qb, sb, "e3m2", "bf16", cuda, algo=kl.ALGO_SKINNY)
+        run_mx(qa, sa, qb, sb, "e3m2", "f32", cuda, algo=kl.ALGO_SKINNY)
     assert e.value.status == kl.KL_ERR_NOT_SUPPORTED
 
 
@@ -290,7 +291,8 @@ def test_mx_reduce_into_bf16_c(cuda, algo):
     check_mx(got, qa, sa, qb, sb, "e4m3", c0=c0.float().numpy().astype(np.float64))
 
 
-@pytest.mark.parametrize("kind,vec", [("e4m3", 32), ("e2m1", 32), ("e2m1", 16)], ids=["mxfp8", "mxfp4", "nvfp4"])
+@pytest.mark.parametrize("kind,vec", [("e4m3", 32), ("e2m1", 32), ("e2m1", 16), ("e3m2", 32), ("e2m3", 32)],
+                         ids=["mxfp8", "mxfp4", "nvfp4", "mxfp6_e3m2", "mxfp6_e2m3"])
 @pytest.mark.parametrize("m", [1, 16, 40, 64, 128])
 def test_block_scaled_decode_skinny(cuda, kind, vec, m):
     """Decode shapes on the stream-K skinny kernel with block scales (weights' scales on the MMA's A
@@ -314,7 +316,7 @@ def test_block_scaled_decode_skinny(cuda, kind, vec, m):
     a, b = to_device(qa, kind, cuda), to_device(qb, kind, cuda)
     for algo in (kl.ALGO_SKINNY, kl.ALGO_AUTO):
         c = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=cuda)
-        kl.gemm(a, b, c, sfa=psa, sfb=psb, scale_vec=vec, algo=algo, **scales)
+        kl.gemm(a, b, c, sfa=psa, sfb=psb, scale_vec=vec, algo=algo, ab_type=kind if kind in FP6 else None, **scales)
         torch.cuda.synchronize()
         assert kl.read_status() == 0
         got = c.float().cpu().numpy()
