@@ -64,3 +64,29 @@ def test_host_pipeline_mxfp8(cuda, m, n, k, chunks):
     elem, norm = og.rel_error(got, want)
     assert elem <= 5e-2 and norm <= 5e-2
     assert torch.equal(c_host.view(torch.int16), ref.cpu().view(torch.int16))
+
+
+@pytest.mark.parametrize("kind", ["e3m2", "e2m3"])
+def test_host_pipeline_mxfp6(cuda, kind):
+    """Packed fp6 through the host-buffer path: column blocks of B start on 256-row boundaries, so
+    every block's device address keeps the 32-byte alignment the fp6 tensor maps need."""
+    from maia_b200 import workloads as wl
+    from oracle import gemm as og
+
+    m, n, k = 384, 3000, 640
+    rng = np.random.default_rng(17)
+    qa, sfa = wl.mx_quantize(rng.standard_normal((m, k)).astype(np.float32), kind)
+    qb, sfb = wl.mx_quantize(rng.standard_normal((n, k)).astype(np.float32), kind)
+    a_dev, b_dev = torch.from_numpy(qa).to(cuda), torch.from_numpy(qb).to(cuda)
+    psa = kl.mx_pack_scales(torch.from_numpy(sfa).to(cuda), k)
+    psb = kl.mx_pack_scales(torch.from_numpy(sfb).to(cuda), k)
+    ref = kl.gemm(a_dev, b_dev, sfa=psa, sfb=psb, ab_type=kind)
+    c_host = torch.full((m, n), float("nan"), dtype=torch.bfloat16).pin_memory()
+    kl.gemm_host(a_dev.cpu().pin_memory(), b_dev.cpu().pin_memory(), c_host, torch.empty_like(a_dev),
+                 torch.empty_like(b_dev), torch.empty((m, n), dtype=torch.bfloat16, device=cuda), chunks=3,
+                 sfa=psa.cpu().pin_memory(), sfb=psb.cpu().pin_memory(), ab_type=kind)
+    torch.cuda.current_stream().synchronize()
+    assert kl.read_status() == 0
+    elem, norm = og.rel_error(c_host.float().numpy(), og.gemm_mx_f64(qa, qb, sfa, sfb, kind))
+    assert elem <= 5e-2 and norm <= 5e-2
+    assert torch.equal(c_host.view(torch.int16), ref.cpu().view(torch.int16))
