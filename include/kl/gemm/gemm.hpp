@@ -53,7 +53,69 @@ struct Problem {
   // group of each 256-row tile's first block, so there blocks 2i and 2i + 1 must agree.
   int groups = 0;
   const int* m_block_group = nullptr;
+  // Stream-K tail (see tn_schedule): 0 = where the last wave would leave many workers idle, 1 =
+  // always (tests), -1 = never. It needs a workspace (kTnStreamKWorkspaceBytes, its first
+  // kTnStreamKTicketBytes zeroed before the first launch; launches keep them zero); without one the
+  // launch is data-parallel.
+  int stream_k = 0;
+  void* sk_workspace = nullptr;
+  size_t sk_workspace_bytes = 0;
 };
+
+// Stream-K workspace: tickets first (zero between launches), then two fp32 slots of one CTA's
+// 128 x 256 accumulator per CTA of every worker (148 one-CTA workers or 74 pairs on a B200).
+inline constexpr size_t kTnStreamKTicketBytes = 64 * 1024;
+inline constexpr size_t kTnStreamKSlotCtas = 148;
+inline constexpr size_t kTnStreamKWorkspaceBytes = kTnStreamKTicketBytes + 2 * kTnStreamKSlotCtas * 128 * 256 * 4;
+
+// How a launch deals its tiles. Data-parallel, the persistent workers take tiles t, t + W, ...; when
+// the tile count leaves the last wave short (fewer than 90 % of the W x waves tile slots used, which
+// N-sharding produces: 8192 x 1024 shards of 256 x 256 tiles are 128 tiles on 74 CTA pairs), the
+// last full wave and the remainder (W + tiles mod W tiles, or all tiles below 2 W) are split along K
+// instead, W equal runs of (tile, K-block) units, so every worker finishes at the same time.
+struct TnSchedule {
+  int tiles = 0;
+  int workers = 0;
+  int sk_tiles = 0;
+  size_t ticket_bytes = 0, slot_bytes = 0;
+};
+
+template <class Cfg>
+TnSchedule tn_schedule(Problem const& pr, int max_workers) {
+  TnSchedule s;
+  const long long tiles_m = (pr.m + Cfg::kTileM - 1) / Cfg::kTileM, tiles_n = (pr.n + Cfg::kTileN - 1) / Cfg::kTileN;
+  const long long tiles = tiles_m * tiles_n * (pr.batch > 1 ? pr.batch : 1);
+  if (tiles <= 0 || tiles > INT32_MAX) return s;
+  s.tiles = int(tiles);
+  int cap = max_workers;
+  if (pr.max_ctas > 0) cap = std::min(cap, std::max(1, pr.max_ctas / Cfg::kCtaGroup));
+  s.workers = std::min(s.tiles, cap);
+  if (pr.stream_k < 0 || cap <= 0) return s;
+  const int W = cap, T = s.tiles;
+  const int tail = T < 2 * W ? T : W + T % W;
+  int sk = 0;
+  if (pr.stream_k > 0) {
+    sk = tail;
+  } else if (T > W && T % W != 0) {
+    const long long waves = (T + W - 1) / W;
+    if (double(T) < 0.9 * double(waves) * double(W)) sk = tail;
+  }
+  if (sk == 0) return s;
+  // Every worker needs at least one unit of the split region (the epilogue counts each worker from
+  // the first to the last contributor of a tile): with fewer units than workers, fewer workers.
+  const long long pack = Cfg::kFp4 ? 2 : 1;
+  const long long k_blocks = (pr.k / pack + Cfg::kBlockK - 1) / Cfg::kBlockK;
+  const int workers = sk == T ? int(std::min<long long>(W, (long long)sk * k_blocks)) : W;
+  const size_t tickets = size_t(sk) * Cfg::kCtaGroup * Cfg::kEpiWarps * sizeof(int);
+  const size_t slots = 2ull * workers * Cfg::kCtaGroup * 128 * Cfg::kTileN * sizeof(float);
+  if (workers <= 0 || tickets > kTnStreamKTicketBytes || kTnStreamKTicketBytes + slots > kTnStreamKWorkspaceBytes)
+    return s;
+  s.workers = workers;
+  s.sk_tiles = sk;
+  s.ticket_bytes = tickets;
+  s.slot_bytes = slots;
+  return s;
+}
 
 // Library defaults for the knobs a Problem leaves at 0.
 inline constexpr int kDefaultPrefetchTn = 0;
@@ -246,8 +308,19 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   const long long all_tiles = (long long)a.tiles_m * a.tiles_n * a.batch;
   if (all_tiles > INT32_MAX) throw std::invalid_argument("kl::gemm: too many tiles");
   const int tiles = int(all_tiles);
-  int workers = std::min(tiles, max_workers);
-  if (pr.max_ctas > 0) workers = std::min(workers, std::max(1, pr.max_ctas / Cfg::kCtaGroup));
+  if (pr.stream_k < -1 || pr.stream_k > 1) throw std::invalid_argument("kl::gemm: stream_k must be -1, 0 or 1");
+  TnSchedule sch = tn_schedule<Cfg>(pr, max_workers);
+  if (sch.sk_tiles > 0 && (pr.sk_workspace == nullptr || pr.sk_workspace_bytes < kTnStreamKWorkspaceBytes)) {
+    Problem dp = pr;  // no workspace: every tile whole
+    dp.stream_k = -1;
+    sch = tn_schedule<Cfg>(dp, max_workers);
+  }
+  const int workers = sch.workers;
+  a.sk_tiles = sch.sk_tiles;
+  a.sk_tickets = sch.sk_tiles > 0 ? static_cast<int*>(pr.sk_workspace) : nullptr;
+  a.sk_slots = sch.sk_tiles > 0 ? reinterpret_cast<float*>(static_cast<char*>(pr.sk_workspace) + kTnStreamKTicketBytes)
+                                : nullptr;
+  if (sch.sk_tiles > 0) a.prefetch = 0;  // the L2 prefetch follows the data-parallel tile order only
 
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];

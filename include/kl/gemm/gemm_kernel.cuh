@@ -185,6 +185,56 @@ struct TnArgs {
   int c_reduce;                 // 0: C = result; 1: C += result (fp32 C: TMA reducing stores; 16-bit C: read, add, store)
   const int* m_block_group;     // m-grouped GEMM: B matrix of each 128-row block of A / C (-1 = padding)
   int sfb_group_blocks;         // m-grouped block-scaled: 128-row scale blocks of each group's B
+  // Stream-K tail: the last `sk_tiles` tiles (in tile order) are not dealt whole to the workers but
+  // split along K, each worker taking an equal run of (tile, K-block) units. A tile split between
+  // workers is summed through fp32 slots (two per worker: the tile its run starts in and the one it
+  // ends in) and a ticket per (tile, CTA of the pair, epilogue warp); the last warp to arrive adds
+  // the slots in worker order and stores C. 0 = every tile whole (data-parallel).
+  int sk_tiles;
+  int* sk_tickets;              // [sk_tiles * CtaGroup * kEpiWarps], zero between launches
+  float* sk_slots;              // [2 * workers * CtaGroup][128 * BlockN]
+};
+
+// The stream-K run of worker w over U units split between W workers: [w U / W, (w + 1) U / W).
+KL_HOST_DEVICE constexpr long long sk_unit_start(int w, long long units, int workers) {
+  return (long long)w * units / workers;
+}
+// The worker whose run holds unit u.
+KL_HOST_DEVICE constexpr int sk_worker_of_unit(long long u, long long units, int workers) {
+  return int(((u + 1) * workers + units - 1) / units) - 1;
+}
+
+// One piece of work: K-blocks [kb0, kb1) of tile t.
+struct TilePiece {
+  int t, kb0, kb1;
+};
+
+// The pieces one worker processes, in order: its data-parallel tiles (every num_workers-th tile
+// of the first num_tiles - sk_tiles, whole K), then its run of the stream-K region cut at tile
+// boundaries. Producer, MMA issuer and epilogue walk the same sequence.
+struct WorkSeq {
+  int workers, dp_tiles, k_blocks, t_dp;
+  long long u, u_end;
+  KL_HOST_DEVICE WorkSeq(int worker, int num_workers, int num_tiles, int sk_tiles, int k_blocks_)
+      : workers(num_workers), dp_tiles(num_tiles - sk_tiles), k_blocks(k_blocks_), t_dp(worker) {
+    const long long units = (long long)sk_tiles * k_blocks_;
+    u = sk_tiles > 0 ? sk_unit_start(worker, units, num_workers) : 0;
+    u_end = sk_tiles > 0 ? sk_unit_start(worker + 1, units, num_workers) : 0;
+  }
+  KL_HOST_DEVICE bool next(TilePiece& w) {
+    if (t_dp < dp_tiles) {
+      w = {t_dp, 0, k_blocks};
+      t_dp += workers;
+      return true;
+    }
+    if (u >= u_end) return false;
+    const long long tu = u / k_blocks;
+    w.t = dp_tiles + int(tu);
+    w.kb0 = int(u - tu * k_blocks);
+    w.kb1 = (u_end - u) < (k_blocks - w.kb0) ? w.kb0 + int(u_end - u) : k_blocks;
+    u += w.kb1 - w.kb0;
+    return true;
+  }
 };
 
 // Most peers an epilogue can push C tiles to (one NVLink/NVSwitch domain of 8 GPUs).
@@ -418,7 +468,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         for (int j = 0; j < pf; ++j) prefetch_unit(worker, j);
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      for (int t = worker; ok && t < num_tiles; t += num_workers) {
+      WorkSeq seq(worker, num_workers, num_tiles, args.sk_tiles, args.k_blocks);
+      TilePiece pc;
+      while (ok && seq.next(pc)) {
+        const int t = pc.t;
         int bz, tm, tn;
         tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, bz, tm, tn);
         const int a_row = tm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM;
@@ -427,8 +480,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         // (a block marked -1 loads B as zeros: padding rows come out 0). A CTA pair's 256-row tile
         // uses the group of its first block: both blocks must name the same group.
         const int gz = args.m_block_group != nullptr ? __ldg(args.m_block_group + tm * CG) : 0;
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
-          if (pf > 0) prefetch_unit(t, kb + pf);
+        for (int kb = pc.kb0; kb < pc.kb1; ++kb) {
+          if (pf > 0) prefetch_unit(t, kb + pf);  // data-parallel launches only (sk_tiles = 0)
           if (!mbarrier_wait(empty_bar(stage), phase ^ 1u, args.timeout_ns)) {
             record_status(args.status, kStatusProducerTimeout);
             ok = false;
@@ -498,7 +551,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
       uint32_t stage = 0, phase = 0;
       uint32_t iter = 0;
       bool ok = true;
-      for (int t = worker; ok && t < num_tiles; t += num_workers, ++iter) {
+      WorkSeq seq(worker, num_workers, num_tiles, args.sk_tiles, args.k_blocks);
+      TilePiece pc;
+      for (; ok && seq.next(pc); ++iter) {
+        const int t = pc.t;
         const uint32_t acc = iter % Cfg::kNumAcc;
         const uint32_t acc_phase = (iter / Cfg::kNumAcc) & 1u;
         if (!mbarrier_wait(tempty_bar(acc), acc_phase ^ 1u, args.timeout_ns)) {
@@ -514,7 +570,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
           tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, tbz, ttm, ttn);
           sfb_word = uint32_t(((ttn * Cfg::kTileN) % 128) / 32);
         }
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
+        for (int kb = pc.kb0; kb < pc.kb1; ++kb) {
           if (!mbarrier_wait(full_bar(stage), phase, args.timeout_ns)) {
             record_status(args.status, kStatusMmaTimeout);
             ok = false;
@@ -545,7 +601,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
           for (int k = 0; k < Cfg::kBlockK / Cfg::kUmmaK; ++k) {
             const uint64_t ka = operand_kstep_16B<typename Cfg::ATile, Cfg::kAMn>(k);
             const uint64_t kb16 = operand_kstep_16B<typename Cfg::BTile, Cfg::kBMn>(k);
-            const uint32_t accumulate = (kb | k) != 0;
+            const uint32_t accumulate = (kb != pc.kb0) || (k != 0);  // a piece starts a fresh sum
             if constexpr (Cfg::kMx) {
               // K-slice k: scale atom q, starting at byte `id` of every 32-bit scale word.
               const int q = k / Cfg::kMmasPerSfAtom;
@@ -713,8 +769,49 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
       if constexpr (Cfg::kChunkCols == 64) tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
     };
 
+    // Stream-K tail. A split tile's partial sums go to the contributing worker's slot as fp32
+    // (element (r, c) of the CTA's 128 x BlockN block at ((c / 32) * 128 + r) * 32 + c % 32: each
+    // warp writes and reads whole 4-KB runs), then each epilogue warp counts in on its own ticket;
+    // the warp that arrives last adds the slots in worker order, so the sum does not depend on
+    // arrival order, and stores C. Nothing waits on another CTA.
+    const int dp_tiles = num_tiles - args.sk_tiles;
+    const long long sk_units = (long long)args.sk_tiles * args.k_blocks;
+    const int erow = quarter * 32 + lane;  // this thread's row of the CTA's 128
+    auto slot_of = [&](int w, int t) -> float* {
+      const int first_t = dp_tiles + int(sk_unit_start(w, sk_units, num_workers) / args.k_blocks);
+      const long long s = 2LL * w + (t == first_t ? 0 : 1);
+      return args.sk_slots + (s * CG + cta_rank) * (128LL * Cfg::kTileN);
+    };
+    auto slot_store = [&](float* slot, int tcol_rel, const uint32_t* v) {
+#pragma unroll
+      for (int g = 0; g < Cfg::kChunkCols / 32; ++g) {
+        float4* dst = reinterpret_cast<float4*>(slot + ((long long)((tcol_rel >> 5) + g) * 128 + erow) * 32);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          __stcg(dst + j, make_float4(__uint_as_float(v[32 * g + 4 * j]), __uint_as_float(v[32 * g + 4 * j + 1]),
+                                      __uint_as_float(v[32 * g + 4 * j + 2]), __uint_as_float(v[32 * g + 4 * j + 3])));
+      }
+    };
+    auto slot_add = [&](const float* slot, int tcol_rel, float* sum) {
+#pragma unroll
+      for (int g = 0; g < Cfg::kChunkCols / 32; ++g) {
+        const float4* src = reinterpret_cast<const float4*>(slot + ((long long)((tcol_rel >> 5) + g) * 128 + erow) * 32);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 x = __ldcg(src + j);  // L2: written by other SMs during this launch
+          sum[32 * g + 4 * j] += x.x;
+          sum[32 * g + 4 * j + 1] += x.y;
+          sum[32 * g + 4 * j + 2] += x.z;
+          sum[32 * g + 4 * j + 3] += x.w;
+        }
+      }
+    };
+
     uint32_t iter = 0;
-    for (int t = worker; t < num_tiles; t += num_workers, ++iter) {
+    WorkSeq seq(worker, num_workers, num_tiles, args.sk_tiles, args.k_blocks);
+    TilePiece pc;
+    for (; seq.next(pc); ++iter) {
+      const int t = pc.t;
       int tm, tn;
       tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, bz, tm, tn);
       const uint32_t acc = iter % Cfg::kNumAcc;
@@ -727,7 +824,50 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
       row0 = tm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM + quarter * 32;
       const int col0 = tn * Cfg::kTileN + wcol;
       const uint32_t tcol = tmem_base + lane_base + acc * Cfg::kAccCols + uint32_t(wcol);
-      if constexpr (Cfg::kEarlyRelease) {
+      int w_first = worker, w_last = worker;  // workers that contribute to tile t
+      if (t >= dp_tiles) {
+        const long long tu0 = (long long)(t - dp_tiles) * args.k_blocks;
+        w_first = sk_worker_of_unit(tu0, sk_units, num_workers);
+        w_last = sk_worker_of_unit(tu0 + args.k_blocks - 1, sk_units, num_workers);
+      }
+      if (w_first != w_last) {
+        // A split tile: this worker's partial sum into its slot, then the ticket.
+        // (Chunk by chunk in every config: a split tile is rare, registers are not.)
+        float* own = slot_of(worker, t);
+#pragma unroll 1
+        for (int c = 0; c < Cfg::kChunks; ++c) {
+          uint32_t v[Cfg::kChunkCols];
+          load_chunk(tcol + uint32_t(c * Cfg::kChunkCols), v);
+          tmem_wait_ld();
+          if (c == Cfg::kChunks - 1) release(acc);
+          slot_store(own, wcol + c * Cfg::kChunkCols, v);
+        }
+        __threadfence();  // this thread's slot writes before the warp's arrival
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+          int* ticket = args.sk_tickets + ((long long)(t - dp_tiles) * CG + cta_rank) * Cfg::kEpiWarps + ew;
+          last = atomicAdd(ticket, 1) == w_last - w_first;
+          if (last) {
+            atomicExch(ticket, 0);  // ready for the next launch
+            __threadfence();        // the other contributors' slots before the reads below
+          }
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        __syncwarp();
+        if (last) {
+#pragma unroll 1
+          for (int c = 0; c < Cfg::kChunks; ++c) {
+            uint32_t v[Cfg::kChunkCols];  // the sum, as fp32 bits (emit_chunk's accumulator form)
+            float* sum = reinterpret_cast<float*>(v);
+#pragma unroll
+            for (int e = 0; e < Cfg::kChunkCols; ++e) sum[e] = 0.0f;
+#pragma unroll 1
+            for (int w = w_first; w <= w_last; ++w) slot_add(slot_of(w, t), wcol + c * Cfg::kChunkCols, sum);
+            emit_chunk(v, col0 + c * Cfg::kChunkCols);
+          }
+        }
+      } else if constexpr (Cfg::kEarlyRelease) {
         // All of this warp's columns into registers, accumulator back to the MMAs, then the stores.
         uint32_t v[Cfg::kWarpCols];
 #pragma unroll

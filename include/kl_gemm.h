@@ -119,7 +119,14 @@ typedef struct kl_gemm_desc {
    * the pair from 256), K-major operands, 128-byte swizzle, batch 1. fp6 (KL_E3M2 / KL_E2M3): K,
    * lda, ldb and stride_b multiples of 128 elements (96 bytes), A and B 32-byte aligned. */
   int32_t block_scale;
-  int32_t reserved; /* must be 0 */
+  /* Tile kernels (KL_ALGO_1CTA / 2CTA, and AUTO's choice of them): 0 = split the last wave along K
+   * across every worker (stream-K) where dealing whole tiles would leave many workers idle at the end
+   * (fewer than 90 % of the tile slots used, as in N-sharded GEMMs: 128 tiles of 256 x 256 on 74 CTA
+   * pairs); 1 = always split the tail; -1 = never. Split tiles are summed through a per-stream
+   * library workspace (37 MiB, allocated on first use, never outside a stream capture; a capture
+   * that finds none runs data-parallel) in a fixed order: results are deterministic but can differ
+   * in the last bits from the data-parallel schedule. */
+  int32_t stream_k;
   const void* sfa;
   const void* sfb;
   /* m-grouped GEMM (mixture-of-experts layout): m_block_group non-NULL makes B a stack of `groups`

@@ -65,7 +65,7 @@ class GemmDesc(ctypes.Structure):
         ("stride_a", ctypes.c_int64), ("stride_b", ctypes.c_int64), ("stride_c", ctypes.c_int64),
         ("a_major", ctypes.c_int32), ("b_major", ctypes.c_int32),
         ("c_reduce", ctypes.c_int32), ("swizzle", ctypes.c_int32),
-        ("block_scale", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("block_scale", ctypes.c_int32), ("stream_k", ctypes.c_int32),
         ("sfa", ctypes.c_void_p), ("sfb", ctypes.c_void_p),
         ("groups", ctypes.c_int32), ("reserved2", ctypes.c_int32),
         ("m_block_group", ctypes.c_void_p),
@@ -240,7 +240,7 @@ def _elements(code: int, units: int) -> int:
 
 def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, group_m=0, max_ctas=0,
               variant=0, prefetch=0, a_major=0, b_major=0, c_reduce=0, swizzle=0, sfa=None, sfb=None,
-              scale_vec=32, ab_type=None) -> GemmDesc:
+              scale_vec=32, ab_type=None, stream_k=0) -> GemmDesc:
     """Descriptor for C = alpha * A . B^T on torch CUDA tensors: A [M,K], B [N,K], C [M,N], or the
     batched forms A [L,M,K], B [L,N,K], C [L,M,N] (L independent GEMMs). a_major / b_major = 1
     pass the operand MN-major: `a` as the stored [K, M] (A transposed in memory), `b` as [K, N].
@@ -248,7 +248,9 @@ def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, gr
     swizzle span in bytes (0 = 128, 64, 32). sfa / sfb (uint8 device tensors in the blocked layout of
     pack_block_scales) make it a block-scaled GEMM: one UE8M0 scale per 32 K-elements of each row
     (MX, scale_vec 32) or one UE4M3 scale per 16 (NVFP4, scale_vec 16, fp4 operands). ab_type =
-    KL_E3M2 / KL_E2M3 passes uint8 `a` / `b` as packed fp6 ([rows, 3 K / 4] bytes)."""
+    KL_E3M2 / KL_E2M3 passes uint8 `a` / `b` as packed fp6 ([rows, 3 K / 4] bytes). stream_k: the
+    tile kernels' stream-K tail, 0 = where the last wave would leave workers idle, 1 = always,
+    -1 = never."""
     for name, t in (("a", a), ("b", b), ("c", c)):
         if t.dim() not in (2, 3) or t.stride(-1) != 1:
             raise ValueError(f"{name} must be a 2-D or 3-D tensor with a contiguous last dimension")
@@ -275,12 +277,13 @@ def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, gr
                     stride_b=bs[1], stride_c=bs[2], a_major=a_major, b_major=b_major, c_reduce=int(c_reduce),
                     swizzle=swizzle,
                     block_scale=0 if sfa is None and sfb is None else (2 if scale_vec == 16 else 1),
+                    stream_k=int(stream_k),
                     sfa=None if sfa is None else sfa.data_ptr(), sfb=None if sfb is None else sfb.data_ptr())
 
 
 def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
          group_m=0, max_ctas=0, variant=0, prefetch=0, a_major=0, b_major=0, accumulate=False, swizzle=0,
-         sfa=None, sfb=None, scale_vec=32, ab_type=None, workspace=None, stream=None):
+         sfa=None, sfb=None, scale_vec=32, ab_type=None, stream_k=0, workspace=None, stream=None):
     """out = alpha * a @ b.T [* scale_a * scale_b] on the current CUDA stream, via kl_gemm.
     accumulate=True: out += alpha * a @ b.T (out must be given). sfa/sfb: block scales (see
     pack_block_scales). ab_type="e3m2" / "e2m3": a and b are uint8 packed fp6."""
@@ -294,7 +297,7 @@ def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=Non
         shape = (a.shape[0], m, n) if a.dim() == 3 else (m, n)
         out = torch.empty(shape, dtype=out_dtype or torch.bfloat16, device=a.device)
     d = gemm_desc(a, b, out, alpha, scale_a, scale_b, algo, group_m, max_ctas, variant, prefetch, a_major, b_major,
-                  int(bool(accumulate)), swizzle, sfa, sfb, scale_vec, ab_type)
+                  int(bool(accumulate)), swizzle, sfa, sfb, scale_vec, ab_type, stream_k)
     s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
     if workspace is None:
         check(lib().kl_gemm(ctypes.byref(d), ctypes.c_void_p(s)))
@@ -310,7 +313,8 @@ def block_scale_bytes(rows: int, k: int, vec: int = 32) -> int:
 
 
 def gemm_grouped(a, b, m_block_group, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=None,
-                 accumulate=False, algo=ALGO_1CTA, sfa=None, sfb=None, scale_vec=32, ab_type=None, stream=None):
+                 accumulate=False, algo=ALGO_1CTA, sfa=None, sfb=None, scale_vec=32, ab_type=None, stream_k=0,
+                 stream=None):
     """m-grouped GEMM (mixture-of-experts layout): a [M, K] holds the groups' rows back to back,
     each group padded to a multiple of 128 rows; b [G, N, K] holds one matrix per group;
     m_block_group is an int32 device tensor of ceil(M / 128) entries naming the group of every
@@ -328,7 +332,7 @@ def gemm_grouped(a, b, m_block_group, out=None, *, out_dtype=None, alpha=1.0, sc
     if out is None:
         out = torch.empty((a.shape[0], b.shape[1]), dtype=out_dtype or torch.bfloat16, device=a.device)
     d = gemm_desc(a, b[0], out, alpha, scale_a, scale_b, algo, c_reduce=int(bool(accumulate)), sfa=sfa, sfb=sfb,
-                  scale_vec=scale_vec, ab_type=ab_type)
+                  scale_vec=scale_vec, ab_type=ab_type, stream_k=stream_k)
     d.groups = b.shape[0]
     d.stride_b = _elements(_operand_type(b, ab_type), b.stride(0))
     d.m_block_group = m_block_group.data_ptr()
@@ -404,13 +408,13 @@ def gemm_host(a_host, b_host, c_host, a_dev, b_dev, c_dev, *, alpha=1.0, scale_a
 
 
 def gemm_gather(a, b, c_shard, peer_ptrs, *, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
-                group_m=0, sfa=None, sfb=None, scale_vec=32, ab_type=None, stream=None):
+                group_m=0, sfa=None, sfb=None, scale_vec=32, ab_type=None, stream_k=0, stream=None):
     """c_shard = alpha * a @ b.T, and the same tiles written to each peer pointer (a view of the same
     columns in another GPU's copy of C, with c_shard's pitch), through kl_gemm_gather."""
     import torch
 
     d = gemm_desc(a, b, c_shard, alpha, scale_a, scale_b, algo, group_m, sfa=sfa, sfb=sfb, scale_vec=scale_vec,
-                  ab_type=ab_type)
+                  ab_type=ab_type, stream_k=stream_k)
     arr = (ctypes.c_void_p * max(1, len(peer_ptrs)))(*[ctypes.c_void_p(p) for p in peer_ptrs])
     s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
     check(lib().kl_gemm_gather(ctypes.byref(d), arr, len(peer_ptrs), ctypes.c_void_p(s)))

@@ -26,7 +26,14 @@ int choose_algo(kl_gemm_desc const& d);
 kl_status skinny_workspace_size(kl_gemm_desc const& d, size_t* bytes);
 kl_status run_skinny(kl_gemm_desc const& d, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 // After a timed-out kernel the library workspace's tickets may be mid-count: re-zero before reuse.
+// (Marks the skinny workspace and every stream-K tile workspace of the device.)
 void mark_workspace_dirty(int device);
+
+// Stream-K workspace of the tile kernels for `stream` on the current device (kl_tile_ws.cu):
+// kl::gemm::kTnStreamKWorkspaceBytes with zeroed tickets, or nullptr where none can be had without
+// allocating inside a stream capture (the launch then deals whole tiles).
+kl_status tile_stream_k_workspace(cudaStream_t stream, void** out);
+void tile_workspaces_mark_dirty(int device);
 
 // Failure-path probe (kl_probe.cu).
 kl_status launch_wait_probe(int* status, unsigned long long timeout_ns, cudaStream_t stream);

@@ -236,6 +236,7 @@ kl_status library_workspace(size_t need, size_t tickets, cudaStream_t stream, vo
 
 void mark_workspace_dirty(int device) {
   if (device < 0 || device >= 64) return;
+  tile_workspaces_mark_dirty(device);
   std::lock_guard<std::mutex> lock(g_ws_mutex);
   g_ws[device].dirty = true;
 }

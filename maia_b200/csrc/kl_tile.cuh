@@ -13,11 +13,27 @@
 namespace kl::capi {
 
 // Queue the tile kernel `Cfg` for `pr`, reporting into the device status word.
+// A launch whose schedule has a stream-K tail gets the stream's workspace (unless the caller
+// brought one); without it the launch deals whole tiles.
 template <class Cfg>
-kl_status run_cfg(kl::gemm::Problem const& pr, cudaStream_t stream, kl::gemm::LaunchInfo* info) {
+kl_status run_cfg(kl::gemm::Problem const& pr0, cudaStream_t stream, kl::gemm::LaunchInfo* info) {
   int* status = nullptr;
   kl_status s = device_status_ptr(&status);
   if (s != KL_OK) return s;
+  kl::gemm::Problem pr = pr0;
+  if (pr.stream_k >= 0 && pr.sk_workspace == nullptr) {
+    int dev = 0, max_workers = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = kl::gemm::detail::prepare_kernel<Cfg>(dev, &max_workers);
+    if (e != cudaSuccess) return cuda_fail(e, "kl_gemm setup");
+    if (kl::gemm::tn_schedule<Cfg>(pr, max_workers).sk_tiles > 0) {
+      void* ws = nullptr;
+      s = tile_stream_k_workspace(stream, &ws);
+      if (s != KL_OK) return s;
+      pr.sk_workspace = ws;
+      pr.sk_workspace_bytes = ws != nullptr ? kl::gemm::kTnStreamKWorkspaceBytes : 0;
+    }
+  }
   cudaError_t e = kl::gemm::launch_tn<Cfg>(pr, status, wait_timeout_ns(), stream, info);
   if (e != cudaSuccess) return cuda_fail(e, "kl_gemm launch");
   return KL_OK;

@@ -1,0 +1,67 @@
+// Stream-K workspaces of the tile kernels: one fixed-size buffer per (device, stream), allocated on
+// first use and never freed or moved while the process runs, so a CUDA graph that captured a launch
+// keeps a valid pointer. Its ticket area is zeroed once and stays zero between launches (the last
+// contributor to each split tile resets its ticket); after a timed-out launch it is re-zeroed on the
+// stream before the next use.
+
+#include <cuda_runtime.h>
+
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include <kl/gemm/gemm.hpp>
+
+#include "kl_internal.cuh"
+
+namespace kl::capi {
+
+namespace {
+
+struct TileWorkspace {
+  void* ptr = nullptr;
+  bool dirty = false;
+};
+std::mutex g_tile_ws_mutex;
+std::map<std::pair<int, cudaStream_t>, TileWorkspace> g_tile_ws;
+
+}  // namespace
+
+kl_status tile_stream_k_workspace(cudaStream_t stream, void** out) {
+  *out = nullptr;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(stream, &cap);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+  const bool capturing = cap != cudaStreamCaptureStatusNone;
+  std::lock_guard<std::mutex> lock(g_tile_ws_mutex);
+  TileWorkspace& w = g_tile_ws[{dev, stream}];
+  if (w.ptr == nullptr) {
+    if (capturing) return KL_OK;  // no allocation inside a capture: this launch stays data-parallel
+    e = cudaMalloc(&w.ptr, kl::gemm::kTnStreamKWorkspaceBytes);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      w.ptr = nullptr;
+      return KL_OK;  // out of memory: data-parallel
+    }
+    w.dirty = true;
+  }
+  if (w.dirty) {
+    if (capturing) return KL_OK;
+    e = cudaMemsetAsync(w.ptr, 0, kl::gemm::kTnStreamKTicketBytes, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(stream-K tickets)");
+    w.dirty = false;
+  }
+  *out = w.ptr;
+  return KL_OK;
+}
+
+void tile_workspaces_mark_dirty(int device) {
+  std::lock_guard<std::mutex> lock(g_tile_ws_mutex);
+  for (auto& [key, w] : g_tile_ws)
+    if (key.first == device) w.dirty = true;
+}
+
+}  // namespace kl::capi

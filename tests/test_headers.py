@@ -57,3 +57,17 @@ def test_cmake_consumer_builds_against_kl_target(tmp_path):
     assert bld.returncode == 0, bld.stdout + bld.stderr
     run = subprocess.run([str(build / "kl_header_example")], capture_output=True, text=True)
     assert run.returncode == 0, run.stdout + run.stderr
+
+
+def test_stream_k_schedule(tmp_path):
+    """The tile kernels' work schedule on the host: every (tile, K-block) unit dealt exactly once,
+    data-parallel tiles before the stream-K run, contributors and slots as the epilogue computes
+    them, and tn_schedule's decisions on the N-sharded shapes (tests/native/test_stream_k_schedule.cu)."""
+    exe = tmp_path / "test_stream_k_schedule"
+    cmd = [nvcc(), "-std=c++20", "--expt-relaxed-constexpr", "-gencode", "arch=compute_100a,code=sm_100a",
+           "-I", str(ROOT / "include"), str(ROOT / "tests" / "native" / "test_stream_k_schedule.cu"), "-o", str(exe)]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-4000:]
+    r = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert " 0 failures" in r.stdout
