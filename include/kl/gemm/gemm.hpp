@@ -53,8 +53,8 @@ struct Problem {
   // group of each 256-row tile's first block, so there blocks 2i and 2i + 1 must agree.
   int groups = 0;
   const int* m_block_group = nullptr;
-  // Stream-K tail (see tn_schedule): 0 = where the last wave would leave many workers idle, 1 =
-  // always (tests), -1 = never. It needs a workspace (kTnStreamKWorkspaceBytes, its first
+  // Split tail (see tn_schedule): 0 = where the last wave would leave workers idle, 1 = always
+  // (tests), -1 = never. It needs a workspace (kTnStreamKWorkspaceBytes, its first
   // kTnStreamKTicketBytes zeroed before the first launch; launches keep them zero); without one the
   // launch is data-parallel.
   int stream_k = 0;
@@ -62,21 +62,26 @@ struct Problem {
   size_t sk_workspace_bytes = 0;
 };
 
-// Stream-K workspace: tickets first (zero between launches), then two fp32 slots of one CTA's
-// 128 x 256 accumulator per CTA of every worker (148 one-CTA workers or 74 pairs on a B200).
+// Split-tail workspace: tickets first (zero between launches), then one fp32 slot of one CTA's
+// 128 x 256 accumulator per CTA of every tail piece (up to 4 pieces for each of 148 one-CTA workers
+// or 74 pairs on a B200).
 inline constexpr size_t kTnStreamKTicketBytes = 64 * 1024;
-inline constexpr size_t kTnStreamKSlotCtas = 148;
-inline constexpr size_t kTnStreamKWorkspaceBytes = kTnStreamKTicketBytes + 2 * kTnStreamKSlotCtas * 128 * 256 * 4;
+inline constexpr size_t kTnStreamKSlotCtas = 4 * 148;
+inline constexpr size_t kTnStreamKWorkspaceBytes = kTnStreamKTicketBytes + kTnStreamKSlotCtas * 128 * 256 * 4;
 
-// How a launch deals its tiles. Data-parallel, the persistent workers take tiles t, t + W, ...; when
-// the tile count leaves the last wave short (fewer than 90 % of the W x waves tile slots used, which
-// N-sharding produces: 8192 x 1024 shards of 256 x 256 tiles are 128 tiles on 74 CTA pairs), the
-// last full wave and the remainder (W + tiles mod W tiles, or all tiles below 2 W) are split along K
-// instead, W equal runs of (tile, K-block) units, so every worker finishes at the same time.
+// How a launch deals its tiles. The persistent workers take whole tiles t, t + W, ...; when that
+// leaves the last wave short (R = tiles mod W of W workers busy, as N-sharding does: an 8192 x 2048
+// shard of 256 x 256 tiles is 256 tiles on 74 CTA pairs, R = 34), the R tail tiles are each cut
+// into s equal K-ranges (s = 2..4, at most one per K-block) and the R s pieces dealt round-robin in
+// range-major order, before the whole tiles: the tail then takes ceil(R s / W) / s of a wave plus the
+// traffic of its partial sums instead of one wave. s is the one that minimises that, used when it
+// saves at least a tenth of a wave (R = 34, W = 74, K 8192: s = 2; R = 54: no split, the four
+// ranges it would need cost more in partial sums than the quarter wave they save); stream_k = 1
+// always splits (s >= 2) where there is a K to split.
 struct TnSchedule {
   int tiles = 0;
   int workers = 0;
-  int sk_tiles = 0;
+  int sk_tiles = 0, sk_split = 1;
   size_t ticket_bytes = 0, slot_bytes = 0;
 };
 
@@ -92,26 +97,38 @@ TnSchedule tn_schedule(Problem const& pr, int max_workers) {
   s.workers = std::min(s.tiles, cap);
   if (pr.stream_k < 0 || cap <= 0) return s;
   const int W = cap, T = s.tiles;
-  const int tail = T < 2 * W ? T : W + T % W;
-  int sk = 0;
-  if (pr.stream_k > 0) {
-    sk = tail;
-  } else if (T > W && T % W != 0) {
-    const long long waves = (T + W - 1) / W;
-    if (double(T) < 0.9 * double(waves) * double(W)) sk = tail;
-  }
-  if (sk == 0) return s;
-  // Every worker needs at least one unit of the split region (the epilogue counts each worker from
-  // the first to the last contributor of a tile): with fewer units than workers, fewer workers.
+  int R = T % W;
+  if (R == 0 && pr.stream_k > 0) R = W;  // forced: split the last full wave
+  if (R == 0) return s;
   const long long pack = Cfg::kFp4 ? 2 : 1;
   const long long k_blocks = (pr.k / pack + Cfg::kBlockK - 1) / Cfg::kBlockK;
-  const int workers = sk == T ? int(std::min<long long>(W, (long long)sk * k_blocks)) : W;
-  const size_t tickets = size_t(sk) * Cfg::kCtaGroup * Cfg::kEpiWarps * sizeof(int);
-  const size_t slots = 2ull * workers * Cfg::kCtaGroup * 128 * Cfg::kTileN * sizeof(float);
-  if (workers <= 0 || tickets > kTnStreamKTicketBytes || kTnStreamKTicketBytes + slots > kTnStreamKWorkspaceBytes)
-    return s;
-  s.workers = workers;
-  s.sk_tiles = sk;
+  // The tail's time in waves of whole tiles, for s K-ranges per tile: ceil(R s / W) / s of MMA
+  // work, plus the fp32 partial sums (written once and read once, 2 x R s CtaGroup 128 BlockN x 4
+  // bytes, at ~6 TB/s) over one tile's MMA time at the power-capped ~1.4 GHz. Measured on B200
+  // (8192 x 8192 bf16 A, 256 x 256 tiles on 74 pairs, K 8192): R 34 x 2 ranges 139.6 us vs 155.5
+  // whole (the model: 0.63 of a wave); R 54 x 4 ranges 88 us vs 83 whole (the model: 1.15).
+  const double tensor_flop_per_clk = sizeof(typename Cfg::in_type) == 2 ? 8192.0 : Cfg::kFp4 ? 32768.0 : 16384.0;
+  const double tile_s = 2.0 * Cfg::kTileM * Cfg::kTileN * double(k_blocks * Cfg::kBlockK * pack) /
+                        (tensor_flop_per_clk * Cfg::kCtaGroup * 1.4e9);
+  int best = 1;
+  double best_cost = 1.0;
+  for (int sp = 2; sp <= 4 && sp <= k_blocks; ++sp) {
+    if (size_t(R) * sp * Cfg::kCtaGroup > kTnStreamKSlotCtas) break;
+    const double fixup_s = 2.0 * R * sp * Cfg::kCtaGroup * 128.0 * Cfg::kTileN * 4.0 / 6.0e12;
+    const double cost = double((R * sp + W - 1) / W) / sp + fixup_s / tile_s;
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = sp;
+    }
+  }
+  if (pr.stream_k > 0 && best == 1 && k_blocks >= 2 && size_t(R) * 2 * Cfg::kCtaGroup <= kTnStreamKSlotCtas) best = 2;
+  if (best == 1 || (pr.stream_k == 0 && best_cost > 0.9)) return s;
+  const size_t tickets = size_t(R) * Cfg::kCtaGroup * Cfg::kEpiWarps * sizeof(int);
+  const size_t slots = size_t(R) * best * Cfg::kCtaGroup * 128 * Cfg::kTileN * sizeof(float);
+  if (tickets > kTnStreamKTicketBytes || kTnStreamKTicketBytes + slots > kTnStreamKWorkspaceBytes) return s;
+  s.workers = T > W ? W : std::min(W, R * best);
+  s.sk_tiles = R;
+  s.sk_split = best;
   s.ticket_bytes = tickets;
   s.slot_bytes = slots;
   return s;
@@ -317,6 +334,7 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   }
   const int workers = sch.workers;
   a.sk_tiles = sch.sk_tiles;
+  a.sk_split = sch.sk_split;
   a.sk_tickets = sch.sk_tiles > 0 ? static_cast<int*>(pr.sk_workspace) : nullptr;
   a.sk_slots = sch.sk_tiles > 0 ? reinterpret_cast<float*>(static_cast<char*>(pr.sk_workspace) + kTnStreamKTicketBytes)
                                 : nullptr;

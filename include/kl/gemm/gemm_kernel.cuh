@@ -185,55 +185,46 @@ struct TnArgs {
   int c_reduce;                 // 0: C = result; 1: C += result (fp32 C: TMA reducing stores; 16-bit C: read, add, store)
   const int* m_block_group;     // m-grouped GEMM: B matrix of each 128-row block of A / C (-1 = padding)
   int sfb_group_blocks;         // m-grouped block-scaled: 128-row scale blocks of each group's B
-  // Stream-K tail: the last `sk_tiles` tiles (in tile order) are not dealt whole to the workers but
-  // split along K, each worker taking an equal run of (tile, K-block) units. A tile split between
-  // workers is summed through fp32 slots (two per worker: the tile its run starts in and the one it
-  // ends in) and a ticket per (tile, CTA of the pair, epilogue warp); the last warp to arrive adds
-  // the slots in worker order and stores C. 0 = every tile whole (data-parallel).
+  // Split tail: when the tile count leaves the last wave short, its `sk_tiles` tiles (the last in
+  // tile order) are each cut into `sk_split` equal K-ranges, dealt round-robin like whole tiles in
+  // range-major order, so the workers of one wave read the same K-range of neighbouring tiles and
+  // keep the L2 reuse of the data-parallel waves. Each range's fp32 partial sum goes to its own slot;
+  // a ticket per (tile, CTA of the pair, epilogue warp) counts them in, and the warp that arrives
+  // last adds the slots in range order and stores C. 0 tail tiles = every tile whole.
   int sk_tiles;
+  int sk_split;
   int* sk_tickets;              // [sk_tiles * CtaGroup * kEpiWarps], zero between launches
-  float* sk_slots;              // [2 * workers * CtaGroup][128 * BlockN]
+  float* sk_slots;              // [sk_tiles * sk_split * CtaGroup][128 * BlockN]
 };
 
-// The stream-K run of worker w over U units split between W workers: [w U / W, (w + 1) U / W).
-KL_HOST_DEVICE constexpr long long sk_unit_start(int w, long long units, int workers) {
-  return (long long)w * units / workers;
-}
-// The worker whose run holds unit u.
-KL_HOST_DEVICE constexpr int sk_worker_of_unit(long long u, long long units, int workers) {
-  return int(((u + 1) * workers + units - 1) / units) - 1;
-}
-
-// One piece of work: K-blocks [kb0, kb1) of tile t.
+// One piece of work: K-blocks [kb0, kb1) of tile t; q = its K-range (0 for a whole tile).
 struct TilePiece {
-  int t, kb0, kb1;
+  int t, kb0, kb1, q;
 };
 
-// The pieces one worker processes, in order: its data-parallel tiles (every num_workers-th tile
-// of the first num_tiles - sk_tiles, whole K), then its run of the stream-K region cut at tile
-// boundaries. Producer, MMA issuer and epilogue walk the same sequence.
+// The pieces one worker processes, in order: first tail pieces p = worker + j W of the sk_tiles *
+// sk_split (piece p is K-range p / sk_tiles of tail tile p % sk_tiles, the tail being the last
+// sk_tiles tiles), then tiles t = worker + i W of the first num_tiles - sk_tiles, whole. Split tiles
+// go first so that their slot traffic and final sums overlap the whole tiles' MMAs instead of
+// trailing the last wave. Producer, MMA issuer and epilogue walk the same sequence.
 struct WorkSeq {
-  int workers, dp_tiles, k_blocks, t_dp;
-  long long u, u_end;
-  KL_HOST_DEVICE WorkSeq(int worker, int num_workers, int num_tiles, int sk_tiles, int k_blocks_)
-      : workers(num_workers), dp_tiles(num_tiles - sk_tiles), k_blocks(k_blocks_), t_dp(worker) {
-    const long long units = (long long)sk_tiles * k_blocks_;
-    u = sk_tiles > 0 ? sk_unit_start(worker, units, num_workers) : 0;
-    u_end = sk_tiles > 0 ? sk_unit_start(worker + 1, units, num_workers) : 0;
-  }
+  int workers, dp_tiles, tail, split, k_blocks, t_dp, p;
+  KL_HOST_DEVICE WorkSeq(int worker, int num_workers, int num_tiles, int sk_tiles, int sk_split, int k_blocks_)
+      : workers(num_workers), dp_tiles(num_tiles - sk_tiles), tail(sk_tiles), split(sk_split > 0 ? sk_split : 1),
+        k_blocks(k_blocks_), t_dp(worker), p(worker) {}
   KL_HOST_DEVICE bool next(TilePiece& w) {
+    if (p < tail * split) {
+      const int q = p / tail, r = p - q * tail;
+      w = {dp_tiles + r, int((long long)q * k_blocks / split), int((long long)(q + 1) * k_blocks / split), q};
+      p += workers;
+      return true;
+    }
     if (t_dp < dp_tiles) {
-      w = {t_dp, 0, k_blocks};
+      w = {t_dp, 0, k_blocks, 0};
       t_dp += workers;
       return true;
     }
-    if (u >= u_end) return false;
-    const long long tu = u / k_blocks;
-    w.t = dp_tiles + int(tu);
-    w.kb0 = int(u - tu * k_blocks);
-    w.kb1 = (u_end - u) < (k_blocks - w.kb0) ? w.kb0 + int(u_end - u) : k_blocks;
-    u += w.kb1 - w.kb0;
-    return true;
+    return false;
   }
 };
 
@@ -468,7 +459,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         for (int j = 0; j < pf; ++j) prefetch_unit(worker, j);
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      WorkSeq seq(worker, num_workers, num_tiles, args.sk_tiles, args.k_blocks);
+      WorkSeq seq(worker, num_workers, num_tiles, args.sk_tiles, args.sk_split, args.k_blocks);
       TilePiece pc;
       while (ok && seq.next(pc)) {
         const int t = pc.t;
@@ -551,7 +542,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
       uint32_t stage = 0, phase = 0;
       uint32_t iter = 0;
       bool ok = true;
-      WorkSeq seq(worker, num_workers, num_tiles, args.sk_tiles, args.k_blocks);
+      WorkSeq seq(worker, num_workers, num_tiles, args.sk_tiles, args.sk_split, args.k_blocks);
       TilePiece pc;
       for (; ok && seq.next(pc); ++iter) {
         const int t = pc.t;
@@ -769,46 +760,39 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
       if constexpr (Cfg::kChunkCols == 64) tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
     };
 
-    // Stream-K tail. A split tile's partial sums go to the contributing worker's slot as fp32
-    // (element (r, c) of the CTA's 128 x BlockN block at ((c / 32) * 128 + r) * 32 + c % 32: each
-    // warp writes and reads whole 4-KB runs), then each epilogue warp counts in on its own ticket;
-    // the warp that arrives last adds the slots in worker order, so the sum does not depend on
-    // arrival order, and stores C. Nothing waits on another CTA.
+    // Split tail: each K-range of a tail tile leaves its fp32 partial sum in its own slot (the CTA's
+    // 128 x BlockN block), then each epilogue warp counts in on its own ticket; the warp that
+    // arrives last adds the slots in K-range order, so the sum does not depend on arrival order, and
+    // stores C. Nothing waits on another CTA.
     const int dp_tiles = num_tiles - args.sk_tiles;
-    const long long sk_units = (long long)args.sk_tiles * args.k_blocks;
     const int erow = quarter * 32 + lane;  // this thread's row of the CTA's 128
-    auto slot_of = [&](int w, int t) -> float* {
-      const int first_t = dp_tiles + int(sk_unit_start(w, sk_units, num_workers) / args.k_blocks);
-      const long long s = 2LL * w + (t == first_t ? 0 : 1);
-      return args.sk_slots + (s * CG + cta_rank) * (128LL * Cfg::kTileN);
+    auto slot_of = [&](int q, int r) -> float* {  // K-range q of tail tile r
+      const long long piece = (long long)q * args.sk_tiles + r;
+      return args.sk_slots + (piece * CG + cta_rank) * (128LL * Cfg::kTileN);
     };
+    // Element (r, c) of a slot at ((c / 4) * 128 + r) * 4 + c % 4: one 16-byte store or load per
+    // thread covers four columns of its row, and a warp's 32 rows are 512 contiguous bytes.
     auto slot_store = [&](float* slot, int tcol_rel, const uint32_t* v) {
+      float4* dst = reinterpret_cast<float4*>(slot) + (long long)(tcol_rel >> 2) * 128 + erow;
 #pragma unroll
-      for (int g = 0; g < Cfg::kChunkCols / 32; ++g) {
-        float4* dst = reinterpret_cast<float4*>(slot + ((long long)((tcol_rel >> 5) + g) * 128 + erow) * 32);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          __stcg(dst + j, make_float4(__uint_as_float(v[32 * g + 4 * j]), __uint_as_float(v[32 * g + 4 * j + 1]),
-                                      __uint_as_float(v[32 * g + 4 * j + 2]), __uint_as_float(v[32 * g + 4 * j + 3])));
-      }
+      for (int j = 0; j < Cfg::kChunkCols / 4; ++j)
+        __stcg(dst + 128 * j, make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                          __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])));
     };
     auto slot_add = [&](const float* slot, int tcol_rel, float* sum) {
+      const float4* src = reinterpret_cast<const float4*>(slot) + (long long)(tcol_rel >> 2) * 128 + erow;
 #pragma unroll
-      for (int g = 0; g < Cfg::kChunkCols / 32; ++g) {
-        const float4* src = reinterpret_cast<const float4*>(slot + ((long long)((tcol_rel >> 5) + g) * 128 + erow) * 32);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 x = __ldcg(src + j);  // L2: written by other SMs during this launch
-          sum[32 * g + 4 * j] += x.x;
-          sum[32 * g + 4 * j + 1] += x.y;
-          sum[32 * g + 4 * j + 2] += x.z;
-          sum[32 * g + 4 * j + 3] += x.w;
-        }
+      for (int j = 0; j < Cfg::kChunkCols / 4; ++j) {
+        const float4 x = __ldcg(src + 128 * j);  // L2: written by other SMs during this launch
+        sum[4 * j] += x.x;
+        sum[4 * j + 1] += x.y;
+        sum[4 * j + 2] += x.z;
+        sum[4 * j + 3] += x.w;
       }
     };
 
     uint32_t iter = 0;
-    WorkSeq seq(worker, num_workers, num_tiles, args.sk_tiles, args.k_blocks);
+    WorkSeq seq(worker, num_workers, num_tiles, args.sk_tiles, args.sk_split, args.k_blocks);
     TilePiece pc;
     for (; seq.next(pc); ++iter) {
       const int t = pc.t;
@@ -824,16 +808,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
       row0 = tm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM + quarter * 32;
       const int col0 = tn * Cfg::kTileN + wcol;
       const uint32_t tcol = tmem_base + lane_base + acc * Cfg::kAccCols + uint32_t(wcol);
-      int w_first = worker, w_last = worker;  // workers that contribute to tile t
-      if (t >= dp_tiles) {
-        const long long tu0 = (long long)(t - dp_tiles) * args.k_blocks;
-        w_first = sk_worker_of_unit(tu0, sk_units, num_workers);
-        w_last = sk_worker_of_unit(tu0 + args.k_blocks - 1, sk_units, num_workers);
-      }
-      if (w_first != w_last) {
-        // A split tile: this worker's partial sum into its slot, then the ticket.
-        // (Chunk by chunk in every config: a split tile is rare, registers are not.)
-        float* own = slot_of(worker, t);
+      const bool split = t >= dp_tiles && args.sk_split > 1;
+      if (split) {
+        // A K-range of a tail tile: its partial sum into its slot, then the ticket.
+        // (Chunk by chunk in every config: split tiles are few, registers are not.)
+        const int r = t - dp_tiles;
+        float* own = slot_of(pc.q, r);
 #pragma unroll 1
         for (int c = 0; c < Cfg::kChunks; ++c) {
           uint32_t v[Cfg::kChunkCols];
@@ -846,8 +826,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         __syncwarp();
         int last = 0;
         if (lane == 0) {
-          int* ticket = args.sk_tickets + ((long long)(t - dp_tiles) * CG + cta_rank) * Cfg::kEpiWarps + ew;
-          last = atomicAdd(ticket, 1) == w_last - w_first;
+          int* ticket = args.sk_tickets + ((long long)r * CG + cta_rank) * Cfg::kEpiWarps + ew;
+          last = atomicAdd(ticket, 1) == args.sk_split - 1;
           if (last) {
             atomicExch(ticket, 0);  // ready for the next launch
             __threadfence();        // the other contributors' slots before the reads below
@@ -863,7 +843,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
 #pragma unroll
             for (int e = 0; e < Cfg::kChunkCols; ++e) sum[e] = 0.0f;
 #pragma unroll 1
-            for (int w = w_first; w <= w_last; ++w) slot_add(slot_of(w, t), wcol + c * Cfg::kChunkCols, sum);
+            for (int q = 0; q < args.sk_split; ++q) slot_add(slot_of(q, r), wcol + c * Cfg::kChunkCols, sum);
             emit_chunk(v, col0 + c * Cfg::kChunkCols);
           }
         }

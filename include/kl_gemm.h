@@ -119,13 +119,12 @@ typedef struct kl_gemm_desc {
    * the pair from 256), K-major operands, 128-byte swizzle, batch 1. fp6 (KL_E3M2 / KL_E2M3): K,
    * lda, ldb and stride_b multiples of 128 elements (96 bytes), A and B 32-byte aligned. */
   int32_t block_scale;
-  /* Tile kernels (KL_ALGO_1CTA / 2CTA, and AUTO's choice of them): 0 = split the last wave along K
-   * across every worker (stream-K) where dealing whole tiles would leave many workers idle at the end
-   * (fewer than 90 % of the tile slots used, as in N-sharded GEMMs: 128 tiles of 256 x 256 on 74 CTA
-   * pairs); 1 = always split the tail; -1 = never. Split tiles are summed through a per-stream
-   * library workspace (37 MiB, allocated on first use, never outside a stream capture; a capture
-   * that finds none runs data-parallel) in a fixed order: results are deterministic but can differ
-   * in the last bits from the data-parallel schedule. */
+  /* Tile kernels (KL_ALGO_1CTA / 2CTA, and AUTO's choice of them): 0 = where dealing whole tiles
+   * leaves the last wave short (N-sharded GEMMs: 128 tiles of 256 x 256 on 74 CTA pairs), cut each
+   * tile of that wave into 2-4 K-ranges spread over every worker; 1 = always cut the last wave; -1 =
+   * never. The ranges are summed through a per-stream library workspace (78 MiB, allocated on first
+   * use, never inside a stream capture: a capture that finds none runs whole tiles) in range order:
+   * results are deterministic but can differ in the last bits from whole-tile results. */
   int32_t stream_k;
   const void* sfa;
   const void* sfb;

@@ -249,8 +249,8 @@ def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, gr
     pack_block_scales) make it a block-scaled GEMM: one UE8M0 scale per 32 K-elements of each row
     (MX, scale_vec 32) or one UE4M3 scale per 16 (NVFP4, scale_vec 16, fp4 operands). ab_type =
     KL_E3M2 / KL_E2M3 passes uint8 `a` / `b` as packed fp6 ([rows, 3 K / 4] bytes). stream_k: the
-    tile kernels' stream-K tail, 0 = where the last wave would leave workers idle, 1 = always,
-    -1 = never."""
+    tile kernels' split tail (the last wave's tiles cut into K-ranges), 0 = where the last wave
+    would leave workers idle, 1 = always, -1 = never."""
     for name, t in (("a", a), ("b", b), ("c", c)):
         if t.dim() not in (2, 3) or t.stride(-1) != 1:
             raise ValueError(f"{name} must be a 2-D or 3-D tensor with a contiguous last dimension")

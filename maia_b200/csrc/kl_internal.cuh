@@ -26,10 +26,10 @@ int choose_algo(kl_gemm_desc const& d);
 kl_status skinny_workspace_size(kl_gemm_desc const& d, size_t* bytes);
 kl_status run_skinny(kl_gemm_desc const& d, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 // After a timed-out kernel the library workspace's tickets may be mid-count: re-zero before reuse.
-// (Marks the skinny workspace and every stream-K tile workspace of the device.)
+// (Marks the skinny workspace and every split-tail workspace of the device.)
 void mark_workspace_dirty(int device);
 
-// Stream-K workspace of the tile kernels for `stream` on the current device (kl_tile_ws.cu):
+// Split-tail workspace of the tile kernels for `stream` on the current device (kl_tile_ws.cu):
 // kl::gemm::kTnStreamKWorkspaceBytes with zeroed tickets, or nullptr where none can be had without
 // allocating inside a stream capture (the launch then deals whole tiles).
 kl_status tile_stream_k_workspace(cudaStream_t stream, void** out);

@@ -13,7 +13,7 @@
 namespace kl::capi {
 
 // Queue the tile kernel `Cfg` for `pr`, reporting into the device status word.
-// A launch whose schedule has a stream-K tail gets the stream's workspace (unless the caller
+// A launch whose schedule splits its tail gets the stream's workspace (unless the caller
 // brought one); without it the launch deals whole tiles.
 template <class Cfg>
 kl_status run_cfg(kl::gemm::Problem const& pr0, cudaStream_t stream, kl::gemm::LaunchInfo* info) {

@@ -1,7 +1,7 @@
-// Stream-K workspaces of the tile kernels: one fixed-size buffer per (device, stream), allocated on
+// Split-tail workspaces of the tile kernels: one fixed-size buffer per (device, stream), allocated on
 // first use and never freed or moved while the process runs, so a CUDA graph that captured a launch
 // keeps a valid pointer. Its ticket area is zeroed once and stays zero between launches (the last
-// contributor to each split tile resets its ticket); after a timed-out launch it is re-zeroed on the
+// K-range of each split tile to arrive resets its ticket); after a timed-out launch it is re-zeroed on the
 // stream before the next use.
 
 #include <cuda_runtime.h>
@@ -39,19 +39,19 @@ kl_status tile_stream_k_workspace(cudaStream_t stream, void** out) {
   std::lock_guard<std::mutex> lock(g_tile_ws_mutex);
   TileWorkspace& w = g_tile_ws[{dev, stream}];
   if (w.ptr == nullptr) {
-    if (capturing) return KL_OK;  // no allocation inside a capture: this launch stays data-parallel
+    if (capturing) return KL_OK;  // no allocation inside a capture: this launch deals whole tiles
     e = cudaMalloc(&w.ptr, kl::gemm::kTnStreamKWorkspaceBytes);
     if (e != cudaSuccess) {
       cudaGetLastError();
       w.ptr = nullptr;
-      return KL_OK;  // out of memory: data-parallel
+      return KL_OK;  // out of memory: whole tiles
     }
     w.dirty = true;
   }
   if (w.dirty) {
     if (capturing) return KL_OK;
     e = cudaMemsetAsync(w.ptr, 0, kl::gemm::kTnStreamKTicketBytes, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(stream-K tickets)");
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(split-tail tickets)");
     w.dirty = false;
   }
   *out = w.ptr;

@@ -1,5 +1,5 @@
-// Host checks of the tile kernels' work schedule (kl::gemm::WorkSeq, tn_schedule, the stream-K
-// contributor and slot bookkeeping the epilogue uses), over many (tiles, workers, K-blocks).
+// Host checks of the tile kernels' work schedule (kl::gemm::WorkSeq and tn_schedule's split tail),
+// over many (tiles, workers, K-blocks, K-ranges per tail tile).
 // Prints "N failures"; exit status 0 when there are none.
 
 #include <algorithm>
@@ -25,48 +25,33 @@ static int failures = 0;
     }                                      \
   } while (0)
 
-// What the epilogue computes for (worker w, tile t) in the stream-K region: the contributors and
-// w's slot.
-static void check_case(int tiles, int sk_tiles, int W, int KB) {
+// The pieces every worker walks, against what the kernel relies on.
+static void check_case(int tiles, int sk_tiles, int split, int W, int KB) {
   const int dp = tiles - sk_tiles;
-  const long long U = (long long)sk_tiles * KB;
   std::vector<std::vector<int>> cover(tiles, std::vector<int>(KB, 0));
-  std::map<int, std::set<int>> contributors;  // tile -> workers with a piece of it
-  std::set<long long> slots_used;
+  std::map<int, std::set<int>> ranges;  // tail tile -> its K-ranges seen
   for (int w = 0; w < W; ++w) {
-    WorkSeq seq(w, W, tiles, sk_tiles, KB);
+    WorkSeq seq(w, W, tiles, sk_tiles, split, KB);
     TilePiece pc;
-    int prev_t = -1;
-    bool in_sk = false;
-    std::set<long long> my_slots;
+    bool in_whole = false;
     while (seq.next(pc)) {
       CHECK(pc.t >= 0 && pc.t < tiles && pc.kb0 >= 0 && pc.kb0 < pc.kb1 && pc.kb1 <= KB, "t %d [%d,%d)", pc.t, pc.kb0, pc.kb1);
       if (!(pc.t >= 0 && pc.t < tiles)) return;
-      CHECK(pc.t > prev_t, "pieces in tile order (w %d t %d after %d)", w, pc.t, prev_t);
       if (pc.t < dp) {
-        CHECK(!in_sk && pc.t % W == w && pc.kb0 == 0 && pc.kb1 == KB, "data-parallel tile %d of w %d", pc.t, w);
+        in_whole = true;
+        CHECK(pc.t % W == w && pc.kb0 == 0 && pc.kb1 == KB && pc.q == 0, "whole tile %d of w %d", pc.t, w);
       } else {
-        in_sk = true;
-        contributors[pc.t].insert(w);
+        CHECK(!in_whole, "tail piece of tile %d after a whole tile (w %d)", pc.t, w);
+        CHECK(pc.q >= 0 && pc.q < split, "range %d of %d", pc.q, split);
+        CHECK(ranges[pc.t].insert(pc.q).second, "tile %d range %d twice", pc.t, pc.q);
+        if (split == 1) CHECK(pc.kb0 == 0 && pc.kb1 == KB, "unsplit tail tile %d", pc.t);
       }
       for (int kb = pc.kb0; kb < pc.kb1; ++kb) ++cover[pc.t][kb];
-      prev_t = pc.t;
     }
   }
   for (int t = 0; t < tiles; ++t)
     for (int kb = 0; kb < KB; ++kb) CHECK(cover[t][kb] == 1, "unit (%d, %d) covered %d times", t, kb, cover[t][kb]);
-  for (auto& [t, ws] : contributors) {
-    const long long tu0 = (long long)(t - dp) * KB;
-    const int wf = sk_worker_of_unit(tu0, U, W), wl = sk_worker_of_unit(tu0 + KB - 1, U, W);
-    CHECK(wf == *ws.begin() && wl == *ws.rbegin() && int(ws.size()) == wl - wf + 1,
-          "tile %d: contributors [%d, %d] vs %d..%d", t, wf, wl, *ws.begin(), *ws.rbegin());
-    if (wf == wl) continue;
-    for (int w : ws) {  // the slot the epilogue's slot_of picks
-      const int first_t = dp + int(sk_unit_start(w, U, W) / KB);
-      const long long s = 2LL * w + (t == first_t ? 0 : 1);
-      CHECK(slots_used.insert(s).second, "slot %lld used twice (tile %d, worker %d)", s, t, w);
-    }
-  }
+  for (int t = dp; t < tiles; ++t) CHECK(int(ranges[t].size()) == split, "tail tile %d has %d ranges", t, int(ranges[t].size()));
 }
 
 template <int CG>
@@ -76,47 +61,60 @@ int main() {
   int cases = 0;
   for (int W : {1, 2, 3, 7, 74, 148})
     for (int tiles : {1, 2, 5, 73, 74, 75, 128, 147, 148, 149, 256, 300})
-      for (int KB : {1, 2, 3, 16, 128}) {
-        const int tail = tiles < 2 * W ? tiles : W + tiles % W;
-        // tn_schedule's worker count for the split region: at least one unit per worker.
-        const int wk = tail == tiles ? std::min(W, tail * KB) : W;
-        check_case(tiles, 0, W, KB);
-        check_case(tiles, tail, wk, KB);
-        ++cases;
-      }
+      for (int KB : {1, 2, 3, 16, 128})
+        for (int split : {1, 2, 3, 4}) {
+          if (split > KB) continue;
+          const int R = tiles % W == 0 ? W : tiles % W;
+          const int workers = tiles > W ? W : std::min(W, R * split);
+          check_case(tiles, 0, 1, W, KB);
+          check_case(tiles, R, split, workers, KB);
+          ++cases;
+        }
   // Decisions on the N-sharded 8192^3 bf16 GEMM (CTA pair, 256 x 256 tiles, 74 pairs).
   Problem pr;
   pr.k = 8192;
   pr.m = 8192;
-  for (auto [n, want] : std::vector<std::pair<int, int>>{{8192, 0}, {4096, 0}, {2048, 108}, {1024, 128}}) {
-    pr.n = n;
+  struct Want { int n, tail, split; };
+  for (Want c : {Want{8192, 0, 1}, Want{4096, 0, 1}, Want{2048, 34, 2}, Want{1024, 0, 1}}) {
+    pr.n = c.n;
     const TnSchedule s = tn_schedule<Pair<2>>(pr, 74);
-    CHECK(s.sk_tiles == want, "n %d: sk_tiles %d, want %d", n, s.sk_tiles, want);
+    CHECK(s.sk_tiles == c.tail && s.sk_split == c.split, "n %d: tail %d x %d, want %d x %d", c.n, s.sk_tiles, s.sk_split,
+          c.tail, c.split);
     CHECK(s.sk_tiles == 0 || (s.workers == 74 && s.ticket_bytes <= kTnStreamKTicketBytes &&
                               kTnStreamKTicketBytes + s.slot_bytes <= kTnStreamKWorkspaceBytes),
-          "n %d: workspace", n);
+          "n %d: workspace", c.n);
   }
-  pr.n = 1024;
+  pr.n = 2048;
   pr.stream_k = -1;
   CHECK(tn_schedule<Pair<2>>(pr, 74).sk_tiles == 0, "stream_k = -1 turns the tail off");
+  pr.n = 1024;
+  pr.stream_k = 1;
+  CHECK(tn_schedule<Pair<2>>(pr, 74).sk_tiles == 54 && tn_schedule<Pair<2>>(pr, 74).sk_split == 2,
+        "forced: the 54-tile tail in two ranges (no s pays, so the smallest)");
   pr.stream_k = 1;
   pr.n = 8192;
-  CHECK(tn_schedule<Pair<2>>(pr, 74).sk_tiles == 74 + 1024 % 74, "stream_k = 1 splits the tail");
+  CHECK(tn_schedule<Pair<2>>(pr, 74).sk_tiles == 1024 % 74 && tn_schedule<Pair<2>>(pr, 74).sk_split >= 2,
+        "stream_k = 1 splits the tail");
   pr.m = 256;
   pr.n = 512;
-  CHECK(tn_schedule<Pair<2>>(pr, 74).sk_tiles == 2 && tn_schedule<Pair<2>>(pr, 74).workers == 74,
-        "small problems split over every worker");
+  CHECK(tn_schedule<Pair<2>>(pr, 74).sk_tiles == 2 && tn_schedule<Pair<2>>(pr, 74).sk_split == 4 &&
+            tn_schedule<Pair<2>>(pr, 74).workers == 8,
+        "two tiles on many workers: four ranges each, eight workers");
   pr.max_ctas = 6;
   CHECK(tn_schedule<Pair<2>>(pr, 74).workers == 3, "max_ctas caps the workers");
   pr.max_ctas = 0;
-  pr.k = 128;  // 2 tiles x 2 K-blocks of 64: four units, so four workers
-  CHECK(tn_schedule<Pair<2>>(pr, 74).workers == 4, "no more workers than units: %d", tn_schedule<Pair<2>>(pr, 74).workers);
+  pr.k = 128;  // two K-blocks of 64: at most two ranges
+  CHECK(tn_schedule<Pair<2>>(pr, 74).sk_split == 2, "no more ranges than K-blocks: %d", tn_schedule<Pair<2>>(pr, 74).sk_split);
+  pr.k = 64;
+  CHECK(tn_schedule<Pair<2>>(pr, 74).sk_tiles == 0, "one K-block: nothing to split");
   pr.k = 8192;
   pr.stream_k = 0;
-  pr.max_ctas = 0;
   pr.m = 8192;
   pr.n = 1024;
-  CHECK(tn_schedule<Pair<1>>(pr, 148).sk_tiles == 256, "one-CTA tiles: 256 on 148 workers (86 %%) all split");
+  CHECK(tn_schedule<Pair<1>>(pr, 148).sk_tiles == 0, "one-CTA tiles: 256 on 148 workers, the four ranges cost more");
+  pr.n = 2048;
+  CHECK(tn_schedule<Pair<1>>(pr, 148).sk_tiles == 68 && tn_schedule<Pair<1>>(pr, 148).sk_split == 2,
+        "one-CTA tiles: 512 on 148 workers, the 68 of the last wave in two ranges");
   std::printf("%d cases, %d failures\n", cases, failures);
   return failures == 0 ? 0 : 1;
 }

@@ -61,8 +61,8 @@ def test_cmake_consumer_builds_against_kl_target(tmp_path):
 
 def test_stream_k_schedule(tmp_path):
     """The tile kernels' work schedule on the host: every (tile, K-block) unit dealt exactly once,
-    data-parallel tiles before the stream-K run, contributors and slots as the epilogue computes
-    them, and tn_schedule's decisions on the N-sharded shapes (tests/native/test_stream_k_schedule.cu)."""
+    the split tail before the whole tiles, every K-range of a tail tile once and never empty, and
+    tn_schedule's decisions on the N-sharded shapes (tests/native/test_stream_k_schedule.cu)."""
     exe = tmp_path / "test_stream_k_schedule"
     cmd = [nvcc(), "-std=c++20", "--expt-relaxed-constexpr", "-gencode", "arch=compute_100a,code=sm_100a",
            "-I", str(ROOT / "include"), str(ROOT / "tests" / "native" / "test_stream_k_schedule.cu"), "-o", str(exe)]

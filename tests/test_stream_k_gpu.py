@@ -1,7 +1,7 @@
-"""The tile kernels' stream-K tail on the GPU, against the fp64 CPU oracle.
+"""The tile kernels' split tail on the GPU, against the fp64 CPU oracle.
 
-On small problems the tail is forced (stream_k = 1) and max_ctas leaves few workers, so most tiles
-are split between workers and summed through the fp32 slots: every element path of the epilogue
+On small problems the split is forced (stream_k = 1) and max_ctas leaves few workers, so the last
+wave's tiles are cut into K-ranges on several workers and summed through the fp32 slots: every element path of the epilogue
 (bf16 / f32 C, fp8 scales, MX block scales with the one-accumulator epilogue, C += result,
 batched and m-grouped problems, peer-less TMA stores) goes through the split-tile reduction.
 Tolerances as elsewhere: 1e-2 for 16-bit inputs, 5e-2 for fp8.
@@ -36,8 +36,8 @@ def test_forced_tail_matches_oracle(cuda, algo, out, shape, ctas):
 
 @ALGOS
 def test_tail_is_deterministic_and_close_to_data_parallel(cuda, algo):
-    """The same split, the same slot order: bit-identical from run to run; the data-parallel
-    schedule sums the K-blocks in another association, so it agrees to fp32 rounding only."""
+    """The same split, the same slot order: bit-identical from run to run; whole tiles sum the
+    K-blocks in another association, so they agree to fp32 rounding only."""
     a, b, _, _ = random_inputs(512, 768, 3072, "bf16", seed=3)
     runs = [run_kl(a, b, "bf16", "f32", cuda, algo, stream_k=1, max_ctas=10) for _ in range(3)]
     assert all(np.array_equal(r, runs[0]) for r in runs[1:])
@@ -47,16 +47,20 @@ def test_tail_is_deterministic_and_close_to_data_parallel(cuda, algo):
 
 @ALGOS
 def test_more_workers_than_units(cuda, algo):
-    """One tile of two K-blocks: two workers, not every SM (each worker needs a unit)."""
+    """One tile of two K-blocks: at most two K-ranges, on two workers."""
     a, b, _, _ = random_inputs(128, 256, 128, "bf16", seed=4)
     check(run_kl(a, b, "bf16", "bf16", cuda, algo, stream_k=1), a, b, 1.0, TOL16)
 
 
 def test_default_splits_a_short_last_wave(cuda):
-    """stream_k = 0 with 10 CTA pairs and 16 tiles (80 % of two waves): the tail is split."""
-    a, b, _, _ = random_inputs(1024, 1024, 2048, "bf16", seed=5)
-    c = run_kl(a, b, "bf16", "bf16", cuda, kl.ALGO_2CTA, max_ctas=20)
-    check(c, a, b, 1.0, TOL16)
+    """stream_k = 0 with 10 CTA pairs and 16 tiles (80 % of two waves), K 8192: the 6 tail tiles are
+    cut into 3 K-ranges (0.67 of a wave plus the partial sums, against 1). The default's bits equal
+    the forced split's (the same ranges) and differ from whole tiles (another association)."""
+    a, b, _, _ = random_inputs(1024, 1024, 8192, "bf16", seed=5)
+    auto = run_kl(a, b, "bf16", "f32", cuda, kl.ALGO_2CTA, max_ctas=20)
+    check(auto, a, b, 1.0, TOL16)
+    assert np.array_equal(auto, run_kl(a, b, "bf16", "f32", cuda, kl.ALGO_2CTA, max_ctas=20, stream_k=1))
+    assert not np.array_equal(auto, run_kl(a, b, "bf16", "f32", cuda, kl.ALGO_2CTA, max_ctas=20, stream_k=-1))
 
 
 @ALGOS
