@@ -392,7 +392,7 @@ def mx_pack_scales(scales, k: int, out=None, stream=None):
 
 
 def gemm_host(a_host, b_host, c_host, a_dev, b_dev, c_dev, *, alpha=1.0, scale_a=None, scale_b=None,
-              algo=ALGO_AUTO, chunks=0, sfa=None, sfb=None, scale_vec=32, ab_type=None, stream=None):
+              algo=ALGO_AUTO, chunks=0, sfa=None, sfb=None, scale_vec=32, ab_type=None, stream_k=0, stream=None):
     """c_host = alpha * a_host @ b_host.T with host (ideally pinned) tensors, through kl_gemm_host:
     the copies in and out overlap the GEMM. a_dev/b_dev/c_dev are device staging tensors of the
     same shapes; sfa/sfb: host MXFP8 scales in the blocked layout (staged by the library). Only
@@ -400,7 +400,7 @@ def gemm_host(a_host, b_host, c_host, a_dev, b_dev, c_dev, *, alpha=1.0, scale_a
     import torch
 
     d = gemm_desc(a_host, b_host, c_host, alpha, scale_a, scale_b, algo, sfa=sfa, sfb=sfb, scale_vec=scale_vec,
-                  ab_type=ab_type)
+                  ab_type=ab_type, stream_k=stream_k)
     s = stream if stream is not None else torch.cuda.current_stream(a_dev.device).cuda_stream
     check(lib().kl_gemm_host(ctypes.byref(d), ctypes.c_void_p(a_dev.data_ptr()), ctypes.c_void_p(b_dev.data_ptr()),
                              ctypes.c_void_p(c_dev.data_ptr()), int(chunks), ctypes.c_void_p(s)))

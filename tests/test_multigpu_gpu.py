@@ -35,12 +35,13 @@ try:
     for (m, n, k) in [(512, 1024, 768), (384, 1000, 520), (1024, 4096, 1024), (256, 2048 + 72, 640)]:
         a_bits, b_bits, _, _ = random_inputs(m, n, k, "bf16", seed=n + k)
         a, b = to_device(a_bits, "bf16", dev), to_device(b_bits, "bf16", dev)
-        ref = kl.gemm(a, b)                                   # whole problem on this GPU
+        # Whole tiles on both sides (stream_k = -1): a shard's tiles are then the full GEMM's tiles.
+        ref = kl.gemm(a, b, stream_k=-1)                      # whole problem on this GPU
         lo, hi = sharding.shard_range(n, world, rank, align=256)
         shared = sharding.SharedC(m, n, torch.bfloat16, dev, dist)
         shared.full.fill_(float("nan"))
         dist.barrier()
-        kl.gemm_gather(a, b[lo:hi], shared.full[:, lo:hi], shared.peer_ptrs(lo))
+        kl.gemm_gather(a, b[lo:hi], shared.full[:, lo:hi], shared.peer_ptrs(lo), stream_k=-1)
         dist.barrier()                                        # every rank's kernel has finished
         torch.cuda.synchronize()
         assert kl.read_status() == 0
