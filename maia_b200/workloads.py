@@ -71,7 +71,13 @@ C3NVF4 = Workload("c3nvf4_8192_nvfp4", 8192, 8192, 8192, "nvfp4", "bf16", "norma
 # C3's shape in MXFP6 (packed e2m3 elements, UE8M0 scales per 32; kind::mxf8f6f4 at the fp8 rate).
 C3MXF6 = Workload("c3mxf6_8192_mxfp6", 8192, 8192, 8192, "mxfp6", "bf16", "normal", 0.02, 0.02, 2)
 
-ALL = {w.name: w for w in (C1, C2, C3, C4, C4MX, C3MX, C3MXF4, C4MXF4, C3NVF4, C3MXF6, *C5.values())}
+# C5's decode shapes with MX-quantised weights and activations (block-scaled decode).
+C5MX = {m: Workload(f"c5mx_skinny_m{m}_mxfp8", m, 28672, 8192, "mxfp8", "bf16", "normal", 1.0, 0.02, 4) for m in (16, 64, 128)}
+C5MXF4 = {m: Workload(f"c5mxf4_skinny_m{m}_mxfp4", m, 28672, 8192, "mxfp4", "bf16", "normal", 1.0, 0.02, 4)
+          for m in (16, 64, 128)}
+
+ALL = {w.name: w for w in (C1, C2, C3, C4, C4MX, C3MX, C3MXF4, C4MXF4, C3NVF4, C3MXF6, *C5.values(), *C5MX.values(),
+                           *C5MXF4.values())}
 MX_ELEMENT = {"mxfp8": "e4m3", "mxfp6": "e2m3", "mxfp4": "e2m1"}  # element format of each MX workload dtype
 
 
@@ -188,15 +194,33 @@ def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
 E2M1_GRID = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])  # the e2m1 magnitudes, by code 0..7
 
 
+def minifloat_codes(x: np.ndarray, eb: int, mb: int) -> np.ndarray:
+    """Round float32 to a sign-magnitude minifloat with `eb` exponent bits (bias 2^(eb-1) - 1), `mb`
+    mantissa bits and no special values: nearest, ties to the even code, saturating at the largest
+    magnitude; returns the codes (sign in bit eb + mb) as uint8. Each value's binade is scaled so
+    that the representable values there are consecutive integers n, rounded with rint (half to
+    even); code = ((e + bias) << mb) + n - 2^mb, which also covers the subnormals (lowest binade)
+    and a carry into the next binade. Every step is exact in float32 for these widths."""
+    bias = (1 << (eb - 1)) - 1
+    vmax = np.float32((2.0 - 2.0 ** -mb) * 2.0 ** ((1 << eb) - 1 - bias))
+    x = np.asarray(x, dtype=np.float32)
+    flat = x.reshape(-1)
+    out = np.empty(flat.shape, dtype=np.uint8)
+    for i in range(0, flat.size, 1 << 24):  # bounded temporaries on large matrices
+        v = flat[i:i + (1 << 24)]
+        a = np.minimum(np.abs(v), vmax)
+        e = np.maximum(np.frexp(a)[1].astype(np.int32) - 1, 1 - bias)  # binade exponent
+        e[a == 0] = 1 - bias  # frexp(0) reports exponent 0, above the lowest binade when bias > 1
+        n = np.rint(np.ldexp(a, mb - e)).astype(np.int32)              # a / 2^(e - mb), exact
+        code = ((e + bias) << mb) + n - (1 << mb)
+        out[i:i + v.size] = np.where(np.signbit(v) & (code != 0), code | (1 << (eb + mb)), code)
+    return out.reshape(x.shape)
+
+
 def f32_to_e2m1_codes(x: np.ndarray) -> np.ndarray:
     """Round float32 to the nearest e2m1 value (ties to the even code, i.e. mantissa 0), saturating
     at +-6; returns 4-bit codes (sign in bit 3) as uint8."""
-    a = np.minimum(np.abs(np.asarray(x, dtype=np.float64)), 6.0)
-    idx = np.clip(np.searchsorted(E2M1_GRID, a), 1, 7)
-    lo, hi = E2M1_GRID[idx - 1], E2M1_GRID[idx]
-    pick_hi = (a - lo > hi - a) | ((a - lo == hi - a) & (idx % 2 == 0))
-    q = np.where(pick_hi, idx, idx - 1).astype(np.uint8)
-    return np.where(np.signbit(x) & (q != 0), q | 8, q).astype(np.uint8)
+    return minifloat_codes(x, 2, 1)
 
 
 def pack_e2m1(codes: np.ndarray) -> np.ndarray:
@@ -220,13 +244,7 @@ FP6_GRID = {"e3m2": _fp6_grid(3), "e2m3": _fp6_grid(2)}  # largest 28 and 7.5
 def f32_to_fp6_codes(x: np.ndarray, kind: str) -> np.ndarray:
     """Round float32 to the nearest fp6 (e3m2 or e2m3) value, ties to the even code (mantissa LSB
     0), saturating at the largest magnitude; returns 6-bit codes (sign in bit 5) as uint8."""
-    grid = FP6_GRID[kind]
-    a = np.minimum(np.abs(np.asarray(x, dtype=np.float64)), grid[-1])
-    idx = np.clip(np.searchsorted(grid, a), 1, 31)
-    lo, hi = grid[idx - 1], grid[idx]
-    pick_hi = (a - lo > hi - a) | ((a - lo == hi - a) & (idx % 2 == 0))
-    q = np.where(pick_hi, idx, idx - 1).astype(np.uint8)
-    return np.where(np.signbit(x) & (q != 0), q | 32, q).astype(np.uint8)
+    return minifloat_codes(x, 3, 2) if kind == "e3m2" else minifloat_codes(x, 2, 3)
 
 
 def pack_fp6(codes: np.ndarray) -> np.ndarray:
