@@ -106,3 +106,26 @@ def test_instr_desc_fp6_formats():
     """kind::f8f6f4 operand formats: e2m3 = 3, e3m2 = 4 (bits 7-9 for A, 10-12 for B)."""
     v = kl.mma_instr_desc(kl.KL_E3M2, kl.KL_E2M3, kl.KL_F32, 128, 256)
     assert (v >> 7) & 7 == 4 and (v >> 10) & 7 == 3
+
+
+@pytest.mark.parametrize("eb,mb", [(2, 1), (3, 2), (2, 3)], ids=["e2m1", "e3m2", "e2m3"])
+def test_minifloat_rounding_matches_a_grid_search(eb, mb):
+    """workloads.minifloat_codes (binade scaling and rint) against the definition: the nearest value
+    of the sorted grid, ties to the even code, saturating; zeros, subnormals, exact ties and the
+    values one ulp either side of every tie included."""
+    bias = (1 << (eb - 1)) - 1
+    codes = np.arange(1 << (eb + mb))
+    e, m = codes >> mb, codes & ((1 << mb) - 1)
+    grid = np.where(e == 0, m * 2.0 ** (1 - bias - mb), (m + (1 << mb)) * 2.0 ** (e - bias - mb))
+    mids = (grid[1:] + grid[:-1]) / 2
+    rng = np.random.default_rng(eb * 10 + mb)
+    x = np.concatenate([rng.standard_normal(200_000) * s for s in (0.01, 0.3, 2.0, 30.0)] +
+                       [mids, -mids, grid, -grid, np.nextafter(mids, 0), np.nextafter(mids, 1e9),
+                        [0.0, -0.0, 1e30, -1e30, 1e-30, -1e-30]]).astype(np.float32)
+    a = np.minimum(np.abs(x.astype(np.float64)), grid[-1])
+    idx = np.clip(np.searchsorted(grid, a), 1, len(grid) - 1)
+    lo, hi = grid[idx - 1], grid[idx]
+    pick_hi = (a - lo > hi - a) | ((a - lo == hi - a) & (idx % 2 == 0))
+    q = np.where(pick_hi, idx, idx - 1)
+    want = np.where(np.signbit(x) & (q != 0), q | (1 << (eb + mb)), q)
+    np.testing.assert_array_equal(wl.minifloat_codes(x, eb, mb), want)
