@@ -220,6 +220,8 @@ def _operand_type(x, ab_type) -> int:
 
     if ab_type is None:
         return _dtype_code(x.dtype)
+    if isinstance(ab_type, str) and ab_type not in FP6_TYPES:
+        raise ValueError(f"ab_type {ab_type!r}: packed fp6 is 'e3m2' or 'e2m3'")
     code = FP6_TYPES[ab_type] if isinstance(ab_type, str) else int(ab_type)
     if code not in (KL_E3M2, KL_E2M3) or x.dtype != torch.uint8:
         raise ValueError("ab_type names packed fp6 (KL_E3M2 / KL_E2M3) on uint8 tensors")
@@ -371,7 +373,10 @@ def mx_quantize(x, kind: str = "e4m3", stream=None):
     rows, k = x.shape
     if x.stride(1) != 1:
         raise ValueError("x must have a contiguous last dimension")
-    code = {"e4m3": KL_E4M3, "e2m1": KL_E2M1, **FP6_TYPES}[kind]
+    kinds = {"e4m3": KL_E4M3, "e2m1": KL_E2M1, **FP6_TYPES}
+    if kind not in kinds:
+        raise ValueError(f"MX element format {kind!r}: one of {sorted(kinds)}")
+    code = kinds[kind]
     if code in (KL_E3M2, KL_E2M3) and k % 128:
         raise ValueError("packed fp6 rows are whole 128-element (96-byte) blocks")
     width = k // 2 if code == KL_E2M1 else k // 4 * 3 if code in (KL_E3M2, KL_E2M3) else k

@@ -100,6 +100,10 @@ def test_descriptor_fields_from_packed_bytes():
         kl.gemm_desc(a.view(torch.float8_e4m3fn), b[0].view(torch.float8_e4m3fn), c, ab_type="e3m2")
     with pytest.raises(ValueError):
         kl.gemm_desc(a, b[0], c, ab_type=kl.KL_E4M3)
+    with pytest.raises(ValueError):
+        kl.gemm_desc(a, b[0], c, ab_type="e5m3")
+    with pytest.raises(ValueError):
+        kl.mx_quantize(torch.zeros(4, 128), "e3m3")
 
 
 def test_instr_desc_fp6_formats():
