@@ -171,6 +171,17 @@ KL_API kl_status kl_mx_pack_scales(const void* src, int64_t rows, int64_t k, int
 KL_API kl_status kl_mx_quantize(const void* x, int32_t x_type, int64_t rows, int64_t k, int64_t ldx, int32_t q_type,
                                 void* q, int64_t ldq, void* scales, void* stream);
 
+/* Device: NVFP4 quantisation of x [rows, k] (KL_F32 or KL_BF16, row pitch ldx elements; k a
+ * multiple of 16): a per-tensor scale g = amax(|x|) / (448 * 6) (1 for an all-zero x), written as
+ * fp32 to *global_scale (device); per 16 consecutive elements a UE4M3 scale s = e4m3(amax_16 /
+ * (6 g)) (nearest, saturating) into `scales` in the blocked layout (kl_block_scale_bytes(rows, k,
+ * 16) bytes, padding 0x38 = 1.0); elements e2m1(x / (s g)) packed two per byte into q (ldq
+ * elements per row, a multiple of 32). x ~ g * s * q. All arithmetic in fp64, so the result
+ * equals a host restatement bit for bit. Three kernels on `stream`; the outputs feed kl_gemm with
+ * block_scale = 2 (scale_a / scale_b = the global scales). */
+KL_API kl_status kl_nv_quantize(const void* x, int32_t x_type, int64_t rows, int64_t k, int64_t ldx, void* q,
+                                int64_t ldq, void* scales, float* global_scale, void* stream);
+
 /* Library version: major * 10000 + minor * 100 + patch. */
 KL_API int32_t kl_version(void);
 

@@ -36,7 +36,7 @@ EXPORTED = (
     "kl_make_tma_desc", "kl_gemm_skinny_noalloc", "kl_gemm_host", "kl_gemm_clock_probe", "kl_gemm_gather",
     "kl_ipc_get_handle", "kl_ipc_open_handle", "kl_ipc_close", "kl_umma_smem_desc_mn", "kl_mma_instr_desc_major",
     "kl_mma_instr_desc_block_scaled", "kl_mx_scale_bytes", "kl_mx_pack_scales", "kl_block_scale_bytes",
-    "kl_pack_block_scales", "kl_mx_quantize",
+    "kl_pack_block_scales", "kl_mx_quantize", "kl_nv_quantize",
 )
 
 
@@ -118,6 +118,7 @@ def lib() -> ctypes.CDLL:
             "kl_block_scale_bytes": (i64, [i64, i64, i32]),
             "kl_pack_block_scales": (i32, [vp, i64, i64, i32, i64, vp, vp]),
             "kl_mx_quantize": (i32, [vp, i32, i64, i64, i64, i32, vp, i64, vp, vp]),
+            "kl_nv_quantize": (i32, [vp, i32, i64, i64, i64, vp, i64, vp, vp, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -389,6 +390,27 @@ def mx_quantize(x, kind: str = "e4m3", stream=None):
     if code == KL_E2M1:
         return q.view(torch.float4_e2m1fn_x2), sc
     return (q, sc) if code != KL_E4M3 else (q.view(torch.float8_e4m3fn), sc)
+
+
+def nv_quantize(x, stream=None):
+    """NVFP4-quantise x (fp32 or bf16 device tensor [rows, K], K a multiple of 16) on the device:
+    returns (q float4_e2m1fn_x2 [rows, K/2], blocked UE4M3 scales per 16 elements, g) with g the
+    per-tensor fp32 scale as a one-element device tensor, ready for gemm(..., sfa=scales,
+    scale_a=g, scale_vec=16)."""
+    import torch
+
+    rows, k = x.shape
+    if x.stride(1) != 1:
+        raise ValueError("x must have a contiguous last dimension")
+    ldq = -(-k // 32) * 32
+    q = torch.empty((rows, ldq // 2), dtype=torch.uint8, device=x.device)
+    sc = torch.empty(block_scale_bytes(rows, k, 16), dtype=torch.uint8, device=x.device)
+    g = torch.empty(1, dtype=torch.float32, device=x.device)
+    s = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
+    check(lib().kl_nv_quantize(ctypes.c_void_p(x.data_ptr()), _dtype_code(x.dtype), rows, k, x.stride(0),
+                               ctypes.c_void_p(q.data_ptr()), ldq, ctypes.c_void_p(sc.data_ptr()),
+                               ctypes.c_void_p(g.data_ptr()), ctypes.c_void_p(s)))
+    return q[:, :k // 2].view(torch.float4_e2m1fn_x2), sc, g
 
 
 def mx_pack_scales(scales, k: int, out=None, stream=None):

@@ -215,6 +215,89 @@ __global__ void mx_quantize_kernel(const XT* __restrict__ x, long long ldx, long
   }
 }
 
+// ---- NVFP4 quantisation -----------------------------------------------------------------------
+
+template <typename XT>
+__device__ __forceinline__ float load_x(const XT* p) {
+  if constexpr (sizeof(XT) == 4)
+    return *p;
+  else
+    return __uint_as_float(uint32_t(*p) << 16);  // bf16 bits
+}
+
+// amax of |x| over the matrix, kept as float bits (non-negative floats order like their patterns):
+// a grid-stride max per thread, a block max, one atomicMax per block into *out (zeroed before).
+template <typename XT>
+__global__ void amax_kernel(const XT* __restrict__ x, long long ldx, long long rows, long long k,
+                            unsigned* __restrict__ out) {
+  float m = 0.0f;
+  const long long n = rows * k;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / k;
+    m = fmaxf(m, fabsf(load_x(x + r * ldx + (i - r * k))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ float warp_max[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) warp_max[warp] = m;
+  __syncthreads();
+  if (warp == 0) {
+    m = lane < int(blockDim.x >> 5) ? warp_max[lane] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) atomicMax(out, __float_as_uint(m));
+  }
+}
+
+// The per-tensor scale g = amax / (448 * 6) (1 for an all-zero x), in fp64 as every step below.
+__device__ __forceinline__ double nv_global_scale(unsigned amax_bits) {
+  const double amax = double(__uint_as_float(amax_bits));
+  return amax > 0.0 ? amax / (448.0 * 6.0) : 1.0;
+}
+
+// One thread per (row, 16-element group) of the padded blocked layout (vec 16: K blocks of 64):
+// scale s = e4m3(amax_group / (6 g)) (nearest, saturating; a UE4M3 byte), elements
+// e2m1(x / (s g)) (0 where s = 0), packed two per byte, the first in the low nibble. Padding
+// positions get scale 0x38 (1.0).
+template <typename XT>
+__global__ void nv_quantize_kernel(const XT* __restrict__ x, long long ldx, long long rows, long long groups,
+                                   uint8_t* __restrict__ q, long long ldq_bytes, uint8_t* __restrict__ sf,
+                                   long long k_blocks, long long rows_pad, const unsigned* __restrict__ amax_bits) {
+  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long groups_pad = k_blocks * 4;
+  if (t >= rows_pad * groups_pad) return;
+  const long long r = t / groups_pad, g = t - r * groups_pad;
+  uint8_t* sfp = sf + ((r / 128) * k_blocks + g / 4) * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + (g % 4);
+  if (r >= rows || g >= groups) {
+    *sfp = 0x38;
+    return;
+  }
+  const double gs = nv_global_scale(*amax_bits);
+  float v[16];
+  const XT* src = x + r * ldx + g * 16;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = load_x(src + i);
+  float bmax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) bmax = fmaxf(bmax, fabsf(v[i]));
+  const uint32_t sbits = cvt_e4m3x2(float(double(bmax) / (6.0 * gs)), 0.0f) & 0x7Fu;
+  const uint32_t se = sbits >> 3, sm = sbits & 7u;  // the e4m3 value, exactly
+  const double s = se == 0 ? ldexp(double(sm), -9) : ldexp(double(8 + sm), int(se) - 10);
+  const double inv = s > 0.0 ? 1.0 / (s * gs) : 0.0;
+  uint32_t w[2] = {0, 0};
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    w[j / 4] |= cvt_e2m1x2(float(double(v[2 * j]) * inv), float(double(v[2 * j + 1]) * inv)) << (8 * (j % 4));
+  *reinterpret_cast<uint2*>(q + r * ldq_bytes + g * 8) = make_uint2(w[0], w[1]);
+  *sfp = uint8_t(sbits);
+}
+
+// amax bits -> g, in place (one thread, after the quantisation has read the amax).
+__global__ void nv_finish_kernel(unsigned* amax_then_g) {
+  *reinterpret_cast<float*>(amax_then_g) = float(nv_global_scale(*amax_then_g));
+}
+
 }  // namespace
 }  // namespace kl::capi
 
@@ -268,4 +351,43 @@ extern "C" kl_status kl_mx_quantize(const void* x, int32_t x_type, int64_t rows,
     by_q(static_cast<const uint16_t*>(x));
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? KL_OK : kl::capi::cuda_fail(e, "kl_mx_quantize launch");
+}
+
+extern "C" kl_status kl_nv_quantize(const void* x, int32_t x_type, int64_t rows, int64_t k, int64_t ldx, void* q,
+                                    int64_t ldq, void* scales, float* global_scale, void* stream) {
+  using kl::capi::fail;
+  if (rows < 0 || k < 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_nv_quantize: negative extent");
+  if (rows == 0 || k == 0) return KL_OK;
+  if (x == nullptr || q == nullptr || scales == nullptr || global_scale == nullptr)
+    return fail(KL_ERR_INVALID_ARGUMENT, "kl_nv_quantize: null pointer");
+  if (x_type != KL_F32 && x_type != KL_BF16) return fail(KL_ERR_NOT_SUPPORTED, "kl_nv_quantize: x must be f32 or bf16");
+  if (k % 16 != 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_nv_quantize: k must be a multiple of 16");
+  if (ldx < k) return fail(KL_ERR_INVALID_ARGUMENT, "kl_nv_quantize: ldx < k");
+  if (ldq < k || ldq % 32 != 0 || reinterpret_cast<uintptr_t>(q) % 16 != 0)
+    return fail(KL_ERR_INVALID_ARGUMENT,
+                "kl_nv_quantize: q must be 16-byte aligned with a row pitch >= k, a multiple of 32 elements");
+  if (reinterpret_cast<uintptr_t>(global_scale) % 4 != 0)
+    return fail(KL_ERR_INVALID_ARGUMENT, "kl_nv_quantize: global_scale must be 4-byte aligned");
+  const long long k_blocks = (k + 63) / 64, rows_pad = (rows + 127) / 128 * 128;
+  const long long blocks = (rows_pad * k_blocks * 4 + 255) / 256;
+  if (blocks > INT32_MAX) return fail(KL_ERR_INVALID_ARGUMENT, "kl_nv_quantize: too large");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto* amax = reinterpret_cast<unsigned*>(global_scale);  // holds amax's bits until the last step
+  cudaError_t e = cudaMemsetAsync(amax, 0, sizeof(unsigned), s);
+  if (e != cudaSuccess) return kl::capi::cuda_fail(e, "cudaMemsetAsync(amax)");
+  auto* qp = static_cast<uint8_t*>(q);
+  auto* sp = static_cast<uint8_t*>(scales);
+  auto run = [&](auto const* xp) {
+    using XT = std::remove_cv_t<std::remove_pointer_t<decltype(xp)>>;
+    kl::capi::amax_kernel<XT><<<1184, 256, 0, s>>>(xp, ldx, rows, k, amax);
+    kl::capi::nv_quantize_kernel<XT><<<unsigned(blocks), 256, 0, s>>>(xp, ldx, rows, k / 16, qp, ldq / 2, sp, k_blocks,
+                                                                     rows_pad, amax);
+  };
+  if (x_type == KL_F32)
+    run(static_cast<const float*>(x));
+  else
+    run(static_cast<const uint16_t*>(x));
+  kl::capi::nv_finish_kernel<<<1, 1, 0, s>>>(amax);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? KL_OK : kl::capi::cuda_fail(e, "kl_nv_quantize launch");
 }

@@ -365,3 +365,50 @@ def test_device_quantize_then_gemm(cuda, kind):
     ref = og.gemm_mx_f64(ra, rb, rsa, rsb, kind)
     elem, norm = og.rel_error(c.cpu().numpy(), ref)
     assert elem <= FP8_TOL and norm <= FP8_TOL
+
+
+@pytest.mark.parametrize("src", ["f32", "bf16"])
+@pytest.mark.parametrize("rows,k", [(1, 16), (200, 336), (129, 1024)])
+def test_device_nv_quantize_matches_reference(cuda, src, rows, k):
+    """kl_nv_quantize = the NVFP4 quantisation restated in maia_b200.workloads.nv_quantize: the same
+    per-tensor scale (to fp32), the same UE4M3 block scales bit for bit, the same element values."""
+    rng = np.random.default_rng(rows + 3 * k)
+    x = (rng.standard_normal((rows, k)) * np.exp2(rng.uniform(-6, 6, (rows, 1)))).astype(np.float32)
+    if src == "bf16":
+        x = wl.bf16_bits_to_f32(wl.f32_to_bf16_bits(x))
+    xt = torch.from_numpy(x).to(cuda)
+    if src == "bf16":
+        xt = xt.to(torch.bfloat16)
+    q, sc, g = kl.nv_quantize(xt)
+    torch.cuda.synchronize()
+    want_q, want_s, want_g = wl.nv_quantize(x)
+    assert g.item() == np.float32(want_g)
+    np.testing.assert_array_equal(sc.cpu().numpy(), og.pack_mx_scales(want_s, k, 16))
+    got_v = og.decode(q.view(torch.uint8).cpu().numpy(), "e2m1")
+    np.testing.assert_array_equal(got_v, og.decode(want_q, "e2m1"))
+
+
+def test_device_nv_quantize_then_gemm(cuda):
+    rng = np.random.default_rng(12)
+    xa = rng.standard_normal((256, 512)).astype(np.float32)
+    xb = (rng.standard_normal((384, 512)) * 0.05).astype(np.float32)
+    qa, sa, ga = kl.nv_quantize(torch.from_numpy(xa).to(cuda))
+    qb, sb, gb = kl.nv_quantize(torch.from_numpy(xb).to(cuda))
+    c = kl.gemm(qa, qb, sfa=sa, sfb=sb, scale_vec=16, scale_a=ga, scale_b=gb, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert kl.read_status() == 0
+    ra, rsa, rga = wl.nv_quantize(xa)
+    rb, rsb, rgb = wl.nv_quantize(xb)
+    elem, norm = og.rel_error(c.cpu().numpy(), og.gemm_nv_f64(ra, rb, rsa, rsb, rga * rgb))
+    assert elem <= FP8_TOL and norm <= FP8_TOL
+
+
+def test_device_nv_quantize_all_zero(cuda):
+    """g = 1 and every scale 0 for an all-zero x; the elements are zeros."""
+    q, sc, g = kl.nv_quantize(torch.zeros(130, 64, device=cuda))
+    torch.cuda.synchronize()
+    assert g.item() == 1.0
+    blocked = sc.cpu().numpy().reshape(-1, 512)
+    want = og.pack_mx_scales(np.zeros((130, 4), dtype=np.uint8), 64, 16).reshape(-1, 512)
+    np.testing.assert_array_equal(blocked, want)
+    assert not q.view(torch.uint8).any()
