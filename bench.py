@@ -130,7 +130,7 @@ def config_of(w, args, world):
     return {"workload": w.name, "m": w.m, "n": w.n, "k": w.k, "out": w.out,
             "parallelism": f"N-sharded x{world}", "output": "C[:, shard] per rank (no gather)",
             "l2": "operands exceed L2 (no flush)", "algo": args.algo, "group_m": args.group_m,
-            "prefetch": args.prefetch, "variant": args.variant, "max_ctas": args.max_ctas}
+            "prefetch": args.prefetch, "variant": args.variant, "max_ctas": args.max_ctas, "stream_k": args.stream_k}
 
 
 def run_reference(args, w):
@@ -170,6 +170,8 @@ def main():
     ap.add_argument("--variant", type=int, default=0, help="kl_gemm_desc.variant (0 = library default)")
     ap.add_argument("--max-ctas", type=int, default=0, help="cap on resident CTAs (0 = library default)")
     ap.add_argument("--chunks", type=int, default=0, help="e2e column blocks of kl_gemm_host (0 = library default)")
+    ap.add_argument("--stream-k", type=int, default=0, choices=[-1, 0, 1],
+                    help="tile kernels' split tail: 0 = library default, 1 = always, -1 = whole tiles")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
 
@@ -241,7 +243,7 @@ def main():
     stream = torch.cuda.current_stream(dev)
     kw = dict(scale_a=scale_a, scale_b=scale_b, algo=args.algo, group_m=args.group_m, prefetch=args.prefetch,
               variant=args.variant, max_ctas=args.max_ctas, sfa=sfa, sfb=sfb, scale_vec=vec,
-              ab_type=wl.MX_ELEMENT[w.dtype] if w.dtype == "mxfp6" else None)
+              ab_type=wl.MX_ELEMENT[w.dtype] if w.dtype == "mxfp6" else None, stream_k=args.stream_k)
 
     def step():
         kl.gemm(a, b, c, **kw)
@@ -289,7 +291,8 @@ def main():
     def e2e_step():
         # The host-buffer entry point: copies in, GEMM and copy out, pipelined over column blocks.
         kl.gemm_host(a_host, b_host, c_host, a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo,
-                     sfa=sfa_host, sfb=sfb_host, scale_vec=vec, chunks=args.chunks, ab_type=kw["ab_type"])
+                     sfa=sfa_host, sfb=sfb_host, scale_vec=vec, chunks=args.chunks, ab_type=kw["ab_type"],
+                     stream_k=args.stream_k)
 
     for _ in range(max(args.warmup, 3)):
         e2e_step()
@@ -330,7 +333,7 @@ def main():
 
         def fused_step():
             kl.gemm_gather(a, b, c_view, peers, scale_a=scale_a, scale_b=scale_b, algo=args.algo, sfa=sfa, sfb=sfb,
-                           scale_vec=vec)
+                           scale_vec=vec, stream_k=args.stream_k)
 
         for _ in range(max(args.warmup, 3)):
             fused_step()
