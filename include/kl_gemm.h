@@ -31,7 +31,7 @@ extern "C" {
 typedef enum kl_status {
   KL_OK = 0,
   KL_ERR_INVALID_ARGUMENT = 1, /* bad shape, stride, alignment or combination */
-  KL_ERR_NOT_SUPPORTED = 2,    /* valid request this build or device cannot run */
+  KL_ERR_NOT_SUPPORTED = 2,    /* a valid request this library or device cannot run */
   KL_ERR_CUDA = 3,             /* a CUDA runtime/driver call failed */
   KL_ERR_TIMEOUT = 4,          /* a bounded device-side wait ran out (kl_read_status) */
   KL_ERR_NCCL = 5              /* reserved for collective failures */

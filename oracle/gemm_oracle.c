@@ -11,7 +11,8 @@
  * reference: there is no reference GEMM output to pin to. The tests pin this file instead against
  * numpy float64 matmul on the same decoded inputs.
  *
- *   kl_oracle_gemm_f64   fp64 accumulation over the decoded inputs, times `scale`: the checker.
+ *   kl_oracle_gemm_f64   fp64 accumulation over the decoded inputs, times `scale`: the result the GPU
+ *                        tests compare against.
  *   kl_oracle_gemm_f32   fp32 accumulation, cache-blocked, all host threads: the timed CPU
  *                        baseline (the "CPU reference GEMM" of the benchmark's smallest config).
  *   kl_oracle_decode     element decoders (bf16, f16, e4m3, e5m2), exposed so tests can check
