@@ -186,3 +186,61 @@ def test_block_scaled_instr_desc_errors():
                                          (16384, 8192, 128 * 64 * 512), (0, 5, 0)])
 def test_mx_scale_bytes(rows, k, want):
     assert kl.mx_scale_bytes(rows, k) == want
+
+
+def _desc(**kw):
+    """A descriptor with placeholder (never dereferenced) device pointers."""
+    d = kl.GemmDesc(m=256, n=256, k=256, a=0x1000, lda=256, b=0x2000, ldb=256, c=0x3000, ldc=256,
+                    ab_type=kl.KL_BF16, c_type=kl.KL_BF16, alpha=1.0)
+    for name, value in kw.items():
+        setattr(d, name, value)
+    return d
+
+
+@pytest.mark.parametrize("field,value,msg", [
+    ("stream_k", 2, "stream_k must be -1, 0 or 1"),
+    ("stream_k", -2, "stream_k must be -1, 0 or 1"),
+    ("c_reduce", 2, "c_reduce must be 0"),
+    ("reserved2", 1, "reserved fields must be 0"),
+    ("m", -1, "negative extent"),
+    ("a_major", 3, "a_major / b_major must be 0"),
+])
+def test_gemm_rejects_bad_descriptors_before_any_launch(field, value, msg):
+    """kl_gemm validates the descriptor on the host: these fail with KL_ERR_INVALID_ARGUMENT and a
+    message, with no GPU in the machine (nothing is launched or read)."""
+    st = kl.lib().kl_gemm(ctypes.byref(_desc(**{field: value})), ctypes.c_void_p(0))
+    assert st == kl.KL_ERR_INVALID_ARGUMENT
+    assert msg in kl.last_error()
+
+
+def test_gemm_of_an_empty_output_is_a_no_op():
+    assert kl.lib().kl_gemm(ctypes.byref(_desc(m=0)), ctypes.c_void_p(0)) == kl.KL_OK
+    assert kl.lib().kl_gemm(ctypes.byref(_desc(n=0, c=0)), ctypes.c_void_p(0)) == kl.KL_OK
+
+
+def test_gather_and_host_entry_points_check_their_arguments():
+    arr = (ctypes.c_void_p * 8)(*[ctypes.c_void_p(0x4000 + i) for i in range(8)])
+    assert kl.lib().kl_gemm_gather(ctypes.byref(_desc()), arr, 8, ctypes.c_void_p(0)) == kl.KL_ERR_INVALID_ARGUMENT
+    assert "0 to 7 peers" in kl.last_error()
+    dev = [ctypes.c_void_p(0x5000), ctypes.c_void_p(0x6000), ctypes.c_void_p(0x7000)]
+    st = kl.lib().kl_gemm_host(ctypes.byref(_desc(c_reduce=1)), *dev, 0, ctypes.c_void_p(0))
+    assert st == kl.KL_ERR_NOT_SUPPORTED and "c_reduce" in kl.last_error()
+    st = kl.lib().kl_gemm_host(ctypes.byref(_desc(batch=2)), *dev, 0, ctypes.c_void_p(0))
+    assert st == kl.KL_ERR_NOT_SUPPORTED and "batch" in kl.last_error()
+    st = kl.lib().kl_gemm_host(ctypes.byref(_desc(lda=100)), *dev, 0, ctypes.c_void_p(0))
+    assert st == kl.KL_ERR_INVALID_ARGUMENT and "leading dimension" in kl.last_error()
+
+
+def test_quantisers_check_their_arguments():
+    p = ctypes.c_void_p(0x8000)
+    st = kl.lib().kl_mx_quantize(p, kl.KL_F32, 4, 48, 48, kl.KL_E4M3, p, 48, p, ctypes.c_void_p(0))
+    assert st == kl.KL_ERR_INVALID_ARGUMENT and "multiple of 32" in kl.last_error()
+    st = kl.lib().kl_mx_quantize(p, kl.KL_F16, 4, 64, 64, kl.KL_E4M3, p, 64, p, ctypes.c_void_p(0))
+    assert st == kl.KL_ERR_NOT_SUPPORTED
+    st = kl.lib().kl_mx_quantize(p, kl.KL_F32, 4, 64, 64, kl.KL_E3M2, p, 64, p, ctypes.c_void_p(0))
+    assert st == kl.KL_ERR_INVALID_ARGUMENT and "128 elements" in kl.last_error()
+    st = kl.lib().kl_nv_quantize(p, kl.KL_F32, 4, 40, 40, p, 64, p, p, ctypes.c_void_p(0))
+    assert st == kl.KL_ERR_INVALID_ARGUMENT and "multiple of 16" in kl.last_error()
+    st = kl.lib().kl_nv_quantize(p, kl.KL_F32, 4, 64, 64, p, 48, p, p, ctypes.c_void_p(0))
+    assert st == kl.KL_ERR_INVALID_ARGUMENT and "multiple of 32" in kl.last_error()
+    assert kl.lib().kl_nv_quantize(p, kl.KL_F32, 0, 64, 64, p, 64, p, p, ctypes.c_void_p(0)) == kl.KL_OK
