@@ -322,7 +322,9 @@ KL_API kl_status kl_mma_instr_desc_major(int32_t a_type, int32_t b_type, int32_t
 /* 128-byte TMA tensor map for a rank-`rank` row-major global tensor (shape/stride outermost
  * first, in elements) moved in tiles of tile_rows x tile_cols with the given swizzle. Needs a CUDA
  * driver (the encoding is the driver's). kernel_lib/include/kl/layout/tma_desc.hpp:100-164
- * (make_tma_desc / make_tma_load / make_tma_store). Same validation and messages. */
+ * (make_tma_desc / make_tma_load / make_tma_store). Same validation and messages. dtype KL_E3M2 /
+ * KL_E2M3 (no counterpart in the reference): packed fp6 in global memory, a 16U6 map of 128-element
+ * boxes (one byte per element in shared memory), with the driver's rules for that type checked. */
 KL_API kl_status kl_make_tma_desc(int32_t dtype, int32_t tile_rows, int32_t tile_cols, int32_t swizzle_span, int32_t is_store,
                            const void* gmem, int32_t rank, const int64_t* shape, const int64_t* stride,
                            void* map_out);

@@ -177,6 +177,8 @@ int elem_bytes_of(int32_t t) {
       return 2;
     case KL_E4M3:
     case KL_E5M2:
+    case KL_E3M2:  // packed fp6: one byte per element in shared memory
+    case KL_E2M3:
     case KL_I8:
     case KL_U8:
       return 1;
@@ -574,8 +576,12 @@ kl_status kl_make_tma_desc(int32_t dtype, int32_t tile_rows, int32_t tile_cols, 
                                       : CU_TENSOR_MAP_SWIZZLE_NONE;
   try {
     CUtensorMap map;
-    kl::detail::encode_tma_map(&map, t, eb, sw, uint32_t(g.inner), uint32_t(g.outer), gmem, rank, shape, stride,
-                               kl::TmaOptions{});
+    if (dtype == KL_E3M2 || dtype == KL_E2M3)  // packed fp6 in global memory: a 16U6 map
+      kl::detail::encode_tma_map_u6(&map, sw, uint32_t(g.inner), uint32_t(g.outer), gmem, rank, shape, stride,
+                                    kl::TmaOptions{});
+    else
+      kl::detail::encode_tma_map(&map, t, eb, sw, uint32_t(g.inner), uint32_t(g.outer), gmem, rank, shape, stride,
+                                 kl::TmaOptions{});
     std::memcpy(map_out, &map, sizeof(CUtensorMap));
   } catch (std::invalid_argument const& ex) {
     return fail(KL_ERR_INVALID_ARGUMENT, ex.what());

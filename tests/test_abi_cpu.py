@@ -113,6 +113,29 @@ def test_tma_desc_validation(ptr, shape, stride, msg):
     assert e.value.message == msg
 
 
+# Packed fp6 (16U6 maps): the driver's extra rules for the type, checked before the driver call.
+@pytest.mark.parametrize("ptr, shape, stride, msg", [
+    (0x10010, (4096, 4096), (4096, 1), "kl::make_tma_desc: packed fp6: global address must be 32-byte aligned"),
+    (0x10000, (4096, 4000), (4096, 1),
+     "kl::make_tma_desc: packed fp6: the innermost extent must be a multiple of 128 elements"),
+    (0x10000, (4096, 4096), (4160, 1),
+     "kl::make_tma_desc: packed fp6: outer strides must be positive multiples of 128 elements (32 bytes)"),
+    (0x10000, (4096, 4096), (3968, 1), "kl::make_tma_desc: rows overlap: the row stride is smaller than cols"),
+])
+@pytest.mark.parametrize("dtype", [kl.KL_E3M2, kl.KL_E2M3], ids=["e3m2", "e2m3"])
+def test_fp6_tma_desc_validation(dtype, ptr, shape, stride, msg):
+    with pytest.raises(kl.KlError) as e:
+        kl.make_tma_desc(dtype, 128, 128, 128, ptr, shape, stride)
+    assert e.value.status == kl.KL_ERR_INVALID_ARGUMENT
+    assert e.value.message == msg
+
+
+def test_fp6_tma_desc_needs_the_128_byte_swizzle():
+    with pytest.raises(kl.KlError) as e:
+        kl.make_tma_desc(kl.KL_E3M2, 128, 64, 64, 0x10000, (4096, 4096), (4096, 1))
+    assert "packed fp6 boxes are 128 elements wide" in e.value.message
+
+
 @pytest.mark.parametrize("t", mn_tiles(), ids=lambda t: f"{t['type']}_mn{t['mn']}_k{t['k']}_sw{t['swizzle']}")
 def test_mn_major_tile_and_descriptors_match_cute(t):
     """MN-major operands: SmemTile<T, K, MN, Sw> (MN contiguous, atoms down K first) is the layout of
