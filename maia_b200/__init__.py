@@ -435,13 +435,13 @@ def gemm_host(a_host, b_host, c_host, a_dev, b_dev, c_dev, *, alpha=1.0, scale_a
 
 
 def gemm_gather(a, b, c_shard, peer_ptrs, *, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
-                group_m=0, sfa=None, sfb=None, scale_vec=32, ab_type=None, stream_k=0, stream=None):
+                group_m=0, max_ctas=0, sfa=None, sfb=None, scale_vec=32, ab_type=None, stream_k=0, stream=None):
     """c_shard = alpha * a @ b.T, and the same tiles written to each peer pointer (a view of the same
     columns in another GPU's copy of C, with c_shard's pitch), through kl_gemm_gather."""
     import torch
 
-    d = gemm_desc(a, b, c_shard, alpha, scale_a, scale_b, algo, group_m, sfa=sfa, sfb=sfb, scale_vec=scale_vec,
-                  ab_type=ab_type, stream_k=stream_k)
+    d = gemm_desc(a, b, c_shard, alpha, scale_a, scale_b, algo, group_m, max_ctas, sfa=sfa, sfb=sfb,
+                  scale_vec=scale_vec, ab_type=ab_type, stream_k=stream_k)
     arr = (ctypes.c_void_p * max(1, len(peer_ptrs)))(*[ctypes.c_void_p(p) for p in peer_ptrs])
     s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
     check(lib().kl_gemm_gather(ctypes.byref(d), arr, len(peer_ptrs), ctypes.c_void_p(s)))

@@ -1,7 +1,8 @@
 """N-sharded GEMM on 2+ GPUs of one node (skipped with fewer): every rank computes its column
 shard with kl_gemm_gather, whose epilogue also stores the tiles into the other ranks' copies of C
 over NVLink; after one collective every rank holds the whole C, equal bit for bit to a single-GPU
-kl_gemm of the full problem."""
+kl_gemm of the full problem (whole tiles on both sides), and with the split tail forced on, within
+the bf16 tolerance of the fp64 oracle."""
 
 import os
 import socket
@@ -48,6 +49,26 @@ try:
         assert torch.equal(shared.full.view(torch.int16), ref.view(torch.int16)), f"rank {rank} shape {(m, n, k)}"
         dist.barrier()
         shared.close()
+    # The split tail forced on (stream_k = 1): the last arrival at a split tile stores it to every
+    # copy of C; checked against the fp64 oracle (the split sums in another order than whole tiles).
+    from oracle import gemm as og
+    m, n, k = 512, 4096, 2048
+    a_bits, b_bits, _, _ = random_inputs(m, n, k, "bf16", seed=77)
+    a, b = to_device(a_bits, "bf16", dev), to_device(b_bits, "bf16", dev)
+    lo, hi = sharding.shard_range(n, world, rank, align=256)
+    shared = sharding.SharedC(m, n, torch.float32, dev, dist)
+    shared.full.fill_(float("nan"))
+    dist.barrier()
+    kl.gemm_gather(a, b[lo:hi], shared.full[:, lo:hi], shared.peer_ptrs(lo), stream_k=1, max_ctas=16)
+    dist.barrier()
+    torch.cuda.synchronize()
+    assert kl.read_status() == 0
+    got = shared.full.cpu().numpy()
+    assert not np.isnan(got).any(), f"rank {rank}: unwritten entries"
+    elem, norm = og.rel_error(got, og.gemm_f64(a_bits, b_bits, 1.0))
+    assert elem <= 1e-2 and norm <= 1e-2, f"rank {rank}: split tail {elem:.3e} / {norm:.3e}"
+    dist.barrier()
+    shared.close()
 finally:
     dist.destroy_process_group()
 print("OK", rank)
