@@ -171,3 +171,33 @@ def test_stream_k_argument_is_checked(cuda):
     with pytest.raises(kl.KlError) as e:
         kl.gemm(a, a, torch.zeros(256, 256, dtype=torch.bfloat16, device=cuda), stream_k=2)
     assert e.value.status == kl.KL_ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("a_major,b_major", [(1, 0), (0, 1), (1, 1)], ids=["a_mn", "b_mn", "both_mn"])
+def test_mn_major_operands(cuda, a_major, b_major):
+    """The split tail on MN-major tiles (A stored [K, M], B stored [K, N]): a K-range starts mid-K."""
+    m, n, k = 512, 768, 1024
+    a, b, _, _ = random_inputs(m, n, k, "bf16", seed=a_major + 2 * b_major)
+    da, db = to_device(a, "bf16", cuda), to_device(b, "bf16", cuda)
+    if a_major:
+        da = da.t().contiguous()
+    if b_major:
+        db = db.t().contiguous()
+    c = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=cuda)
+    kl.gemm(da, db, c, algo=kl.ALGO_2CTA, a_major=a_major, b_major=b_major, stream_k=1, max_ctas=6)
+    torch.cuda.synchronize()
+    assert kl.read_status() == 0
+    check(c.float().cpu().numpy(), a, b, 1.0, TOL16)
+
+
+@pytest.mark.parametrize("swizzle", [64, 32])
+def test_narrow_swizzle(cuda, swizzle):
+    a, b, _, _ = random_inputs(384, 520, 1000, "bf16", seed=swizzle)
+    c = run_kl(a, b, "bf16", "f32", cuda, kl.ALGO_1CTA, swizzle=swizzle, stream_k=1, max_ctas=8)
+    check(c, a, b, 1.0, TOL16)
+
+
+def test_f16_inputs(cuda):
+    a, b, _, _ = random_inputs(300, 600, 1536, "f16", seed=15)
+    c = run_kl(a, b, "f16", "f16", cuda, kl.ALGO_2CTA, stream_k=1, max_ctas=10)
+    check(c, a, b, 1.0, TOL16, kind="f16")
