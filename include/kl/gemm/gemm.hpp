@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <stdexcept>
 #include <type_traits>
@@ -145,23 +146,25 @@ struct LaunchInfo {
 
 namespace detail {
 
+// Per-device caches below are filled on first use from whichever host thread gets there; the
+// values are the same whoever computes them, and atomics keep concurrent first calls race-free.
 inline int sm_count(int device) {
-  static int cache[64] = {};
+  static std::atomic<int> cache[64];
   if (device < 0 || device >= 64) return 0;
-  if (cache[device] == 0) {
-    int n = 0;
+  int n = cache[device].load(std::memory_order_acquire);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
-    cache[device] = n;
+    cache[device].store(n, std::memory_order_release);
   }
-  return cache[device];
+  return n;
 }
 
 template <class Cfg>
 inline cudaError_t prepare_kernel(int device, int* max_workers) {
   // Per device: opt in to the shared-memory size and ask how many CTA groups fit at once.
-  static int workers[64] = {};
+  static std::atomic<int> workers[64];
   if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
-  if (workers[device] == 0) {
+  if (workers[device].load(std::memory_order_acquire) == 0) {
     auto kernel = gemm_tn_kernel<Cfg>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::kSmemBytes));
     if (e != cudaSuccess) return e;
@@ -188,9 +191,9 @@ inline cudaError_t prepare_kernel(int device, int* max_workers) {
       if (e != cudaSuccess) return e;
     }
     if (n <= 0) return cudaErrorInvalidConfiguration;
-    workers[device] = n;
+    workers[device].store(n, std::memory_order_release);
   }
-  *max_workers = workers[device];
+  *max_workers = workers[device].load(std::memory_order_acquire);
   return cudaSuccess;
 }
 

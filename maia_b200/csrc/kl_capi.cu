@@ -4,6 +4,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include <cstdint>
 #include <cstring>
 #include <exception>
@@ -41,18 +43,20 @@ kl_status cuda_fail(cudaError_t e, char const* where) {
 unsigned long long wait_timeout_ns() { return g_timeout_ns; }
 
 kl_status device_status_ptr(int** out) {
-  static int* cache[64] = {};
+  static std::atomic<int*> cache[64];  // per device; the same address whoever looks it up first
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(KL_ERR_NOT_SUPPORTED, "device index above 63");
-  if (cache[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, kl_device_status_word);
+  int* p = cache[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, kl_device_status_word);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status)");
-    cache[dev] = static_cast<int*>(p);
+    p = static_cast<int*>(addr);
+    cache[dev].store(p, std::memory_order_release);
   }
-  *out = cache[dev];
+  *out = p;
   return KL_OK;
 }
 

@@ -3,6 +3,8 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include <algorithm>
 #include <cstdint>
 #include <mutex>
@@ -96,14 +98,14 @@ kl_status launch(kl_gemm_desc const& d, Plan const& pl, void* ws, cudaStream_t s
   int* status = nullptr;
   kl_status s = device_status_ptr(&status);
   if (s != KL_OK) return s;
-  static int configured[64] = {};
+  static std::atomic<int> configured[64];  // per device; idempotent, so concurrent first calls are fine
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
+  if (dev >= 0 && dev < 64 && !configured[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(gemm_skinny_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          int(Cfg::kSmemBytes));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(skinny)");
-    configured[dev] = 1;
+    configured[dev].store(1, std::memory_order_release);
   }
   SkinnyParams p{};
   // Packed fp4: K and the pitches count elements, the maps bytes.

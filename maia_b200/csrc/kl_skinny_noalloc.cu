@@ -15,6 +15,8 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include <algorithm>
 #include <cstdint>
 #include <mutex>
@@ -71,14 +73,15 @@ kl_status launch(kl_gemm_desc const& d, int n_tiles, int k_blocks, int grid, uns
   int* status = nullptr;
   kl_status s = kl::capi::device_status_ptr(&status);
   if (s != KL_OK) return s;
-  static int configured[64] = {};
+  static std::atomic<int> configured[64];  // per device; idempotent, so concurrent first calls are fine
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!configured[dev]) {
+  if (dev < 0 || dev >= 64) return kl::capi::fail(KL_ERR_NOT_SUPPORTED, "device index above 63");
+  if (!configured[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(gemm_skinny_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          int(Cfg::kSmemBytes));
     if (e != cudaSuccess) return kl::capi::cuda_fail(e, "cudaFuncSetAttribute(no-alloc skinny)");
-    configured[dev] = 1;
+    configured[dev].store(1, std::memory_order_release);
   }
   SkinnyParams p{};
   p.map_w = kl::make_tma_load<typename Cfg::WTile>(kl::row_major_strided(static_cast<InT const*>(d.b), d.n, d.k, d.ldb)).map;
