@@ -182,6 +182,12 @@ KL_API kl_status kl_mx_quantize(const void* x, int32_t x_type, int64_t rows, int
 KL_API kl_status kl_nv_quantize(const void* x, int32_t x_type, int64_t rows, int64_t k, int64_t ldx, void* q,
                                 int64_t ldq, void* scales, float* global_scale, void* stream);
 
+/* Frees every workspace the library allocated for kl_gemm (the skinny kernel's per-device buffer,
+ * the tile kernels' per-stream split-tail buffers), after synchronising each device that has one;
+ * later calls allocate afresh. No launch that uses them may be in flight or captured in a CUDA
+ * graph that will still be replayed. KL_OK when there is nothing to free. */
+KL_API kl_status kl_release_workspaces(void);
+
 /* Library version: major * 10000 + minor * 100 + patch. */
 KL_API int32_t kl_version(void);
 

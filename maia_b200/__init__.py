@@ -30,7 +30,7 @@ FP6_TYPES = {"e3m2": KL_E3M2, "e2m3": KL_E2M3}
 ALGO_AUTO, ALGO_1CTA, ALGO_2CTA, ALGO_SKINNY = range(4)
 
 EXPORTED = (
-    "kl_version", "kl_last_error", "kl_gemm", "kl_gemm_workspace_size", "kl_gemm_ws",
+    "kl_version", "kl_last_error", "kl_gemm", "kl_gemm_workspace_size", "kl_gemm_ws", "kl_release_workspaces",
     "kl_set_wait_timeout_ns", "kl_read_status", "kl_probe_wait_timeout", "kl_smem_tile_offset",
     "kl_tma_box_geometry", "kl_tma_box_position", "kl_umma_smem_desc", "kl_mma_instr_desc",
     "kl_make_tma_desc", "kl_gemm_skinny_noalloc", "kl_gemm_host", "kl_gemm_clock_probe", "kl_gemm_gather",
@@ -90,6 +90,7 @@ def lib() -> ctypes.CDLL:
         P = ctypes.POINTER
         sig = {
             "kl_version": (i32, []),
+            "kl_release_workspaces": (i32, []),
             "kl_last_error": (ctypes.c_char_p, []),
             "kl_gemm": (i32, [P(GemmDesc), vp]),
             "kl_gemm_workspace_size": (i32, [P(GemmDesc), P(ctypes.c_size_t)]),
@@ -494,6 +495,12 @@ def workspace_size(a, b, c, **kw) -> int:
     n = ctypes.c_size_t()
     check(lib().kl_gemm_workspace_size(ctypes.byref(d), ctypes.byref(n)))
     return n.value
+
+
+def release_workspaces() -> None:
+    """Free the library's own workspaces (kl_release_workspaces): nothing that uses them may still
+    run or be replayed from a captured graph."""
+    check(lib().kl_release_workspaces())
 
 
 def read_status(clear=True) -> int:

@@ -210,6 +210,12 @@ extern "C" {
 
 int32_t kl_version(void) { return 100; }
 
+kl_status kl_release_workspaces(void) {
+  kl_status s = kl::capi::release_tile_workspaces();
+  if (s != KL_OK) return s;
+  return kl::capi::release_skinny_workspaces();
+}
+
 const char* kl_last_error(void) { return g_last_error.c_str(); }
 
 void kl_set_wait_timeout_ns(uint64_t ns) { g_timeout_ns = ns; }

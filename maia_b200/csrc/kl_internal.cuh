@@ -35,6 +35,11 @@ void mark_workspace_dirty(int device);
 kl_status tile_stream_k_workspace(cudaStream_t stream, void** out);
 void tile_workspaces_mark_dirty(int device);
 
+// kl_release_workspaces' two halves: free every library-owned workspace (after synchronising its
+// device) so the next call allocates afresh.
+kl_status release_skinny_workspaces();
+kl_status release_tile_workspaces();
+
 // Failure-path probe (kl_probe.cu).
 kl_status launch_wait_probe(int* status, unsigned long long timeout_ns, cudaStream_t stream);
 

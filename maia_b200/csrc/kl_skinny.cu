@@ -237,6 +237,23 @@ kl_status library_workspace(size_t need, size_t tickets, cudaStream_t stream, vo
 
 }  // namespace
 
+kl_status release_skinny_workspaces() {
+  std::lock_guard<std::mutex> lock(g_ws_mutex);
+  for (int dev = 0; dev < 64; ++dev) {
+    DeviceWorkspace& w = g_ws[dev];
+    if (w.ptr == nullptr) continue;
+    int prev = 0;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e == cudaSuccess) e = cudaSetDevice(dev);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();  // no launch may still use it
+    if (e == cudaSuccess) e = cudaFree(w.ptr);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return cuda_fail(e, "kl_release_workspaces (skinny)");
+    w = DeviceWorkspace{};
+  }
+  return KL_OK;
+}
+
 void mark_workspace_dirty(int device) {
   if (device < 0 || device >= 64) return;
   tile_workspaces_mark_dirty(device);

@@ -58,6 +58,25 @@ kl_status tile_stream_k_workspace(cudaStream_t stream, void** out) {
   return KL_OK;
 }
 
+kl_status release_tile_workspaces() {
+  std::lock_guard<std::mutex> lock(g_tile_ws_mutex);
+  if (g_tile_ws.empty()) return KL_OK;
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  while (e == cudaSuccess && !g_tile_ws.empty()) {
+    auto it = g_tile_ws.begin();
+    if (it->second.ptr != nullptr) {
+      e = cudaSetDevice(it->first.first);
+      if (e == cudaSuccess) e = cudaDeviceSynchronize();  // no launch may still use it
+      if (e == cudaSuccess) e = cudaFree(it->second.ptr);
+      if (e != cudaSuccess) break;
+    }
+    g_tile_ws.erase(it);
+  }
+  cudaSetDevice(prev);
+  return e == cudaSuccess ? KL_OK : cuda_fail(e, "kl_release_workspaces (split tail)");
+}
+
 void tile_workspaces_mark_dirty(int device) {
   std::lock_guard<std::mutex> lock(g_tile_ws_mutex);
   for (auto& [key, w] : g_tile_ws)

@@ -267,3 +267,9 @@ def test_quantisers_check_their_arguments():
     st = kl.lib().kl_nv_quantize(p, kl.KL_F32, 4, 64, 64, p, 48, p, p, ctypes.c_void_p(0))
     assert st == kl.KL_ERR_INVALID_ARGUMENT and "multiple of 32" in kl.last_error()
     assert kl.lib().kl_nv_quantize(p, kl.KL_F32, 0, 64, 64, p, 64, p, p, ctypes.c_void_p(0)) == kl.KL_OK
+
+
+def test_release_workspaces_with_none_allocated():
+    """Nothing allocated yet (no GPU here): a no-op that succeeds, twice."""
+    kl.release_workspaces()
+    kl.release_workspaces()
