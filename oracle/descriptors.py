@@ -83,6 +83,21 @@ def instr_desc(a: str, b: str, acc: str, m: int, n: int, a_major: int = 0, b_maj
             | (n >> 3) << 17 | (m >> 4) << 24)
 
 
+# Operand format codes of the block-scaled kinds: kind::mxf8f6f4 (e4m3 0, e5m2 1, e2m3 3, e3m2 4) and
+# kind::mxf4 / mxf4nvf4 (e2m1 1).
+BLOCK_SCALED_FORMAT = {"e4m3": 0, "e5m2": 1, "e2m3": 3, "e3m2": 4, "e2m1": 1}
+
+
+def instr_desc_block_scaled(a: str, b: str, m: int, n: int, a_sf_id: int = 0, b_sf_id: int = 0,
+                            ue4m3: bool = False) -> int:
+    """Instruction descriptor of a block-scaled tcgen05.mma (no counterpart in the reference; the
+    field layout of CuTe's InstrDescriptorBlockScaled): b_sf_id [4,6), a_fmt [7,10), b_fmt [10,13),
+    both operands K-major (bits 15, 16 clear), N >> 3 [17,23), scale format [23] (1 = UE8M0,
+    0 = UE4M3), M >> 4 [24,29), a_sf_id [29,31); no accumulator-format field (fp32 always)."""
+    return (b_sf_id << 4 | BLOCK_SCALED_FORMAT[a] << 7 | BLOCK_SCALED_FORMAT[b] << 10 | (n >> 3) << 17
+            | (0 if ue4m3 else 1) << 23 | (m >> 4) << 24 | a_sf_id << 29)
+
+
 def tma_encode_args(elem_bytes: int, tile_rows: int, tile_cols: int, swizzle: int, ptr: int, shape, stride):
     """The arguments kl::make_tma_desc hands to cuTensorMapEncodeTiled, or the exception message it
     raises (kernel_lib/include/kl/layout/tma_desc.hpp:114-152)."""

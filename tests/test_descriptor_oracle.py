@@ -69,3 +69,17 @@ def test_tma_args_and_errors():
     assert "multiples of 16 bytes" in od.tma_encode_args(2, 128, 64, 128, 0x10000, [4096, 4100], [4100, 1])
     assert "extents" in od.tma_encode_args(2, 128, 64, 128, 0x10000, [0, 4096], [4096, 1])
     assert isinstance(od.tma_encode_args(2, 128, 64, 128, 0x10000, [4096, 4096], [4160, 1]), dict)  # padded rows
+
+
+def test_block_scaled_instr_desc_matches_cute():
+    """The restated block-scaled layout against CuTe's make_instr_desc_block_scaled for every row
+    the reference dump holds (MXFP8, MXFP6, MXFP4, NVFP4; with and without scale-factor ids)."""
+    from golden_util import host_tables
+
+    rows = [t for t in host_tables() if t["kind"] == "idesc_block_scaled"]
+    assert len(rows) == 29
+    for d in rows:
+        a, _, sf = d["a"].partition("/")
+        b = d["b"].partition("/")[0]
+        got = od.instr_desc_block_scaled(a, b, d["m"], d["n"], d["a_sf_id"], d["b_sf_id"], ue4m3=sf == "ue4m3")
+        assert got == int(d["value"], 16), d
