@@ -1,8 +1,8 @@
 #pragma once
 
 // Persistent, warp-specialised dense GEMM for sm_100a:  C[M,N] (+)= alpha * A[M,K] . B[N,K]^T
-// (K-major operands by default, MN-major ones as options; C row-major), in bf16 / f16 / fp8 / fp4,
-// optionally block-scaled (MX, NVFP4), batched or m-grouped. No counterpart in the reference:
+// (K-major operands by default, MN-major ones as options; C row-major), in bf16 / f16 / fp8 /
+// fp6 / fp4, optionally block-scaled (MX, NVFP4), batched or m-grouped. No counterpart in the reference:
 // kernel_lib ships the descriptor encoders (tma_desc.hpp, umma_desc.hpp) this kernel is built
 // from, but no kernel.
 //
@@ -14,7 +14,8 @@
 // Two TMEM accumulators (2 x BlockN fp32 columns) let the epilogue of tile i overlap the main
 // loop of tile i + 1 (block-scaled 256-column tiles keep one; see kNumAcc). Tiles are walked
 // persistently in groups of `group_m` tile-rows so that the CTAs running at the same time share A
-// and B tiles in L2.
+// and B tiles in L2; when that leaves the last wave short, its tiles are cut into K-ranges and
+// summed through fp32 slots (the split tail, see TnArgs::sk_tiles and WorkSeq).
 //
 // CtaGroup = 2 runs a CTA pair (cluster of 2) on a 256-row tile with cta_group::2 MMAs: each CTA
 // loads its own 128 rows of A and its own half of B (no multicast), the even CTA issues the MMAs,
