@@ -13,6 +13,12 @@ exceed the 126 MB L2, so no flush runs between steps.
              in from pinned host memory and C back out, overlapped with the GEMM in column blocks.
   roofline   the GEMM kernel's achieved TFLOP/s against the measured dense bf16 (or fp8) peak.
   cpu_baseline  the CPU GEMM (fp32 accumulate, all host threads) on a bounded row slab.
+  workloads  the other two targets on the same line: the fp8 GEMM (16384 x 16384 x 8192 e4m3,
+             per-tensor scales, N-sharded like the headline) against twice the measured bf16
+             peak, and (one GPU) the decode shapes M = 16 / 64 / 128, N = 28672, K = 8192 bf16
+             against the measured copy bandwidth. Their operands are drawn on the device
+             (torch's generator, the same distributions and seeds as the workload definitions).
+  gather_check  (N > 1) the fused gather's full C compared bit for bit with the NCCL-gathered C.
 `--impl reference` times only the reference arm: the CPU GEMM restatement (the reference ships no
 GEMM of its own), rank 0 only.
 """
@@ -125,6 +131,109 @@ def cpu_baseline(w, budget_s: float = 6.0):
 METRIC = "GEMM TFLOP/s per B200 and % of tcgen05 dense peak"
 
 
+def timed(fn, steps: int, warmup: int, stream, device, sync):
+    """Device time per call of fn (CUDA events on `stream`, after `warmup` untimed calls), with the
+    NVML clock samples taken meanwhile."""
+    import torch
+
+    for _ in range(max(warmup, 3)):
+        fn()
+    sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index) as clocks:
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        sync()
+    return e0.elapsed_time(e1) / steps, clocks.summary()
+
+
+def extra_workloads(world, rank, dev, dist, peaks, peak_src, sync, max_over_ranks):
+    """The fp8 GEMM (every rank, N-sharded) and the decode shapes (rank 0 of a one-GPU run) on
+    device-drawn operands; one entry each for the JSON line's `workloads`."""
+    import torch
+
+    import maia_b200 as kl
+    from maia_b200 import sharding
+    from maia_b200 import workloads as wl
+
+    out = {}
+    stream = torch.cuda.current_stream(dev)
+
+    def normal(rows, cols, seed, scale):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        x = torch.randn((rows, cols), generator=g, device=dev, dtype=torch.float32)
+        return x.mul_(scale) if scale != 1.0 else x
+
+    # fp8 e4m3, per-tensor scales amax / 448, scale_a * scale_b applied in the epilogue, bf16 C.
+    w = wl.C4
+    n_lo, n_hi = sharding.shard_range(w.n, world, rank, align=256)
+    xa = normal(w.m, w.k, w.seed * 1000 + 0, w.a_scale)
+    sa = xa.abs().max() / 448.0
+    a = (xa / sa).to(torch.float8_e4m3fn)
+    del xa
+    xb = normal(w.n, w.k, w.seed * 1000 + 1, w.b_scale)
+    sb = xb.abs().max() / 448.0
+    b = (xb[n_lo:n_hi] / sb).to(torch.float8_e4m3fn)
+    del xb
+    scale_a = sa.reshape(1).float()
+    scale_b = sb.reshape(1).float()
+    c = torch.empty((w.m, n_hi - n_lo), dtype=torch.bfloat16, device=dev)
+    steps = 40
+    ms, clocks = timed(lambda: kl.gemm(a, b, c, scale_a=scale_a, scale_b=scale_b), steps, 3, stream, dev, sync)
+    in_kernel = kl.clock_probe(a, b, c, scale_a=scale_a, scale_b=scale_b)
+    if kl.read_status() != 0:
+        raise RuntimeError("a device-side wait timed out in the fp8 workload")
+    ms_all = max_over_ranks(ms)
+    per_rank = 2.0 * w.m * (n_hi - n_lo) * w.k
+    achieved = per_rank / (ms * 1e-3) / 1e12
+    peak = 2.0 * peaks["bf16_tflops"]
+    out[w.name] = {
+        "value": w.flops / (ms_all * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_all, "steps": steps,
+        "warmup": 3, "n_gpus": world, "dtype": "e4m3", "out": "bf16",
+        "data": "N(0,1) drawn on the device (torch generator, seeds 3000 / 3001), per-tensor amax/448 scales",
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": f"{peak_src} 2 x bf16_tflops (burst; the dense fp8 rate is twice bf16)",
+                     "algorithmic_flops_per_launch": per_rank},
+        "clocks": dict(clocks, in_kernel=in_kernel),
+        "gpu_launches": steps,
+    }
+    del a, b, c
+    torch.cuda.empty_cache()
+
+    if world == 1:
+        # Decode shapes: weights N(0,1) * 0.02, activations N(0,1), bf16 in and out; the skinny
+        # kernel or the one-CTA tile kernel, whichever KL_ALGO_AUTO picks (the library default).
+        w0 = wl.C5[16]
+        wgt = normal(w0.n, w0.k, w0.seed * 1000 + 1, w0.b_scale).to(torch.bfloat16)
+        for m, w in wl.C5.items():
+            x = normal(m, w.k, w.seed * 1000 + 0, w.a_scale).to(torch.bfloat16)
+            y = torch.empty((m, w.n), dtype=torch.bfloat16, device=dev)
+            steps = 300
+            ms, clocks = timed(lambda: kl.gemm(x, wgt, y), steps, 10, stream, dev, sync)
+            if kl.read_status() != 0:
+                raise RuntimeError("a device-side wait timed out in the decode workload")
+            alg = (m * w.k + w.n * w.k) * 2 + m * w.n * 2
+            achieved = alg / (ms * 1e-3) / 1e9
+            out[w.name] = {
+                "value": achieved, "unit": "GB/s", "ms_per_step": ms, "steps": steps, "warmup": 10, "n_gpus": 1,
+                "dtype": "bf16", "tflops": w.flops / (ms * 1e-3) / 1e12,
+                "route": {kl.ALGO_SKINNY: "skinny", kl.ALGO_1CTA: "one-CTA tile kernel",
+                          kl.ALGO_2CTA: "CTA-pair tile kernel"}[kl.resolve_algo(x, wgt, y)],
+                "data": "weights N(0,1)*0.02, activations N(0,1), drawn on the device (seeds 4001 / 4000)",
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                             "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peak_src} hbm_gbs",
+                             "algorithmic_bytes_per_launch": alg},
+                "clocks": clocks,
+                "gpu_launches": steps,
+                "l2": "weights (470 MB) exceed L2 (no flush)",
+            }
+        del wgt
+        torch.cuda.empty_cache()
+    return out
+
+
 def config_of(w, args, world):
     """The `config` both arms report: the workload and the launch knobs."""
     return {"workload": w.name, "m": w.m, "n": w.n, "k": w.k, "out": w.out,
@@ -173,6 +282,8 @@ def main():
     ap.add_argument("--stream-k", type=int, default=0, choices=[-1, 0, 1],
                     help="tile kernels' split tail: 0 = library default, 1 = always, -1 = whole tiles")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra-workloads", action="store_true",
+                    help="skip the fp8 and decode entries of `workloads` (run by default with the headline workload)")
     args = ap.parse_args()
 
     from maia_b200 import workloads as wl
@@ -307,6 +418,7 @@ def main():
 
     # ---- N > 1: the same GEMM followed by the NCCL all-gather of C (where the full C is needed)
     gather = None
+    gather_check = None
     if dist is not None:
         def gather_step():
             kl.gemm(a, b, c, **kw)
@@ -347,10 +459,35 @@ def main():
         f_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps)
         gather["fused"] = {"value": flops_total / (f_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": f_ms,
                            "what": "kl_gemm_gather: tiles stored to every rank's C by the GEMM epilogue (P2P over NVLink)"}
+        # Outside the timed region: every rank's kernels have finished (barrier), so its copy of the
+        # full C is complete. Compare it with the NCCL-gathered C of the plain GEMM, bit for bit (the
+        # same kernel and schedule produce both), on every rank.
+        barrier()
+        kl.gemm(a, b, c, **kw)
+        want = sharding.gather_columns(c, w.n, dist, align=256)
+        torch.cuda.synchronize(dev)
+        bits = torch.int16 if odt == torch.bfloat16 else torch.int32
+        same = torch.equal(shared.full.view(bits), want.view(bits))
+        diff = (shared.full.float() - want.float()).abs().max() / want.float().abs().max().clamp_min(1e-30)
+        flags = torch.tensor([1.0 if same else 0.0, float(diff)], dtype=torch.float64, device=dev)
+        lo = flags[:1].clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        hi = flags[1:].clone()
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        gather_check = {"fused_vs_nccl_bitexact": bool(lo.item() == 1.0), "max_rel_diff": float(hi.item()),
+                        "ranks": world}
+        del want
         barrier()
         shared.close()
+        if float(hi.item()) > 1e-2:
+            raise RuntimeError(f"the fused gather's C differs from the NCCL-gathered C: {gather_check}")
 
     peaks, peak_src = load_peaks()
+    extra = None
+    if args.workload == DEFAULT_WORKLOAD and not args.no_extra_workloads:
+        del a, b
+        torch.cuda.empty_cache()
+        extra = extra_workloads(world, rank, dev, dist, peaks, peak_src, barrier, max_over_ranks)
     per_rank_flops = 2.0 * w.m * nshard * w.k
     memory_bound = w.m <= 256
     if memory_bound:
@@ -388,7 +525,9 @@ def main():
             "roofline": roofline,
             "gpu_launches": args.steps,
             "gemm_plus_allgather": gather,
+            "gather_check": gather_check,
             "clocks": dict(clocks.summary(), in_kernel=in_kernel),
+            "workloads": extra,
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w)

@@ -185,7 +185,9 @@ KL_API kl_status kl_nv_quantize(const void* x, int32_t x_type, int64_t rows, int
 /* Frees every workspace the library allocated for kl_gemm (the skinny kernel's per-device buffer,
  * the tile kernels' per-stream split-tail buffers), after synchronising each device that has one;
  * later calls allocate afresh. No launch that uses them may be in flight or captured in a CUDA
- * graph that will still be replayed. KL_OK when there is nothing to free. */
+ * graph that will still be replayed. KL_OK when there is nothing to free. It also forgets the
+ * cached device address of kl_gemm_skinny_noalloc's scratch array: call it after resetting a device
+ * (cudaDeviceReset) and before the next kl_gemm_skinny_noalloc call on that device. */
 KL_API kl_status kl_release_workspaces(void);
 
 /* Library version: major * 10000 + minor * 100 + patch. */
@@ -201,6 +203,11 @@ KL_API kl_status kl_gemm(const kl_gemm_desc* desc, void* stream);
 /* No reference counterpart. Bytes of device workspace kl_gemm needs for `desc` (0 for every
  * algorithm except KL_ALGO_SKINNY, which keeps fp32 partial sums). */
 KL_API kl_status kl_gemm_workspace_size(const kl_gemm_desc* desc, size_t* bytes);
+
+/* No reference counterpart. The kernel family kl_gemm runs for `desc` (KL_ALGO_1CTA, KL_ALGO_2CTA
+ * or KL_ALGO_SKINNY): desc->algo, or the library's choice for KL_ALGO_AUTO. Reads only the
+ * descriptor's extents, types and options; launches nothing and needs no GPU. */
+KL_API kl_status kl_gemm_resolve_algo(const kl_gemm_desc* desc, int32_t* algo);
 
 /* No reference counterpart. Like kl_gemm, with caller-provided device workspace: at least
  * kl_gemm_workspace_size bytes, 16-byte aligned, zero-filled before its first use. Its head holds
@@ -236,9 +243,14 @@ KL_API kl_status kl_gemm_host(const kl_gemm_desc* desc, void* dev_a, void* dev_b
  * 32, 64, 128 or 256; at N = 28672 on a 148-SM B200 that is M <= 64); larger problems are
  * rejected with KL_ERR_INVALID_ARGUMENT and a message. The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress); make that first call before any stream capture.
+ * Under CUDA's lazy module loading (the default) that first call is also what loads the module
+ * holding the array, i.e. where its 16 MiB are committed: make it a warm-up call, made while
+ * memory is still free; it can fail with KL_ERR_CUDA (out of memory) where a later one cannot.
  * Every call shares the one array, which keeps the last call's contents: each call clears the
  * arrival counters it uses on `stream` before its kernel, and calls that overlap on the GPU race
- * on the array, so serialise them. desc->algo must be KL_ALGO_AUTO or KL_ALGO_SKINNY. */
+ * on the array, so serialise them. desc->algo must be KL_ALGO_AUTO or KL_ALGO_SKINNY;
+ * desc->variant 0 or 1 (both the one-box kernel; variant 2 is KL_ERR_NOT_SUPPORTED here); C
+ * aligned to its element size. A call that is rejected queues nothing on `stream`. */
 KL_API kl_status kl_gemm_skinny_noalloc(const kl_gemm_desc* desc, void* stream);
 
 /* No reference counterpart. The tile-kernel GEMM (KL_ALGO_1CTA / 2CTA) whose epilogue also writes

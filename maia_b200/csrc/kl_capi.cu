@@ -204,13 +204,49 @@ kl_status check_tile(int32_t elem_bytes, int32_t rows, int32_t cols, int32_t spa
   return KL_OK;
 }
 
+// The kernel family kl_gemm runs for `d`: desc->algo, or KL_ALGO_AUTO resolved. m-grouped GEMMs
+// run on the tile kernels (the one-CTA kernel takes any 128-row grouping; the CTA pair needs groups
+// padded to 256 rows, since it reads the group of each tile's first block, so it runs only when
+// asked for); batched, MN-major and non-default-swizzle problems on the tile kernels; the rest by
+// the size rule of choose_algo.
+kl_status resolve_algo(kl_gemm_desc const& d, int* out) {
+  const int64_t batch = d.batch > 1 ? d.batch : 1;
+  const bool a_mn = d.a_major == 1, b_mn = d.b_major == 1;
+  const bool default_swizzle = d.swizzle == 0 || d.swizzle == 128;
+  int algo = d.algo;
+  if (d.m_block_group != nullptr) {
+    if (algo != KL_ALGO_AUTO && algo != KL_ALGO_1CTA && algo != KL_ALGO_2CTA)
+      return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: m-grouped GEMMs run on the tile kernels (KL_ALGO_1CTA / 2CTA)");
+    if (batch > 1 || a_mn || b_mn)
+      return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: m-grouped GEMMs take K-major operands, batch 1");
+    if (algo == KL_ALGO_AUTO) algo = KL_ALGO_1CTA;
+  }
+  if (algo == KL_ALGO_AUTO && d.block_scale != 0)
+    algo = kl::capi::choose_algo(d);
+  else if (algo == KL_ALGO_AUTO)
+    algo = (batch > 1 || a_mn || b_mn || !default_swizzle) ? (d.m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA)
+                                                           : kl::capi::choose_algo(d);
+  *out = algo;
+  return KL_OK;
+}
+
 }  // namespace
 
 extern "C" {
 
 int32_t kl_version(void) { return 100; }
 
+kl_status kl_gemm_resolve_algo(const kl_gemm_desc* d, int32_t* algo) {
+  if (d == nullptr || algo == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null argument");
+  if (d->m <= 0 || d->n <= 0 || d->k <= 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_resolve_algo: empty problem");
+  int a = KL_ALGO_AUTO;
+  kl_status s = resolve_algo(*d, &a);
+  if (s == KL_OK) *algo = a;
+  return s;
+}
+
 kl_status kl_release_workspaces(void) {
+  kl::capi::forget_noalloc_scratch();
   kl_status s = kl::capi::release_tile_workspaces();
   if (s != KL_OK) return s;
   return kl::capi::release_skinny_workspaces();
@@ -257,21 +293,9 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
   const bool default_swizzle = d->swizzle == 0 || d->swizzle == 128;
   if (d->reserved2 != 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: reserved fields must be 0");
   if (d->stream_k < -1 || d->stream_k > 1) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: stream_k must be -1, 0 or 1");
-  int algo = d->algo;
-  if (d->m_block_group != nullptr) {
-    // The one-CTA kernel takes any 128-row grouping; the CTA pair needs groups padded to 256 rows
-    // (it reads the group of each tile's first block), so it is used only when asked for.
-    if (algo != KL_ALGO_AUTO && algo != KL_ALGO_1CTA && algo != KL_ALGO_2CTA)
-      return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: m-grouped GEMMs run on the tile kernels (KL_ALGO_1CTA / 2CTA)");
-    if (batch > 1 || a_mn || b_mn)
-      return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: m-grouped GEMMs take K-major operands, batch 1");
-    if (algo == KL_ALGO_AUTO) algo = KL_ALGO_1CTA;
-  }
-  if (algo == KL_ALGO_AUTO && d->block_scale != 0)
-    algo = kl::capi::choose_algo(*d);
-  else if (algo == KL_ALGO_AUTO)
-    algo = (batch > 1 || a_mn || b_mn || !default_swizzle) ? (d->m >= 256 ? KL_ALGO_2CTA : KL_ALGO_1CTA)
-                                                           : kl::capi::choose_algo(*d);
+  int algo = KL_ALGO_AUTO;
+  kl_status rs = resolve_algo(*d, &algo);
+  if (rs != KL_OK) return rs;
   if (algo == KL_ALGO_SKINNY && batch > 1) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: KL_ALGO_SKINNY is not batched");
   if (algo == KL_ALGO_SKINNY && (a_mn || b_mn))
     return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm: KL_ALGO_SKINNY takes K-major operands");

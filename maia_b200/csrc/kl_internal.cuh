@@ -39,6 +39,9 @@ void tile_workspaces_mark_dirty(int device);
 // device) so the next call allocates afresh.
 kl_status release_skinny_workspaces();
 kl_status release_tile_workspaces();
+// Drops the cached device addresses of kl_gemm_skinny_noalloc's scratch array (looked up again on
+// the next call).
+void forget_noalloc_scratch();
 
 // Failure-path probe (kl_probe.cu).
 kl_status launch_wait_probe(int* status, unsigned long long timeout_ns, cudaStream_t stream);

@@ -48,7 +48,8 @@ static __device__ __align__(256) unsigned char kl_noalloc_scratch[kScratchBytes]
 template <typename InT, typename OutT, int Tok>
 using Skinny = SkinnyConfig<InT, OutT, Tok, (Tok == 16 ? 11 : Tok == 32 ? 10 : Tok == 64 ? 8 : Tok == 128 ? 6 : 4)>;
 
-// Device address of kl_noalloc_scratch, per device.
+// Device address of kl_noalloc_scratch, per device. Cleared by kl_release_workspaces, so that a
+// caller who resets a device (which unloads the module holding the array) can look it up again.
 std::mutex g_mutex;
 unsigned char* g_scratch[64] = {};
 
@@ -66,6 +67,8 @@ kl_status setup_device(int dev, unsigned char** out) {
   return KL_OK;
 }
 
+// Encodes the tensor maps first (they can reject the call), then queues the ticket clear and the
+// kernel: a rejected call leaves nothing on the stream.
 template <class Cfg>
 kl_status launch(kl_gemm_desc const& d, int n_tiles, int k_blocks, int grid, unsigned char* scratch,
                  cudaStream_t stream) {
@@ -105,8 +108,14 @@ kl_status launch(kl_gemm_desc const& d, int n_tiles, int k_blocks, int grid, uns
   a.timeout_ns = kl::capi::wait_timeout_ns();
   a.prefetch = d.prefetch > 0 ? d.prefetch : d.prefetch < 0 ? 0 : kDefaultPrefetchSkinny;
   a.c_reduce = d.c_reduce;
+  // The arrival tickets this call uses must start at zero. The kernel re-arms them when it
+  // finishes, but a kernel stopped by a timed-out wait would leave them mid-count, and the array
+  // keeps whatever the last call left; so clear them on the stream, ahead of the kernel. The
+  // partial-sum slots need no clearing: each is written before it is read.
+  cudaError_t e = cudaMemsetAsync(scratch, 0, size_t(n_tiles) * 16, stream);
+  if (e != cudaSuccess) return kl::capi::cuda_fail(e, "cudaMemsetAsync(no-alloc tickets)");
   gemm_skinny_kernel<Cfg><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
+  e = cudaGetLastError();
   return e == cudaSuccess ? KL_OK : kl::capi::cuda_fail(e, "no-alloc skinny launch");
 }
 
@@ -123,6 +132,13 @@ kl_status dispatch(kl_gemm_desc const& d, int tok, int n_tiles, int k_blocks, in
 }
 
 }  // namespace
+
+namespace kl::capi {
+void forget_noalloc_scratch() {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  for (auto& p : g_scratch) p = nullptr;
+}
+}  // namespace kl::capi
 
 extern "C" kl_status kl_gemm_skinny_noalloc(const kl_gemm_desc* d, void* stream_ptr) {
   using kl::capi::fail;
@@ -145,6 +161,18 @@ extern "C" kl_status kl_gemm_skinny_noalloc(const kl_gemm_desc* d, void* stream_
   if (d->a == nullptr || d->b == nullptr || d->c == nullptr)
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_skinny_noalloc: null A, B or C");
   if (d->ldc < d->n) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_skinny_noalloc: ldc < n");
+  if (reinterpret_cast<uintptr_t>(d->c) % (d->c_type == KL_F32 ? 4 : 2) != 0)
+    return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_skinny_noalloc: C is not aligned to its element size");
+  // Variant 2 (two 128-row weight boxes per stage) has no no-alloc build; 0 and 1 both name the
+  // one-box kernel that kl_gemm runs for them.
+  if (d->variant != 0 && d->variant != 1)
+    return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_skinny_noalloc: variant must be 0 or 1");
+  const bool bf16_bf16 = d->ab_type == KL_BF16 && d->c_type == KL_BF16;
+  const bool bf16_f32 = d->ab_type == KL_BF16 && d->c_type == KL_F32;
+  const bool e4m3_bf16 = d->ab_type == KL_E4M3 && d->c_type == KL_BF16;
+  if (!bf16_bf16 && !bf16_f32 && !e4m3_bf16)
+    return fail(KL_ERR_NOT_SUPPORTED,
+                "kl_gemm_skinny_noalloc supports (A/B, C) = (bf16, bf16), (bf16, f32), (e4m3, bf16)");
 
   int dev = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -177,21 +205,11 @@ extern "C" kl_status kl_gemm_skinny_noalloc(const kl_gemm_desc* d, void* stream_
   unsigned char* scratch = nullptr;
   kl_status s = setup_device(dev, &scratch);
   if (s != KL_OK) return s;
-  // The arrival tickets this call uses must start at zero. The kernel re-arms them when it
-  // finishes, but a kernel stopped by a timed-out wait would leave them mid-count, and the array
-  // keeps whatever the last call left; so clear them on the stream, ahead of the kernel. The
-  // partial-sum slots need no clearing: each is written before it is read.
-  e = cudaMemsetAsync(scratch, 0, size_t(n_tiles) * 16, stream);
-  if (e != cudaSuccess) return kl::capi::cuda_fail(e, "cudaMemsetAsync(no-alloc tickets)");
   try {
-    if (d->ab_type == KL_BF16 && d->c_type == KL_BF16)
-      return dispatch<kl::bf16, kl::bf16>(*d, tok, n_tiles, k_blocks, grid, scratch, stream);
-    if (d->ab_type == KL_BF16 && d->c_type == KL_F32)
-      return dispatch<kl::bf16, float>(*d, tok, n_tiles, k_blocks, grid, scratch, stream);
-    if (d->ab_type == KL_E4M3 && d->c_type == KL_BF16)
-      return dispatch<kl::e4m3, kl::bf16>(*d, tok, n_tiles, k_blocks, grid, scratch, stream);
+    if (bf16_bf16) return dispatch<kl::bf16, kl::bf16>(*d, tok, n_tiles, k_blocks, grid, scratch, stream);
+    if (bf16_f32) return dispatch<kl::bf16, float>(*d, tok, n_tiles, k_blocks, grid, scratch, stream);
+    return dispatch<kl::e4m3, kl::bf16>(*d, tok, n_tiles, k_blocks, grid, scratch, stream);
   } catch (std::invalid_argument const& ex) {
     return fail(KL_ERR_INVALID_ARGUMENT, ex.what());
   }
-  return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_skinny_noalloc supports (A/B, C) = (bf16, bf16), (bf16, f32), (e4m3, bf16)");
 }

@@ -117,15 +117,21 @@ def f32_to_e4m3_bits(x: np.ndarray) -> np.ndarray:
     moves into the exponent) and rebias the exponent from 127 to 7. Below 2^-6 the e4m3 grid is
     uniform (step 2^-9), so the pattern is the rounded multiple of 2^-9."""
     x = np.ascontiguousarray(x, dtype=np.float32)
-    u = x.view(np.uint32)
-    sign = ((u >> 24) & np.uint32(0x80)).astype(np.uint8)
-    mag = u & np.uint32(0x7FFFFFFF)
-    rounded = (mag + np.uint32(0x7FFFF) + ((mag >> 20) & np.uint32(1))) >> 20
-    normal = rounded.astype(np.int64) - (120 << 3)
-    sub = np.rint(np.abs(x).astype(np.float64) * 512.0).astype(np.int64)  # rint: ties to even
-    q = np.where(mag < np.uint32(0x3C800000), sub, normal)               # 0x3C800000 = 2^-6
-    q = np.clip(q, 0, 0x7E).astype(np.uint8)
-    return np.where(q != 0, q | sign, q).astype(np.uint8)
+    flat = x.reshape(-1)
+    out = np.empty(flat.shape, dtype=np.uint8)
+    for i in range(0, flat.size, 1 << 22):  # bounded temporaries on large matrices
+        v = flat[i:i + (1 << 22)]
+        u = v.view(np.uint32)
+        sign = ((u >> 24) & np.uint32(0x80)).astype(np.uint8)
+        mag = u & np.uint32(0x7FFFFFFF)
+        rounded = (mag + np.uint32(0x7FFFF) + ((mag >> 20) & np.uint32(1))) >> 20
+        normal = rounded.astype(np.int32) - (120 << 3)
+        # Below 2^-6 (0x3C800000) the value times 512 is below 8: exact in float32, rint ties to even.
+        sub = np.rint(np.minimum(np.abs(v), np.float32(1.0)) * np.float32(512.0)).astype(np.int32)
+        q = np.where(mag < np.uint32(0x3C800000), sub, normal)
+        q = np.clip(q, 0, 0x7E).astype(np.uint8)
+        out[i:i + v.size] = np.where(q != 0, q | sign, q)
+    return out.reshape(x.shape)
 
 
 def f32_to_e4m3_bits_nearest(x: np.ndarray) -> np.ndarray:
@@ -164,15 +170,21 @@ def f32_to_e5m2_bits(x: np.ndarray) -> np.ndarray:
     As for e4m3: keep 2 mantissa bits of the float32 pattern with round-to-nearest-even and rebias
     the exponent from 127 to 15; below 2^-14 the grid is uniform with step 2^-16."""
     x = np.ascontiguousarray(x, dtype=np.float32)
-    u = x.view(np.uint32)
-    sign = ((u >> 24) & np.uint32(0x80)).astype(np.uint8)
-    mag = u & np.uint32(0x7FFFFFFF)
-    rounded = (mag + np.uint32(0xFFFFF) + ((mag >> 21) & np.uint32(1))) >> 21
-    normal = rounded.astype(np.int64) - (112 << 2)
-    sub = np.rint(np.minimum(np.abs(x).astype(np.float64), 1.0) * 65536.0).astype(np.int64)
-    q = np.where(mag < np.uint32(0x38800000), sub, normal)                # 0x38800000 = 2^-14
-    q = np.clip(q, 0, 0x7B).astype(np.uint8)
-    return np.where(q != 0, q | sign, q).astype(np.uint8)
+    flat = x.reshape(-1)
+    out = np.empty(flat.shape, dtype=np.uint8)
+    for i in range(0, flat.size, 1 << 22):  # bounded temporaries on large matrices
+        v = flat[i:i + (1 << 22)]
+        u = v.view(np.uint32)
+        sign = ((u >> 24) & np.uint32(0x80)).astype(np.uint8)
+        mag = u & np.uint32(0x7FFFFFFF)
+        rounded = (mag + np.uint32(0xFFFFF) + ((mag >> 21) & np.uint32(1))) >> 21
+        normal = rounded.astype(np.int32) - (112 << 2)
+        # Below 2^-14 the value times 65536 is below 4: exact in float32, rint ties to even.
+        sub = np.rint(np.minimum(np.abs(v), np.float32(1.0)) * np.float32(65536.0)).astype(np.int32)
+        q = np.where(mag < np.uint32(0x38800000), sub, normal)
+        q = np.clip(q, 0, 0x7B).astype(np.uint8)
+        out[i:i + v.size] = np.where(q != 0, q | sign, q)
+    return out.reshape(x.shape)
 
 
 def f32_to_e5m2_bits_nearest(x: np.ndarray) -> np.ndarray:

@@ -273,3 +273,25 @@ def test_release_workspaces_with_none_allocated():
     """Nothing allocated yet (no GPU here): a no-op that succeeds, twice."""
     kl.release_workspaces()
     kl.release_workspaces()
+
+
+@pytest.mark.parametrize("m, n, k, ab, c, want", [
+    (16, 28672, 8192, "KL_BF16", "KL_BF16", "ALGO_SKINNY"),
+    (64, 28672, 8192, "KL_BF16", "KL_BF16", "ALGO_SKINNY"),
+    (128, 28672, 8192, "KL_BF16", "KL_BF16", "ALGO_1CTA"),
+    (128, 28672, 8192, "KL_E4M3", "KL_BF16", "ALGO_SKINNY"),
+    (8192, 8192, 8192, "KL_BF16", "KL_BF16", "ALGO_2CTA"),
+    (16384, 16384, 8192, "KL_E4M3", "KL_BF16", "ALGO_2CTA"),
+])
+def test_resolve_algo_names_the_default_route(kl, m, n, k, ab, c, want):
+    """kl_gemm_resolve_algo reports the kernel family KL_ALGO_AUTO runs, with no GPU and no launch."""
+    import ctypes
+
+    d = kl.GemmDesc(m=m, n=n, k=k, a=0x1000, lda=k, b=0x2000, ldb=k, c=0x3000, ldc=n, ab_type=getattr(kl, ab),
+                    c_type=getattr(kl, c), alpha=1.0, algo=kl.ALGO_AUTO)
+    out = ctypes.c_int32(-1)
+    assert kl.lib().kl_gemm_resolve_algo(ctypes.byref(d), ctypes.byref(out)) == kl.KL_OK
+    assert out.value == getattr(kl, want)
+    d.algo = kl.ALGO_SKINNY
+    assert kl.lib().kl_gemm_resolve_algo(ctypes.byref(d), ctypes.byref(out)) == kl.KL_OK
+    assert out.value == kl.ALGO_SKINNY

@@ -29,6 +29,16 @@ def test_c5_decode_shapes(cuda, m, variant):
     check(c, a, b, 1.0, BF16_TOL)
 
 
+@pytest.mark.parametrize("m", [16, 64, 128])
+def test_c5_decode_shapes_default_route(cuda, m):
+    """The decode configs through KL_ALGO_AUTO, the route the benchmark times (the skinny kernel
+    up to 64 rows, the one-CTA tile kernel over 112 weight bands at 128), every entry against
+    the fp64 oracle."""
+    w = wl.C5[m]
+    a, b, _, _ = wl.make_inputs(w)
+    check(run_kl(a, b, "bf16", "bf16", cuda, kl.ALGO_AUTO), a, b, 1.0, BF16_TOL)
+
+
 @pytest.mark.parametrize("variant", [1, 2], ids=["w128", "w256"])
 @pytest.mark.parametrize("shape", [(1, 8, 64), (5, 136, 200), (17, 1000, 512), (33, 640, 1096), (100, 384, 2048),
                                    (200, 256, 640), (256, 520, 320), (128, 128, 64)])
