@@ -131,14 +131,38 @@ def cpu_baseline(w, budget_s: float = 6.0):
 METRIC = "GEMM TFLOP/s per B200 and % of tcgen05 dense peak"
 
 
-def timed(fn, steps: int, warmup: int, stream, device, sync):
+def nvlink_bytes(index: int):
+    """(transmitted, received) NVLink data bytes of GPU `index` so far, all links, from NVML's
+    throughput counters (read-only), or None where NVML does not report them."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByIndex(index)
+        ids = [(pynvml.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_TX, 0xFFFFFFFF),
+               (pynvml.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_RX, 0xFFFFFFFF)]
+        vals = pynvml.nvmlDeviceGetFieldValues(h, ids)
+        if any(v.nvmlReturn != 0 for v in vals):
+            return None
+        return tuple(int(v.value.ullVal) * 1024 for v in vals)
+    except Exception:
+        return None
+
+
+def timed(fn, steps: int, warmup: int, stream, device, sync, nvlink: bool = False):
     """Device time per call of fn (CUDA events on `stream`, after `warmup` untimed calls), with the
-    NVML clock samples taken meanwhile."""
+    NVML clock samples taken meanwhile; with nvlink=True also the NVLink bytes per call this GPU
+    sent and received (NVML counters read around the timed calls, after a pause that lets them
+    settle)."""
     import torch
 
     for _ in range(max(warmup, 3)):
         fn()
     sync()
+    link0 = None
+    if nvlink:
+        time.sleep(0.3)
+        link0 = nvlink_bytes(device.index)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(device.index) as clocks:
         e0.record(stream)
@@ -146,6 +170,15 @@ def timed(fn, steps: int, warmup: int, stream, device, sync):
             fn()
         e1.record(stream)
         sync()
+    link = None
+    if link0 is not None:
+        time.sleep(0.3)
+        link1 = nvlink_bytes(device.index)
+        if link1 is not None:
+            link = {"tx_bytes_per_step": (link1[0] - link0[0]) / steps, "rx_bytes_per_step": (link1[1] - link0[1]) / steps,
+                    "source": "NVML NVLink data throughput counters (all links), read around the timed calls"}
+    if nvlink:
+        return e0.elapsed_time(e1) / steps, clocks.summary(), link
     return e0.elapsed_time(e1) / steps, clocks.summary()
 
 
@@ -181,7 +214,7 @@ def extra_workloads(world, rank, dev, dist, peaks, peak_src, sync, max_over_rank
     scale_b = sb.reshape(1).float()
     c = torch.empty((w.m, n_hi - n_lo), dtype=torch.bfloat16, device=dev)
     steps = 40
-    ms, clocks = timed(lambda: kl.gemm(a, b, c, scale_a=scale_a, scale_b=scale_b), steps, 3, stream, dev, sync)
+    ms, clocks = timed(kl.gemm_launcher(a, b, c, scale_a=scale_a, scale_b=scale_b), steps, 3, stream, dev, sync)
     in_kernel = kl.clock_probe(a, b, c, scale_a=scale_a, scale_b=scale_b)
     if kl.read_status() != 0:
         raise RuntimeError("a device-side wait timed out in the fp8 workload")
@@ -211,7 +244,7 @@ def extra_workloads(world, rank, dev, dist, peaks, peak_src, sync, max_over_rank
             x = normal(m, w.k, w.seed * 1000 + 0, w.a_scale).to(torch.bfloat16)
             y = torch.empty((m, w.n), dtype=torch.bfloat16, device=dev)
             steps = 300
-            ms, clocks = timed(lambda: kl.gemm(x, wgt, y), steps, 10, stream, dev, sync)
+            ms, clocks = timed(kl.gemm_launcher(x, wgt, y), steps, 10, stream, dev, sync)
             if kl.read_status() != 0:
                 raise RuntimeError("a device-side wait timed out in the decode workload")
             alg = (m * w.k + w.n * w.k) * 2 + m * w.n * 2
@@ -356,8 +389,7 @@ def main():
               variant=args.variant, max_ctas=args.max_ctas, sfa=sfa, sfb=sfb, scale_vec=vec,
               ab_type=wl.MX_ELEMENT[w.dtype] if w.dtype == "mxfp6" else None, stream_k=args.stream_k)
 
-    def step():
-        kl.gemm(a, b, c, **kw)
+    step = kl.gemm_launcher(a, b, c, **kw)  # one kl_gemm per call, the descriptor built once
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -394,16 +426,31 @@ def main():
     value = flops_total / (dev_ms * 1e-3) / 1e12
 
     # ---- end to end through the public API with host buffers
-    h2d = a_host.numel() * a_host.element_size() + b_host.numel() * b_host.element_size()
-    if mx:
-        h2d += sfa_host.numel() + sfb_host.numel()
     d2h = c.numel() * c.element_size()
+    e2e_how = "kl_gemm_host: all of A and this rank's B copied in, C's block copied out, pipelined over column blocks"
+    if dist is not None and not mx:
+        # Each rank copies only its slab of A's rows in and the ranks all-gather A over NVLink, while
+        # the B shard streams in (sharding.HostShardedGemm over kl_gemm_host_b).
+        hs = sharding.HostShardedGemm(w.m, nshard, w.k, tdt, odt, dev, dist)
+        s_lo, s_hi = hs.slab_rows()
+        a_slab_host = a_host[s_lo:s_hi]
+        h2d = a_slab_host.numel() * a_slab_host.element_size() + b_host.numel() * b_host.element_size()
+        e2e_how = ("sharding.HostShardedGemm: this rank's slab of A's rows copied in and all-gathered over NVLink "
+                   "(NCCL), B's shard streamed in and C's block out through kl_gemm_host_b")
 
-    def e2e_step():
-        # The host-buffer entry point: copies in, GEMM and copy out, pipelined over column blocks.
-        kl.gemm_host(a_host, b_host, c_host, a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo,
-                     sfa=sfa_host, sfb=sfb_host, scale_vec=vec, chunks=args.chunks, ab_type=kw["ab_type"],
-                     stream_k=args.stream_k)
+        def e2e_step():
+            hs(a_slab_host, b_host, c_host, scale_a=scale_a, scale_b=scale_b, algo=args.algo, chunks=args.chunks,
+               stream_k=args.stream_k)
+    else:
+        h2d = a_host.numel() * a_host.element_size() + b_host.numel() * b_host.element_size()
+        if mx:
+            h2d += sfa_host.numel() + sfb_host.numel()
+
+        def e2e_step():
+            # The host-buffer entry point: copies in, GEMM and copy out, pipelined over column blocks.
+            kl.gemm_host(a_host, b_host, c_host, a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo,
+                         sfa=sfa_host, sfb=sfb_host, scale_vec=vec, chunks=args.chunks, ab_type=kw["ab_type"],
+                         stream_k=args.stream_k)
 
     for _ in range(max(args.warmup, 3)):
         e2e_step()
@@ -415,6 +462,18 @@ def main():
     e1.record(stream)
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    # Outside the timed region: the host-side C of the last step against the device-resident GEMM's C
+    # (column blocks may split the tail differently, so agreement is to fp32 rounding, not bits).
+    if not mx:
+        step()
+        torch.cuda.synchronize(dev)
+        ref_c = c.float()
+        e2e_diff = float((c_host.to(dev).float() - ref_c).abs().max() / ref_c.abs().max().clamp_min(1e-30))
+        if e2e_diff > 1e-2:
+            raise RuntimeError(f"the host-buffer path's C differs from the device GEMM's: {e2e_diff:.3e}")
+        del ref_c
+    else:
+        e2e_diff = None
 
     # ---- N > 1: the same GEMM followed by the NCCL all-gather of C (where the full C is needed)
     gather = None
@@ -427,15 +486,11 @@ def main():
         for _ in range(max(args.warmup, 3)):
             gather_step()
         barrier()
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        g0.record(stream)
-        for _ in range(args.steps):
-            gather_step()
-        g1.record(stream)
-        barrier()
-        g_ms = max_over_ranks(g0.elapsed_time(g1) / args.steps)
+        g_ms, _, g_link = timed(gather_step, args.steps, 0, stream, dev, barrier, nvlink=True)
+        g_ms = max_over_ranks(g_ms)
         gather = {"value": flops_total / (g_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": g_ms,
-                  "what": "kl_gemm + NCCL all-gather of C and re-layout to [M, N] on every rank"}
+                  "what": "kl_gemm + NCCL all-gather of C and re-layout to [M, N] on every rank",
+                  "nvlink_rank0": g_link}
 
         # The same result with the gather fused into the GEMM: every tile is also TMA-stored into
         # the other ranks' copies of C over NVLink (kl_gemm_gather).
@@ -450,15 +505,11 @@ def main():
         for _ in range(max(args.warmup, 3)):
             fused_step()
         barrier()
-        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        f0.record(stream)
-        for _ in range(args.steps):
-            fused_step()
-        f1.record(stream)
-        barrier()
-        f_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps)
+        f_ms, _, f_link = timed(fused_step, args.steps, 0, stream, dev, barrier, nvlink=True)
+        f_ms = max_over_ranks(f_ms)
         gather["fused"] = {"value": flops_total / (f_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": f_ms,
-                           "what": "kl_gemm_gather: tiles stored to every rank's C by the GEMM epilogue (P2P over NVLink)"}
+                           "what": "kl_gemm_gather: tiles stored to every rank's C by the GEMM epilogue (P2P over NVLink)",
+                           "nvlink_rank0": f_link}
         # Outside the timed region: every rank's kernels have finished (barrier), so its copy of the
         # full C is complete. Compare it with the NCCL-gathered C of the plain GEMM, bit for bit (the
         # same kernel and schedule produce both), on every rank.
@@ -476,11 +527,44 @@ def main():
         dist.all_reduce(hi, op=dist.ReduceOp.MAX)
         gather_check = {"fused_vs_nccl_bitexact": bool(lo.item() == 1.0), "max_rel_diff": float(hi.item()),
                         "ranks": world}
-        del want
         barrier()
         shared.close()
-        if float(hi.item()) > 1e-2:
-            raise RuntimeError(f"the fused gather's C differs from the NCCL-gathered C: {gather_check}")
+
+        # The same through an NVLink multicast object: each tile stored once, the switch delivering it
+        # to every rank's C (kl_gemm_gather_multicast).
+        mcc = sharding.MulticastC(w.m, w.n, odt, dev, dist)
+        mc_bad = None
+        if mcc.available:
+            mc_view = mcc.full[:, n_lo:n_hi]
+            mc_addr = mcc.mc_ptr(n_lo)
+
+            def mc_step():
+                kl.gemm_gather_multicast(a, b, mc_view, mc_addr, scale_a=scale_a, scale_b=scale_b, algo=args.algo,
+                                         sfa=sfa, sfb=sfb, scale_vec=vec, stream_k=args.stream_k)
+
+            m_ms, _, m_link = timed(mc_step, args.steps, args.warmup, stream, dev, barrier, nvlink=True)
+            m_ms = max_over_ranks(m_ms)
+            barrier()
+            same = torch.equal(mcc.full.view(bits), want.view(bits))
+            mdiff = float((mcc.full.float() - want.float()).abs().max() / want.float().abs().max().clamp_min(1e-30))
+            flags = torch.tensor([1.0 if same else 0.0], dtype=torch.float64, device=dev)
+            dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+            md = torch.tensor([mdiff], dtype=torch.float64, device=dev)
+            dist.all_reduce(md, op=dist.ReduceOp.MAX)
+            gather_check["multicast_vs_nccl_bitexact"] = bool(flags.item() == 1.0)
+            gather_check["multicast_max_rel_diff"] = float(md.item())
+            mc_bad = float(md.item()) > 1e-2
+            gather["multicast"] = {"value": flops_total / (m_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": m_ms,
+                                   "what": "kl_gemm_gather_multicast: each tile stored once through an NVLink "
+                                           "multicast address (multimem.st), the switch writing every rank's C",
+                                   "nvlink_rank0": m_link}
+        else:
+            gather["multicast"] = {"unavailable": mcc.reason}
+        mcc.close()
+        del want
+        barrier()
+        if float(hi.item()) > 1e-2 or mc_bad:
+            raise RuntimeError(f"a fused gather's C differs from the NCCL-gathered C: {gather_check}")
 
     peaks, peak_src = load_peaks()
     extra = None
@@ -521,7 +605,8 @@ def main():
             "dtype": w.dtype, "data": "synthetic",
             "config": config_of(w, args, world),
             "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "what": e2e_how,
+                    "max_rel_diff_vs_device": e2e_diff},
             "roofline": roofline,
             "gpu_launches": args.steps,
             "gemm_plus_allgather": gather,

@@ -35,6 +35,11 @@ struct Problem {
   // process): the epilogue TMA-stores every tile there too. Not with the direct-store epilogue.
   void* const* peer_c = nullptr;
   int n_peers = 0;
+  // NVLink multicast address of C (the same element (0, 0) and pitch as `c`, in a buffer bound to a
+  // multicast object on every GPU): the epilogue writes every tile there once with multimem stores
+  // instead of TMA-storing it to `c` and the peers. One problem, C = result, no peer copies; base,
+  // pitch and width of C multiples of 16 bytes.
+  void* mc_c = nullptr;
   // Batched GEMM: `batch` independent problems, A/B/C matrix b at a/b/c + b * stride_*.
   int64_t batch = 1;
   int64_t stride_a = 0, stride_b = 0, stride_c = 0;  // elements
@@ -282,6 +287,14 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
                                  : make_tma_store<typename Cfg::CBox>(row_major_strided(pc, pr.m, pr.n, pr.ldc)).map;
   }
   p.n_peers = pr.n_peers;
+  if (pr.mc_c != nullptr) {
+    if (Cfg::kDirectStore || pr.c_reduce != 0 || pr.batch > 1 || pr.n_peers > 0)
+      throw std::invalid_argument(
+          "kl::gemm: multicast C takes the staged epilogue, one problem, C = result and no peer copies");
+    if (reinterpret_cast<uintptr_t>(pr.mc_c) % 16 != 0 || (pr.ldc * int64_t(sizeof(OutT))) % 16 != 0 ||
+        (pr.n * int64_t(sizeof(OutT))) % 16 != 0)
+      throw std::invalid_argument("kl::gemm: multicast C needs its base, pitch and width in multiples of 16 bytes");
+  }
 
   TnArgs& a = p.args;
   a.m = int(pr.m);
@@ -305,6 +318,7 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   a.batch_stride_c = pr.stride_c;
   a.c_reduce = pr.c_reduce;
   a.m_block_group = pr.m_block_group;
+  a.mc_c = pr.mc_c;
   if constexpr (Cfg::kMx) {
     if (pr.sfa == nullptr || pr.sfb == nullptr) throw std::invalid_argument("kl::gemm: block scaling needs scales of A and B");
     if (pr.batch > 1) throw std::invalid_argument("kl::gemm: block-scaled GEMMs are not batched");

@@ -34,6 +34,7 @@
 
 #include <kl/arch/cluster.hpp>
 #include <kl/arch/mbarrier.hpp>
+#include <kl/arch/multimem.hpp>
 #include <kl/arch/tcgen05.hpp>
 #include <kl/arch/tma.hpp>
 #include <kl/kl.hpp>
@@ -196,6 +197,11 @@ struct TnArgs {
   int sk_split;
   int* sk_tickets;              // [sk_tiles * CtaGroup * kEpiWarps], zero between launches
   float* sk_slots;              // [sk_tiles * sk_split * CtaGroup][128 * BlockN]
+  // NVLink multicast address of C's element (0, 0) (pitch ldc), or nullptr. When set, every
+  // finished chunk of C is read back from its staging buffer and written once with multimem
+  // stores, which land in the C of every GPU bound to the multicast object (this one's included):
+  // the column-sharded GEMM leaves the whole C everywhere and each GPU sends its shard once.
+  void* mc_c;
 };
 
 // One piece of work: K-blocks [kb0, kb1) of tile t; q = its K-range (0 for a whole tile).
@@ -272,6 +278,12 @@ KL_DEVICE void record_status(int* status, int bit) { atomicOr(status, bit); }
 
 KL_DEVICE void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+KL_DEVICE uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
+  return v;
 }
 
 KL_DEVICE uint32_t ld_shared_u32(uint32_t addr) {
@@ -721,7 +733,25 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) {
+        if (args.mc_c != nullptr) {
+          // Multicast C: the warp reads its 32 staged rows back, four rows of 128 bytes per pass
+          // (lane = 8 x row-in-pass + 16-byte piece), and stores every piece once to the multicast
+          // address, coalesced along the rows. The host checks that the base, the pitch and the
+          // width of C are multiples of 16 bytes, so a piece is wholly in or out of C.
+          if (store) {
+            const int piece = lane & 7;
+            const int pcol = col + piece * (16 / int(sizeof(OutT)));
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+              const int r = it * 4 + (lane >> 3);
+              const uint4 x = ld_shared_v4(buf + uint32_t(r) * 128u + ((uint32_t(piece) ^ uint32_t(r & 7)) << 4));
+              if (row0 + r < args.m && pcol < args.n)
+                multimem_st_v4(static_cast<OutT*>(args.mc_c) + (long long)(row0 + r) * args.ldc + pcol, x.x, x.y, x.z,
+                               x.w);
+            }
+          }
+          __syncwarp();  // every lane's reads of this buffer before any lane writes it again
+        } else if (lane == 0) {
           if (store) {
             if (args.c_reduce && sizeof(OutT) == 4) {
               // C += tile on an fp32 C: the TMA unit reads C, adds the staged values and writes back.
@@ -871,6 +901,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
     if constexpr (!Cfg::kDirectStore) {
       if (lane == 0) tma_store_wait<0>();
     }
+    if (args.mc_c != nullptr) multimem_fence();  // this thread's multicast stores, before the kernel ends
   }
 
   // ------------------------------------------------------------------ teardown

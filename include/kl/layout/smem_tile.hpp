@@ -105,9 +105,11 @@ struct SmemTensor {
   KL_HOST_DEVICE static constexpr Layout layout() { return {}; }
 };
 
-// A swizzled, row-major (cols contiguous) tile in shared memory. MMA operands are (M or N, K), so
-// they are K-major. The tile owns its storage, so it can be a plain member of a kernel's shared
-// memory struct. Members as in kernel_lib/include/kl/layout/smem_tile.hpp:48-76.
+// Rows x Cols elements of T in shared memory, each row's Cols elements contiguous and the 16-byte
+// chunks of every 8-row group permuted by the swizzle Sw. Used for the operands of an MMA, whose
+// rows are M (or N) and whose columns run along K. The storage is an aligned array inside the
+// struct itself, so a kernel lays out its shared memory by declaring tiles as members. The member
+// names follow kernel_lib/include/kl/layout/smem_tile.hpp:48-76.
 template <typename T, int Rows, int Cols, typename Sw = Swizzle128B>
 struct SmemTile {
   using value_type = T;

@@ -29,7 +29,10 @@ enum class UmmaLayout : uint8_t {
   SWIZZLE_32B = 6,
 };
 
-// 64-bit UMMA shared-memory descriptor.
+// 64-bit UMMA shared-memory descriptor. The union's field names and its lo / hi view follow CuTe's
+// UMMA::SmemDescriptor (CUTLASS, Copyright (c) 2017 - 2025 NVIDIA CORPORATION & AFFILIATES, BSD-3-
+// Clause licence), because callers of the reference read those names; the bit positions are the
+// hardware's.
 //   [0,14)  start address >> 4        [16,30) leading byte offset >> 4
 //   [32,46) stride byte offset >> 4   [46,48) version (1 on sm_100)
 //   [49,52) base offset               [52]    LBO mode
@@ -68,10 +71,12 @@ KL_HOST_DEVICE constexpr uint64_t encode_smem_desc(uint32_t start_bytes, uint32_
          (uint64_t(static_cast<uint8_t>(layout) & 7u) << 61);
 }
 
-// K covered by one dense tcgen05.mma (kind::f16, tf32, f8f6f4, i8): always 32 bytes.
+// Elements of K that a single dense tcgen05.mma consumes: the instruction reads 32 bytes of every
+// operand row whatever the kind (f16, tf32, f8f6f4, i8), so 16 for 16-bit types, 32 for 8-bit.
 template <typename T>
 inline constexpr int mma_k = 256 / bits_of<T>;
 
+// MMAs needed to cover the K extent (the columns) of one operand tile.
 template <SmemTileType Tile>
 inline constexpr int num_k_blocks = Tile::cols / mma_k<typename Tile::value_type>;
 

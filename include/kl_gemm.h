@@ -233,6 +233,16 @@ KL_API kl_status kl_gemm_ws(const kl_gemm_desc* desc, void* workspace, size_t wo
 KL_API kl_status kl_gemm_host(const kl_gemm_desc* desc, void* dev_a, void* dev_b, void* dev_c, int32_t chunks,
                               void* stream);
 
+/* No reference counterpart. kl_gemm_host with A already in device memory: desc->a (and desc->sfa
+ * when block-scaled) are DEVICE pointers, desc->b, desc->c (and desc->sfb) host pointers staged
+ * through dev_b / dev_c as in kl_gemm_host. The copies of B start once the work already on `stream`
+ * is done; the GEMMs also wait for `a_ready` (a cudaEvent_t the caller recorded after whatever
+ * produces A, e.g. an all-gather of A's row slabs from the other GPUs; NULL = none). This is the
+ * per-GPU half of an end-to-end N-sharded GEMM in which each GPU copies only its slab of A over
+ * PCIe. */
+KL_API kl_status kl_gemm_host_b(const kl_gemm_desc* desc, void* a_ready, void* dev_b, void* dev_c, int32_t chunks,
+                                void* stream);
+
 /* No counterpart in the reference. The skinny (KL_ALGO_SKINNY) GEMM for callers that may not
  * allocate device memory while they run and cannot lend the library a workspace (for example an
  * inference-runtime plugin that is handed only its input and output tensors, or a serving loop
@@ -261,6 +271,38 @@ KL_API kl_status kl_gemm_skinny_noalloc(const kl_gemm_desc* desc, void* stream);
  * transfers overlap the next tiles' math. The kernel only stores to peer memory. Before reading C,
  * every rank's kernel must have finished (e.g. a stream-ordered collective after this call). */
 KL_API kl_status kl_gemm_gather(const kl_gemm_desc* desc, void* const* peer_c, int32_t n_peers, void* stream);
+
+/* No reference counterpart. The same gather through NVLink multicast: `mc_c` is the multicast
+ * address of desc->c (the same element and pitch, in a buffer bound to an NVSwitch multicast object
+ * on every GPU of the group, e.g. torch's symmetric memory `multicast_ptr` plus desc->c's offset).
+ * The epilogue writes every finished tile once with multimem stores, which the switch delivers to
+ * every GPU's copy of C, this one's included, so each GPU sends its shard once instead of once per
+ * peer. Tile kernels (KL_ALGO_1CTA / 2CTA, AUTO picks), one problem, C = result (c_reduce 0); the
+ * base, pitch and width of C multiples of 16 bytes. Before another GPU reads C, this GPU's kernel
+ * must have finished and a synchronisation across the GPUs must order that read after it (e.g. a
+ * collective queued on `stream` after this call). */
+KL_API kl_status kl_gemm_gather_multicast(const kl_gemm_desc* desc, void* mc_c, void* stream);
+
+/* ---- Bounded collectives for the N-sharded path. No counterpart in the reference (it has no
+ * multi-GPU code); the failure contract follows its status-code style (tma_desc.hpp:134-152 throws,
+ * this ABI returns codes). An NCCL communicator created non-blocking: initialisation, enqueueing
+ * and completion are polled against a host deadline, and NCCL's asynchronous errors are read on
+ * every poll. When the deadline passes (a rank has left, a link is down) or an error shows, the
+ * communicator is aborted, which also ends its kernels still waiting on the GPU, the stream is
+ * drained, and the call returns KL_ERR_TIMEOUT or KL_ERR_NCCL instead of hanging; every later use
+ * of the communicator returns KL_ERR_NCCL. NCCL is loaded at run time (the libnccl.so.2 already in
+ * the process, else the system's); without it these return KL_ERR_NOT_SUPPORTED. */
+typedef struct kl_comm kl_comm;
+/* 128 bytes that every rank passes to kl_comm_init (made on one rank, sent to the others). */
+KL_API kl_status kl_comm_get_unique_id(void* id);
+KL_API kl_status kl_comm_init(const void* id, int32_t world, int32_t rank, int64_t timeout_ms, kl_comm** comm);
+/* recv (world x bytes) = every rank's `bytes` of send, in rank order; queued on `stream`. */
+KL_API kl_status kl_comm_all_gather(kl_comm* comm, const void* send, void* recv, int64_t bytes, void* stream);
+/* Waits until `stream` (with the communicator's collectives on it) is done, at most timeout_ms. */
+KL_API kl_status kl_comm_wait(kl_comm* comm, void* stream, int64_t timeout_ms);
+KL_API int32_t kl_comm_is_aborted(const kl_comm* comm);
+/* Finalises (waiting at most timeout_ms for the other ranks) and frees; an aborted one is only freed. */
+KL_API kl_status kl_comm_destroy(kl_comm* comm, int64_t timeout_ms);
 
 /* CUDA IPC for peer copies of C: a 64-byte handle of the device allocation that contains dev_ptr
  * plus dev_ptr's byte offset inside it; kl_ipc_open_handle maps the allocation in another process

@@ -33,10 +33,12 @@ EXPORTED = (
     "kl_version", "kl_last_error", "kl_gemm", "kl_gemm_workspace_size", "kl_gemm_resolve_algo", "kl_gemm_ws", "kl_release_workspaces",
     "kl_set_wait_timeout_ns", "kl_read_status", "kl_probe_wait_timeout", "kl_smem_tile_offset",
     "kl_tma_box_geometry", "kl_tma_box_position", "kl_umma_smem_desc", "kl_mma_instr_desc",
-    "kl_make_tma_desc", "kl_gemm_skinny_noalloc", "kl_gemm_host", "kl_gemm_clock_probe", "kl_gemm_gather",
+    "kl_make_tma_desc", "kl_gemm_skinny_noalloc", "kl_gemm_host", "kl_gemm_host_b", "kl_gemm_clock_probe", "kl_gemm_gather", "kl_gemm_gather_multicast",
     "kl_ipc_get_handle", "kl_ipc_open_handle", "kl_ipc_close", "kl_umma_smem_desc_mn", "kl_mma_instr_desc_major",
     "kl_mma_instr_desc_block_scaled", "kl_mx_scale_bytes", "kl_mx_pack_scales", "kl_block_scale_bytes",
     "kl_pack_block_scales", "kl_mx_quantize", "kl_nv_quantize",
+    "kl_comm_get_unique_id", "kl_comm_init", "kl_comm_all_gather", "kl_comm_wait", "kl_comm_is_aborted",
+    "kl_comm_destroy",
 )
 
 
@@ -107,8 +109,10 @@ def lib() -> ctypes.CDLL:
             "kl_make_tma_desc": (i32, [i32, i32, i32, i32, i32, vp, i32, P(i64), P(i64), vp]),
             "kl_gemm_skinny_noalloc": (i32, [P(GemmDesc), vp]),
             "kl_gemm_host": (i32, [P(GemmDesc), vp, vp, vp, i32, vp]),
+            "kl_gemm_host_b": (i32, [P(GemmDesc), vp, vp, vp, i32, vp]),
             "kl_gemm_clock_probe": (i32, [P(GemmDesc), P(u64), i32, P(i32), vp]),
             "kl_gemm_gather": (i32, [P(GemmDesc), P(vp), i32, vp]),
+            "kl_gemm_gather_multicast": (i32, [P(GemmDesc), vp, vp]),
             "kl_ipc_get_handle": (i32, [vp, vp, P(i64)]),
             "kl_ipc_open_handle": (i32, [vp, P(vp)]),
             "kl_ipc_close": (i32, [vp]),
@@ -121,6 +125,12 @@ def lib() -> ctypes.CDLL:
             "kl_pack_block_scales": (i32, [vp, i64, i64, i32, i64, vp, vp]),
             "kl_mx_quantize": (i32, [vp, i32, i64, i64, i64, i32, vp, i64, vp, vp]),
             "kl_nv_quantize": (i32, [vp, i32, i64, i64, i64, vp, i64, vp, vp, vp]),
+            "kl_comm_get_unique_id": (i32, [vp]),
+            "kl_comm_init": (i32, [vp, i32, i32, i64, P(vp)]),
+            "kl_comm_all_gather": (i32, [vp, vp, vp, i64, vp]),
+            "kl_comm_wait": (i32, [vp, vp, i64]),
+            "kl_comm_is_aborted": (i32, [vp]),
+            "kl_comm_destroy": (i32, [vp, i64]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -312,6 +322,28 @@ def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=Non
     return out
 
 
+def gemm_launcher(a, b, out, *, stream=None, **kw):
+    """A zero-argument callable that queues out = a @ b.T (the options of `gemm`) with a descriptor
+    built once: each call is one kl_gemm through the C ABI, for loops where the launch itself must
+    cost the host as little as possible (short decode-shaped GEMMs). The tensors must stay alive and
+    in place while the callable is used."""
+    import torch
+
+    accumulate = kw.pop("accumulate", False)
+    d = gemm_desc(a, b, out, c_reduce=int(bool(accumulate)), **kw)
+    s = ctypes.c_void_p(stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream)
+    ref = ctypes.byref(d)
+    fn = lib().kl_gemm
+
+    def launch():
+        st = fn(ref, s)
+        if st != KL_OK:
+            check(st)
+
+    launch.desc = d  # keeps the descriptor alive with the callable
+    return launch
+
+
 def block_scale_bytes(rows: int, k: int, vec: int = 32) -> int:
     """Bytes of the blocked scale array for `rows` rows of `k` K-elements, one scale per `vec`."""
     return int(lib().kl_block_scale_bytes(int(rows), int(k), int(vec)))
@@ -436,6 +468,23 @@ def gemm_host(a_host, b_host, c_host, a_dev, b_dev, c_dev, *, alpha=1.0, scale_a
     return c_host
 
 
+def gemm_host_b(a_dev, b_host, c_host, b_dev, c_dev, *, a_ready=None, alpha=1.0, scale_a=None, scale_b=None,
+                algo=ALGO_AUTO, chunks=0, sfa=None, sfb=None, scale_vec=32, ab_type=None, stream_k=0, stream=None):
+    """c_host = alpha * a_dev @ b_host.T with A already on the device and B, C in host memory, through
+    kl_gemm_host_b: B streams in over b_dev in column blocks while the GEMMs (which also wait for the
+    recorded torch.cuda.Event `a_ready`, if given) and the copies of C back to c_host follow. sfa is
+    then A's device-side blocked scales, sfb B's host-side ones. Queues the work only."""
+    import torch
+
+    d = gemm_desc(a_dev, b_host, c_host, alpha, scale_a, scale_b, algo, sfa=sfa, sfb=sfb, scale_vec=scale_vec,
+                  ab_type=ab_type, stream_k=stream_k)
+    s = stream if stream is not None else torch.cuda.current_stream(a_dev.device).cuda_stream
+    ev = ctypes.c_void_p(a_ready.cuda_event) if a_ready is not None else None
+    check(lib().kl_gemm_host_b(ctypes.byref(d), ev, ctypes.c_void_p(b_dev.data_ptr()),
+                               ctypes.c_void_p(c_dev.data_ptr()), int(chunks), ctypes.c_void_p(s)))
+    return c_host
+
+
 def gemm_gather(a, b, c_shard, peer_ptrs, *, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
                 group_m=0, max_ctas=0, sfa=None, sfb=None, scale_vec=32, ab_type=None, stream_k=0, stream=None):
     """c_shard = alpha * a @ b.T, and the same tiles written to each peer pointer (a view of the same
@@ -447,6 +496,21 @@ def gemm_gather(a, b, c_shard, peer_ptrs, *, alpha=1.0, scale_a=None, scale_b=No
     arr = (ctypes.c_void_p * max(1, len(peer_ptrs)))(*[ctypes.c_void_p(p) for p in peer_ptrs])
     s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
     check(lib().kl_gemm_gather(ctypes.byref(d), arr, len(peer_ptrs), ctypes.c_void_p(s)))
+    return c_shard
+
+
+def gemm_gather_multicast(a, b, c_shard, mc_ptr, *, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
+                          group_m=0, max_ctas=0, sfa=None, sfb=None, scale_vec=32, ab_type=None, stream_k=0,
+                          stream=None):
+    """c_shard = alpha * a @ b.T written once through `mc_ptr`, the NVLink multicast address of
+    c_shard's first element (kl_gemm_gather_multicast): every GPU bound to the multicast object gets
+    the tiles in its copy of C, this one's included."""
+    import torch
+
+    d = gemm_desc(a, b, c_shard, alpha, scale_a, scale_b, algo, group_m, max_ctas, sfa=sfa, sfb=sfb,
+                  scale_vec=scale_vec, ab_type=ab_type, stream_k=stream_k)
+    s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
+    check(lib().kl_gemm_gather_multicast(ctypes.byref(d), ctypes.c_void_p(mc_ptr), ctypes.c_void_p(s)))
     return c_shard
 
 

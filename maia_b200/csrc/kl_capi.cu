@@ -76,6 +76,9 @@ using E4m3Bf16_1 = TnConfig<kl::e4m3, kl::bf16, 1, 256, 4>;
 using Bf16Bf16_2 = TnConfig<kl::bf16, kl::bf16, 2, 256, 6>;
 using Bf16F32_2 = TnConfig<kl::bf16, float, 2, 256, 6>;
 using E4m3Bf16_2 = TnConfig<kl::e4m3, kl::bf16, 2, 256, 6>;
+// CTA pair, 256 x 128 tiles (variant 2): twice the tiles of the 256 x 256 kernel, for narrow
+// column shards whose 256-wide tiles leave the last wave short; 8 stages of 24 KB per CTA.
+using Bf16Bf16_2n128 = TnConfig<kl::bf16, kl::bf16, 2, 128, 8>;
 
 template <class Cfg>
 kl_status run(Problem const& pr, cudaStream_t stream, LaunchInfo* info = nullptr) {
@@ -127,8 +130,10 @@ kl_status run_tile(kl_gemm_desc const& d, Problem const& pr, bool pair, cudaStre
     if (handled) return s;
     return fail(KL_ERR_NOT_SUPPORTED, std::string(who) + ": 64- and 32-byte operand swizzle take bf16 inputs and bf16 or f32 C");
   }
-  if (d.ab_type == KL_BF16 && d.c_type == KL_BF16)
+  if (d.ab_type == KL_BF16 && d.c_type == KL_BF16) {
+    if (pair && d.variant == 2) return run<Bf16Bf16_2n128>(pr, stream, info);
     return pair ? run<Bf16Bf16_2>(pr, stream, info) : run<Bf16Bf16_1>(pr, stream, info);
+  }
   if (d.ab_type == KL_BF16 && d.c_type == KL_F32)
     return pair ? run<Bf16F32_2>(pr, stream, info) : run<Bf16F32_1>(pr, stream, info);
   if (d.ab_type == KL_E4M3 && d.c_type == KL_BF16)
@@ -336,6 +341,33 @@ kl_status kl_gemm_gather(const kl_gemm_desc* d, void* const* peer_c, int32_t n_p
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   try {
     return run_tile(*d, pr, algo == KL_ALGO_2CTA, stream, nullptr, "kl_gemm_gather");
+  } catch (std::invalid_argument const& ex) {
+    return fail(KL_ERR_INVALID_ARGUMENT, ex.what());
+  } catch (std::exception const& ex) {
+    return fail(KL_ERR_CUDA, ex.what());
+  }
+}
+
+kl_status kl_gemm_gather_multicast(const kl_gemm_desc* d, void* mc_c, void* stream_ptr) {
+  if (d == nullptr || mc_c == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null argument");
+  g_last_error.clear();
+  if (d->m < 0 || d->n < 0 || d->k < 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather_multicast: negative extent");
+  if (d->m == 0 || d->n == 0) return KL_OK;  // an empty shard: nothing to compute or send
+  if (d->k == 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather_multicast: k must be positive");
+  if (d->a == nullptr || d->b == nullptr || d->c == nullptr)
+    return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather_multicast: null A, B or C");
+  if (d->c_reduce != 0) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_gather_multicast: C = result only (c_reduce 0)");
+  if (d->batch > 1) return fail(KL_ERR_NOT_SUPPORTED, "kl_gemm_gather_multicast: one problem per call");
+  int algo = d->algo;
+  if (algo == KL_ALGO_AUTO || algo == KL_ALGO_SKINNY)
+    algo = (d->m >= 256 && d->m_block_group == nullptr) ? KL_ALGO_2CTA : KL_ALGO_1CTA;
+  if (algo != KL_ALGO_1CTA && algo != KL_ALGO_2CTA)
+    return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_gather_multicast: unknown algo");
+  Problem pr = problem_of(*d);
+  pr.mc_c = mc_c;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  try {
+    return run_tile(*d, pr, algo == KL_ALGO_2CTA, stream, nullptr, "kl_gemm_gather_multicast");
   } catch (std::invalid_argument const& ex) {
     return fail(KL_ERR_INVALID_ARGUMENT, ex.what());
   } catch (std::exception const& ex) {

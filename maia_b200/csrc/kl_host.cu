@@ -2,7 +2,9 @@
 // device, then streams B in column blocks of C, so that the host-to-device copies of block j+1,
 // the GEMM of block j and the device-to-host copy of block j-1 run at the same time on three
 // streams (two copy engines and the SMs). Chained with events; ordered after and before the
-// caller's stream. Block-scaled problems (block_scale 1 or 2) also stage the blocked scale arrays: A's whole,
+// caller's stream. kl_gemm_host_b is the same with A already on the device (a sharded caller
+// gathers it from the other GPUs over NVLink instead of copying all of it over PCIe on every GPU):
+// the B copies start at once and the GEMMs also wait for the caller's "A ready" event. Block-scaled problems (block_scale 1 or 2) also stage the blocked scale arrays: A's whole,
 // then B's row blocks along with each block of B.
 
 #include <cuda_runtime.h>
@@ -58,13 +60,13 @@ int elem_bytes(int32_t t) {
   return (t == KL_BF16 || t == KL_F16) ? 2 : (t == KL_E4M3 || t == KL_E5M2 || t == KL_I8 || t == KL_U8) ? 1 : 4;
 }
 
-}  // namespace
-
-extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_b, void* dev_c, int32_t chunks,
-                                  void* stream_ptr) {
+// Both entry points. copy_a: A (and its scales) come from the host into dev_a; otherwise desc->a
+// (and desc->sfa) are device pointers already, and the GEMMs also wait for `a_ready` (if given).
+kl_status host_gemm(const kl_gemm_desc* h, void* dev_a, bool copy_a, cudaEvent_t a_ready, void* dev_b, void* dev_c,
+                    int32_t chunks, void* stream_ptr) {
   using kl::capi::cuda_fail;
   using kl::capi::fail;
-  if (h == nullptr || dev_a == nullptr || dev_b == nullptr || dev_c == nullptr)
+  if (h == nullptr || (copy_a && dev_a == nullptr) || dev_b == nullptr || dev_c == nullptr || (!copy_a && h->a == nullptr))
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_host: null argument");
   if (h->m <= 0 || h->n <= 0 || h->k <= 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_host: m, n and k must be positive");
   if (h->lda < h->k || h->ldb < h->k || h->ldc < h->n) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_host: leading dimension too small");
@@ -105,7 +107,7 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
   };
   // Block scales: blocked arrays, A's then B's, in one staging buffer.
   const int32_t vec = h->block_scale == 2 ? 16 : 32;
-  const int64_t sfa_bytes = mx ? kl_block_scale_bytes(h->m, h->k, vec) : 0;
+  const int64_t sfa_bytes = (mx && copy_a) ? kl_block_scale_bytes(h->m, h->k, vec) : 0;
   const int64_t sfb_bytes = mx ? kl_block_scale_bytes(h->n, h->k, vec) : 0;
   const int64_t sf_row_block = ((h->k + 4 * vec - 1) / (4 * vec)) * 512;  // bytes per 128 rows
   if (mx && p->scale_bytes < size_t(sfa_bytes + sfb_bytes)) {
@@ -131,10 +133,14 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
   // Start after everything already queued on the caller's stream.
   if ((e = cudaEventRecord(p->start, caller)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   if ((e = cudaStreamWaitEvent(p->in, p->start, 0)) != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
-  if ((e = cudaMemcpyAsync(da, ha, ab_bytes(h->m * h->lda), cudaMemcpyHostToDevice, p->in)) != cudaSuccess)
-    return cuda_fail(e, "kl_gemm_host: copy of A");
-  if (mx && (e = cudaMemcpyAsync(dsfa, h->sfa, size_t(sfa_bytes), cudaMemcpyHostToDevice, p->in)) != cudaSuccess)
-    return cuda_fail(e, "kl_gemm_host: copy of A's scales");
+  if (copy_a) {
+    if ((e = cudaMemcpyAsync(da, ha, ab_bytes(h->m * h->lda), cudaMemcpyHostToDevice, p->in)) != cudaSuccess)
+      return cuda_fail(e, "kl_gemm_host: copy of A");
+    if (mx && (e = cudaMemcpyAsync(dsfa, h->sfa, size_t(sfa_bytes), cudaMemcpyHostToDevice, p->in)) != cudaSuccess)
+      return cuda_fail(e, "kl_gemm_host: copy of A's scales");
+  } else if (a_ready != nullptr) {
+    if ((e = cudaStreamWaitEvent(p->mm, a_ready, 0)) != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent(A ready)");
+  }
   for (int j = 0; j < chunks; ++j) {
     const int64_t n0 = int64_t(j) * block, nj = std::min<int64_t>(block, h->n - n0);
     e = cudaMemcpyAsync(db + ab_bytes(n0 * h->ldb), hb + ab_bytes(n0 * h->ldb), ab_bytes(nj * h->ldb),
@@ -151,11 +157,11 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
     if ((e = cudaStreamWaitEvent(p->mm, p->loaded[j], 0)) != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
     kl_gemm_desc d = *h;
     d.n = nj;
-    d.a = da;
+    d.a = copy_a ? da : h->a;
     d.b = db + ab_bytes(n0 * h->ldb);
     d.c = dc + size_t(n0) * ec;
     if (mx) {
-      d.sfa = dsfa;
+      d.sfa = copy_a ? dsfa : h->sfa;
       d.sfb = dsfb + sf_off;
     }
     s = kl_gemm(&d, p->mm);
@@ -170,4 +176,16 @@ extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_
   if ((e = cudaEventRecord(p->done, p->out)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   if ((e = cudaStreamWaitEvent(caller, p->done, 0)) != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
   return KL_OK;
+}
+
+}  // namespace
+
+extern "C" kl_status kl_gemm_host(const kl_gemm_desc* h, void* dev_a, void* dev_b, void* dev_c, int32_t chunks,
+                                  void* stream_ptr) {
+  return host_gemm(h, dev_a, true, nullptr, dev_b, dev_c, chunks, stream_ptr);
+}
+
+extern "C" kl_status kl_gemm_host_b(const kl_gemm_desc* h, void* a_ready, void* dev_b, void* dev_c, int32_t chunks,
+                                    void* stream_ptr) {
+  return host_gemm(h, nullptr, false, static_cast<cudaEvent_t>(a_ready), dev_b, dev_c, chunks, stream_ptr);
 }

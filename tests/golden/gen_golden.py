@@ -1,9 +1,9 @@
 """Regenerate the golden descriptor fixtures from the reference itself.
 
-Run in a checkout that has the reference sources (REF_ROOT, default /root/reference) and the
-CUTLASS/CuTe headers:
+Run with REF_ROOT naming a checkout of the reference sources (the directory holding kernel_lib/;
+there is no default) and the CUTLASS/CuTe headers importable through flashinfer:
 
-    python tests/golden/gen_golden.py
+    REF_ROOT=<maia checkout> python tests/golden/gen_golden.py
 
 1. ref_host_tables.json: oracle/_ref/ref_host_dump, i.e. the reference's own headers
    (kernel_lib/include/kl) compiled against CuTe 4.5.0, evaluated on the host: smem layouts
@@ -32,15 +32,26 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
-REF_ROOT = Path(os.environ.get("REF_ROOT", "/root/reference"))
+# The reference checkout (its kernel_lib/ sources); given by the caller, e.g.
+#   REF_ROOT=<maia checkout> python tests/golden/gen_golden.py
+_REF_ENV = os.environ.get("REF_ROOT")
+REF_ROOT = Path(_REF_ENV) if _REF_ENV else None
 
 
 def sha(values) -> str:
     return hashlib.sha256(np.asarray(values, dtype="<i8").tobytes()).hexdigest()
 
 
+def require_ref_root() -> Path:
+    if REF_ROOT is None or not (REF_ROOT / "kernel_lib" / "include").is_dir():
+        sys.exit("gen_golden: set REF_ROOT to a checkout of the reference (the directory holding kernel_lib/); "
+                 f"got {_REF_ENV!r}")
+    return REF_ROOT
+
+
 def host_tables() -> list:
-    subprocess.run(["make", "-C", str(ROOT / "oracle"), "ref"], check=True)
+    ref = require_ref_root()
+    subprocess.run(["make", "-C", str(ROOT / "oracle"), "ref", f"REF={ref / 'kernel_lib' / 'include'}"], check=True)
     with tempfile.TemporaryDirectory() as tmp:
         out = Path(tmp) / "t.json"
         subprocess.run([str(ROOT / "oracle" / "_ref" / "ref_host_dump"), str(out)], check=True,
@@ -117,9 +128,7 @@ def known_answers() -> list:
 
 
 def main() -> int:
-    if not REF_ROOT.exists():
-        print(f"reference sources not found at {REF_ROOT}", file=sys.stderr)
-        return 1
+    require_ref_root()
     (HERE / "ref_host_tables.json").write_text(json.dumps(host_tables(), indent=1) + "\n")
     (HERE / "ref_test_known_answers.json").write_text(json.dumps(known_answers(), indent=1) + "\n")
     print("wrote", HERE / "ref_host_tables.json", HERE / "ref_test_known_answers.json")

@@ -295,3 +295,19 @@ def test_resolve_algo_names_the_default_route(kl, m, n, k, ab, c, want):
     d.algo = kl.ALGO_SKINNY
     assert kl.lib().kl_gemm_resolve_algo(ctypes.byref(d), ctypes.byref(out)) == kl.KL_OK
     assert out.value == kl.ALGO_SKINNY
+
+
+def test_gather_multicast_argument_checks(kl):
+    """kl_gemm_gather_multicast's checks that need no GPU: a null multicast address, C += result and
+    batched problems are refused before anything is queued."""
+    import ctypes
+
+    d = kl.GemmDesc(m=512, n=1024, k=512, a=0x1000, lda=512, b=0x2000, ldb=512, c=0x3000, ldc=2048,
+                    ab_type=kl.KL_BF16, c_type=kl.KL_BF16, alpha=1.0, algo=kl.ALGO_AUTO)
+    assert kl.lib().kl_gemm_gather_multicast(ctypes.byref(d), None, None) == kl.KL_ERR_INVALID_ARGUMENT
+    d.c_reduce = 1
+    assert kl.lib().kl_gemm_gather_multicast(ctypes.byref(d), ctypes.c_void_p(0x4000), None) == kl.KL_ERR_NOT_SUPPORTED
+    d.c_reduce, d.batch = 0, 2
+    assert kl.lib().kl_gemm_gather_multicast(ctypes.byref(d), ctypes.c_void_p(0x4000), None) == kl.KL_ERR_NOT_SUPPORTED
+    d.batch, d.m = 0, 0  # an empty shard: nothing to do
+    assert kl.lib().kl_gemm_gather_multicast(ctypes.byref(d), ctypes.c_void_p(0x4000), None) == kl.KL_OK
