@@ -149,13 +149,17 @@ def nvlink_bytes(index: int):
         return None
 
 
-def timed(fn, steps: int, warmup: int, stream, device, sync, nvlink: bool = False):
+def timed(fn, steps: int, warmup: int, stream, device, sync, nvlink: bool = False, settle_s: float = 0.0):
     """Device time per call of fn (CUDA events on `stream`, after `warmup` untimed calls), with the
     NVML clock samples taken meanwhile; with nvlink=True also the NVLink bytes per call this GPU
     sent and received (NVML counters read around the timed calls, after a pause that lets them
-    settle)."""
+    settle). settle_s: an idle pause first, so that a workload does not start in the power state the
+    previous one left."""
     import torch
 
+    if settle_s > 0:
+        sync()
+        time.sleep(settle_s)
     for _ in range(max(warmup, 3)):
         fn()
     sync()
@@ -199,42 +203,6 @@ def extra_workloads(world, rank, dev, dist, peaks, peak_src, sync, max_over_rank
         x = torch.randn((rows, cols), generator=g, device=dev, dtype=torch.float32)
         return x.mul_(scale) if scale != 1.0 else x
 
-    # fp8 e4m3, per-tensor scales amax / 448, scale_a * scale_b applied in the epilogue, bf16 C.
-    w = wl.C4
-    n_lo, n_hi = sharding.shard_range(w.n, world, rank, align=256)
-    xa = normal(w.m, w.k, w.seed * 1000 + 0, w.a_scale)
-    sa = xa.abs().max() / 448.0
-    a = (xa / sa).to(torch.float8_e4m3fn)
-    del xa
-    xb = normal(w.n, w.k, w.seed * 1000 + 1, w.b_scale)
-    sb = xb.abs().max() / 448.0
-    b = (xb[n_lo:n_hi] / sb).to(torch.float8_e4m3fn)
-    del xb
-    scale_a = sa.reshape(1).float()
-    scale_b = sb.reshape(1).float()
-    c = torch.empty((w.m, n_hi - n_lo), dtype=torch.bfloat16, device=dev)
-    steps = 40
-    ms, clocks = timed(kl.gemm_launcher(a, b, c, scale_a=scale_a, scale_b=scale_b), steps, 3, stream, dev, sync)
-    in_kernel = kl.clock_probe(a, b, c, scale_a=scale_a, scale_b=scale_b)
-    if kl.read_status() != 0:
-        raise RuntimeError("a device-side wait timed out in the fp8 workload")
-    ms_all = max_over_ranks(ms)
-    per_rank = 2.0 * w.m * (n_hi - n_lo) * w.k
-    achieved = per_rank / (ms * 1e-3) / 1e12
-    peak = 2.0 * peaks["bf16_tflops"]
-    out[w.name] = {
-        "value": w.flops / (ms_all * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_all, "steps": steps,
-        "warmup": 3, "n_gpus": world, "dtype": "e4m3", "out": "bf16",
-        "data": "N(0,1) drawn on the device (torch generator, seeds 3000 / 3001), per-tensor amax/448 scales",
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                     "peak_source": f"{peak_src} 2 x bf16_tflops (burst; the dense fp8 rate is twice bf16)",
-                     "algorithmic_flops_per_launch": per_rank},
-        "clocks": dict(clocks, in_kernel=in_kernel),
-        "gpu_launches": steps,
-    }
-    del a, b, c
-    torch.cuda.empty_cache()
-
     if world == 1:
         # Decode shapes: weights N(0,1) * 0.02, activations N(0,1), bf16 in and out; the skinny
         # kernel or the one-CTA tile kernel, whichever KL_ALGO_AUTO picks (the library default).
@@ -244,7 +212,7 @@ def extra_workloads(world, rank, dev, dist, peaks, peak_src, sync, max_over_rank
             x = normal(m, w.k, w.seed * 1000 + 0, w.a_scale).to(torch.bfloat16)
             y = torch.empty((m, w.n), dtype=torch.bfloat16, device=dev)
             steps = 300
-            ms, clocks = timed(kl.gemm_launcher(x, wgt, y), steps, 10, stream, dev, sync)
+            ms, clocks = timed(kl.gemm_launcher(x, wgt, y), steps, 10, stream, dev, sync, settle_s=1.0)
             if kl.read_status() != 0:
                 raise RuntimeError("a device-side wait timed out in the decode workload")
             alg = (m * w.k + w.n * w.k) * 2 + m * w.n * 2
@@ -260,10 +228,47 @@ def extra_workloads(world, rank, dev, dist, peaks, peak_src, sync, max_over_rank
                              "algorithmic_bytes_per_launch": alg},
                 "clocks": clocks,
                 "gpu_launches": steps,
-                "l2": "weights (470 MB) exceed L2 (no flush)",
+                "l2": "weights (470 MB) exceed L2 (no flush)", "settle_s": 1.0,
             }
         del wgt
         torch.cuda.empty_cache()
+    # fp8 e4m3, per-tensor scales amax / 448, scale_a * scale_b applied in the epilogue, bf16 C.
+    w = wl.C4
+    n_lo, n_hi = sharding.shard_range(w.n, world, rank, align=256)
+    xa = normal(w.m, w.k, w.seed * 1000 + 0, w.a_scale)
+    sa = xa.abs().max() / 448.0
+    a = (xa / sa).to(torch.float8_e4m3fn)
+    del xa
+    xb = normal(w.n, w.k, w.seed * 1000 + 1, w.b_scale)
+    sb = xb.abs().max() / 448.0
+    b = (xb[n_lo:n_hi] / sb).to(torch.float8_e4m3fn)
+    del xb
+    scale_a = sa.reshape(1).float()
+    scale_b = sb.reshape(1).float()
+    c = torch.empty((w.m, n_hi - n_lo), dtype=torch.bfloat16, device=dev)
+    steps = 40
+    ms, clocks = timed(kl.gemm_launcher(a, b, c, scale_a=scale_a, scale_b=scale_b), steps, 3, stream, dev, sync,
+                       settle_s=1.0)
+    in_kernel = kl.clock_probe(a, b, c, scale_a=scale_a, scale_b=scale_b)
+    if kl.read_status() != 0:
+        raise RuntimeError("a device-side wait timed out in the fp8 workload")
+    ms_all = max_over_ranks(ms)
+    per_rank = 2.0 * w.m * (n_hi - n_lo) * w.k
+    achieved = per_rank / (ms * 1e-3) / 1e12
+    peak = 2.0 * peaks["bf16_tflops"]
+    out[w.name] = {
+        "value": w.flops / (ms_all * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_all, "steps": steps,
+        "warmup": 3, "n_gpus": world, "dtype": "e4m3", "out": "bf16",
+        "data": "N(0,1) drawn on the device (torch generator, seeds 3000 / 3001), per-tensor amax/448 scales",
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": f"{peak_src} 2 x bf16_tflops (burst; the dense fp8 rate is twice bf16)",
+                     "algorithmic_flops_per_launch": per_rank},
+        "clocks": dict(clocks, in_kernel=in_kernel),
+        "gpu_launches": steps, "settle_s": 1.0,
+    }
+    del a, b, c
+    torch.cuda.empty_cache()
+
     return out
 
 

@@ -76,9 +76,6 @@ using E4m3Bf16_1 = TnConfig<kl::e4m3, kl::bf16, 1, 256, 4>;
 using Bf16Bf16_2 = TnConfig<kl::bf16, kl::bf16, 2, 256, 6>;
 using Bf16F32_2 = TnConfig<kl::bf16, float, 2, 256, 6>;
 using E4m3Bf16_2 = TnConfig<kl::e4m3, kl::bf16, 2, 256, 6>;
-// CTA pair, 256 x 128 tiles (variant 2): twice the tiles of the 256 x 256 kernel, for narrow
-// column shards whose 256-wide tiles leave the last wave short; 8 stages of 24 KB per CTA.
-using Bf16Bf16_2n128 = TnConfig<kl::bf16, kl::bf16, 2, 128, 8>;
 
 template <class Cfg>
 kl_status run(Problem const& pr, cudaStream_t stream, LaunchInfo* info = nullptr) {
@@ -130,10 +127,8 @@ kl_status run_tile(kl_gemm_desc const& d, Problem const& pr, bool pair, cudaStre
     if (handled) return s;
     return fail(KL_ERR_NOT_SUPPORTED, std::string(who) + ": 64- and 32-byte operand swizzle take bf16 inputs and bf16 or f32 C");
   }
-  if (d.ab_type == KL_BF16 && d.c_type == KL_BF16) {
-    if (pair && d.variant == 2) return run<Bf16Bf16_2n128>(pr, stream, info);
+  if (d.ab_type == KL_BF16 && d.c_type == KL_BF16)
     return pair ? run<Bf16Bf16_2>(pr, stream, info) : run<Bf16Bf16_1>(pr, stream, info);
-  }
   if (d.ab_type == KL_BF16 && d.c_type == KL_F32)
     return pair ? run<Bf16F32_2>(pr, stream, info) : run<Bf16F32_1>(pr, stream, info);
   if (d.ab_type == KL_E4M3 && d.c_type == KL_BF16)

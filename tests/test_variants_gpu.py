@@ -186,3 +186,4 @@ def test_reduce_add_needs_out(cuda):
     a = torch.zeros(256, 64, dtype=torch.bfloat16, device=cuda)
     with pytest.raises(ValueError):
         kl.gemm(a, a, accumulate=True)
+
