@@ -139,12 +139,15 @@ def nvlink_bytes(index: int):
 
         pynvml.nvmlInit()
         h = pynvml.nvmlDeviceGetHandleByIndex(index)
-        ids = [(pynvml.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_TX, 0xFFFFFFFF),
-               (pynvml.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_RX, 0xFFFFFFFF)]
-        vals = pynvml.nvmlDeviceGetFieldValues(h, ids)
-        if any(v.nvmlReturn != 0 for v in vals):
+        tx_id, rx_id = pynvml.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_TX, pynvml.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_RX
+        # Per link (scope = link index), summed over the links that report.
+        links = 18
+        vals = pynvml.nvmlDeviceGetFieldValues(h, [(tx_id, l) for l in range(links)] + [(rx_id, l) for l in range(links)])
+        tx = [int(v.value.ullVal) for v in vals[:links] if v.nvmlReturn == 0]
+        rx = [int(v.value.ullVal) for v in vals[links:] if v.nvmlReturn == 0]
+        if not tx or not rx:
             return None
-        return tuple(int(v.value.ullVal) * 1024 for v in vals)
+        return sum(tx) * 1024, sum(rx) * 1024
     except Exception:
         return None
 

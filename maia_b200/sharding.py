@@ -81,9 +81,11 @@ class SharedC:
         self.full = torch.empty((m, n), dtype=dtype, device=device)
         handles = [None] * self.world
         dist.all_gather_object(handles, kl.ipc_handle(self.full.data_ptr()))
-        self.bases = [kl.ipc_open(h) for r, (h, _) in enumerate(handles) if r != self.rank]
-        self.peers = [base + off for base, (r, (_, off)) in
-                      zip(self.bases, [(r, x) for r, x in enumerate(handles) if r != self.rank])]
+        # Peers in the order rank + 1, rank + 2, ... (mod g): the epilogue stores to them in this
+        # order, so at any moment the ranks are sending to different GPUs rather than all to one.
+        order = [(self.rank + i) % self.world for i in range(1, self.world)]
+        self.bases = [kl.ipc_open(handles[r][0]) for r in order]
+        self.peers = [base + handles[r][1] for base, r in zip(self.bases, order)]
         self.elem = self.full.element_size()
 
     def peer_ptrs(self, col0: int) -> list[int]:

@@ -71,6 +71,24 @@ try:
     assert elem <= 1e-2 and norm <= 1e-2, f"rank {rank}: split tail {elem:.3e} / {norm:.3e}"
     dist.barrier()
     shared.close()
+    # End to end from host memory: each rank brings only its slab of A's rows (the last one short),
+    # the ranks all-gather A over NVLink, and B's shard and C's block go through kl_gemm_host_b.
+    m, n, k = 1000, 2048, 1024
+    a_bits, b_bits, _, _ = random_inputs(m, n, k, "bf16", seed=91)
+    lo, hi = sharding.shard_range(n, world, rank, align=256)
+    hs = sharding.HostShardedGemm(m, hi - lo, k, torch.bfloat16, torch.float32, dev, dist)
+    r0, r1 = hs.slab_rows()
+    a_host = torch.from_numpy(a_bits[r0:r1].view(np.int16)).view(torch.bfloat16).pin_memory()
+    b_host = torch.from_numpy(np.ascontiguousarray(b_bits[lo:hi]).view(np.int16)).view(torch.bfloat16).pin_memory()
+    c_host = torch.full((m, hi - lo), float("nan"), dtype=torch.float32).pin_memory()
+    for _ in range(2):
+        hs(a_host, b_host, c_host)
+        torch.cuda.synchronize()
+        assert kl.read_status() == 0
+        got = c_host.numpy()
+        elem, norm = og.rel_error(got, og.gemm_f64(a_bits, b_bits[lo:hi], 1.0))
+        assert not np.isnan(got).any() and elem <= 1e-2 and norm <= 1e-2, f"rank {rank}: host path {elem:.3e}"
+    dist.barrier()
 finally:
     dist.destroy_process_group()
 print("OK", rank)
