@@ -277,8 +277,9 @@ def extra_workloads(world, rank, dev, dist, peaks, peak_src, sync, max_over_rank
 
 def config_of(w, args, world):
     """The `config` both arms report: the workload and the launch knobs."""
+    par = f"N-sharded x{world}" if not getattr(args, "shard_of", 0) else f"shard 0 of {args.shard_of} on one GPU"
     return {"workload": w.name, "m": w.m, "n": w.n, "k": w.k, "out": w.out,
-            "parallelism": f"N-sharded x{world}", "output": "C[:, shard] per rank (no gather)",
+            "parallelism": par, "output": "C[:, shard] per rank (no gather)",
             "l2": "operands exceed L2 (no flush)", "algo": args.algo, "group_m": args.group_m,
             "prefetch": args.prefetch, "variant": args.variant, "max_ctas": args.max_ctas, "stream_k": args.stream_k}
 
@@ -323,6 +324,9 @@ def main():
     ap.add_argument("--stream-k", type=int, default=0, choices=[-1, 0, 1],
                     help="tile kernels' split tail: 0 = library default, 1 = always, -1 = whole tiles")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shard-of", type=int, default=0,
+                    help="one GPU only: time the first column shard of a G-way N-split (the GEMM one rank of "
+                         "G runs), for profiling the sharded kernel without a multi-rank launch")
     ap.add_argument("--no-extra-workloads", action="store_true",
                     help="skip the fp8 and decode entries of `workloads` (run by default with the headline workload)")
     args = ap.parse_args()
@@ -355,7 +359,12 @@ def main():
     from maia_b200 import sharding
 
     a_bits, b_bits, sa, sb = wl.make_inputs(w)
-    n_lo, n_hi = sharding.shard_range(w.n, world, rank, align=256)
+    split = world
+    if args.shard_of > 0:
+        if world != 1:
+            raise SystemExit("--shard-of runs on one GPU")
+        split = args.shard_of
+    n_lo, n_hi = sharding.shard_range(w.n, split, rank, align=256)
     b_bits = np.ascontiguousarray(b_bits[n_lo:n_hi])
     mx = w.dtype in ("mxfp8", "mxfp6", "mxfp4", "nvfp4")
     vec = 16 if w.dtype == "nvfp4" else 32
@@ -430,7 +439,7 @@ def main():
     if kl.read_status() != 0:
         raise RuntimeError("a device-side wait timed out during the benchmark")
     dev_ms = max_over_ranks(dev_ms)
-    flops_total = 2.0 * w.m * w.n * w.k
+    flops_total = 2.0 * w.m * (w.n if split == world else n_hi - n_lo) * w.k
     value = flops_total / (dev_ms * 1e-3) / 1e12
 
     # ---- end to end through the public API with host buffers
@@ -576,7 +585,7 @@ def main():
 
     peaks, peak_src = load_peaks()
     extra = None
-    if args.workload == DEFAULT_WORKLOAD and not args.no_extra_workloads:
+    if args.workload == DEFAULT_WORKLOAD and not args.no_extra_workloads and not args.shard_of:
         del a, b
         torch.cuda.empty_cache()
         extra = extra_workloads(world, rank, dev, dist, peaks, peak_src, barrier, max_over_ranks)

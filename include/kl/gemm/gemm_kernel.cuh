@@ -873,8 +873,36 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
             float* sum = reinterpret_cast<float*>(v);
 #pragma unroll
             for (int e = 0; e < Cfg::kChunkCols; ++e) sum[e] = 0.0f;
+            // The slots two at a time, both loads in flight before either is added (the L2 round
+            // trips, not the adds, bound this sum), still added in K-range order.
+            const int trel = wcol + c * Cfg::kChunkCols;
+            int q = 0;
 #pragma unroll 1
-            for (int q = 0; q < args.sk_split; ++q) slot_add(slot_of(q, r), wcol + c * Cfg::kChunkCols, sum);
+            for (; q + 1 < args.sk_split; q += 2) {
+              const float4* s0 = reinterpret_cast<const float4*>(slot_of(q, r)) + (long long)(trel >> 2) * 128 + erow;
+              const float4* s1 = reinterpret_cast<const float4*>(slot_of(q + 1, r)) + (long long)(trel >> 2) * 128 + erow;
+              float4 x0[Cfg::kChunkCols / 4], x1[Cfg::kChunkCols / 4];
+#pragma unroll
+              for (int j = 0; j < Cfg::kChunkCols / 4; ++j) {
+                x0[j] = __ldcg(s0 + 128 * j);
+                x1[j] = __ldcg(s1 + 128 * j);
+              }
+#pragma unroll
+              for (int j = 0; j < Cfg::kChunkCols / 4; ++j) {
+                sum[4 * j] += x0[j].x;
+                sum[4 * j + 1] += x0[j].y;
+                sum[4 * j + 2] += x0[j].z;
+                sum[4 * j + 3] += x0[j].w;
+              }
+#pragma unroll
+              for (int j = 0; j < Cfg::kChunkCols / 4; ++j) {
+                sum[4 * j] += x1[j].x;
+                sum[4 * j + 1] += x1[j].y;
+                sum[4 * j + 2] += x1[j].z;
+                sum[4 * j + 3] += x1[j].w;
+              }
+            }
+            if (q < args.sk_split) slot_add(slot_of(q, r), trel, sum);
             emit_chunk(v, col0 + c * Cfg::kChunkCols);
           }
         }
