@@ -64,6 +64,8 @@ class ClockSampler:
     def __enter__(self):
         import threading
 
+        if self.index is None:  # sampling off
+            return self
         try:
             import pynvml
 
@@ -152,12 +154,15 @@ def nvlink_bytes(index: int):
         return None
 
 
-def timed(fn, steps: int, warmup: int, stream, device, sync, nvlink: bool = False, settle_s: float = 0.0):
+def timed(fn, steps: int, warmup: int, stream, device, sync, nvlink: bool = False, settle_s: float = 0.0,
+          sample_clocks: bool = True):
     """Device time per call of fn (CUDA events on `stream`, after `warmup` untimed calls), with the
     NVML clock samples taken meanwhile; with nvlink=True also the NVLink bytes per call this GPU
     sent and received (NVML counters read around the timed calls, after a pause that lets them
     settle). settle_s: an idle pause first, so that a workload does not start in the power state the
-    previous one left."""
+    previous one left. sample_clocks=False leaves the sampling thread out: a step that queues many
+    small launches from Python (the NCCL gather path) is host-bound, and a thread polling NVML in
+    every rank's process slows that host work down."""
     import torch
 
     if settle_s > 0:
@@ -171,7 +176,7 @@ def timed(fn, steps: int, warmup: int, stream, device, sync, nvlink: bool = Fals
         time.sleep(0.3)
         link0 = nvlink_bytes(device.index)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device.index) as clocks:
+    with ClockSampler(device.index if sample_clocks else None) as clocks:
         e0.record(stream)
         for _ in range(steps):
             fn()
@@ -503,7 +508,7 @@ def main():
         for _ in range(max(args.warmup, 3)):
             gather_step()
         barrier()
-        g_ms, _, g_link = timed(gather_step, args.steps, 0, stream, dev, barrier, nvlink=True)
+        g_ms, _, g_link = timed(gather_step, args.steps, 0, stream, dev, barrier, nvlink=True, sample_clocks=False)
         g_ms = max_over_ranks(g_ms)
         gather = {"value": flops_total / (g_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": g_ms,
                   "what": "kl_gemm + NCCL all-gather of C and re-layout to [M, N] on every rank",
@@ -522,7 +527,7 @@ def main():
         for _ in range(max(args.warmup, 3)):
             fused_step()
         barrier()
-        f_ms, _, f_link = timed(fused_step, args.steps, 0, stream, dev, barrier, nvlink=True)
+        f_ms, _, f_link = timed(fused_step, args.steps, 0, stream, dev, barrier, nvlink=True, sample_clocks=False)
         f_ms = max_over_ranks(f_ms)
         gather["fused"] = {"value": flops_total / (f_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": f_ms,
                            "what": "kl_gemm_gather: tiles stored to every rank's C by the GEMM epilogue (P2P over NVLink)",
@@ -559,7 +564,8 @@ def main():
                 kl.gemm_gather_multicast(a, b, mc_view, mc_addr, scale_a=scale_a, scale_b=scale_b, algo=args.algo,
                                          sfa=sfa, sfb=sfb, scale_vec=vec, stream_k=args.stream_k)
 
-            m_ms, _, m_link = timed(mc_step, args.steps, args.warmup, stream, dev, barrier, nvlink=True)
+            m_ms, _, m_link = timed(mc_step, args.steps, args.warmup, stream, dev, barrier, nvlink=True,
+                                     sample_clocks=False)
             m_ms = max_over_ranks(m_ms)
             barrier()
             same = torch.equal(mcc.full.view(bits), want.view(bits))
