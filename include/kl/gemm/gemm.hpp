@@ -30,6 +30,9 @@ struct Problem {
   int group_m = 0;   // 0 = default for the config
   int max_ctas = 0;  // 0 = every SM
   int prefetch = 0;  // L2 prefetch distance in K-blocks: 0 = default, < 0 = off
+  // Programmatic dependent launch: true lets this launch start its prologue while the kernel before
+  // it on the stream finishes (the kernel waits for that kernel's results before reading memory).
+  bool overlap_launch = true;
   unsigned long long* clock_probe = nullptr;  // device [4 * grid]: per CTA clock64/globaltimer at start and end
   // Peer copies of C (same shape and pitch, in other GPUs' memory, already mapped into this
   // process): the epilogue TMA-stores every tile there too. Not with the direct-store epilogue.
@@ -358,19 +361,26 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   if (sch.sk_tiles > 0) a.prefetch = 0;  // the L2 prefetch follows the data-parallel tile order only
 
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  unsigned n_attr = 0;
   cfg.gridDim = dim3(unsigned(workers * Cfg::kCtaGroup), 1, 1);
   cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
   cfg.dynamicSmemBytes = Cfg::kSmemBytes;
   cfg.stream = stream;
   if constexpr (Cfg::kCtaGroup > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = Cfg::kCtaGroup;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[n_attr].id = cudaLaunchAttributeClusterDimension;
+    attr[n_attr].val.clusterDim.x = Cfg::kCtaGroup;
+    attr[n_attr].val.clusterDim.y = 1;
+    attr[n_attr].val.clusterDim.z = 1;
+    ++n_attr;
   }
+  if (pr.overlap_launch) {
+    attr[n_attr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n_attr].val.programmaticStreamSerializationAllowed = 1;
+    ++n_attr;
+  }
+  cfg.attrs = n_attr > 0 ? attr : nullptr;
+  cfg.numAttrs = n_attr;
   if (info) {
     info->grid = workers * Cfg::kCtaGroup;
     info->tiles = tiles;

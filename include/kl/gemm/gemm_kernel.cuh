@@ -33,6 +33,7 @@
 #include <type_traits>
 
 #include <kl/arch/cluster.hpp>
+#include <kl/arch/griddep.hpp>
 #include <kl/arch/mbarrier.hpp>
 #include <kl/arch/multimem.hpp>
 #include <kl/arch/tcgen05.hpp>
@@ -403,10 +404,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
   const uint32_t drain_bar = bar0 + 8u * (2 * S + 2 * Cfg::kNumAcc);
 
   const TnArgs& args = p.args;
-  if (args.clock_probe != nullptr && threadIdx.x == 0) {
-    args.clock_probe[4 * blockIdx.x + 0] = clock64();
-    args.clock_probe[4 * blockIdx.x + 1] = globaltimer_ns();
-  }
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t cta_rank = (CG == 2) ? cluster_ctarank() : 0u;  // rank inside the pair
@@ -448,6 +445,15 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
   }
   tcgen05_fence_after();
   const uint32_t tmem_base = ld_shared_u32(tmem_slot);
+  // Launched with programmatic serialization, this CTA may have started while the previous kernel
+  // on the stream still runs: the prologue above touched no global memory, everything below may.
+  // Then let the next launch start its own prologue on SMs this grid leaves free.
+  griddep_wait();
+  griddep_launch_dependents();
+  if (args.clock_probe != nullptr && threadIdx.x == 0) {
+    args.clock_probe[4 * blockIdx.x + 0] = clock64();
+    args.clock_probe[4 * blockIdx.x + 1] = globaltimer_ns();
+  }
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer

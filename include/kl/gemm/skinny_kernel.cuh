@@ -28,6 +28,7 @@
 #include <cstdint>
 
 #include <kl/arch/cluster.hpp>
+#include <kl/arch/griddep.hpp>
 #include <kl/arch/mbarrier.hpp>
 #include <kl/arch/tcgen05.hpp>
 #include <kl/arch/tma.hpp>
@@ -228,6 +229,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_skinny_kernel(const __g
   __syncthreads();
   tcgen05_fence_after();
   const uint32_t tmem_base = ld_shared_u32(tmem_slot);
+  // Programmatic serialization: no global memory above this line (see the tile kernel).
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer

@@ -138,7 +138,12 @@ typedef struct kl_gemm_desc {
    * same group). K-major, batch 1. With block scaling, sfb holds the groups' blocked scale arrays
    * back to back (kl_block_scale_bytes(N, K, vec) bytes each) and sfa A's. */
   int32_t groups;
-  int32_t reserved2; /* must be 0 */
+  /* Programmatic dependent launch (tile and skinny kernels): 0 = library default (on), 1 = on,
+   * -1 = off. On, the launch may start while the kernel before it on the stream is finishing: its
+   * CTAs set up shared memory, barriers and TMEM on SMs that kernel has left, and wait for it to
+   * complete (its writes visible) before reading or writing any global memory. Results and
+   * stream order are those of a plain launch. */
+  int32_t launch_overlap;
   const int32_t* m_block_group;
 } kl_gemm_desc;
 

@@ -69,7 +69,7 @@ class GemmDesc(ctypes.Structure):
         ("c_reduce", ctypes.c_int32), ("swizzle", ctypes.c_int32),
         ("block_scale", ctypes.c_int32), ("stream_k", ctypes.c_int32),
         ("sfa", ctypes.c_void_p), ("sfb", ctypes.c_void_p),
-        ("groups", ctypes.c_int32), ("reserved2", ctypes.c_int32),
+        ("groups", ctypes.c_int32), ("launch_overlap", ctypes.c_int32),
         ("m_block_group", ctypes.c_void_p),
     ]
 
@@ -255,7 +255,7 @@ def _elements(code: int, units: int) -> int:
 
 def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, group_m=0, max_ctas=0,
               variant=0, prefetch=0, a_major=0, b_major=0, c_reduce=0, swizzle=0, sfa=None, sfb=None,
-              scale_vec=32, ab_type=None, stream_k=0) -> GemmDesc:
+              scale_vec=32, ab_type=None, stream_k=0, overlap=0) -> GemmDesc:
     """Descriptor for C = alpha * A . B^T on torch CUDA tensors: A [M,K], B [N,K], C [M,N], or the
     batched forms A [L,M,K], B [L,N,K], C [L,M,N] (L independent GEMMs). a_major / b_major = 1
     pass the operand MN-major: `a` as the stored [K, M] (A transposed in memory), `b` as [K, N].
@@ -265,7 +265,9 @@ def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, gr
     (MX, scale_vec 32) or one UE4M3 scale per 16 (NVFP4, scale_vec 16, fp4 operands). ab_type =
     KL_E3M2 / KL_E2M3 passes uint8 `a` / `b` as packed fp6 ([rows, 3 K / 4] bytes). stream_k: the
     tile kernels' split tail (the last wave's tiles cut into K-ranges), 0 = where the last wave
-    would leave workers idle, 1 = always, -1 = never."""
+    would leave workers idle, 1 = always, -1 = never. overlap: programmatic dependent launch (the
+    kernel's prologue overlaps the end of the kernel before it on the stream), 0 = library default
+    (on), 1 = on, -1 = off."""
     for name, t in (("a", a), ("b", b), ("c", c)):
         if t.dim() not in (2, 3) or t.stride(-1) != 1:
             raise ValueError(f"{name} must be a 2-D or 3-D tensor with a contiguous last dimension")
@@ -292,13 +294,13 @@ def gemm_desc(a, b, c, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO, gr
                     stride_b=bs[1], stride_c=bs[2], a_major=a_major, b_major=b_major, c_reduce=int(c_reduce),
                     swizzle=swizzle,
                     block_scale=0 if sfa is None and sfb is None else (2 if scale_vec == 16 else 1),
-                    stream_k=int(stream_k),
+                    stream_k=int(stream_k), launch_overlap=int(overlap),
                     sfa=None if sfa is None else sfa.data_ptr(), sfb=None if sfb is None else sfb.data_ptr())
 
 
 def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=None, algo=ALGO_AUTO,
          group_m=0, max_ctas=0, variant=0, prefetch=0, a_major=0, b_major=0, accumulate=False, swizzle=0,
-         sfa=None, sfb=None, scale_vec=32, ab_type=None, stream_k=0, workspace=None, stream=None):
+         sfa=None, sfb=None, scale_vec=32, ab_type=None, stream_k=0, overlap=0, workspace=None, stream=None):
     """out = alpha * a @ b.T [* scale_a * scale_b] on the current CUDA stream, via kl_gemm.
     accumulate=True: out += alpha * a @ b.T (out must be given). sfa/sfb: block scales (see
     pack_block_scales). ab_type="e3m2" / "e2m3": a and b are uint8 packed fp6."""
@@ -312,7 +314,7 @@ def gemm(a, b, out=None, *, out_dtype=None, alpha=1.0, scale_a=None, scale_b=Non
         shape = (a.shape[0], m, n) if a.dim() == 3 else (m, n)
         out = torch.empty(shape, dtype=out_dtype or torch.bfloat16, device=a.device)
     d = gemm_desc(a, b, out, alpha, scale_a, scale_b, algo, group_m, max_ctas, variant, prefetch, a_major, b_major,
-                  int(bool(accumulate)), swizzle, sfa, sfb, scale_vec, ab_type, stream_k)
+                  int(bool(accumulate)), swizzle, sfa, sfb, scale_vec, ab_type, stream_k, overlap)
     s = stream if stream is not None else torch.cuda.current_stream(a.device).cuda_stream
     if workspace is None:
         check(lib().kl_gemm(ctypes.byref(d), ctypes.c_void_p(s)))

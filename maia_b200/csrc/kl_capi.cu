@@ -168,6 +168,7 @@ Problem problem_of(kl_gemm_desc const& d) {
   pr.groups = d.groups;
   pr.m_block_group = d.m_block_group;
   pr.stream_k = d.stream_k;
+  pr.overlap_launch = d.launch_overlap >= 0;
   return pr;
 }
 
@@ -291,7 +292,8 @@ kl_status kl_gemm_ws(const kl_gemm_desc* d, void* workspace, size_t workspace_by
   if ((d->a_major != 0 && !a_mn) || (d->b_major != 0 && !b_mn))
     return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: a_major / b_major must be 0 (K) or 1 (MN)");
   const bool default_swizzle = d->swizzle == 0 || d->swizzle == 128;
-  if (d->reserved2 != 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: reserved fields must be 0");
+  if (d->launch_overlap < -1 || d->launch_overlap > 1)
+    return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: launch_overlap must be -1, 0 or 1");
   if (d->stream_k < -1 || d->stream_k > 1) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm: stream_k must be -1, 0 or 1");
   int algo = KL_ALGO_AUTO;
   kl_status rs = resolve_algo(*d, &algo);

@@ -150,8 +150,19 @@ kl_status launch(kl_gemm_desc const& d, Plan const& pl, void* ws, cudaStream_t s
   a.timeout_ns = wait_timeout_ns();
   a.prefetch = d.prefetch > 0 ? d.prefetch : d.prefetch < 0 ? 0 : kDefaultPrefetchSkinny;
   a.c_reduce = d.c_reduce;
-  gemm_skinny_kernel<Cfg><<<pl.grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(unsigned(pl.grid), 1, 1);
+  cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  if (d.launch_overlap >= 0) {  // programmatic dependent launch (the kernel waits before any global access)
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_skinny_kernel<Cfg>, p);
   return e == cudaSuccess ? KL_OK : cuda_fail(e, "skinny launch");
 }
 

@@ -224,7 +224,7 @@ def _desc(**kw):
     ("stream_k", 2, "stream_k must be -1, 0 or 1"),
     ("stream_k", -2, "stream_k must be -1, 0 or 1"),
     ("c_reduce", 2, "c_reduce must be 0"),
-    ("reserved2", 1, "reserved fields must be 0"),
+    ("launch_overlap", 2, "launch_overlap must be -1, 0 or 1"),
     ("m", -1, "negative extent"),
     ("a_major", 3, "a_major / b_major must be 0"),
 ])
