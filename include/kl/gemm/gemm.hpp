@@ -105,6 +105,7 @@ TnSchedule tn_schedule(Problem const& pr, int max_workers) {
   if (pr.max_ctas > 0) cap = std::min(cap, std::max(1, pr.max_ctas / Cfg::kCtaGroup));
   s.workers = std::min(s.tiles, cap);
   if (pr.stream_k < 0 || cap <= 0) return s;
+  if constexpr (Cfg::kNSub > 1) return s;  // wide tiles: whole tiles only
   const int W = cap, T = s.tiles;
   int R = T % W;
   if (R == 0 && pr.stream_k > 0) R = W;  // forced: split the last full wave

@@ -51,7 +51,7 @@ enum : int {
 };
 
 template <typename InT, typename OutT, int CtaGroup, int BlockN, int Stages, bool DirectStore = false,
-          bool AMn = false, bool BMn = false, class Sw = Swizzle128B, int SfVec = 0>
+          bool AMn = false, bool BMn = false, class Sw = Swizzle128B, int SfVec = 0, int NSub = 1>
 struct TnConfig {
   using in_type = InT;
   using out_type = OutT;
@@ -61,8 +61,14 @@ struct TnConfig {
   static constexpr bool kDirectStore = DirectStore;
   static constexpr int kCtaM = 128;                    // rows of A (= TMEM lanes) per CTA
   static constexpr int kTileM = kCtaM * CtaGroup;      // rows of C per tile
-  static constexpr int kTileN = BlockN;                // columns of C per tile (UMMA N)
-  static constexpr int kCtaN = BlockN / CtaGroup;      // rows of B each CTA loads
+  // Wide tiles (NSub > 1): NSub MMAs of N = BlockN side by side share every stage of A, so a tile is
+  // BlockN * NSub columns of C and each byte of A brought from L2 feeds NSub times the MACs (a 256 x
+  // 512 CTA-pair tile moves 3/4 of the operand bytes per MAC of a 256 x 256 one). Its accumulator
+  // takes all of TMEM: one buffer, drained by eight epilogue warps before the next tile starts.
+  static constexpr int kNSub = NSub;
+  static constexpr int kBlockN = BlockN;               // N of one MMA
+  static constexpr int kTileN = BlockN * NSub;         // columns of C per tile
+  static constexpr int kCtaN = BlockN / CtaGroup;      // rows of B each CTA loads per sub-tile
   static constexpr int kBlockK = 128 / int(sizeof(InT));  // 128 bytes of K per stage
   static constexpr int kUmmaK = 32 / int(sizeof(InT));    // K of one tcgen05.mma
   static constexpr int kStages = Stages;
@@ -96,8 +102,8 @@ struct TnConfig {
   static constexpr uint32_t kSfbBytes = 512u * kSfAtomsK * kSfbAtoms;
   // Two TMEM accumulators (epilogue of tile i overlaps the MMAs of tile i + 1), except for block
   // scaling with 256 columns: 2 x 256 accumulator columns would leave none for the scales.
-  static constexpr int kNumAcc = (kMx && BlockN == 256) ? 1 : 2;
-  static constexpr int kAccCols = BlockN;              // fp32 accumulator columns per buffer
+  static constexpr int kNumAcc = ((kMx && BlockN == 256) || NSub > 1) ? 1 : 2;
+  static constexpr int kAccCols = kTileN;              // fp32 accumulator columns per buffer
   static constexpr int kSfaCol = kAccCols * kNumAcc;   // TMEM columns of A's and B's scales
   static constexpr int kSfbCol = kSfaCol + 4 * kSfAtomsK;
   static constexpr int kTmemUsed = kAccCols * kNumAcc + 4 * kSfAtomsK * (1 + kSfbAtoms);
@@ -107,10 +113,11 @@ struct TnConfig {
   // the MMAs fill the other. With one, the MMAs wait for the drain, so 8 warps (two per quarter,
   // each half of the columns) first load all their columns into registers, hand the accumulator
   // back, and only then convert and store.
+  // Wide tiles drain chunk by chunk (their columns do not fit in registers).
   static constexpr int kEpiWarps = kNumAcc == 1 ? 8 : 4;
-  static constexpr bool kEarlyRelease = kNumAcc == 1;
+  static constexpr bool kEarlyRelease = kNumAcc == 1 && NSub == 1;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
-  static constexpr int kWarpCols = BlockN / (kEpiWarps / 4);  // accumulator columns per epilogue warp
+  static constexpr int kWarpCols = kTileN / (kEpiWarps / 4);  // accumulator columns per epilogue warp
   static constexpr int kChunkCols = 128 / int(sizeof(OutT));  // epilogue store box width (128 B)
   static constexpr int kChunks = kWarpCols / kChunkCols;       // chunks per epilogue warp and tile
   static constexpr int kStageBufs = kEpiWarps == 4 ? 2 : 1;    // C staging buffers per epilogue warp
@@ -129,7 +136,8 @@ struct TnConfig {
   using CBox = SmemTile<OutT, 32, kChunkCols>;
 
   static constexpr uint32_t kABytes = ATile::bytes;
-  static constexpr uint32_t kBBytes = BTile::bytes;
+  static constexpr uint32_t kBSubBytes = BTile::bytes;  // one sub-tile of B
+  static constexpr uint32_t kBBytes = BTile::bytes * NSub;
   static constexpr uint32_t kStageTx = (kFp6 ? (kABytes + kBBytes) / 4 * 3 : kABytes + kBBytes) + kSfaBytes + kSfbBytes;
   static constexpr uint32_t kCBytes = CBox::bytes;     // 4 KB per staging buffer
   static constexpr uint32_t kOffA = 0;
@@ -158,6 +166,7 @@ struct TnConfig {
   static_assert(!kMx || (sizeof(InT) == 1 && !AMn && !BMn && std::is_same_v<Sw, Swizzle128B> && BlockN % 32 == 0),
                 "block-scaled: 8-bit or packed fp4 K-major operands, 128-byte swizzle, tile N a multiple of 32");
   static_assert(SfVec == 0 || SfVec == 32 || (SfVec == 16 && kFp4), "scales per 32 elements, or per 16 for fp4");
+  static_assert(NSub == 1 || (NSub == 2 && !kMx && !DirectStore), "wide tiles: two sub-tiles, no block scaling");
   static_assert(!kFp4 || kMx, "packed fp4 operands are block-scaled (kind::mxf4 / mxf4nvf4)");
   static_assert(!kFp6 || SfVec == 32, "fp6 operands are MX block-scaled (kind::mxf8f6f4, a scale per 32)");
   static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
@@ -472,7 +481,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
         tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, pbz, ptm, ptn);
         if (batched || Cfg::kAMn || Cfg::kBMn || args.m_block_group != nullptr) return;  // 2-D, K-major maps only
         tma_prefetch_l2_2d(&p.map_a, kb * Cfg::kBlockK, ptm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM);
-        tma_prefetch_l2_2d(&p.map_b, kb * Cfg::kBlockK, ptn * Cfg::kTileN + int(cta_rank) * Cfg::kCtaN);
+#pragma unroll
+        for (int j = 0; j < Cfg::kNSub; ++j)
+          tma_prefetch_l2_2d(&p.map_b, kb * Cfg::kBlockK, ptn * Cfg::kTileN + j * Cfg::kBlockN + int(cta_rank) * Cfg::kCtaN);
       };
       if (pf > 0)
         for (int j = 0; j < pf; ++j) prefetch_unit(worker, j);
@@ -502,12 +513,16 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
             mbarrier_arrive_expect_tx(full_bar(stage), Cfg::kStageTx);
             load_operand<typename Cfg::ATile, Cfg::kAMn, 1>(a_smem + stage * Cfg::kABytes, &p.map_a, full_bar(stage),
                                                             kx, a_row, bz, batched);
-            if (args.m_block_group != nullptr)
-              load_operand<typename Cfg::BTile, Cfg::kBMn, 1>(b_smem + stage * Cfg::kBBytes, &p.map_b, full_bar(stage),
-                                                              kx, b_row, gz, true);
-            else
-              load_operand<typename Cfg::BTile, Cfg::kBMn, 1>(b_smem + stage * Cfg::kBBytes, &p.map_b, full_bar(stage),
-                                                              kx, b_row, bz, batched);
+#pragma unroll
+            for (int j = 0; j < Cfg::kNSub; ++j) {  // sub-tile j: B rows [j BlockN, (j + 1) BlockN) of the tile
+              const uint32_t bd = b_smem + stage * Cfg::kBBytes + j * Cfg::kBSubBytes;
+              if (args.m_block_group != nullptr)
+                load_operand<typename Cfg::BTile, Cfg::kBMn, 1>(bd, &p.map_b, full_bar(stage), kx,
+                                                                b_row + j * Cfg::kBlockN, gz, true);
+              else
+                load_operand<typename Cfg::BTile, Cfg::kBMn, 1>(bd, &p.map_b, full_bar(stage), kx,
+                                                                b_row + j * Cfg::kBlockN, bz, batched);
+            }
             if constexpr (Cfg::kMx) {
               // K-block kb's scale atoms: A's row block (tm) and the tile's row blocks of B (a block
               // past the end of B loads as zeros, for output columns that are never stored).
@@ -525,12 +540,15 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
             const uint32_t fb = leader_full0 + 8u * stage;
             load_operand<typename Cfg::ATile, Cfg::kAMn, 2>(a_smem + stage * Cfg::kABytes, &p.map_a, fb, kx, a_row, bz,
                                                             batched);
-            if (args.m_block_group != nullptr)
-              load_operand<typename Cfg::BTile, Cfg::kBMn, 2>(b_smem + stage * Cfg::kBBytes, &p.map_b, fb, kx, b_row,
-                                                              gz, true);
-            else
-              load_operand<typename Cfg::BTile, Cfg::kBMn, 2>(b_smem + stage * Cfg::kBBytes, &p.map_b, fb, kx, b_row,
-                                                              bz, batched);
+#pragma unroll
+            for (int j = 0; j < Cfg::kNSub; ++j) {  // sub-tile j: this CTA's half of its BlockN rows of B
+              const uint32_t bd = b_smem + stage * Cfg::kBBytes + j * Cfg::kBSubBytes;
+              if (args.m_block_group != nullptr)
+                load_operand<typename Cfg::BTile, Cfg::kBMn, 2>(bd, &p.map_b, fb, kx, b_row + j * Cfg::kBlockN, gz, true);
+              else
+                load_operand<typename Cfg::BTile, Cfg::kBMn, 2>(bd, &p.map_b, fb, kx, b_row + j * Cfg::kBlockN, bz,
+                                                                batched);
+            }
             if constexpr (Cfg::kMx) {
               // Each CTA: the scales of its own 128 rows of A, and of all the tile's rows of B.
               const int sy = kb * Cfg::kSfAtomsK;
@@ -626,10 +644,17 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
               else
                 umma_mxf8_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16, idesc, sfa_t, sfb_t, accumulate);
             }
-            else if constexpr (Cfg::kIsF8)
-              umma_f8_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16, Cfg::kIdesc, accumulate);
-            else
-              umma_f16_ss<CG>(d_tmem, a_desc + ka, b_desc + kb16, Cfg::kIdesc, accumulate);
+            else {
+#pragma unroll
+              for (int j = 0; j < Cfg::kNSub; ++j) {  // sub-tile j into accumulator columns [j BlockN, ...)
+                const uint64_t bj = b_desc + kb16 + ((j * Cfg::kBSubBytes) >> 4);
+                const uint32_t dj = d_tmem + uint32_t(j * Cfg::kBlockN);
+                if constexpr (Cfg::kIsF8)
+                  umma_f8_ss<CG>(dj, a_desc + ka, bj, Cfg::kIdesc, accumulate);
+                else
+                  umma_f16_ss<CG>(dj, a_desc + ka, bj, Cfg::kIdesc, accumulate);
+              }
+            }
           }
           // Stage consumed once these MMAs complete: release it in both CTAs of the pair.
           umma_commit<CG>(empty_bar(stage));
@@ -845,7 +870,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) gemm_tn_kernel(const __grid_
       row0 = tm * Cfg::kTileM + int(cta_rank) * Cfg::kCtaM + quarter * 32;
       const int col0 = tn * Cfg::kTileN + wcol;
       const uint32_t tcol = tmem_base + lane_base + acc * Cfg::kAccCols + uint32_t(wcol);
-      const bool split = t >= dp_tiles && args.sk_split > 1;
+      const bool split = Cfg::kNSub == 1 && t >= dp_tiles && args.sk_split > 1;
       if (split) {
         // A K-range of a tail tile: its partial sum into its slot, then the ticket.
         // (Chunk by chunk in every config: split tiles are few, registers are not.)

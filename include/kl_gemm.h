@@ -86,7 +86,12 @@ typedef struct kl_gemm_desc {
   int32_t group_m;        /* tile-raster group height in tiles; 0 = library default */
   int32_t max_ctas;       /* cap on resident CTAs; 0 = one per SM */
   int32_t variant;        /* algorithm variant, 0 = library default. KL_ALGO_SKINNY: weight rows
-                             per tile / 128 (1 or 2) */
+                             per tile / 128 (1 or 2). KL_ALGO_2CTA without block scaling: 1 = 256 x 256
+                             tiles, 4 = 256 x 512 tiles (two MMAs of N = 256 per stage of A; (bf16,
+                             bf16) and (e4m3, bf16), K-major, 128-byte swizzle, no split tail), 0 =
+                             256 x 512 for bf16 where they fill as many worker-waves as 256 x 256
+                             tiles and those need no split tail (8192^3, N-shards of 1024), else
+                             256 x 256 */
   int32_t prefetch;       /* L2 prefetch distance in K-blocks: 0 = library default, < 0 = off */
   /* Batched GEMM: `batch` independent problems (0 or 1 = one), matrix i of A/B/C at
    * a/b/c + i * stride_a/b/c elements (strides positive, multiples of 16 bytes). Tile kernels

@@ -127,6 +127,12 @@ kl_status run_tile(kl_gemm_desc const& d, Problem const& pr, bool pair, cudaStre
     if (handled) return s;
     return fail(KL_ERR_NOT_SUPPORTED, std::string(who) + ": 64- and 32-byte operand swizzle take bf16 inputs and bf16 or f32 C");
   }
+  if (pair && (d.variant == 4 || (d.variant == 0 && kl::capi::wide_tiles_pay(d.ab_type, d.c_type, pr)))) {
+    // 256 x 512 tiles: asked for, or the library default where they measured faster
+    s = kl::capi::run_tile_wide(d.ab_type, d.c_type, pr, stream, info, &handled);
+    if (handled) return s;
+    return fail(KL_ERR_NOT_SUPPORTED, std::string(who) + ": 256 x 512 tiles (variant 4) take (bf16, bf16) or (e4m3, bf16)");
+  }
   if (d.ab_type == KL_BF16 && d.c_type == KL_BF16)
     return pair ? run<Bf16Bf16_2>(pr, stream, info) : run<Bf16Bf16_1>(pr, stream, info);
   if (d.ab_type == KL_BF16 && d.c_type == KL_F32)

@@ -84,6 +84,14 @@ kl_status run_tile_types(int32_t ab_type, int32_t c_type, kl::gemm::Problem cons
 kl_status run_tile_swizzle(int32_t swizzle, int32_t ab_type, int32_t c_type, kl::gemm::Problem const& pr, bool pair,
                            cudaStream_t stream, kl::gemm::LaunchInfo* info, bool* handled);
 
+// kl_tile_wide.cu: 256 x 512 CTA-pair tiles (two MMAs of N = 256 per stage of A), (bf16, bf16) and
+// (e4m3, bf16), K-major, 128-byte swizzle.
+kl_status run_tile_wide(int32_t ab_type, int32_t c_type, kl::gemm::Problem const& pr, cudaStream_t stream,
+                        kl::gemm::LaunchInfo* info, bool* handled);
+// Whether the pair's default (variant 0) takes the wide tiles for this problem: bf16 in and out,
+// one problem, no split tail on the 256 x 256 tiles and at least their share of busy worker-waves.
+bool wide_tiles_pay(int32_t ab_type, int32_t c_type, kl::gemm::Problem const& pr);
+
 // kl_tile_mx.cu: block-scaled GEMMs (MXFP8, MXFP4, NVFP4), bf16 or f32 C. `pair`: 256 x 256 tiles on a
 // CTA pair; one CTA: variant 0/1 = 128 x 256 tiles with one accumulator, 2 = 128 x 128 with two.
 // mode: 1 = MX (UE8M0 scales per 32 elements), 2 = NVFP4 (UE4M3 per 16, e2m1 only).
