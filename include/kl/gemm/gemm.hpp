@@ -307,7 +307,13 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   a.tiles_m = int((pr.m + Cfg::kTileM - 1) / Cfg::kTileM);
   a.tiles_n = int((pr.n + Cfg::kTileN - 1) / Cfg::kTileN);
   a.k_blocks = int((ku + Cfg::kBlockK - 1) / Cfg::kBlockK);
-  a.group_m = pr.group_m > 0 ? pr.group_m : (Cfg::kCtaGroup == 2 ? 8 : 16);
+  // Default raster group: 8 tile-rows for the CTA pair, 16 for one CTA; per-tensor fp8 pairs take 16
+  // once there are 32 or more tile columns (measured on B200, fp8 16384 x N x 8192: N = 16384 1419 vs
+  // 1444 us, N = 8192 715 vs 725; N = 4096 and 2048 equal or faster with 8).
+  int group_default = Cfg::kCtaGroup == 2 ? 8 : 16;
+  if constexpr (Cfg::kCtaGroup == 2 && Cfg::kIsF8 && !Cfg::kMx)
+    if (a.tiles_n >= 32) group_default = 16;
+  a.group_m = pr.group_m > 0 ? pr.group_m : group_default;
   a.group_m = std::min(a.group_m, a.tiles_m);
   a.alpha = pr.alpha;
   a.scale_a = pr.scale_a;
