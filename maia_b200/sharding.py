@@ -36,11 +36,13 @@ def max_over_ranks(x: float, dist=None, device=None) -> float:
     return float(t.item())
 
 
-def gather_columns(c_shard, n: int, dist, align: int = 1):
+def gather_columns(c_shard, n: int, dist, align: int = 1, out=None, work=None):
     """All-gather the column blocks C[:, shard_r] of every rank into the full row-major C[M, N].
 
     Shards may differ in width by one column, so each is padded to the widest before the
-    collective and cut back afterwards."""
+    collective and cut back afterwards. `out` ([M, N]) and `work` ([world, M, widest shard], NCCL
+    only) are optional preallocated buffers: a loop that passes them allocates nothing per call, and
+    equal shards are re-laid out with one strided copy."""
     import torch
 
     world = dist.get_world_size()
@@ -53,13 +55,21 @@ def gather_columns(c_shard, n: int, dist, align: int = 1):
     else:
         padded = c_shard.contiguous()
     if dist.get_backend() == "nccl":
-        gathered = torch.empty((world, m, wmax), dtype=c_shard.dtype, device=c_shard.device)
+        gathered = work if work is not None else torch.empty((world, m, wmax), dtype=c_shard.dtype,
+                                                             device=c_shard.device)
         dist.all_gather_into_tensor(gathered, padded)
+        if out is not None and all(w == wmax for w in widths):
+            out.view(m, world, wmax).copy_(gathered.permute(1, 0, 2))
+            return out
         parts = list(gathered.unbind(0))
     else:
         parts = [torch.empty_like(padded) for _ in range(world)]
         dist.all_gather(parts, padded)
-    return torch.cat([p[:, :w] for p, w in zip(parts, widths)], dim=1)
+    full = torch.cat([p[:, :w] for p, w in zip(parts, widths)], dim=1)
+    if out is not None:
+        out.copy_(full)
+        return out
+    return full
 
 
 class SharedC:

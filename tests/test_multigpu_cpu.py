@@ -49,6 +49,11 @@ def _rank_main(rank, world, port, out_dir):
         c_shard = torch.from_numpy(og.gemm_f64(a, b[lo:hi], threads=1))
         t = sharding.max_over_ranks(0.5 + rank, dist)
         full = sharding.gather_columns(c_shard, n, dist)
+        # The same into a preallocated C, twice (a loop that reuses its buffers).
+        out = torch.full((m, n), float("nan"), dtype=c_shard.dtype)
+        for _ in range(2):
+            got = sharding.gather_columns(c_shard, n, dist, out=out)
+            assert got is out and torch.equal(out, full)
         np.save(os.path.join(out_dir, f"rank{rank}.npy"), full.numpy())
         np.save(os.path.join(out_dir, f"t{rank}.npy"), np.array([t]))
     finally:
