@@ -83,17 +83,21 @@ def test_chain_keeps_stream_order(cuda, m, algo, variant):
         prev = out
 
 
-@pytest.mark.parametrize("m,algo,variant", [(256, kl.ALGO_2CTA, 1), (16, kl.ALGO_SKINNY, 0)], ids=["pair", "skinny"])
+@pytest.mark.parametrize("m,algo,variant", [(256, kl.ALGO_2CTA, 1), (128, kl.ALGO_1CTA, 0), (16, kl.ALGO_SKINNY, 0)],
+                         ids=["pair", "one_cta", "skinny"])
 def test_chain_in_a_cuda_graph(cuda, m, algo, variant):
     x0, ws = _inputs(m, 70 + m, cuda)
     want = _step_by_step(x0, ws, algo, variant)[-1]
     bufs = [x0.clone(), torch.empty_like(x0)]
-    for f in _launchers(bufs, ws, algo, variant, 1):  # warm-up outside the capture
+    s = torch.cuda.Stream()
+    fns = _launchers(bufs, ws, algo, variant, 1, stream=s.cuda_stream)
+    # Warm-up on the capture stream, outside the capture: these small problems split their K across
+    # the CTAs through the stream's workspace, which is made on a first eager launch and never
+    # inside a capture (a capture on a stream without one records whole tiles, other bits).
+    for f in fns:
         f()
     torch.cuda.synchronize()
-    s = torch.cuda.Stream()
     g = torch.cuda.CUDAGraph()
-    fns = _launchers(bufs, ws, algo, variant, 1, stream=s.cuda_stream)
     with torch.cuda.graph(g, stream=s):
         for f in fns:
             f()
