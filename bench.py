@@ -133,36 +133,12 @@ def cpu_baseline(w, budget_s: float = 6.0):
 METRIC = "GEMM TFLOP/s per B200 and % of tcgen05 dense peak"
 
 
-def nvlink_bytes(index: int):
-    """(transmitted, received) NVLink data bytes of GPU `index` so far, all links, from NVML's
-    throughput counters (read-only), or None where NVML does not report them."""
-    try:
-        import pynvml
-
-        pynvml.nvmlInit()
-        h = pynvml.nvmlDeviceGetHandleByIndex(index)
-        tx_id, rx_id = pynvml.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_TX, pynvml.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_RX
-        # Per link (scope = link index), summed over the links that report.
-        links = 18
-        vals = pynvml.nvmlDeviceGetFieldValues(h, [(tx_id, l) for l in range(links)] + [(rx_id, l) for l in range(links)])
-        tx = [int(v.value.ullVal) for v in vals[:links] if v.nvmlReturn == 0]
-        rx = [int(v.value.ullVal) for v in vals[links:] if v.nvmlReturn == 0]
-        if not tx or not rx:
-            return None
-        return sum(tx) * 1024, sum(rx) * 1024
-    except Exception:
-        return None
-
-
-def timed(fn, steps: int, warmup: int, stream, device, sync, nvlink: bool = False, settle_s: float = 0.0,
-          sample_clocks: bool = True):
+def timed(fn, steps: int, warmup: int, stream, device, sync, settle_s: float = 0.0, sample_clocks: bool = True):
     """Device time per call of fn (CUDA events on `stream`, after `warmup` untimed calls), with the
-    NVML clock samples taken meanwhile; with nvlink=True also the NVLink bytes per call this GPU
-    sent and received (NVML counters read around the timed calls, after a pause that lets them
-    settle). settle_s: an idle pause first, so that a workload does not start in the power state the
-    previous one left. sample_clocks=False leaves the sampling thread out: a step that queues many
-    small launches from Python (the NCCL gather path) is host-bound, and a thread polling NVML in
-    every rank's process slows that host work down."""
+    NVML clock samples taken meanwhile. settle_s: an idle pause first, so that a workload does not
+    start in the power state the previous one left. sample_clocks=False leaves the sampling thread
+    out: a step that queues many small launches from Python (the NCCL gather path) is host-bound,
+    and a thread polling NVML in every rank's process slows that host work down."""
     import torch
 
     if settle_s > 0:
@@ -171,10 +147,6 @@ def timed(fn, steps: int, warmup: int, stream, device, sync, nvlink: bool = Fals
     for _ in range(max(warmup, 3)):
         fn()
     sync()
-    link0 = None
-    if nvlink:
-        time.sleep(0.3)
-        link0 = nvlink_bytes(device.index)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(device.index if sample_clocks else None) as clocks:
         e0.record(stream)
@@ -182,15 +154,6 @@ def timed(fn, steps: int, warmup: int, stream, device, sync, nvlink: bool = Fals
             fn()
         e1.record(stream)
         sync()
-    link = None
-    if link0 is not None:
-        time.sleep(0.3)
-        link1 = nvlink_bytes(device.index)
-        if link1 is not None:
-            link = {"tx_bytes_per_step": (link1[0] - link0[0]) / steps, "rx_bytes_per_step": (link1[1] - link0[1]) / steps,
-                    "source": "NVML NVLink data throughput counters (all links), read around the timed calls"}
-    if nvlink:
-        return e0.elapsed_time(e1) / steps, clocks.summary(), link
     return e0.elapsed_time(e1) / steps, clocks.summary()
 
 
@@ -515,11 +478,14 @@ def main():
         for _ in range(max(args.warmup, 3)):
             gather_step()
         barrier()
-        g_ms, _, g_link = timed(gather_step, args.steps, 0, stream, dev, barrier, nvlink=True, sample_clocks=False)
+        # The gather legs are short (0.1-0.6 ms a step): at least 50 timed steps each, back to back after
+        # their own warm-up (they are reported beside `value`, not as it).
+        g_steps = max(args.steps, 50)
+        g_ms, _ = timed(gather_step, g_steps, 0, stream, dev, barrier, sample_clocks=False)
         g_ms = max_over_ranks(g_ms)
         gather = {"value": flops_total / (g_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": g_ms,
                   "what": "kl_gemm + NCCL all-gather of C and re-layout to [M, N] on every rank (buffers made once)",
-                  "nvlink_rank0": g_link}
+                  "steps": g_steps}
 
         # The same result with the gather fused into the GEMM: every tile is also TMA-stored into
         # the other ranks' copies of C over NVLink (kl_gemm_gather).
@@ -534,11 +500,11 @@ def main():
         for _ in range(max(args.warmup, 3)):
             fused_step()
         barrier()
-        f_ms, _, f_link = timed(fused_step, args.steps, 0, stream, dev, barrier, nvlink=True, sample_clocks=False)
+        f_ms, _ = timed(fused_step, g_steps, 0, stream, dev, barrier, sample_clocks=False)
         f_ms = max_over_ranks(f_ms)
         gather["fused"] = {"value": flops_total / (f_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": f_ms,
                            "what": "kl_gemm_gather: tiles stored to every rank's C by the GEMM epilogue (P2P over NVLink)",
-                           "nvlink_rank0": f_link}
+                           "steps": g_steps}
         # Outside the timed region: every rank's kernels have finished (barrier), so its copy of the
         # full C is complete. Compare it with the NCCL-gathered C of the plain GEMM, bit for bit (the
         # same kernel and schedule produce both), on every rank.
@@ -571,8 +537,7 @@ def main():
                 kl.gemm_gather_multicast(a, b, mc_view, mc_addr, scale_a=scale_a, scale_b=scale_b, algo=args.algo,
                                          sfa=sfa, sfb=sfb, scale_vec=vec, stream_k=args.stream_k)
 
-            m_ms, _, m_link = timed(mc_step, args.steps, args.warmup, stream, dev, barrier, nvlink=True,
-                                     sample_clocks=False)
+            m_ms, _ = timed(mc_step, g_steps, args.warmup, stream, dev, barrier, sample_clocks=False)
             m_ms = max_over_ranks(m_ms)
             barrier()
             same = torch.equal(mcc.full.view(bits), want.view(bits))
@@ -587,7 +552,7 @@ def main():
             gather["multicast"] = {"value": flops_total / (m_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": m_ms,
                                    "what": "kl_gemm_gather_multicast: each tile stored once through an NVLink "
                                            "multicast address (multimem.st), the switch writing every rank's C",
-                                   "nvlink_rank0": m_link}
+                                   "steps": g_steps}
         else:
             gather["multicast"] = {"unavailable": mcc.reason}
         mcc.close()
