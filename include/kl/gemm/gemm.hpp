@@ -310,9 +310,12 @@ cudaError_t launch_tn(Problem const& pr, int* status, unsigned long long timeout
   // Default raster group: 8 tile-rows for the CTA pair, 16 for one CTA; per-tensor fp8 pairs take 16
   // once there are 32 or more tile columns (measured on B200, fp8 16384 x N x 8192: N = 16384 1419 vs
   // 1444 us, N = 8192 715 vs 725; N = 4096 and 2048 equal or faster with 8).
+  // 256 x 512 pair tiles take 16 too (8192^3 bf16 under ncu: DRAM 0.969 GB per launch vs 1.031 with
+  // 8, 673 vs 678 us).
   int group_default = Cfg::kCtaGroup == 2 ? 8 : 16;
   if constexpr (Cfg::kCtaGroup == 2 && Cfg::kIsF8 && !Cfg::kMx)
     if (a.tiles_n >= 32) group_default = 16;
+  if constexpr (Cfg::kNSub > 1) group_default = 16;
   a.group_m = pr.group_m > 0 ? pr.group_m : group_default;
   a.group_m = std::min(a.group_m, a.tiles_m);
   a.alpha = pr.alpha;
