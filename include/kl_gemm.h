@@ -271,8 +271,8 @@ KL_API kl_status kl_gemm_host_b(const kl_gemm_desc* desc, void* a_ready, void* d
  * on the array, so serialise them. desc->algo must be KL_ALGO_AUTO or KL_ALGO_SKINNY;
  * desc->variant 0 or 1 (both the one-box kernel; variant 2 is KL_ERR_NOT_SUPPORTED here); C
  * aligned to its element size. A call that is rejected queues nothing on `stream`. The kernel is
- * launched plainly (desc->launch_overlap is not used): its arrival counters are cleared by a copy-
- * engine memset queued just before it. */
+ * launched plainly (desc->launch_overlap is not used): its arrival counters are cleared by a
+ * cudaMemsetAsync queued just before it. */
 KL_API kl_status kl_gemm_skinny_noalloc(const kl_gemm_desc* desc, void* stream);
 
 /* No reference counterpart. The tile-kernel GEMM (KL_ALGO_1CTA / 2CTA) whose epilogue also writes
