@@ -385,6 +385,11 @@ def main():
               ab_type=wl.MX_ELEMENT[w.dtype] if w.dtype == "mxfp6" else None, stream_k=args.stream_k)
 
     step = kl.gemm_launcher(a, b, c, **kw)  # one kl_gemm per call, the descriptor built once
+    # The kernel the launches run: its family and C tile (kl_gemm_resolve_algo / _tile).
+    route = {kl.ALGO_SKINNY: "skinny (stream-K)", kl.ALGO_1CTA: "one CTA", kl.ALGO_2CTA: "CTA pair"}[
+        kl.resolve_algo(a, b, c, **kw)]
+    tile_m, tile_n = kl.resolve_tile(a, b, c, **kw)
+    kernel = f"{route}, {tile_m} x {tile_n} tiles" if tile_m else route
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -608,7 +613,7 @@ def main():
             "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": w.dtype, "data": "synthetic",
-            "config": config_of(w, args, world),
+            "config": dict(config_of(w, args, world), kernel=kernel),
             "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "what": e2e_how,
                     "max_rel_diff_vs_device": e2e_diff},

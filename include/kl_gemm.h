@@ -219,6 +219,12 @@ KL_API kl_status kl_gemm_workspace_size(const kl_gemm_desc* desc, size_t* bytes)
  * descriptor's extents, types and options; launches nothing and needs no GPU. */
 KL_API kl_status kl_gemm_resolve_algo(const kl_gemm_desc* desc, int32_t* algo);
 
+/* No reference counterpart. The C tile (rows x columns) of the kernel kl_gemm runs for `desc`:
+ * 128 x 256 (or 128 x 128) on one CTA, 256 x 256, 256 x 512, 256 x 192 or 256 x 128 on a CTA pair,
+ * 0 x 0 for the stream-K skinny kernel. The CTA-pair choice of variant 0 depends on the current
+ * device's SM count, so this needs a CUDA device (KL_ERR_CUDA without one); nothing is launched. */
+KL_API kl_status kl_gemm_resolve_tile(const kl_gemm_desc* desc, int32_t* tile_m, int32_t* tile_n);
+
 /* No reference counterpart. Like kl_gemm, with caller-provided device workspace: at least
  * kl_gemm_workspace_size bytes, 16-byte aligned, zero-filled before its first use. Its head holds
  * 16 bytes of arrival counters per 128 rows of B, which the skinny kernel leaves at zero after

@@ -30,7 +30,7 @@ FP6_TYPES = {"e3m2": KL_E3M2, "e2m3": KL_E2M3}
 ALGO_AUTO, ALGO_1CTA, ALGO_2CTA, ALGO_SKINNY = range(4)
 
 EXPORTED = (
-    "kl_version", "kl_last_error", "kl_gemm", "kl_gemm_workspace_size", "kl_gemm_resolve_algo", "kl_gemm_ws", "kl_release_workspaces",
+    "kl_version", "kl_last_error", "kl_gemm", "kl_gemm_workspace_size", "kl_gemm_resolve_algo", "kl_gemm_resolve_tile", "kl_gemm_ws", "kl_release_workspaces",
     "kl_set_wait_timeout_ns", "kl_read_status", "kl_probe_wait_timeout", "kl_smem_tile_offset",
     "kl_tma_box_geometry", "kl_tma_box_position", "kl_umma_smem_desc", "kl_mma_instr_desc",
     "kl_make_tma_desc", "kl_gemm_skinny_noalloc", "kl_gemm_host", "kl_gemm_host_b", "kl_gemm_clock_probe", "kl_gemm_gather", "kl_gemm_gather_multicast",
@@ -97,6 +97,7 @@ def lib() -> ctypes.CDLL:
             "kl_gemm": (i32, [P(GemmDesc), vp]),
             "kl_gemm_workspace_size": (i32, [P(GemmDesc), P(ctypes.c_size_t)]),
             "kl_gemm_resolve_algo": (i32, [P(GemmDesc), P(ctypes.c_int32)]),
+            "kl_gemm_resolve_tile": (i32, [P(GemmDesc), P(ctypes.c_int32), P(ctypes.c_int32)]),
             "kl_gemm_ws": (i32, [P(GemmDesc), vp, ctypes.c_size_t, vp]),
             "kl_set_wait_timeout_ns": (None, [u64]),
             "kl_read_status": (i32, [P(i32), i32]),
@@ -564,6 +565,15 @@ def resolve_algo(a, b, c, **kw) -> int:
     out = ctypes.c_int32()
     check(lib().kl_gemm_resolve_algo(ctypes.byref(d), ctypes.byref(out)))
     return out.value
+
+
+def resolve_tile(a, b, c, **kw) -> tuple:
+    """(rows, columns) of the C tile kl_gemm runs for these operands and options, through
+    kl_gemm_resolve_tile ((0, 0) for the stream-K skinny kernel); nothing is launched."""
+    d = gemm_desc(a, b, c, **kw)
+    tm, tn = ctypes.c_int32(), ctypes.c_int32()
+    check(lib().kl_gemm_resolve_tile(ctypes.byref(d), ctypes.byref(tm), ctypes.byref(tn)))
+    return tm.value, tn.value
 
 
 def workspace_size(a, b, c, **kw) -> int:

@@ -94,6 +94,13 @@ kl_status run_mn(Problem const& pr, bool pair, bool a_mn, bool b_mn, cudaStream_
   return pair ? run<Bf16Mn_2<false, true>>(pr, stream, info) : run<Bf16Mn_1<false, true>>(pr, stream, info);
 }
 
+// Whether a CTA-pair request runs on the 256 x 512 tiles: asked for (variant 4), or the library's
+// choice for variant 0. Block-scaled, MN-major and 64 / 32-byte-swizzle requests never do.
+bool takes_wide_tiles(kl_gemm_desc const& d, Problem const& pr) {
+  if (d.block_scale != 0 || d.a_major == 1 || d.b_major == 1 || (d.swizzle != 0 && d.swizzle != 128)) return false;
+  return d.variant == 4 || (d.variant == 0 && kl::capi::wide_tiles_pay(d.ab_type, d.c_type, pr));
+}
+
 // The tile kernel for a request: by operand majors, operand swizzle and (A/B, C) types. Throws
 // std::invalid_argument from the tensor-map builders, like launch_tn.
 kl_status run_tile(kl_gemm_desc const& d, Problem const& pr, bool pair, cudaStream_t stream, LaunchInfo* info,
@@ -127,7 +134,7 @@ kl_status run_tile(kl_gemm_desc const& d, Problem const& pr, bool pair, cudaStre
     if (handled) return s;
     return fail(KL_ERR_NOT_SUPPORTED, std::string(who) + ": 64- and 32-byte operand swizzle take bf16 inputs and bf16 or f32 C");
   }
-  if (pair && (d.variant == 4 || (d.variant == 0 && kl::capi::wide_tiles_pay(d.ab_type, d.c_type, pr)))) {
+  if (pair && takes_wide_tiles(d, pr)) {
     // 256 x 512 tiles: asked for, or the library default where they measured faster
     s = kl::capi::run_tile_wide(d.ab_type, d.c_type, pr, stream, info, &handled);
     if (handled) return s;
@@ -250,6 +257,34 @@ kl_status kl_gemm_resolve_algo(const kl_gemm_desc* d, int32_t* algo) {
   kl_status s = resolve_algo(*d, &a);
   if (s == KL_OK) *algo = a;
   return s;
+}
+
+kl_status kl_gemm_resolve_tile(const kl_gemm_desc* d, int32_t* tile_m, int32_t* tile_n) {
+  if (d == nullptr || tile_m == nullptr || tile_n == nullptr) return fail(KL_ERR_INVALID_ARGUMENT, "null argument");
+  if (d->m <= 0 || d->n <= 0 || d->k <= 0) return fail(KL_ERR_INVALID_ARGUMENT, "kl_gemm_resolve_tile: empty problem");
+  int a = KL_ALGO_AUTO;
+  kl_status s = resolve_algo(*d, &a);
+  if (s != KL_OK) return s;
+  const bool mx = d->block_scale != 0;
+  if (a == KL_ALGO_SKINNY) {
+    *tile_m = 0;  // stream-K over the weight rows: no fixed C tile
+    *tile_n = 0;
+  } else if (a == KL_ALGO_1CTA) {
+    *tile_m = 128;
+    *tile_n = (mx && d->variant == 2) ? 128 : 256;
+  } else {
+    *tile_m = 256;
+    *tile_n = mx ? (d->variant == 2 ? 128 : d->variant == 3 ? 192 : 256) : 256;
+    if (!mx) {
+      int count = 0;
+      if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+        (void)cudaGetLastError();
+        return fail(KL_ERR_CUDA, "kl_gemm_resolve_tile: no CUDA device (the CTA-pair choice reads its SM count)");
+      }
+      if (takes_wide_tiles(*d, problem_of(*d))) *tile_n = 512;
+    }
+  }
+  return KL_OK;
 }
 
 kl_status kl_release_workspaces(void) {

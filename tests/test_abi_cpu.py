@@ -311,3 +311,23 @@ def test_gather_multicast_argument_checks(kl):
     assert kl.lib().kl_gemm_gather_multicast(ctypes.byref(d), ctypes.c_void_p(0x4000), None) == kl.KL_ERR_NOT_SUPPORTED
     d.batch, d.m = 0, 0  # an empty shard: nothing to do
     assert kl.lib().kl_gemm_gather_multicast(ctypes.byref(d), ctypes.c_void_p(0x4000), None) == kl.KL_OK
+
+
+def test_resolve_tile_reports_a_missing_device(kl):
+    """kl_gemm_resolve_tile needs the device's SM count for the CTA pair's choice: with no GPU it
+    returns KL_ERR_CUDA with a message instead of guessing; the skinny and one-CTA routes answer
+    from the descriptor alone."""
+    import ctypes
+
+    tm, tn = ctypes.c_int32(-1), ctypes.c_int32(-1)
+    d = kl.GemmDesc(m=16, n=28672, k=8192, a=0x1000, lda=8192, b=0x2000, ldb=8192, c=0x3000, ldc=28672,
+                    ab_type=kl.KL_BF16, c_type=kl.KL_BF16, alpha=1.0, algo=kl.ALGO_AUTO)
+    assert kl.lib().kl_gemm_resolve_tile(ctypes.byref(d), ctypes.byref(tm), ctypes.byref(tn)) == kl.KL_OK
+    assert (tm.value, tn.value) == (0, 0)
+    d.m = 128
+    assert kl.lib().kl_gemm_resolve_tile(ctypes.byref(d), ctypes.byref(tm), ctypes.byref(tn)) == kl.KL_OK
+    assert (tm.value, tn.value) == (128, 256)
+    d.m = 8192
+    d.n = d.ldc = 8192
+    st = kl.lib().kl_gemm_resolve_tile(ctypes.byref(d), ctypes.byref(tm), ctypes.byref(tn))
+    assert st == kl.KL_ERR_CUDA and b"no CUDA device" in kl.lib().kl_last_error()

@@ -74,3 +74,24 @@ def test_wide_rejects_other_types(cuda):
     c = torch.zeros((256, 512), dtype=torch.float32, device=cuda)
     with pytest.raises(kl.KlError, match="variant 4"):
         kl.gemm(a, b, c, algo=kl.ALGO_2CTA, variant=4)
+
+
+@pytest.mark.parametrize("m,n,k,dtype,want", [
+    (8192, 8192, 8192, "bf16", (256, 512)),    # 512 tiles on 74 pairs: as full as 1024 narrow ones
+    (8192, 1024, 8192, "bf16", (256, 512)),    # one rank's shard of 8: one wave of 64 tiles
+    (8192, 4096, 8192, "bf16", (256, 256)),    # wide tiles would fill 3.46 waves instead of 6.92
+    (8192, 2048, 8192, "bf16", (256, 256)),    # the split tail fills the narrow tiles' last wave
+    (16384, 16384, 8192, "e4m3", (256, 256)),  # fp8 stays on 256 x 256
+    (128, 28672, 8192, "bf16", (128, 256)),    # decode, 128 rows: one CTA
+    (16, 28672, 8192, "bf16", (0, 0)),         # decode, 16 rows: the stream-K skinny kernel
+])
+def test_default_tile_choice(cuda, m, n, k, dtype, want):
+    """kl_gemm_resolve_tile names the tile kl_gemm's defaults run (nothing is launched)."""
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float8_e4m3fn
+    a = torch.empty((m, k), dtype=tdt, device=cuda)
+    b = torch.empty((n, k), dtype=tdt, device=cuda)
+    c = torch.empty((m, n), dtype=torch.bfloat16, device=cuda)
+    assert kl.resolve_tile(a, b, c) == want
+    if m >= 256:  # variant 1 asks for the 256 x 256 tiles, variant 4 for the wide ones
+        assert kl.resolve_tile(a, b, c, algo=kl.ALGO_2CTA, variant=1) == (256, 256)
+        assert kl.resolve_tile(a, b, c, algo=kl.ALGO_2CTA, variant=4) == (256, 512)
