@@ -56,6 +56,11 @@ static void check_case(int tiles, int sk_tiles, int split, int W, int KB) {
 
 template <int CG>
 using Pair = TnConfig<kl::bf16, kl::bf16, CG, 256, CG == 2 ? 6 : 4>;
+// 256 x 512 CTA-pair tiles (two N = 256 sub-tiles per stage of A).
+using Wide = TnConfig<kl::bf16, kl::bf16, 2, 256, 4, false, false, false, kl::Swizzle128B, 0, 2>;
+static_assert(Wide::kTileN == 512 && Wide::kCtaN == 128 && Wide::kAccCols == 512 && Wide::kNumAcc == 1 &&
+                  Wide::kEpiWarps == 8 && !Wide::kEarlyRelease && Wide::kBBytes == 2 * Wide::kBSubBytes,
+              "wide tile geometry");
 
 int main() {
   int cases = 0;
@@ -115,6 +120,17 @@ int main() {
   pr.n = 2048;
   CHECK(tn_schedule<Pair<1>>(pr, 148).sk_tiles == 68 && tn_schedule<Pair<1>>(pr, 148).sk_split == 2,
         "one-CTA tiles: 512 on 148 workers, the 68 of the last wave in two ranges");
+  // Wide tiles: whole tiles only, and the tile counts behind the default choice.
+  pr.stream_k = 0;
+  pr.m = 8192;
+  for (int n : {8192, 4096, 2048, 1024}) {
+    pr.n = n;
+    const TnSchedule w = tn_schedule<Wide>(pr, 74);
+    CHECK(w.tiles == 32 * (n / 512) && w.sk_tiles == 0 && w.workers == std::min(74, w.tiles), "wide n %d: %d tiles",
+          n, w.tiles);
+  }
+  pr.stream_k = 1;
+  CHECK(tn_schedule<Wide>(pr, 74).sk_tiles == 0, "wide tiles never split, even when asked");
   std::printf("%d cases, %d failures\n", cases, failures);
   return failures == 0 ? 0 : 1;
 }
