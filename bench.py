@@ -425,57 +425,8 @@ def main():
     flops_total = 2.0 * w.m * (w.n if split == world else n_hi - n_lo) * w.k
     value = flops_total / (dev_ms * 1e-3) / 1e12
 
-    # ---- end to end through the public API with host buffers
-    d2h = c.numel() * c.element_size()
-    e2e_how = "kl_gemm_host: all of A and this rank's B copied in, C's block copied out, pipelined over column blocks"
-    if dist is not None and not mx:
-        # Each rank copies only its slab of A's rows in and the ranks all-gather A over NVLink, while
-        # the B shard streams in (sharding.HostShardedGemm over kl_gemm_host_b).
-        hs = sharding.HostShardedGemm(w.m, nshard, w.k, tdt, odt, dev, dist)
-        s_lo, s_hi = hs.slab_rows()
-        a_slab_host = a_host[s_lo:s_hi]
-        h2d = a_slab_host.numel() * a_slab_host.element_size() + b_host.numel() * b_host.element_size()
-        e2e_how = ("sharding.HostShardedGemm: this rank's slab of A's rows copied in and all-gathered over NVLink "
-                   "(NCCL), B's shard streamed in and C's block out through kl_gemm_host_b")
-
-        def e2e_step():
-            hs(a_slab_host, b_host, c_host, scale_a=scale_a, scale_b=scale_b, algo=args.algo, chunks=args.chunks,
-               stream_k=args.stream_k)
-    else:
-        h2d = a_host.numel() * a_host.element_size() + b_host.numel() * b_host.element_size()
-        if mx:
-            h2d += sfa_host.numel() + sfb_host.numel()
-
-        def e2e_step():
-            # The host-buffer entry point: copies in, GEMM and copy out, pipelined over column blocks.
-            kl.gemm_host(a_host, b_host, c_host, a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo,
-                         sfa=sfa_host, sfb=sfb_host, scale_vec=vec, chunks=args.chunks, ab_type=kw["ab_type"],
-                         stream_k=args.stream_k)
-
-    for _ in range(max(args.warmup, 3)):
-        e2e_step()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record(stream)
-    barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
-    # Outside the timed region: the host-side C of the last step against the device-resident GEMM's C
-    # (column blocks may split the tail differently, so agreement is to fp32 rounding, not bits).
-    if not mx:
-        step()
-        torch.cuda.synchronize(dev)
-        ref_c = c.float()
-        e2e_diff = float((c_host.to(dev).float() - ref_c).abs().max() / ref_c.abs().max().clamp_min(1e-30))
-        if e2e_diff > 1e-2:
-            raise RuntimeError(f"the host-buffer path's C differs from the device GEMM's: {e2e_diff:.3e}")
-        del ref_c
-    else:
-        e2e_diff = None
-
-    # ---- N > 1: the same GEMM followed by the NCCL all-gather of C (where the full C is needed)
+    # ---- N > 1: the same GEMM followed by the NCCL all-gather of C (where the full C is needed). The
+    # gather legs run before the end-to-end leg, whose NCCL all-gather of A runs on a side stream.
     gather = None
     gather_check = None
     if dist is not None:
@@ -575,6 +526,56 @@ def main():
         barrier()
         if float(hi.item()) > 1e-2 or mc_bad:
             raise RuntimeError(f"a fused gather's C differs from the NCCL-gathered C: {gather_check}")
+
+    # ---- end to end through the public API with host buffers
+    d2h = c.numel() * c.element_size()
+    e2e_how = "kl_gemm_host: all of A and this rank's B copied in, C's block copied out, pipelined over column blocks"
+    if dist is not None and not mx:
+        # Each rank copies only its slab of A's rows in and the ranks all-gather A over NVLink, while
+        # the B shard streams in (sharding.HostShardedGemm over kl_gemm_host_b).
+        hs = sharding.HostShardedGemm(w.m, nshard, w.k, tdt, odt, dev, dist)
+        s_lo, s_hi = hs.slab_rows()
+        a_slab_host = a_host[s_lo:s_hi]
+        h2d = a_slab_host.numel() * a_slab_host.element_size() + b_host.numel() * b_host.element_size()
+        e2e_how = ("sharding.HostShardedGemm: this rank's slab of A's rows copied in and all-gathered over NVLink "
+                   "(NCCL), B's shard streamed in and C's block out through kl_gemm_host_b")
+
+        def e2e_step():
+            hs(a_slab_host, b_host, c_host, scale_a=scale_a, scale_b=scale_b, algo=args.algo, chunks=args.chunks,
+               stream_k=args.stream_k)
+    else:
+        h2d = a_host.numel() * a_host.element_size() + b_host.numel() * b_host.element_size()
+        if mx:
+            h2d += sfa_host.numel() + sfb_host.numel()
+
+        def e2e_step():
+            # The host-buffer entry point: copies in, GEMM and copy out, pipelined over column blocks.
+            kl.gemm_host(a_host, b_host, c_host, a, b, c, scale_a=scale_a, scale_b=scale_b, algo=args.algo,
+                         sfa=sfa_host, sfb=sfb_host, scale_vec=vec, chunks=args.chunks, ab_type=kw["ab_type"],
+                         stream_k=args.stream_k)
+
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    # Outside the timed region: the host-side C of the last step against the device-resident GEMM's C
+    # (column blocks may split the tail differently, so agreement is to fp32 rounding, not bits).
+    if not mx:
+        step()
+        torch.cuda.synchronize(dev)
+        ref_c = c.float()
+        e2e_diff = float((c_host.to(dev).float() - ref_c).abs().max() / ref_c.abs().max().clamp_min(1e-30))
+        if e2e_diff > 1e-2:
+            raise RuntimeError(f"the host-buffer path's C differs from the device GEMM's: {e2e_diff:.3e}")
+        del ref_c
+    else:
+        e2e_diff = None
 
     peaks, peak_src = load_peaks()
     extra = None
