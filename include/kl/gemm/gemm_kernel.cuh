@@ -101,7 +101,8 @@ struct TnConfig {
   static constexpr uint32_t kSfaBytes = 512u * kSfAtomsK;
   static constexpr uint32_t kSfbBytes = 512u * kSfAtomsK * kSfbAtoms;
   // Two TMEM accumulators (epilogue of tile i overlaps the MMAs of tile i + 1), except for block
-  // scaling with 256 columns: 2 x 256 accumulator columns would leave none for the scales.
+  // scaling with 256 columns (2 x 256 accumulator columns would leave none for the scales) and for
+  // wide tiles, whose one accumulator of 2 x 256 columns fills TMEM.
   static constexpr int kNumAcc = ((kMx && BlockN == 256) || NSub > 1) ? 1 : 2;
   static constexpr int kAccCols = kTileN;              // fp32 accumulator columns per buffer
   static constexpr int kSfaCol = kAccCols * kNumAcc;   // TMEM columns of A's and B's scales
