@@ -17,7 +17,9 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 LIB = PKG / "libkl_b200.so"
 SOURCES = sorted((PKG / "csrc").glob("*.cu"))
-HEADERS = sorted((ROOT / "include").rglob("*.h*")) + sorted((PKG / "csrc").glob("*.cuh"))
+# Every header the sources can include: .h / .hpp and the .cuh kernel headers.
+HEADERS = sorted(p for p in (ROOT / "include").rglob("*") if p.suffix in (".h", ".hpp", ".cuh")) + \
+    sorted((PKG / "csrc").glob("*.cuh"))
 
 NVCC_FLAGS = [
     "-std=c++20",
