@@ -71,3 +71,15 @@ def test_stream_k_schedule(tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True)
     assert r.returncode == 0, r.stdout + r.stderr
     assert " 0 failures" in r.stdout
+
+
+def test_library_build_tracks_every_header():
+    """The library is rebuilt when any header its sources can include changes, the .cuh kernel
+    headers included (an edit to one of them alone must not leave a stale libkl_b200.so)."""
+    from maia_b200 import build as b
+
+    tracked = {p.resolve() for p in b.HEADERS}
+    for p in (ROOT / "include").rglob("*"):
+        if p.suffix in (".h", ".hpp", ".cuh"):
+            assert p.resolve() in tracked, p
+    assert any(p.name == "gemm_kernel.cuh" for p in tracked)
